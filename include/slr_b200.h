@@ -1,0 +1,224 @@
+/*
+ * slr_b200.h — C ABI of libslr_b200.so, the B200 (sm_100a) implementation of
+ * S-SALAAD's sparse-plus-low-rank (S+LR) linear forward
+ *
+ *     y = x · Sᵀ + (x · Bᵀ) · Aᵀ + bias
+ *
+ * with S block-sparse in BSR form.  Names follow the reference: the weight is
+ * W ≈ A·B + S with A [out, r] and B [r, in] (ssalaad/efficient/ls_linear.py:
+ * 20-27), BSR indices are int32 crow/col, BSR values are stored per block
+ * TRANSPOSED as [nnz, block_q, block_p] (ls_linear.py:92-94), and
+ * active_rows lists the block-rows that hold at least one block
+ * (ls_linear.py:95-97).  Paths in citations are within the S-SALAAD project.
+ *
+ * Conventions shared by every entry point:
+ *   - Plain pointers and sizes; no framework types.  Device pointers refer to
+ *     memory on the CUDA device that is current on the calling thread.
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default
+ *     stream).  Work is enqueued on it; nothing synchronises the host unless
+ *     the entry point's comment says so.
+ *   - The return value is an slr_status; 0 means success.  Nothing calls
+ *     exit() or abort().  slr_last_error() returns a message for the last
+ *     failing call on the calling thread.
+ *   - The library allocates no device memory inside these calls.  Scratch
+ *     memory is the caller's "workspace" (size from the matching *_size
+ *     query).
+ *   - dtype is an slr_dtype: every floating-point tensor of one call has the
+ *     same element type, as in the reference (addmm_inplace.py:100-104).
+ */
+#ifndef SLR_B200_H_
+#define SLR_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SLR_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define SLR_API __attribute__((visibility("default")))
+#else
+#define SLR_API
+#endif
+
+typedef enum slr_status {
+  SLR_OK = 0,
+  SLR_ERR_INVALID_ARGUMENT = 1, /* bad shape / size / null pointer (Python: ValueError) */
+  SLR_ERR_UNSUPPORTED_DTYPE = 2, /* element type not supported (Python: TypeError) */
+  SLR_ERR_UNSUPPORTED = 3,       /* valid but unsupported configuration (Python: RuntimeError) */
+  SLR_ERR_CUDA = 4,              /* a CUDA runtime call or launch failed */
+  SLR_ERR_WORKSPACE = 5,         /* workspace missing, too small or misaligned */
+  SLR_ERR_BAD_INDEX = 6,         /* slr_validate_bsr found an index out of range */
+  SLR_ERR_TIMEOUT = 7            /* a bounded device-side wait gave up */
+} slr_status;
+
+typedef enum slr_dtype {
+  SLR_F32 = 0,
+  SLR_F16 = 1,
+  SLR_BF16 = 2
+} slr_dtype;
+
+/* ------------------------------------------------------------ library -- */
+
+SLR_API int slr_abi_version(void);
+SLR_API const char* slr_status_string(int status);
+/* Message of the last failing call on this thread ("" if none). */
+SLR_API const char* slr_last_error(void);
+/* Reads and clears the device-side status word that bounded waits set when
+ * they time out (SLR_OK or SLR_ERR_TIMEOUT).  Synchronises the device. */
+SLR_API int slr_device_status(int* status_out);
+
+/* ------------------------------------------------- in-place BSR addmm -- */
+
+/*
+ * out[M, NB*block_p] += x[M, K] · Sᵀ, in place, for the block-rows listed in
+ * active_rows (others untouched); fp32 accumulation, one rounding to dtype.
+ *
+ * Replaces the torch operator
+ *   ssalaad::tilelang_bsr_addmm_inplace_dense_(Tensor(a!) out_inplace,
+ *       Tensor x, Tensor crow_indices, Tensor col_indices, Tensor values,
+ *       Tensor active_rows) -> ()
+ * defined at ssalaad/tilelang_sparse/addmm_inplace.py:130-141, whose
+ * implementation is _tilelang_bsr_addmm_inplace_dense_impl (:88-127) and
+ * kernel _bsr_body (:41-82); and, for dtype SLR_F32, the CPU operator
+ * bsr_addmm_avx2_ (ssalaad/cpu_sparse/bsr_addmm_avx2.cpp:144-178).
+ *
+ *   out          device, [M, NB*block_p] row-major, dtype
+ *   x            device, [M, K] row-major, dtype; K % block_q == 0
+ *   crow         device int32 [NB+1]
+ *   col          device int32 [nnz], each in [0, K/block_q)
+ *   values       device, [nnz, block_q, block_p], dtype
+ *   active_rows  device int32 [active_nb], each in [0, NB)
+ *   block_p, block_q: multiples of 16 for SLR_F16/SLR_BF16 (the reference
+ *     CUDA kernel's rule, ls_linear.py:114-117), multiples of 8 for SLR_F32.
+ * Unlike the reference CUDA operator, M needs no padding to a tile multiple.
+ * For SLR_F32 each output element is accumulated in exactly the reference
+ * AVX2 kernel's order (fused multiply-adds over blocks in crow order, then k
+ * ascending), so the result is bit-identical to bsr_addmm_avx2_.
+ */
+SLR_API int slr_bsr_addmm_inplace(void* out, const void* x, int64_t M, int64_t K,
+                          const int32_t* crow, int64_t NB, const int32_t* col,
+                          const void* values, int64_t nnz, int64_t block_p,
+                          int64_t block_q, const int32_t* active_rows,
+                          int64_t active_nb, int dtype, void* stream);
+
+/*
+ * Checks a BSR structure on the device: crow[0] == 0, crow non-decreasing,
+ * crow[NB] == nnz, every col in [0, nbk), every active row in [0, NB) with a
+ * nonempty block-row.  The reference checks none of this on the GPU (its
+ * kernel only assumes col in range, addmm_inplace.py:76-77); the layer
+ * classes call this once at construction.  Synchronises `stream`.
+ * Returns SLR_OK or SLR_ERR_BAD_INDEX.
+ */
+SLR_API int slr_validate_bsr(const int32_t* crow, int64_t NB, const int32_t* col,
+                     int64_t nnz, int64_t nbk, const int32_t* active_rows,
+                     int64_t active_nb, void* stream);
+
+/* ------------------------------------------------------ S+LR forward -- */
+
+/* One S+LR linear layer: the buffers of _LRSLinearLRBlockBase
+ * (ls_linear.py:57-97) plus an optional block-row schedule. */
+typedef struct slr_layer {
+  int64_t in_features;    /* K */
+  int64_t out_features;   /* N */
+  int64_t rank;           /* r (A.shape[1] == B.shape[0]); may be 0 */
+  int64_t block_p;        /* rows of a block (output features); 0 if nnz == 0 */
+  int64_t block_q;        /* cols of a block (input features);  0 if nnz == 0 */
+  int64_t nnz;            /* number of stored blocks; 0 = low-rank only */
+  const int32_t* crow;    /* device int32 [N/block_p + 1] (ignored if nnz == 0) */
+  const int32_t* col;     /* device int32 [nnz] */
+  const void* values;     /* device [nnz, block_q, block_p] */
+  const int32_t* row_order; /* device int32 [N/block_p] permutation of the
+                               block-rows, heaviest first, from
+                               slr_plan_row_order; NULL = natural order */
+  const void* A;          /* device [N, r] */
+  const void* B;          /* device [r, K] */
+  const void* bias;       /* device [N] or NULL */
+  int32_t dtype;          /* slr_dtype of x, y, values, A, B, bias */
+  int32_t flags;          /* reserved, must be 0 */
+} slr_layer;
+
+/*
+ * Workspace bytes that slr_lrs_linear_forward needs for M tokens.  The
+ * workspace must be 256-byte aligned, zero-filled before its FIRST use (the
+ * library leaves its counters at zero after every call), and not shared by
+ * calls that may overlap on the GPU.
+ */
+SLR_API size_t slr_lrs_linear_workspace_size(const slr_layer* layer, int64_t M);
+
+/*
+ * y[M, N] = x[M, K] · Sᵀ + (x · Bᵀ) · Aᵀ + bias.
+ *
+ * Replaces the forward of the compressed layer on CUDA,
+ * _LRSLinearLRBlockCUDA.forward (ls_linear.py:124-137: pad, two F.linear
+ * calls, the in-place sparse operator, the bias add, slice), and with
+ * nnz == 0 the low-rank-only layer _LRSLinearLR.forward (ls_linear.py:47-51).
+ * For SLR_F32 it computes the CPU layer's arithmetic
+ * (_LRSLinearLRBlockCPU.forward, ls_linear.py:155-164): the low-rank
+ * product in fp32, then the sparse term accumulated in the reference
+ * kernel's order, then the bias.  For 16-bit dtypes x·Bᵀ is rounded to the
+ * dtype (as the reference's first F.linear does) and everything after it is
+ * accumulated in fp32 and rounded once.
+ * y must not overlap x.  No M padding is needed.
+ */
+SLR_API int slr_lrs_linear_forward(const slr_layer* layer, const void* x, void* y,
+                           int64_t M, void* workspace, size_t workspace_bytes,
+                           void* stream);
+
+/* --------------------------------------------------- dense -> BSR -- */
+
+/*
+ * Block mask and crow of dense S[n, m] (row-major, dtype) cut into
+ * block_p x block_q blocks — steps 1-3 of dense_to_bsr
+ * (ssalaad/efficient/artifact.py:20-33): a block is kept iff the sum of |s|
+ * over it is > 0, i.e. it holds a nonzero and no NaN.
+ *   mask  device uint8 [(n/block_p) * (m/block_q)]  (1 = kept)
+ *   crow  device int64 [n/block_p + 1]              (crow[0] = 0)
+ * nnz = crow[n/block_p] (the caller reads it back to size the outputs).
+ */
+SLR_API int slr_dense_to_bsr_mask(const void* S, int64_t n, int64_t m, int64_t block_p,
+                          int64_t block_q, int dtype, uint8_t* mask,
+                          int64_t* crow, void* stream);
+
+/*
+ * Steps 4-5 of dense_to_bsr (artifact.py:34-37): col indices of the kept
+ * blocks in row-major order (torch.nonzero order) and their values, copied
+ * bit for bit.
+ *   col     device int64 [nnz]
+ *   values  device, dtype: [nnz, block_p, block_q] if transpose == 0 (the
+ *           artifact / torch.sparse_bsr_tensor layout), or [nnz, block_q,
+ *           block_p] if transpose == 1 (the layer layout, ls_linear.py:92-94)
+ */
+SLR_API int slr_dense_to_bsr_fill(const void* S, int64_t n, int64_t m, int64_t block_p,
+                          int64_t block_q, int dtype, const uint8_t* mask,
+                          const int64_t* crow, int64_t* col, void* values,
+                          int transpose, void* stream);
+
+/* -------------------------------------------------- planning (host) -- */
+
+/*
+ * Host-only.  Writes the block-rows in the order a persistent schedule should
+ * take them: descending work (nnz of the row), ties by row index.  The
+ * reference launches one CTA per active row in index order
+ * (addmm_inplace.py:65); this order feeds heavy (skewed) rows first.
+ */
+SLR_API int slr_plan_row_order(const int32_t* crow_host, int64_t NB, int32_t* order);
+
+/*
+ * Host-only.  Splits NB block-rows into `world` contiguous ranges of nearly
+ * equal cost c_i = nnz_i*block_p*block_q + block_p*rank (the multiply-adds a
+ * row costs per token).  bounds[world+1]: rank p owns block-rows
+ * [bounds[p], bounds[p+1]).  No reference counterpart: the reference runs on
+ * one device.
+ */
+SLR_API int slr_plan_shards(const int32_t* crow_host, int64_t NB, int64_t block_p,
+                    int64_t block_q, int64_t rank, int world, int64_t* bounds);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SLR_B200_H_ */

@@ -1,0 +1,72 @@
+// Internal launcher interface of libslr_b200 (not part of the C ABI).
+#pragma once
+
+#include "common.cuh"
+
+namespace slr {
+
+enum RowMode : int {
+  MODE_FUSED = 0,  // y = sparse + H·Aᵀ + bias, y written
+  MODE_ADDMM = 1,  // y += sparse, y read and written (active rows only)
+};
+
+// One launch over a list of block-rows x token tiles.
+struct RowblockArgs {
+  const void* x = nullptr;      // [M, K]
+  void* y = nullptr;            // [M, N]
+  const void* H = nullptr;      // [M, ldh] low-rank intermediate x·Bᵀ (FUSED)
+  int64_t ldh = 0;
+  const void* A = nullptr;      // [N, r]
+  const void* bias = nullptr;   // [N] or null
+  const int32_t* crow = nullptr;  // [NB+1] or null (no sparse term)
+  const int32_t* col = nullptr;
+  const void* values = nullptr;   // [nnz, bq, bp]
+  const int32_t* rows = nullptr;  // block-row list (null = 0..nrows-1)
+  int64_t nrows = 0;
+  int64_t M = 0, K = 0, N = 0, r = 0, nnz = 0;
+  int bp = 0, bq = 0;
+  int dtype = SLR_F32;
+  int mode = MODE_FUSED;
+};
+
+// ---- SIMT (CUDA-core FFMA) kernels: fp32 parity path and generic fallback.
+// H element type is float when h_f32, else the I/O dtype.
+int launch_simt_h(const void* x, const void* B, void* H, int64_t M, int64_t K, int64_t r,
+                  int64_t ldh, int dtype, bool h_f32, cudaStream_t s);
+int launch_simt_rowblock(const RowblockArgs& a, bool h_f32, cudaStream_t s);
+
+// ---- mma.sync + TMA kernels (16-bit dtypes): small token batches.
+struct HSmallPlan {
+  int tt = 8;        // tokens per CTA (8 * NT)
+  int rt = 0;        // 16-row tiles of r covering ldh
+  int ks = 1;        // K splits
+  int64_t kchunk = 0;
+  int tc = 0;        // token chunks
+  size_t part_floats = 0;
+  size_t counters = 0;
+};
+HSmallPlan plan_h_small(int64_t M, int64_t K, int64_t ldh);
+int launch_h_small(const void* x, const void* B, void* H, float* part, unsigned* counters,
+                   int64_t M, int64_t K, int64_t r, int64_t ldh, const HSmallPlan& plan,
+                   int dtype, cudaStream_t s);
+bool mma_rowblock_supported(int bp, int bq, int64_t K, int64_t r);
+int launch_mma_rowblock(const RowblockArgs& a, bool pdl, cudaStream_t s);
+
+// ---- dense -> BSR conversion.
+int launch_bsr_mask(const void* S, int64_t n, int64_t m, int64_t bp, int64_t bq, int dtype,
+                    uint8_t* mask, int64_t* crow, cudaStream_t s);
+int launch_bsr_fill(const void* S, int64_t n, int64_t m, int64_t bp, int64_t bq, int dtype,
+                    const uint8_t* mask, const int64_t* crow, int64_t* col, void* values,
+                    bool transpose, cudaStream_t s);
+int launch_validate_bsr(const int32_t* crow, int64_t NB, const int32_t* col, int64_t nnz,
+                        int64_t nbk, const int32_t* active, int64_t active_nb, int* flag,
+                        cudaStream_t s);
+
+// Device status words (bounded-wait timeouts) of each translation unit.
+int read_and_clear_status_mma(unsigned* out);
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+inline int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
+inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+}  // namespace slr

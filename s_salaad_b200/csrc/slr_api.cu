@@ -1,0 +1,371 @@
+// C ABI of libslr_b200.so (declared in include/slr_b200.h): argument
+// validation with the reference's error classes, path dispatch, workspace
+// layout, TMA tensor-map encoding and host-side planning.
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cstring>
+#include <mutex>
+#include <numeric>
+#include <string>
+#include <vector>
+
+#include "internal.hpp"
+
+namespace slr {
+
+static thread_local std::string t_last_error;
+
+void set_error(const std::string& msg) { t_last_error = msg; }
+int fail(int status, const std::string& msg) {
+  t_last_error = msg;
+  return status;
+}
+int cuda_fail(cudaError_t e, const char* what) {
+  t_last_error = std::string(what) + ": " + cudaGetErrorName(e) + " (" + cudaGetErrorString(e) + ")";
+  return SLR_ERR_CUDA;
+}
+
+// ------------------------------------------------------------ tensor maps --
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+int make_tmap_2d(CUtensorMap* map, const void* base, int dtype, uint64_t inner, uint64_t outer,
+                 uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer) {
+  auto fn = encode_fn();
+  if (!fn) return fail(SLR_ERR_CUDA, "cuTensorMapEncodeTiled unavailable from the driver");
+  const size_t es = dtype_size(dtype);
+  const size_t box_bytes = box_inner * es;
+  CUtensorMapSwizzle sw = CU_TENSOR_MAP_SWIZZLE_NONE;
+  if (box_bytes == 32) sw = CU_TENSOR_MAP_SWIZZLE_32B;
+  else if (box_bytes == 64) sw = CU_TENSOR_MAP_SWIZZLE_64B;
+  else if (box_bytes == 128) sw = CU_TENSOR_MAP_SWIZZLE_128B;
+  const CUtensorMapDataType dt = dtype == SLR_F32   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                 : dtype == SLR_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                    : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_stride_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(SLR_ERR_INVALID_ARGUMENT, "cuTensorMapEncodeTiled failed (code " + std::to_string(int(r)) +
+                                              "): base/stride must be 16-byte aligned");
+  return SLR_OK;
+}
+
+}  // namespace slr
+
+using namespace slr;
+
+namespace {
+
+bool valid_dtype(int d) { return d == SLR_F32 || d == SLR_F16 || d == SLR_BF16; }
+
+// Workspace layout of slr_lrs_linear_forward for a given (layer, M).
+struct FwdPlan {
+  int path = 0;          // 0 = simt, 1 = mma (small M)
+  int64_t ldh = 0;       // row stride of H
+  size_t h_bytes = 0;
+  size_t part_off = 0, part_bytes = 0;
+  size_t cnt_off = 0, cnt_bytes = 0;
+  size_t total = 0;
+  int row_bp = 0;        // block-row height used by the kernels
+  HSmallPlan hs;
+};
+
+size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+int effective_bp(const slr_layer& L) {
+  if (L.nnz > 0) return int(L.block_p);
+  // Low-rank only: any row blocking works; prefer the tensor-core sizes.
+  for (int b : {64, 32, 16, 8, 4, 2, 1})
+    if (L.out_features % b == 0) return b;
+  return 1;
+}
+
+bool layer_aligned16(const slr_layer& L) {
+  return aligned16(L.A) && aligned16(L.B) && (L.nnz == 0 || aligned16(L.values));
+}
+
+FwdPlan plan_forward(const slr_layer& L, int64_t M, const void* x, const void* y) {
+  FwdPlan p;
+  p.row_bp = effective_bp(L);
+  const bool is16 = L.dtype != SLR_F32;
+  const int bq = L.nnz > 0 ? int(L.block_q) : 16;
+  if (is16 && mma_rowblock_supported(p.row_bp, bq, L.in_features, L.rank) && layer_aligned16(L) &&
+      (x == nullptr || aligned16(x)) && (y == nullptr || aligned16(y)))
+    p.path = 1;
+  p.ldh = L.rank > 0 ? round_up(L.rank, 64) : 0;
+  const size_t hes = (p.path == 0 && !is16) ? 4 : dtype_size(L.dtype);
+  p.h_bytes = align256(size_t(std::max<int64_t>(M, 0)) * p.ldh * hes);
+  p.part_off = p.h_bytes;
+  if (p.path == 1 && L.rank > 0) {
+    p.hs = plan_h_small(M, L.in_features, p.ldh);
+    p.part_bytes = align256(p.hs.part_floats * sizeof(float));
+    p.cnt_bytes = align256(p.hs.counters * sizeof(unsigned));
+  }
+  p.cnt_off = p.part_off + p.part_bytes;
+  p.total = p.cnt_off + p.cnt_bytes;
+  return p;
+}
+
+int check_layer(const slr_layer* L) {
+  if (!L) return fail(SLR_ERR_INVALID_ARGUMENT, "layer is NULL");
+  if (!valid_dtype(L->dtype))
+    return fail(SLR_ERR_UNSUPPORTED_DTYPE, "dtype must be SLR_F32, SLR_F16 or SLR_BF16");
+  if (L->flags != 0) return fail(SLR_ERR_INVALID_ARGUMENT, "flags must be 0");
+  if (L->in_features <= 0 || L->out_features <= 0 || L->rank < 0)
+    return fail(SLR_ERR_INVALID_ARGUMENT, "in_features/out_features must be > 0 and rank >= 0");
+  if (L->rank > 0 && (!L->A || !L->B)) return fail(SLR_ERR_INVALID_ARGUMENT, "A and B are required when rank > 0");
+  if (L->nnz < 0) return fail(SLR_ERR_INVALID_ARGUMENT, "nnz must be >= 0");
+  if (L->nnz > 0) {
+    if (!L->crow || !L->col || !L->values) return fail(SLR_ERR_INVALID_ARGUMENT, "crow/col/values are required when nnz > 0");
+    if (L->block_p <= 0 || L->block_q <= 0) return fail(SLR_ERR_INVALID_ARGUMENT, "block_p/block_q must be > 0");
+    if (L->out_features % L->block_p || L->in_features % L->block_q)
+      return fail(SLR_ERR_INVALID_ARGUMENT, "S shape must be divisible by the block shape");
+    const int mult = L->dtype == SLR_F32 ? 8 : 16;
+    if (L->block_p % mult || L->block_q % mult)
+      return fail(SLR_ERR_UNSUPPORTED, std::string("block dimensions must be divisible by ") + std::to_string(mult));
+    if (L->nnz > int64_t(L->out_features / L->block_p) * (L->in_features / L->block_q))
+      return fail(SLR_ERR_INVALID_ARGUMENT, "nnz exceeds the number of blocks");
+  }
+  return SLR_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int slr_abi_version(void) { return SLR_ABI_VERSION; }
+
+const char* slr_status_string(int status) {
+  switch (status) {
+    case SLR_OK: return "SLR_OK";
+    case SLR_ERR_INVALID_ARGUMENT: return "SLR_ERR_INVALID_ARGUMENT";
+    case SLR_ERR_UNSUPPORTED_DTYPE: return "SLR_ERR_UNSUPPORTED_DTYPE";
+    case SLR_ERR_UNSUPPORTED: return "SLR_ERR_UNSUPPORTED";
+    case SLR_ERR_CUDA: return "SLR_ERR_CUDA";
+    case SLR_ERR_WORKSPACE: return "SLR_ERR_WORKSPACE";
+    case SLR_ERR_BAD_INDEX: return "SLR_ERR_BAD_INDEX";
+    case SLR_ERR_TIMEOUT: return "SLR_ERR_TIMEOUT";
+    default: return "SLR_ERR_UNKNOWN";
+  }
+}
+
+const char* slr_last_error(void) { return t_last_error.c_str(); }
+
+int slr_device_status(int* status_out) {
+  if (!status_out) return fail(SLR_ERR_INVALID_ARGUMENT, "status_out is NULL");
+  SLR_CHECK_CUDA(cudaDeviceSynchronize());
+  unsigned v = 0;
+  int rc = read_and_clear_status_mma(&v);
+  if (rc) return rc;
+  *status_out = (v & SLR_TIMEOUT_BIT) ? SLR_ERR_TIMEOUT : SLR_OK;
+  return SLR_OK;
+}
+
+int slr_bsr_addmm_inplace(void* out, const void* x, int64_t M, int64_t K, const int32_t* crow,
+                          int64_t NB, const int32_t* col, const void* values, int64_t nnz,
+                          int64_t block_p, int64_t block_q, const int32_t* active_rows,
+                          int64_t active_nb, int dtype, void* stream) {
+  if (!valid_dtype(dtype))
+    return fail(SLR_ERR_UNSUPPORTED_DTYPE, "BSR kernel supports float32/float16/bfloat16");
+  if (M < 0 || K < 0 || NB < 0 || nnz < 0 || active_nb < 0)
+    return fail(SLR_ERR_INVALID_ARGUMENT, "sizes must be non-negative");
+  if (block_p <= 0 || block_q <= 0) return fail(SLR_ERR_INVALID_ARGUMENT, "block_p/block_q must be > 0");
+  const int mult = dtype == SLR_F32 ? 8 : 16;
+  if (block_p % mult || block_q % mult)
+    return fail(SLR_ERR_UNSUPPORTED, "block dimensions must be divisible by " + std::to_string(mult));
+  if (K % block_q) return fail(SLR_ERR_INVALID_ARGUMENT, "x K must be divisible by block_q");
+  if (M == 0 || active_nb == 0 || NB == 0) return SLR_OK;
+  if (!out || !x || !crow || !active_rows || (nnz > 0 && (!col || !values)))
+    return fail(SLR_ERR_INVALID_ARGUMENT, "null tensor pointer");
+  RowblockArgs a;
+  a.x = x;
+  a.y = out;
+  a.crow = crow;
+  a.col = col;
+  a.values = values;
+  a.rows = active_rows;
+  a.nrows = active_nb;
+  a.M = M;
+  a.K = K;
+  a.N = NB * block_p;
+  a.nnz = nnz;
+  a.bp = int(block_p);
+  a.bq = int(block_q);
+  a.dtype = dtype;
+  a.mode = MODE_ADDMM;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype != SLR_F32 && nnz > 0 && mma_rowblock_supported(a.bp, a.bq, K, 0) && aligned16(values) &&
+      aligned16(x) && aligned16(out))
+    return launch_mma_rowblock(a, false, s);
+  return launch_simt_rowblock(a, true, s);
+}
+
+int slr_validate_bsr(const int32_t* crow, int64_t NB, const int32_t* col, int64_t nnz, int64_t nbk,
+                     const int32_t* active_rows, int64_t active_nb, void* stream) {
+  if (NB < 0 || nnz < 0 || nbk < 0 || active_nb < 0) return fail(SLR_ERR_INVALID_ARGUMENT, "sizes must be >= 0");
+  if (!crow || (nnz > 0 && !col) || (active_nb > 0 && !active_rows))
+    return fail(SLR_ERR_INVALID_ARGUMENT, "null pointer");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int* flag = nullptr;
+  // The flag lives in pinned host memory mapped into the device: no device allocation.
+  SLR_CHECK_CUDA(cudaHostAlloc(&flag, sizeof(int), cudaHostAllocMapped));
+  *flag = 0;
+  int* dflag = nullptr;
+  cudaError_t e = cudaHostGetDevicePointer(&dflag, flag, 0);
+  int rc = SLR_OK;
+  if (e != cudaSuccess) rc = cuda_fail(e, "cudaHostGetDevicePointer");
+  if (!rc) rc = launch_validate_bsr(crow, NB, col, nnz, nbk, active_rows, active_nb, dflag, s);
+  if (!rc) {
+    e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) rc = cuda_fail(e, "validate_bsr sync");
+  }
+  const int bad = *flag;
+  cudaFreeHost(flag);
+  if (rc) return rc;
+  if (bad) return fail(SLR_ERR_BAD_INDEX, "BSR structure invalid: crow not monotone / crow[0]!=0 / crow[NB]!=nnz, "
+                                          "col out of [0, K/block_q), or a bad active row");
+  return SLR_OK;
+}
+
+size_t slr_lrs_linear_workspace_size(const slr_layer* layer, int64_t M) {
+  if (check_layer(layer) != SLR_OK || M < 0) return 0;
+  return plan_forward(*layer, M, nullptr, nullptr).total;
+}
+
+int slr_lrs_linear_forward(const slr_layer* layer, const void* x, void* y, int64_t M,
+                           void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_layer(layer);
+  if (rc) return rc;
+  const slr_layer& L = *layer;
+  if (M < 0) return fail(SLR_ERR_INVALID_ARGUMENT, "M must be >= 0");
+  if (M == 0) return SLR_OK;
+  if (!x || !y) return fail(SLR_ERR_INVALID_ARGUMENT, "x/y is NULL");
+  const FwdPlan p = plan_forward(L, M, x, y);
+  if (p.total > 0) {
+    if (!workspace) return fail(SLR_ERR_WORKSPACE, "workspace is NULL");
+    if (workspace_bytes < p.total)
+      return fail(SLR_ERR_WORKSPACE, "workspace too small: need " + std::to_string(p.total) + " bytes");
+    if (reinterpret_cast<uintptr_t>(workspace) & 255u) return fail(SLR_ERR_WORKSPACE, "workspace must be 256-byte aligned");
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  void* H = L.rank > 0 ? ws : nullptr;
+
+  RowblockArgs a;
+  a.x = x;
+  a.y = y;
+  a.H = H;
+  a.ldh = p.ldh;
+  a.A = L.A;
+  a.bias = L.bias;
+  a.crow = L.nnz > 0 ? L.crow : nullptr;
+  a.col = L.col;
+  a.values = L.values;
+  a.rows = L.nnz > 0 ? L.row_order : nullptr;
+  a.nrows = L.out_features / p.row_bp;
+  a.M = M;
+  a.K = L.in_features;
+  a.N = L.out_features;
+  a.r = L.rank;
+  a.nnz = L.nnz;
+  a.bp = p.row_bp;
+  a.bq = L.nnz > 0 ? int(L.block_q) : 16;
+  a.dtype = L.dtype;
+  a.mode = MODE_FUSED;
+
+  if (p.path == 1) {
+    bool pdl = false;
+    if (L.rank > 0) {
+      rc = launch_h_small(x, L.B, H, reinterpret_cast<float*>(ws + p.part_off),
+                          reinterpret_cast<unsigned*>(ws + p.cnt_off), M, L.in_features, L.rank, p.ldh, p.hs,
+                          L.dtype, s);
+      if (rc) return rc;
+      pdl = true;
+    }
+    return launch_mma_rowblock(a, pdl, s);
+  }
+  const bool h_f32 = L.dtype == SLR_F32;
+  if (L.rank > 0) {
+    rc = launch_simt_h(x, L.B, H, M, L.in_features, L.rank, p.ldh, L.dtype, h_f32, s);
+    if (rc) return rc;
+  }
+  return launch_simt_rowblock(a, h_f32, s);
+}
+
+int slr_dense_to_bsr_mask(const void* S, int64_t n, int64_t m, int64_t block_p, int64_t block_q,
+                          int dtype, uint8_t* mask, int64_t* crow, void* stream) {
+  if (!valid_dtype(dtype)) return fail(SLR_ERR_UNSUPPORTED_DTYPE, "dense_to_bsr: dtype must be f32/f16/bf16");
+  if (block_p <= 0 || block_q <= 0 || n < 0 || m < 0) return fail(SLR_ERR_INVALID_ARGUMENT, "bad sizes");
+  if (n % block_p || m % block_q)
+    return fail(SLR_ERR_INVALID_ARGUMENT, "shape (" + std::to_string(n) + ", " + std::to_string(m) +
+                                              ") not divisible by block (" + std::to_string(block_p) + ", " +
+                                              std::to_string(block_q) + ")");
+  if (!crow || ((n / block_p) * (m / block_q) > 0 && (!S || !mask)))
+    return fail(SLR_ERR_INVALID_ARGUMENT, "null pointer");
+  return launch_bsr_mask(S, n, m, block_p, block_q, dtype, mask, crow, static_cast<cudaStream_t>(stream));
+}
+
+int slr_dense_to_bsr_fill(const void* S, int64_t n, int64_t m, int64_t block_p, int64_t block_q, int dtype,
+                          const uint8_t* mask, const int64_t* crow, int64_t* col, void* values,
+                          int transpose, void* stream) {
+  if (!valid_dtype(dtype)) return fail(SLR_ERR_UNSUPPORTED_DTYPE, "dense_to_bsr: dtype must be f32/f16/bf16");
+  if (block_p <= 0 || block_q <= 0 || n < 0 || m < 0 || n % block_p || m % block_q)
+    return fail(SLR_ERR_INVALID_ARGUMENT, "bad sizes");
+  if (!crow) return fail(SLR_ERR_INVALID_ARGUMENT, "null pointer");
+  return launch_bsr_fill(S, n, m, block_p, block_q, dtype, mask, crow, col, values, transpose != 0,
+                         static_cast<cudaStream_t>(stream));
+}
+
+int slr_plan_row_order(const int32_t* crow_host, int64_t NB, int32_t* order) {
+  if (NB < 0 || (NB > 0 && (!crow_host || !order))) return fail(SLR_ERR_INVALID_ARGUMENT, "bad arguments");
+  std::vector<int32_t> idx(static_cast<size_t>(NB));
+  std::iota(idx.begin(), idx.end(), 0);
+  std::stable_sort(idx.begin(), idx.end(), [&](int32_t a, int32_t b) {
+    return (crow_host[a + 1] - crow_host[a]) > (crow_host[b + 1] - crow_host[b]);
+  });
+  std::memcpy(order, idx.data(), sizeof(int32_t) * size_t(NB));
+  return SLR_OK;
+}
+
+int slr_plan_shards(const int32_t* crow_host, int64_t NB, int64_t block_p, int64_t block_q, int64_t rank,
+                    int world, int64_t* bounds) {
+  if (world <= 0 || NB < 0 || !bounds || (NB > 0 && !crow_host))
+    return fail(SLR_ERR_INVALID_ARGUMENT, "bad arguments");
+  // Prefix sums of per-row cost; boundary p sits where the prefix first
+  // reaches p/world of the total (ties resolve to the earlier row).
+  std::vector<double> pre(static_cast<size_t>(NB) + 1, 0.0);
+  for (int64_t i = 0; i < NB; ++i)
+    pre[size_t(i) + 1] = pre[size_t(i)] + double(crow_host[i + 1] - crow_host[i]) * double(block_p * block_q) +
+                         double(block_p) * double(rank);
+  const double total = pre[size_t(NB)];
+  bounds[0] = 0;
+  for (int p = 1; p < world; ++p) {
+    const double target = total * p / world;
+    int64_t b = std::lower_bound(pre.begin(), pre.end(), target) - pre.begin();
+    // pick the closer of b-1 and b
+    if (b > 0 && (target - pre[size_t(b - 1)]) <= (pre[size_t(std::min(b, NB))] - target)) b -= 1;
+    b = std::max<int64_t>(b, bounds[p - 1]);
+    bounds[p] = std::min<int64_t>(b, NB);
+  }
+  bounds[world] = NB;
+  return SLR_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,162 @@
+"""S+LR linear modules on B200, with the reference's module API.
+
+Mirrors ``ssalaad/efficient/ls_linear.py`` of S-SALAAD: the same class names,
+constructor arguments, registered buffers (``A``, ``B``, ``bias``,
+``S_crow``, ``S_col``, ``S_values``, ``S_active_rows``, so state dicts are
+interchangeable) and exceptions, with the forward routed to the fused CUDA
+kernels of libslr_b200 instead of F.linear + TileLang:
+
+* :class:`_LRSLinearLR` (reference :47-54) — ``S == 0``: the fused kernel
+  with no sparse term.
+* :class:`_LRSLinearLRBlockBase` (reference :57-104) — BSR buffers.
+* :class:`_LRSLinearLRBlockCUDA` (reference :107-137) — one fused launch pair
+  (``x·Bᵀ`` then sparse + up-projection + bias) instead of pad, two cuBLAS
+  calls, the in-place TileLang kernel and a bias pass.
+* :func:`LRSLinear` (reference :227-285) — the factory.
+
+There is no CPU path: CPU tensors are rejected with ValueError (the
+reference's CPU kernel stays the oracle).  The N:M kind (reference :167-224)
+is not provided.
+"""
+from __future__ import annotations
+
+import torch
+import torch.nn as nn
+
+from .. import ops
+
+
+class _LRSLinearBase(nn.Module):
+    kind: str = ""
+
+    def __init__(self, A: torch.Tensor, B: torch.Tensor, *, in_features: int, out_features: int,
+                 bias: torch.Tensor | None = None) -> None:
+        super().__init__()
+        (n, r) = A.shape
+        (rB, m) = B.shape
+        if rB != r:
+            raise ValueError(f"A.shape[1]={r} must match B.shape[0]={rB}")
+        if (n, m) != (out_features, in_features):
+            raise ValueError(
+                f"L = A·B shape ({n},{m}) must equal (out_features={out_features}, in_features={in_features})")
+        self.in_features = in_features
+        self.out_features = out_features
+        self.r = int(r)
+        self.register_buffer("B", B.contiguous())
+        self.register_buffer("A", A.contiguous())
+        if bias is not None:
+            self.register_buffer("bias", bias.contiguous().to(A.dtype))
+        else:
+            self.bias = None
+        self._desc: ops.LayerDesc | None = None
+
+    # ------------------------------------------------------------ kernels --
+    def _check_device(self) -> None:
+        if not self.A.is_cuda:
+            raise ValueError("s_salaad_b200 layers require CUDA tensors (no CPU path).")
+        if self.A.dtype not in (torch.float16, torch.bfloat16, torch.float32):
+            raise ValueError("s_salaad_b200 layers require fp16, bf16 or fp32.")
+
+    def _desc_tensors(self) -> dict:
+        return dict(A=self.A, B=self.B, bias=self.bias)
+
+    def _layer_desc(self) -> ops.LayerDesc:
+        t = self._desc_tensors()
+        key = tuple(None if v is None else v.data_ptr() for v in t.values())
+        d = self._desc
+        if d is None or d.key != key or d.dtype != self.A.dtype:
+            d = ops.LayerDesc(in_features=self.in_features, out_features=self.out_features,
+                              block_p=getattr(self, "block_p", 0), block_q=getattr(self, "block_q", 0), **t)
+            self._desc = d
+        return d
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        return ops.lrs_linear_forward(self._layer_desc(), x)
+
+
+class _LRSLinearLR(_LRSLinearBase):
+    kind = "lr_only"
+
+    def __init__(self, *args, **kwargs) -> None:
+        super().__init__(*args, **kwargs)
+        self._check_device()
+
+    def extra_repr(self) -> str:
+        return (f"in_features={self.in_features}, out_features={self.out_features}, rank={self.r}, "
+                f"S=zero (skipped), bias={self.bias is not None}")
+
+
+class _LRSLinearLRBlockBase(_LRSLinearBase):
+    """Block-sparse S in BSR layout (same buffers as the reference)."""
+
+    kind = "block_sparse"
+
+    def __init__(self, A: torch.Tensor, B: torch.Tensor, S_sparse: torch.Tensor, *, in_features: int,
+                 out_features: int, bias: torch.Tensor | None, block_p: int, block_q: int) -> None:
+        super().__init__(A, B, in_features=in_features, out_features=out_features, bias=bias)
+        if tuple(S_sparse.shape) != (out_features, in_features):
+            raise ValueError(f"S shape {tuple(S_sparse.shape)} must equal "
+                             f"(out_features, in_features)=({out_features},{in_features})")
+        self.block_p = int(block_p)
+        self.block_q = int(block_q)
+        self.S_nnz = int(S_sparse._nnz())
+        crow = S_sparse.crow_indices()
+        self.register_buffer("S_crow", crow.to(torch.int32).clone())
+        self.register_buffer("S_col", S_sparse.col_indices().to(torch.int32).clone())
+        self.register_buffer("S_values", S_sparse.values().transpose(1, 2).contiguous().clone().to(A.dtype))
+        active = (crow[1:] - crow[:-1]).nonzero(as_tuple=False).squeeze(-1)
+        self.register_buffer("S_active_rows", active.to(torch.int32).clone())
+
+    def extra_repr(self) -> str:
+        return (f"in_features={self.in_features}, out_features={self.out_features}, rank={self.r}, "
+                f"S_nnz={self.S_nnz}, block=({self.block_p}×{self.block_q}), bias={self.bias is not None}")
+
+
+class _LRSLinearLRBlockCUDA(_LRSLinearLRBlockBase):
+    """Fused sm_100a block-sparse + low-rank kernels of libslr_b200."""
+
+    def __init__(self, *args, **kwargs) -> None:
+        super().__init__(*args, **kwargs)
+        if self.S_values.device.type != "cuda":
+            raise ValueError("The B200 block kernel requires CUDA.")
+        mult = 8 if self.S_values.dtype == torch.float32 else 16
+        if self.block_p % mult or self.block_q % mult:
+            raise ValueError(f"The B200 block kernel requires block dimensions divisible by {mult}.")
+        if self.S_values.dtype not in (torch.float16, torch.bfloat16, torch.float32):
+            raise ValueError("The B200 block kernel requires fp16, bf16 or fp32.")
+        # One device-side structure check at load time; the forward trusts it.
+        ops.validate_bsr(self.S_crow, self.S_col, self.in_features // self.block_q, self.S_active_rows)
+        # Heaviest block-rows first (persistent-schedule order).
+        order = ops.plan_row_order(self.S_crow)
+        self.register_buffer("_row_order", torch.from_numpy(order).to(self.S_crow.device), persistent=False)
+
+    def _desc_tensors(self) -> dict:
+        return dict(A=self.A, B=self.B, bias=self.bias, crow=self.S_crow, col=self.S_col,
+                    values=self.S_values, row_order=self._row_order)
+
+
+def LRSLinear(A, B, S_sparse, *, in_features, out_features, bias=None, block_p=None, block_q=None,
+              nm_n=None, nm_m=None):
+    """Compute ``x @ (A @ B + S).T + bias`` with the B200 kernels.
+
+    Same dispatch as the reference factory (ls_linear.py:227-285): LR-only
+    when S has no stored entry, the block kernel for BSR S.  N:M S and CPU
+    tensors are rejected (ValueError) — this package is the CUDA path only.
+    """
+    if S_sparse.layout == torch.strided:
+        nnz = int(torch.count_nonzero(S_sparse))
+    else:
+        nnz = S_sparse._nnz()
+    kwargs = dict(in_features=in_features, out_features=out_features, bias=bias)
+    if not A.is_cuda:
+        raise ValueError("s_salaad_b200.LRSLinear requires CUDA tensors (the CPU path is the reference's).")
+    if nnz == 0:
+        return _LRSLinearLR(A, B, **kwargs)
+    if nm_n is not None:
+        raise ValueError("N:M inference is not provided by s_salaad_b200.")
+    if block_p is None or block_q is None:
+        raise ValueError("Sparse S needs a recorded block shape to pick a kernel.")
+    if S_sparse.layout == torch.strided:
+        from .artifact import dense_to_bsr
+        S_sparse = dense_to_bsr(S_sparse, int(block_p), int(block_q))
+    return _LRSLinearLRBlockCUDA(A, B, S_sparse, block_p=block_p, block_q=block_q, **kwargs)

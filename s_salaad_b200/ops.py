@@ -1,0 +1,258 @@
+"""Tensor-level entry points over the C ABI (CUDA tensors only).
+
+* :func:`bsr_addmm_inplace_`  — in-place ``out += x @ S.T`` for BSR S; the
+  implementation behind the ``ssalaad::tilelang_bsr_addmm_inplace_dense_``
+  operator (reference: ssalaad/tilelang_sparse/addmm_inplace.py:88-141).
+* :class:`LayerDesc` / :func:`lrs_linear_forward` — the fused S+LR forward
+  ``y = x @ S.T + (x @ B.T) @ A.T + bias`` (reference:
+  ssalaad/efficient/ls_linear.py:124-137).
+* :func:`dense_to_bsr_cuda` — bit-exact GPU ``dense_to_bsr``
+  (reference: ssalaad/efficient/artifact.py:20-37).
+* :func:`plan_row_order`, :func:`plan_shards` — host planning helpers.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import torch
+
+from . import _lib
+
+_DTYPES = {torch.float32: _lib.SLR_F32, torch.float16: _lib.SLR_F16, torch.bfloat16: _lib.SLR_BF16}
+
+
+def slr_dtype(dtype: torch.dtype) -> int:
+    try:
+        return _DTYPES[dtype]
+    except KeyError:
+        raise TypeError(f"s_salaad_b200 supports float32/float16/bfloat16, got {dtype}") from None
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _require_cuda(name: str, t: torch.Tensor) -> None:
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor (s_salaad_b200 has no CPU path)")
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+class _DeviceGuard:
+    """Make `device` current for the C call (cheap when it already is)."""
+
+    __slots__ = ("dev", "prev")
+
+    def __init__(self, device: torch.device):
+        self.dev = device.index if device.index is not None else torch.cuda.current_device()
+        self.prev = None
+
+    def __enter__(self):
+        cur = torch.cuda.current_device()
+        if cur != self.dev:
+            self.prev = cur
+            torch.cuda.set_device(self.dev)
+
+    def __exit__(self, *exc):
+        if self.prev is not None:
+            torch.cuda.set_device(self.prev)
+
+
+# --------------------------------------------------------------- addmm --
+
+def bsr_addmm_inplace_(out, x, crow_indices, col_indices, values, active_rows) -> None:
+    """In place ``out += x @ S.T`` (S in BSR with values ``[nnz, bq, bp]``).
+
+    Same contract as ``ssalaad::tilelang_bsr_addmm_inplace_dense_``
+    (addmm_inplace.py:130-141): ``out``/``x`` contiguous 2-D of one dtype,
+    int32 ``crow``/``col``/``active_rows``, all on one CUDA device; only the
+    block-rows in ``active_rows`` are touched.  Unlike the reference, M needs
+    no padding, and float32 is accepted (bit-identical to the AVX2 kernel).
+    """
+    lib = _lib.load()
+    dtype = slr_dtype(out.dtype)
+    if x.dtype != out.dtype or values.dtype != out.dtype:
+        raise TypeError(f"out/x/values dtypes differ: {out.dtype}, {x.dtype}, {values.dtype}")
+    for name, t in (("out", out), ("x", x), ("crow", crow_indices), ("col", col_indices),
+                    ("values", values), ("active_rows", active_rows)):
+        _require_cuda(name, t)
+        if not t.is_contiguous():
+            raise ValueError(f"{name} must be contiguous")
+    for name, t in (("crow", crow_indices), ("col", col_indices), ("active_rows", active_rows)):
+        if t.dtype != torch.int32:
+            raise TypeError(f"{name} must be int32, got {t.dtype}")
+    if out.dim() != 2 or x.dim() != 2 or values.dim() != 3:
+        raise ValueError("out and x must be 2-D and values 3-D (nnz, block_q, block_p)")
+    M, K = x.shape
+    bq, bp = int(values.shape[1]), int(values.shape[2])
+    NB = crow_indices.numel() - 1
+    if out.shape[0] != M or out.shape[1] != NB * bp:
+        raise ValueError(f"out shape {tuple(out.shape)} does not match ({M}, {NB * bp})")
+    if values.shape[0] != col_indices.numel():
+        raise ValueError("values nnz must match col nnz")
+    with _DeviceGuard(out.device):
+        rc = lib.slr_bsr_addmm_inplace(
+            out.data_ptr(), x.data_ptr(), M, K, crow_indices.data_ptr(), NB,
+            col_indices.data_ptr(), values.data_ptr(), values.shape[0], bp, bq,
+            active_rows.data_ptr(), active_rows.numel(), dtype, _stream(out.device))
+    _lib.check(rc, "bsr_addmm_inplace_")
+
+
+def validate_bsr(crow, col, nbk: int, active_rows) -> None:
+    """Device-side structure check (raises ValueError on a bad index)."""
+    lib = _lib.load()
+    with _DeviceGuard(crow.device):
+        rc = lib.slr_validate_bsr(crow.data_ptr(), crow.numel() - 1, col.data_ptr(), col.numel(), nbk,
+                                  active_rows.data_ptr(), active_rows.numel(), _stream(crow.device))
+    _lib.check(rc, "validate_bsr")
+
+
+# ------------------------------------------------------------ S+LR layer --
+
+class LayerDesc:
+    """Owns an ``slr_layer`` descriptor plus the layer's workspace.
+
+    The descriptor holds raw device pointers of the tensors given here; call
+    :meth:`refresh` (or construct anew) whenever those tensors move.
+    """
+
+    def __init__(self, *, A, B, bias=None, crow=None, col=None, values=None, row_order=None,
+                 in_features: int, out_features: int, block_p: int = 0, block_q: int = 0):
+        self.tensors = dict(A=A, B=B, bias=bias, crow=crow, col=col, values=values, row_order=row_order)
+        self.in_features = int(in_features)
+        self.out_features = int(out_features)
+        self.block_p = int(block_p)
+        self.block_q = int(block_q)
+        self.struct = _lib.SlrLayer()
+        self._ws: torch.Tensor | None = None
+        self.refresh()
+
+    def refresh(self, **tensors) -> None:
+        self.tensors.update(tensors)
+        t = self.tensors
+        A = t["A"]
+        s = self.struct
+        s.in_features = self.in_features
+        s.out_features = self.out_features
+        s.rank = int(A.shape[1])
+        nnz = 0 if t["col"] is None else int(t["col"].numel())
+        s.nnz = nnz
+        s.block_p = self.block_p if nnz else 0
+        s.block_q = self.block_q if nnz else 0
+        s.crow = _ptr(t["crow"]) if nnz else None
+        s.col = _ptr(t["col"]) if nnz else None
+        s.values = _ptr(t["values"]) if nnz else None
+        s.row_order = _ptr(t["row_order"]) if nnz else None
+        s.A = A.data_ptr() if A.numel() else None
+        s.B = t["B"].data_ptr() if t["B"].numel() else None
+        s.bias = _ptr(t["bias"])
+        s.dtype = slr_dtype(A.dtype)
+        s.flags = 0
+        self.device = A.device
+        self.dtype = A.dtype
+        self.key = tuple(_ptr(v) for v in t.values())
+
+    def workspace_bytes(self, M: int) -> int:
+        return int(_lib.load().slr_lrs_linear_workspace_size(ctypes.byref(self.struct), M))
+
+    def workspace(self, M: int) -> torch.Tensor | None:
+        need = self.workspace_bytes(M)
+        if need == 0:
+            return None
+        if self._ws is None or self._ws.numel() < need or self._ws.device != self.device:
+            # zero-filled once: the library keeps its split-K counters at zero
+            self._ws = torch.zeros(need, dtype=torch.uint8, device=self.device)
+        return self._ws
+
+    def forward(self, x2: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        lib = _lib.load()
+        M = x2.shape[0]
+        if out is None:
+            out = torch.empty(M, self.out_features, dtype=self.dtype, device=self.device)
+        ws = self.workspace(M)
+        with _DeviceGuard(self.device):
+            rc = lib.slr_lrs_linear_forward(
+                ctypes.byref(self.struct), x2.data_ptr(), out.data_ptr(), M,
+                None if ws is None else ws.data_ptr(), 0 if ws is None else ws.numel(),
+                _stream(self.device))
+        _lib.check(rc, "lrs_linear_forward")
+        return out
+
+
+def lrs_linear_forward(desc: LayerDesc, x: torch.Tensor) -> torch.Tensor:
+    """``y = x @ S.T + (x @ B.T) @ A.T + bias`` for x of shape ``[..., in]``."""
+    _require_cuda("x", x)
+    if x.dtype != desc.dtype:
+        raise TypeError(f"x dtype {x.dtype} does not match the layer dtype {desc.dtype}")
+    shape = x.shape
+    if shape[-1] != desc.in_features:
+        raise ValueError(f"x last dim {shape[-1]} != in_features {desc.in_features}")
+    x2 = x.reshape(-1, shape[-1])
+    if not x2.is_contiguous():
+        x2 = x2.contiguous()
+    return desc.forward(x2).reshape(*shape[:-1], desc.out_features)
+
+
+# ---------------------------------------------------------- dense -> BSR --
+
+def dense_to_bsr_cuda(S: torch.Tensor, block_p: int, block_q: int, *, transpose: bool = False,
+                      index_dtype=torch.int64):
+    """GPU ``dense_to_bsr`` (artifact.py:20-37), bit-exact.
+
+    Returns ``(crow, col, values)`` on S's device: int64 indices (or
+    ``index_dtype``) and values ``[nnz, bp, bq]`` (``[nnz, bq, bp]`` when
+    ``transpose``).  Raises ValueError like the reference when the shape is
+    not divisible by the block shape.
+    """
+    lib = _lib.load()
+    _require_cuda("S", S)
+    if S.dim() != 2:
+        raise ValueError("S must be 2-D")
+    n, m = S.shape
+    if n % block_p or m % block_q:
+        raise ValueError(f"shape ({n}, {m}) not divisible by block ({block_p}, {block_q})")
+    S = S.contiguous()
+    dtype = slr_dtype(S.dtype)
+    rb, cb = n // block_p, m // block_q
+    dev = S.device
+    mask = torch.empty(rb * cb, dtype=torch.uint8, device=dev)
+    crow = torch.empty(rb + 1, dtype=torch.int64, device=dev)
+    stream = _stream(dev)
+    with _DeviceGuard(dev):
+        _lib.check(lib.slr_dense_to_bsr_mask(S.data_ptr(), n, m, block_p, block_q, dtype,
+                                             mask.data_ptr(), crow.data_ptr(), stream), "dense_to_bsr")
+        nnz = int(crow[-1].item())
+        col = torch.empty(nnz, dtype=torch.int64, device=dev)
+        shape = (nnz, block_q, block_p) if transpose else (nnz, block_p, block_q)
+        values = torch.empty(shape, dtype=S.dtype, device=dev)
+        _lib.check(lib.slr_dense_to_bsr_fill(S.data_ptr(), n, m, block_p, block_q, dtype, mask.data_ptr(),
+                                             crow.data_ptr(), col.data_ptr(), values.data_ptr(),
+                                             int(transpose), stream), "dense_to_bsr")
+    if index_dtype != torch.int64:
+        crow, col = crow.to(index_dtype), col.to(index_dtype)
+    return crow, col, values
+
+
+# ---------------------------------------------------------------- plans --
+
+def plan_row_order(crow) -> np.ndarray:
+    """Block-rows heaviest first (ties by index), from the host planner."""
+    c = np.ascontiguousarray(np.asarray(crow.cpu() if hasattr(crow, "cpu") else crow), dtype=np.int32)
+    NB = c.shape[0] - 1
+    out = np.empty(max(NB, 0), dtype=np.int32)
+    _lib.check(_lib.load().slr_plan_row_order(c.ctypes.data, NB, out.ctypes.data), "plan_row_order")
+    return out
+
+
+def plan_shards(crow, block_p: int, block_q: int, rank: int, world: int) -> np.ndarray:
+    """Contiguous, cost-balanced block-row ranges: bounds[world+1]."""
+    c = np.ascontiguousarray(np.asarray(crow.cpu() if hasattr(crow, "cpu") else crow), dtype=np.int32)
+    NB = c.shape[0] - 1
+    out = np.empty(world + 1, dtype=np.int64)
+    _lib.check(_lib.load().slr_plan_shards(c.ctypes.data, NB, block_p, block_q, rank, world, out.ctypes.data),
+               "plan_shards")
+    return out

@@ -1,0 +1,385 @@
+"""GPU parity of libslr_b200 against the CPU oracle (and the golden vectors).
+
+Tolerances (stated per test):
+  * fp32 in-place addmm: bit-exact with the reference AVX2 kernel (same FMA
+    order per output element).
+  * fp32 fused layer: |y - y_ref| <= 1e-5 * |y_ref| + 1e-5 * RMS(y_ref).
+  * fp16/bf16: max |y - y_ref| <= 2e-2 * RMS(y_ref), y_ref = the fp32 CPU
+    oracle on fp32 copies of the 16-bit tensors.
+All calls go through the C ABI (ctypes) of libslr_b200.so.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import load_golden
+from s_salaad_b200 import ops, workloads
+from s_salaad_b200.efficient import LRSLinear, _LRSLinearLR, _LRSLinearLRBlockCUDA, dense_to_bsr
+
+pytestmark = pytest.mark.gpu
+
+BF16_TOL = 2e-2
+
+
+def rms(t: torch.Tensor) -> float:
+    return float(t.float().pow(2).mean().sqrt())
+
+
+def assert_16bit_close(y: torch.Tensor, ref: torch.Tensor, tol: float = BF16_TOL):
+    y = y.float().cpu()
+    ref = ref.float().cpu()
+    assert torch.isfinite(y).all()
+    err = float((y - ref).abs().max())
+    assert err <= tol * rms(ref) + 1e-6, f"max abs err {err:.3e} > {tol} * RMS {rms(ref):.3e}"
+
+
+def assert_f32_close(y: torch.Tensor, ref: torch.Tensor):
+    y = y.cpu()
+    ref = ref.cpu()
+    torch.testing.assert_close(y, ref, rtol=1e-5, atol=1e-5 * rms(ref))
+
+
+def random_layer(n, k, bp, bq, r, density, seed, bias=True, value_std=0.02, lr_std=0.02):
+    crow, col = workloads.bernoulli_structure(n // bp, k // bq, density, seed)
+    return workloads.LayerSpec(f"rand{seed}", n, k, r, bp, bq, crow, col, seed + 7, value_std, lr_std,
+                               0.01 if bias else None)
+
+
+def desc_for(t: dict, spec: workloads.LayerSpec, device, dtype, row_order=True, bias=True) -> ops.LayerDesc:
+    d = {k: (v.to(device) if v is not None else None) for k, v in t.items()}
+    A, B = d["A"].to(dtype), d["B"].to(dtype)
+    order = None
+    if spec.nnz and row_order:
+        order = torch.from_numpy(ops.plan_row_order(spec.crow.astype(np.int32))).to(device)
+    return ops.LayerDesc(A=A, B=B, bias=d["bias"].to(dtype) if (bias and d["bias"] is not None) else None,
+                         crow=d["S_crow"] if spec.nnz else None, col=d["S_col"] if spec.nnz else None,
+                         values=d["S_values"].to(dtype).contiguous() if spec.nnz else None, row_order=order,
+                         in_features=spec.in_features, out_features=spec.out_features,
+                         block_p=spec.block_p, block_q=spec.block_q)
+
+
+def oracle_layer(oracle, t, x, bias=True):
+    f = lambda v: None if v is None else v.float().cpu()  # noqa: E731
+    return oracle.lrs_forward_f32(f(x), f(t["A"]), f(t["B"]), t["S_crow"].cpu(), t["S_col"].cpu(),
+                                  f(t["S_values"]), t["S_active_rows"].cpu(), f(t["bias"]) if bias else None)
+
+
+# ------------------------------------------------------- in-place addmm --
+
+@pytest.mark.parametrize("block", [8, 16, 32, 64])
+def test_addmm_f32_bit_exact_with_reference_golden(cuda, block):
+    g = load_golden(f"avx2_block{block}")
+    T = lambda a: torch.from_numpy(a).to(cuda)  # noqa: E731
+    out = T(g["out0"].copy())
+    ops.bsr_addmm_inplace_(out, T(g["x"]), T(g["crow"]), T(g["col"]), T(g["values"]), T(g["active_rows"]))
+    torch.cuda.synchronize()
+    assert np.array_equal(out.cpu().numpy().view(np.uint32), g["out_acc"].view(np.uint32))
+
+
+@pytest.mark.parametrize("bp,bq", [(8, 16), (16, 8), (24, 40), (64, 64)])
+@pytest.mark.parametrize("M", [1, 3, 37])
+def test_addmm_f32_bit_exact_with_oracle(cuda, oracle, bp, bq, M):
+    spec = random_layer(4 * bp, 5 * bq, bp, bq, 8, 0.5, seed=bp * 31 + bq + M)
+    t = spec.tensors("cpu", torch.float32)
+    x = workloads.tokens(M, spec.in_features, seed=M)
+    out0 = workloads.tokens(M, spec.out_features, seed=M + 1)
+    ref = out0.numpy().copy()
+    oracle.bsr_addmm_f32_(ref, x, t["S_crow"], t["S_col"], t["S_values"], t["S_active_rows"])
+    out = out0.to(cuda)
+    ops.bsr_addmm_inplace_(out, x.to(cuda), t["S_crow"].to(cuda), t["S_col"].to(cuda), t["S_values"].to(cuda),
+                           t["S_active_rows"].to(cuda))
+    assert np.array_equal(out.cpu().numpy().view(np.uint32), ref.view(np.uint32))
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("bp,bq", [(16, 16), (32, 32), (64, 64), (16, 32), (32, 16), (64, 16), (16, 64),
+                                   (32, 128), (128, 32)])
+@pytest.mark.parametrize("M", [1, 7, 64, 130])
+def test_addmm_16bit_matches_oracle(cuda, oracle, dtype, bp, bq, M):
+    spec = random_layer(6 * bp, 5 * bq, bp, bq, 8, 0.4, seed=bp + 3 * bq + M)
+    t = spec.tensors("cpu", dtype)
+    x = workloads.tokens(M, spec.in_features, seed=M, dtype=dtype)
+    out0 = workloads.tokens(M, spec.out_features, seed=M + 1, dtype=dtype)
+    ref = out0.float().numpy().copy()
+    oracle.bsr_addmm_f32_(ref, x.float(), t["S_crow"], t["S_col"], t["S_values"].float(), t["S_active_rows"])
+    out = out0.to(cuda)
+    ops.bsr_addmm_inplace_(out, x.to(cuda), t["S_crow"].to(cuda), t["S_col"].to(cuda), t["S_values"].to(cuda),
+                           t["S_active_rows"].to(cuda))
+    assert_16bit_close(out, torch.from_numpy(ref))
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_addmm_leaves_empty_block_rows_untouched(cuda, dtype):
+    g = load_golden("avx2_empty_rows")
+    T = lambda a: torch.from_numpy(a).to(cuda)  # noqa: E731
+    out = torch.full((3, 48), 7.0, device=cuda, dtype=dtype)
+    ops.bsr_addmm_inplace_(out, T(g["x"]).to(dtype), T(g["crow"]), T(g["col"]), T(g["values"]).to(dtype),
+                           T(g["active_rows"]))
+    assert torch.equal(out[:, :32].float().cpu(), torch.full((3, 32), 7.0))
+    if dtype == torch.float32:
+        assert np.array_equal(out.cpu().numpy().view(np.uint32), g["out"].view(np.uint32))
+
+
+def test_addmm_rejects_bad_arguments(cuda):
+    out = torch.zeros(4, 32, device=cuda, dtype=torch.bfloat16)
+    x = torch.zeros(4, 32, device=cuda, dtype=torch.float16)
+    crow = torch.zeros(3, dtype=torch.int32, device=cuda)
+    col = torch.zeros(0, dtype=torch.int32, device=cuda)
+    vals = torch.zeros(0, 16, 16, device=cuda, dtype=torch.bfloat16)
+    with pytest.raises(TypeError):
+        ops.bsr_addmm_inplace_(out, x, crow, col, vals, crow[:1])
+    with pytest.raises(TypeError):
+        ops.bsr_addmm_inplace_(out.double(), x.double(), crow, col, vals.double(), crow[:1])
+
+
+# ------------------------------------------------------------ fused layer --
+
+def test_fused_f32_cfg1_full_size(cuda, oracle):
+    spec = workloads.cfg1_layer(0)
+    t = spec.tensors("cpu", torch.float32)
+    x = workloads.tokens(256, spec.in_features, seed=9)
+    ref = oracle_layer(oracle, t, x)
+    y = ops.lrs_linear_forward(desc_for(t, spec, cuda, torch.float32), x.to(cuda))
+    assert_f32_close(y, ref)
+
+
+def test_fused_f32_matches_reference_golden(cuda):
+    g = load_golden("lrs_cfg1_T32")
+    spec = workloads.cfg1_layer(0)
+    t = spec.tensors("cpu", torch.float32)
+    x = workloads.tokens(32, spec.in_features, seed=5)
+    y = ops.lrs_linear_forward(desc_for(t, spec, cuda, torch.float32), x.to(cuda))
+    assert_f32_close(y, torch.from_numpy(g["y"]))
+
+
+def test_fused_bf16_matches_reference_golden(cuda):
+    g = load_golden("lrs_b32_bf16vals")
+    crow, col = workloads.bernoulli_structure(256 // 32, 512 // 32, 0.3, seed=21)
+    spec = workloads.LayerSpec("b32", 256, 512, 64, 32, 32, crow, col, seed=22)
+    t = spec.tensors("cpu", torch.bfloat16)
+    x = workloads.tokens(16, 512, seed=23, dtype=torch.bfloat16)
+    y = ops.lrs_linear_forward(desc_for(t, spec, cuda, torch.bfloat16), x.to(cuda))
+    assert_16bit_close(y, torch.from_numpy(g["y"]))
+
+
+FUSED_SHAPES = [
+    # n, k, bp, bq, r, density
+    (256, 192, 16, 16, 64, 0.5),
+    (384, 256, 32, 32, 256, 0.3),
+    (512, 512, 64, 64, 512, 0.2),
+    (256, 512, 16, 32, 32, 0.3),
+    (192, 256, 64, 16, 48, 0.4),
+    (256, 256, 32, 64, 24, 0.5),   # r % 16 != 0
+]
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("shape", FUSED_SHAPES, ids=lambda s: "x".join(map(str, s)))
+@pytest.mark.parametrize("T", [1, 5, 16, 33, 64, 100, 257])
+def test_fused_16bit_matches_oracle(cuda, oracle, dtype, shape, T):
+    n, k, bp, bq, r, dens = shape
+    spec = random_layer(n, k, bp, bq, r, dens, seed=n + k + r + T)
+    t = spec.tensors("cpu", dtype)
+    x = workloads.tokens(T, k, seed=T, dtype=dtype)
+    ref = oracle_layer(oracle, t, x)
+    y = ops.lrs_linear_forward(desc_for(t, spec, cuda, dtype), x.to(cuda))
+    assert y.shape == (T, n)
+    assert_16bit_close(y, ref)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("T", [1, 40, 300])
+def test_fused_fallback_shapes(cuda, oracle, dtype, T):
+    """Shapes outside the tensor-core kernels' range take the generic path:
+    rank 4 (the reference bundle test's rank), 128x128 blocks, no bias."""
+    for (n, k, bp, bq, r) in ((64, 96, 16, 16, 4), (256, 256, 128, 128, 16)):
+        spec = random_layer(n, k, bp, bq, r, 0.5, seed=r + T, bias=False)
+        t = spec.tensors("cpu", dtype)
+        x = workloads.tokens(T, k, seed=T, dtype=dtype)
+        ref = oracle_layer(oracle, t, x, bias=False)
+        y = ops.lrs_linear_forward(desc_for(t, spec, cuda, dtype, bias=False), x.to(cuda))
+        (assert_f32_close if dtype == torch.float32 else assert_16bit_close)(y, ref)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("T", [1, 24, 200])
+def test_low_rank_only_layer(cuda, oracle, dtype, T):
+    """nnz == 0: _LRSLinearLR (reference ls_linear.py:47-54)."""
+    spec = random_layer(192, 128, 16, 16, 32, 0.0, seed=3)
+    assert spec.nnz == 0
+    t = spec.tensors("cpu", dtype)
+    x = workloads.tokens(T, 128, seed=T, dtype=dtype)
+    ref = oracle.lr_forward_f32(x.float(), t["A"].float(), t["B"].float(), t["bias"].float())
+    y = ops.lrs_linear_forward(desc_for(t, spec, cuda, dtype), x.to(cuda))
+    (assert_f32_close if dtype == torch.float32 else assert_16bit_close)(y, ref)
+
+
+def test_fused_without_row_order_and_deterministic(cuda):
+    spec = random_layer(512, 512, 32, 32, 64, 0.3, seed=5)
+    t = spec.tensors("cpu", torch.bfloat16)
+    x = workloads.tokens(48, 512, seed=1, dtype=torch.bfloat16).to(cuda)
+    d1 = desc_for(t, spec, cuda, torch.bfloat16, row_order=True)
+    d2 = desc_for(t, spec, cuda, torch.bfloat16, row_order=False)
+    y1 = ops.lrs_linear_forward(d1, x)
+    y1b = ops.lrs_linear_forward(d1, x)
+    y2 = ops.lrs_linear_forward(d2, x)
+    assert torch.equal(y1, y1b)  # run-to-run deterministic
+    assert torch.equal(y1, y2)   # schedule order does not change the arithmetic
+
+
+def test_forward_captures_in_cuda_graph(cuda):
+    spec = random_layer(512, 512, 16, 16, 32, 0.1, seed=8)
+    t = spec.tensors("cpu", torch.bfloat16)
+    d = desc_for(t, spec, cuda, torch.bfloat16)
+    x = workloads.tokens(1, 512, seed=2, dtype=torch.bfloat16).to(cuda)
+    y_eager = ops.lrs_linear_forward(d, x)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        out = torch.empty_like(y_eager)
+        d.forward(x, out)  # warm-up allocates the workspace outside capture
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            d.forward(x, out)
+    torch.cuda.current_stream().wait_stream(s)
+    out.zero_()
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(out, y_eager)
+
+
+# -------------------------------------------------- full-size properties --
+
+def torch_ref(t: dict, spec, x: torch.Tensor) -> torch.Tensor:
+    """Plain PyTorch fp32 reference of the same op (on the GPU, full size)."""
+    S = torch.zeros(spec.out_features, spec.in_features, device=x.device)
+    vals = t["values_pq"].to(x.device).float()
+    rows = torch.from_numpy(np.repeat(np.arange(spec.nb), np.diff(spec.crow))).to(x.device)
+    cols = torch.from_numpy(spec.col).to(x.device)
+    bp, bq = spec.block_p, spec.block_q
+    Sb = S.view(spec.nb, bp, spec.in_features // bq, bq).permute(0, 2, 1, 3)
+    Sb[rows, cols] = vals
+    S = Sb.permute(0, 2, 1, 3).reshape(spec.out_features, spec.in_features)
+    xf = x.float()
+    y = xf @ S.T + (xf @ t["B"].to(x.device).float().T) @ t["A"].to(x.device).float().T
+    if t["bias"] is not None:
+        y = y + t["bias"].to(x.device).float()
+    return y
+
+
+@pytest.mark.parametrize("cfg,T", [("cfg3", 1), ("cfg3", 16), ("cfg3", 128), ("cfg3", 2048), ("cfg5", 1),
+                                   ("cfg5", 32), ("cfg4", 4096)])
+def test_full_size_configs_match_torch_fp32(cuda, cfg, T):
+    specs = workloads.layer_set(cfg)
+    if cfg == "cfg4":
+        specs = [specs[0], specs[6]]  # one 4096x4096 and the 4096x11008 down projection
+    for i, spec in enumerate(specs):
+        t = spec.tensors(cuda, torch.bfloat16)
+        x = workloads.tokens(T, spec.in_features, seed=i, device=cuda, dtype=torch.bfloat16)
+        y = ops.lrs_linear_forward(desc_for(t, spec, cuda, torch.bfloat16), x)
+        assert_16bit_close(y, torch_ref(t, spec, x))
+
+
+# ------------------------------------------------------------ conversion --
+
+def test_dense_to_bsr_gpu_is_bit_exact_with_reference(cuda):
+    from conftest import GOLDEN
+
+    with np.load(GOLDEN / "dense_to_bsr.npz") as z:
+        cases = {}
+        for key in z.files:
+            case, f = key.split("__")
+            cases.setdefault(case, {})[f] = z[key]
+    for case, g in cases.items():
+        S = g["S"]
+        if case.startswith("d2b_bf16"):
+            St = torch.from_numpy(S.view(np.int16).copy()).view(torch.bfloat16)
+        else:
+            St = torch.from_numpy(S)
+        if g["values"].ndim == 3 and g["values"].shape[0]:
+            bp, bq = g["values"].shape[1:]
+        elif case.endswith(("zero", "full")):
+            bp, bq = 16, 16
+        else:
+            bp, bq = map(int, case.split("_")[-1].split("x"))
+        crow, col, vals = ops.dense_to_bsr_cuda(St.to(cuda), int(bp), int(bq))
+        assert np.array_equal(crow.cpu().numpy(), g["crow"]), case
+        assert np.array_equal(col.cpu().numpy(), g["col"]), case
+        v = vals.cpu()
+        v = v.view(torch.int16).numpy().view(np.uint16) if v.dtype == torch.bfloat16 else v.numpy()
+        assert np.array_equal(v.view(np.uint8), np.ascontiguousarray(g["values"]).view(np.uint8)), case
+        bsr = dense_to_bsr(St.to(cuda), int(bp), int(bq))
+        assert bsr.layout == torch.sparse_bsr and torch.equal(bsr.crow_indices().cpu(), torch.from_numpy(g["crow"]))
+
+
+@pytest.mark.parametrize("n,m,bp,bq", [(8192, 8192, 16, 16), (11008, 4096, 64, 64), (2048, 5504, 32, 32)])
+def test_dense_to_bsr_large_matches_torch(cuda, n, m, bp, bq):
+    """At full size: identical to Tensor.to_sparse_bsr (which the reference's
+    dense_to_bsr equals) on a masked random matrix."""
+    g = torch.Generator(device=cuda).manual_seed(0)
+    keep = torch.rand(n // bp, m // bq, device=cuda, generator=g) < 0.2
+    S = torch.randn(n, m, device=cuda, generator=g, dtype=torch.bfloat16)
+    S = S * keep.repeat_interleave(bp, 0).repeat_interleave(bq, 1)
+    crow, col, vals = ops.dense_to_bsr_cuda(S, bp, bq)
+    ref = S.to_sparse_bsr(blocksize=(bp, bq))
+    assert torch.equal(crow, ref.crow_indices()) and torch.equal(col, ref.col_indices())
+    assert torch.equal(vals.view(torch.int16), ref.values().view(torch.int16))
+
+
+# ------------------------------------------------------------- module API --
+
+def test_module_api_mirrors_reference(cuda, oracle):
+    spec = random_layer(128, 96, 16, 16, 8, 0.5, seed=4)
+    t = spec.tensors("cpu", torch.bfloat16)
+    S = spec.dense_S(t).to(cuda)
+    layer = LRSLinear(t["A"].to(cuda), t["B"].to(cuda), dense_to_bsr(S, 16, 16), in_features=96,
+                      out_features=128, bias=t["bias"].to(cuda), block_p=16, block_q=16)
+    assert isinstance(layer, _LRSLinearLRBlockCUDA)
+    assert set(layer.state_dict()) == {"A", "B", "bias", "S_crow", "S_col", "S_values", "S_active_rows"}
+    assert torch.equal(layer.S_values.cpu(), t["S_values"])
+    assert torch.equal(layer.S_active_rows.cpu(), t["S_active_rows"])
+    x = workloads.tokens(10, 96, seed=3, dtype=torch.bfloat16)
+    y = layer(x.to(cuda).view(2, 5, 96))
+    assert y.shape == (2, 5, 128)
+    assert_16bit_close(y.view(10, 128), oracle_layer(oracle, t, x))
+    lr = LRSLinear(t["A"].to(cuda), t["B"].to(cuda), torch.zeros(128, 96, device=cuda).to_sparse_bsr((16, 16)),
+                   in_features=96, out_features=128, block_p=16, block_q=16)
+    assert isinstance(lr, _LRSLinearLR)
+
+
+def test_module_api_errors(cuda):
+    A = torch.randn(64, 8, device=cuda, dtype=torch.bfloat16)
+    B = torch.randn(8, 96, device=cuda, dtype=torch.bfloat16)
+    S = torch.zeros(64, 96, device=cuda, dtype=torch.bfloat16)
+    S[:8, 8:16] = 1.0
+    with pytest.raises(ValueError, match="divisible by 16"):
+        LRSLinear(A, B, S.to_sparse_bsr((8, 8)), in_features=96, out_features=64, block_p=8, block_q=8)
+    with pytest.raises(ValueError, match="must match"):
+        LRSLinear(A, B[:4], S.to_sparse_bsr((16, 16)), in_features=96, out_features=64, block_p=16, block_q=16)
+    with pytest.raises(ValueError, match="block shape"):
+        LRSLinear(A, B, S.to_sparse_bsr((16, 16)), in_features=96, out_features=64)
+    bad = S.to_sparse_bsr((16, 16))
+    col = bad.col_indices().clone()
+    col[0] = 17  # out of range: caught once at construction
+    bad = torch.sparse_bsr_tensor(bad.crow_indices(), col, bad.values(), size=(64, 96))
+    with pytest.raises(ValueError, match="BSR structure invalid"):
+        LRSLinear(A, B, bad, in_features=96, out_features=64, block_p=16, block_q=16)
+
+
+def test_reference_operator_name(cuda, oracle):
+    from s_salaad_b200.cuda_sparse import get_tuned_config, register_reference_op
+
+    register_reference_op()
+    spec = random_layer(128, 128, 32, 32, 8, 0.5, seed=2)
+    t = spec.tensors("cpu", torch.bfloat16)
+    x = workloads.tokens(9, 128, seed=1, dtype=torch.bfloat16)
+    y0 = workloads.tokens(9, 128, seed=2, dtype=torch.bfloat16)
+    ref = y0.float().numpy().copy()
+    oracle.bsr_addmm_f32_(ref, x.float(), t["S_crow"], t["S_col"], t["S_values"].float(), t["S_active_rows"])
+    y = y0.to(cuda)
+    torch.ops.ssalaad.tilelang_bsr_addmm_inplace_dense_(y, x.to(cuda), t["S_crow"].to(cuda), t["S_col"].to(cuda),
+                                                        t["S_values"].to(cuda), t["S_active_rows"].to(cuda))
+    assert_16bit_close(y, torch.from_numpy(ref))
+    assert get_tuned_config(32, 32)["BM"] == 1

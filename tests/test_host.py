@@ -1,0 +1,158 @@
+"""Host-side logic that needs no GPU: the C ABI library loads and exports
+every declared symbol, argument validation maps to the reference's exception
+classes, the planners, and the synthetic workload generators."""
+from __future__ import annotations
+
+import ctypes
+import re
+import subprocess
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import REPO
+from s_salaad_b200 import _lib, ops, workloads
+
+
+def _declared_symbols() -> set[str]:
+    text = (REPO / "include" / "slr_b200.h").read_text()
+    return set(re.findall(r"^SLR_API\s+[\w\s\*]+?\b(slr_\w+)\(", text, flags=re.M))
+
+
+def test_header_and_binding_agree():
+    assert _declared_symbols() == set(_lib.EXPORTED)
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    out = subprocess.run(["nm", "-D", "--defined-only", str(_lib.LIB_PATH)], capture_output=True, text=True,
+                         check=True).stdout
+    exported = {line.split()[-1] for line in out.splitlines() if " T " in line}
+    for name in _declared_symbols():
+        assert name in exported, name
+        assert getattr(lib, name) is not None
+    assert lib.slr_abi_version() == 1
+
+
+def test_library_is_built_for_sm100a():
+    out = subprocess.run(["/usr/local/cuda/bin/cuobjdump", "--list-elf", str(_lib.LIB_PATH)],
+                         capture_output=True, text=True)
+    if out.returncode != 0:
+        pytest.skip("cuobjdump unavailable")
+    assert "sm_100a" in out.stdout
+
+
+def test_status_strings():
+    lib = _lib.load()
+    assert lib.slr_status_string(0) == b"SLR_OK"
+    assert lib.slr_status_string(7) == b"SLR_ERR_TIMEOUT"
+
+
+def test_addmm_argument_errors_need_no_gpu():
+    lib = _lib.load()
+    # bad dtype -> TypeError class
+    rc = lib.slr_bsr_addmm_inplace(None, None, 4, 32, None, 2, None, None, 0, 16, 16, None, 1, 9, None)
+    assert rc == _lib.SLR_ERR_UNSUPPORTED_DTYPE
+    with pytest.raises(TypeError):
+        _lib.check(rc)
+    # block not divisible by 16 for bf16 -> RuntimeError class (reference: ValueError at construction)
+    rc = lib.slr_bsr_addmm_inplace(None, None, 4, 32, None, 2, None, None, 0, 8, 16, None, 1, _lib.SLR_BF16, None)
+    assert rc == _lib.SLR_ERR_UNSUPPORTED
+    # K not divisible by block_q
+    rc = lib.slr_bsr_addmm_inplace(None, None, 4, 33, None, 2, None, None, 0, 16, 16, None, 1, _lib.SLR_BF16, None)
+    assert rc == _lib.SLR_ERR_INVALID_ARGUMENT
+    assert "divisible" in _lib.last_error()
+    # null pointers with work to do
+    rc = lib.slr_bsr_addmm_inplace(None, None, 4, 32, None, 2, None, None, 1, 16, 16, None, 1, _lib.SLR_BF16, None)
+    assert rc == _lib.SLR_ERR_INVALID_ARGUMENT
+    # nothing to do: OK without touching the device
+    rc = lib.slr_bsr_addmm_inplace(None, None, 0, 32, None, 2, None, None, 0, 16, 16, None, 0, _lib.SLR_BF16, None)
+    assert rc == _lib.SLR_OK
+
+
+def test_layer_descriptor_validation_needs_no_gpu():
+    lib = _lib.load()
+    L = _lib.SlrLayer(in_features=64, out_features=64, rank=8, block_p=16, block_q=16, nnz=0, dtype=_lib.SLR_BF16)
+    # rank > 0 without A/B
+    assert lib.slr_lrs_linear_forward(ctypes.byref(L), 1, 1, 4, None, 0, None) == _lib.SLR_ERR_INVALID_ARGUMENT
+    L.A, L.B = 0x1000, 0x2000
+    L.flags = 1
+    assert lib.slr_lrs_linear_forward(ctypes.byref(L), 1, 1, 4, None, 0, None) == _lib.SLR_ERR_INVALID_ARGUMENT
+    L.flags = 0
+    L.dtype = 5
+    assert lib.slr_lrs_linear_forward(ctypes.byref(L), 1, 1, 4, None, 0, None) == _lib.SLR_ERR_UNSUPPORTED_DTYPE
+    L.dtype = _lib.SLR_BF16
+    # workspace is required for rank > 0
+    need = lib.slr_lrs_linear_workspace_size(ctypes.byref(L), 4)
+    assert need > 0 and need % 256 == 0
+    assert lib.slr_lrs_linear_forward(ctypes.byref(L), 0x100, 0x200, 4, None, 0, None) == _lib.SLR_ERR_WORKSPACE
+    # M == 0 is a no-op
+    assert lib.slr_lrs_linear_forward(ctypes.byref(L), 0x100, 0x200, 0, None, 0, None) == _lib.SLR_OK
+
+
+def test_dense_to_bsr_shape_error_text_matches_reference():
+    lib = _lib.load()
+    rc = lib.slr_dense_to_bsr_mask(None, 30, 32, 16, 16, _lib.SLR_F32, None, None, None)
+    assert rc == _lib.SLR_ERR_INVALID_ARGUMENT
+    assert "not divisible by block (16, 16)" in _lib.last_error()
+
+
+def test_row_order_is_heaviest_first_and_stable():
+    crow = np.array([0, 2, 2, 7, 8, 11, 13], dtype=np.int32)  # counts 2,0,5,1,3,2
+    order = ops.plan_row_order(crow)
+    assert order.tolist() == [2, 4, 0, 5, 3, 1]
+
+
+@pytest.mark.parametrize("world", [1, 2, 3, 4, 8])
+def test_shards_are_contiguous_and_balanced(world):
+    spec = workloads.layer_set("cfg4")[0]
+    crow = spec.crow.astype(np.int32)
+    b = ops.plan_shards(crow, 64, 64, 512, world)
+    assert b[0] == 0 and b[-1] == spec.nb and np.all(np.diff(b) >= 0)
+    cost = np.diff(crow) * 64 * 64 + 64 * 512
+    parts = np.array([cost[b[p]:b[p + 1]].sum() for p in range(world)])
+    # no shard exceeds the ideal share by more than one (the heaviest) row
+    assert parts.max() <= cost.sum() / world + cost.max()
+
+
+def test_zipf_generator_properties():
+    rng = np.random.Generator(np.random.PCG64(3))
+    counts = workloads.zipf_counts(64, 64, 0.2, 1.1, rng)
+    assert counts.sum() == round(0.2 * 64 * 64)
+    assert counts.max() == 64  # the head is capped at NB_K
+    assert counts.min() >= 0
+    crow, col = workloads.zipf_structure(172, 64, 0.2, 1.1, 0)
+    for i in range(172):
+        c = col[crow[i]:crow[i + 1]]
+        assert np.all(np.diff(c) > 0) and (c.size == 0 or (c.min() >= 0 and c.max() < 64))
+
+
+def test_band_generator_density():
+    crow, col = workloads.band_structure(512, 512, 32, 0.04, 0.01, 0)
+    nnz = col.shape[0]
+    assert abs(nnz / (512 * 512) - 0.05) < 0.003
+    rows = np.repeat(np.arange(512), np.diff(crow))
+    d = col - rows
+    band = (d >= -32) & (d < 32)
+    assert abs(band.sum() / (512 * 512) - 0.04) < 0.003
+
+
+def test_generators_are_deterministic():
+    a = workloads.layer_set("cfg3", seed=0)
+    b = workloads.layer_set("cfg3", seed=0)
+    assert [x.structure_digest() for x in a] == [y.structure_digest() for y in b]
+    t1 = a[0].tensors("cpu", torch.bfloat16)
+    t2 = b[0].tensors("cpu", torch.bfloat16)
+    assert torch.equal(t1["A"], t2["A"]) and torch.equal(t1["values_pq"], t2["values_pq"])
+
+
+def test_layer_api_rejects_cpu_tensors():
+    from s_salaad_b200.efficient import LRSLinear
+
+    A, B = torch.randn(64, 8), torch.randn(8, 96)
+    S = torch.zeros(64, 96)
+    S[:16, 16:32] = 1.0
+    with pytest.raises(ValueError, match="CUDA"):
+        LRSLinear(A, B, S.to_sparse_bsr(blocksize=(16, 16)), in_features=96, out_features=64, block_p=16,
+                  block_q=16)
