@@ -1,0 +1,462 @@
+#!/usr/bin/env python
+"""S+LR linear forward benchmark (B200).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload cfg4|cfg3-T<T>|cfg5-T<T>|cfg1|cfg2]
+
+Prints ONE JSON line (rank 0).  A step is one forward of the workload's
+layer set over one batch of T synthetic tokens:
+
+* cfg4 (default): the seven projections of a LLaMA-7B-shaped decoder layer
+  (q/k/v/o 4096x4096, gate/up 11008x4096, down 4096x11008), 64x64 blocks,
+  20% of blocks with Zipf(1.1) skew over block-rows, rank 512, T = 4096
+  tokens, bf16.  q/k/v read one input, gate/up another, as in the model.
+
+`value` is whole-job tokens/s with inputs resident in HBM (device time from
+CUDA events, L2 flushed between steps, max over ranks).  `e2e` is the same
+through the public API with pinned host inputs copied in and every output
+copied back inside the timed region.  At N > 1 every projection is
+block-row sharded over the ranks and y is all-gathered (NCCL), so the total
+work is fixed (strong scaling).  `--impl reference` times the reference's
+CPU implementation of the path (its AVX2 BSR kernel, compiled from the
+reference sources into oracle/_ref, plus the low-rank F.linear calls and the
+bias, in fp32) on this host's cores over a bounded token sample.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+METRIC = "S+LR linear tokens/s + %HBM/TC roofline at 1/2/4/8 B200 vs AVX2 CPU & cuBLAS"
+L2_FLUSH_BYTES = 256 << 20  # > 126 MB L2
+
+
+# ------------------------------------------------------------ workloads --
+
+def parse_workload(name: str) -> tuple[str, int]:
+    from s_salaad_b200 import workloads
+
+    if "-T" in name:
+        cfg, t = name.split("-T")
+        return cfg, int(t)
+    return name, workloads.CFG_TOKENS[name][0]
+
+
+def input_roles(specs) -> list[int]:
+    """Index of the shared input each projection reads (q/k/v share one,
+    gate/up share one, as in a decoder layer); singletons otherwise."""
+    roles, seen = [], {}
+    for s in specs:
+        key = {"q_proj": "attn", "k_proj": "attn", "v_proj": "attn", "gate_proj": "mlp",
+               "up_proj": "mlp"}.get(s.name.rsplit(".", 1)[-1], s.name)
+        if key not in seen:
+            seen[key] = len(seen)
+        roles.append(seen[key])
+    return roles
+
+
+def peaks() -> tuple[dict, str]:
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.is_file():
+        return json.loads(p.read_text()), "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+# --------------------------------------------------------------- clocks --
+
+class ClockSampler:
+    """Polls NVML (SM clock, max clock, throttle reasons) in a thread."""
+
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown"}
+
+    def __init__(self, index: int):
+        self.samples: list[tuple[int, int]] = []
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception:  # noqa: BLE001 - clocks are best effort
+            self.nv = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                mhz = self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM)
+                rs = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                self.samples.append((mhz, rs))
+            except Exception:  # noqa: BLE001
+                pass
+            time.sleep(0.002)
+
+    def __enter__(self):
+        if self.nv is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread:
+            self._thread.join()
+
+    def summary(self) -> dict:
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
+        mhz = [m for m, _ in self.samples]
+        bits = 0
+        for _, r in self.samples:
+            bits |= r
+        return {"sm_mhz": float(statistics.median(mhz)), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(n for b, n in self.REASONS.items() if bits & b), "samples": len(mhz)}
+
+
+# ---------------------------------------------------------- CPU leg --
+
+def cpu_reference_run(specs, T_sample: int, steps: int, warmup: int, budget_s: float | None):
+    """Time the reference CPU path (AVX2 kernel from oracle/_ref + MKL
+    F.linear + bias, fp32) on T_sample tokens through the layer set.
+    Returns (seconds per sample, kind, cores, reps)."""
+    sys.path.insert(0, str(REPO / "oracle"))
+    import slr_oracle  # noqa: E402  (CPU baseline leg)
+
+    cores = slr_oracle.max_threads()
+    torch.set_num_threads(cores)
+    mod = slr_oracle.ref_avx2_module()
+    kind = "reference" if mod is not None else "port"
+    from s_salaad_b200 import workloads
+
+    layers = []
+    for s in specs:
+        t = s.tensors("cpu", torch.float32)
+        x = workloads.tokens(T_sample, s.in_features, seed=7)
+        layers.append((t, x))
+
+    def one():
+        for t, x in layers:
+            if mod is not None:
+                slr_oracle.lrs_forward_f32_ref_kernel(x, t["A"], t["B"], t["S_crow"], t["S_col"], t["S_values"],
+                                                      t["S_active_rows"], t["bias"], mod=mod)
+            else:
+                slr_oracle.lrs_forward_f32(x, t["A"], t["B"], t["S_crow"], t["S_col"], t["S_values"],
+                                           t["S_active_rows"], t["bias"])
+
+    for _ in range(max(warmup, 1)):
+        one()
+    times = []
+    t_end = None if budget_s is None else time.perf_counter() + budget_s
+    while True:
+        t0 = time.perf_counter()
+        one()
+        times.append(time.perf_counter() - t0)
+        if budget_s is None and len(times) >= steps:
+            break
+        if budget_s is not None and (time.perf_counter() > t_end and len(times) >= 3):
+            break
+    if kind == "port":
+        cores = 1
+    return times, kind, cores
+
+
+# ---------------------------------------------------------------- main --
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", default="cfg4")
+    ap.add_argument("--cpu-sample-tokens", type=int, default=0)
+    ap.add_argument("--cpu-budget-s", type=float, default=12.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-cublas", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        args.warmup = 3
+
+    from s_salaad_b200 import workloads
+
+    cfg, T = parse_workload(args.workload)
+    specs = workloads.layer_set(cfg)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    T_sample = args.cpu_sample_tokens or min(T, 256)
+    config = {"workload": f"{cfg}: {len(specs)} S+LR projections, T={T}",
+              "tokens_per_step": T, "projections": [[s.name, s.out_features, s.in_features] for s in specs],
+              "block": [specs[0].block_p, specs[0].block_q], "rank": specs[0].rank,
+              "nnz_blocks": sum(s.nnz for s in specs)}
+
+    # ------------------------------------------------ reference (CPU) arm
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        times, kind, cores = cpu_reference_run(specs, T_sample, args.steps, args.warmup, None)
+        tok_s = T_sample * len(times) / sum(times)
+        line = {"metric": METRIC, "impl": "reference", "value": tok_s, "unit": "tokens/s", "n_gpus": world,
+                "steps": len(times), "warmup": args.warmup, "ms_per_step": 1e3 * statistics.mean(times),
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+                "data": "synthetic (seeded; no dataset)",
+                "config": {**config, "cpu_sample_tokens": T_sample, "parallelism": "host threads"},
+                "cpu_baseline": {"value": tok_s, "unit": "tokens/s", "cores": cores, "kind": kind,
+                                 "sample": f"{T_sample} of {T} tokens per step through all {len(specs)} projections"},
+                "e2e": {"value": tok_s, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
+
+    # ------------------------------------------------------------ our arm
+    import torch.distributed as dist
+
+    from s_salaad_b200 import ops
+    from s_salaad_b200.shard import ShardedLayer
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+    dtype = torch.float32 if cfg == "cfg1" else torch.bfloat16
+    esize = 4 if dtype == torch.float32 else 2
+
+    layers, tens = [], []
+    for s in specs:
+        t = s.tensors(dev, dtype)
+        tens.append(t)
+        if world > 1:
+            layers.append(ShardedLayer(t, s.crow, in_features=s.in_features, out_features=s.out_features,
+                                       block_p=s.block_p, block_q=s.block_q, rank=rank, world=world))
+        else:
+            order = torch.from_numpy(ops.plan_row_order(s.crow.astype(np.int32))).to(dev)
+            layers.append(ops.LayerDesc(A=t["A"], B=t["B"], bias=t["bias"], crow=t["S_crow"], col=t["S_col"],
+                                        values=t["S_values"], row_order=order, in_features=s.in_features,
+                                        out_features=s.out_features, block_p=s.block_p, block_q=s.block_q))
+    roles = input_roles(specs)
+    xin = {}
+    for i, s in enumerate(specs):
+        if roles[i] not in xin:
+            xin[roles[i]] = workloads.tokens(T, s.in_features, seed=100 + roles[i], device=dev, dtype=dtype)
+    xs = [xin[roles[i]] for i in range(len(specs))]
+    ys = [torch.empty(T, s.out_features, dtype=dtype, device=dev) for s in specs]
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step(ev=None):
+        """One forward of the layer set; ev = per-projection event triples."""
+        for i, L in enumerate(layers):
+            if world > 1:
+                desc = L.desc
+                buf = L.gather_buffer(T)
+                if desc is not None:
+                    out_i = buf[rank][:, :L.width]
+                    if ev is not None:
+                        ev[i][0].record(stream)
+                    desc.lowrank(xs[i])
+                    if ev is not None:
+                        ev[i][1].record(stream)
+                    desc.combine(xs[i], out_i)
+                    if ev is not None:
+                        ev[i][2].record(stream)
+                L.gather(buf, ys[i])
+            else:
+                if ev is not None:
+                    ev[i][0].record(stream)
+                L.lowrank(xs[i])
+                if ev is not None:
+                    ev[i][1].record(stream)
+                L.combine(xs[i], ys[i])
+                if ev is not None:
+                    ev[i][2].record(stream)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+
+    K = args.steps
+    mk = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
+    step_ev = [(mk(), mk()) for _ in range(K)]
+    kern_ev = [[(mk(), mk(), mk()) for _ in specs] for _ in range(K)]
+    with ClockSampler(local) as clocks:
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        for k in range(K):
+            flush.zero_()  # evict L2 between timed steps (outside the events)
+            step_ev[k][0].record(stream)
+            step(kern_ev[k])
+            step_ev[k][1].record(stream)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+    step_ms = [a.elapsed_time(b) for a, b in step_ev]
+    total_ms = sum(step_ms)
+    has_local = [world == 1 or layers[i].desc is not None for i in range(len(specs))]
+    h_ms = [sum(kern_ev[k][i][0].elapsed_time(kern_ev[k][i][1]) for k in range(K)) if has_local[i] else 0.0
+            for i in range(len(specs))]
+    c_ms = [sum(kern_ev[k][i][1].elapsed_time(kern_ev[k][i][2]) for k in range(K)) if has_local[i] else 0.0
+            for i in range(len(specs))]
+    t = torch.tensor([total_ms, sum(c_ms), sum(h_ms)], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_ms, comb_ms_max, low_ms_max = t.tolist()
+
+    # ------------------------------------------------- roofline (combine)
+    P, pk_src = peaks()
+    comb_flops = comb_bytes = low_flops = 0
+    for i, s in enumerate(specs):
+        if world > 1:
+            L = layers[i]
+            if L.desc is None:
+                continue
+            crow = s.crow[L.bounds[rank]:L.bounds[rank + 1] + 1]
+            nnz = int(crow[-1] - crow[0])
+            N = L.width
+        else:
+            nnz, N = s.nnz, s.out_features
+        NB = N // s.block_p
+        comb_flops += 2 * T * (nnz * s.block_p * s.block_q + s.rank * N)
+        comb_bytes += (esize * nnz * s.block_p * s.block_q + 4 * nnz + 8 * (NB + 1) + esize * s.rank * N
+                       + esize * T * (s.in_features + s.rank + N))
+        low_flops += 2 * T * s.rank * s.in_features
+    tensor_bound = T >= 128
+    comb_s = sum(c_ms) / 1e3
+    if tensor_bound:
+        achieved = comb_flops * K / comb_s / 1e12
+        peak = P["bf16_tflops"]
+        roof = {"bound": "tensor", "unit": "TFLOP/s", "algorithmic_per_step": comb_flops}
+    else:
+        achieved = comb_bytes * K / comb_s / 1e9
+        peak = P["hbm_gbs"]
+        roof = {"bound": "hbm", "unit": "GB/s", "algorithmic_per_step": comb_bytes}
+    traffic = None
+    tfile = REPO / "profiles" / "traffic.json"
+    if tfile.is_file():
+        traffic = json.loads(tfile.read_text()).get(args.workload)
+    roof.update({"kernel": "combine (sparse + H*A^T + bias; one launch per projection)",
+                 "achieved": achieved, "peak": peak, "peak_source": pk_src,
+                 "frac": achieved / peak, "traffic": traffic,
+                 "launch_ms_mean": sum(c_ms) / (K * len(specs)),
+                 "lowrank_kernel_ms_mean": sum(h_ms) / (K * len(specs)),
+                 "lowrank_tflops": low_flops * K / (sum(h_ms) / 1e3) / 1e12 if sum(h_ms) else None})
+
+    value = T * K / (total_ms / 1e3)
+    launches_per_step = sum((1 if s.rank > 0 else 0) + 1 for i, s in enumerate(specs) if has_local[i])
+
+    # ------------------------------------------------------------- e2e
+    x_host = {r: xin[r].cpu().pin_memory() for r in xin}
+    xin_dev = {r: torch.empty_like(xin[r]) for r in xin}
+    y_host = [torch.empty(T, s.out_features, dtype=dtype).pin_memory() for s in specs]
+    h2d = sum(v.numel() * v.element_size() for v in x_host.values())
+    d2h = sum(v.numel() * v.element_size() for v in y_host) if rank == 0 else 0
+
+    def e2e_step():
+        for r in xin:
+            xin_dev[r].copy_(x_host[r], non_blocking=True)
+        for i, L in enumerate(layers):
+            x_i = xin_dev[roles[i]]
+            if world > 1:
+                L.forward(x_i, ys[i])
+            else:
+                L.forward(x_i, ys[i])
+            if rank == 0:
+                y_host[i].copy_(ys[i], non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    e2e_ev = [(mk(), mk()) for _ in range(K)]
+    for k in range(K):
+        flush.zero_()
+        e2e_ev[k][0].record(stream)
+        e2e_step()
+        e2e_ev[k][1].record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = torch.tensor([sum(a.elapsed_time(b) for a, b in e2e_ev)], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+    e2e_val = T * K / (e2e_ms.item() / 1e3)
+
+    # ------------------------------------------------ cuBLAS dense (N=1)
+    cublas = None
+    if world == 1 and not args.no_cublas:
+        Ws = []
+        for s, tt in zip(specs, tens):
+            W = (tt["A"].float() @ tt["B"].float())
+            Wv = W.view(s.nb, s.block_p, s.in_features // s.block_q, s.block_q).permute(0, 2, 1, 3)
+            rows = torch.from_numpy(np.repeat(np.arange(s.nb), np.diff(s.crow))).to(dev)
+            cols = torch.from_numpy(s.col).to(dev)
+            Wv[rows, cols] += tt["values_pq"].float()
+            Ws.append(W.to(dtype))
+            del W, Wv
+        biases = [tt["bias"] for tt in tens]
+        fl = torch.nn.functional.linear
+        for _ in range(3):
+            for i in range(len(specs)):
+                fl(xs[i], Ws[i], biases[i])
+        torch.cuda.synchronize()
+        dev_ev = [(mk(), mk()) for _ in range(K)]
+        for k in range(K):
+            flush.zero_()
+            dev_ev[k][0].record(stream)
+            for i in range(len(specs)):
+                torch.matmul(xs[i], Ws[i].T, out=ys[i]) if biases[i] is None else fl(xs[i], Ws[i], biases[i])
+            dev_ev[k][1].record(stream)
+        torch.cuda.synchronize()
+        cb_ms = sum(a.elapsed_time(b) for a, b in dev_ev)
+        dense_flops = sum(2 * T * s.out_features * s.in_features for s in specs)
+        cublas = {"value": T * K / (cb_ms / 1e3), "unit": "tokens/s", "ms_per_step": cb_ms / K,
+                  "tflops": dense_flops * K / (cb_ms / 1e3) / 1e12, "what": "torch F.linear (cuBLAS) on dense "
+                  "W = A*B + S in bf16, same shapes and inputs"}
+        del Ws
+
+    # ------------------------------------------------------- CPU baseline
+    cpu = None
+    if world == 1 and rank == 0 and not args.no_cpu_baseline:
+        times, kind, cores = cpu_reference_run(specs, T_sample, 0, 1, args.cpu_budget_s)
+        cpu = {"value": T_sample * len(times) / sum(times), "unit": "tokens/s", "cores": cores, "kind": kind,
+               "sample": f"{T_sample} of {T} tokens x {len(times)} reps through all {len(specs)} projections, "
+                         f"fp32 (reference AVX2 BSR kernel + MKL low-rank + bias)"}
+
+    if rank == 0:
+        all_flops = sum(s.flops_per_token() for s in specs) * T
+        line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K,
+                "warmup": args.warmup, "ms_per_step": total_ms / K, "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": "bf16" if dtype == torch.bfloat16 else "f32",
+                "data": "synthetic (seeded generators; random-init weights; no dataset)",
+                "config": {**config, "l2": "flushed (256 MB write) between timed steps",
+                           "parallelism": f"block-row shards x{world} + NCCL all-gather" if world > 1 else "1 GPU",
+                           "algorithmic_tflop_per_step": all_flops / 1e12},
+                "roofline": roof, "e2e": {"value": e2e_val, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                                          "d2h_bytes_per_step": d2h},
+                "gpu_launches": launches_per_step * K, "clocks": clocks.summary(),
+                "cpu_baseline": cpu, "cublas_dense": cublas}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -162,11 +162,31 @@ SLR_API size_t slr_lrs_linear_workspace_size(const slr_layer* layer, int64_t M);
  * kernel's order, then the bias.  For 16-bit dtypes x·Bᵀ is rounded to the
  * dtype (as the reference's first F.linear does) and everything after it is
  * accumulated in fp32 and rounded once.
- * y must not overlap x.  No M padding is needed.
+ *   ldx  row stride of x in elements (0 = K); ldy row stride of y (0 = N).
+ * y must not overlap x.  No M padding is needed.  Equivalent to
+ * slr_lrs_linear_lowrank followed by slr_lrs_linear_combine, with the second
+ * launch allowed to start its sparse part while the first finishes.
  */
-SLR_API int slr_lrs_linear_forward(const slr_layer* layer, const void* x, void* y,
+SLR_API int slr_lrs_linear_forward(const slr_layer* layer, const void* x, int64_t ldx,
+                           void* y, int64_t ldy, int64_t M, void* workspace,
+                           size_t workspace_bytes, void* stream);
+
+/*
+ * Phase 1 alone: H = x · Bᵀ into the workspace (the reference's first
+ * F.linear, ls_linear.py:131).  A no-op when rank == 0.
+ */
+SLR_API int slr_lrs_linear_lowrank(const slr_layer* layer, const void* x, int64_t ldx,
                            int64_t M, void* workspace, size_t workspace_bytes,
                            void* stream);
+
+/*
+ * Phase 2 alone: y = x · Sᵀ + H · Aᵀ + bias with H read from a workspace that
+ * slr_lrs_linear_lowrank filled for the same layer, x and M (the reference's
+ * second F.linear, sparse operator and bias, ls_linear.py:131-137).
+ */
+SLR_API int slr_lrs_linear_combine(const slr_layer* layer, const void* x, int64_t ldx,
+                           void* y, int64_t ldy, int64_t M, void* workspace,
+                           size_t workspace_bytes, void* stream);
 
 /* --------------------------------------------------- dense -> BSR -- */
 

@@ -34,6 +34,8 @@ EXPORTED = (
     "slr_validate_bsr",
     "slr_lrs_linear_workspace_size",
     "slr_lrs_linear_forward",
+    "slr_lrs_linear_lowrank",
+    "slr_lrs_linear_combine",
     "slr_dense_to_bsr_mask",
     "slr_dense_to_bsr_fill",
     "slr_plan_row_order",
@@ -73,7 +75,9 @@ _SIGS = {
     "slr_bsr_addmm_inplace": ([vp, vp, i64, i64, vp, i64, vp, vp, i64, i64, i64, vp, i64, i32, vp], i32),
     "slr_validate_bsr": ([vp, i64, vp, i64, i64, vp, i64, vp], i32),
     "slr_lrs_linear_workspace_size": ([ctypes.POINTER(SlrLayer), i64], sz),
-    "slr_lrs_linear_forward": ([ctypes.POINTER(SlrLayer), vp, vp, i64, vp, sz, vp], i32),
+    "slr_lrs_linear_forward": ([ctypes.POINTER(SlrLayer), vp, i64, vp, i64, i64, vp, sz, vp], i32),
+    "slr_lrs_linear_lowrank": ([ctypes.POINTER(SlrLayer), vp, i64, i64, vp, sz, vp], i32),
+    "slr_lrs_linear_combine": ([ctypes.POINTER(SlrLayer), vp, i64, vp, i64, i64, vp, sz, vp], i32),
     "slr_dense_to_bsr_mask": ([vp, i64, i64, i64, i64, i32, vp, vp, vp], i32),
     "slr_dense_to_bsr_fill": ([vp, i64, i64, i64, i64, i32, vp, vp, vp, vp, i32, vp], i32),
     "slr_plan_row_order": ([vp, i64, vp], i32),

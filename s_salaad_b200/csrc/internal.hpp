@@ -24,6 +24,7 @@ struct RowblockArgs {
   const int32_t* rows = nullptr;  // block-row list (null = 0..nrows-1)
   int64_t nrows = 0;
   int64_t M = 0, K = 0, N = 0, r = 0, nnz = 0;
+  int64_t ldx = 0, ldy = 0;  // row strides of x and y (elements)
   int bp = 0, bq = 0;
   int dtype = SLR_F32;
   int mode = MODE_FUSED;
@@ -31,7 +32,7 @@ struct RowblockArgs {
 
 // ---- SIMT (CUDA-core FFMA) kernels: fp32 parity path and generic fallback.
 // H element type is float when h_f32, else the I/O dtype.
-int launch_simt_h(const void* x, const void* B, void* H, int64_t M, int64_t K, int64_t r,
+int launch_simt_h(const void* x, int64_t ldx, const void* B, void* H, int64_t M, int64_t K, int64_t r,
                   int64_t ldh, int dtype, bool h_f32, cudaStream_t s);
 int launch_simt_rowblock(const RowblockArgs& a, bool h_f32, cudaStream_t s);
 
@@ -46,7 +47,7 @@ struct HSmallPlan {
   size_t counters = 0;
 };
 HSmallPlan plan_h_small(int64_t M, int64_t K, int64_t ldh);
-int launch_h_small(const void* x, const void* B, void* H, float* part, unsigned* counters,
+int launch_h_small(const void* x, int64_t ldx, const void* B, void* H, float* part, unsigned* counters,
                    int64_t M, int64_t K, int64_t r, int64_t ldh, const HSmallPlan& plan,
                    int dtype, cudaStream_t s);
 bool mma_rowblock_supported(int bp, int bq, int64_t K, int64_t r);

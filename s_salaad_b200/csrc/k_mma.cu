@@ -39,7 +39,7 @@ struct MmaArgs {
   const int32_t* crow;
   const int32_t* col;
   const int32_t* rows;
-  int64_t M, K, N, ldh;
+  int64_t M, K, N, ldh, ldx, ldy;
   int r, bq, rb, kc;
 };
 
@@ -146,7 +146,7 @@ __global__ void __launch_bounds__(kThreads)
             const int64_t t = t0 + 8 * nt + g;
             uint32_t b0 = 0, b1 = 0;
             if (t < a.M) {
-              const TI* xr = x + t * a.K + xk + 2 * tig;
+              const TI* xr = x + t * a.ldx + xk + 2 * tig;
               b0 = ldg_u32(xr);
               b1 = ldg_u32(xr + 8);
             }
@@ -205,7 +205,7 @@ __global__ void __launch_bounds__(kThreads)
     float v = 0.f;
 #pragma unroll
     for (int k = 0; k < KG; ++k) v += red[(k * BP + n) * TT + t];
-    const int64_t gi = tok * a.N + int64_t(br) * BP + n;
+    const int64_t gi = tok * a.ldy + int64_t(br) * BP + n;
     if (MODE == MODE_ADDMM) {
       v = to_f(y[gi]) + v;
     } else if (bias != nullptr) {
@@ -223,7 +223,7 @@ struct HArgs {
   void* H;
   float* part;
   unsigned* counters;
-  int64_t M, K, kchunk;
+  int64_t M, K, ldx, kchunk;
   int r, ldh, ks, rt;
 };
 
@@ -269,7 +269,7 @@ __global__ void __launch_bounds__(128) h_small_kernel(const HArgs a) {
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
       const int64_t t = t0 + 8 * nt + g;
-      const uint4 X = (t < a.M && kin) ? ldg_u128(x + t * a.K + kk) : z;
+      const uint4 X = (t < a.M && kin) ? ldg_u128(x + t * a.ldx + kk) : z;
       const uint32_t s0[4] = {A0.x, A1.x, A0.y, A1.y};
       const uint32_t s1[4] = {A0.z, A1.z, A0.w, A1.w};
       mma16816<TI>::run(acc[nt], s0, X.x, X.y);
@@ -400,11 +400,11 @@ HSmallPlan plan_h_small(int64_t M, int64_t K, int64_t ldh) {
   return p;
 }
 
-int launch_h_small(const void* x, const void* B, void* H, float* part, unsigned* counters,
+int launch_h_small(const void* x, int64_t ldx, const void* B, void* H, float* part, unsigned* counters,
                    int64_t M, int64_t K, int64_t r, int64_t ldh, const HSmallPlan& plan,
                    int dtype, cudaStream_t s) {
   if (M <= 0 || ldh <= 0) return SLR_OK;
-  HArgs a{x, B, H, part, counters, M, K, plan.kchunk, int(r), int(ldh), plan.ks, plan.rt};
+  HArgs a{x, B, H, part, counters, M, K, ldx, plan.kchunk, int(r), int(ldh), plan.ks, plan.rt};
   const dim3 grid(unsigned(plan.rt), unsigned(plan.ks), unsigned(plan.tc));
   if (dtype == SLR_BF16) return launch_h_small_t<__nv_bfloat16>(a, plan.tt, grid, s);
   if (dtype == SLR_F16) return launch_h_small_t<__half>(a, plan.tt, grid, s);
@@ -422,7 +422,7 @@ bool mma_rowblock_supported(int bp, int bq, int64_t K, int64_t r) {
 int launch_mma_rowblock(const RowblockArgs& a, bool pdl, cudaStream_t s) {
   if (a.nrows <= 0 || a.M <= 0) return SLR_OK;
   const int bp = a.bp;
-  MmaArgs k{a.x, a.y, a.H, a.bias, a.crow, a.col, a.rows, a.M, a.K, a.N, a.ldh,
+  MmaArgs k{a.x, a.y, a.H, a.bias, a.crow, a.col, a.rows, a.M, a.K, a.N, a.ldh, a.ldx, a.ldy,
             int(a.r), a.bq, 0, 0};
   k.rb = std::min(256, kStageBytes / (bp * 2));
   k.kc = a.r >= 64 ? 64 : (a.r >= 32 ? 32 : 16);

@@ -20,7 +20,7 @@ constexpr int kChunk = 8;  // k elements staged per step (block_q % 8 == 0)
 template <typename TI, typename TH>
 __global__ void __launch_bounds__(kThreads)
     simt_h_kernel(const TI* __restrict__ x, const TI* __restrict__ B, TH* __restrict__ H,
-                  int64_t M, int64_t K, int64_t r, int64_t ldh) {
+                  int64_t M, int64_t K, int64_t ldx, int64_t r, int64_t ldh) {
   __shared__ float xs[32][33];
   __shared__ float bs[32][33];
   const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
@@ -31,7 +31,7 @@ __global__ void __launch_bounds__(kThreads)
     for (int i = 0; i < 4; ++i) {
       const int row = ty + 8 * i;
       const int64_t k = k0 + tx;
-      xs[row][tx] = (m0 + row < M && k < K) ? to_f(x[(m0 + row) * K + k]) : 0.f;
+      xs[row][tx] = (m0 + row < M && k < K) ? to_f(x[(m0 + row) * ldx + k]) : 0.f;
       bs[row][tx] = (p0 + row < r && k < K) ? to_f(B[(p0 + row) * K + k]) : 0.f;
     }
     __syncthreads();
@@ -61,7 +61,7 @@ struct SimtArgs {
   const int32_t* col;
   const void* values;
   const int32_t* rows;
-  int64_t M, K, N, r;
+  int64_t M, K, N, r, ldx, ldy;
   int bp, bq, tm;
 };
 
@@ -89,7 +89,7 @@ __global__ void __launch_bounds__(kThreads) simt_rowblock_kernel(SimtArgs a) {
     on[i] = o - om[i] * bp;
     ok[i] = o < tm * bp && m0 + om[i] < a.M;
     acc[i] = 0.f;
-    if (MODE == MODE_ADDMM && ok[i]) acc[i] = to_f(y[(m0 + om[i]) * a.N + col0 + on[i]]);
+    if (MODE == MODE_ADDMM && ok[i]) acc[i] = to_f(y[(m0 + om[i]) * a.ldy + col0 + on[i]]);
   }
 
   if (MODE == MODE_FUSED && a.r > 0) {
@@ -130,7 +130,7 @@ __global__ void __launch_bounds__(kThreads) simt_rowblock_kernel(SimtArgs a) {
       for (int k0 = 0; k0 < a.bq; k0 += kChunk) {
         for (int e = threadIdx.x; e < tm * kChunk; e += kThreads) {
           const int m = e / kChunk, kk = e % kChunk;
-          xs[m * (kChunk + 1) + kk] = (m0 + m < a.M) ? to_f(x[(m0 + m) * a.K + xc + k0 + kk]) : 0.f;
+          xs[m * (kChunk + 1) + kk] = (m0 + m < a.M) ? to_f(x[(m0 + m) * a.ldx + xc + k0 + kk]) : 0.f;
         }
         const TI* vb = vals + (int64_t(ji) * a.bq + k0) * bp;
         for (int e = threadIdx.x; e < kChunk * bp; e += kThreads) ws[e] = to_f(vb[e]);
@@ -153,14 +153,14 @@ __global__ void __launch_bounds__(kThreads) simt_rowblock_kernel(SimtArgs a) {
     if (!ok[i]) continue;
     float v = acc[i];
     if (MODE == MODE_FUSED && bias != nullptr) v = v + to_f(bias[col0 + on[i]]);
-    y[(m0 + om[i]) * a.N + col0 + on[i]] = from_f<TI>(v);
+    y[(m0 + om[i]) * a.ldy + col0 + on[i]] = from_f<TI>(v);
   }
 }
 
 template <typename TI, typename TH>
 int launch_rowblock_t(const RowblockArgs& a, cudaStream_t s) {
   SimtArgs k{a.x, a.y, a.H, a.ldh, a.A, a.bias, a.crow, a.col, a.values, a.rows,
-             a.M, a.K, a.N, a.r, a.bp, a.bq, 0};
+             a.M, a.K, a.N, a.r, a.ldx, a.ldy, a.bp, a.bq, 0};
   k.tm = int(std::max<int64_t>(1, std::min<int64_t>(32, 2048 / a.bp)));
   const size_t smem =
       sizeof(float) * (size_t(k.tm) * (kChunk + 1) + size_t(std::max(kChunk * a.bp, a.bp * (kChunk + 1))));
@@ -181,31 +181,31 @@ int launch_rowblock_t(const RowblockArgs& a, cudaStream_t s) {
 
 }  // namespace
 
-int launch_simt_h(const void* x, const void* B, void* H, int64_t M, int64_t K, int64_t r,
+int launch_simt_h(const void* x, int64_t ldx, const void* B, void* H, int64_t M, int64_t K, int64_t r,
                   int64_t ldh, int dtype, bool h_f32, cudaStream_t s) {
   const dim3 grid(unsigned(ceil_div(ldh, 32)), unsigned(ceil_div(M, 32)));
   if (grid.x == 0 || grid.y == 0) return SLR_OK;
   switch (dtype) {
     case SLR_F32:
       simt_h_kernel<float, float><<<grid, kThreads, 0, s>>>(
-          static_cast<const float*>(x), static_cast<const float*>(B), static_cast<float*>(H), M, K, r, ldh);
+          static_cast<const float*>(x), static_cast<const float*>(B), static_cast<float*>(H), M, K, ldx, r, ldh);
       break;
     case SLR_F16:
       if (h_f32)
         simt_h_kernel<__half, float><<<grid, kThreads, 0, s>>>(
-            static_cast<const __half*>(x), static_cast<const __half*>(B), static_cast<float*>(H), M, K, r, ldh);
+            static_cast<const __half*>(x), static_cast<const __half*>(B), static_cast<float*>(H), M, K, ldx, r, ldh);
       else
         simt_h_kernel<__half, __half><<<grid, kThreads, 0, s>>>(
-            static_cast<const __half*>(x), static_cast<const __half*>(B), static_cast<__half*>(H), M, K, r, ldh);
+            static_cast<const __half*>(x), static_cast<const __half*>(B), static_cast<__half*>(H), M, K, ldx, r, ldh);
       break;
     case SLR_BF16:
       if (h_f32)
         simt_h_kernel<__nv_bfloat16, float><<<grid, kThreads, 0, s>>>(
-            static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(B), static_cast<float*>(H), M, K, r, ldh);
+            static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(B), static_cast<float*>(H), M, K, ldx, r, ldh);
       else
         simt_h_kernel<__nv_bfloat16, __nv_bfloat16><<<grid, kThreads, 0, s>>>(
             static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(B),
-            static_cast<__nv_bfloat16*>(H), M, K, r, ldh);
+            static_cast<__nv_bfloat16*>(H), M, K, ldx, r, ldh);
       break;
     default:
       return fail(SLR_ERR_UNSUPPORTED_DTYPE, "simt_h: bad dtype");

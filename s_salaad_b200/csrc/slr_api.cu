@@ -101,13 +101,13 @@ bool layer_aligned16(const slr_layer& L) {
   return aligned16(L.A) && aligned16(L.B) && (L.nnz == 0 || aligned16(L.values));
 }
 
-FwdPlan plan_forward(const slr_layer& L, int64_t M, const void* x, const void* y) {
+FwdPlan plan_forward(const slr_layer& L, int64_t M, const void* x) {
   FwdPlan p;
   p.row_bp = effective_bp(L);
   const bool is16 = L.dtype != SLR_F32;
   const int bq = L.nnz > 0 ? int(L.block_q) : 16;
   if (is16 && mma_rowblock_supported(p.row_bp, bq, L.in_features, L.rank) && layer_aligned16(L) &&
-      (x == nullptr || aligned16(x)) && (y == nullptr || aligned16(y)))
+      (x == nullptr || aligned16(x)))
     p.path = 1;
   p.ldh = L.rank > 0 ? round_up(L.rank, 64) : 0;
   const size_t hes = (p.path == 0 && !is16) ? 4 : dtype_size(L.dtype);
@@ -205,6 +205,8 @@ int slr_bsr_addmm_inplace(void* out, const void* x, int64_t M, int64_t K, const 
   a.M = M;
   a.K = K;
   a.N = NB * block_p;
+  a.ldx = K;
+  a.ldy = NB * block_p;
   a.nnz = nnz;
   a.bp = int(block_p);
   a.bq = int(block_q);
@@ -246,67 +248,112 @@ int slr_validate_bsr(const int32_t* crow, int64_t NB, const int32_t* col, int64_
 
 size_t slr_lrs_linear_workspace_size(const slr_layer* layer, int64_t M) {
   if (check_layer(layer) != SLR_OK || M < 0) return 0;
-  return plan_forward(*layer, M, nullptr, nullptr).total;
+  return plan_forward(*layer, M, nullptr).total;
 }
 
-int slr_lrs_linear_forward(const slr_layer* layer, const void* x, void* y, int64_t M,
-                           void* workspace, size_t workspace_bytes, void* stream) {
+}  // extern "C"
+
+namespace {
+
+// Shared argument checks and argument packing of the three forward entry points.
+struct FwdCall {
+  FwdPlan p;
+  RowblockArgs a;
+  uint8_t* ws = nullptr;
+};
+
+int prepare_forward(const slr_layer* layer, const void* x, int64_t ldx, void* y, int64_t ldy, int64_t M,
+                    void* workspace, size_t workspace_bytes, bool need_y, FwdCall& c) {
   int rc = check_layer(layer);
   if (rc) return rc;
   const slr_layer& L = *layer;
   if (M < 0) return fail(SLR_ERR_INVALID_ARGUMENT, "M must be >= 0");
-  if (M == 0) return SLR_OK;
-  if (!x || !y) return fail(SLR_ERR_INVALID_ARGUMENT, "x/y is NULL");
-  const FwdPlan p = plan_forward(L, M, x, y);
-  if (p.total > 0) {
+  if (ldx == 0) ldx = L.in_features;
+  if (ldy == 0) ldy = L.out_features;
+  if (ldx < L.in_features || ldy < L.out_features)
+    return fail(SLR_ERR_INVALID_ARGUMENT, "ldx/ldy must be >= in_features/out_features");
+  if (M > 0 && (!x || (need_y && !y))) return fail(SLR_ERR_INVALID_ARGUMENT, "x/y is NULL");
+  // Every 16-bit path keeps H as [M, ldh] in the I/O dtype, so the two phases
+  // may pick different kernels; the path only depends on x, never on y.
+  c.p = plan_forward(L, M, (ldx % 8 == 0) ? x : reinterpret_cast<const void*>(uintptr_t(1)));
+  if (c.p.total > 0 && M > 0) {
     if (!workspace) return fail(SLR_ERR_WORKSPACE, "workspace is NULL");
-    if (workspace_bytes < p.total)
-      return fail(SLR_ERR_WORKSPACE, "workspace too small: need " + std::to_string(p.total) + " bytes");
+    if (workspace_bytes < c.p.total)
+      return fail(SLR_ERR_WORKSPACE, "workspace too small: need " + std::to_string(c.p.total) + " bytes");
     if (reinterpret_cast<uintptr_t>(workspace) & 255u) return fail(SLR_ERR_WORKSPACE, "workspace must be 256-byte aligned");
   }
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  uint8_t* ws = static_cast<uint8_t*>(workspace);
-  void* H = L.rank > 0 ? ws : nullptr;
-
-  RowblockArgs a;
+  c.ws = static_cast<uint8_t*>(workspace);
+  RowblockArgs& a = c.a;
   a.x = x;
   a.y = y;
-  a.H = H;
-  a.ldh = p.ldh;
+  a.H = L.rank > 0 ? c.ws : nullptr;
+  a.ldh = c.p.ldh;
   a.A = L.A;
   a.bias = L.bias;
   a.crow = L.nnz > 0 ? L.crow : nullptr;
   a.col = L.col;
   a.values = L.values;
   a.rows = L.nnz > 0 ? L.row_order : nullptr;
-  a.nrows = L.out_features / p.row_bp;
+  a.nrows = L.out_features / c.p.row_bp;
   a.M = M;
   a.K = L.in_features;
   a.N = L.out_features;
+  a.ldx = ldx;
+  a.ldy = ldy;
   a.r = L.rank;
   a.nnz = L.nnz;
-  a.bp = p.row_bp;
+  a.bp = c.p.row_bp;
   a.bq = L.nnz > 0 ? int(L.block_q) : 16;
   a.dtype = L.dtype;
   a.mode = MODE_FUSED;
+  return SLR_OK;
+}
 
-  if (p.path == 1) {
-    bool pdl = false;
-    if (L.rank > 0) {
-      rc = launch_h_small(x, L.B, H, reinterpret_cast<float*>(ws + p.part_off),
-                          reinterpret_cast<unsigned*>(ws + p.cnt_off), M, L.in_features, L.rank, p.ldh, p.hs,
-                          L.dtype, s);
-      if (rc) return rc;
-      pdl = true;
-    }
-    return launch_mma_rowblock(a, pdl, s);
-  }
-  const bool h_f32 = L.dtype == SLR_F32;
-  if (L.rank > 0) {
-    rc = launch_simt_h(x, L.B, H, M, L.in_features, L.rank, p.ldh, L.dtype, h_f32, s);
-    if (rc) return rc;
-  }
-  return launch_simt_rowblock(a, h_f32, s);
+int run_lowrank(const slr_layer& L, const FwdCall& c, cudaStream_t s) {
+  if (L.rank == 0 || c.a.M == 0) return SLR_OK;
+  if (c.p.path == 1)
+    return launch_h_small(c.a.x, c.a.ldx, L.B, c.ws, reinterpret_cast<float*>(c.ws + c.p.part_off),
+                          reinterpret_cast<unsigned*>(c.ws + c.p.cnt_off), c.a.M, L.in_features, L.rank, c.p.ldh,
+                          c.p.hs, L.dtype, s);
+  return launch_simt_h(c.a.x, c.a.ldx, L.B, c.ws, c.a.M, L.in_features, L.rank, c.p.ldh, L.dtype,
+                       L.dtype == SLR_F32, s);
+}
+
+int run_combine(const slr_layer& L, const FwdCall& c, bool pdl, cudaStream_t s) {
+  if (c.a.M == 0) return SLR_OK;
+  if (c.p.path == 1) return launch_mma_rowblock(c.a, pdl && L.rank > 0, s);
+  return launch_simt_rowblock(c.a, L.dtype == SLR_F32, s);
+}
+
+}  // namespace
+
+extern "C" {
+
+int slr_lrs_linear_forward(const slr_layer* layer, const void* x, int64_t ldx, void* y, int64_t ldy, int64_t M,
+                           void* workspace, size_t workspace_bytes, void* stream) {
+  FwdCall c;
+  int rc = prepare_forward(layer, x, ldx, y, ldy, M, workspace, workspace_bytes, true, c);
+  if (rc) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  rc = run_lowrank(*layer, c, s);
+  if (rc) return rc;
+  return run_combine(*layer, c, true, s);
+}
+
+int slr_lrs_linear_lowrank(const slr_layer* layer, const void* x, int64_t ldx, int64_t M, void* workspace,
+                           size_t workspace_bytes, void* stream) {
+  FwdCall c;
+  int rc = prepare_forward(layer, x, ldx, nullptr, 0, M, workspace, workspace_bytes, false, c);
+  if (rc) return rc;
+  return run_lowrank(*layer, c, static_cast<cudaStream_t>(stream));
+}
+
+int slr_lrs_linear_combine(const slr_layer* layer, const void* x, int64_t ldx, void* y, int64_t ldy, int64_t M,
+                           void* workspace, size_t workspace_bytes, void* stream) {
+  FwdCall c;
+  int rc = prepare_forward(layer, x, ldx, y, ldy, M, workspace, workspace_bytes, true, c);
+  if (rc) return rc;
+  return run_combine(*layer, c, false, static_cast<cudaStream_t>(stream));
 }
 
 int slr_dense_to_bsr_mask(const void* S, int64_t n, int64_t m, int64_t block_p, int64_t block_q,

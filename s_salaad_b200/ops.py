@@ -168,7 +168,14 @@ class LayerDesc:
             self._ws = torch.zeros(need, dtype=torch.uint8, device=self.device)
         return self._ws
 
+    @staticmethod
+    def _ld(t: torch.Tensor) -> int:
+        if t.dim() != 2 or t.stride(1) != 1:
+            raise ValueError("x/out must be 2-D with unit stride in the last dimension")
+        return t.stride(0)
+
     def forward(self, x2: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        """y = x2 @ S.T + (x2 @ B.T) @ A.T + bias; x2/out may be row-strided."""
         lib = _lib.load()
         M = x2.shape[0]
         if out is None:
@@ -176,10 +183,31 @@ class LayerDesc:
         ws = self.workspace(M)
         with _DeviceGuard(self.device):
             rc = lib.slr_lrs_linear_forward(
-                ctypes.byref(self.struct), x2.data_ptr(), out.data_ptr(), M,
+                ctypes.byref(self.struct), x2.data_ptr(), self._ld(x2), out.data_ptr(), self._ld(out), M,
                 None if ws is None else ws.data_ptr(), 0 if ws is None else ws.numel(),
                 _stream(self.device))
         _lib.check(rc, "lrs_linear_forward")
+        return out
+
+    def lowrank(self, x2: torch.Tensor) -> None:
+        """Phase 1 alone: H = x2 @ B.T into this layer's workspace."""
+        M = x2.shape[0]
+        ws = self.workspace(M)
+        with _DeviceGuard(self.device):
+            rc = _lib.load().slr_lrs_linear_lowrank(
+                ctypes.byref(self.struct), x2.data_ptr(), self._ld(x2), M,
+                None if ws is None else ws.data_ptr(), 0 if ws is None else ws.numel(), _stream(self.device))
+        _lib.check(rc, "lrs_linear_lowrank")
+
+    def combine(self, x2: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+        """Phase 2 alone: out = x2 @ S.T + H @ A.T + bias (H from lowrank())."""
+        M = x2.shape[0]
+        ws = self.workspace(M)
+        with _DeviceGuard(self.device):
+            rc = _lib.load().slr_lrs_linear_combine(
+                ctypes.byref(self.struct), x2.data_ptr(), self._ld(x2), out.data_ptr(), self._ld(out), M,
+                None if ws is None else ws.data_ptr(), 0 if ws is None else ws.numel(), _stream(self.device))
+        _lib.check(rc, "lrs_linear_combine")
         return out
 
 

@@ -4,8 +4,11 @@ Tolerances (stated per test):
   * fp32 in-place addmm: bit-exact with the reference AVX2 kernel (same FMA
     order per output element).
   * fp32 fused layer: |y - y_ref| <= 1e-5 * |y_ref| + 1e-5 * RMS(y_ref).
-  * fp16/bf16: max |y - y_ref| <= 2e-2 * RMS(y_ref), y_ref = the fp32 CPU
-    oracle on fp32 copies of the 16-bit tensors.
+  * fp16/bf16: |y - y_ref| <= 2e-2 * RMS(y_ref) + ulp(y_ref)/2 elementwise,
+    y_ref = the fp32 CPU oracle on fp32 copies of the 16-bit tensors.  The
+    half-ulp term is the final rounding of y to the output dtype, which no
+    16-bit-output implementation avoids (at |y| >= 4 a bf16 half-ulp is
+    0.0156, above 2e-2 * RMS for RMS < 0.78).
 All calls go through the C ABI (ctypes) of libslr_b200.so.
 """
 from __future__ import annotations
@@ -27,12 +30,24 @@ def rms(t: torch.Tensor) -> float:
     return float(t.float().pow(2).mean().sqrt())
 
 
+def half_ulp(ref: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+    """Half a unit in the last place of |ref| in `dtype` (normal range)."""
+    mant = 7 if dtype == torch.bfloat16 else 10
+    e = torch.floor(torch.log2(ref.abs().clamp_min(1e-30)))
+    return torch.pow(2.0, e - mant - 1)
+
+
 def assert_16bit_close(y: torch.Tensor, ref: torch.Tensor, tol: float = BF16_TOL):
+    dtype = y.dtype
     y = y.float().cpu()
     ref = ref.float().cpu()
     assert torch.isfinite(y).all()
-    err = float((y - ref).abs().max())
-    assert err <= tol * rms(ref) + 1e-6, f"max abs err {err:.3e} > {tol} * RMS {rms(ref):.3e}"
+    err = (y - ref).abs()
+    bound = tol * rms(ref) + half_ulp(ref, dtype) + 1e-6
+    worst = int(torch.argmax(err - bound))
+    assert bool((err <= bound).all()), (
+        f"max abs err {float(err.flatten()[worst]):.3e} > bound {float(bound.flatten()[worst]):.3e} "
+        f"(2e-2 * RMS {rms(ref):.3e} + half-ulp) at |y_ref| = {float(ref.flatten()[worst].abs()):.3e}")
 
 
 def assert_f32_close(y: torch.Tensor, ref: torch.Tensor):

@@ -75,20 +75,25 @@ def test_layer_descriptor_validation_needs_no_gpu():
     lib = _lib.load()
     L = _lib.SlrLayer(in_features=64, out_features=64, rank=8, block_p=16, block_q=16, nnz=0, dtype=_lib.SLR_BF16)
     # rank > 0 without A/B
-    assert lib.slr_lrs_linear_forward(ctypes.byref(L), 1, 1, 4, None, 0, None) == _lib.SLR_ERR_INVALID_ARGUMENT
+    fwd = lambda x, y, M, ldx=0, ldy=0: lib.slr_lrs_linear_forward(  # noqa: E731
+        ctypes.byref(L), x, ldx, y, ldy, M, None, 0, None)
+    assert fwd(1, 1, 4) == _lib.SLR_ERR_INVALID_ARGUMENT
     L.A, L.B = 0x1000, 0x2000
     L.flags = 1
-    assert lib.slr_lrs_linear_forward(ctypes.byref(L), 1, 1, 4, None, 0, None) == _lib.SLR_ERR_INVALID_ARGUMENT
+    assert fwd(1, 1, 4) == _lib.SLR_ERR_INVALID_ARGUMENT
     L.flags = 0
     L.dtype = 5
-    assert lib.slr_lrs_linear_forward(ctypes.byref(L), 1, 1, 4, None, 0, None) == _lib.SLR_ERR_UNSUPPORTED_DTYPE
+    assert fwd(1, 1, 4) == _lib.SLR_ERR_UNSUPPORTED_DTYPE
     L.dtype = _lib.SLR_BF16
     # workspace is required for rank > 0
     need = lib.slr_lrs_linear_workspace_size(ctypes.byref(L), 4)
     assert need > 0 and need % 256 == 0
-    assert lib.slr_lrs_linear_forward(ctypes.byref(L), 0x100, 0x200, 4, None, 0, None) == _lib.SLR_ERR_WORKSPACE
+    assert fwd(0x100, 0x200, 4) == _lib.SLR_ERR_WORKSPACE
+    assert lib.slr_lrs_linear_lowrank(ctypes.byref(L), 0x100, 0, 4, None, 0, None) == _lib.SLR_ERR_WORKSPACE
+    # strides below the row length are rejected
+    assert fwd(0x100, 0x200, 4, ldx=32) == _lib.SLR_ERR_INVALID_ARGUMENT
     # M == 0 is a no-op
-    assert lib.slr_lrs_linear_forward(ctypes.byref(L), 0x100, 0x200, 0, None, 0, None) == _lib.SLR_OK
+    assert fwd(0x100, 0x200, 0) == _lib.SLR_OK
 
 
 def test_dense_to_bsr_shape_error_text_matches_reference():
