@@ -1,0 +1,646 @@
+// Large-token-batch path (prefill), 16-bit dtypes, on the 5th-generation
+// tensor cores: tcgen05.mma with the accumulator in tensor memory (TMEM),
+// operands staged in shared memory by TMA, completion tracked by mbarriers.
+//
+//   tc_rowblock_kernel  persistent; one work item = (128-token tile, block-row
+//                       of bp output features).  The K loop walks the row's
+//                       BSR blocks (x tile 128 x bq gathered at col*bq, values
+//                       block bq x bp, MN-major) and then, for the fused
+//                       layer, rank chunks of 64 (H tile 128 x 64, rows of A
+//                       64-wide, K-major) into ONE fp32 accumulator 128 x bp in
+//                       TMEM.  The epilogue adds bias (fused layer) or the old
+//                       `out` (in-place operator) and stores y once.
+//   tc_dense_kernel     persistent dense GEMM H[M, ldh] = x · Bᵀ (tiles
+//                       128 x 64), the rank-r down-projection, rounded to the
+//                       I/O dtype like the reference's first F.linear.
+//
+// Warp roles (192 threads): warp 0 lane 0 issues TMA loads, warp 1 lane 0
+// issues MMAs (warp 1 also owns the TMEM allocation), warps 2-5 drain TMEM
+// (warp w reads TMEM lanes 32*(w%4) .. +31, i.e. tokens of that quarter).
+// The accumulator is double-buffered in TMEM so the epilogue of one item
+// overlaps the MMAs of the next.  Shared memory holds an 8-stage ring.
+//
+// Reference counterparts: _bsr_body (ssalaad/tilelang_sparse/addmm_inplace.py:
+// 41-82) and the F.linear pair + bias of _LRSLinearLRBlockCUDA.forward
+// (ssalaad/efficient/ls_linear.py:124-137).
+#include <algorithm>
+#include <type_traits>
+
+#include "internal.hpp"
+
+namespace slr {
+namespace {
+
+__device__ unsigned g_status_tc = 0;
+
+constexpr int kThreads = 192;
+constexpr int kTileM = 128;
+
+// ------------------------------------------------------ tcgen05 wrappers --
+
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+// D[tmem] (+)= A[smem] * B[smem], kind::f16 (bf16/fp16 in, fp32 accumulate).
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
+  const uint32_t z = 0;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(z), "r"(z), "r"(z), "r"(z));
+}
+// Arrive on `bar` once every MMA issued so far by this thread has completed.
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Shared-memory matrix descriptor (sm_100): start, leading/stride byte
+// offsets (>>4), version 1 at bit 46, layout (swizzle) at bits 61-63.
+__device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo, uint32_t sbo, uint32_t layout) {
+  return uint64_t((saddr >> 4) & 0x3FFFu) | (uint64_t((lbo >> 4) & 0x3FFFu) << 16) |
+         (uint64_t((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (uint64_t(layout) << 61);
+}
+// Swizzle layout code for a row of `bytes` (TMA swizzle of the same width).
+constexpr uint32_t layout_for(int bytes) { return bytes == 128 ? 2u : (bytes == 64 ? 4u : 6u); }
+
+// Instruction descriptor, kind::f16: fp32 accumulate, A K-major, B K- or
+// MN-major, shape M x N.
+template <typename TI>
+constexpr uint32_t idesc_f16(int M, int N, bool b_mn_major) {
+  constexpr uint32_t fmt = std::is_same<TI, __nv_bfloat16>::value ? 1u : 0u;
+  return (1u << 4) | (fmt << 7) | (fmt << 10) | ((b_mn_major ? 1u : 0u) << 16) | (uint32_t(N >> 3) << 17) |
+         (uint32_t(M >> 4) << 24);
+}
+
+__device__ __forceinline__ uint32_t pack2(float lo, float hi, __nv_bfloat16*) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+__device__ __forceinline__ uint32_t pack2(float lo, float hi, __half*) {
+  __half2 v = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+__device__ __forceinline__ float2 unpack2(uint32_t u, __nv_bfloat16*) {
+  return __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&u));
+}
+__device__ __forceinline__ float2 unpack2(uint32_t u, __half*) {
+  return __half22float2(*reinterpret_cast<__half2*>(&u));
+}
+
+struct TcArgs {
+  void* y;
+  const void* bias;
+  const int32_t* crow;
+  const int32_t* col;
+  const int32_t* rows;
+  int64_t M, ldy;
+  int nrows, n_mtiles, n_lr;
+};
+
+// Drain-and-exit after a bounded wait gave up: record the timeout.
+__device__ __forceinline__ void tc_timeout(volatile int* abort_flag) {
+  atomicOr(&g_status_tc, SLR_TIMEOUT_BIT);
+  *abort_flag = 1;
+}
+
+template <int BP, int BQ, typename TI, int MODE>
+__global__ void __launch_bounds__(kThreads, 1)
+    tc_rowblock_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_v,
+                       const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ CUtensorMap tm_a,
+                       const TcArgs a) {
+  constexpr int KS = BQ < 64 ? BQ : 64;  // k per sparse step (one swizzle row)
+  constexpr int SUB = BQ / KS;           // sparse steps per block
+  constexpr int XW = KS * 2;             // x-tile row bytes
+  constexpr int VW = BP * 2;             // values row bytes
+  constexpr uint32_t X_BYTES = kTileM * XW, V_BYTES = KS * VW;
+  constexpr uint32_t H_BYTES = kTileM * 128, AR_BYTES = BP * 128;
+  constexpr uint32_t A_SLOT = 16384;
+  constexpr uint32_t B_SLOT = V_BYTES > AR_BYTES ? V_BYTES : AR_BYTES;
+  constexpr uint32_t STAGE = A_SLOT + B_SLOT;
+  constexpr int STAGES = (196 * 1024) / STAGE > 8 ? 8 : (196 * 1024) / STAGE;
+  constexpr uint32_t TMEM_COLS = 2 * BP < 32 ? 32 : 2 * BP;
+  constexpr uint32_t IDESC_SP = idesc_f16<TI>(kTileM, BP, true);
+  constexpr uint32_t IDESC_LR = idesc_f16<TI>(kTileM, BP, false);
+  static_assert(X_BYTES <= A_SLOT && H_BYTES <= A_SLOT, "A slot");
+  static_assert(STAGE % 1024 == 0, "stages must stay 1024-byte aligned");
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  __shared__ volatile int s_abort;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 4);
+    }
+    fence_mbar_init();
+    s_abort = 0;
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int n_items = a.nrows * a.n_mtiles;
+
+  if (warp == 0) {
+    // ------------------------------------------------------- TMA producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tm_x);
+      tma_prefetch_desc(&tm_v);
+      if (a.n_lr) {
+        tma_prefetch_desc(&tm_h);
+        tma_prefetch_desc(&tm_a);
+      }
+      bool waited = false;
+      uint32_t g = 0;
+      for (int item = blockIdx.x; item < n_items && !s_abort; item += gridDim.x) {
+        const int ri = item / a.n_mtiles, mt = item - ri * a.n_mtiles;
+        const int br = a.rows ? a.rows[ri] : ri;
+        const int m0 = mt * kTileM;
+        const int j0 = a.crow ? a.crow[br] : 0, j1 = a.crow ? a.crow[br + 1] : 0;
+        const int n_sp = (j1 - j0) * SUB, n_tot = n_sp + a.n_lr;
+        for (int s = 0; s < n_tot; ++s, ++g) {
+          const uint32_t slot = g % STAGES, ph = (g / STAGES) & 1;
+          if (!mbar_wait(&empty[slot], ph ^ 1)) {
+            tc_timeout(&s_abort);
+            break;
+          }
+          uint8_t* adst = smem + slot * STAGE;
+          uint8_t* bdst = adst + A_SLOT;
+          if (s < n_sp) {
+            const int blk = j0 + s / SUB, sub = s % SUB;
+            const int c = __ldg(a.col + blk);
+            mbar_arrive_expect_tx(&full[slot], X_BYTES + V_BYTES);
+            tma_load_2d(adst, &tm_x, c * BQ + sub * KS, m0, &full[slot]);
+            tma_load_2d(bdst, &tm_v, 0, blk * BQ + sub * KS, &full[slot]);
+          } else {
+            if (!waited) {
+              pdl_wait_primary();  // H comes from the preceding kernel
+              waited = true;
+            }
+            const int l = s - n_sp;
+            mbar_arrive_expect_tx(&full[slot], H_BYTES + AR_BYTES);
+            tma_load_2d(adst, &tm_h, l * 64, m0, &full[slot]);
+            tma_load_2d(bdst, &tm_a, l * 64, br * BP, &full[slot]);
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      uint32_t g = 0, it = 0;
+      for (int item = blockIdx.x; item < n_items && !s_abort; item += gridDim.x, ++it) {
+        const int ri = item / a.n_mtiles;
+        const int br = a.rows ? a.rows[ri] : ri;
+        const int j0 = a.crow ? a.crow[br] : 0, j1 = a.crow ? a.crow[br + 1] : 0;
+        const int n_sp = (j1 - j0) * SUB, n_tot = n_sp + a.n_lr;
+        const uint32_t buf = it & 1, tph = (it >> 1) & 1;
+        if (!mbar_wait(&tempty[buf], tph ^ 1)) {
+          tc_timeout(&s_abort);
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem + buf * BP;
+        uint32_t acc = 0;
+        for (int s = 0; s < n_tot; ++s, ++g) {
+          const uint32_t slot = g % STAGES, ph = (g / STAGES) & 1;
+          if (!mbar_wait(&full[slot], ph)) {
+            tc_timeout(&s_abort);
+            break;
+          }
+          tc_fence_after();
+          const uint32_t abase = smem_u32(smem + slot * STAGE);
+          const uint32_t bbase = abase + A_SLOT;
+          if (s < n_sp) {
+#pragma unroll
+            for (int kk = 0; kk < KS / 16; ++kk) {
+              const uint64_t ad = sdesc(abase + kk * 32, 16, 8 * XW, layout_for(XW));
+              const uint64_t bd = sdesc(bbase + kk * 16 * VW, V_BYTES, 8 * VW, layout_for(VW));
+              umma_f16(d, ad, bd, IDESC_SP, acc);
+              acc = 1;
+            }
+          } else {
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+              const uint64_t ad = sdesc(abase + kk * 32, 16, 1024, 2);
+              const uint64_t bd = sdesc(bbase + kk * 32, 16, 1024, 2);
+              umma_f16(d, ad, bd, IDESC_LR, acc);
+              acc = 1;
+            }
+          }
+          umma_commit(&empty[slot]);  // frees the stage once these MMAs finish
+        }
+        umma_commit(&tfull[buf]);     // accumulator ready for the epilogue
+      }
+    }
+  } else {
+    // ---------------------------------------------------------- epilogue
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int row = 32 * q + lane;
+    TI* __restrict__ y = static_cast<TI*>(a.y);
+    const TI* __restrict__ bias = static_cast<const TI*>(a.bias);
+    uint32_t it = 0;
+    for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++it) {
+      const int ri = item / a.n_mtiles, mt = item - ri * a.n_mtiles;
+      const int br = a.rows ? a.rows[ri] : ri;
+      const int j0 = a.crow ? a.crow[br] : 0, j1 = a.crow ? a.crow[br + 1] : 0;
+      const int n_tot = (j1 - j0) * SUB + a.n_lr;
+      const uint32_t buf = it & 1, tph = (it >> 1) & 1;
+      if (!mbar_wait(&tfull[buf], tph)) {
+        tc_timeout(&s_abort);
+        break;
+      }
+      tc_fence_after();
+      float v[BP];
+      if (n_tot > 0) {
+#pragma unroll
+        for (int c0 = 0; c0 < BP; c0 += 16) {
+          uint32_t r[16];
+          tmem_ld16(tmem + (uint32_t(32 * q) << 16) + buf * BP + c0, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 16; ++j) v[c0 + j] = __uint_as_float(r[j]);
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < BP; ++j) v[j] = 0.f;
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[buf]);
+
+      const int64_t tok = int64_t(mt) * kTileM + row;
+      if (tok < a.M) {
+        TI* yr = y + tok * a.ldy + int64_t(br) * BP;
+        if (MODE == MODE_ADDMM) {
+#pragma unroll
+          for (int c = 0; c < BP; c += 8) {
+            const uint4 o = *reinterpret_cast<const uint4*>(yr + c);
+            const uint32_t ow[4] = {o.x, o.y, o.z, o.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const float2 f = unpack2(ow[j], (TI*)nullptr);
+              v[c + 2 * j] = f.x + v[c + 2 * j];
+              v[c + 2 * j + 1] = f.y + v[c + 2 * j + 1];
+            }
+          }
+        } else if (bias != nullptr) {
+          const TI* bb = bias + int64_t(br) * BP;
+#pragma unroll
+          for (int c = 0; c < BP; c += 8) {
+            const uint4 o = __ldg(reinterpret_cast<const uint4*>(bb + c));
+            const uint32_t ow[4] = {o.x, o.y, o.z, o.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const float2 f = unpack2(ow[j], (TI*)nullptr);
+              v[c + 2 * j] = v[c + 2 * j] + f.x;
+              v[c + 2 * j + 1] = v[c + 2 * j + 1] + f.y;
+            }
+          }
+        }
+#pragma unroll
+        for (int c = 0; c < BP; c += 8) {
+          uint4 o;
+          o.x = pack2(v[c + 0], v[c + 1], (TI*)nullptr);
+          o.y = pack2(v[c + 2], v[c + 3], (TI*)nullptr);
+          o.z = pack2(v[c + 4], v[c + 5], (TI*)nullptr);
+          o.w = pack2(v[c + 6], v[c + 7], (TI*)nullptr);
+          *reinterpret_cast<uint4*>(yr + c) = o;
+        }
+      }
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------- dense GEMM --
+
+struct DenseArgs {
+  void* H;
+  int64_t M, ldh;
+  int n_mtiles, n_ntiles, n_k;
+};
+
+template <typename TI>
+__global__ void __launch_bounds__(kThreads, 1)
+    tc_dense_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_b,
+                    const DenseArgs a) {
+  constexpr int BN = 64;
+  constexpr uint32_t A_BYTES = kTileM * 128, B_BYTES = BN * 128;
+  constexpr uint32_t STAGE = A_BYTES + B_BYTES;
+  constexpr int STAGES = 8;
+  constexpr uint32_t TMEM_COLS = 2 * BN;
+  constexpr uint32_t IDESC = idesc_f16<TI>(kTileM, BN, false);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  __shared__ volatile int s_abort;
+
+  pdl_launch_dependents();  // the combine kernel may start its sparse part
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 4);
+    }
+    fence_mbar_init();
+    s_abort = 0;
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int n_items = a.n_mtiles * a.n_ntiles;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tm_x);
+      tma_prefetch_desc(&tm_b);
+      uint32_t g = 0;
+      for (int item = blockIdx.x; item < n_items && !s_abort; item += gridDim.x) {
+        const int mt = item % a.n_mtiles, nt = item / a.n_mtiles;
+        for (int s = 0; s < a.n_k; ++s, ++g) {
+          const uint32_t slot = g % STAGES, ph = (g / STAGES) & 1;
+          if (!mbar_wait(&empty[slot], ph ^ 1)) {
+            tc_timeout(&s_abort);
+            break;
+          }
+          uint8_t* adst = smem + slot * STAGE;
+          mbar_arrive_expect_tx(&full[slot], STAGE);
+          tma_load_2d(adst, &tm_x, s * 64, mt * kTileM, &full[slot]);
+          tma_load_2d(adst + A_BYTES, &tm_b, s * 64, nt * BN, &full[slot]);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      uint32_t g = 0, it = 0;
+      for (int item = blockIdx.x; item < n_items && !s_abort; item += gridDim.x, ++it) {
+        const uint32_t buf = it & 1, tph = (it >> 1) & 1;
+        if (!mbar_wait(&tempty[buf], tph ^ 1)) {
+          tc_timeout(&s_abort);
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem + buf * BN;
+        uint32_t acc = 0;
+        for (int s = 0; s < a.n_k; ++s, ++g) {
+          const uint32_t slot = g % STAGES, ph = (g / STAGES) & 1;
+          if (!mbar_wait(&full[slot], ph)) {
+            tc_timeout(&s_abort);
+            break;
+          }
+          tc_fence_after();
+          const uint32_t abase = smem_u32(smem + slot * STAGE);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            umma_f16(d, sdesc(abase + kk * 32, 16, 1024, 2), sdesc(abase + A_BYTES + kk * 32, 16, 1024, 2),
+                     IDESC, acc);
+            acc = 1;
+          }
+          umma_commit(&empty[slot]);
+        }
+        umma_commit(&tfull[buf]);
+      }
+    }
+  } else {
+    const int q = warp & 3;
+    const int row = 32 * q + lane;
+    TI* __restrict__ H = static_cast<TI*>(a.H);
+    uint32_t it = 0;
+    for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++it) {
+      const int mt = item % a.n_mtiles, nt = item / a.n_mtiles;
+      const uint32_t buf = it & 1, tph = (it >> 1) & 1;
+      if (!mbar_wait(&tfull[buf], tph)) {
+        tc_timeout(&s_abort);
+        break;
+      }
+      tc_fence_after();
+      uint32_t packed[BN / 2];
+#pragma unroll
+      for (int c0 = 0; c0 < BN; c0 += 16) {
+        uint32_t r[16];
+        tmem_ld16(tmem + (uint32_t(32 * q) << 16) + buf * BN + c0, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          packed[c0 / 2 + j] = pack2(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]), (TI*)nullptr);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[buf]);
+      const int64_t tok = int64_t(mt) * kTileM + row;
+      if (tok < a.M) {
+        uint4* hr = reinterpret_cast<uint4*>(H + tok * a.ldh + int64_t(nt) * BN);
+#pragma unroll
+        for (int c = 0; c < BN / 8; ++c)
+          hr[c] = make_uint4(packed[4 * c], packed[4 * c + 1], packed[4 * c + 2], packed[4 * c + 3]);
+      }
+    }
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+int num_sms() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
+template <int BP, int BQ, typename TI, int MODE>
+int launch_rowblock_inst(const CUtensorMap& tx, const CUtensorMap& tv, const CUtensorMap& th,
+                         const CUtensorMap& ta, const TcArgs& k, bool pdl, cudaStream_t s) {
+  constexpr int KS = BQ < 64 ? BQ : 64;
+  constexpr uint32_t B_SLOT = (KS * BP * 2) > (BP * 128) ? (KS * BP * 2) : (BP * 128);
+  constexpr uint32_t STAGE = 16384 + B_SLOT;
+  constexpr int STAGES = (196 * 1024) / STAGE > 8 ? 8 : (196 * 1024) / STAGE;
+  const size_t smem = 1024 + size_t(STAGES) * STAGE + (2 * STAGES + 4) * 8 + 16;
+  auto kern = tc_rowblock_kernel<BP, BQ, TI, MODE>;
+  SLR_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+  const int items = k.nrows * k.n_mtiles;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(std::min(items, num_sms())));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  SLR_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kern, tx, tv, th, ta, k));
+  return SLR_OK;
+}
+
+template <int BP, typename TI, int MODE>
+int dispatch_bq(int bq, const CUtensorMap& tx, const CUtensorMap& tv, const CUtensorMap& th,
+                const CUtensorMap& ta, const TcArgs& k, bool pdl, cudaStream_t s) {
+  switch (bq) {
+    case 16: return launch_rowblock_inst<BP, 16, TI, MODE>(tx, tv, th, ta, k, pdl, s);
+    case 32: return launch_rowblock_inst<BP, 32, TI, MODE>(tx, tv, th, ta, k, pdl, s);
+    case 64: return launch_rowblock_inst<BP, 64, TI, MODE>(tx, tv, th, ta, k, pdl, s);
+    case 128: return launch_rowblock_inst<BP, 128, TI, MODE>(tx, tv, th, ta, k, pdl, s);
+    default: return fail(SLR_ERR_UNSUPPORTED, "tcgen05 path: block_q must be 16, 32, 64 or 128");
+  }
+}
+
+template <typename TI, int MODE>
+int dispatch_bp(int bp, int bq, const CUtensorMap& tx, const CUtensorMap& tv, const CUtensorMap& th,
+                const CUtensorMap& ta, const TcArgs& k, bool pdl, cudaStream_t s) {
+  switch (bp) {
+    case 16: return dispatch_bq<16, TI, MODE>(bq, tx, tv, th, ta, k, pdl, s);
+    case 32: return dispatch_bq<32, TI, MODE>(bq, tx, tv, th, ta, k, pdl, s);
+    case 64: return dispatch_bq<64, TI, MODE>(bq, tx, tv, th, ta, k, pdl, s);
+    default: return fail(SLR_ERR_UNSUPPORTED, "tcgen05 path: block_p must be 16, 32 or 64");
+  }
+}
+
+}  // namespace
+
+bool tc_rowblock_supported(const RowblockArgs& a) {
+  if (a.dtype == SLR_F32) return false;
+  if (a.bp != 16 && a.bp != 32 && a.bp != 64) return false;
+  if (a.crow != nullptr && a.bq != 16 && a.bq != 32 && a.bq != 64 && a.bq != 128) return false;
+  if (a.mode == MODE_FUSED && a.r != 0 && (a.r < 64 || a.r % 8 != 0)) return false;
+  if (a.ldx % 8 != 0 || a.ldy % 8 != 0 || a.K % 8 != 0 || a.K < 64 || a.M < kTileM) return false;
+  if (!aligned16(a.x) || !aligned16(a.y)) return false;
+  if (a.crow != nullptr && !aligned16(a.values)) return false;
+  if (a.mode == MODE_FUSED && a.r != 0 && !aligned16(a.A)) return false;
+  if (a.bias != nullptr && !aligned16(a.bias)) return false;
+  return a.nrows <= (1 << 24) && ceil_div(a.M, kTileM) <= (1 << 20);
+}
+
+int launch_tc_rowblock(const RowblockArgs& a, bool pdl, cudaStream_t s) {
+  if (a.nrows <= 0 || a.M <= 0) return SLR_OK;
+  const bool sparse = a.crow != nullptr && a.nnz > 0;
+  const int bq = sparse ? a.bq : 64;
+  const int ks = bq < 64 ? bq : 64;
+  CUtensorMap tx{}, tv{}, th{}, ta{};
+  int rc = make_tmap_2d(&tx, a.x, a.dtype, uint64_t(a.K), uint64_t(a.M), uint64_t(a.ldx) * 2, uint32_t(ks),
+                        uint32_t(kTileM));
+  if (rc) return rc;
+  if (sparse) {
+    rc = make_tmap_2d(&tv, a.values, a.dtype, uint64_t(a.bp), uint64_t(a.nnz) * a.bq, uint64_t(a.bp) * 2,
+                      uint32_t(a.bp), uint32_t(ks));
+    if (rc) return rc;
+  }
+  TcArgs k{a.y, a.mode == MODE_FUSED ? a.bias : nullptr, sparse ? a.crow : nullptr, a.col, a.rows, a.M, a.ldy,
+           int(a.nrows), int(ceil_div(a.M, kTileM)), 0};
+  if (a.mode == MODE_FUSED && a.r > 0) {
+    k.n_lr = int(ceil_div(a.r, 64));
+    rc = make_tmap_2d(&th, a.H, a.dtype, uint64_t(a.ldh), uint64_t(a.M), uint64_t(a.ldh) * 2, 64u,
+                      uint32_t(kTileM));
+    if (rc) return rc;
+    rc = make_tmap_2d(&ta, a.A, a.dtype, uint64_t(a.r), uint64_t(a.N), uint64_t(a.r) * 2, 64u, uint32_t(a.bp));
+    if (rc) return rc;
+  }
+  if (a.dtype == SLR_BF16)
+    return a.mode == MODE_ADDMM ? dispatch_bp<__nv_bfloat16, MODE_ADDMM>(a.bp, bq, tx, tv, th, ta, k, pdl, s)
+                                : dispatch_bp<__nv_bfloat16, MODE_FUSED>(a.bp, bq, tx, tv, th, ta, k, pdl, s);
+  return a.mode == MODE_ADDMM ? dispatch_bp<__half, MODE_ADDMM>(a.bp, bq, tx, tv, th, ta, k, pdl, s)
+                              : dispatch_bp<__half, MODE_FUSED>(a.bp, bq, tx, tv, th, ta, k, pdl, s);
+}
+
+bool tc_dense_supported(const void* x, int64_t ldx, const void* B, int64_t K, int64_t r, int dtype) {
+  return dtype != SLR_F32 && r >= 64 && K >= 64 && K % 8 == 0 && ldx % 8 == 0 && aligned16(x) && aligned16(B);
+}
+
+int launch_tc_dense(const void* x, int64_t ldx, const void* B, void* H, int64_t M, int64_t K, int64_t r,
+                    int64_t ldh, int dtype, cudaStream_t s) {
+  if (M <= 0 || r <= 0) return SLR_OK;
+  CUtensorMap tx{}, tb{};
+  int rc = make_tmap_2d(&tx, x, dtype, uint64_t(K), uint64_t(M), uint64_t(ldx) * 2, 64u, uint32_t(kTileM));
+  if (rc) return rc;
+  rc = make_tmap_2d(&tb, B, dtype, uint64_t(K), uint64_t(r), uint64_t(K) * 2, 64u, 64u);
+  if (rc) return rc;
+  DenseArgs k{H, M, ldh, int(ceil_div(M, kTileM)), int(ldh / 64), int(ceil_div(K, 64))};
+  const size_t smem = 1024 + 8 * (kTileM * 128 + 64 * 128) + (2 * 8 + 4) * 8 + 16;
+  const int items = k.n_mtiles * k.n_ntiles;
+  auto launch = [&](auto kern) -> int {
+    SLR_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+    kern<<<unsigned(std::min(items, num_sms())), kThreads, smem, s>>>(tx, tb, k);
+    SLR_CHECK_LAUNCH("tc_dense_kernel");
+    return SLR_OK;
+  };
+  if (dtype == SLR_BF16) return launch(tc_dense_kernel<__nv_bfloat16>);
+  return launch(tc_dense_kernel<__half>);
+}
+
+int read_and_clear_status_tc(unsigned* out) {
+  unsigned v = 0, zero = 0;
+  SLR_CHECK_CUDA(cudaMemcpyFromSymbol(&v, g_status_tc, sizeof(v)));
+  if (v) SLR_CHECK_CUDA(cudaMemcpyToSymbol(g_status_tc, &zero, sizeof(zero)));
+  *out = v;
+  return SLR_OK;
+}
+
+}  // namespace slr

@@ -171,9 +171,12 @@ const char* slr_last_error(void) { return t_last_error.c_str(); }
 int slr_device_status(int* status_out) {
   if (!status_out) return fail(SLR_ERR_INVALID_ARGUMENT, "status_out is NULL");
   SLR_CHECK_CUDA(cudaDeviceSynchronize());
-  unsigned v = 0;
+  unsigned v = 0, w = 0;
   int rc = read_and_clear_status_mma(&v);
   if (rc) return rc;
+  rc = read_and_clear_status_tc(&w);
+  if (rc) return rc;
+  v |= w;
   *status_out = (v & SLR_TIMEOUT_BIT) ? SLR_ERR_TIMEOUT : SLR_OK;
   return SLR_OK;
 }
@@ -213,6 +216,8 @@ int slr_bsr_addmm_inplace(void* out, const void* x, int64_t M, int64_t K, const 
   a.dtype = dtype;
   a.mode = MODE_ADDMM;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype != SLR_F32 && nnz > 0 && M >= kTcMinTokens && tc_rowblock_supported(a))
+    return launch_tc_rowblock(a, false, s);
   if (dtype != SLR_F32 && nnz > 0 && mma_rowblock_supported(a.bp, a.bq, K, 0) && aligned16(values) &&
       aligned16(x) && aligned16(out))
     return launch_mma_rowblock(a, false, s);
@@ -311,6 +316,9 @@ int prepare_forward(const slr_layer* layer, const void* x, int64_t ldx, void* y,
 
 int run_lowrank(const slr_layer& L, const FwdCall& c, cudaStream_t s) {
   if (L.rank == 0 || c.a.M == 0) return SLR_OK;
+  if (c.p.path == 1 && c.a.M >= kTcMinTokens &&
+      tc_dense_supported(c.a.x, c.a.ldx, L.B, L.in_features, L.rank, L.dtype))
+    return launch_tc_dense(c.a.x, c.a.ldx, L.B, c.ws, c.a.M, L.in_features, L.rank, c.p.ldh, L.dtype, s);
   if (c.p.path == 1)
     return launch_h_small(c.a.x, c.a.ldx, L.B, c.ws, reinterpret_cast<float*>(c.ws + c.p.part_off),
                           reinterpret_cast<unsigned*>(c.ws + c.p.cnt_off), c.a.M, L.in_features, L.rank, c.p.ldh,
@@ -321,6 +329,8 @@ int run_lowrank(const slr_layer& L, const FwdCall& c, cudaStream_t s) {
 
 int run_combine(const slr_layer& L, const FwdCall& c, bool pdl, cudaStream_t s) {
   if (c.a.M == 0) return SLR_OK;
+  if (c.p.path == 1 && c.a.M >= kTcMinTokens && tc_rowblock_supported(c.a))
+    return launch_tc_rowblock(c.a, pdl && L.rank > 0, s);
   if (c.p.path == 1) return launch_mma_rowblock(c.a, pdl && L.rank > 0, s);
   return launch_simt_rowblock(c.a, L.dtype == SLR_F32, s);
 }

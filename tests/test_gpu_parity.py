@@ -398,3 +398,94 @@ def test_reference_operator_name(cuda, oracle):
                                                         t["S_values"].to(cuda), t["S_active_rows"].to(cuda))
     assert_16bit_close(y, torch.from_numpy(ref))
     assert get_tuned_config(32, 32)["BM"] == 1
+
+
+# ------------------------------------------------- tcgen05 (M >= 128) path --
+
+TC_SHAPES = [
+    # n, k, bp, bq, r, density, bias
+    (256, 256, 64, 64, 64, 0.3, True),
+    (384, 512, 32, 32, 256, 0.3, True),
+    (256, 384, 16, 16, 128, 0.5, False),
+    (512, 512, 64, 128, 512, 0.2, True),
+    (256, 256, 32, 64, 72, 0.4, True),     # r not a multiple of 64
+    (192, 320, 64, 16, 0, 0.5, True),      # rank 0: sparse + bias only
+]
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("shape", TC_SHAPES, ids=lambda s: "x".join(map(str, s)))
+@pytest.mark.parametrize("T", [128, 129, 384, 1000])
+def test_tc_fused_matches_oracle(cuda, oracle, dtype, shape, T):
+    n, k, bp, bq, r, dens, bias = shape
+    spec = random_layer(n, k, bp, bq, r, dens, seed=n + k + r + T, bias=bias)
+    t = spec.tensors("cpu", dtype)
+    x = workloads.tokens(T, k, seed=T, dtype=dtype)
+    ref = oracle_layer(oracle, t, x, bias=bias)
+    y = ops.lrs_linear_forward(desc_for(t, spec, cuda, dtype, bias=bias), x.to(cuda))
+    assert_16bit_close(y, ref)
+
+
+@pytest.mark.parametrize("T", [128, 700])
+def test_tc_low_rank_only(cuda, oracle, T):
+    spec = random_layer(256, 192, 16, 16, 64, 0.0, seed=11)
+    t = spec.tensors("cpu", torch.bfloat16)
+    x = workloads.tokens(T, 192, seed=T, dtype=torch.bfloat16)
+    ref = oracle.lr_forward_f32(x.float(), t["A"].float(), t["B"].float(), t["bias"].float())
+    y = ops.lrs_linear_forward(desc_for(t, spec, cuda, torch.bfloat16), x.to(cuda))
+    assert_16bit_close(y, ref)
+
+
+def test_tc_strided_input_and_output(cuda, oracle):
+    """x and y as column slices of wider buffers (row strides != K, N)."""
+    spec = random_layer(256, 256, 32, 32, 64, 0.3, seed=12)
+    t = spec.tensors("cpu", torch.bfloat16)
+    x = workloads.tokens(300, 256, seed=1, dtype=torch.bfloat16)
+    ref = oracle_layer(oracle, t, x)
+    xw = torch.zeros(300, 320, dtype=torch.bfloat16, device=cuda)
+    xw[:, 32:288] = x.to(cuda)
+    yw = torch.full((300, 400), 5.0, dtype=torch.bfloat16, device=cuda)
+    d = desc_for(t, spec, cuda, torch.bfloat16)
+    d.forward(xw[:, 32:288], out=yw[:, 64:320])
+    assert_16bit_close(yw[:, 64:320], ref)
+    assert torch.all(yw[:, :64] == 5.0) and torch.all(yw[:, 320:] == 5.0)
+
+
+@pytest.mark.parametrize("M", [128, 300])
+def test_tc_addmm_leaves_empty_rows_untouched(cuda, oracle, M):
+    spec = random_layer(512, 256, 64, 64, 8, 0.25, seed=M)
+    assert (np.diff(spec.crow) == 0).any()
+    t = spec.tensors("cpu", torch.bfloat16)
+    x = workloads.tokens(M, 256, seed=3, dtype=torch.bfloat16)
+    out0 = workloads.tokens(M, 512, seed=4, dtype=torch.bfloat16)
+    ref = out0.float().numpy().copy()
+    oracle.bsr_addmm_f32_(ref, x.float(), t["S_crow"], t["S_col"], t["S_values"].float(), t["S_active_rows"])
+    out = out0.to(cuda)
+    ops.bsr_addmm_inplace_(out, x.to(cuda), t["S_crow"].to(cuda), t["S_col"].to(cuda), t["S_values"].to(cuda),
+                           t["S_active_rows"].to(cuda))
+    assert_16bit_close(out, torch.from_numpy(ref))
+    empty = np.nonzero(np.diff(spec.crow) == 0)[0]
+    for br in empty:
+        assert torch.equal(out[:, br * 64:(br + 1) * 64].cpu(), out0[:, br * 64:(br + 1) * 64])
+
+
+def test_two_phase_calls_equal_forward(cuda):
+    for T in (4, 300):
+        spec = random_layer(256, 256, 32, 32, 64, 0.3, seed=T)
+        t = spec.tensors("cpu", torch.bfloat16)
+        d = desc_for(t, spec, cuda, torch.bfloat16)
+        x = workloads.tokens(T, 256, seed=2, dtype=torch.bfloat16).to(cuda)
+        y1 = d.forward(x)
+        d.lowrank(x)
+        y2 = d.combine(x, torch.empty_like(y1))
+        assert torch.equal(y1, y2)
+
+
+def test_device_status_is_clean(cuda):
+    import ctypes
+
+    from s_salaad_b200 import _lib
+
+    st = ctypes.c_int(-1)
+    _lib.check(_lib.load().slr_device_status(ctypes.byref(st)))
+    assert st.value == _lib.SLR_OK
