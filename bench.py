@@ -189,7 +189,11 @@ def main() -> None:
     ap.add_argument("--cpu-budget-s", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-cublas", action="store_true")
+    ap.add_argument("--ncu", action="store_true",
+                    help="profiling mode: warm-up + timed steps only (no e2e, cuBLAS or CPU legs)")
     args = ap.parse_args()
+    if args.ncu:
+        args.no_cublas = args.no_cpu_baseline = True
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
 
@@ -362,6 +366,12 @@ def main() -> None:
                  "lowrank_tflops": low_flops * K / (sum(h_ms) / 1e3) / 1e12 if sum(h_ms) else None})
 
     value = T * K / (total_ms / 1e3)
+    if args.ncu:
+        if rank == 0:
+            print(json.dumps({"ncu_mode": True, "ms_per_step": total_ms / K, "roofline": roof}), flush=True)
+        if world > 1:
+            dist.destroy_process_group()
+        return
     launches_per_step = sum((1 if s.rank > 0 else 0) + 1 for i, s in enumerate(specs) if has_local[i])
 
     # ------------------------------------------------------------- e2e

@@ -114,6 +114,16 @@ __device__ __forceinline__ float2 unpack2(uint32_t u, __half*) {
   return __half22float2(*reinterpret_cast<__half2*>(&u));
 }
 
+__device__ __forceinline__ void tmem_st16_zero(uint32_t taddr) {
+  const uint32_t z = 0;
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr),
+      "r"(z)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
 struct TcArgs {
   void* y;
   const void* bias;
@@ -121,7 +131,7 @@ struct TcArgs {
   const int32_t* col;
   const int32_t* rows;
   int64_t M, ldy;
-  int nrows, n_mtiles, n_lr;
+  int nrows, n_groups, n_mtiles, n_lr;
 };
 
 // Drain-and-exit after a bounded wait gave up: record the timeout.
@@ -130,26 +140,40 @@ __device__ __forceinline__ void tc_timeout(volatile int* abort_flag) {
   *abort_flag = 1;
 }
 
+constexpr uint32_t kMetaLR = 1u << 30;    // stage holds an H tile + rows of A
+constexpr uint32_t kMetaLast = 1u << 31;  // last stage of the work item
+
+// Persistent fused kernel.  One work item = 128 tokens x a group of
+// G = 256/BP block-rows, taken consecutively from the row list (heaviest
+// first for the fused layer), so the item's accumulator is 128 x 256 fp32 in
+// TMEM (double-buffered: all 512 columns).  The producer merges the G rows'
+// sorted column lists: each distinct column is one stage holding the x tile
+// once plus the value block of every row of the group that has that column,
+// so an x tile feeds up to G block-rows.  The low-rank steps then add
+// H[128 x 64] · A_rows[256 x 64]ᵀ with one N = 256 MMA per k-slice.  Every
+// MMA accumulates: the epilogue re-zeroes each accumulator after draining it.
 template <int BP, int BQ, typename TI, int MODE>
 __global__ void __launch_bounds__(kThreads, 1)
     tc_rowblock_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_v,
                        const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ CUtensorMap tm_a,
                        const TcArgs a) {
-  constexpr int KS = BQ < 64 ? BQ : 64;  // k per sparse step (one swizzle row)
-  constexpr int SUB = BQ / KS;           // sparse steps per block
+  constexpr int G = 256 / BP;            // block-rows per item
+  constexpr int KS = BQ < 64 ? BQ : 64;  // k per sparse stage (one swizzle row)
+  constexpr int SUB = BQ / KS;           // sparse stages per block column
   constexpr int XW = KS * 2;             // x-tile row bytes
   constexpr int VW = BP * 2;             // values row bytes
   constexpr uint32_t X_BYTES = kTileM * XW, V_BYTES = KS * VW;
   constexpr uint32_t H_BYTES = kTileM * 128, AR_BYTES = BP * 128;
   constexpr uint32_t A_SLOT = 16384;
-  constexpr uint32_t B_SLOT = V_BYTES > AR_BYTES ? V_BYTES : AR_BYTES;
+  constexpr uint32_t B_SLOT = (G * V_BYTES > G * AR_BYTES) ? G * V_BYTES : G * AR_BYTES;
   constexpr uint32_t STAGE = A_SLOT + B_SLOT;
-  constexpr int STAGES = (196 * 1024) / STAGE > 8 ? 8 : (196 * 1024) / STAGE;
-  constexpr uint32_t TMEM_COLS = 2 * BP < 32 ? 32 : 2 * BP;
+  constexpr int STAGES = 4;
+  constexpr uint32_t ACC = 256;          // accumulator columns
   constexpr uint32_t IDESC_SP = idesc_f16<TI>(kTileM, BP, true);
-  constexpr uint32_t IDESC_LR = idesc_f16<TI>(kTileM, BP, false);
+  constexpr uint32_t IDESC_LR = idesc_f16<TI>(kTileM, 256, false);
   static_assert(X_BYTES <= A_SLOT && H_BYTES <= A_SLOT, "A slot");
-  static_assert(STAGE % 1024 == 0, "stages must stay 1024-byte aligned");
+  static_assert(G * BP == 256 && G <= 16, "group must span 256 columns");
+  static_assert(STAGE % 1024 == 0 && V_BYTES % 256 == 0, "alignment of stages / value slots");
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -157,7 +181,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint32_t* meta = reinterpret_cast<uint32_t*>(tempty + 2);  // [STAGES]
+  uint32_t* tmem_slot = meta + STAGES;
   __shared__ volatile int s_abort;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -174,20 +199,28 @@ __global__ void __launch_bounds__(kThreads, 1)
     s_abort = 0;
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_alloc(tmem_slot, 2 * ACC);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const int n_items = a.nrows * a.n_mtiles;
+  if (warp >= 2) {  // both accumulators start at zero
+    const uint32_t lane_base = uint32_t(32 * (warp & 3)) << 16;
+    for (uint32_t c = 0; c < 2 * ACC; c += 16) tmem_st16_zero(tmem + lane_base + c);
+    tmem_st_wait();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const int n_items = a.n_groups * a.n_mtiles;
 
   if (warp == 0) {
     // ------------------------------------------------------- TMA producer
     if (lane == 0) {
       tma_prefetch_desc(&tm_x);
-      tma_prefetch_desc(&tm_v);
+      if (a.crow) tma_prefetch_desc(&tm_v);
       if (a.n_lr) {
         tma_prefetch_desc(&tm_h);
         tma_prefetch_desc(&tm_a);
@@ -195,35 +228,85 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool waited = false;
       uint32_t g = 0;
       for (int item = blockIdx.x; item < n_items && !s_abort; item += gridDim.x) {
-        const int ri = item / a.n_mtiles, mt = item - ri * a.n_mtiles;
-        const int br = a.rows ? a.rows[ri] : ri;
+        const int gi = item / a.n_mtiles, mt = item - gi * a.n_mtiles;
+        const int r0 = gi * G;
+        const int gcount = min(G, a.nrows - r0);
         const int m0 = mt * kTileM;
-        const int j0 = a.crow ? a.crow[br] : 0, j1 = a.crow ? a.crow[br + 1] : 0;
-        const int n_sp = (j1 - j0) * SUB, n_tot = n_sp + a.n_lr;
-        for (int s = 0; s < n_tot; ++s, ++g) {
+        int rw[G], ptr[G], end[G], cur[G];
+#pragma unroll
+        for (int j = 0; j < G; ++j) {
+          rw[j] = j < gcount ? (a.rows ? a.rows[r0 + j] : r0 + j) : 0;
+          ptr[j] = (a.crow && j < gcount) ? a.crow[rw[j]] : 0;
+          end[j] = (a.crow && j < gcount) ? a.crow[rw[j] + 1] : 0;
+          cur[j] = ptr[j] < end[j] ? __ldg(a.col + ptr[j]) : 0x7fffffff;
+        }
+        int c = 0x7fffffff;
+#pragma unroll
+        for (int j = 0; j < G; ++j) c = min(c, cur[j]);
+        bool published = false;
+        // One stage per (column, sub-slice) of the union of the group's columns.
+        while (c != 0x7fffffff && !s_abort) {
+          uint32_t mask = 0;
+          int blk[G];
+#pragma unroll
+          for (int j = 0; j < G; ++j) {
+            blk[j] = ptr[j];
+            if (cur[j] == c) {
+              mask |= 1u << j;
+              ++ptr[j];
+              cur[j] = ptr[j] < end[j] ? __ldg(a.col + ptr[j]) : 0x7fffffff;
+            }
+          }
+          int cn = 0x7fffffff;
+#pragma unroll
+          for (int j = 0; j < G; ++j) cn = min(cn, cur[j]);
+          for (int sub = 0; sub < SUB; ++sub, ++g) {
+            const uint32_t slot = g % STAGES, ph = (g / STAGES) & 1;
+            if (!mbar_wait(&empty[slot], ph ^ 1)) {
+              tc_timeout(&s_abort);
+              break;
+            }
+            const bool last = cn == 0x7fffffff && a.n_lr == 0 && sub == SUB - 1;
+            meta[slot] = mask | (last ? kMetaLast : 0u);
+            uint8_t* adst = smem + slot * STAGE;
+            mbar_arrive_expect_tx(&full[slot], X_BYTES + __popc(mask) * V_BYTES);
+            tma_load_2d(adst, &tm_x, c * BQ + sub * KS, m0, &full[slot]);
+#pragma unroll
+            for (int j = 0; j < G; ++j)
+              if (mask & (1u << j))
+                tma_load_2d(adst + A_SLOT + j * V_BYTES, &tm_v, 0, blk[j] * BQ + sub * KS, &full[slot]);
+            published = true;
+          }
+          c = cn;
+        }
+        for (int l = 0; l < a.n_lr && !s_abort; ++l, ++g) {
+          if (!waited) {
+            pdl_wait_primary();  // H comes from the preceding kernel
+            waited = true;
+          }
           const uint32_t slot = g % STAGES, ph = (g / STAGES) & 1;
           if (!mbar_wait(&empty[slot], ph ^ 1)) {
             tc_timeout(&s_abort);
             break;
           }
+          meta[slot] = kMetaLR | (l == a.n_lr - 1 ? kMetaLast : 0u);
           uint8_t* adst = smem + slot * STAGE;
-          uint8_t* bdst = adst + A_SLOT;
-          if (s < n_sp) {
-            const int blk = j0 + s / SUB, sub = s % SUB;
-            const int c = __ldg(a.col + blk);
-            mbar_arrive_expect_tx(&full[slot], X_BYTES + V_BYTES);
-            tma_load_2d(adst, &tm_x, c * BQ + sub * KS, m0, &full[slot]);
-            tma_load_2d(bdst, &tm_v, 0, blk * BQ + sub * KS, &full[slot]);
-          } else {
-            if (!waited) {
-              pdl_wait_primary();  // H comes from the preceding kernel
-              waited = true;
-            }
-            const int l = s - n_sp;
-            mbar_arrive_expect_tx(&full[slot], H_BYTES + AR_BYTES);
-            tma_load_2d(adst, &tm_h, l * 64, m0, &full[slot]);
-            tma_load_2d(bdst, &tm_a, l * 64, br * BP, &full[slot]);
+          mbar_arrive_expect_tx(&full[slot], H_BYTES + gcount * AR_BYTES);
+          tma_load_2d(adst, &tm_h, l * 64, m0, &full[slot]);
+          for (int j = 0; j < gcount; ++j)
+            tma_load_2d(adst + A_SLOT + j * AR_BYTES, &tm_a, l * 64, rw[j] * BP, &full[slot]);
+          published = true;
+        }
+        if (!published && !s_abort) {
+          // No block and no rank: a terminator stage so the item still completes.
+          const uint32_t slot = g % STAGES, ph = (g / STAGES) & 1;
+          if (!mbar_wait(&empty[slot], ph ^ 1)) {
+            tc_timeout(&s_abort);
+            break;
           }
+          meta[slot] = kMetaLast;
+          mbar_arrive(&full[slot]);
+          ++g;
         }
       }
     }
@@ -232,45 +315,43 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       uint32_t g = 0, it = 0;
       for (int item = blockIdx.x; item < n_items && !s_abort; item += gridDim.x, ++it) {
-        const int ri = item / a.n_mtiles;
-        const int br = a.rows ? a.rows[ri] : ri;
-        const int j0 = a.crow ? a.crow[br] : 0, j1 = a.crow ? a.crow[br + 1] : 0;
-        const int n_sp = (j1 - j0) * SUB, n_tot = n_sp + a.n_lr;
         const uint32_t buf = it & 1, tph = (it >> 1) & 1;
         if (!mbar_wait(&tempty[buf], tph ^ 1)) {
           tc_timeout(&s_abort);
           break;
         }
         tc_fence_after();
-        const uint32_t d = tmem + buf * BP;
-        uint32_t acc = 0;
-        for (int s = 0; s < n_tot; ++s, ++g) {
+        const uint32_t d = tmem + buf * ACC;
+        while (true) {
           const uint32_t slot = g % STAGES, ph = (g / STAGES) & 1;
           if (!mbar_wait(&full[slot], ph)) {
             tc_timeout(&s_abort);
             break;
           }
           tc_fence_after();
+          const uint32_t m = meta[slot];
           const uint32_t abase = smem_u32(smem + slot * STAGE);
           const uint32_t bbase = abase + A_SLOT;
-          if (s < n_sp) {
+          if (m & kMetaLR) {
 #pragma unroll
-            for (int kk = 0; kk < KS / 16; ++kk) {
-              const uint64_t ad = sdesc(abase + kk * 32, 16, 8 * XW, layout_for(XW));
-              const uint64_t bd = sdesc(bbase + kk * 16 * VW, V_BYTES, 8 * VW, layout_for(VW));
-              umma_f16(d, ad, bd, IDESC_SP, acc);
-              acc = 1;
-            }
+            for (int kk = 0; kk < 4; ++kk)
+              umma_f16(d, sdesc(abase + kk * 32, 16, 1024, 2), sdesc(bbase + kk * 32, 16, 1024, 2), IDESC_LR, 1u);
           } else {
+            uint32_t mask = m & 0xffffu;
+            while (mask) {
+              const int j = __ffs(mask) - 1;
+              mask &= mask - 1;
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {
-              const uint64_t ad = sdesc(abase + kk * 32, 16, 1024, 2);
-              const uint64_t bd = sdesc(bbase + kk * 32, 16, 1024, 2);
-              umma_f16(d, ad, bd, IDESC_LR, acc);
-              acc = 1;
+              for (int kk = 0; kk < KS / 16; ++kk) {
+                const uint64_t ad = sdesc(abase + kk * 32, 16, 8 * XW, layout_for(XW));
+                const uint64_t bd = sdesc(bbase + j * V_BYTES + kk * 16 * VW, V_BYTES, 8 * VW, layout_for(VW));
+                umma_f16(d + j * BP, ad, bd, IDESC_SP, 1u);
+              }
             }
           }
           umma_commit(&empty[slot]);  // frees the stage once these MMAs finish
+          ++g;
+          if (m & kMetaLast) break;
         }
         umma_commit(&tfull[buf]);     // accumulator ready for the epilogue
       }
@@ -278,85 +359,83 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // ---------------------------------------------------------- epilogue
     const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const uint32_t lane_base = uint32_t(32 * q) << 16;
     const int row = 32 * q + lane;
     TI* __restrict__ y = static_cast<TI*>(a.y);
     const TI* __restrict__ bias = static_cast<const TI*>(a.bias);
     uint32_t it = 0;
     for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++it) {
-      const int ri = item / a.n_mtiles, mt = item - ri * a.n_mtiles;
-      const int br = a.rows ? a.rows[ri] : ri;
-      const int j0 = a.crow ? a.crow[br] : 0, j1 = a.crow ? a.crow[br + 1] : 0;
-      const int n_tot = (j1 - j0) * SUB + a.n_lr;
+      const int gi = item / a.n_mtiles, mt = item - gi * a.n_mtiles;
+      const int r0 = gi * G;
+      const int gcount = min(G, a.nrows - r0);
       const uint32_t buf = it & 1, tph = (it >> 1) & 1;
       if (!mbar_wait(&tfull[buf], tph)) {
         tc_timeout(&s_abort);
         break;
       }
       tc_fence_after();
-      float v[BP];
-      if (n_tot > 0) {
+      const int64_t tok = int64_t(mt) * kTileM + row;
+      const uint32_t acc = tmem + lane_base + buf * ACC;
+      for (int j = 0; j < G; ++j) {
+        if (j >= gcount) {
+#pragma unroll
+          for (int c0 = 0; c0 < BP; c0 += 16) tmem_st16_zero(acc + j * BP + c0);
+          continue;
+        }
+        const int br = a.rows ? a.rows[r0 + j] : r0 + j;
+        TI* yr = y + tok * a.ldy + int64_t(br) * BP;
+        const TI* bb = bias ? bias + int64_t(br) * BP : nullptr;
 #pragma unroll
         for (int c0 = 0; c0 < BP; c0 += 16) {
           uint32_t r[16];
-          tmem_ld16(tmem + (uint32_t(32 * q) << 16) + buf * BP + c0, r);
+          tmem_ld16(acc + j * BP + c0, r);
           tmem_ld_wait();
+          tmem_st16_zero(acc + j * BP + c0);
+          if (tok < a.M) {
+            float v[16];
 #pragma unroll
-          for (int j = 0; j < 16; ++j) v[c0 + j] = __uint_as_float(r[j]);
+            for (int e = 0; e < 16; ++e) v[e] = __uint_as_float(r[e]);
+            if (MODE == MODE_ADDMM || bb != nullptr) {
+              const TI* src = MODE == MODE_ADDMM ? yr + c0 : bb + c0;
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                const uint4 o = MODE == MODE_ADDMM ? *reinterpret_cast<const uint4*>(src + 8 * h)
+                                                   : __ldg(reinterpret_cast<const uint4*>(src + 8 * h));
+                const uint32_t ow[4] = {o.x, o.y, o.z, o.w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  const float2 f = unpack2(ow[e], (TI*)nullptr);
+                  // in-place operator: old + sum (the reference's acc = out; acc += ...)
+                  v[8 * h + 2 * e] = MODE == MODE_ADDMM ? f.x + v[8 * h + 2 * e] : v[8 * h + 2 * e] + f.x;
+                  v[8 * h + 2 * e + 1] = MODE == MODE_ADDMM ? f.y + v[8 * h + 2 * e + 1] : v[8 * h + 2 * e + 1] + f.y;
+                }
+              }
+            }
+            uint4 o0, o1;
+            o0.x = pack2(v[0], v[1], (TI*)nullptr);
+            o0.y = pack2(v[2], v[3], (TI*)nullptr);
+            o0.z = pack2(v[4], v[5], (TI*)nullptr);
+            o0.w = pack2(v[6], v[7], (TI*)nullptr);
+            o1.x = pack2(v[8], v[9], (TI*)nullptr);
+            o1.y = pack2(v[10], v[11], (TI*)nullptr);
+            o1.z = pack2(v[12], v[13], (TI*)nullptr);
+            o1.w = pack2(v[14], v[15], (TI*)nullptr);
+            reinterpret_cast<uint4*>(yr + c0)[0] = o0;
+            reinterpret_cast<uint4*>(yr + c0)[1] = o1;
+          }
         }
-      } else {
-#pragma unroll
-        for (int j = 0; j < BP; ++j) v[j] = 0.f;
       }
+      tmem_st_wait();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[buf]);
-
-      const int64_t tok = int64_t(mt) * kTileM + row;
-      if (tok < a.M) {
-        TI* yr = y + tok * a.ldy + int64_t(br) * BP;
-        if (MODE == MODE_ADDMM) {
-#pragma unroll
-          for (int c = 0; c < BP; c += 8) {
-            const uint4 o = *reinterpret_cast<const uint4*>(yr + c);
-            const uint32_t ow[4] = {o.x, o.y, o.z, o.w};
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const float2 f = unpack2(ow[j], (TI*)nullptr);
-              v[c + 2 * j] = f.x + v[c + 2 * j];
-              v[c + 2 * j + 1] = f.y + v[c + 2 * j + 1];
-            }
-          }
-        } else if (bias != nullptr) {
-          const TI* bb = bias + int64_t(br) * BP;
-#pragma unroll
-          for (int c = 0; c < BP; c += 8) {
-            const uint4 o = __ldg(reinterpret_cast<const uint4*>(bb + c));
-            const uint32_t ow[4] = {o.x, o.y, o.z, o.w};
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const float2 f = unpack2(ow[j], (TI*)nullptr);
-              v[c + 2 * j] = v[c + 2 * j] + f.x;
-              v[c + 2 * j + 1] = v[c + 2 * j + 1] + f.y;
-            }
-          }
-        }
-#pragma unroll
-        for (int c = 0; c < BP; c += 8) {
-          uint4 o;
-          o.x = pack2(v[c + 0], v[c + 1], (TI*)nullptr);
-          o.y = pack2(v[c + 2], v[c + 3], (TI*)nullptr);
-          o.z = pack2(v[c + 4], v[c + 5], (TI*)nullptr);
-          o.w = pack2(v[c + 6], v[c + 7], (TI*)nullptr);
-          *reinterpret_cast<uint4*>(yr + c) = o;
-        }
-      }
     }
   }
 
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, TMEM_COLS);
+    tmem_dealloc(tmem, 2 * ACC);
   }
 }
 
@@ -368,14 +447,13 @@ struct DenseArgs {
   int n_mtiles, n_ntiles, n_k;
 };
 
-template <typename TI>
+template <int BN, typename TI>
 __global__ void __launch_bounds__(kThreads, 1)
     tc_dense_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_b,
                     const DenseArgs a) {
-  constexpr int BN = 64;
   constexpr uint32_t A_BYTES = kTileM * 128, B_BYTES = BN * 128;
   constexpr uint32_t STAGE = A_BYTES + B_BYTES;
-  constexpr int STAGES = 8;
+  constexpr int STAGES = (196 * 1024) / STAGE > 8 ? 8 : (196 * 1024) / STAGE;
   constexpr uint32_t TMEM_COLS = 2 * BN;
   constexpr uint32_t IDESC = idesc_f16<TI>(kTileM, BN, false);
 
@@ -428,7 +506,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* adst = smem + slot * STAGE;
           mbar_arrive_expect_tx(&full[slot], STAGE);
           tma_load_2d(adst, &tm_x, s * 64, mt * kTileM, &full[slot]);
-          tma_load_2d(adst + A_BYTES, &tm_b, s * 64, nt * BN, &full[slot]);
+#pragma unroll
+          for (int j = 0; j < BN / 64; ++j)
+            tma_load_2d(adst + A_BYTES + j * 8192, &tm_b, s * 64, nt * BN + j * 64, &full[slot]);
         }
       }
     }
@@ -476,26 +556,24 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
-      uint32_t packed[BN / 2];
-#pragma unroll
+      const int64_t tok = int64_t(mt) * kTileM + row;
+#pragma unroll 1
       for (int c0 = 0; c0 < BN; c0 += 16) {
         uint32_t r[16];
         tmem_ld16(tmem + (uint32_t(32 * q) << 16) + buf * BN + c0, r);
         tmem_ld_wait();
+        uint32_t p[8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j)
-          packed[c0 / 2 + j] = pack2(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]), (TI*)nullptr);
+        for (int j = 0; j < 8; ++j) p[j] = pack2(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]), (TI*)nullptr);
+        if (tok < a.M) {
+          uint4* hr = reinterpret_cast<uint4*>(H + tok * a.ldh + int64_t(nt) * BN + c0);
+          hr[0] = make_uint4(p[0], p[1], p[2], p[3]);
+          hr[1] = make_uint4(p[4], p[5], p[6], p[7]);
+        }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[buf]);
-      const int64_t tok = int64_t(mt) * kTileM + row;
-      if (tok < a.M) {
-        uint4* hr = reinterpret_cast<uint4*>(H + tok * a.ldh + int64_t(nt) * BN);
-#pragma unroll
-        for (int c = 0; c < BN / 8; ++c)
-          hr[c] = make_uint4(packed[4 * c], packed[4 * c + 1], packed[4 * c + 2], packed[4 * c + 3]);
-      }
     }
   }
   __syncthreads();
@@ -519,14 +597,14 @@ int num_sms() {
 template <int BP, int BQ, typename TI, int MODE>
 int launch_rowblock_inst(const CUtensorMap& tx, const CUtensorMap& tv, const CUtensorMap& th,
                          const CUtensorMap& ta, const TcArgs& k, bool pdl, cudaStream_t s) {
+  constexpr int G = 256 / BP;
   constexpr int KS = BQ < 64 ? BQ : 64;
-  constexpr uint32_t B_SLOT = (KS * BP * 2) > (BP * 128) ? (KS * BP * 2) : (BP * 128);
-  constexpr uint32_t STAGE = 16384 + B_SLOT;
-  constexpr int STAGES = (196 * 1024) / STAGE > 8 ? 8 : (196 * 1024) / STAGE;
-  const size_t smem = 1024 + size_t(STAGES) * STAGE + (2 * STAGES + 4) * 8 + 16;
+  constexpr uint32_t V = KS * BP * 2, AR = BP * 128;
+  constexpr uint32_t STAGE = 16384 + (G * V > G * AR ? G * V : G * AR);
+  const size_t smem = 1024 + size_t(4) * STAGE + (2 * 4 + 4) * 8 + 4 * 4 + 16;
   auto kern = tc_rowblock_kernel<BP, BQ, TI, MODE>;
   SLR_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
-  const int items = k.nrows * k.n_mtiles;
+  const int items = k.n_groups * k.n_mtiles;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(unsigned(std::min(items, num_sms())));
   cfg.blockDim = dim3(kThreads);
@@ -593,8 +671,9 @@ int launch_tc_rowblock(const RowblockArgs& a, bool pdl, cudaStream_t s) {
                       uint32_t(a.bp), uint32_t(ks));
     if (rc) return rc;
   }
+  const int G = 256 / a.bp;
   TcArgs k{a.y, a.mode == MODE_FUSED ? a.bias : nullptr, sparse ? a.crow : nullptr, a.col, a.rows, a.M, a.ldy,
-           int(a.nrows), int(ceil_div(a.M, kTileM)), 0};
+           int(a.nrows), int(ceil_div(a.nrows, G)), int(ceil_div(a.M, kTileM)), 0};
   if (a.mode == MODE_FUSED && a.r > 0) {
     k.n_lr = int(ceil_div(a.r, 64));
     rc = make_tmap_2d(&th, a.H, a.dtype, uint64_t(a.ldh), uint64_t(a.M), uint64_t(a.ldh) * 2, 64u,
@@ -622,17 +701,31 @@ int launch_tc_dense(const void* x, int64_t ldx, const void* B, void* H, int64_t 
   if (rc) return rc;
   rc = make_tmap_2d(&tb, B, dtype, uint64_t(K), uint64_t(r), uint64_t(K) * 2, 64u, 64u);
   if (rc) return rc;
-  DenseArgs k{H, M, ldh, int(ceil_div(M, kTileM)), int(ldh / 64), int(ceil_div(K, 64))};
-  const size_t smem = 1024 + 8 * (kTileM * 128 + 64 * 128) + (2 * 8 + 4) * 8 + 16;
+  const int n_mtiles = int(ceil_div(M, kTileM));
+  // Widest tile that divides ldh and still gives the SMs work: wide tiles
+  // move fewer operand bytes per MAC (the bound of this kernel).
+  int bn = 64;
+  if (ldh % 256 == 0 && int64_t(n_mtiles) * (ldh / 256) * 2 >= num_sms()) bn = 256;
+  else if (ldh % 128 == 0) bn = 128;
+  DenseArgs k{H, M, ldh, n_mtiles, int(ldh / bn), int(ceil_div(K, 64))};
   const int items = k.n_mtiles * k.n_ntiles;
-  auto launch = [&](auto kern) -> int {
+  auto launch = [&](auto kern, int BN) -> int {
+    const uint32_t stage = kTileM * 128 + BN * 128;
+    const int stages = std::min(8, int((196 * 1024) / stage));
+    const size_t smem = 1024 + size_t(stages) * stage + (2 * stages + 4) * 8 + 16;
     SLR_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
     kern<<<unsigned(std::min(items, num_sms())), kThreads, smem, s>>>(tx, tb, k);
     SLR_CHECK_LAUNCH("tc_dense_kernel");
     return SLR_OK;
   };
-  if (dtype == SLR_BF16) return launch(tc_dense_kernel<__nv_bfloat16>);
-  return launch(tc_dense_kernel<__half>);
+  if (dtype == SLR_BF16) {
+    if (bn == 256) return launch(tc_dense_kernel<256, __nv_bfloat16>, 256);
+    if (bn == 128) return launch(tc_dense_kernel<128, __nv_bfloat16>, 128);
+    return launch(tc_dense_kernel<64, __nv_bfloat16>, 64);
+  }
+  if (bn == 256) return launch(tc_dense_kernel<256, __half>, 256);
+  if (bn == 128) return launch(tc_dense_kernel<128, __half>, 128);
+  return launch(tc_dense_kernel<64, __half>, 64);
 }
 
 int read_and_clear_status_tc(unsigned* out) {
