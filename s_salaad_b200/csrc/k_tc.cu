@@ -149,7 +149,8 @@ constexpr uint32_t kMetaLast = 1u << 31;  // last stage of the work item
 // TMEM (double-buffered: all 512 columns).  The producer merges the G rows'
 // sorted column lists: each distinct column is one stage holding the x tile
 // once plus the value block of every row of the group that has that column,
-// so an x tile feeds up to G block-rows.  The low-rank steps then add
+// so an x tile feeds up to G block-rows, and each run of consecutive rows
+// present in a stage is one MMA with N = run length * BP.  The low-rank steps then add
 // H[128 x 64] · A_rows[256 x 64]ᵀ with one N = 256 MMA per k-slice.  Every
 // MMA accumulates: the epilogue re-zeroes each accumulator after draining it.
 template <int BP, int BQ, typename TI, int MODE>
@@ -169,7 +170,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr uint32_t STAGE = A_SLOT + B_SLOT;
   constexpr int STAGES = 4;
   constexpr uint32_t ACC = 256;          // accumulator columns
-  constexpr uint32_t IDESC_SP = idesc_f16<TI>(kTileM, BP, true);
+  constexpr uint32_t IDESC_SP = idesc_f16<TI>(kTileM, 0, true);  // N set per run of rows
   constexpr uint32_t IDESC_LR = idesc_f16<TI>(kTileM, 256, false);
   static_assert(X_BYTES <= A_SLOT && H_BYTES <= A_SLOT, "A slot");
   static_assert(G * BP == 256 && G <= 16, "group must span 256 columns");
@@ -337,15 +338,20 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int kk = 0; kk < 4; ++kk)
               umma_f16(d, sdesc(abase + kk * 32, 16, 1024, 2), sdesc(bbase + kk * 32, 16, 1024, 2), IDESC_LR, 1u);
           } else {
+            // One MMA per run of consecutive rows that have this column: their
+            // value slots are adjacent N-atoms (LBO = slot stride), so the x
+            // k-slice is read from shared memory once per run, not per row.
             uint32_t mask = m & 0xffffu;
             while (mask) {
               const int j = __ffs(mask) - 1;
-              mask &= mask - 1;
+              const int len = __ffs(~(mask >> j)) - 1;
+              mask &= ~(((1u << len) - 1u) << j);
+              const uint32_t idesc = IDESC_SP | (uint32_t(len * BP) >> 3) << 17;
 #pragma unroll
               for (int kk = 0; kk < KS / 16; ++kk) {
                 const uint64_t ad = sdesc(abase + kk * 32, 16, 8 * XW, layout_for(XW));
                 const uint64_t bd = sdesc(bbase + j * V_BYTES + kk * 16 * VW, V_BYTES, 8 * VW, layout_for(VW));
-                umma_f16(d + j * BP, ad, bd, IDESC_SP, 1u);
+                umma_f16(d + j * BP, ad, bd, idesc, 1u);
               }
             }
           }
