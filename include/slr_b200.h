@@ -188,6 +188,22 @@ SLR_API int slr_lrs_linear_combine(const slr_layer* layer, const void* x, int64_
                            void* y, int64_t ldy, int64_t M, void* workspace,
                            size_t workspace_bytes, void* stream);
 
+/*
+ * slr_lrs_linear_forward without a workspace argument, for callers that
+ * cannot allocate device memory (a plugin inside a framework that owns all
+ * allocations, code running under someone else's stream capture, a serving
+ * loop that must not enter the allocator).  No counterpart in the reference.
+ * Scratch comes from a fixed 16 MiB array in this library's device image
+ * (held by every GPU that loads the library until exit); a token count that
+ * needs more is rejected with SLR_ERR_WORKSPACE before any launch.  The first
+ * call on a device looks up the array's address for that device: make it
+ * before any stream capture.  All calls share the array (each clears what it
+ * uses on `stream`); calls that overlap on the GPU race on it.
+ */
+SLR_API int slr_lrs_linear_forward_noalloc(const slr_layer* layer, const void* x,
+                           int64_t ldx, void* y, int64_t ldy, int64_t M,
+                           void* stream);
+
 /* --------------------------------------------------- dense -> BSR -- */
 
 /*

@@ -36,6 +36,7 @@ EXPORTED = (
     "slr_lrs_linear_forward",
     "slr_lrs_linear_lowrank",
     "slr_lrs_linear_combine",
+    "slr_lrs_linear_forward_noalloc",
     "slr_dense_to_bsr_mask",
     "slr_dense_to_bsr_fill",
     "slr_plan_row_order",
@@ -78,6 +79,7 @@ _SIGS = {
     "slr_lrs_linear_forward": ([ctypes.POINTER(SlrLayer), vp, i64, vp, i64, i64, vp, sz, vp], i32),
     "slr_lrs_linear_lowrank": ([ctypes.POINTER(SlrLayer), vp, i64, i64, vp, sz, vp], i32),
     "slr_lrs_linear_combine": ([ctypes.POINTER(SlrLayer), vp, i64, vp, i64, i64, vp, sz, vp], i32),
+    "slr_lrs_linear_forward_noalloc": ([ctypes.POINTER(SlrLayer), vp, i64, vp, i64, i64, vp], i32),
     "slr_dense_to_bsr_mask": ([vp, i64, i64, i64, i64, i32, vp, vp, vp], i32),
     "slr_dense_to_bsr_fill": ([vp, i64, i64, i64, i64, i32, vp, vp, vp, vp, i32, vp], i32),
     "slr_plan_row_order": ([vp, i64, vp], i32),
