@@ -269,7 +269,7 @@ def main() -> None:
         for i, L in enumerate(layers):
             if world > 1:
                 desc = L.desc
-                buf = L.gather_buffer(T)
+                buf = L.local_buffer(T)
                 if desc is not None:
                     out_i = buf[rank][:, :L.width]
                     if ev is not None:

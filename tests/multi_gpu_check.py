@@ -1,0 +1,56 @@
+"""Run under torchrun (one process per GPU): every rank computes its
+block-row shard of real-size layers with the CUDA kernels, NCCL all-gathers
+y, and each rank compares the result with the single-GPU forward of the full
+layer (computed on its own device).  Exit status 0 = all equal."""
+from __future__ import annotations
+
+import datetime
+import os
+import sys
+from pathlib import Path
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+sys.path.insert(0, str(Path(__file__).resolve().parent.parent))
+from s_salaad_b200 import ops, workloads  # noqa: E402
+from s_salaad_b200.shard import ShardedLayer  # noqa: E402
+
+
+def main() -> int:
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+    bad = 0
+    cases = [("cfg4", 0, 1024), ("cfg4", 6, 300), ("cfg3", 4, 16), ("cfg5", 0, 1)]
+    for cfg, idx, T in cases:
+        s = workloads.layer_set(cfg)[idx]
+        t = s.tensors(dev, torch.bfloat16)
+        x = workloads.tokens(T, s.in_features, seed=3, device=dev, dtype=torch.bfloat16)
+        order = torch.from_numpy(ops.plan_row_order(s.crow.astype(np.int32))).to(dev)
+        full = ops.LayerDesc(A=t["A"], B=t["B"], bias=t["bias"], crow=t["S_crow"], col=t["S_col"],
+                             values=t["S_values"], row_order=order, in_features=s.in_features,
+                             out_features=s.out_features, block_p=s.block_p, block_q=s.block_q)
+        ref = full.forward(x)
+        sh = ShardedLayer(t, s.crow, in_features=s.in_features, out_features=s.out_features, block_p=s.block_p,
+                          block_q=s.block_q, rank=rank, world=world)
+        y = sh.forward(x)
+        torch.cuda.synchronize()
+        err = float((y.float() - ref.float()).abs().max())
+        scale = float(ref.float().pow(2).mean().sqrt())
+        ok = err <= 1e-6 * max(scale, 1.0)
+        bad += 0 if ok else 1
+        print(f"rank {rank}/{world} {cfg}[{idx}] T={T} bounds={sh.bounds.tolist()} max|diff|={err:.3e} "
+              f"{'ok' if ok else 'MISMATCH'}", flush=True)
+    flag = torch.tensor([bad], device=dev)
+    dist.all_reduce(flag)
+    dist.barrier()
+    dist.destroy_process_group()
+    return 0 if int(flag.item()) == 0 else 1
+
+
+if __name__ == "__main__":
+    sys.exit(main())
