@@ -239,6 +239,8 @@ def main() -> None:
         from datetime import timedelta
 
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+        # y all-gathers on their own communicator so they overlap the small H exchanges and kernels
+        group_y = dist.new_group(list(range(world)))
     dtype = torch.float32 if cfg == "cfg1" else torch.bfloat16
     esize = 4 if dtype == torch.float32 else 2
 
@@ -248,7 +250,8 @@ def main() -> None:
         tens.append(t)
         if world > 1:
             layers.append(ShardedLayer(t, s.crow, in_features=s.in_features, out_features=s.out_features,
-                                       block_p=s.block_p, block_q=s.block_q, rank=rank, world=world))
+                                       block_p=s.block_p, block_q=s.block_q, rank=rank, world=world,
+                                       group=group_y, group_h=None))
         else:
             order = torch.from_numpy(ops.plan_row_order(s.crow.astype(np.int32))).to(dev)
             layers.append(ops.LayerDesc(A=t["A"], B=t["B"], bias=t["bias"], crow=t["S_crow"], col=t["S_col"],
@@ -266,30 +269,36 @@ def main() -> None:
 
     def step(ev=None):
         """One forward of the layer set; ev = per-projection event triples."""
-        for i, L in enumerate(layers):
-            if world > 1:
-                desc = L.desc
-                buf = L.local_buffer(T)
-                if desc is not None:
-                    out_i = buf[rank][:, :L.width]
+        if world > 1:
+            handles = []
+            for i, L in enumerate(layers):
+                if L.desc is not None:
                     if ev is not None:
                         ev[i][0].record(stream)
-                    desc.lowrank(xs[i])
+                    L._lowrank(xs[i])
                     if ev is not None:
                         ev[i][1].record(stream)
-                    desc.combine(xs[i], out_i)
+                    buf = L.local_buffer(T)
+                    L.desc.combine(xs[i], buf[rank][:, :L.width])
                     if ev is not None:
                         ev[i][2].record(stream)
-                L.gather(buf, ys[i])
-            else:
-                if ev is not None:
-                    ev[i][0].record(stream)
-                L.lowrank(xs[i])
-                if ev is not None:
-                    ev[i][1].record(stream)
-                L.combine(xs[i], ys[i])
-                if ev is not None:
-                    ev[i][2].record(stream)
+                    work = dist.all_gather_into_tensor(buf.view(-1), buf[rank].view(-1), group=L.group,
+                                                       async_op=True)
+                    handles.append((work, buf))
+                else:
+                    handles.append(L.start(xs[i]))
+            for i, L in enumerate(layers):
+                L.finish(handles[i], ys[i])
+            return
+        for i, L in enumerate(layers):
+            if ev is not None:
+                ev[i][0].record(stream)
+            L.lowrank(xs[i])
+            if ev is not None:
+                ev[i][1].record(stream)
+            L.combine(xs[i], ys[i])
+            if ev is not None:
+                ev[i][2].record(stream)
 
     for _ in range(args.warmup):
         step()
@@ -386,10 +395,7 @@ def main() -> None:
             xin_dev[r].copy_(x_host[r], non_blocking=True)
         for i, L in enumerate(layers):
             x_i = xin_dev[roles[i]]
-            if world > 1:
-                L.forward(x_i, ys[i])
-            else:
-                L.forward(x_i, ys[i])
+            L.forward(x_i, ys[i])
             if rank == 0:
                 y_host[i].copy_(ys[i], non_blocking=True)
 

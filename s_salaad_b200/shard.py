@@ -4,10 +4,12 @@ Rank p of P owns the contiguous block-rows [bounds[p], bounds[p+1]) chosen
 by ``slr_plan_shards`` so that every rank gets a nearly equal share of the
 per-token cost ``nnz_i*bp*bq + bp*r`` (the Zipf-skewed rows of a layer do not
 all land on one rank).  Each rank keeps the rebased crow/col/values slice,
-its rows of A and bias, and the whole of B (``x·Bᵀ`` is recomputed per rank,
-2*T*r*K flops, instead of exchanging it).  After the local fused forward
-into its slot of a ``[P, T, Nmax]`` buffer, one all-gather (NCCL on GPUs)
-gives every rank all slots and the columns are assembled into y.
+its rows of A and bias, and the whole of B.  ``x·Bᵀ`` is split by tokens
+(each rank computes T/P rows of H, an all-gather of H follows) when T/P is
+at least one 128-token tile, else recomputed by every rank.  After the local
+fused forward into its slot of a ``[P, T, Nmax]`` buffer, one all-gather
+(NCCL on GPUs) gives every rank all slots and the columns are assembled
+into y.
 
 The reference runs on one device only; this module has no reference
 counterpart and keeps the single-device arithmetic exactly (each output
@@ -73,13 +75,24 @@ class ShardPlan:
 
 
 class ShardedLayer(ShardPlan):
-    """One rank's part of a block-row-sharded S+LR layer on CUDA."""
+    """One rank's part of a block-row-sharded S+LR layer on CUDA.
+
+    ``x·Bᵀ`` is split by tokens when T is divisible by the world size: each
+    rank writes the H rows of its token slice straight into its row range of
+    the layer workspace and an in-place all-gather (on ``group_h``) completes
+    H on every rank; otherwise every rank computes all of H.  The y
+    all-gather runs asynchronously on ``group_y`` (a second communicator, so
+    it overlaps the next layer's H exchange and kernels): :meth:`start`
+    returns a handle, :meth:`finish` waits and assembles y.
+    """
 
     def __init__(self, t: dict, crow: np.ndarray, *, in_features: int, out_features: int, block_p: int,
-                 block_q: int, rank: int, world: int, group=None):
+                 block_q: int, rank: int, world: int, group=None, group_h=None):
         super().__init__(crow, out_features=out_features, block_p=block_p, block_q=block_q,
                          rank_r=int(t["A"].shape[1]), rank=rank, world=world, group=group)
+        self.group_h = group_h  # None: the default process group
         self.in_features = in_features
+        self.rank_r = int(t["A"].shape[1])
         self.dtype = t["A"].dtype
         self.device = t["A"].device
         self.desc = None
@@ -99,12 +112,58 @@ class ShardedLayer(ShardPlan):
             self._buf = self.gather_buffer(T, self.dtype, self.device)
         return self._buf
 
-    def local(self, x2: torch.Tensor) -> torch.Tensor:
-        """This rank's columns of y, written into its slot of the gather buffer."""
-        buf = self.local_buffer(x2.shape[0])
+    def _lowrank(self, x2: torch.Tensor) -> None:
+        """H = x2·Bᵀ into the layer workspace, token-split across ranks when possible."""
+        T = x2.shape[0]
+        d = self.desc
+        ws = d.workspace(T)
+        if self.rank_r == 0 or ws is None:
+            return
+        tp = T // self.world
+        # token split only on the tensor-core path (>= 128 rows per rank): the small-M
+        # path keeps split-K counters after its H rows, which the H all-gather would overwrite
+        if self.world > 1 and T % self.world == 0 and tp >= 128 and x2.stride(1) == 1:
+            ldh = (self.rank_r + 63) // 64 * 64
+            hbytes = T * ldh * x2.element_size()
+            off = self.rank * tp * ldh * x2.element_size()
+            if off % 256 == 0 and ws.numel() >= hbytes:
+                import ctypes
+
+                from . import _lib
+
+                xs = x2[self.rank * tp:(self.rank + 1) * tp]
+                rc = _lib.load().slr_lrs_linear_lowrank(
+                    ctypes.byref(d.struct), xs.data_ptr(), xs.stride(0), tp, ws.data_ptr() + off, ws.numel() - off,
+                    torch.cuda.current_stream(self.device).cuda_stream)
+                _lib.check(rc, "lrs_linear_lowrank (token shard)")
+                h = ws[:hbytes]
+                dist.all_gather_into_tensor(h, h[off:off + tp * ldh * x2.element_size()], group=self.group_h)
+                return
+        d.lowrank(x2)
+
+    def start(self, x2: torch.Tensor):
+        """Local shard of y plus an asynchronous all-gather; returns a handle for finish()."""
+        T = x2.shape[0]
+        buf = self.local_buffer(T)
         if self.desc is not None:
-            self.desc.forward(x2, out=buf[self.rank][:, :self.width])
-        return buf
+            self._lowrank(x2)
+            self.desc.combine(x2, buf[self.rank][:, :self.width])
+        work = None
+        if self.world > 1:
+            work = dist.all_gather_into_tensor(buf.view(-1), buf[self.rank].view(-1), group=self.group,
+                                               async_op=True)
+        return work, buf
+
+    def finish(self, handle, out: torch.Tensor | None = None) -> torch.Tensor:
+        work, buf = handle
+        if work is not None:
+            work.wait()
+        T = buf.shape[1]
+        if out is None:
+            out = torch.empty(T, self.out_features, dtype=buf.dtype, device=buf.device)
+        parts = [buf[p][:, :int(w)] for p, w in enumerate(self.widths) if w]
+        torch.cat(parts, dim=1, out=out)
+        return out
 
     def forward(self, x2: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
-        return self.gather(self.local(x2), out)
+        return self.finish(self.start(x2), out)

@@ -25,7 +25,7 @@ def main() -> int:
     dev = torch.device("cuda", local)
     dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
     bad = 0
-    cases = [("cfg4", 0, 1024), ("cfg4", 6, 300), ("cfg3", 4, 16), ("cfg5", 0, 1)]
+    cases = [("cfg4", 0, 1024), ("cfg4", 6, 300), ("cfg3", 4, 16), ("cfg3", 0, 2048), ("cfg5", 0, 1)]
     for cfg, idx, T in cases:
         s = workloads.layer_set(cfg)[idx]
         t = s.tensors(dev, torch.bfloat16)
