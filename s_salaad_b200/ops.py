@@ -159,8 +159,8 @@ class LayerDesc:
     def workspace_bytes(self, M: int) -> int:
         return int(_lib.load().slr_lrs_linear_workspace_size(ctypes.byref(self.struct), M))
 
-    def workspace(self, M: int) -> torch.Tensor | None:
-        need = self.workspace_bytes(M)
+    def workspace(self, M: int, at_least: int = 0) -> torch.Tensor | None:
+        need = max(self.workspace_bytes(M), at_least)
         if need == 0:
             return None
         if self._ws is None or self._ws.numel() < need or self._ws.device != self.device:

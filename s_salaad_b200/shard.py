@@ -126,7 +126,9 @@ class ShardedLayer(ShardPlan):
             ldh = (self.rank_r + 63) // 64 * 64
             hbytes = T * ldh * x2.element_size()
             off = self.rank * tp * ldh * x2.element_size()
-            if off % 256 == 0 and ws.numel() >= hbytes:
+            if off % 256 == 0:
+                # room for the slice call's own layout (H rows, then its scratch) at the offset
+                ws = d.workspace(T, at_least=off + d.workspace_bytes(tp))
                 import ctypes
 
                 from . import _lib
