@@ -39,6 +39,14 @@ import torch
 REPO = Path(__file__).resolve().parent
 sys.path.insert(0, str(REPO))
 
+_RESULT_FD = 1
+
+
+def emit(line: dict) -> None:
+    """Write the one JSON result line to the original stdout."""
+    os.write(_RESULT_FD, (json.dumps(line) + "\n").encode())
+
+
 METRIC = "S+LR linear tokens/s + %HBM/TC roofline at 1/2/4/8 B200 vs AVX2 CPU & cuBLAS"
 L2_FLUSH_BYTES = 256 << 20  # > 126 MB L2
 
@@ -179,6 +187,14 @@ def cpu_reference_run(specs, T_sample: int, steps: int, warmup: int, budget_s: f
 # ---------------------------------------------------------------- main --
 
 def main() -> None:
+    # Only the result line goes to stdout: libraries (NCCL, torch) may print
+    # there, so fd 1 points at stderr for the run and the line is written to
+    # the saved original stdout.
+    out_fd = os.dup(1)
+    os.dup2(2, 1)
+    sys.stdout = os.fdopen(os.dup(2), "w")
+    global _RESULT_FD
+    _RESULT_FD = out_fd
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=30)
@@ -224,7 +240,7 @@ def main() -> None:
                 "cpu_baseline": {"value": tok_s, "unit": "tokens/s", "cores": cores, "kind": kind,
                                  "sample": f"{T_sample} of {T} tokens per step through all {len(specs)} projections"},
                 "e2e": {"value": tok_s, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-        print(json.dumps(line), flush=True)
+        emit(line)
         return
 
     # ------------------------------------------------------------ our arm
@@ -377,7 +393,7 @@ def main() -> None:
     value = T * K / (total_ms / 1e3)
     if args.ncu:
         if rank == 0:
-            print(json.dumps({"ncu_mode": True, "ms_per_step": total_ms / K, "roofline": roof}), flush=True)
+            emit({"ncu_mode": True, "ms_per_step": total_ms / K, "roofline": roof})
         if world > 1:
             dist.destroy_process_group()
         return
@@ -468,7 +484,7 @@ def main() -> None:
                                           "d2h_bytes_per_step": d2h},
                 "gpu_launches": launches_per_step * K, "clocks": clocks.summary(),
                 "cpu_baseline": cpu, "cublas_dense": cublas}
-        print(json.dumps(line), flush=True)
+        emit(line)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

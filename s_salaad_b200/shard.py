@@ -4,9 +4,8 @@ Rank p of P owns the contiguous block-rows [bounds[p], bounds[p+1]) chosen
 by ``slr_plan_shards`` so that every rank gets a nearly equal share of the
 per-token cost ``nnz_i*bp*bq + bp*r`` (the Zipf-skewed rows of a layer do not
 all land on one rank).  Each rank keeps the rebased crow/col/values slice,
-its rows of A and bias, and the whole of B.  ``x·Bᵀ`` is split by tokens
-(each rank computes T/P rows of H, an all-gather of H follows) when T/P is
-at least one 128-token tile, else recomputed by every rank.  After the local
+its rows of A and bias, and the whole of B; ``x·Bᵀ`` is recomputed by every
+rank (optionally split by tokens with an all-gather of H).  After the local
 fused forward into its slot of a ``[P, T, Nmax]`` buffer, one all-gather
 (NCCL on GPUs) gives every rank all slots and the columns are assembled
 into y.
@@ -77,20 +76,23 @@ class ShardPlan:
 class ShardedLayer(ShardPlan):
     """One rank's part of a block-row-sharded S+LR layer on CUDA.
 
-    ``x·Bᵀ`` is split by tokens when T is divisible by the world size: each
-    rank writes the H rows of its token slice straight into its row range of
-    the layer workspace and an in-place all-gather (on ``group_h``) completes
-    H on every rank; otherwise every rank computes all of H.  The y
+    ``x·Bᵀ`` is recomputed by every rank by default.  With
+    ``split_lowrank=True`` (and T divisible by the world size) each rank
+    writes the H rows of its token slice straight into its row range of the
+    layer workspace and an in-place all-gather (on ``group_h``) completes H on
+    every rank; on B200 the collective's latency exceeds the GEMM time it
+    saves at these sizes, so it is off by default.  The y
     all-gather runs asynchronously on ``group_y`` (a second communicator, so
     it overlaps the next layer's H exchange and kernels): :meth:`start`
     returns a handle, :meth:`finish` waits and assembles y.
     """
 
     def __init__(self, t: dict, crow: np.ndarray, *, in_features: int, out_features: int, block_p: int,
-                 block_q: int, rank: int, world: int, group=None, group_h=None):
+                 block_q: int, rank: int, world: int, group=None, group_h=None, split_lowrank: bool = False):
         super().__init__(crow, out_features=out_features, block_p=block_p, block_q=block_q,
                          rank_r=int(t["A"].shape[1]), rank=rank, world=world, group=group)
         self.group_h = group_h  # None: the default process group
+        self.split_lowrank = split_lowrank
         self.in_features = in_features
         self.rank_r = int(t["A"].shape[1])
         self.dtype = t["A"].dtype
@@ -122,7 +124,7 @@ class ShardedLayer(ShardPlan):
         tp = T // self.world
         # token split only on the tensor-core path (>= 128 rows per rank): the small-M
         # path keeps split-K counters after its H rows, which the H all-gather would overwrite
-        if self.world > 1 and T % self.world == 0 and tp >= 128 and x2.stride(1) == 1:
+        if self.split_lowrank and self.world > 1 and T % self.world == 0 and tp >= 128 and x2.stride(1) == 1:
             ldh = (self.rank_r + 63) // 64 * 64
             hbytes = T * ldh * x2.element_size()
             off = self.rank * tp * ldh * x2.element_size()

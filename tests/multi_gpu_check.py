@@ -35,11 +35,14 @@ def main() -> int:
                              values=t["S_values"], row_order=order, in_features=s.in_features,
                              out_features=s.out_features, block_p=s.block_p, block_q=s.block_q)
         ref = full.forward(x)
-        sh = ShardedLayer(t, s.crow, in_features=s.in_features, out_features=s.out_features, block_p=s.block_p,
-                          block_q=s.block_q, rank=rank, world=world)
-        y = sh.forward(x)
-        torch.cuda.synchronize()
-        err = float((y.float() - ref.float()).abs().max())
+        errs = []
+        for split in (False, True):
+            sh = ShardedLayer(t, s.crow, in_features=s.in_features, out_features=s.out_features,
+                              block_p=s.block_p, block_q=s.block_q, rank=rank, world=world, split_lowrank=split)
+            y = sh.forward(x)
+            torch.cuda.synchronize()
+            errs.append(float((y.float() - ref.float()).abs().max()))
+        err = max(errs)
         scale = float(ref.float().pow(2).mean().sqrt())
         ok = err <= 1e-6 * max(scale, 1.0)
         bad += 0 if ok else 1
