@@ -57,6 +57,8 @@ int launch_mma_rowblock(const RowblockArgs& a, bool pdl, cudaStream_t s);
 constexpr int64_t kTcMinTokens = 128;  // below this the mma.sync path is used
 bool tc_rowblock_supported(const RowblockArgs& a);
 int launch_tc_rowblock(const RowblockArgs& a, bool pdl, cudaStream_t s);
+bool tc2_rowblock_supported(const RowblockArgs& a);  // 2-SM pairs, M >= 256, bp 32/64
+int launch_tc2_rowblock(const RowblockArgs& a, bool pdl, cudaStream_t s);
 bool tc_dense_supported(const void* x, int64_t ldx, const void* B, int64_t K, int64_t r, int dtype);
 int launch_tc_dense(const void* x, int64_t ldx, const void* B, void* H, int64_t M, int64_t K, int64_t r,
                     int64_t ldh, int dtype, cudaStream_t s);
@@ -74,6 +76,7 @@ int launch_validate_bsr(const int32_t* crow, int64_t NB, const int32_t* col, int
 // Device status words (bounded-wait timeouts) of each translation unit.
 int read_and_clear_status_mma(unsigned* out);
 int read_and_clear_status_tc(unsigned* out);
+int read_and_clear_status_tc2(unsigned* out);
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 inline int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }

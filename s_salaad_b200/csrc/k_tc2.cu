@@ -1,0 +1,474 @@
+// Large-token-batch path on CTA pairs: the fused S+LR kernel with 2-SM
+// tcgen05 MMAs (cta_group::2, M = 256 tokens per pair).
+//
+// Same work decomposition as tc_rowblock_kernel (k_tc.cu): one work item =
+// a token tile x a group of G = 256/bp consecutive block-rows of the row
+// list, the producer merges the group's column lists, each distinct column
+// is one stage, each run of consecutive present rows one MMA, then the
+// low-rank chunks as N = 256 MMAs, all into one fp32 TMEM accumulator.
+// What changes on a pair of SMs:
+//   * the token tile is 256: each CTA loads the x (and H) rows of its own 128
+//     tokens and keeps those 128 accumulator rows in its own TMEM;
+//   * the B operand is split by N halves between the two CTAs.  Value blocks
+//     are therefore stored as two half-width N-atoms (bp/2 columns each); for
+//     a run of `len` rows (2*len atoms) the leader loads the first len atoms
+//     and the peer the last len, both into the same packed positions, and the
+//     A rows of the low-rank step are split 128/128;
+//   * only the leader issues MMAs; TMA loads of both CTAs complete on the
+//     leader's barriers; MMA completions are multicast to both CTAs.
+// Per stage each SM moves at most 32 KB (x or H tile 16 KB + its half of the
+// B operand), and each MMA reads half as much B from each SM's shared memory.
+//
+// Reference counterparts: _bsr_body (ssalaad/tilelang_sparse/addmm_inplace.py:
+// 41-82) and the F.linear pair + bias of _LRSLinearLRBlockCUDA.forward
+// (ssalaad/efficient/ls_linear.py:124-137).
+#include <algorithm>
+
+#include "internal.hpp"
+#include "tcgen05.cuh"
+
+namespace slr {
+namespace {
+using namespace tc;
+
+__device__ unsigned g_status_tc2 = 0;
+
+constexpr int kThreads = 192;
+constexpr uint32_t kMetaLR = 1u << 30;
+constexpr uint32_t kMetaLast = 1u << 31;
+
+struct Tc2Args {
+  void* y;
+  const void* bias;
+  const int32_t* crow;
+  const int32_t* col;
+  const int32_t* rows;
+  int64_t M, ldy;
+  int nrows, n_groups, n_mtiles, n_lr;
+};
+
+__device__ __forceinline__ void timeout2(volatile int* abort_flag) {
+  atomicOr(&g_status_tc2, SLR_TIMEOUT_BIT);
+  *abort_flag = 1;
+}
+
+template <int BP, int BQ, typename TI, int MODE>
+__global__ void __launch_bounds__(kThreads, 1)
+    tc2_rowblock_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_v,
+                        const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ CUtensorMap tm_a,
+                        const Tc2Args a) {
+  constexpr int G = 256 / BP;            // block-rows per item
+  constexpr int KS = BQ < 64 ? BQ : 64;  // k per sparse stage
+  constexpr int SUB = BQ / KS;
+  constexpr int XW = KS * 2;             // x-tile row bytes
+  constexpr int HW = BP;                 // row bytes of a half-block atom (bp/2 columns)
+  constexpr uint32_t X_BYTES = 128 * XW;
+  constexpr uint32_t POS = KS * HW;      // one half-block atom column
+  constexpr uint32_t H_BYTES = 128 * 128;
+  constexpr uint32_t AR_ROW = BP * 128;  // one block-row's A rows, 64 k
+  constexpr uint32_t A_SLOT = 16384;
+  constexpr uint32_t B_SLOT = (G * POS > (G / 2) * AR_ROW) ? G * POS : (G / 2) * AR_ROW;
+  constexpr uint32_t STAGE = A_SLOT + B_SLOT;
+  constexpr int STAGES = (196 * 1024) / STAGE > 8 ? 8 : (196 * 1024) / STAGE;
+  constexpr uint32_t ACC = 256;
+  constexpr uint32_t IDESC_SP = idesc_f16<TI>(256, 0, true);  // N set per run
+  constexpr uint32_t IDESC_LR = idesc_f16<TI>(256, 256, false);
+  static_assert(BP == 32 || BP == 64, "2-SM path: block_p 32 or 64");
+  static_assert(STAGE % 1024 == 0 && POS % 256 == 0, "stage alignment");
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* meta = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint32_t* tmem_slot = meta + STAGES;
+  __shared__ volatile int s_abort;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 8);  // 4 epilogue warps in each CTA of the pair
+    }
+    fence_mbar_init();
+    s_abort = 0;
+  }
+  if (warp == 1) {
+    tmem_alloc2(tmem_slot, 2 * ACC);
+    tmem_relinquish2();
+  }
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  if (warp >= 2) {
+    const uint32_t lane_base = uint32_t(32 * (warp & 3)) << 16;
+    for (uint32_t c = 0; c < 2 * ACC; c += 16) tmem_st16_zero(tmem + lane_base + c);
+    tmem_st_wait();
+  }
+  tc_fence_before();
+  cluster_sync();  // both halves of every accumulator are zero before the first MMA
+  tc_fence_after();
+
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  const int n_items = a.n_groups * a.n_mtiles;
+
+  if (warp == 0) {
+    // ------------------------------------------------------- TMA producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tm_x);
+      if (a.crow) tma_prefetch_desc(&tm_v);
+      if (a.n_lr) {
+        tma_prefetch_desc(&tm_h);
+        tma_prefetch_desc(&tm_a);
+      }
+      bool waited = false;
+      uint32_t g = 0;
+      for (int item = pair; item < n_items && !s_abort; item += npairs) {
+        const int gi = item / a.n_mtiles, mt = item - gi * a.n_mtiles;
+        const int r0 = gi * G;
+        const int gcount = min(G, a.nrows - r0);
+        const int m0 = mt * 256 + int(rank) * 128;  // this CTA's tokens
+        int rw[G], ptr[G], end[G], cur[G];
+#pragma unroll
+        for (int j = 0; j < G; ++j) {
+          rw[j] = j < gcount ? (a.rows ? a.rows[r0 + j] : r0 + j) : 0;
+          ptr[j] = (a.crow && j < gcount) ? a.crow[rw[j]] : 0;
+          end[j] = (a.crow && j < gcount) ? a.crow[rw[j] + 1] : 0;
+          cur[j] = ptr[j] < end[j] ? __ldg(a.col + ptr[j]) : 0x7fffffff;
+        }
+        int c = 0x7fffffff;
+#pragma unroll
+        for (int j = 0; j < G; ++j) c = min(c, cur[j]);
+        bool published = false;
+        while (c != 0x7fffffff && !s_abort) {
+          uint32_t mask = 0;
+          int blk[G];
+#pragma unroll
+          for (int j = 0; j < G; ++j) {
+            blk[j] = ptr[j];
+            if (cur[j] == c) {
+              mask |= 1u << j;
+              ++ptr[j];
+              cur[j] = ptr[j] < end[j] ? __ldg(a.col + ptr[j]) : 0x7fffffff;
+            }
+          }
+          int cn = 0x7fffffff;
+#pragma unroll
+          for (int j = 0; j < G; ++j) cn = min(cn, cur[j]);
+          const uint32_t pc = __popc(mask);
+          for (int sub = 0; sub < SUB; ++sub, ++g) {
+            const uint32_t slot = g % STAGES, ph = (g / STAGES) & 1;
+            if (!mbar_wait(&empty[slot], ph ^ 1)) {
+              timeout2(&s_abort);
+              break;
+            }
+            const uint32_t fb = mapa(smem_u32(&full[slot]), 0);
+            if (leader) {
+              const bool last = cn == 0x7fffffff && a.n_lr == 0 && sub == SUB - 1;
+              meta[slot] = mask | (last ? kMetaLast : 0u);
+              mbar_arrive_expect_tx(&full[slot], 2 * (X_BYTES + pc * POS));
+            }
+            uint8_t* adst = smem + slot * STAGE;
+            tma2_load_2d(adst, &tm_x, c * BQ + sub * KS, m0, fb);
+            // runs of consecutive rows: this CTA's len atoms of each run, packed
+            uint32_t m = mask, p = 0;
+            while (m) {
+              const int j = __ffs(m) - 1;
+              const int len = __ffs(~(m >> j)) - 1;
+              m &= ~(((1u << len) - 1u) << j);
+              for (int i = 0; i < len; ++i) {
+                const int at = int(rank) * len + i;  // atom index within the run
+                const int row = j + (at >> 1), half = at & 1;
+                tma2_load_2d(adst + A_SLOT + (p + i) * POS, &tm_v, half * (BP / 2), blk[row] * BQ + sub * KS, fb);
+              }
+              p += len;
+            }
+            published = true;
+          }
+          c = cn;
+        }
+        for (int l = 0; l < a.n_lr && !s_abort; ++l, ++g) {
+          if (!waited) {
+            pdl_wait_primary();  // H comes from the preceding kernel
+            waited = true;
+          }
+          const uint32_t slot = g % STAGES, ph = (g / STAGES) & 1;
+          if (!mbar_wait(&empty[slot], ph ^ 1)) {
+            timeout2(&s_abort);
+            break;
+          }
+          const uint32_t fb = mapa(smem_u32(&full[slot]), 0);
+          if (leader) {
+            meta[slot] = kMetaLR | (l == a.n_lr - 1 ? kMetaLast : 0u);
+            mbar_arrive_expect_tx(&full[slot], 2 * H_BYTES + gcount * AR_ROW);
+          }
+          uint8_t* adst = smem + slot * STAGE;
+          tma2_load_2d(adst, &tm_h, l * 64, m0, fb);
+          for (int j = int(rank) * (G / 2); j < (int(rank) + 1) * (G / 2) && j < gcount; ++j)
+            tma2_load_2d(adst + A_SLOT + (j - int(rank) * (G / 2)) * AR_ROW, &tm_a, l * 64, rw[j] * BP, fb);
+          published = true;
+        }
+        if (!published && !s_abort) {
+          // No block and no rank: a stage without loads so the item still completes.
+          const uint32_t slot = g % STAGES, ph = (g / STAGES) & 1;
+          if (!mbar_wait(&empty[slot], ph ^ 1)) {
+            timeout2(&s_abort);
+            break;
+          }
+          if (leader) {
+            meta[slot] = kMetaLast;
+            mbar_arrive(&full[slot]);
+          }
+          ++g;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------ MMA issuer (leader)
+    if (lane == 0 && leader) {
+      uint32_t g = 0, it = 0;
+      for (int item = pair; item < n_items && !s_abort; item += npairs, ++it) {
+        const uint32_t buf = it & 1, tph = (it >> 1) & 1;
+        if (!mbar_wait(&tempty[buf], tph ^ 1)) {
+          timeout2(&s_abort);
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem + buf * ACC;
+        while (true) {
+          const uint32_t slot = g % STAGES, ph = (g / STAGES) & 1;
+          if (!mbar_wait(&full[slot], ph)) {
+            timeout2(&s_abort);
+            break;
+          }
+          tc_fence_after();
+          const uint32_t m = meta[slot];
+          const uint32_t abase = smem_u32(smem + slot * STAGE);
+          const uint32_t bbase = abase + A_SLOT;
+          if (m & kMetaLR) {
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+              umma2_f16(d, sdesc(abase + kk * 32, 16, 1024, 2), sdesc(bbase + kk * 32, 16, 1024, 2), IDESC_LR, 1u);
+          } else {
+            uint32_t mask = m & 0xffffu, p = 0;
+            while (mask) {
+              const int j = __ffs(mask) - 1;
+              const int len = __ffs(~(mask >> j)) - 1;
+              mask &= ~(((1u << len) - 1u) << j);
+              const uint32_t idesc = IDESC_SP | (uint32_t(len * BP) >> 3) << 17;
+#pragma unroll
+              for (int kk = 0; kk < KS / 16; ++kk) {
+                const uint64_t ad = sdesc(abase + kk * 32, 16, 8 * XW, layout_for(XW));
+                const uint64_t bd = sdesc(bbase + p * POS + kk * 16 * HW, POS, 8 * HW, layout_for(HW));
+                umma2_f16(d + j * BP, ad, bd, idesc, 1u);
+              }
+              p += len;
+            }
+          }
+          umma2_commit_both(&empty[slot]);
+          ++g;
+          if (m & kMetaLast) break;
+        }
+        umma2_commit_both(&tfull[buf]);
+      }
+    }
+  } else {
+    // ---------------------------------------------------------- epilogue
+    const int q = warp & 3;
+    const uint32_t lane_base = uint32_t(32 * q) << 16;
+    const int row = 32 * q + lane;
+    TI* __restrict__ y = static_cast<TI*>(a.y);
+    const TI* __restrict__ bias = static_cast<const TI*>(a.bias);
+    const uint32_t te0 = mapa(smem_u32(&tempty[0]), 0);
+    uint32_t it = 0;
+    for (int item = pair; item < n_items; item += npairs, ++it) {
+      const int gi = item / a.n_mtiles, mt = item - gi * a.n_mtiles;
+      const int r0 = gi * G;
+      const int gcount = min(G, a.nrows - r0);
+      const uint32_t buf = it & 1, tph = (it >> 1) & 1;
+      if (!mbar_wait(&tfull[buf], tph)) {
+        timeout2(&s_abort);
+        break;
+      }
+      tc_fence_after();
+      const int64_t tok = int64_t(mt) * 256 + int64_t(rank) * 128 + row;
+      const uint32_t acc = tmem + lane_base + buf * ACC;
+      for (int j = 0; j < G; ++j) {
+        if (j >= gcount) {
+#pragma unroll
+          for (int c0 = 0; c0 < BP; c0 += 16) tmem_st16_zero(acc + j * BP + c0);
+          continue;
+        }
+        const int br = a.rows ? a.rows[r0 + j] : r0 + j;
+        TI* yr = y + tok * a.ldy + int64_t(br) * BP;
+        const TI* bb = bias ? bias + int64_t(br) * BP : nullptr;
+#pragma unroll
+        for (int c0 = 0; c0 < BP; c0 += 16) {
+          uint32_t r[16];
+          tmem_ld16(acc + j * BP + c0, r);
+          tmem_ld_wait();
+          tmem_st16_zero(acc + j * BP + c0);
+          if (tok < a.M) {
+            float v[16];
+#pragma unroll
+            for (int e = 0; e < 16; ++e) v[e] = __uint_as_float(r[e]);
+            if (MODE == MODE_ADDMM || bb != nullptr) {
+              const TI* src = MODE == MODE_ADDMM ? yr + c0 : bb + c0;
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                const uint4 o = MODE == MODE_ADDMM ? *reinterpret_cast<const uint4*>(src + 8 * h)
+                                                   : __ldg(reinterpret_cast<const uint4*>(src + 8 * h));
+                const uint32_t ow[4] = {o.x, o.y, o.z, o.w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  const float2 f = unpack2(ow[e], (TI*)nullptr);
+                  v[8 * h + 2 * e] = MODE == MODE_ADDMM ? f.x + v[8 * h + 2 * e] : v[8 * h + 2 * e] + f.x;
+                  v[8 * h + 2 * e + 1] = MODE == MODE_ADDMM ? f.y + v[8 * h + 2 * e + 1] : v[8 * h + 2 * e + 1] + f.y;
+                }
+              }
+            }
+            uint4 o0, o1;
+            o0.x = pack2(v[0], v[1], (TI*)nullptr);
+            o0.y = pack2(v[2], v[3], (TI*)nullptr);
+            o0.z = pack2(v[4], v[5], (TI*)nullptr);
+            o0.w = pack2(v[6], v[7], (TI*)nullptr);
+            o1.x = pack2(v[8], v[9], (TI*)nullptr);
+            o1.y = pack2(v[10], v[11], (TI*)nullptr);
+            o1.z = pack2(v[12], v[13], (TI*)nullptr);
+            o1.w = pack2(v[14], v[15], (TI*)nullptr);
+            reinterpret_cast<uint4*>(yr + c0)[0] = o0;
+            reinterpret_cast<uint4*>(yr + c0)[1] = o1;
+          }
+        }
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(te0 + buf * 8);
+    }
+  }
+
+  tc_fence_before();
+  cluster_sync();  // no CTA leaves while its pair may still touch its barriers or smem
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc2(tmem, 2 * ACC);
+  }
+}
+
+int num_sms() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
+template <int BP, int BQ, typename TI, int MODE>
+int launch_inst(const CUtensorMap& tx, const CUtensorMap& tv, const CUtensorMap& th, const CUtensorMap& ta,
+                const Tc2Args& k, bool pdl, cudaStream_t s) {
+  constexpr int G = 256 / BP;
+  constexpr int KS = BQ < 64 ? BQ : 64;
+  constexpr uint32_t POS = KS * BP, AR_ROW = BP * 128;
+  constexpr uint32_t B_SLOT = (G * POS > (G / 2) * AR_ROW) ? G * POS : (G / 2) * AR_ROW;
+  constexpr uint32_t STAGE = 16384 + B_SLOT;
+  constexpr int STAGES = (196 * 1024) / STAGE > 8 ? 8 : (196 * 1024) / STAGE;
+  const size_t smem = 1024 + size_t(STAGES) * STAGE + (2 * STAGES + 4) * 8 + STAGES * 4 + 16;
+  auto kern = tc2_rowblock_kernel<BP, BQ, TI, MODE>;
+  SLR_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+  const int items = k.n_groups * k.n_mtiles;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(2 * std::min(items, num_sms() / 2)));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 2 : 1;
+  SLR_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kern, tx, tv, th, ta, k));
+  return SLR_OK;
+}
+
+template <int BP, typename TI, int MODE>
+int dispatch_bq(int bq, const CUtensorMap& tx, const CUtensorMap& tv, const CUtensorMap& th,
+                const CUtensorMap& ta, const Tc2Args& k, bool pdl, cudaStream_t s) {
+  switch (bq) {
+    case 16: return launch_inst<BP, 16, TI, MODE>(tx, tv, th, ta, k, pdl, s);
+    case 32: return launch_inst<BP, 32, TI, MODE>(tx, tv, th, ta, k, pdl, s);
+    case 64: return launch_inst<BP, 64, TI, MODE>(tx, tv, th, ta, k, pdl, s);
+    case 128: return launch_inst<BP, 128, TI, MODE>(tx, tv, th, ta, k, pdl, s);
+    default: return fail(SLR_ERR_UNSUPPORTED, "2-SM path: block_q must be 16, 32, 64 or 128");
+  }
+}
+
+template <typename TI, int MODE>
+int dispatch_bp(int bp, int bq, const CUtensorMap& tx, const CUtensorMap& tv, const CUtensorMap& th,
+                const CUtensorMap& ta, const Tc2Args& k, bool pdl, cudaStream_t s) {
+  if (bp == 32) return dispatch_bq<32, TI, MODE>(bq, tx, tv, th, ta, k, pdl, s);
+  if (bp == 64) return dispatch_bq<64, TI, MODE>(bq, tx, tv, th, ta, k, pdl, s);
+  return fail(SLR_ERR_UNSUPPORTED, "2-SM path: block_p must be 32 or 64");
+}
+
+}  // namespace
+
+bool tc2_rowblock_supported(const RowblockArgs& a) {
+  return (a.bp == 32 || a.bp == 64) && a.M >= 256 && tc_rowblock_supported(a);
+}
+
+int launch_tc2_rowblock(const RowblockArgs& a, bool pdl, cudaStream_t s) {
+  if (a.nrows <= 0 || a.M <= 0) return SLR_OK;
+  const bool sparse = a.crow != nullptr && a.nnz > 0;
+  const int bq = sparse ? a.bq : 64;
+  const int ks = bq < 64 ? bq : 64;
+  CUtensorMap tx{}, tv{}, th{}, ta{};
+  int rc = make_tmap_2d(&tx, a.x, a.dtype, uint64_t(a.K), uint64_t(a.M), uint64_t(a.ldx) * 2, uint32_t(ks), 128u);
+  if (rc) return rc;
+  if (sparse) {
+    rc = make_tmap_2d(&tv, a.values, a.dtype, uint64_t(a.bp), uint64_t(a.nnz) * a.bq, uint64_t(a.bp) * 2,
+                      uint32_t(a.bp / 2), uint32_t(ks));
+    if (rc) return rc;
+  }
+  const int G = 256 / a.bp;
+  Tc2Args k{a.y, a.mode == MODE_FUSED ? a.bias : nullptr, sparse ? a.crow : nullptr, a.col, a.rows, a.M, a.ldy,
+            int(a.nrows), int(ceil_div(a.nrows, G)), int(ceil_div(a.M, 256)), 0};
+  if (a.mode == MODE_FUSED && a.r > 0) {
+    k.n_lr = int(ceil_div(a.r, 64));
+    rc = make_tmap_2d(&th, a.H, a.dtype, uint64_t(a.ldh), uint64_t(a.M), uint64_t(a.ldh) * 2, 64u, 128u);
+    if (rc) return rc;
+    rc = make_tmap_2d(&ta, a.A, a.dtype, uint64_t(a.r), uint64_t(a.N), uint64_t(a.r) * 2, 64u, uint32_t(a.bp));
+    if (rc) return rc;
+  }
+  if (a.dtype == SLR_BF16)
+    return a.mode == MODE_ADDMM ? dispatch_bp<__nv_bfloat16, MODE_ADDMM>(a.bp, bq, tx, tv, th, ta, k, pdl, s)
+                                : dispatch_bp<__nv_bfloat16, MODE_FUSED>(a.bp, bq, tx, tv, th, ta, k, pdl, s);
+  return a.mode == MODE_ADDMM ? dispatch_bp<__half, MODE_ADDMM>(a.bp, bq, tx, tv, th, ta, k, pdl, s)
+                              : dispatch_bp<__half, MODE_FUSED>(a.bp, bq, tx, tv, th, ta, k, pdl, s);
+}
+
+int read_and_clear_status_tc2(unsigned* out) {
+  unsigned v = 0, zero = 0;
+  SLR_CHECK_CUDA(cudaMemcpyFromSymbol(&v, g_status_tc2, sizeof(v)));
+  if (v) SLR_CHECK_CUDA(cudaMemcpyToSymbol(g_status_tc2, &zero, sizeof(zero)));
+  *out = v;
+  return SLR_OK;
+}
+
+}  // namespace slr

@@ -177,6 +177,9 @@ int slr_device_status(int* status_out) {
   rc = read_and_clear_status_tc(&w);
   if (rc) return rc;
   v |= w;
+  rc = read_and_clear_status_tc2(&w);
+  if (rc) return rc;
+  v |= w;
   *status_out = (v & SLR_TIMEOUT_BIT) ? SLR_ERR_TIMEOUT : SLR_OK;
   return SLR_OK;
 }
@@ -216,6 +219,7 @@ int slr_bsr_addmm_inplace(void* out, const void* x, int64_t M, int64_t K, const 
   a.dtype = dtype;
   a.mode = MODE_ADDMM;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype != SLR_F32 && nnz > 0 && tc2_rowblock_supported(a)) return launch_tc2_rowblock(a, false, s);
   if (dtype != SLR_F32 && nnz > 0 && M >= kTcMinTokens && tc_rowblock_supported(a))
     return launch_tc_rowblock(a, false, s);
   if (dtype != SLR_F32 && nnz > 0 && mma_rowblock_supported(a.bp, a.bq, K, 0) && aligned16(values) &&
@@ -329,6 +333,7 @@ int run_lowrank(const slr_layer& L, const FwdCall& c, cudaStream_t s) {
 
 int run_combine(const slr_layer& L, const FwdCall& c, bool pdl, cudaStream_t s) {
   if (c.a.M == 0) return SLR_OK;
+  if (c.p.path == 1 && tc2_rowblock_supported(c.a)) return launch_tc2_rowblock(c.a, pdl && L.rank > 0, s);
   if (c.p.path == 1 && c.a.M >= kTcMinTokens && tc_rowblock_supported(c.a))
     return launch_tc_rowblock(c.a, pdl && L.rank > 0, s);
   if (c.p.path == 1) return launch_mma_rowblock(c.a, pdl && L.rank > 0, s);
