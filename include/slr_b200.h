@@ -55,6 +55,11 @@ typedef enum slr_status {
   SLR_ERR_TIMEOUT = 7            /* a bounded device-side wait gave up */
 } slr_status;
 
+/* slr_layer.flags: run the combine phase of large batches (M >= 256, block_p
+ * 32 or 64) on SM pairs with 2-SM MMAs (M = 256).  Faster only when most
+ * column runs of a row group are long (dense-ish row groups); off by default. */
+#define SLR_FLAG_PAIR_MMA 1
+
 typedef enum slr_dtype {
   SLR_F32 = 0,
   SLR_F16 = 1,
@@ -138,7 +143,7 @@ typedef struct slr_layer {
   const void* B;          /* device [r, K] */
   const void* bias;       /* device [N] or NULL */
   int32_t dtype;          /* slr_dtype of x, y, values, A, B, bias */
-  int32_t flags;          /* reserved, must be 0 */
+  int32_t flags;          /* 0, or SLR_FLAG_PAIR_MMA */
 } slr_layer;
 
 /*

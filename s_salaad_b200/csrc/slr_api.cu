@@ -73,6 +73,9 @@ using namespace slr;
 
 namespace {
 
+// slr_layer.flags value that selects the 2-SM pair kernel for the combine phase.
+constexpr int32_t kFlagPairMma = SLR_FLAG_PAIR_MMA;
+
 bool valid_dtype(int d) { return d == SLR_F32 || d == SLR_F16 || d == SLR_BF16; }
 
 // Workspace layout of slr_lrs_linear_forward for a given (layer, M).
@@ -127,7 +130,7 @@ int check_layer(const slr_layer* L) {
   if (!L) return fail(SLR_ERR_INVALID_ARGUMENT, "layer is NULL");
   if (!valid_dtype(L->dtype))
     return fail(SLR_ERR_UNSUPPORTED_DTYPE, "dtype must be SLR_F32, SLR_F16 or SLR_BF16");
-  if (L->flags != 0) return fail(SLR_ERR_INVALID_ARGUMENT, "flags must be 0");
+  if (L->flags != 0 && L->flags != kFlagPairMma) return fail(SLR_ERR_INVALID_ARGUMENT, "unknown flags");
   if (L->in_features <= 0 || L->out_features <= 0 || L->rank < 0)
     return fail(SLR_ERR_INVALID_ARGUMENT, "in_features/out_features must be > 0 and rank >= 0");
   if (L->rank > 0 && (!L->A || !L->B)) return fail(SLR_ERR_INVALID_ARGUMENT, "A and B are required when rank > 0");
@@ -219,7 +222,6 @@ int slr_bsr_addmm_inplace(void* out, const void* x, int64_t M, int64_t K, const 
   a.dtype = dtype;
   a.mode = MODE_ADDMM;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (dtype != SLR_F32 && nnz > 0 && tc2_rowblock_supported(a)) return launch_tc2_rowblock(a, false, s);
   if (dtype != SLR_F32 && nnz > 0 && M >= kTcMinTokens && tc_rowblock_supported(a))
     return launch_tc_rowblock(a, false, s);
   if (dtype != SLR_F32 && nnz > 0 && mma_rowblock_supported(a.bp, a.bq, K, 0) && aligned16(values) &&
@@ -333,7 +335,8 @@ int run_lowrank(const slr_layer& L, const FwdCall& c, cudaStream_t s) {
 
 int run_combine(const slr_layer& L, const FwdCall& c, bool pdl, cudaStream_t s) {
   if (c.a.M == 0) return SLR_OK;
-  if (c.p.path == 1 && tc2_rowblock_supported(c.a)) return launch_tc2_rowblock(c.a, pdl && L.rank > 0, s);
+  if (c.p.path == 1 && L.flags == kFlagPairMma && tc2_rowblock_supported(c.a))
+    return launch_tc2_rowblock(c.a, pdl && L.rank > 0, s);
   if (c.p.path == 1 && c.a.M >= kTcMinTokens && tc_rowblock_supported(c.a))
     return launch_tc_rowblock(c.a, pdl && L.rank > 0, s);
   if (c.p.path == 1) return launch_mma_rowblock(c.a, pdl && L.rank > 0, s);

@@ -489,3 +489,19 @@ def test_device_status_is_clean(cuda):
     st = ctypes.c_int(-1)
     _lib.check(_lib.load().slr_device_status(ctypes.byref(st)))
     assert st.value == _lib.SLR_OK
+
+
+@pytest.mark.parametrize("shape", [(512, 512, 64, 64, 512, 0.2, True), (384, 512, 32, 32, 256, 0.3, False),
+                                   (256, 512, 64, 128, 64, 0.5, True)], ids=lambda s: "x".join(map(str, s)))
+@pytest.mark.parametrize("T", [256, 700])
+def test_pair_mma_kernel_matches_oracle(cuda, oracle, shape, T):
+    """The opt-in 2-SM combine kernel (slr_layer.flags = SLR_FLAG_PAIR_MMA)."""
+    n, k, bp, bq, r, dens, bias = shape
+    spec = random_layer(n, k, bp, bq, r, dens, seed=n + r + T, bias=bias)
+    t = spec.tensors("cpu", torch.bfloat16)
+    x = workloads.tokens(T, k, seed=T, dtype=torch.bfloat16)
+    ref = oracle_layer(oracle, t, x, bias=bias)
+    d = desc_for(t, spec, cuda, torch.bfloat16, bias=bias)
+    d.struct.flags = 1
+    y = ops.lrs_linear_forward(d, x.to(cuda))
+    assert_16bit_close(y, ref)

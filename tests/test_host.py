@@ -79,7 +79,7 @@ def test_layer_descriptor_validation_needs_no_gpu():
         ctypes.byref(L), x, ldx, y, ldy, M, None, 0, None)
     assert fwd(1, 1, 4) == _lib.SLR_ERR_INVALID_ARGUMENT
     L.A, L.B = 0x1000, 0x2000
-    L.flags = 1
+    L.flags = 8
     assert fwd(1, 1, 4) == _lib.SLR_ERR_INVALID_ARGUMENT
     L.flags = 0
     L.dtype = 5
