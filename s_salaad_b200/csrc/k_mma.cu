@@ -5,13 +5,14 @@
 //   h_small_kernel      H[M, ldh] = x · Bᵀ (rounded to the I/O dtype): split-K
 //                       over the CTAs, partial sums reduced deterministically
 //                       by the last CTA of each 16-row tile (fixed order).
-//   mma_rowblock_kernel one CTA per (block-row, <=64 tokens): a producer warp
-//                       streams the block-row's BSR values (contiguous rows of
-//                       the [nnz*bq, bp] view) and, for the fused layer, its
-//                       rows of A through a 4-stage TMA/mbarrier ring; eight
-//                       consumer warps take ldmatrix fragments and run
-//                       m16n8k16 MMAs; the epilogue adds bias (fused) or the
-//                       previous `out` (in-place operator) and stores once.
+//   mma_rowblock_kernel one CTA per (16 output features of a block-row, <=64
+//                       tokens): a producer warp streams the 16-column slice of
+//                       the row's BSR values, the x tiles at those blocks'
+//                       columns, and (fused layer) the row's A rows and H tiles
+//                       through a 6-stage TMA/mbarrier ring; eight consumer
+//                       warps run m16n8k16 MMAs from shared memory only; the
+//                       epilogue adds bias (fused) or the previous `out`
+//                       (in-place operator) and stores once.
 //
 // Reference counterparts: the GPU kernel _bsr_body
 // (ssalaad/tilelang_sparse/addmm_inplace.py:41-82: acc = out; acc += x_tile ·
@@ -28,52 +29,72 @@ __device__ unsigned g_status_mma = 0;
 
 constexpr int kConsumerWarps = 8;
 constexpr int kThreads = (kConsumerWarps + 1) * 32;
-constexpr int kStages = 4;
-constexpr int kStageBytes = 16384;
+constexpr int kStages = 6;
+constexpr int kFT = 16;  // output features per CTA (one m16 tile)
+// Low-rank stage layout: A rows (16 x kc, at most 2 KB) at 0, H tile at 2 KB
+// (1024-aligned for its swizzle).
+constexpr uint32_t kHOff = 2048;
 
 struct MmaArgs {
-  const void* x;
   void* y;
-  const void* H;
   const void* bias;
   const int32_t* crow;
   const int32_t* col;
   const int32_t* rows;
-  int64_t M, K, N, ldh, ldx, ldy;
-  int r, bq, rb, kc;
+  int64_t M, N, ldy;
+  int bp, bq, r, kc;   // kc: rank chunk per low-rank stage
+  int sb;              // value blocks per sparse stage
+  int ft_per_row;      // bp / 16
+  int nrows;
 };
 
 __device__ __forceinline__ uint32_t ld_u32(const void* p) {
   return *static_cast<const uint32_t*>(p);
 }
-__device__ __forceinline__ uint32_t ldg_u32(const void* p) {
-  return __ldg(static_cast<const unsigned int*>(p));
+
+__device__ __forceinline__ void ldsm_x2(uint32_t addr, uint32_t& r0, uint32_t& r1) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(addr));
 }
 
-template <int BP, int NT, typename TI, int MODE>
+// One CTA = 16 output features (a column slice of one block-row) x 8*NT
+// tokens.  Warp 8 is the producer: per sparse stage it TMA-loads the 16-column
+// slice of `sb` consecutive value blocks of the row (one box) and, for each of
+// those blocks, the x tile [tokens x bq] at that block's column (it reads col[]
+// itself, stages ahead of the consumers); per low-rank stage the 16 rows of A
+// and the H tile [tokens x kc].  Warps 0-7 split each stage's k16 steps, take
+// ldmatrix fragments from shared memory only, and run m16n8k16 MMAs (features
+// on M, tokens on N); partial sums are reduced across warps in a fixed order.
+template <int NT, int KX, typename TI, int MODE>
 __global__ void __launch_bounds__(kThreads)
-    mma_rowblock_kernel(const __grid_constant__ CUtensorMap tm_vals,
-                        const __grid_constant__ CUtensorMap tm_A, const MmaArgs a) {
-  constexpr int MT = BP / 16;              // 16-feature m-tiles
-  constexpr int KG = kConsumerWarps / MT;  // k-groups splitting the k-steps
-  constexpr int TT = 8 * NT;               // tokens per CTA
-  constexpr int RWV = BP * 2;              // bytes per values row
-  static_assert(MT >= 1 && KG >= 1 && KG * MT == kConsumerWarps, "BP must be 16, 32 or 64");
-
+    mma_rowblock_kernel(const __grid_constant__ CUtensorMap tm_vals, const __grid_constant__ CUtensorMap tm_x,
+                        const __grid_constant__ CUtensorMap tm_A, const __grid_constant__ CUtensorMap tm_h,
+                        const MmaArgs a) {
+  constexpr int TT = 8 * NT;                 // tokens per CTA
+  constexpr int XB = TT * KX * 2;            // one x sub-tile (tokens x KX columns)
+  constexpr int RWX = KX * 2;                // x tile row bytes (its TMA swizzle width)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  float* red = reinterpret_cast<float*>(smem + kStages * kStageBytes);  // [KG][BP][TT]
-  uint64_t* full = reinterpret_cast<uint64_t*>(red + KG * BP * TT);
+  const int nsub = a.bq / KX;                            // x sub-tiles per block
+  const uint32_t v_bytes = uint32_t(a.sb * a.bq * kFT * 2);   // values box of a stage
+  const uint32_t v_slot = (v_bytes + 1023) & ~1023u;
+  const uint32_t x_region = uint32_t(a.sb * nsub * XB);
+  const uint32_t lr_bytes = uint32_t(kFT * a.kc * 2 + TT * a.kc * 2);
+  uint32_t stage_bytes = v_slot + x_region;
+  if (stage_bytes < kHOff + TT * a.kc * 2) stage_bytes = kHOff + TT * a.kc * 2;
+  stage_bytes = (stage_bytes + 1023) & ~1023u;
+  float* red = reinterpret_cast<float*>(smem + kStages * stage_bytes);  // [8][16][TT]
+  uint64_t* full = reinterpret_cast<uint64_t*>(red + kConsumerWarps * kFT * TT);
   uint64_t* empty = full + kStages;
   __shared__ int s_abort;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int br = a.rows ? a.rows[blockIdx.x] : int(blockIdx.x);
+  const int ri = blockIdx.x / a.ft_per_row;
+  const int f0 = (blockIdx.x - ri * a.ft_per_row) * kFT;  // feature offset inside the block
+  const int br = a.rows ? a.rows[ri] : ri;
   const int64_t t0 = int64_t(blockIdx.y) * TT;
   const int jb0 = a.crow ? a.crow[br] : 0;
-  const int jb1 = a.crow ? a.crow[br + 1] : 0;
-  const int rows_sp = (jb1 - jb0) * a.bq;
-  const int n_sp = (rows_sp + a.rb - 1) / a.rb;
+  const int nblk = a.crow ? a.crow[br + 1] - jb0 : 0;
+  const int n_sp = (nblk + a.sb - 1) / a.sb;
   const int n_lr = MODE == MODE_FUSED ? (a.r + a.kc - 1) / a.kc : 0;
   const int n_total = n_sp + n_lr;
 
@@ -90,8 +111,15 @@ __global__ void __launch_bounds__(kThreads)
   if (warp == kConsumerWarps) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      if (n_sp) tma_prefetch_desc(&tm_vals);
-      if (n_lr) tma_prefetch_desc(&tm_A);
+      if (n_sp) {
+        tma_prefetch_desc(&tm_vals);
+        tma_prefetch_desc(&tm_x);
+      }
+      if (n_lr) {
+        tma_prefetch_desc(&tm_A);
+        tma_prefetch_desc(&tm_h);
+      }
+      bool waited = false;
       for (int s = 0; s < n_total; ++s) {
         const int slot = s % kStages;
         if (!mbar_wait(&empty[slot], ((s / kStages) & 1) ^ 1)) {
@@ -99,29 +127,37 @@ __global__ void __launch_bounds__(kThreads)
           s_abort = 1;
           break;
         }
-        uint8_t* dst = smem + slot * kStageBytes;
+        uint8_t* dst = smem + slot * stage_bytes;
         if (s < n_sp) {
-          mbar_arrive_expect_tx(&full[slot], uint32_t(a.rb * RWV));
-          tma_load_2d(dst, &tm_vals, 0, jb0 * a.bq + s * a.rb, &full[slot]);
+          const int j0 = s * a.sb;
+          const int nb = min(a.sb, nblk - j0);
+          mbar_arrive_expect_tx(&full[slot], v_bytes + uint32_t(nb * nsub * XB));
+          tma_load_2d(dst, &tm_vals, f0, (jb0 + j0) * a.bq, &full[slot]);
+          for (int j = 0; j < nb; ++j) {
+            const int c = __ldg(a.col + jb0 + j0 + j);
+            for (int h = 0; h < nsub; ++h)
+              tma_load_2d(dst + v_slot + (j * nsub + h) * XB, &tm_x, c * a.bq + h * KX, int(t0), &full[slot]);
+          }
         } else {
-          mbar_arrive_expect_tx(&full[slot], uint32_t(BP * a.kc * 2));
-          tma_load_2d(dst, &tm_A, (s - n_sp) * a.kc, br * BP, &full[slot]);
+          if (!waited) {
+            pdl_wait_primary();  // H is written by the preceding kernel
+            waited = true;
+          }
+          const int l = s - n_sp;
+          mbar_arrive_expect_tx(&full[slot], lr_bytes);
+          tma_load_2d(dst, &tm_A, l * a.kc, br * a.bp + f0, &full[slot]);
+          tma_load_2d(dst + kHOff, &tm_h, l * a.kc, int(t0), &full[slot]);
         }
       }
     }
   } else {
     // ----------------------------------------------------------- consumers
-    const int mt = warp % MT, kg = warp / MT;
-    const int g = lane >> 2, tig = lane & 3;
     const int lj = lane >> 3, li = lane & 7;
-    const TI* __restrict__ x = static_cast<const TI*>(a.x);
-    const TI* H = static_cast<const TI*>(a.H);
     float acc[NT][4];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
       for (int e = 0; e < 4; ++e) acc[nt][e] = 0.f;
-    bool waited_primary = false;
 
     for (int s = 0; s < n_total; ++s) {
       const int slot = s % kStages;
@@ -130,51 +166,37 @@ __global__ void __launch_bounds__(kThreads)
         s_abort = 1;
         break;
       }
-      const uint32_t base = smem_u32(smem + slot * kStageBytes);
+      const uint32_t base = smem_u32(smem + slot * stage_bytes);
       if (s < n_sp) {
-        const int steps = min(a.rb, rows_sp - s * a.rb) >> 4;
-        for (int kk = kg; kk < steps; kk += KG) {
-          const int q = s * a.rb + 16 * kk;
-          const int jb = q / a.bq;
-          const int kin = q - jb * a.bq;
-          const int64_t xk = int64_t(__ldg(a.col + jb0 + jb)) * a.bq + kin;
+        const int nb = min(a.sb, nblk - s * a.sb);
+        const int steps = nb * (a.bq >> 4);
+        for (int kk = warp; kk < steps; kk += kConsumerWarps) {
+          const int row = 16 * kk;              // k row inside the stage's value rows
+          const int j = row / a.bq, kin = row - j * a.bq;
           uint32_t af[4];
-          ldsm_x4_trans(base + swz_offset(16 * kk + (lj >> 1) * 8 + li, 2 * mt + (lj & 1), RWV),
-                        af[0], af[1], af[2], af[3]);
+          // values slice [k rows x 16 features], 32-byte rows (SWIZZLE_32B)
+          ldsm_x4_trans(base + swz_offset(row + (lj >> 1) * 8 + li, lj & 1, 32), af[0], af[1], af[2], af[3]);
+          const uint32_t xt = base + v_slot + uint32_t((j * nsub + kin / KX) * XB);
+          const int kc16 = (kin % KX) >> 3;     // 16-byte chunk of the k16 step in the x row
 #pragma unroll
           for (int nt = 0; nt < NT; ++nt) {
-            const int64_t t = t0 + 8 * nt + g;
-            uint32_t b0 = 0, b1 = 0;
-            if (t < a.M) {
-              const TI* xr = x + t * a.ldx + xk + 2 * tig;
-              b0 = ldg_u32(xr);
-              b1 = ldg_u32(xr + 8);
-            }
+            uint32_t b0, b1;
+            ldsm_x2(xt + swz_offset(8 * nt + li, kc16 + (lj & 1), RWX), b0, b1);
             mma16816<TI>::run(acc[nt], af, b0, b1);
           }
         }
       } else {
-        if (!waited_primary) {
-          pdl_wait_primary();  // H is written by the preceding kernel
-          waited_primary = true;
-        }
-        const int l = s - n_sp;
         const int steps = a.kc >> 4;
-        for (int kk = kg; kk < steps; kk += KG) {
-          const int rho = l * a.kc + 16 * kk;
-          if (rho >= a.r) break;
+        const int l = s - n_sp;
+        const int kcb = a.kc * 2;               // A / H tile row bytes
+        for (int kk = warp; kk < steps; kk += kConsumerWarps) {
+          if (l * a.kc + 16 * kk >= a.r) break;
           uint32_t af[4];
-          ldsm_x4(base + swz_offset(16 * mt + (lj & 1) * 8 + li, 2 * kk + (lj >> 1), a.kc * 2),
-                  af[0], af[1], af[2], af[3]);
+          ldsm_x4(base + swz_offset((lj & 1) * 8 + li, 2 * kk + (lj >> 1), kcb), af[0], af[1], af[2], af[3]);
 #pragma unroll
           for (int nt = 0; nt < NT; ++nt) {
-            const int64_t t = t0 + 8 * nt + g;
-            uint32_t b0 = 0, b1 = 0;
-            if (t < a.M) {
-              const TI* hr = H + t * a.ldh + rho + 2 * tig;
-              b0 = ld_u32(hr);
-              b1 = ld_u32(hr + 8);
-            }
+            uint32_t b0, b1;
+            ldsm_x2(base + kHOff + swz_offset(8 * nt + li, 2 * kk + (lj & 1), kcb), b0, b1);
             mma16816<TI>::run(acc[nt], af, b0, b1);
           }
         }
@@ -182,14 +204,14 @@ __global__ void __launch_bounds__(kThreads)
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[slot]);
     }
-    // accumulators -> red[kg][feature][token]
+    const int g = lane >> 2, tig = lane & 3;
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const int m = 16 * mt + g + ((e & 2) ? 8 : 0);
+        const int m = g + ((e & 2) ? 8 : 0);
         const int t = 8 * nt + 2 * tig + (e & 1);
-        red[(kg * BP + m) * TT + t] = acc[nt][e];
+        red[(warp * kFT + m) * TT + t] = acc[nt][e];
       }
   }
   __syncthreads();
@@ -198,18 +220,19 @@ __global__ void __launch_bounds__(kThreads)
   // ------------------------------------------------------------- epilogue
   TI* __restrict__ y = static_cast<TI*>(a.y);
   const TI* __restrict__ bias = static_cast<const TI*>(a.bias);
-  for (int idx = threadIdx.x; idx < BP * TT; idx += kThreads) {
-    const int n = idx % BP, t = idx / BP;
+  const int64_t n0 = int64_t(br) * a.bp + f0;
+  for (int idx = threadIdx.x; idx < kFT * TT; idx += kThreads) {
+    const int n = idx % kFT, t = idx / kFT;
     const int64_t tok = t0 + t;
     if (tok >= a.M) continue;
     float v = 0.f;
 #pragma unroll
-    for (int k = 0; k < KG; ++k) v += red[(k * BP + n) * TT + t];
-    const int64_t gi = tok * a.ldy + int64_t(br) * BP + n;
+    for (int w = 0; w < kConsumerWarps; ++w) v += red[(w * kFT + n) * TT + t];
+    const int64_t gi = tok * a.ldy + n0 + n;
     if (MODE == MODE_ADDMM) {
       v = to_f(y[gi]) + v;
     } else if (bias != nullptr) {
-      v = v + to_f(bias[int64_t(br) * BP + n]);
+      v = v + to_f(bias[n0 + n]);
     }
     y[gi] = from_f<TI>(v);
   }
@@ -336,13 +359,32 @@ int pick_tt(int64_t M) {
   return 64;
 }
 
-template <int BP, int NT, typename TI, int MODE>
-int launch_rowblock_inst(const CUtensorMap& tv, const CUtensorMap& ta, const MmaArgs& k,
-                         dim3 grid, bool pdl, cudaStream_t s) {
-  constexpr int TT = 8 * NT;
-  constexpr int KG = kConsumerWarps / (BP / 16);
-  const size_t smem = 1024 + kStages * kStageBytes + sizeof(float) * KG * BP * TT + 2 * kStages * 8;
-  auto kern = mma_rowblock_kernel<BP, NT, TI, MODE>;
+struct MmaShape {
+  int sb, kc, kx;
+  size_t smem;
+};
+
+MmaShape mma_shape(int bq, int r, int tt) {
+  MmaShape m;
+  m.kx = bq < 64 ? bq : 64;
+  m.kc = r >= 64 ? 64 : (r >= 32 ? 32 : 16);
+  // value rows per sparse stage: 128 (fewer for wide token tiles), at least one block
+  const int rows = tt >= 64 ? 64 : (tt >= 32 ? 128 : 256);
+  m.sb = std::max(1, rows / bq);
+  const uint32_t v_bytes = uint32_t(m.sb * bq * kFT * 2);
+  const uint32_t v_slot = (v_bytes + 1023) & ~1023u;
+  const uint32_t x_region = uint32_t(m.sb * (bq / m.kx) * tt * m.kx * 2);
+  uint32_t stage = v_slot + x_region;
+  if (stage < kHOff + uint32_t(tt * m.kc * 2)) stage = kHOff + uint32_t(tt * m.kc * 2);
+  stage = (stage + 1023) & ~1023u;
+  m.smem = 1024 + size_t(kStages) * stage + sizeof(float) * kConsumerWarps * kFT * tt + 2 * kStages * 8;
+  return m;
+}
+
+template <int NT, int KX, typename TI, int MODE>
+int launch_inst(const CUtensorMap& tv, const CUtensorMap& tx, const CUtensorMap& ta, const CUtensorMap& th,
+                const MmaArgs& k, size_t smem, dim3 grid, bool pdl, cudaStream_t s) {
+  auto kern = mma_rowblock_kernel<NT, KX, TI, MODE>;
   SLR_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
@@ -354,30 +396,28 @@ int launch_rowblock_inst(const CUtensorMap& tv, const CUtensorMap& ta, const Mma
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  SLR_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kern, tv, ta, k));
+  SLR_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kern, tv, tx, ta, th, k));
   return SLR_OK;
 }
 
-template <int BP, typename TI, int MODE>
-int launch_rowblock_nt(const CUtensorMap& tv, const CUtensorMap& ta, const MmaArgs& k,
-                       int tt, unsigned nrows, bool pdl, cudaStream_t s) {
-  const dim3 grid(nrows, unsigned(ceil_div(k.M, tt)));
+template <int KX, typename TI, int MODE>
+int launch_nt(int tt, const CUtensorMap& tv, const CUtensorMap& tx, const CUtensorMap& ta,
+              const CUtensorMap& th, const MmaArgs& k, size_t smem, dim3 grid, bool pdl, cudaStream_t s) {
   switch (tt) {
-    case 8: return launch_rowblock_inst<BP, 1, TI, MODE>(tv, ta, k, grid, pdl, s);
-    case 16: return launch_rowblock_inst<BP, 2, TI, MODE>(tv, ta, k, grid, pdl, s);
-    case 32: return launch_rowblock_inst<BP, 4, TI, MODE>(tv, ta, k, grid, pdl, s);
-    default: return launch_rowblock_inst<BP, 8, TI, MODE>(tv, ta, k, grid, pdl, s);
+    case 8: return launch_inst<1, KX, TI, MODE>(tv, tx, ta, th, k, smem, grid, pdl, s);
+    case 16: return launch_inst<2, KX, TI, MODE>(tv, tx, ta, th, k, smem, grid, pdl, s);
+    case 32: return launch_inst<4, KX, TI, MODE>(tv, tx, ta, th, k, smem, grid, pdl, s);
+    default: return launch_inst<8, KX, TI, MODE>(tv, tx, ta, th, k, smem, grid, pdl, s);
   }
 }
 
 template <typename TI, int MODE>
-int launch_rowblock_bp(const CUtensorMap& tv, const CUtensorMap& ta, const MmaArgs& k, int bp,
-                       int tt, unsigned nrows, bool pdl, cudaStream_t s) {
-  switch (bp) {
-    case 16: return launch_rowblock_nt<16, TI, MODE>(tv, ta, k, tt, nrows, pdl, s);
-    case 32: return launch_rowblock_nt<32, TI, MODE>(tv, ta, k, tt, nrows, pdl, s);
-    case 64: return launch_rowblock_nt<64, TI, MODE>(tv, ta, k, tt, nrows, pdl, s);
-    default: return fail(SLR_ERR_UNSUPPORTED, "mma path: block_p must be 16, 32 or 64");
+int launch_kx(int kx, int tt, const CUtensorMap& tv, const CUtensorMap& tx, const CUtensorMap& ta,
+              const CUtensorMap& th, const MmaArgs& k, size_t smem, dim3 grid, bool pdl, cudaStream_t s) {
+  switch (kx) {
+    case 16: return launch_nt<16, TI, MODE>(tt, tv, tx, ta, th, k, smem, grid, pdl, s);
+    case 32: return launch_nt<32, TI, MODE>(tt, tv, tx, ta, th, k, smem, grid, pdl, s);
+    default: return launch_nt<64, TI, MODE>(tt, tv, tx, ta, th, k, smem, grid, pdl, s);
   }
 }
 
@@ -412,8 +452,8 @@ int launch_h_small(const void* x, int64_t ldx, const void* B, void* H, float* pa
 }
 
 bool mma_rowblock_supported(int bp, int bq, int64_t K, int64_t r) {
-  if (bp != 16 && bp != 32 && bp != 64) return false;
-  if (bq % 16 != 0 || bq <= 0) return false;
+  if (bp % 16 != 0 || bp <= 0) return false;
+  if (bq <= 0 || (bq != 16 && bq != 32 && bq % 64 != 0) || bq > 256) return false;
   if (K % 8 != 0) return false;
   if (r != 0 && (r % 8 != 0 || r < 16)) return false;
   return true;
@@ -421,38 +461,40 @@ bool mma_rowblock_supported(int bp, int bq, int64_t K, int64_t r) {
 
 int launch_mma_rowblock(const RowblockArgs& a, bool pdl, cudaStream_t s) {
   if (a.nrows <= 0 || a.M <= 0) return SLR_OK;
-  const int bp = a.bp;
-  MmaArgs k{a.x, a.y, a.H, a.bias, a.crow, a.col, a.rows, a.M, a.K, a.N, a.ldh, a.ldx, a.ldy,
-            int(a.r), a.bq, 0, 0};
-  k.rb = std::min(256, kStageBytes / (bp * 2));
-  k.kc = a.r >= 64 ? 64 : (a.r >= 32 ? 32 : 16);
-  CUtensorMap tv{}, ta{};
-  int rc;
-  if (a.crow != nullptr && a.nnz > 0) {
-    rc = make_tmap_2d(&tv, a.values, a.dtype, uint64_t(bp), uint64_t(a.nnz) * a.bq, uint64_t(bp) * 2,
-                      uint32_t(bp), uint32_t(k.rb));
-    if (rc) return rc;
-  } else {
-    k.crow = nullptr;
-  }
-  if (a.mode == MODE_FUSED && a.r > 0) {
-    rc = make_tmap_2d(&ta, a.A, a.dtype, uint64_t(a.r), uint64_t(a.N), uint64_t(a.r) * 2,
-                      uint32_t(k.kc), uint32_t(bp));
-    if (rc) return rc;
-  } else {
-    k.r = 0;
-  }
+  if (a.ldx % 8 != 0 || !aligned16(a.x)) return fail(SLR_ERR_UNSUPPORTED, "mma path: x must be 16-byte aligned");
   const int tt = pick_tt(a.M);
-  const unsigned nrows = unsigned(a.nrows);
-  if (a.dtype == SLR_BF16) {
+  const bool sparse = a.crow != nullptr && a.nnz > 0;
+  const int bq = sparse ? a.bq : 16;
+  const int r = a.mode == MODE_FUSED ? int(a.r) : 0;
+  const MmaShape sh = mma_shape(bq, r, tt);
+  MmaArgs k{a.y, a.bias, sparse ? a.crow : nullptr, a.col, a.rows, a.M, a.N, a.ldy,
+            a.bp, bq, r, sh.kc, sh.sb, a.bp / kFT, int(a.nrows)};
+  CUtensorMap tv{}, tx{}, ta{}, th{};
+  int rc;
+  if (sparse) {
+    rc = make_tmap_2d(&tv, a.values, a.dtype, uint64_t(a.bp), uint64_t(a.nnz) * a.bq, uint64_t(a.bp) * 2,
+                      uint32_t(kFT), uint32_t(sh.sb * a.bq));
+    if (rc) return rc;
+    rc = make_tmap_2d(&tx, a.x, a.dtype, uint64_t(a.K), uint64_t(a.M), uint64_t(a.ldx) * 2, uint32_t(sh.kx),
+                      uint32_t(tt));
+    if (rc) return rc;
+  }
+  if (r > 0) {
+    rc = make_tmap_2d(&ta, a.A, a.dtype, uint64_t(a.r), uint64_t(a.N), uint64_t(a.r) * 2, uint32_t(sh.kc),
+                      uint32_t(kFT));
+    if (rc) return rc;
+    rc = make_tmap_2d(&th, a.H, a.dtype, uint64_t(a.ldh), uint64_t(a.M), uint64_t(a.ldh) * 2, uint32_t(sh.kc),
+                      uint32_t(tt));
+    if (rc) return rc;
+  }
+  const dim3 grid(unsigned(a.nrows * (a.bp / kFT)), unsigned(ceil_div(a.M, tt)));
+  if (a.dtype == SLR_BF16)
     return a.mode == MODE_ADDMM
-               ? launch_rowblock_bp<__nv_bfloat16, MODE_ADDMM>(tv, ta, k, bp, tt, nrows, pdl, s)
-               : launch_rowblock_bp<__nv_bfloat16, MODE_FUSED>(tv, ta, k, bp, tt, nrows, pdl, s);
-  }
-  if (a.dtype == SLR_F16) {
-    return a.mode == MODE_ADDMM ? launch_rowblock_bp<__half, MODE_ADDMM>(tv, ta, k, bp, tt, nrows, pdl, s)
-                                : launch_rowblock_bp<__half, MODE_FUSED>(tv, ta, k, bp, tt, nrows, pdl, s);
-  }
+               ? launch_kx<__nv_bfloat16, MODE_ADDMM>(sh.kx, tt, tv, tx, ta, th, k, sh.smem, grid, pdl, s)
+               : launch_kx<__nv_bfloat16, MODE_FUSED>(sh.kx, tt, tv, tx, ta, th, k, sh.smem, grid, pdl, s);
+  if (a.dtype == SLR_F16)
+    return a.mode == MODE_ADDMM ? launch_kx<__half, MODE_ADDMM>(sh.kx, tt, tv, tx, ta, th, k, sh.smem, grid, pdl, s)
+                                : launch_kx<__half, MODE_FUSED>(sh.kx, tt, tv, tx, ta, th, k, sh.smem, grid, pdl, s);
   return fail(SLR_ERR_UNSUPPORTED_DTYPE, "mma path: 16-bit dtypes only");
 }
 
