@@ -59,6 +59,16 @@ typedef enum slr_status {
  * 32 or 64) on SM pairs with 2-SM MMAs (M = 256).  Faster only when most
  * column runs of a row group are long (dense-ish row groups); off by default. */
 #define SLR_FLAG_PAIR_MMA 1
+/* slr_layer.flags: launch every kernel of a call only after all earlier work
+ * on the stream has finished.  Without it, the small-batch kernels (M < 128)
+ * of slr_lrs_linear_forward / _lowrank / _combine / _forward_noalloc start
+ * while the kernel issued before them is still running (programmatic
+ * dependent launch) and load the layer's weights (values, col, crow,
+ * row_order, A, B, bias) meanwhile; x, y and the workspace are touched only
+ * after that kernel has completed.  Set it when the kernel issued just before
+ * the call may still be writing this layer's weights and signals early
+ * completion itself (griddepcontrol.launch_dependents). */
+#define SLR_FLAG_STRICT_ORDER 2
 
 typedef enum slr_dtype {
   SLR_F32 = 0,
@@ -143,7 +153,7 @@ typedef struct slr_layer {
   const void* B;          /* device [r, K] */
   const void* bias;       /* device [N] or NULL */
   int32_t dtype;          /* slr_dtype of x, y, values, A, B, bias */
-  int32_t flags;          /* 0, or SLR_FLAG_PAIR_MMA */
+  int32_t flags;          /* 0, or SLR_FLAG_PAIR_MMA | SLR_FLAG_STRICT_ORDER */
 } slr_layer;
 
 /*

@@ -14,6 +14,9 @@ LIB_PATH = Path(__file__).resolve().parent / "libslr_b200.so"
 
 # slr_status codes (include/slr_b200.h)
 SLR_OK = 0
+# slr_layer.flags bits (include/slr_b200.h)
+SLR_FLAG_PAIR_MMA = 1
+SLR_FLAG_STRICT_ORDER = 2
 SLR_ERR_INVALID_ARGUMENT = 1
 SLR_ERR_UNSUPPORTED_DTYPE = 2
 SLR_ERR_UNSUPPORTED = 3

@@ -129,6 +129,13 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
 __device__ __forceinline__ void tma_prefetch_desc(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
 }
+// Pull one box of a 2-D tensor into L2 (no shared memory, no completion).
+__device__ __forceinline__ void tma_prefetch_l2_2d(const void* tmap, int32_t c0, int32_t c1) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+                   reinterpret_cast<uint64_t>(tmap)),
+               "r"(c0), "r"(c1)
+               : "memory");
+}
 // 2-D tiled load of one box into shared memory; completes `bytes` on `bar`.
 // c0 is the innermost (contiguous) coordinate in elements.
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const void* tmap, int32_t c0,

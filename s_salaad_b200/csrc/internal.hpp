@@ -49,7 +49,7 @@ struct HSmallPlan {
 HSmallPlan plan_h_small(int64_t M, int64_t K, int64_t ldh);
 int launch_h_small(const void* x, int64_t ldx, const void* B, void* H, float* part, unsigned* counters,
                    int64_t M, int64_t K, int64_t r, int64_t ldh, const HSmallPlan& plan,
-                   int dtype, cudaStream_t s);
+                   int dtype, bool pdl, cudaStream_t s);
 bool mma_rowblock_supported(int bp, int bq, int64_t K, int64_t r);
 int launch_mma_rowblock(const RowblockArgs& a, bool pdl, cudaStream_t s);
 

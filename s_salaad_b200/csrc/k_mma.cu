@@ -59,11 +59,17 @@ __device__ __forceinline__ void ldsm_x2(uint32_t addr, uint32_t& r0, uint32_t& r
 // One CTA = 16 output features (a column slice of one block-row) x 8*NT
 // tokens.  Warp 8 is the producer: per sparse stage it TMA-loads the 16-column
 // slice of `sb` consecutive value blocks of the row (one box) and, for each of
-// those blocks, the x tile [tokens x bq] at that block's column (it reads col[]
-// itself, stages ahead of the consumers); per low-rank stage the 16 rows of A
-// and the H tile [tokens x kc].  Warps 0-7 split each stage's k16 steps, take
+// those blocks, the x tile [tokens x bq] at that block's column (lane j reads
+// col[] of block j and issues its x tiles); per low-rank stage the 16 rows of
+// A and the H tile [tokens x kc].  Warps 0-7 split each stage's k16 steps, take
 // ldmatrix fragments from shared memory only, and run m16n8k16 MMAs (features
 // on M, tokens on N); partial sums are reduced across warps in a fixed order.
+//
+// Launched as a programmatic dependent (PDL): before griddepcontrol.wait the
+// CTA touches weights only -- the value and A boxes of the first kStages
+// stages go to shared memory, those of later stages to L2, bias to shared
+// memory -- so a decode step streams its weights while the previous kernel
+// finishes.  x, H and y are read or written only after the wait.
 template <int NT, int KX, typename TI, int MODE>
 __global__ void __launch_bounds__(kThreads)
     mma_rowblock_kernel(const __grid_constant__ CUtensorMap tm_vals, const __grid_constant__ CUtensorMap tm_x,
@@ -86,7 +92,9 @@ __global__ void __launch_bounds__(kThreads)
   uint64_t* full = reinterpret_cast<uint64_t*>(red + kConsumerWarps * kFT * TT);
   uint64_t* empty = full + kStages;
   __shared__ int s_abort;
+  __shared__ float s_bias[kFT];
 
+  pdl_launch_dependents();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ri = blockIdx.x / a.ft_per_row;
   const int f0 = (blockIdx.x - ri * a.ft_per_row) * kFT;  // feature offset inside the block
@@ -97,6 +105,7 @@ __global__ void __launch_bounds__(kThreads)
   const int n_sp = (nblk + a.sb - 1) / a.sb;
   const int n_lr = MODE == MODE_FUSED ? (a.r + a.kc - 1) / a.kc : 0;
   const int n_total = n_sp + n_lr;
+  const int64_t n0 = int64_t(br) * a.bp + f0;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -105,6 +114,10 @@ __global__ void __launch_bounds__(kThreads)
     }
     fence_mbar_init();
     s_abort = 0;
+  }
+  if (threadIdx.x < kFT) {
+    const TI* bias = static_cast<const TI*>(a.bias);
+    s_bias[threadIdx.x] = (MODE == MODE_FUSED && bias != nullptr) ? to_f(bias[n0 + threadIdx.x]) : 0.f;
   }
   __syncthreads();
 
@@ -119,35 +132,85 @@ __global__ void __launch_bounds__(kThreads)
         tma_prefetch_desc(&tm_A);
         tma_prefetch_desc(&tm_h);
       }
-      bool waited = false;
-      for (int s = 0; s < n_total; ++s) {
-        const int slot = s % kStages;
-        if (!mbar_wait(&empty[slot], ((s / kStages) & 1) ^ 1)) {
-          atomicOr(&g_status_mma, SLR_TIMEOUT_BIT);
-          s_abort = 1;
-          break;
-        }
-        uint8_t* dst = smem + slot * stage_bytes;
+    }
+    const int npre = min(n_total, kStages);
+    // Weights of the first npre stages (fresh slots: no empty-barrier wait).
+    int colr[kStages];
+#pragma unroll
+    for (int s = 0; s < kStages; ++s) {
+      colr[s] = 0;
+      if (s < npre) {
+        uint8_t* dst = smem + s * stage_bytes;
         if (s < n_sp) {
           const int j0 = s * a.sb;
           const int nb = min(a.sb, nblk - j0);
+          if (lane < nb) colr[s] = __ldg(a.col + jb0 + j0 + lane);
+          if (lane == 0) {
+            mbar_arrive_expect_tx(&full[s], v_bytes + uint32_t(nb * nsub * XB));
+            tma_load_2d(dst, &tm_vals, f0, (jb0 + j0) * a.bq, &full[s]);
+          }
+        } else if (lane == 0) {
+          mbar_arrive_expect_tx(&full[s], lr_bytes);
+          tma_load_2d(dst, &tm_A, (s - n_sp) * a.kc, br * a.bp + f0, &full[s]);
+        }
+      }
+    }
+    // Weights of the later stages into L2.
+    for (int s = npre + lane; s < n_total; s += 32) {
+      if (s < n_sp)
+        tma_prefetch_l2_2d(&tm_vals, f0, (jb0 + s * a.sb) * a.bq);
+      else
+        tma_prefetch_l2_2d(&tm_A, (s - n_sp) * a.kc, br * a.bp + f0);
+    }
+    pdl_wait_primary();  // x and H come from preceding kernels
+    __syncwarp();
+    // Activations of the pre-filled stages.
+#pragma unroll
+    for (int s = 0; s < kStages; ++s) {
+      if (s < npre) {
+        uint8_t* dst = smem + s * stage_bytes;
+        if (s < n_sp) {
+          const int nb = min(a.sb, nblk - s * a.sb);
+          if (lane < nb)
+            for (int h = 0; h < nsub; ++h)
+              tma_load_2d(dst + v_slot + (lane * nsub + h) * XB, &tm_x, colr[s] * a.bq + h * KX, int(t0),
+                          &full[s]);
+        } else if (lane == 0) {
+          tma_load_2d(dst + kHOff, &tm_h, (s - n_sp) * a.kc, int(t0), &full[s]);
+        }
+      }
+    }
+    // Remaining stages through the ring.
+    for (int s = npre; s < n_total; ++s) {
+      const int slot = s % kStages;
+      int ok = 1;
+      if (lane == 0) ok = mbar_wait(&empty[slot], ((s / kStages) & 1) ^ 1) ? 1 : 0;
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) {
+        if (lane == 0) {
+          atomicOr(&g_status_mma, SLR_TIMEOUT_BIT);
+          s_abort = 1;
+        }
+        break;
+      }
+      uint8_t* dst = smem + slot * stage_bytes;
+      if (s < n_sp) {
+        const int j0 = s * a.sb;
+        const int nb = min(a.sb, nblk - j0);
+        const int c = lane < nb ? __ldg(a.col + jb0 + j0 + lane) : 0;
+        if (lane == 0) {
           mbar_arrive_expect_tx(&full[slot], v_bytes + uint32_t(nb * nsub * XB));
           tma_load_2d(dst, &tm_vals, f0, (jb0 + j0) * a.bq, &full[slot]);
-          for (int j = 0; j < nb; ++j) {
-            const int c = __ldg(a.col + jb0 + j0 + j);
-            for (int h = 0; h < nsub; ++h)
-              tma_load_2d(dst + v_slot + (j * nsub + h) * XB, &tm_x, c * a.bq + h * KX, int(t0), &full[slot]);
-          }
-        } else {
-          if (!waited) {
-            pdl_wait_primary();  // H is written by the preceding kernel
-            waited = true;
-          }
-          const int l = s - n_sp;
-          mbar_arrive_expect_tx(&full[slot], lr_bytes);
-          tma_load_2d(dst, &tm_A, l * a.kc, br * a.bp + f0, &full[slot]);
-          tma_load_2d(dst + kHOff, &tm_h, l * a.kc, int(t0), &full[slot]);
         }
+        __syncwarp();
+        if (lane < nb)
+          for (int h = 0; h < nsub; ++h)
+            tma_load_2d(dst + v_slot + (lane * nsub + h) * XB, &tm_x, c * a.bq + h * KX, int(t0), &full[slot]);
+      } else if (lane == 0) {
+        const int l = s - n_sp;
+        mbar_arrive_expect_tx(&full[slot], lr_bytes);
+        tma_load_2d(dst, &tm_A, l * a.kc, br * a.bp + f0, &full[slot]);
+        tma_load_2d(dst + kHOff, &tm_h, l * a.kc, int(t0), &full[slot]);
       }
     }
   } else {
@@ -218,9 +281,8 @@ __global__ void __launch_bounds__(kThreads)
   if (s_abort) return;
 
   // ------------------------------------------------------------- epilogue
+  pdl_wait_primary();  // y may be read (in-place operator) or written by preceding kernels
   TI* __restrict__ y = static_cast<TI*>(a.y);
-  const TI* __restrict__ bias = static_cast<const TI*>(a.bias);
-  const int64_t n0 = int64_t(br) * a.bp + f0;
   for (int idx = threadIdx.x; idx < kFT * TT; idx += kThreads) {
     const int n = idx % kFT, t = idx / kFT;
     const int64_t tok = t0 + t;
@@ -231,8 +293,8 @@ __global__ void __launch_bounds__(kThreads)
     const int64_t gi = tok * a.ldy + n0 + n;
     if (MODE == MODE_ADDMM) {
       v = to_f(y[gi]) + v;
-    } else if (bias != nullptr) {
-      v = v + to_f(bias[n0 + n]);
+    } else if (a.bias != nullptr) {
+      v = v + s_bias[n];
     }
     y[gi] = from_f<TI>(v);
   }
@@ -283,12 +345,8 @@ __global__ void __launch_bounds__(128) h_small_kernel(const HArgs a) {
 #pragma unroll
     for (int e = 0; e < 4; ++e) acc[nt][e] = 0.f;
 
-  for (int64_t k = kb + 32 * warp; k < ke; k += 128) {
-    const int64_t kk = k + 8 * tig;
-    const bool kin = kk < ke;
-    const uint4 z = make_uint4(0, 0, 0, 0);
-    const uint4 A0 = (v0 && kin) ? ldg_u128(B0 + kk) : z;
-    const uint4 A1 = (v1 && kin) ? ldg_u128(B1 + kk) : z;
+  const uint4 z = make_uint4(0, 0, 0, 0);
+  auto step = [&](int64_t kk, bool kin, const uint4& A0, const uint4& A1) {
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
       const int64_t t = t0 + 8 * nt + g;
@@ -298,6 +356,29 @@ __global__ void __launch_bounds__(128) h_small_kernel(const HArgs a) {
       mma16816<TI>::run(acc[nt], s0, X.x, X.y);
       mma16816<TI>::run(acc[nt], s1, X.z, X.w);
     }
+  };
+  // B (a weight) for the first kPre slices is loaded before griddepcontrol.wait,
+  // overlapping the preceding kernel; x only after it.
+  constexpr int kPre = 4;
+  uint4 pa0[kPre], pa1[kPre];
+#pragma unroll
+  for (int i = 0; i < kPre; ++i) {
+    const int64_t k = kb + 32 * warp + 128 * i;
+    const int64_t kk = k + 8 * tig;
+    const bool kin = k < ke && kk < ke;
+    pa0[i] = (v0 && kin) ? ldg_u128(B0 + kk) : z;
+    pa1[i] = (v1 && kin) ? ldg_u128(B1 + kk) : z;
+  }
+  pdl_wait_primary();
+#pragma unroll
+  for (int i = 0; i < kPre; ++i) {
+    const int64_t k = kb + 32 * warp + 128 * i;
+    if (k < ke) step(k + 8 * tig, k + 8 * tig < ke, pa0[i], pa1[i]);
+  }
+  for (int64_t k = kb + 32 * warp + 128 * kPre; k < ke; k += 128) {
+    const int64_t kk = k + 8 * tig;
+    const bool kin = kk < ke;
+    step(kk, kin, (v0 && kin) ? ldg_u128(B0 + kk) : z, (v1 && kin) ? ldg_u128(B1 + kk) : z);
   }
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt)
@@ -340,16 +421,29 @@ __global__ void __launch_bounds__(128) h_small_kernel(const HArgs a) {
   if (threadIdx.x == 0) a.counters[tile] = 0u;  // ready for the next call
 }
 
-template <typename TI>
-int launch_h_small_t(const HArgs& a, int tt, dim3 grid, cudaStream_t s) {
-  switch (tt) {
-    case 8: h_small_kernel<1, TI><<<grid, 128, 0, s>>>(a); break;
-    case 16: h_small_kernel<2, TI><<<grid, 128, 0, s>>>(a); break;
-    case 32: h_small_kernel<4, TI><<<grid, 128, 0, s>>>(a); break;
-    default: h_small_kernel<8, TI><<<grid, 128, 0, s>>>(a); break;
-  }
-  SLR_CHECK_LAUNCH("h_small_kernel");
+template <int NT, typename TI>
+int launch_h_small_inst(const HArgs& a, dim3 grid, bool pdl, cudaStream_t s) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(128);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  SLR_CHECK_CUDA(cudaLaunchKernelEx(&cfg, h_small_kernel<NT, TI>, a));
   return SLR_OK;
+}
+
+template <typename TI>
+int launch_h_small_t(const HArgs& a, int tt, dim3 grid, bool pdl, cudaStream_t s) {
+  switch (tt) {
+    case 8: return launch_h_small_inst<1, TI>(a, grid, pdl, s);
+    case 16: return launch_h_small_inst<2, TI>(a, grid, pdl, s);
+    case 32: return launch_h_small_inst<4, TI>(a, grid, pdl, s);
+    default: return launch_h_small_inst<8, TI>(a, grid, pdl, s);
+  }
 }
 
 int pick_tt(int64_t M) {
@@ -442,12 +536,12 @@ HSmallPlan plan_h_small(int64_t M, int64_t K, int64_t ldh) {
 
 int launch_h_small(const void* x, int64_t ldx, const void* B, void* H, float* part, unsigned* counters,
                    int64_t M, int64_t K, int64_t r, int64_t ldh, const HSmallPlan& plan,
-                   int dtype, cudaStream_t s) {
+                   int dtype, bool pdl, cudaStream_t s) {
   if (M <= 0 || ldh <= 0) return SLR_OK;
   HArgs a{x, B, H, part, counters, M, K, ldx, plan.kchunk, int(r), int(ldh), plan.ks, plan.rt};
   const dim3 grid(unsigned(plan.rt), unsigned(plan.ks), unsigned(plan.tc));
-  if (dtype == SLR_BF16) return launch_h_small_t<__nv_bfloat16>(a, plan.tt, grid, s);
-  if (dtype == SLR_F16) return launch_h_small_t<__half>(a, plan.tt, grid, s);
+  if (dtype == SLR_BF16) return launch_h_small_t<__nv_bfloat16>(a, plan.tt, grid, pdl, s);
+  if (dtype == SLR_F16) return launch_h_small_t<__half>(a, plan.tt, grid, pdl, s);
   return fail(SLR_ERR_UNSUPPORTED_DTYPE, "h_small: 16-bit dtypes only");
 }
 

@@ -73,8 +73,10 @@ using namespace slr;
 
 namespace {
 
-// slr_layer.flags value that selects the 2-SM pair kernel for the combine phase.
+// slr_layer.flags bit that selects the 2-SM pair kernel for the combine phase.
 constexpr int32_t kFlagPairMma = SLR_FLAG_PAIR_MMA;
+// slr_layer.flags bit that turns off programmatic dependent launch.
+constexpr int32_t kFlagStrict = SLR_FLAG_STRICT_ORDER;
 
 bool valid_dtype(int d) { return d == SLR_F32 || d == SLR_F16 || d == SLR_BF16; }
 
@@ -130,7 +132,7 @@ int check_layer(const slr_layer* L) {
   if (!L) return fail(SLR_ERR_INVALID_ARGUMENT, "layer is NULL");
   if (!valid_dtype(L->dtype))
     return fail(SLR_ERR_UNSUPPORTED_DTYPE, "dtype must be SLR_F32, SLR_F16 or SLR_BF16");
-  if (L->flags != 0 && L->flags != kFlagPairMma) return fail(SLR_ERR_INVALID_ARGUMENT, "unknown flags");
+  if ((L->flags & ~(kFlagPairMma | kFlagStrict)) != 0) return fail(SLR_ERR_INVALID_ARGUMENT, "unknown flags");
   if (L->in_features <= 0 || L->out_features <= 0 || L->rank < 0)
     return fail(SLR_ERR_INVALID_ARGUMENT, "in_features/out_features must be > 0 and rank >= 0");
   if (L->rank > 0 && (!L->A || !L->B)) return fail(SLR_ERR_INVALID_ARGUMENT, "A and B are required when rank > 0");
@@ -320,6 +322,18 @@ int prepare_forward(const slr_layer* layer, const void* x, int64_t ldx, void* y,
   return SLR_OK;
 }
 
+// True when the combine phase runs on the small-batch kernel (mma_rowblock).
+// That kernel and h_small read x and H only after griddepcontrol.wait, so
+// both may be launched as programmatic dependents of the preceding kernel.
+bool small_batch_path(const slr_layer& L, const FwdCall& c) {
+  if (c.p.path != 1) return false;
+  if ((L.flags & kFlagPairMma) && tc2_rowblock_supported(c.a)) return false;
+  if (c.a.M >= kTcMinTokens && tc_rowblock_supported(c.a)) return false;
+  return true;
+}
+
+bool early_start(const slr_layer& L) { return (L.flags & kFlagStrict) == 0; }
+
 int run_lowrank(const slr_layer& L, const FwdCall& c, cudaStream_t s) {
   if (L.rank == 0 || c.a.M == 0) return SLR_OK;
   if (c.p.path == 1 && c.a.M >= kTcMinTokens &&
@@ -328,18 +342,20 @@ int run_lowrank(const slr_layer& L, const FwdCall& c, cudaStream_t s) {
   if (c.p.path == 1)
     return launch_h_small(c.a.x, c.a.ldx, L.B, c.ws, reinterpret_cast<float*>(c.ws + c.p.part_off),
                           reinterpret_cast<unsigned*>(c.ws + c.p.cnt_off), c.a.M, L.in_features, L.rank, c.p.ldh,
-                          c.p.hs, L.dtype, s);
+                          c.p.hs, L.dtype, early_start(L) && small_batch_path(L, c), s);
   return launch_simt_h(c.a.x, c.a.ldx, L.B, c.ws, c.a.M, L.in_features, L.rank, c.p.ldh, L.dtype,
                        L.dtype == SLR_F32, s);
 }
 
+// pdl: the tensor-core combine may overlap the x*B^T kernel issued just
+// before it by this library (it reads H only after griddepcontrol.wait).
 int run_combine(const slr_layer& L, const FwdCall& c, bool pdl, cudaStream_t s) {
   if (c.a.M == 0) return SLR_OK;
-  if (c.p.path == 1 && L.flags == kFlagPairMma && tc2_rowblock_supported(c.a))
-    return launch_tc2_rowblock(c.a, pdl && L.rank > 0, s);
+  if (c.p.path == 1 && (L.flags & kFlagPairMma) && tc2_rowblock_supported(c.a))
+    return launch_tc2_rowblock(c.a, pdl && L.rank > 0 && early_start(L), s);
   if (c.p.path == 1 && c.a.M >= kTcMinTokens && tc_rowblock_supported(c.a))
-    return launch_tc_rowblock(c.a, pdl && L.rank > 0, s);
-  if (c.p.path == 1) return launch_mma_rowblock(c.a, pdl && L.rank > 0, s);
+    return launch_tc_rowblock(c.a, pdl && L.rank > 0 && early_start(L), s);
+  if (c.p.path == 1) return launch_mma_rowblock(c.a, early_start(L), s);
   return launch_simt_rowblock(c.a, L.dtype == SLR_F32, s);
 }
 

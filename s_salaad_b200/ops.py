@@ -121,8 +121,9 @@ class LayerDesc:
     """
 
     def __init__(self, *, A, B, bias=None, crow=None, col=None, values=None, row_order=None,
-                 in_features: int, out_features: int, block_p: int = 0, block_q: int = 0):
+                 in_features: int, out_features: int, block_p: int = 0, block_q: int = 0, flags: int = 0):
         self.tensors = dict(A=A, B=B, bias=bias, crow=crow, col=col, values=values, row_order=row_order)
+        self.flags = int(flags)  # slr_layer.flags: SLR_FLAG_PAIR_MMA | SLR_FLAG_STRICT_ORDER
         self.in_features = int(in_features)
         self.out_features = int(out_features)
         self.block_p = int(block_p)
@@ -151,7 +152,7 @@ class LayerDesc:
         s.B = t["B"].data_ptr() if t["B"].numel() else None
         s.bias = _ptr(t["bias"])
         s.dtype = slr_dtype(A.dtype)
-        s.flags = 0
+        s.flags = self.flags
         self.device = A.device
         self.dtype = A.dtype
         self.key = tuple(_ptr(v) for v in t.values())

@@ -18,7 +18,7 @@ import pytest
 import torch
 
 from conftest import load_golden
-from s_salaad_b200 import ops, workloads
+from s_salaad_b200 import _lib, ops, workloads
 from s_salaad_b200.efficient import LRSLinear, _LRSLinearLR, _LRSLinearLRBlockCUDA, dense_to_bsr
 
 pytestmark = pytest.mark.gpu
@@ -263,6 +263,62 @@ def test_forward_captures_in_cuda_graph(cuda):
     g.replay()
     torch.cuda.synchronize()
     assert torch.equal(out, y_eager)
+
+
+def _chain(cuda, T, flags, between=None, shared_ws=True):
+    specs = [random_layer(1024, 1024, 32, 32, 64, 0.3, seed=60 + i, value_std=0.05) for i in range(6)]
+    ds = [desc_for(s.tensors("cpu", torch.bfloat16), s, cuda, torch.bfloat16) for s in specs]
+    for d in ds:
+        d.flags = flags
+        d.refresh()
+    if shared_ws:
+        ws = torch.zeros(max(d.workspace_bytes(T) for d in ds), dtype=torch.uint8, device=cuda)
+        for d in ds:
+            d._ws = ws
+
+    def run(x):
+        h = x
+        for d in ds:
+            h = d.forward(h)  # y of one layer is x of the next
+            if between is not None:
+                h = between(h)
+        return h
+    return run
+
+
+@pytest.mark.parametrize("T", [1, 16, 64])
+@pytest.mark.parametrize("variant", ["shared_ws", "own_ws", "torch_op_between"])
+def test_chained_layers_early_start_equals_strict_order(cuda, T, variant):
+    """Back-to-back small-batch calls overlap through programmatic dependent
+    launch (weights loaded before griddepcontrol.wait); the results must be
+    bit-identical to fully serialised launches (SLR_FLAG_STRICT_ORDER)."""
+    between = (lambda h: h * 0.5) if variant == "torch_op_between" else None
+    x = workloads.tokens(T, 1024, seed=T, dtype=torch.bfloat16).to(cuda)
+    y_early = _chain(cuda, T, 0, between, variant != "own_ws")(x)
+    y_strict = _chain(cuda, T, _lib.SLR_FLAG_STRICT_ORDER, between, variant != "own_ws")(x)
+    torch.cuda.synchronize()
+    assert torch.isfinite(y_strict.float()).all() and y_strict.float().abs().max() > 0
+    assert torch.equal(y_early, y_strict)
+
+
+def test_chained_layers_in_cuda_graph(cuda):
+    T = 8
+    run = _chain(cuda, T, 0)
+    x = workloads.tokens(T, 1024, seed=3, dtype=torch.bfloat16).to(cuda)
+    x2 = workloads.tokens(T, 1024, seed=4, dtype=torch.bfloat16).to(cuda)
+    ref2 = _chain(cuda, T, _lib.SLR_FLAG_STRICT_ORDER)(x2)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        run(x)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            out = run(x)
+    torch.cuda.current_stream().wait_stream(s)
+    x.copy_(x2)
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(out, ref2)
 
 
 # -------------------------------------------------- full-size properties --
