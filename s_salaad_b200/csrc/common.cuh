@@ -111,10 +111,23 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// Non-blocking test of the phase (about a third of try_wait's latency when
+// the phase has already completed).
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
 // Bounded wait for the phase of `parity` to complete.  Returns false after
 // SLR_WAIT_LIMIT_NS; the caller then records SLR_TIMEOUT_BIT and unwinds.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-  if (mbar_try_wait(bar, parity)) return true;
+  if (mbar_test_wait(bar, parity)) return true;
   const unsigned long long t0 = globaltimer_ns();
   while (true) {
 #pragma unroll 1
@@ -122,6 +135,29 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
       if (mbar_try_wait(bar, parity)) return true;
     if (globaltimer_ns() - t0 > SLR_WAIT_LIMIT_NS) return false;
   }
+}
+
+// Warp-wide bounded wait (all 32 lanes call it): lane 0 polls, sleeping
+// `sleep_ns` between polls when nonzero, so a waiting warp does not flood the
+// shared-memory pipe with 32 polls per round; then every lane acquires the
+// completed phase once.  Returns false after SLR_WAIT_LIMIT_NS.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, uint32_t sleep_ns) {
+  int ok = 1;
+  if ((threadIdx.x & 31) == 0) {
+    ok = 0;
+    const unsigned long long t0 = globaltimer_ns();
+    while (true) {
+      if (mbar_try_wait(bar, parity)) {
+        ok = 1;
+        break;
+      }
+      if (globaltimer_ns() - t0 > SLR_WAIT_LIMIT_NS) break;
+      if (sleep_ns) __nanosleep(sleep_ns);
+    }
+  }
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  if (ok) (void)mbar_try_wait(bar, parity);
+  return ok != 0;
 }
 
 // ------------------------------------------------------------- PTX: TMA ----

@@ -14,9 +14,12 @@
 //                       128 x 64), the rank-r down-projection, rounded to the
 //                       I/O dtype like the reference's first F.linear.
 //
-// Warp roles (192 threads): warp 0 lane 0 issues TMA loads, warp 1 lane 0
-// issues MMAs (warp 1 also owns the TMEM allocation), warps 2-5 drain TMEM
-// (warp w reads TMEM lanes 32*(w%4) .. +31, i.e. tokens of that quarter).
+// Warp roles: warp 1 lane 0 issues MMAs (warp 1 also owns the TMEM
+// allocation), warps 2-5 drain TMEM (warp w reads TMEM lanes 32*(w%4) .. +31,
+// i.e. tokens of that quarter).  TMA loads: warp 0 lane 0 in the dense kernel;
+// in the fused kernel warps 0 and 6 both walk the item's stages (lane j of
+// each follows block-row j of the group) and split each stage's TMA loads
+// between them, because one thread issues a TMA load only every ~60 cycles.
 // The accumulator is double-buffered in TMEM so the epilogue of one item
 // overlaps the MMAs of the next.  Shared memory holds an 8-stage ring.
 //
@@ -35,7 +38,9 @@ using namespace tc;
 
 __device__ unsigned g_status_tc = 0;
 
-constexpr int kThreads = 192;
+constexpr int kThreads = 192;        // tc_dense_kernel
+constexpr int kRowThreads = 224;     // tc_rowblock_kernel: + a second TMA warp
+constexpr int kProd2 = 6;            // that warp
 constexpr int kTileM = 128;
 
 struct TcArgs {
@@ -54,41 +59,63 @@ __device__ __forceinline__ void tc_timeout(volatile int* abort_flag) {
   *abort_flag = 1;
 }
 
+// Operand staging of tc_rowblock_kernel.  Stages carry k-slices of up to 64
+// (sparse: x tile 128 x 64 plus the group's value blocks; low-rank: H tile
+// 128 x 64 plus A rows of the group; 48 KB).  Every stage costs the issuing
+// threads a fixed ~1000 cycles of barrier waits and TMA / MMA issue, so
+// fewer, fuller stages beat a deeper ring of small ones.
+constexpr int kSparseK = 64;  // k per sparse stage
+constexpr int kLrK = 64;      // rank columns per low-rank stage
+
+template <int BP, int BQ>
+struct RowCfg {
+  static constexpr int G = 256 / BP;                     // block-rows per item
+  static constexpr int KS = BQ < kSparseK ? BQ : kSparseK;
+  static constexpr int SUB = BQ / KS;                    // sparse stages per block column
+  static constexpr int XW = KS * 2, VW = BP * 2;         // x-tile / values row bytes
+  static constexpr uint32_t X_BYTES = kTileM * XW, V_BYTES = KS * VW;
+  static constexpr uint32_t H_BYTES = kTileM * kLrK * 2, AR_BYTES = BP * kLrK * 2;
+  static constexpr uint32_t BOFF = X_BYTES > H_BYTES ? X_BYTES : H_BYTES;
+  static constexpr uint32_t BREG = G * (V_BYTES > AR_BYTES ? V_BYTES : AR_BYTES);  // value blocks / A rows
+  static constexpr uint32_t STAGE = (BOFF + BREG + 1023u) & ~1023u;
+  static constexpr int STAGES = (200 * 1024) / STAGE > 8 ? 8 : (200 * 1024) / STAGE;
+  static constexpr size_t SMEM = 1024 + size_t(STAGES) * STAGE + (3 * STAGES + 4) * 8 + STAGES * 4 + 16;
+};
+
 constexpr uint32_t kMetaLR = 1u << 30;    // stage holds an H tile + rows of A
 constexpr uint32_t kMetaLast = 1u << 31;  // last stage of the work item
 
 // Persistent fused kernel.  One work item = 128 tokens x a group of
 // G = 256/BP block-rows, taken consecutively from the row list (heaviest
 // first for the fused layer), so the item's accumulator is 128 x 256 fp32 in
-// TMEM (double-buffered: all 512 columns).  The producer merges the G rows'
+// TMEM (double-buffered: all 512 columns).  The producers merge the G rows'
 // sorted column lists: each distinct column is one stage holding the x tile
-// once plus the value block of every row of the group that has that column,
+// once plus, in slot j, the value block of group row j if it has the column,
 // so an x tile feeds up to G block-rows, and each run of consecutive rows
-// present in a stage is one MMA with N = run length * BP.  The low-rank steps then add
-// H[128 x 64] · A_rows[256 x 64]ᵀ with one N = 256 MMA per k-slice.  Every
-// MMA accumulates: the epilogue re-zeroes each accumulator after draining it.
+// present in a stage is one MMA with N = run length * BP.  The low-rank
+// steps then add H[128 x 64] · A_rows[256 x 64]ᵀ with one N = 256 MMA per
+// k16.  Every MMA accumulates: the epilogue re-zeroes each accumulator after
+// draining it.
+//
+// Warps: 0 and 6 TMA producers, 1 MMA issuer, 2-5 epilogue.
 template <int BP, int BQ, typename TI, int MODE>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kRowThreads, 1)
     tc_rowblock_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_v,
                        const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ CUtensorMap tm_a,
                        const TcArgs a) {
-  constexpr int G = 256 / BP;            // block-rows per item
-  constexpr int KS = BQ < 64 ? BQ : 64;  // k per sparse stage (one swizzle row)
-  constexpr int SUB = BQ / KS;           // sparse stages per block column
-  constexpr int XW = KS * 2;             // x-tile row bytes
-  constexpr int VW = BP * 2;             // values row bytes
-  constexpr uint32_t X_BYTES = kTileM * XW, V_BYTES = KS * VW;
-  constexpr uint32_t H_BYTES = kTileM * 128, AR_BYTES = BP * 128;
-  constexpr uint32_t A_SLOT = 16384;
-  constexpr uint32_t B_SLOT = (G * V_BYTES > G * AR_BYTES) ? G * V_BYTES : G * AR_BYTES;
-  constexpr uint32_t STAGE = A_SLOT + B_SLOT;
-  constexpr int STAGES = 4;
+  using C = RowCfg<BP, BQ>;
+  constexpr int G = C::G, KS = C::KS, SUB = C::SUB, XW = C::XW, VW = C::VW;
+  constexpr uint32_t X_BYTES = C::X_BYTES, V_BYTES = C::V_BYTES, H_BYTES = C::H_BYTES, AR_BYTES = C::AR_BYTES;
+  constexpr uint32_t STAGE = C::STAGE;
+  constexpr int STAGES = C::STAGES;
+  constexpr uint32_t BOFF = C::BOFF;     // slot offset of the value blocks / A rows
+  constexpr int LRW = kLrK * 2;          // H / A row bytes
   constexpr uint32_t ACC = 256;          // accumulator columns
   constexpr uint32_t IDESC_SP = idesc_f16<TI>(kTileM, 0, true);  // N set per run of rows
   constexpr uint32_t IDESC_LR = idesc_f16<TI>(kTileM, 256, false);
-  static_assert(X_BYTES <= A_SLOT && H_BYTES <= A_SLOT, "A slot");
+  static_assert(X_BYTES % 1024 == 0 && H_BYTES % 1024 == 0 && AR_BYTES % 512 == 0, "tile alignment");
   static_assert(G * BP == 256 && G <= 16, "group must span 256 columns");
-  static_assert(STAGE % 1024 == 0 && V_BYTES % 256 == 0, "alignment of stages / value slots");
+  static_assert(STAGE % 1024 == 0 && V_BYTES % 256 == 0 && BOFF % 1024 == 0, "alignment of stages / value slots");
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -121,7 +148,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  if (warp >= 2) {  // both accumulators start at zero
+  if (warp >= 2 && warp < 6) {  // both accumulators start at zero
     const uint32_t lane_base = uint32_t(32 * (warp & 3)) << 16;
     for (uint32_t c = 0; c < 2 * ACC; c += 16) tmem_st16_zero(tmem + lane_base + c);
     tmem_st_wait();
@@ -131,8 +158,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const int n_items = a.n_groups * a.n_mtiles;
 
-  if (warp == 0) {
-    // ------------------------------------------------------- TMA producer
+  if (warp == 0 || warp == kProd2) {
+    // ------------------------------------------------------- TMA producers
+    // Both warps walk the same stage sequence.  Lane j (< G) follows block-row
+    // j of the item's group: its cursor into the row's columns; the next
+    // column is the warp minimum and the rows having it a ballot.  Warp 0
+    // publishes each stage (row mask, expected bytes); warp 6 loads the x
+    // tile; the value blocks (and A rows) alternate between the two warps.
+    const int pw = warp == 0 ? 0 : 1;
+    constexpr uint32_t kNone = 0x7fffffffu;
     if (lane == 0) {
       tma_prefetch_desc(&tm_x);
       if (a.crow) tma_prefetch_desc(&tm_v);
@@ -140,89 +174,109 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_prefetch_desc(&tm_h);
         tma_prefetch_desc(&tm_a);
       }
-      bool waited = false;
-      uint32_t g = 0;
-      for (int item = blockIdx.x; item < n_items && !s_abort; item += gridDim.x) {
-        const int gi = item / a.n_mtiles, mt = item - gi * a.n_mtiles;
-        const int r0 = gi * G;
-        const int gcount = min(G, a.nrows - r0);
-        const int m0 = mt * kTileM;
-        int rw[G], ptr[G], end[G], cur[G];
-#pragma unroll
-        for (int j = 0; j < G; ++j) {
-          rw[j] = j < gcount ? (a.rows ? a.rows[r0 + j] : r0 + j) : 0;
-          ptr[j] = (a.crow && j < gcount) ? a.crow[rw[j]] : 0;
-          end[j] = (a.crow && j < gcount) ? a.crow[rw[j] + 1] : 0;
-          cur[j] = ptr[j] < end[j] ? __ldg(a.col + ptr[j]) : 0x7fffffff;
+    }
+    bool waited = false;
+    uint32_t g = 0;
+    // warp-uniform view of the abort flag (the loops below use warp collectives)
+    auto stop = [&]() { return __any_sync(0xffffffffu, s_abort != 0); };
+    for (int item = blockIdx.x; item < n_items && !stop(); item += gridDim.x) {
+      const int gi = item / a.n_mtiles, mt = item - gi * a.n_mtiles;
+      const int r0 = gi * G;
+      const int gcount = min(G, a.nrows - r0);
+      const int m0 = mt * kTileM;
+      // cur = column of the row's next block, nxt = the one after (loaded a
+      // step ahead so no stage waits on a col[] load)
+      int rw = 0, ptr = 0, end = 0;
+      uint32_t cur = kNone, nxt = kNone;
+      if (lane < gcount) {
+        rw = a.rows ? a.rows[r0 + lane] : r0 + lane;
+        if (a.crow) {
+          ptr = a.crow[rw];
+          end = a.crow[rw + 1];
         }
-        int c = 0x7fffffff;
-#pragma unroll
-        for (int j = 0; j < G; ++j) c = min(c, cur[j]);
-        bool published = false;
-        // One stage per (column, sub-slice) of the union of the group's columns.
-        while (c != 0x7fffffff && !s_abort) {
-          uint32_t mask = 0;
-          int blk[G];
-#pragma unroll
-          for (int j = 0; j < G; ++j) {
-            blk[j] = ptr[j];
-            if (cur[j] == c) {
-              mask |= 1u << j;
-              ++ptr[j];
-              cur[j] = ptr[j] < end[j] ? __ldg(a.col + ptr[j]) : 0x7fffffff;
-            }
-          }
-          int cn = 0x7fffffff;
-#pragma unroll
-          for (int j = 0; j < G; ++j) cn = min(cn, cur[j]);
-          for (int sub = 0; sub < SUB; ++sub, ++g) {
-            const uint32_t slot = g % STAGES, ph = (g / STAGES) & 1;
-            if (!mbar_wait(&empty[slot], ph ^ 1)) {
-              tc_timeout(&s_abort);
-              break;
-            }
-            const bool last = cn == 0x7fffffff && a.n_lr == 0 && sub == SUB - 1;
-            meta[slot] = mask | (last ? kMetaLast : 0u);
-            uint8_t* adst = smem + slot * STAGE;
-            mbar_arrive_expect_tx(&full[slot], X_BYTES + __popc(mask) * V_BYTES);
-            tma_load_2d(adst, &tm_x, c * BQ + sub * KS, m0, &full[slot]);
-#pragma unroll
-            for (int j = 0; j < G; ++j)
-              if (mask & (1u << j))
-                tma_load_2d(adst + A_SLOT + j * V_BYTES, &tm_v, 0, blk[j] * BQ + sub * KS, &full[slot]);
-            published = true;
-          }
-          c = cn;
+        if (ptr < end) cur = uint32_t(__ldg(a.col + ptr));
+        if (ptr + 1 < end) nxt = uint32_t(__ldg(a.col + ptr + 1));
+      }
+      bool published = false;
+      bool abort_now = false;
+      uint32_t c = __reduce_min_sync(0xffffffffu, cur);
+      // One stage per (column, sub-slice) of the union of the group's columns.
+      while (c != kNone && !abort_now) {
+        const bool mine = cur == c;
+        const uint32_t mask = __ballot_sync(0xffffffffu, mine);
+        const int blk = ptr;
+        const uint32_t cidx = __popc(mask & ((1u << lane) - 1u));
+        if (mine) {
+          ++ptr;
+          cur = nxt;
+          nxt = ptr + 1 < end ? uint32_t(__ldg(a.col + ptr + 1)) : kNone;
         }
-        for (int l = 0; l < a.n_lr && !s_abort; ++l, ++g) {
-          if (!waited) {
-            pdl_wait_primary();  // H comes from the preceding kernel
-            waited = true;
-          }
+        const uint32_t cn = __reduce_min_sync(0xffffffffu, cur);
+        for (int sub = 0; sub < SUB; ++sub, ++g) {
           const uint32_t slot = g % STAGES, ph = (g / STAGES) & 1;
-          if (!mbar_wait(&empty[slot], ph ^ 1)) {
-            tc_timeout(&s_abort);
+          int ok = lane == 0 ? int(mbar_wait(&empty[slot], ph ^ 1)) : 1;
+          ok = __shfl_sync(0xffffffffu, ok, 0);
+          if (!ok) {
+            if (lane == 0) tc_timeout(&s_abort);
+            abort_now = true;
             break;
           }
-          meta[slot] = kMetaLR | (l == a.n_lr - 1 ? kMetaLast : 0u);
           uint8_t* adst = smem + slot * STAGE;
-          mbar_arrive_expect_tx(&full[slot], H_BYTES + gcount * AR_BYTES);
-          tma_load_2d(adst, &tm_h, l * 64, m0, &full[slot]);
-          for (int j = 0; j < gcount; ++j)
-            tma_load_2d(adst + A_SLOT + j * AR_BYTES, &tm_a, l * 64, rw[j] * BP, &full[slot]);
+          if (lane == 0) {
+            if (pw == 0) {
+              const bool last = cn == kNone && a.n_lr == 0 && sub == SUB - 1;
+              meta[slot] = mask | (last ? kMetaLast : 0u);
+              mbar_arrive_expect_tx(&full[slot], X_BYTES + __popc(mask) * V_BYTES);
+            } else {
+              tma_load_2d(adst, &tm_x, c * BQ + sub * KS, m0, &full[slot]);
+            }
+          }
+          if (mine && int(cidx & 1u) == pw)
+            tma_load_2d(adst + BOFF + lane * V_BYTES, &tm_v, 0, blk * BQ + sub * KS, &full[slot]);
           published = true;
         }
-        if (!published && !s_abort) {
-          // No block and no rank: a terminator stage so the item still completes.
-          const uint32_t slot = g % STAGES, ph = (g / STAGES) & 1;
-          if (!mbar_wait(&empty[slot], ph ^ 1)) {
-            tc_timeout(&s_abort);
-            break;
-          }
-          meta[slot] = kMetaLast;
-          mbar_arrive(&full[slot]);
-          ++g;
+        c = cn;
+      }
+      for (int l = 0; l < a.n_lr && !abort_now; ++l, ++g) {
+        if (!waited && pw == 0) {
+          pdl_wait_primary();  // H comes from the preceding kernel
+          waited = true;
         }
+        const uint32_t slot = g % STAGES, ph = (g / STAGES) & 1;
+        int ok = lane == 0 ? int(mbar_wait(&empty[slot], ph ^ 1)) : 1;
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) {
+          if (lane == 0) tc_timeout(&s_abort);
+          abort_now = true;
+          break;
+        }
+        uint8_t* adst = smem + slot * STAGE;
+        if (pw == 0 && lane == 0) {
+          meta[slot] = kMetaLR | uint32_t(gcount) | (l == a.n_lr - 1 ? kMetaLast : 0u);
+          mbar_arrive_expect_tx(&full[slot], H_BYTES + gcount * AR_BYTES);
+          tma_load_2d(adst, &tm_h, l * kLrK, m0, &full[slot]);
+        }
+        if (lane < gcount && (lane & 1) == pw)
+          tma_load_2d(adst + BOFF + lane * AR_BYTES, &tm_a, l * kLrK, rw * BP, &full[slot]);
+        published = true;
+      }
+      if (abort_now) break;
+      if (!published) {
+        // No block and no rank: a terminator stage so the item still completes.
+        const uint32_t slot = g % STAGES, ph = (g / STAGES) & 1;
+        int ok = 1;
+        if (pw == 0 && lane == 0) {
+          ok = int(mbar_wait(&empty[slot], ph ^ 1));
+          if (!ok) {
+            tc_timeout(&s_abort);
+          } else {
+            meta[slot] = kMetaLast;
+            mbar_arrive(&full[slot]);
+          }
+        }
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) break;
+        ++g;
       }
     }
   } else if (warp == 1) {
@@ -246,11 +300,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_after();
           const uint32_t m = meta[slot];
           const uint32_t abase = smem_u32(smem + slot * STAGE);
-          const uint32_t bbase = abase + A_SLOT;
+          const uint32_t bbase = abase + BOFF;
           if (m & kMetaLR) {
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk)
-              umma_f16(d, sdesc(abase + kk * 32, 16, 1024, 2), sdesc(bbase + kk * 32, 16, 1024, 2), IDESC_LR, 1u);
+            for (int kk = 0; kk < kLrK / 16; ++kk)
+              umma_f16(d, sdesc(abase + kk * 32, 16, 8 * LRW, layout_for(LRW)),
+                       sdesc(bbase + kk * 32, 16, 8 * LRW, layout_for(LRW)), IDESC_LR, 1u);
           } else {
             // One MMA per run of consecutive rows that have this column: their
             // value slots are adjacent N-atoms (LBO = slot stride), so the x
@@ -289,8 +344,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int r0 = gi * G;
       const int gcount = min(G, a.nrows - r0);
       const uint32_t buf = it & 1, tph = (it >> 1) & 1;
-      if (!mbar_wait(&tfull[buf], tph)) {
-        tc_timeout(&s_abort);
+      if (!mbar_wait_warp(&tfull[buf], tph, 256)) {
+        if (lane == 0) tc_timeout(&s_abort);
         break;
       }
       tc_fence_after();
@@ -471,8 +526,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++it) {
       const int mt = item % a.n_mtiles, nt = item / a.n_mtiles;
       const uint32_t buf = it & 1, tph = (it >> 1) & 1;
-      if (!mbar_wait(&tfull[buf], tph)) {
-        tc_timeout(&s_abort);
+      if (!mbar_wait_warp(&tfull[buf], tph, 256)) {
+        if (lane == 0) tc_timeout(&s_abort);
         break;
       }
       tc_fence_after();
@@ -517,17 +572,13 @@ int num_sms() {
 template <int BP, int BQ, typename TI, int MODE>
 int launch_rowblock_inst(const CUtensorMap& tx, const CUtensorMap& tv, const CUtensorMap& th,
                          const CUtensorMap& ta, const TcArgs& k, bool pdl, cudaStream_t s) {
-  constexpr int G = 256 / BP;
-  constexpr int KS = BQ < 64 ? BQ : 64;
-  constexpr uint32_t V = KS * BP * 2, AR = BP * 128;
-  constexpr uint32_t STAGE = 16384 + (G * V > G * AR ? G * V : G * AR);
-  const size_t smem = 1024 + size_t(4) * STAGE + (2 * 4 + 4) * 8 + 4 * 4 + 16;
+  const size_t smem = RowCfg<BP, BQ>::SMEM;
   auto kern = tc_rowblock_kernel<BP, BQ, TI, MODE>;
   SLR_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
   const int items = k.n_groups * k.n_mtiles;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(unsigned(std::min(items, num_sms())));
-  cfg.blockDim = dim3(kThreads);
+  cfg.blockDim = dim3(kRowThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
@@ -581,7 +632,7 @@ int launch_tc_rowblock(const RowblockArgs& a, bool pdl, cudaStream_t s) {
   if (a.nrows <= 0 || a.M <= 0) return SLR_OK;
   const bool sparse = a.crow != nullptr && a.nnz > 0;
   const int bq = sparse ? a.bq : 64;
-  const int ks = bq < 64 ? bq : 64;
+  const int ks = bq < kSparseK ? bq : kSparseK;
   CUtensorMap tx{}, tv{}, th{}, ta{};
   int rc = make_tmap_2d(&tx, a.x, a.dtype, uint64_t(a.K), uint64_t(a.M), uint64_t(a.ldx) * 2, uint32_t(ks),
                         uint32_t(kTileM));
@@ -595,11 +646,12 @@ int launch_tc_rowblock(const RowblockArgs& a, bool pdl, cudaStream_t s) {
   TcArgs k{a.y, a.mode == MODE_FUSED ? a.bias : nullptr, sparse ? a.crow : nullptr, a.col, a.rows, a.M, a.ldy,
            int(a.nrows), int(ceil_div(a.nrows, G)), int(ceil_div(a.M, kTileM)), 0};
   if (a.mode == MODE_FUSED && a.r > 0) {
-    k.n_lr = int(ceil_div(a.r, 64));
-    rc = make_tmap_2d(&th, a.H, a.dtype, uint64_t(a.ldh), uint64_t(a.M), uint64_t(a.ldh) * 2, 64u,
+    k.n_lr = int(ceil_div(a.r, kLrK));
+    rc = make_tmap_2d(&th, a.H, a.dtype, uint64_t(a.ldh), uint64_t(a.M), uint64_t(a.ldh) * 2, uint32_t(kLrK),
                       uint32_t(kTileM));
     if (rc) return rc;
-    rc = make_tmap_2d(&ta, a.A, a.dtype, uint64_t(a.r), uint64_t(a.N), uint64_t(a.r) * 2, 64u, uint32_t(a.bp));
+    rc = make_tmap_2d(&ta, a.A, a.dtype, uint64_t(a.r), uint64_t(a.N), uint64_t(a.r) * 2, uint32_t(kLrK),
+                      uint32_t(a.bp));
     if (rc) return rc;
   }
   if (a.dtype == SLR_BF16)

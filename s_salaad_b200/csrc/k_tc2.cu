@@ -295,8 +295,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int r0 = gi * G;
       const int gcount = min(G, a.nrows - r0);
       const uint32_t buf = it & 1, tph = (it >> 1) & 1;
-      if (!mbar_wait(&tfull[buf], tph)) {
-        timeout2(&s_abort);
+      if (!mbar_wait_warp(&tfull[buf], tph, 256)) {
+        if (lane == 0) timeout2(&s_abort);
         break;
       }
       tc_fence_after();
