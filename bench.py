@@ -279,6 +279,14 @@ def main() -> None:
         if roles[i] not in xin:
             xin[roles[i]] = workloads.tokens(T, s.in_features, seed=100 + roles[i], device=dev, dtype=dtype)
     xs = [xin[roles[i]] for i in range(len(specs))]
+    # projections that read one x (q/k/v, gate/up) run as one grouped call on
+    # one GPU: their x*B^T products are a single GEMM
+    members: dict[int, list[int]] = {}
+    for i, r in enumerate(roles):
+        members.setdefault(r, []).append(i)
+    groups = {}
+    if world == 1:
+        groups = {r: ops.LayerGroup([layers[i] for i in idx]) for r, idx in members.items() if len(idx) > 1}
     ys = [torch.empty(T, s.out_features, dtype=dtype, device=dev) for s in specs]
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
@@ -306,15 +314,31 @@ def main() -> None:
             for i, L in enumerate(layers):
                 L.finish(handles[i], ys[i])
             return
-        for i, L in enumerate(layers):
-            if ev is not None:
-                ev[i][0].record(stream)
-            L.lowrank(xs[i])
-            if ev is not None:
-                ev[i][1].record(stream)
-            L.combine(xs[i], ys[i])
-            if ev is not None:
-                ev[i][2].record(stream)
+        for r, idx in members.items():
+            grp = groups.get(r)
+            if grp is None:
+                for i in idx:
+                    L = layers[i]
+                    if ev is not None:
+                        ev[i][0].record(stream)
+                    L.lowrank(xs[i])
+                    if ev is not None:
+                        ev[i][1].record(stream)
+                    L.combine(xs[i], ys[i])
+                    if ev is not None:
+                        ev[i][2].record(stream)
+            elif ev is None:
+                grp.forward(xs[idx[0]], [ys[i] for i in idx])
+            else:
+                # the group's x*B^T is charged to its first projection
+                ev[idx[0]][0].record(stream)
+                grp.lowrank(xs[idx[0]])
+                for j, i in enumerate(idx):
+                    if j:
+                        ev[i][0].record(stream)
+                    ev[i][1].record(stream)
+                    grp.combine(j, xs[i], ys[i])
+                    ev[i][2].record(stream)
 
     for _ in range(args.warmup):
         step()
@@ -427,6 +451,9 @@ def main() -> None:
             dist.destroy_process_group()
         return
     launches_per_step = sum((1 if s.rank > 0 else 0) + 1 for i, s in enumerate(specs) if has_local[i])
+    for r, grp in groups.items():  # one x*B^T launch per group (tensor-core path)
+        if T >= 128:
+            launches_per_step -= len(members[r]) - 1
 
     # ------------------------------------------------------------- e2e
     x_host = {r: xin[r].cpu().pin_memory() for r in xin}
@@ -438,11 +465,16 @@ def main() -> None:
     def e2e_step():
         for r in xin:
             xin_dev[r].copy_(x_host[r], non_blocking=True)
-        for i, L in enumerate(layers):
-            x_i = xin_dev[roles[i]]
-            L.forward(x_i, ys[i])
+        for r, idx in members.items():
+            x_r = xin_dev[r]
+            if r in groups:
+                groups[r].forward(x_r, [ys[i] for i in idx])
+            else:
+                for i in idx:
+                    layers[i].forward(x_r, ys[i])
             if rank == 0:
-                y_host[i].copy_(ys[i], non_blocking=True)
+                for i in idx:
+                    y_host[i].copy_(ys[i], non_blocking=True)
 
     for _ in range(2):
         e2e_step()

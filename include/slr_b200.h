@@ -219,6 +219,30 @@ SLR_API int slr_lrs_linear_forward_noalloc(const slr_layer* layer, const void* x
                            int64_t ldx, void* y, int64_t ldy, int64_t M,
                            void* stream);
 
+/*
+ * n (1..4) layers that read the same x — the q/k/v or gate/up projections of
+ * a decoder layer, each an _LRSLinearLRBlockCUDA (ls_linear.py:124-137)
+ * called on one input by the reference: y[i] = x · S_iᵀ + (x · B_iᵀ) · A_iᵀ
+ * + bias_i, the results of slr_lrs_linear_forward on each layer, bit for
+ * bit.  With M >= 128 on the tensor-core path the x · B_iᵀ products are one
+ * GEMM over the stacked B_i (x is read once, the GEMM has n times the tiles).
+ * Layers must share in_features and dtype; ldy may be NULL (packed rows).
+ * The workspace rules are those of slr_lrs_linear_forward.
+ */
+SLR_API size_t slr_lrs_linear_group_workspace_size(const slr_layer* layers, int n, int64_t M);
+SLR_API int slr_lrs_linear_forward_group(const slr_layer* layers, int n, const void* x,
+                           int64_t ldx, void* const* y, const int64_t* ldy, int64_t M,
+                           void* workspace, size_t workspace_bytes, void* stream);
+/* The two phases of slr_lrs_linear_forward_group, like _lowrank / _combine
+ * for one layer: the group's x · B_iᵀ, then layer i's combine (any order of
+ * i, same x, M and workspace). */
+SLR_API int slr_lrs_linear_group_lowrank(const slr_layer* layers, int n, const void* x,
+                           int64_t ldx, int64_t M, void* workspace,
+                           size_t workspace_bytes, void* stream);
+SLR_API int slr_lrs_linear_group_combine(const slr_layer* layers, int n, int i,
+                           const void* x, int64_t ldx, void* y, int64_t ldy, int64_t M,
+                           void* workspace, size_t workspace_bytes, void* stream);
+
 /* --------------------------------------------------- dense -> BSR -- */
 
 /*

@@ -40,6 +40,10 @@ EXPORTED = (
     "slr_lrs_linear_lowrank",
     "slr_lrs_linear_combine",
     "slr_lrs_linear_forward_noalloc",
+    "slr_lrs_linear_group_workspace_size",
+    "slr_lrs_linear_forward_group",
+    "slr_lrs_linear_group_lowrank",
+    "slr_lrs_linear_group_combine",
     "slr_dense_to_bsr_mask",
     "slr_dense_to_bsr_fill",
     "slr_plan_row_order",
@@ -83,6 +87,11 @@ _SIGS = {
     "slr_lrs_linear_lowrank": ([ctypes.POINTER(SlrLayer), vp, i64, i64, vp, sz, vp], i32),
     "slr_lrs_linear_combine": ([ctypes.POINTER(SlrLayer), vp, i64, vp, i64, i64, vp, sz, vp], i32),
     "slr_lrs_linear_forward_noalloc": ([ctypes.POINTER(SlrLayer), vp, i64, vp, i64, i64, vp], i32),
+    "slr_lrs_linear_group_workspace_size": ([ctypes.POINTER(SlrLayer), i32, i64], sz),
+    "slr_lrs_linear_forward_group": ([ctypes.POINTER(SlrLayer), i32, vp, i64, ctypes.POINTER(vp),
+                                      ctypes.POINTER(i64), i64, vp, sz, vp], i32),
+    "slr_lrs_linear_group_lowrank": ([ctypes.POINTER(SlrLayer), i32, vp, i64, i64, vp, sz, vp], i32),
+    "slr_lrs_linear_group_combine": ([ctypes.POINTER(SlrLayer), i32, i32, vp, i64, vp, i64, i64, vp, sz, vp], i32),
     "slr_dense_to_bsr_mask": ([vp, i64, i64, i64, i64, i32, vp, vp, vp], i32),
     "slr_dense_to_bsr_fill": ([vp, i64, i64, i64, i64, i32, vp, vp, vp, vp, i32, vp], i32),
     "slr_plan_row_order": ([vp, i64, vp], i32),

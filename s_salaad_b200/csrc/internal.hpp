@@ -62,6 +62,10 @@ int launch_tc2_rowblock(const RowblockArgs& a, bool pdl, cudaStream_t s);
 bool tc_dense_supported(const void* x, int64_t ldx, const void* B, int64_t K, int64_t r, int dtype);
 int launch_tc_dense(const void* x, int64_t ldx, const void* B, void* H, int64_t M, int64_t K, int64_t r,
                     int64_t ldh, int dtype, cudaStream_t s);
+// x · [B_0; ...; B_{n-1}]ᵀ (n <= 4, same K) into H [M, ldh]: segment i takes
+// columns [sum_{j<i} round_up(r_j, 64), + round_up(r_i, 64)).
+int launch_tc_dense_group(const void* x, int64_t ldx, const void* const* Bs, const int64_t* rs, int n,
+                          void* H, int64_t M, int64_t K, int64_t ldh, int dtype, cudaStream_t s);
 
 // ---- dense -> BSR conversion.
 int launch_bsr_mask(const void* S, int64_t n, int64_t m, int64_t bp, int64_t bq, int dtype,

@@ -39,6 +39,7 @@ using namespace tc;
 __device__ unsigned g_status_tc = 0;
 
 constexpr int kThreads = 192;        // tc_dense_kernel
+constexpr int kMaxSeg = 4;           // weight matrices per grouped x*B^T
 constexpr int kRowThreads = 224;     // tc_rowblock_kernel: + a second TMA warp
 constexpr int kProd2 = 6;            // that warp
 constexpr int kTileM = 128;
@@ -416,15 +417,23 @@ __global__ void __launch_bounds__(kRowThreads, 1)
 
 // ---------------------------------------------------------- dense GEMM --
 
+// H[M, ldh] = x · [B_0; B_1; ...]ᵀ: up to kMaxSeg weight matrices that share
+// x (the q/k/v or gate/up projections of a decoder layer) are one GEMM; the
+// N tiles of segment s are [seg_nt[s], seg_nt[s+1]) and read B_s.
 struct DenseArgs {
   void* H;
   int64_t M, ldh;
   int n_mtiles, n_ntiles, n_k;
+  int n_seg;
+  int seg_nt[kMaxSeg + 1];
+};
+struct DenseMaps {
+  CUtensorMap b[kMaxSeg];
 };
 
 template <int BN, typename TI>
 __global__ void __launch_bounds__(kThreads, 1)
-    tc_dense_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_b,
+    tc_dense_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ DenseMaps maps,
                     const DenseArgs a) {
   constexpr uint32_t A_BYTES = kTileM * 128, B_BYTES = BN * 128;
   constexpr uint32_t STAGE = A_BYTES + B_BYTES;
@@ -468,10 +477,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     if (lane == 0) {
       tma_prefetch_desc(&tm_x);
-      tma_prefetch_desc(&tm_b);
+      for (int sg = 0; sg < a.n_seg; ++sg) tma_prefetch_desc(&maps.b[sg]);
       uint32_t g = 0;
       for (int item = blockIdx.x; item < n_items && !s_abort; item += gridDim.x) {
         const int mt = item % a.n_mtiles, nt = item / a.n_mtiles;
+        int sg = 0;
+        while (sg + 1 < a.n_seg && nt >= a.seg_nt[sg + 1]) ++sg;
+        const CUtensorMap* tm_b = &maps.b[sg];
+        const int nl = nt - a.seg_nt[sg];
         for (int s = 0; s < a.n_k; ++s, ++g) {
           const uint32_t slot = g % STAGES, ph = (g / STAGES) & 1;
           if (!mbar_wait(&empty[slot], ph ^ 1)) {
@@ -483,7 +496,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           tma_load_2d(adst, &tm_x, s * 64, mt * kTileM, &full[slot]);
 #pragma unroll
           for (int j = 0; j < BN / 64; ++j)
-            tma_load_2d(adst + A_BYTES + j * 8192, &tm_b, s * 64, nt * BN + j * 64, &full[slot]);
+            tma_load_2d(adst + A_BYTES + j * 8192, tm_b, s * 64, nl * BN + j * 64, &full[slot]);
         }
       }
     }
@@ -665,28 +678,42 @@ bool tc_dense_supported(const void* x, int64_t ldx, const void* B, int64_t K, in
   return dtype != SLR_F32 && r >= 64 && K >= 64 && K % 8 == 0 && ldx % 8 == 0 && aligned16(x) && aligned16(B);
 }
 
-int launch_tc_dense(const void* x, int64_t ldx, const void* B, void* H, int64_t M, int64_t K, int64_t r,
-                    int64_t ldh, int dtype, cudaStream_t s) {
-  if (M <= 0 || r <= 0) return SLR_OK;
-  CUtensorMap tx{}, tb{};
+int launch_tc_dense_group(const void* x, int64_t ldx, const void* const* Bs, const int64_t* rs, int n,
+                          void* H, int64_t M, int64_t K, int64_t ldh, int dtype, cudaStream_t s) {
+  if (M <= 0 || n <= 0) return SLR_OK;
+  if (n > kMaxSeg) return fail(SLR_ERR_UNSUPPORTED, "tc_dense: too many weight matrices in one group");
+  CUtensorMap tx{};
+  DenseMaps maps{};
   int rc = make_tmap_2d(&tx, x, dtype, uint64_t(K), uint64_t(M), uint64_t(ldx) * 2, 64u, uint32_t(kTileM));
   if (rc) return rc;
-  rc = make_tmap_2d(&tb, B, dtype, uint64_t(K), uint64_t(r), uint64_t(K) * 2, 64u, 64u);
-  if (rc) return rc;
+  // Each segment's columns [r_s rounded up to 64) of H; the tile width must divide every one.
+  int64_t cols[kMaxSeg];
+  int64_t total = 0;
+  bool all256 = true, all128 = true;
+  for (int i = 0; i < n; ++i) {
+    cols[i] = round_up(rs[i], 64);
+    total += cols[i];
+    all256 = all256 && cols[i] % 256 == 0;
+    all128 = all128 && cols[i] % 128 == 0;
+    rc = make_tmap_2d(&maps.b[i], Bs[i], dtype, uint64_t(K), uint64_t(rs[i]), uint64_t(K) * 2, 64u, 64u);
+    if (rc) return rc;
+  }
+  if (total > ldh) return fail(SLR_ERR_WORKSPACE, "tc_dense: H row narrower than the group's columns");
   const int n_mtiles = int(ceil_div(M, kTileM));
-  // Widest tile that divides ldh and still gives the SMs work: wide tiles
-  // move fewer operand bytes per MAC (the bound of this kernel).
+  // Widest tile that divides every segment and still gives the SMs work:
+  // wide tiles move fewer operand bytes per MAC (the bound of this kernel).
   int bn = 64;
-  if (ldh % 256 == 0 && int64_t(n_mtiles) * (ldh / 256) * 2 >= num_sms()) bn = 256;
-  else if (ldh % 128 == 0) bn = 128;
-  DenseArgs k{H, M, ldh, n_mtiles, int(ldh / bn), int(ceil_div(K, 64))};
+  if (all256 && int64_t(n_mtiles) * (total / 256) * 2 >= num_sms()) bn = 256;
+  else if (all128) bn = 128;
+  DenseArgs k{H, M, ldh, n_mtiles, int(total / bn), int(ceil_div(K, 64)), n, {0}};
+  for (int i = 0; i < n; ++i) k.seg_nt[i + 1] = k.seg_nt[i] + int(cols[i] / bn);
   const int items = k.n_mtiles * k.n_ntiles;
   auto launch = [&](auto kern, int BN) -> int {
     const uint32_t stage = kTileM * 128 + BN * 128;
     const int stages = std::min(8, int((196 * 1024) / stage));
     const size_t smem = 1024 + size_t(stages) * stage + (2 * stages + 4) * 8 + 16;
     SLR_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
-    kern<<<unsigned(std::min(items, num_sms())), kThreads, smem, s>>>(tx, tb, k);
+    kern<<<unsigned(std::min(items, num_sms())), kThreads, smem, s>>>(tx, maps, k);
     SLR_CHECK_LAUNCH("tc_dense_kernel");
     return SLR_OK;
   };
@@ -698,6 +725,12 @@ int launch_tc_dense(const void* x, int64_t ldx, const void* B, void* H, int64_t 
   if (bn == 256) return launch(tc_dense_kernel<256, __half>, 256);
   if (bn == 128) return launch(tc_dense_kernel<128, __half>, 128);
   return launch(tc_dense_kernel<64, __half>, 64);
+}
+
+int launch_tc_dense(const void* x, int64_t ldx, const void* B, void* H, int64_t M, int64_t K, int64_t r,
+                    int64_t ldh, int dtype, cudaStream_t s) {
+  if (M <= 0 || r <= 0) return SLR_OK;
+  return launch_tc_dense_group(x, ldx, &B, &r, 1, H, M, K, ldh, dtype, s);
 }
 
 int read_and_clear_status_tc(unsigned* out) {

@@ -390,6 +390,185 @@ int slr_lrs_linear_combine(const slr_layer* layer, const void* x, int64_t ldx, v
   return run_combine(*layer, c, false, static_cast<cudaStream_t>(stream));
 }
 
+}  // extern "C"
+
+namespace {
+
+constexpr int kMaxGroup = 4;  // layers per grouped call (weight segments of one x*B^T GEMM)
+
+// Workspace of slr_lrs_linear_forward_group: the group's H [M, ldh_all]
+// (layer i owns columns [col[i], col[i] + round_up(r_i, 64))), then each
+// layer's own workspace, used when the call falls back to one forward per
+// layer.
+struct GroupPlan {
+  int64_t ldh_all = 0;
+  int64_t col[kMaxGroup] = {};
+  size_t off[kMaxGroup] = {}, bytes[kMaxGroup] = {};
+  size_t total = 0;
+};
+
+int plan_group(const slr_layer* layers, int n, int64_t M, GroupPlan& g) {
+  if (!layers || n <= 0 || n > kMaxGroup)
+    return fail(SLR_ERR_INVALID_ARGUMENT, "a group holds 1 to " + std::to_string(kMaxGroup) + " layers");
+  for (int i = 0; i < n; ++i) {
+    int rc = check_layer(&layers[i]);
+    if (rc) return rc;
+    if (layers[i].in_features != layers[0].in_features || layers[i].dtype != layers[0].dtype)
+      return fail(SLR_ERR_INVALID_ARGUMENT, "grouped layers must share in_features and dtype (they read one x)");
+  }
+  size_t off = 0;
+  if (M > 0) {
+    for (int i = 0; i < n; ++i) {
+      g.col[i] = g.ldh_all;
+      g.ldh_all += round_up(layers[i].rank, 64);
+    }
+    off = align256(size_t(M) * size_t(g.ldh_all) * dtype_size(layers[0].dtype));
+  }
+  for (int i = 0; i < n; ++i) {
+    g.off[i] = off;
+    g.bytes[i] = M > 0 ? plan_forward(layers[i], M, nullptr).total : 0;
+    off += align256(g.bytes[i]);
+  }
+  g.total = off;
+  return SLR_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t slr_lrs_linear_group_workspace_size(const slr_layer* layers, int n, int64_t M) {
+  GroupPlan g;
+  if (M < 0 || plan_group(layers, n, M, g) != SLR_OK) return 0;
+  return g.total;
+}
+
+}  // extern "C"
+
+namespace {
+
+// Argument checks, per-layer packing and the grouped/per-layer decision of
+// the group entry points.  y may be NULL (x*B^T phase only).
+struct GroupCall {
+  GroupPlan g;
+  FwdCall c[kMaxGroup];
+  bool grouped = false;
+  uint8_t* ws = nullptr;
+};
+
+int prepare_group(const slr_layer* layers, int n, const void* x, int64_t ldx, void* const* y, const int64_t* ldy,
+                  int64_t M, void* workspace, size_t workspace_bytes, GroupCall& gc) {
+  int rc = plan_group(layers, n, M, gc.g);
+  if (rc) return rc;
+  if (M < 0) return fail(SLR_ERR_INVALID_ARGUMENT, "M must be >= 0");
+  if (M == 0) return SLR_OK;
+  if (gc.g.total > 0) {
+    if (!workspace) return fail(SLR_ERR_WORKSPACE, "workspace is NULL");
+    if (workspace_bytes < gc.g.total)
+      return fail(SLR_ERR_WORKSPACE, "workspace too small: need " + std::to_string(gc.g.total) + " bytes");
+    if (reinterpret_cast<uintptr_t>(workspace) & 255u) return fail(SLR_ERR_WORKSPACE, "workspace must be 256-byte aligned");
+  }
+  gc.ws = static_cast<uint8_t*>(workspace);
+  for (int i = 0; i < n; ++i) {
+    rc = prepare_forward(&layers[i], x, ldx, y ? y[i] : nullptr, ldy ? ldy[i] : 0, M, gc.ws + gc.g.off[i],
+                         gc.g.bytes[i], y != nullptr, gc.c[i]);
+    if (rc) return rc;
+  }
+  // One x*B^T GEMM for the whole group when every layer takes the
+  // tensor-core path; otherwise the layers run one after another.
+  bool grouped = n > 1 && M >= kTcMinTokens;
+  for (int i = 0; grouped && i < n; ++i) {
+    const slr_layer& L = layers[i];
+    grouped = gc.c[i].p.path == 1 && (L.flags & kFlagPairMma) == 0 &&
+              tc_dense_supported(x, gc.c[i].a.ldx, L.B, L.in_features, L.rank, L.dtype);
+    if (grouped) {
+      RowblockArgs a = gc.c[i].a;
+      a.H = gc.ws + size_t(gc.g.col[i]) * dtype_size(L.dtype);
+      a.ldh = gc.g.ldh_all;
+      // The layout may not depend on y (the x*B^T phase runs without it): check
+      // with an aligned stand-in; a combine whose real y is unaligned takes
+      // the small-batch kernel, which reads the grouped H all the same.
+      a.y = gc.ws;
+      a.ldy = L.out_features;
+      grouped = tc_rowblock_supported(a);
+    }
+  }
+  gc.grouped = grouped;
+  if (grouped)
+    for (int i = 0; i < n; ++i) {
+      gc.c[i].a.H = gc.ws + size_t(gc.g.col[i]) * dtype_size(layers[i].dtype);
+      gc.c[i].a.ldh = gc.g.ldh_all;
+    }
+  return SLR_OK;
+}
+
+int group_lowrank(const slr_layer* layers, int n, const GroupCall& gc, cudaStream_t s) {
+  if (!gc.grouped) {
+    for (int i = 0; i < n; ++i) {
+      int rc = run_lowrank(layers[i], gc.c[i], s);
+      if (rc) return rc;
+    }
+    return SLR_OK;
+  }
+  const void* Bs[kMaxGroup];
+  int64_t rs[kMaxGroup];
+  for (int i = 0; i < n; ++i) {
+    Bs[i] = layers[i].B;
+    rs[i] = layers[i].rank;
+  }
+  return launch_tc_dense_group(gc.c[0].a.x, gc.c[0].a.ldx, Bs, rs, n, gc.ws, gc.c[0].a.M, layers[0].in_features,
+                               gc.g.ldh_all, layers[0].dtype, s);
+}
+
+}  // namespace
+
+extern "C" {
+
+int slr_lrs_linear_forward_group(const slr_layer* layers, int n, const void* x, int64_t ldx, void* const* y,
+                                 const int64_t* ldy, int64_t M, void* workspace, size_t workspace_bytes,
+                                 void* stream) {
+  if (!y) return fail(SLR_ERR_INVALID_ARGUMENT, "y is NULL");
+  GroupCall gc;
+  int rc = prepare_group(layers, n, x, ldx, y, ldy, M, workspace, workspace_bytes, gc);
+  if (rc || M == 0) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (!gc.grouped) {
+    for (int i = 0; i < n; ++i) {
+      rc = run_lowrank(layers[i], gc.c[i], s);
+      if (rc) return rc;
+      rc = run_combine(layers[i], gc.c[i], true, s);
+      if (rc) return rc;
+    }
+    return SLR_OK;
+  }
+  rc = group_lowrank(layers, n, gc, s);
+  for (int i = 0; rc == SLR_OK && i < n; ++i) rc = run_combine(layers[i], gc.c[i], true, s);
+  return rc;
+}
+
+int slr_lrs_linear_group_lowrank(const slr_layer* layers, int n, const void* x, int64_t ldx, int64_t M,
+                                 void* workspace, size_t workspace_bytes, void* stream) {
+  GroupCall gc;
+  int rc = prepare_group(layers, n, x, ldx, nullptr, nullptr, M, workspace, workspace_bytes, gc);
+  if (rc || M == 0) return rc;
+  return group_lowrank(layers, n, gc, static_cast<cudaStream_t>(stream));
+}
+
+int slr_lrs_linear_group_combine(const slr_layer* layers, int n, int i, const void* x, int64_t ldx, void* y,
+                                 int64_t ldy, int64_t M, void* workspace, size_t workspace_bytes, void* stream) {
+  if (i < 0 || i >= n) return fail(SLR_ERR_INVALID_ARGUMENT, "layer index out of range");
+  if (!y) return fail(SLR_ERR_INVALID_ARGUMENT, "y is NULL");
+  GroupCall gc;
+  int rc = prepare_group(layers, n, x, ldx, nullptr, nullptr, M, workspace, workspace_bytes, gc);
+  if (rc || M == 0) return rc;
+  FwdCall c = gc.c[i];
+  rc = prepare_forward(&layers[i], x, ldx, y, ldy, M, gc.ws + gc.g.off[i], gc.g.bytes[i], true, c);
+  if (rc) return rc;
+  c.a.H = gc.c[i].a.H;
+  c.a.ldh = gc.c[i].a.ldh;
+  return run_combine(layers[i], c, false, static_cast<cudaStream_t>(stream));
+}
+
 int slr_dense_to_bsr_mask(const void* S, int64_t n, int64_t m, int64_t block_p, int64_t block_q,
                           int dtype, uint8_t* mask, int64_t* crow, void* stream) {
   if (!valid_dtype(dtype)) return fail(SLR_ERR_UNSUPPORTED_DTYPE, "dense_to_bsr: dtype must be f32/f16/bf16");

@@ -212,6 +212,76 @@ class LayerDesc:
         return out
 
 
+class LayerGroup:
+    """Layers that read the same input (q/k/v, gate/up): one grouped call.
+
+    ``forward(x)`` returns each layer's ``y`` exactly as
+    :meth:`LayerDesc.forward` would; for 128 or more tokens the ``x · Bᵀ``
+    products run as one GEMM over the stacked ``B`` matrices.
+    """
+
+    def __init__(self, descs: list[LayerDesc]):
+        if not 1 <= len(descs) <= 4:
+            raise ValueError("a group holds 1 to 4 layers")
+        if len({d.in_features for d in descs}) != 1 or len({d.dtype for d in descs}) != 1:
+            raise ValueError("grouped layers must share in_features and dtype")
+        self.descs = list(descs)
+        self.device = descs[0].device
+        self.dtype = descs[0].dtype
+        self._ws: torch.Tensor | None = None
+
+    def _structs(self):
+        arr = (_lib.SlrLayer * len(self.descs))()
+        for i, d in enumerate(self.descs):
+            ctypes.memmove(ctypes.byref(arr[i]), ctypes.byref(d.struct), ctypes.sizeof(_lib.SlrLayer))
+        return arr
+
+    def workspace(self, M: int) -> torch.Tensor | None:
+        need = int(_lib.load().slr_lrs_linear_group_workspace_size(self._structs(), len(self.descs), M))
+        if need == 0:
+            return None
+        if self._ws is None or self._ws.numel() < need:
+            self._ws = torch.zeros(need, dtype=torch.uint8, device=self.device)
+        return self._ws
+
+    def forward(self, x2: torch.Tensor, outs: list[torch.Tensor] | None = None) -> list[torch.Tensor]:
+        M = x2.shape[0]
+        n = len(self.descs)
+        if outs is None:
+            outs = [torch.empty(M, d.out_features, dtype=self.dtype, device=self.device) for d in self.descs]
+        ws = self.workspace(M)
+        ys = (ctypes.c_void_p * n)(*[o.data_ptr() for o in outs])
+        lds = (ctypes.c_int64 * n)(*[LayerDesc._ld(o) for o in outs])
+        with _DeviceGuard(self.device):
+            rc = _lib.load().slr_lrs_linear_forward_group(
+                self._structs(), n, x2.data_ptr(), LayerDesc._ld(x2), ys, lds, M,
+                None if ws is None else ws.data_ptr(), 0 if ws is None else ws.numel(), _stream(self.device))
+        _lib.check(rc, "lrs_linear_forward_group")
+        return outs
+
+    def lowrank(self, x2: torch.Tensor) -> None:
+        """Phase 1 alone: every layer's x2 @ B.T into the group workspace."""
+        M = x2.shape[0]
+        ws = self.workspace(M)
+        with _DeviceGuard(self.device):
+            rc = _lib.load().slr_lrs_linear_group_lowrank(
+                self._structs(), len(self.descs), x2.data_ptr(), LayerDesc._ld(x2), M,
+                None if ws is None else ws.data_ptr(), 0 if ws is None else ws.numel(), _stream(self.device))
+        _lib.check(rc, "lrs_linear_group_lowrank")
+
+    def combine(self, i: int, x2: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+        """Phase 2 of layer i (after lowrank() on the same x2)."""
+        M = x2.shape[0]
+        ws = self.workspace(M)
+        with _DeviceGuard(self.device):
+            rc = _lib.load().slr_lrs_linear_group_combine(
+                self._structs(), len(self.descs), i, x2.data_ptr(), LayerDesc._ld(x2), out.data_ptr(),
+                LayerDesc._ld(out), M, None if ws is None else ws.data_ptr(), 0 if ws is None else ws.numel(),
+                _stream(self.device))
+        _lib.check(rc, "lrs_linear_group_combine")
+        return out
+
+
 def lrs_linear_forward(desc: LayerDesc, x: torch.Tensor) -> torch.Tensor:
     """``y = x @ S.T + (x @ B.T) @ A.T + bias`` for x of shape ``[..., in]``."""
     _require_cuda("x", x)

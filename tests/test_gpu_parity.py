@@ -321,6 +321,32 @@ def test_chained_layers_in_cuda_graph(cuda):
     assert torch.equal(out, ref2)
 
 
+GROUPS = {
+    # q/k/v-like: one x, different widths and ranks
+    "qkv": [(512, 512, 32, 32, 64, 0.3), (256, 512, 32, 32, 64, 0.3), (256, 512, 32, 32, 128, 0.25)],
+    # gate/up-like with 64x64 blocks
+    "gateup": [(1024, 512, 64, 64, 128, 0.2), (1024, 512, 64, 64, 128, 0.2)],
+    # a low-rank-only layer and a layer without bias or rank >= 64: falls back per layer
+    "mixed": [(512, 512, 16, 16, 64, 0.0), (256, 512, 16, 16, 32, 0.1)],
+}
+
+
+@pytest.mark.parametrize("group", list(GROUPS))
+@pytest.mark.parametrize("T", [1, 64, 128, 300, 1000])
+def test_group_forward_equals_per_layer(cuda, group, T):
+    specs = [random_layer(n, k, bp, bq, r, dens, seed=17 * n + r + i) for i, (n, k, bp, bq, r, dens)
+             in enumerate(GROUPS[group])]
+    descs = [desc_for(s.tensors("cpu", torch.bfloat16), s, cuda, torch.bfloat16) for s in specs]
+    x = workloads.tokens(T, specs[0].in_features, seed=T + 5, dtype=torch.bfloat16).to(cuda)
+    grp = ops.LayerGroup(descs)
+    ys = grp.forward(x)
+    grp.lowrank(x)
+    for i, (d, y) in enumerate(zip(descs, ys)):
+        ref = d.forward(x)
+        assert torch.equal(y, ref)
+        assert torch.equal(grp.combine(i, x, torch.empty_like(ref)), ref)
+
+
 # -------------------------------------------------- full-size properties --
 
 def torch_ref(t: dict, spec, x: torch.Tensor) -> torch.Tensor:

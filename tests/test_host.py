@@ -96,6 +96,32 @@ def test_layer_descriptor_validation_needs_no_gpu():
     assert fwd(0x100, 0x200, 0) == _lib.SLR_OK
 
 
+def test_group_call_validation_needs_no_gpu():
+    lib = _lib.load()
+    arr = (_lib.SlrLayer * 5)()
+    for i in range(5):
+        arr[i] = _lib.SlrLayer(in_features=64, out_features=64, rank=64, block_p=16, block_q=16, nnz=0,
+                               A=0x1000, B=0x2000, dtype=_lib.SLR_BF16)
+    ys = (ctypes.c_void_p * 5)(*([0x3000] * 5))
+    grp = lambda n, M=4: lib.slr_lrs_linear_forward_group(arr, n, 0x100, 0, ys, None, M, None, 0, None)  # noqa: E731
+    # size: H [M, 64 + 64] plus one workspace per layer, all 256-aligned
+    one = lib.slr_lrs_linear_workspace_size(ctypes.byref(arr[0]), 4)
+    two = lib.slr_lrs_linear_group_workspace_size(arr, 2, 4)
+    assert two >= 2 * one + 4 * 128 * 2 and two % 256 == 0
+    assert grp(2) == _lib.SLR_ERR_WORKSPACE
+    assert grp(0) == _lib.SLR_ERR_INVALID_ARGUMENT
+    assert grp(5) == _lib.SLR_ERR_INVALID_ARGUMENT
+    assert lib.slr_lrs_linear_group_workspace_size(arr, 5, 4) == 0
+    arr[1].in_features = 128  # layers of a group read one x
+    assert grp(2) == _lib.SLR_ERR_INVALID_ARGUMENT
+    assert "in_features" in _lib.last_error()
+    arr[1].in_features = 64
+    arr[1].dtype = _lib.SLR_F16
+    assert grp(2) == _lib.SLR_ERR_INVALID_ARGUMENT
+    arr[1].dtype = _lib.SLR_BF16
+    assert grp(2, M=0) == _lib.SLR_OK
+
+
 def test_dense_to_bsr_shape_error_text_matches_reference():
     lib = _lib.load()
     rc = lib.slr_dense_to_bsr_mask(None, 30, 32, 16, 16, _lib.SLR_F32, None, None, None)
