@@ -36,7 +36,7 @@
 extern "C" {
 #endif
 
-#define SLR_ABI_VERSION 1
+#define SLR_ABI_VERSION 2
 
 #if defined(__GNUC__)
 #define SLR_API __attribute__((visibility("default")))
@@ -154,6 +154,11 @@ typedef struct slr_layer {
   const void* bias;       /* device [N] or NULL */
   int32_t dtype;          /* slr_dtype of x, y, values, A, B, bias */
   int32_t flags;          /* 0, or SLR_FLAG_PAIR_MMA | SLR_FLAG_STRICT_ORDER */
+  const uint32_t* stage_plan;  /* device: column schedule of the tensor-core
+                                  path from slr_plan_stages for these crow, col,
+                                  row_order and block_p; NULL = computed on
+                                  the fly by the kernel (same result) */
+  const int32_t* stage_start;  /* device int32 [groups + 1] from slr_plan_stages */
 } slr_layer;
 
 /*
@@ -280,6 +285,24 @@ SLR_API int slr_dense_to_bsr_fill(const void* S, int64_t n, int64_t m, int64_t b
  * reference launches one CTA per active row in index order
  * (addmm_inplace.py:65); this order feeds heavy (skewed) rows first.
  */
+/*
+ * Column schedule of the tensor-core path (M >= 128), built once per layer on
+ * the host.  The kernel processes block-rows in groups of G = 256 / block_p
+ * (block_p 16, 32 or 64) taken consecutively from row_order (NULL = natural
+ * order); for each group it visits the union of the rows' columns, one stage
+ * per distinct column.  slr_plan_stages writes, per group, one record per
+ * stage (column | mask of the group rows that have it << 16) to `stages`
+ * and the group's first record index to stage_start[group] (stage_start has
+ * groups + 1 entries); the kernel then reads the schedule instead of merging
+ * col[] lists at run time.  With stages == NULL only *n_stages is set.
+ * SLR_ERR_UNSUPPORTED if block_p is not 16, 32 or 64 or a column index
+ * exceeds 65535.  No reference counterpart (the reference kernel walks one
+ * row per CTA, addmm_inplace.py:67-80).
+ */
+SLR_API int slr_plan_stages(const int32_t* crow_host, const int32_t* col_host, int64_t NB,
+                            const int32_t* row_order_host, int64_t block_p, uint32_t* stages,
+                            int32_t* stage_start, int64_t capacity, int64_t* n_stages);
+
 SLR_API int slr_plan_row_order(const int32_t* crow_host, int64_t NB, int32_t* order);
 
 /*

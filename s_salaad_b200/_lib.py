@@ -46,6 +46,7 @@ EXPORTED = (
     "slr_lrs_linear_group_combine",
     "slr_dense_to_bsr_mask",
     "slr_dense_to_bsr_fill",
+    "slr_plan_stages",
     "slr_plan_row_order",
     "slr_plan_shards",
 )
@@ -72,6 +73,8 @@ class SlrLayer(ctypes.Structure):
         ("bias", ctypes.c_void_p),
         ("dtype", ctypes.c_int32),
         ("flags", ctypes.c_int32),
+        ("stage_plan", ctypes.c_void_p),
+        ("stage_start", ctypes.c_void_p),
     ]
 
 
@@ -94,6 +97,7 @@ _SIGS = {
     "slr_lrs_linear_group_combine": ([ctypes.POINTER(SlrLayer), i32, i32, vp, i64, vp, i64, i64, vp, sz, vp], i32),
     "slr_dense_to_bsr_mask": ([vp, i64, i64, i64, i64, i32, vp, vp, vp], i32),
     "slr_dense_to_bsr_fill": ([vp, i64, i64, i64, i64, i32, vp, vp, vp, vp, i32, vp], i32),
+    "slr_plan_stages": ([vp, vp, i64, vp, i64, vp, vp, i64, ctypes.POINTER(i64)], i32),
     "slr_plan_row_order": ([vp, i64, vp], i32),
     "slr_plan_shards": ([vp, i64, i64, i64, i64, i32, vp], i32),
 }
@@ -125,7 +129,7 @@ def load(path: Path | str | None = None) -> ctypes.CDLL:
             fn = getattr(lib, name)
             fn.argtypes = args
             fn.restype = res
-        if lib.slr_abi_version() != 1:
+        if lib.slr_abi_version() != 2:
             raise RuntimeError("s_salaad_b200: libslr_b200.so ABI version mismatch")
         if path is None:
             _lib = lib

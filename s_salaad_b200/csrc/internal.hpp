@@ -22,6 +22,8 @@ struct RowblockArgs {
   const int32_t* col = nullptr;
   const void* values = nullptr;   // [nnz, bq, bp]
   const int32_t* rows = nullptr;  // block-row list (null = 0..nrows-1)
+  const uint32_t* stage_plan = nullptr;  // column schedule of each 256-feature row group
+  const int32_t* stage_start = nullptr;  // (from slr_plan_stages), or null
   int64_t nrows = 0;
   int64_t M = 0, K = 0, N = 0, r = 0, nnz = 0;
   int64_t ldx = 0, ldy = 0;  // row strides of x and y (elements)

@@ -50,6 +50,8 @@ struct TcArgs {
   const int32_t* crow;
   const int32_t* col;
   const int32_t* rows;
+  const uint32_t* plan;   // stage records (column | row mask << 16) per row group, or null
+  const int32_t* plan_start;
   int64_t M, ldy;
   int nrows, n_groups, n_mtiles, n_lr;
 };
@@ -185,8 +187,11 @@ __global__ void __launch_bounds__(kRowThreads, 1)
       const int r0 = gi * G;
       const int gcount = min(G, a.nrows - r0);
       const int m0 = mt * kTileM;
-      // cur = column of the row's next block, nxt = the one after (loaded a
-      // step ahead so no stage waits on a col[] load)
+      // Column source: the precomputed schedule (one 32-bit record per stage,
+      // 32 records per coalesced load, handed out by shuffles) or, without
+      // one, a merge of the rows' column lists: cur = column of the row's next
+      // block, nxt = the one after (loaded a step ahead so no stage waits on
+      // a col[] load), next column = warp minimum, its rows = a ballot.
       int rw = 0, ptr = 0, end = 0;
       uint32_t cur = kNone, nxt = kNone;
       if (lane < gcount) {
@@ -195,24 +200,42 @@ __global__ void __launch_bounds__(kRowThreads, 1)
           ptr = a.crow[rw];
           end = a.crow[rw + 1];
         }
-        if (ptr < end) cur = uint32_t(__ldg(a.col + ptr));
-        if (ptr + 1 < end) nxt = uint32_t(__ldg(a.col + ptr + 1));
+        if (!a.plan) {
+          if (ptr < end) cur = uint32_t(__ldg(a.col + ptr));
+          if (ptr + 1 < end) nxt = uint32_t(__ldg(a.col + ptr + 1));
+        }
       }
+      const int p0 = a.plan ? __ldg(a.plan_start + gi) : 0;
+      const int p1 = a.plan ? __ldg(a.plan_start + gi + 1) : 0;
+      int pos = p0;
+      uint32_t rec = 0;
       bool published = false;
       bool abort_now = false;
-      uint32_t c = __reduce_min_sync(0xffffffffu, cur);
+      uint32_t c = a.plan ? (p0 < p1 ? 0u : kNone) : __reduce_min_sync(0xffffffffu, cur);
       // One stage per (column, sub-slice) of the union of the group's columns.
       while (c != kNone && !abort_now) {
-        const bool mine = cur == c;
-        const uint32_t mask = __ballot_sync(0xffffffffu, mine);
+        uint32_t mask, cn;
+        if (a.plan) {
+          if (((pos - p0) & 31) == 0) rec = pos + lane < p1 ? __ldg(a.plan + pos + lane) : 0u;
+          const uint32_t r = __shfl_sync(0xffffffffu, rec, (pos - p0) & 31);
+          c = r & 0xffffu;
+          mask = r >> 16;
+          ++pos;
+          cn = pos < p1 ? 0u : kNone;
+        } else {
+          mask = __ballot_sync(0xffffffffu, cur == c);
+        }
+        const bool mine = (mask >> lane) & 1u;
         const int blk = ptr;
         const uint32_t cidx = __popc(mask & ((1u << lane) - 1u));
         if (mine) {
           ++ptr;
-          cur = nxt;
-          nxt = ptr + 1 < end ? uint32_t(__ldg(a.col + ptr + 1)) : kNone;
+          if (!a.plan) {
+            cur = nxt;
+            nxt = ptr + 1 < end ? uint32_t(__ldg(a.col + ptr + 1)) : kNone;
+          }
         }
-        const uint32_t cn = __reduce_min_sync(0xffffffffu, cur);
+        if (!a.plan) cn = __reduce_min_sync(0xffffffffu, cur);
         for (int sub = 0; sub < SUB; ++sub, ++g) {
           const uint32_t slot = g % STAGES, ph = (g / STAGES) & 1;
           int ok = lane == 0 ? int(mbar_wait(&empty[slot], ph ^ 1)) : 1;
@@ -656,7 +679,8 @@ int launch_tc_rowblock(const RowblockArgs& a, bool pdl, cudaStream_t s) {
     if (rc) return rc;
   }
   const int G = 256 / a.bp;
-  TcArgs k{a.y, a.mode == MODE_FUSED ? a.bias : nullptr, sparse ? a.crow : nullptr, a.col, a.rows, a.M, a.ldy,
+  TcArgs k{a.y, a.mode == MODE_FUSED ? a.bias : nullptr, sparse ? a.crow : nullptr, a.col, a.rows,
+           sparse ? a.stage_plan : nullptr, sparse ? a.stage_start : nullptr, a.M, a.ldy,
            int(a.nrows), int(ceil_div(a.nrows, G)), int(ceil_div(a.M, kTileM)), 0};
   if (a.mode == MODE_FUSED && a.r > 0) {
     k.n_lr = int(ceil_div(a.r, kLrK));

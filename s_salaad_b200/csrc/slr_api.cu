@@ -307,6 +307,8 @@ int prepare_forward(const slr_layer* layer, const void* x, int64_t ldx, void* y,
   a.col = L.col;
   a.values = L.values;
   a.rows = L.nnz > 0 ? L.row_order : nullptr;
+  a.stage_plan = (L.nnz > 0 && L.stage_start) ? L.stage_plan : nullptr;
+  a.stage_start = a.stage_plan ? L.stage_start : nullptr;
   a.nrows = L.out_features / c.p.row_bp;
   a.M = M;
   a.K = L.in_features;
@@ -591,6 +593,52 @@ int slr_dense_to_bsr_fill(const void* S, int64_t n, int64_t m, int64_t block_p, 
   if (!crow) return fail(SLR_ERR_INVALID_ARGUMENT, "null pointer");
   return launch_bsr_fill(S, n, m, block_p, block_q, dtype, mask, crow, col, values, transpose != 0,
                          static_cast<cudaStream_t>(stream));
+}
+
+int slr_plan_stages(const int32_t* crow, const int32_t* col, int64_t NB, const int32_t* order, int64_t block_p,
+                    uint32_t* stages, int32_t* stage_start, int64_t capacity, int64_t* n_stages) {
+  if (!n_stages || NB < 0 || (NB > 0 && (!crow || (crow[NB] > 0 && !col))))
+    return fail(SLR_ERR_INVALID_ARGUMENT, "bad arguments");
+  if (block_p != 16 && block_p != 32 && block_p != 64)
+    return fail(SLR_ERR_UNSUPPORTED, "stage schedules exist for block_p 16, 32 or 64 only");
+  const int G = int(256 / block_p);
+  const int64_t groups = (NB + G - 1) / G;
+  if (stages && !stage_start) return fail(SLR_ERR_INVALID_ARGUMENT, "stage_start is NULL");
+  // The same merge as the kernel's: the next column is the smallest head
+  // among the group's rows; every row whose head equals it advances.
+  int64_t n = 0;
+  for (int64_t gi = 0; gi < groups; ++gi) {
+    if (stages) stage_start[gi] = int32_t(n);
+    const int cnt = int(std::min<int64_t>(G, NB - gi * G));
+    int64_t ptr[16], end[16];
+    for (int j = 0; j < cnt; ++j) {
+      const int64_t r = order ? order[gi * G + j] : gi * G + j;
+      if (r < 0 || r >= NB) return fail(SLR_ERR_INVALID_ARGUMENT, "row_order entry out of range");
+      ptr[j] = crow[r];
+      end[j] = crow[r + 1];
+    }
+    while (true) {
+      int64_t c = INT64_MAX;
+      for (int j = 0; j < cnt; ++j)
+        if (ptr[j] < end[j]) c = std::min<int64_t>(c, col[ptr[j]]);
+      if (c == INT64_MAX) break;
+      if (c < 0 || c > 0xffff) return fail(SLR_ERR_UNSUPPORTED, "column index outside [0, 65535]");
+      uint32_t mask = 0;
+      for (int j = 0; j < cnt; ++j)
+        if (ptr[j] < end[j] && col[ptr[j]] == c) {
+          mask |= 1u << j;
+          ++ptr[j];
+        }
+      if (stages) {
+        if (n >= capacity) return fail(SLR_ERR_INVALID_ARGUMENT, "stage capacity too small");
+        stages[n] = uint32_t(c) | (mask << 16);
+      }
+      ++n;
+    }
+  }
+  if (stages) stage_start[groups] = int32_t(n);
+  *n_stages = n;
+  return SLR_OK;
 }
 
 int slr_plan_row_order(const int32_t* crow_host, int64_t NB, int32_t* order) {

@@ -130,6 +130,8 @@ class LayerDesc:
         self.block_q = int(block_q)
         self.struct = _lib.SlrLayer()
         self._ws: torch.Tensor | None = None
+        self._plan_key = None
+        self._plan = None
         self.refresh()
 
     def refresh(self, **tensors) -> None:
@@ -156,6 +158,18 @@ class LayerDesc:
         self.device = A.device
         self.dtype = A.dtype
         self.key = tuple(_ptr(v) for v in t.values())
+        # column schedule of the tensor-core path, rebuilt when the indices move
+        pk = (_ptr(t["crow"]), _ptr(t["col"]), _ptr(t["row_order"]), self.block_p) if nnz else None
+        if pk != self._plan_key:
+            self._plan_key = pk
+            self._plan = None
+            if nnz and A.dtype != torch.float32:
+                p = plan_stages(t["crow"], t["col"], self.block_p, t["row_order"])
+                if p is not None:
+                    self._plan = tuple(torch.from_numpy(a.view(np.int32) if a.dtype == np.uint32 else a).to(A.device)
+                                       for a in p)
+        s.stage_plan = self._plan[0].data_ptr() if self._plan is not None else None
+        s.stage_start = self._plan[1].data_ptr() if self._plan is not None else None
 
     def workspace_bytes(self, M: int) -> int:
         return int(_lib.load().slr_lrs_linear_workspace_size(ctypes.byref(self.struct), M))
@@ -345,6 +359,29 @@ def plan_row_order(crow) -> np.ndarray:
     out = np.empty(max(NB, 0), dtype=np.int32)
     _lib.check(_lib.load().slr_plan_row_order(c.ctypes.data, NB, out.ctypes.data), "plan_row_order")
     return out
+
+
+def plan_stages(crow, col, block_p: int, row_order=None) -> tuple[np.ndarray, np.ndarray] | None:
+    """Column schedule of the tensor-core path (``slr_plan_stages``): stage
+    records and per-group starts, or None when the layer has no such path
+    (block_p not 16/32/64, or a column index above 65535)."""
+    host = lambda t: np.ascontiguousarray(np.asarray(t.cpu() if hasattr(t, "cpu") else t), dtype=np.int32)  # noqa: E731
+    c, k = host(crow), host(col)
+    o = None if row_order is None else host(row_order)
+    NB = c.shape[0] - 1
+    if block_p not in (16, 32, 64) or NB <= 0 or int(c[-1]) == 0:
+        return None
+    lib = _lib.load()
+    n = ctypes.c_int64(0)
+    args = (c.ctypes.data, k.ctypes.data, NB, None if o is None else o.ctypes.data, block_p)
+    if lib.slr_plan_stages(*args, None, None, 0, ctypes.byref(n)) != _lib.SLR_OK:
+        return None
+    G = 256 // block_p
+    stages = np.empty(max(n.value, 1), dtype=np.uint32)
+    starts = np.empty((NB + G - 1) // G + 1, dtype=np.int32)
+    _lib.check(lib.slr_plan_stages(*args, stages.ctypes.data, starts.ctypes.data, stages.shape[0], ctypes.byref(n)),
+               "plan_stages")
+    return stages[:n.value], starts
 
 
 def plan_shards(crow, block_p: int, block_q: int, rank: int, world: int) -> np.ndarray:

@@ -265,6 +265,24 @@ def test_forward_captures_in_cuda_graph(cuda):
     assert torch.equal(out, y_eager)
 
 
+@pytest.mark.parametrize("shape", [(512, 512, 32, 32, 64, 0.3), (512, 256, 16, 16, 64, 0.2),
+                                   (512, 1024, 64, 64, 128, 0.25), (384, 512, 64, 128, 64, 0.4)],
+                         ids=lambda s: "x".join(map(str, s)))
+def test_stage_schedule_equals_runtime_merge(cuda, shape):
+    """The tensor-core kernel gives identical results with the precomputed
+    column schedule and with its own run-time merge of col[] lists."""
+    n, k, bp, bq, r, dens = shape
+    spec = random_layer(n, k, bp, bq, r, dens, seed=n + k)
+    d = desc_for(spec.tensors("cpu", torch.bfloat16), spec, cuda, torch.bfloat16)
+    assert d.struct.stage_plan
+    x = workloads.tokens(300, k, seed=9, dtype=torch.bfloat16).to(cuda)
+    y_plan = d.forward(x)
+    d.struct.stage_plan = None
+    d.struct.stage_start = None
+    y_merge = d.forward(x)
+    assert torch.equal(y_plan, y_merge)
+
+
 def _chain(cuda, T, flags, between=None, shared_ws=True):
     specs = [random_layer(1024, 1024, 32, 32, 64, 0.3, seed=60 + i, value_std=0.05) for i in range(6)]
     ds = [desc_for(s.tensors("cpu", torch.bfloat16), s, cuda, torch.bfloat16) for s in specs]

@@ -32,7 +32,7 @@ def test_library_exports_every_declared_symbol():
     for name in _declared_symbols():
         assert name in exported, name
         assert getattr(lib, name) is not None
-    assert lib.slr_abi_version() == 1
+    assert lib.slr_abi_version() == 2
 
 
 def test_library_is_built_for_sm100a():
@@ -94,6 +94,35 @@ def test_layer_descriptor_validation_needs_no_gpu():
     assert fwd(0x100, 0x200, 4, ldx=32) == _lib.SLR_ERR_INVALID_ARGUMENT
     # M == 0 is a no-op
     assert fwd(0x100, 0x200, 0) == _lib.SLR_OK
+
+
+def test_stage_schedule_matches_a_python_merge():
+    from s_salaad_b200 import ops, workloads
+
+    for bp, bq, dens, seed in [(32, 32, 0.3, 1), (16, 16, 0.05, 2), (64, 64, 0.5, 3)]:
+        crow, col = workloads.bernoulli_structure(1024 // bp, 2048 // bq, dens, seed)
+        crow, col = crow.astype(np.int32), col.astype(np.int32)
+        order = ops.plan_row_order(crow)
+        stages, starts = ops.plan_stages(crow, col, bp, order)
+        G = 256 // bp
+        NB = crow.shape[0] - 1
+        recs = []
+        for gi in range((NB + G - 1) // G):
+            assert starts[gi] == len(recs)
+            rows = [int(order[r]) for r in range(gi * G, min(NB, gi * G + G))]
+            heads = [list(col[crow[r]:crow[r + 1]]) for r in rows]
+            while any(heads):
+                c = min(h[0] for h in heads if h)
+                mask = 0
+                for j, h in enumerate(heads):
+                    if h and h[0] == c:
+                        mask |= 1 << j
+                        h.pop(0)
+                recs.append(int(c) | (mask << 16))
+        assert starts[-1] == len(recs)
+        assert stages.tolist() == recs
+    # no tensor-core schedule for other block heights
+    assert ops.plan_stages(np.array([0, 1], np.int32), np.array([0], np.int32), 8) is None
 
 
 def test_group_call_validation_needs_no_gpu():
