@@ -290,18 +290,20 @@ SLR_API int slr_dense_to_bsr_fill(const void* S, int64_t n, int64_t m, int64_t b
  * the host.  The kernel processes block-rows in groups of G = 256 / block_p
  * (block_p 16, 32 or 64) taken consecutively from row_order (NULL = natural
  * order); for each group it visits the union of the rows' columns, one stage
- * per distinct column.  slr_plan_stages writes, per group, one record per
- * stage (column | mask of the group rows that have it << 16) to `stages`
- * and the group's first record index to stage_start[group] (stage_start has
- * groups + 1 entries); the kernel then reads the schedule instead of merging
- * col[] lists at run time.  With stages == NULL only *n_stages is set.
- * SLR_ERR_UNSUPPORTED if block_p is not 16, 32 or 64 or a column index
- * exceeds 65535.  No reference counterpart (the reference kernel walks one
- * row per CTA, addmm_inplace.py:67-80).
+ * per distinct column.  slr_plan_stages writes `plan` (uint32 words): for
+ * every stage a record {column | (mask of the group rows that have it) << 16,
+ * index of its first block index}, i.e. words [2s, 2s+1], then, after all
+ * records, the value-block index of each present row of each stage.
+ * stage_start[group] is the group's first stage (groups + 1 entries, the
+ * last = total stages).  The kernel's producers then take stages
+ * independently instead of merging col[] lists.  With plan == NULL only
+ * *n_words is set.  SLR_ERR_UNSUPPORTED if block_p is not 16, 32 or 64 or a
+ * column index exceeds 65535.  No reference counterpart (the reference kernel
+ * walks one row per CTA, addmm_inplace.py:67-80).
  */
 SLR_API int slr_plan_stages(const int32_t* crow_host, const int32_t* col_host, int64_t NB,
-                            const int32_t* row_order_host, int64_t block_p, uint32_t* stages,
-                            int32_t* stage_start, int64_t capacity, int64_t* n_stages);
+                            const int32_t* row_order_host, int64_t block_p, uint32_t* plan,
+                            int32_t* stage_start, int64_t capacity, int64_t* n_words);
 
 SLR_API int slr_plan_row_order(const int32_t* crow_host, int64_t NB, int32_t* order);
 

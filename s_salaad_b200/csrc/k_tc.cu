@@ -17,9 +17,10 @@
 // Warp roles: warp 1 lane 0 issues MMAs (warp 1 also owns the TMEM
 // allocation), warps 2-5 drain TMEM (warp w reads TMEM lanes 32*(w%4) .. +31,
 // i.e. tokens of that quarter).  TMA loads: warp 0 lane 0 in the dense kernel;
-// in the fused kernel warps 0 and 6 both walk the item's stages (lane j of
-// each follows block-row j of the group) and split each stage's TMA loads
-// between them, because one thread issues a TMA load only every ~60 cycles.
+// in the fused kernel four warps (0, 6, 7, 8) each fill every fourth stage
+// from the layer's precomputed column schedule, because one warp needs ~1000
+// cycles of issue work per stage (waits, descriptors, ~60 cycles per TMA
+// load) and the tensor core would otherwise wait on it.
 // The accumulator is double-buffered in TMEM so the epilogue of one item
 // overlaps the MMAs of the next.  Shared memory holds an 8-stage ring.
 //
@@ -40,8 +41,9 @@ __device__ unsigned g_status_tc = 0;
 
 constexpr int kThreads = 192;        // tc_dense_kernel
 constexpr int kMaxSeg = 4;           // weight matrices per grouped x*B^T
-constexpr int kRowThreads = 224;     // tc_rowblock_kernel: + a second TMA warp
-constexpr int kProd2 = 6;            // that warp
+constexpr int kRowThreads = 288;     // tc_rowblock_kernel: warps 0, 6, 7, 8 load operands
+constexpr int kProd2 = 6;            // first of the extra TMA warps
+constexpr int kProducers = 4;        // TMA warps working from a column schedule
 constexpr int kTileM = 128;
 
 struct TcArgs {
@@ -81,7 +83,7 @@ struct RowCfg {
   static constexpr uint32_t BOFF = X_BYTES > H_BYTES ? X_BYTES : H_BYTES;
   static constexpr uint32_t BREG = G * (V_BYTES > AR_BYTES ? V_BYTES : AR_BYTES);  // value blocks / A rows
   static constexpr uint32_t STAGE = (BOFF + BREG + 1023u) & ~1023u;
-  static constexpr int STAGES = (200 * 1024) / STAGE > 8 ? 8 : (200 * 1024) / STAGE;
+  static constexpr int STAGES = 4;  // a multiple of kProducers (each producer warp owns slots)
   static constexpr size_t SMEM = 1024 + size_t(STAGES) * STAGE + (3 * STAGES + 4) * 8 + STAGES * 4 + 16;
 };
 
@@ -100,7 +102,7 @@ constexpr uint32_t kMetaLast = 1u << 31;  // last stage of the work item
 // k16.  Every MMA accumulates: the epilogue re-zeroes each accumulator after
 // draining it.
 //
-// Warps: 0 and 6 TMA producers, 1 MMA issuer, 2-5 epilogue.
+// Warps: 0 and 6-8 TMA producers, 1 MMA issuer, 2-5 epilogue.
 template <int BP, int BQ, typename TI, int MODE>
 __global__ void __launch_bounds__(kRowThreads, 1)
     tc_rowblock_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_v,
@@ -118,6 +120,7 @@ __global__ void __launch_bounds__(kRowThreads, 1)
   constexpr uint32_t IDESC_LR = idesc_f16<TI>(kTileM, 256, false);
   static_assert(X_BYTES % 1024 == 0 && H_BYTES % 1024 == 0 && AR_BYTES % 512 == 0, "tile alignment");
   static_assert(G * BP == 256 && G <= 16, "group must span 256 columns");
+  static_assert(STAGES % kProducers == 0, "each producer warp owns whole ring slots");
   static_assert(STAGE % 1024 == 0 && V_BYTES % 256 == 0 && BOFF % 1024 == 0, "alignment of stages / value slots");
 
   extern __shared__ uint8_t smem_raw[];
@@ -161,15 +164,8 @@ __global__ void __launch_bounds__(kRowThreads, 1)
   tc_fence_after();
   const int n_items = a.n_groups * a.n_mtiles;
 
-  if (warp == 0 || warp == kProd2) {
+  if (warp == 0 || warp >= kProd2) {
     // ------------------------------------------------------- TMA producers
-    // Both warps walk the same stage sequence.  Lane j (< G) follows block-row
-    // j of the item's group: its cursor into the row's columns; the next
-    // column is the warp minimum and the rows having it a ballot.  Warp 0
-    // publishes each stage (row mask, expected bytes); warp 6 loads the x
-    // tile; the value blocks (and A rows) alternate between the two warps.
-    const int pw = warp == 0 ? 0 : 1;
-    constexpr uint32_t kNone = 0x7fffffffu;
     if (lane == 0) {
       tma_prefetch_desc(&tm_x);
       if (a.crow) tma_prefetch_desc(&tm_v);
@@ -178,6 +174,77 @@ __global__ void __launch_bounds__(kRowThreads, 1)
         tma_prefetch_desc(&tm_a);
       }
     }
+    if (a.plan) {
+      // With the column schedule every stage is independent: producer warp p
+      // (warps 0, 6, 7, 8) fills the stages g with g % 4 == p, i.e. always
+      // the same ring slot, so its waits on that slot stay in phase order.
+      const int pw = warp == 0 ? 0 : warp - kProd2 + 1;
+      const uint32_t* blk_idx = a.plan;  // records' second words index into the plan
+      uint32_t g = 0;
+      bool waited = false, abort_now = false;
+      for (int item = blockIdx.x; item < n_items && !abort_now; item += gridDim.x) {
+        const int gi = item / a.n_mtiles, mt = item - gi * a.n_mtiles;
+        const int r0 = gi * G;
+        const int gcount = min(G, a.nrows - r0);
+        const int m0 = mt * kTileM;
+        const int p0 = __ldg(a.plan_start + gi), p1 = __ldg(a.plan_start + gi + 1);
+        const int n_sp = (p1 - p0) * SUB;
+        const int n_st = max(n_sp + a.n_lr, 1);  // a terminator stage when there is nothing
+        const int rw = lane < gcount ? (a.rows ? a.rows[r0 + lane] : r0 + lane) : 0;
+        for (int s = (pw - int(g % kProducers) + kProducers) % kProducers; s < n_st; s += kProducers) {
+          const uint32_t gg = g + uint32_t(s);
+          const uint32_t slot = gg % STAGES, ph = (gg / STAGES) & 1;
+          int ok = lane == 0 ? int(mbar_wait(&empty[slot], ph ^ 1)) : 1;
+          ok = __shfl_sync(0xffffffffu, ok, 0);
+          if (!ok) {
+            if (lane == 0) tc_timeout(&s_abort);
+            abort_now = true;
+            break;
+          }
+          uint8_t* adst = smem + slot * STAGE;
+          const bool last = s == n_st - 1;
+          if (s < n_sp) {
+            const int k = p0 + s / SUB, sub = s % SUB;
+            const uint32_t rec = __ldg(a.plan + 2 * k), first = __ldg(a.plan + 2 * k + 1);
+            const uint32_t c = rec & 0xffffu, mask = rec >> 16;
+            if (lane == 0) {
+              meta[slot] = mask | (last ? kMetaLast : 0u);
+              mbar_arrive_expect_tx(&full[slot], X_BYTES + __popc(mask) * V_BYTES);
+              tma_load_2d(adst, &tm_x, int(c) * BQ + sub * KS, m0, &full[slot]);
+            }
+            if ((mask >> lane) & 1u) {
+              const int blk = int(__ldg(blk_idx + first + __popc(mask & ((1u << lane) - 1u))));
+              tma_load_2d(adst + BOFF + lane * V_BYTES, &tm_v, 0, blk * BQ + sub * KS, &full[slot]);
+            }
+          } else if (s < n_sp + a.n_lr) {
+            const int l = s - n_sp;
+            if (!waited) {
+              pdl_wait_primary();  // H comes from the preceding kernel
+              waited = true;
+            }
+            if (lane == 0) {
+              meta[slot] = kMetaLR | uint32_t(gcount) | (last ? kMetaLast : 0u);
+              mbar_arrive_expect_tx(&full[slot], H_BYTES + gcount * AR_BYTES);
+              tma_load_2d(adst, &tm_h, l * kLrK, m0, &full[slot]);
+            }
+            if (lane < gcount)
+              tma_load_2d(adst + BOFF + lane * AR_BYTES, &tm_a, l * kLrK, rw * BP, &full[slot]);
+          } else if (lane == 0) {
+            meta[slot] = kMetaLast;  // no block and no rank: the item still completes
+            mbar_arrive(&full[slot]);
+          }
+        }
+        g += uint32_t(n_st);
+      }
+    } else if (warp == 0 || warp == kProd2) {
+    // Without a schedule, warps 0 and 6 both walk the stage sequence.  Lane j
+    // (< G) follows block-row j of the item's group: cur = column of the
+    // row's next block, nxt = the one after (loaded a step ahead so no stage
+    // waits on a col[] load); the next column is the warp minimum and its
+    // rows a ballot.  Warp 0 publishes each stage (row mask, expected bytes),
+    // warp 6 loads the x tile, the value blocks (and A rows) alternate.
+    const int pw = warp == 0 ? 0 : 1;
+    constexpr uint32_t kNone = 0x7fffffffu;
     bool waited = false;
     uint32_t g = 0;
     // warp-uniform view of the abort flag (the loops below use warp collectives)
@@ -187,11 +254,6 @@ __global__ void __launch_bounds__(kRowThreads, 1)
       const int r0 = gi * G;
       const int gcount = min(G, a.nrows - r0);
       const int m0 = mt * kTileM;
-      // Column source: the precomputed schedule (one 32-bit record per stage,
-      // 32 records per coalesced load, handed out by shuffles) or, without
-      // one, a merge of the rows' column lists: cur = column of the row's next
-      // block, nxt = the one after (loaded a step ahead so no stage waits on
-      // a col[] load), next column = warp minimum, its rows = a ballot.
       int rw = 0, ptr = 0, end = 0;
       uint32_t cur = kNone, nxt = kNone;
       if (lane < gcount) {
@@ -200,42 +262,24 @@ __global__ void __launch_bounds__(kRowThreads, 1)
           ptr = a.crow[rw];
           end = a.crow[rw + 1];
         }
-        if (!a.plan) {
-          if (ptr < end) cur = uint32_t(__ldg(a.col + ptr));
-          if (ptr + 1 < end) nxt = uint32_t(__ldg(a.col + ptr + 1));
-        }
+        if (ptr < end) cur = uint32_t(__ldg(a.col + ptr));
+        if (ptr + 1 < end) nxt = uint32_t(__ldg(a.col + ptr + 1));
       }
-      const int p0 = a.plan ? __ldg(a.plan_start + gi) : 0;
-      const int p1 = a.plan ? __ldg(a.plan_start + gi + 1) : 0;
-      int pos = p0;
-      uint32_t rec = 0;
       bool published = false;
       bool abort_now = false;
-      uint32_t c = a.plan ? (p0 < p1 ? 0u : kNone) : __reduce_min_sync(0xffffffffu, cur);
+      uint32_t c = __reduce_min_sync(0xffffffffu, cur);
       // One stage per (column, sub-slice) of the union of the group's columns.
       while (c != kNone && !abort_now) {
-        uint32_t mask, cn;
-        if (a.plan) {
-          if (((pos - p0) & 31) == 0) rec = pos + lane < p1 ? __ldg(a.plan + pos + lane) : 0u;
-          const uint32_t r = __shfl_sync(0xffffffffu, rec, (pos - p0) & 31);
-          c = r & 0xffffu;
-          mask = r >> 16;
-          ++pos;
-          cn = pos < p1 ? 0u : kNone;
-        } else {
-          mask = __ballot_sync(0xffffffffu, cur == c);
-        }
-        const bool mine = (mask >> lane) & 1u;
+        const bool mine = cur == c;
+        const uint32_t mask = __ballot_sync(0xffffffffu, mine);
         const int blk = ptr;
         const uint32_t cidx = __popc(mask & ((1u << lane) - 1u));
         if (mine) {
           ++ptr;
-          if (!a.plan) {
-            cur = nxt;
-            nxt = ptr + 1 < end ? uint32_t(__ldg(a.col + ptr + 1)) : kNone;
-          }
+          cur = nxt;
+          nxt = ptr + 1 < end ? uint32_t(__ldg(a.col + ptr + 1)) : kNone;
         }
-        if (!a.plan) cn = __reduce_min_sync(0xffffffffu, cur);
+        const uint32_t cn = __reduce_min_sync(0xffffffffu, cur);
         for (int sub = 0; sub < SUB; ++sub, ++g) {
           const uint32_t slot = g % STAGES, ph = (g / STAGES) & 1;
           int ok = lane == 0 ? int(mbar_wait(&empty[slot], ph ^ 1)) : 1;
@@ -302,6 +346,7 @@ __global__ void __launch_bounds__(kRowThreads, 1)
         if (!ok) break;
         ++g;
       }
+    }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------- MMA issuer

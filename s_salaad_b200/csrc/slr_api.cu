@@ -596,48 +596,64 @@ int slr_dense_to_bsr_fill(const void* S, int64_t n, int64_t m, int64_t block_p, 
 }
 
 int slr_plan_stages(const int32_t* crow, const int32_t* col, int64_t NB, const int32_t* order, int64_t block_p,
-                    uint32_t* stages, int32_t* stage_start, int64_t capacity, int64_t* n_stages) {
-  if (!n_stages || NB < 0 || (NB > 0 && (!crow || (crow[NB] > 0 && !col))))
+                    uint32_t* plan, int32_t* stage_start, int64_t capacity, int64_t* n_words) {
+  if (!n_words || NB < 0 || (NB > 0 && (!crow || (crow[NB] > 0 && !col))))
     return fail(SLR_ERR_INVALID_ARGUMENT, "bad arguments");
   if (block_p != 16 && block_p != 32 && block_p != 64)
     return fail(SLR_ERR_UNSUPPORTED, "stage schedules exist for block_p 16, 32 or 64 only");
   const int G = int(256 / block_p);
   const int64_t groups = (NB + G - 1) / G;
-  if (stages && !stage_start) return fail(SLR_ERR_INVALID_ARGUMENT, "stage_start is NULL");
-  // The same merge as the kernel's: the next column is the smallest head
-  // among the group's rows; every row whose head equals it advances.
-  int64_t n = 0;
-  for (int64_t gi = 0; gi < groups; ++gi) {
-    if (stages) stage_start[gi] = int32_t(n);
-    const int cnt = int(std::min<int64_t>(G, NB - gi * G));
-    int64_t ptr[16], end[16];
-    for (int j = 0; j < cnt; ++j) {
-      const int64_t r = order ? order[gi * G + j] : gi * G + j;
-      if (r < 0 || r >= NB) return fail(SLR_ERR_INVALID_ARGUMENT, "row_order entry out of range");
-      ptr[j] = crow[r];
-      end[j] = crow[r + 1];
-    }
-    while (true) {
-      int64_t c = INT64_MAX;
-      for (int j = 0; j < cnt; ++j)
-        if (ptr[j] < end[j]) c = std::min<int64_t>(c, col[ptr[j]]);
-      if (c == INT64_MAX) break;
-      if (c < 0 || c > 0xffff) return fail(SLR_ERR_UNSUPPORTED, "column index outside [0, 65535]");
-      uint32_t mask = 0;
-      for (int j = 0; j < cnt; ++j)
-        if (ptr[j] < end[j] && col[ptr[j]] == c) {
-          mask |= 1u << j;
-          ++ptr[j];
-        }
-      if (stages) {
-        if (n >= capacity) return fail(SLR_ERR_INVALID_ARGUMENT, "stage capacity too small");
-        stages[n] = uint32_t(c) | (mask << 16);
+  if (plan && !stage_start) return fail(SLR_ERR_INVALID_ARGUMENT, "stage_start is NULL");
+  // Pass 1 counts stages (records) and blocks; pass 2 writes records
+  // [0, 2 * stages) and the block indices after them.  The merge is the
+  // kernel's: the next column is the smallest head among the group's rows;
+  // every row whose head equals it advances.
+  int64_t n_st = 0, n_blk = 0;
+  for (int pass = 0; pass < 2; ++pass) {
+    if (pass == 1 && !plan) break;
+    if (pass == 1 && 2 * n_st + n_blk > capacity) return fail(SLR_ERR_INVALID_ARGUMENT, "plan capacity too small");
+    int64_t st = 0, bk = 2 * n_st;
+    for (int64_t gi = 0; gi < groups; ++gi) {
+      if (pass == 1) stage_start[gi] = int32_t(st);
+      const int cnt = int(std::min<int64_t>(G, NB - gi * G));
+      int64_t ptr[16], end[16];
+      for (int j = 0; j < cnt; ++j) {
+        const int64_t r = order ? order[gi * G + j] : gi * G + j;
+        if (r < 0 || r >= NB) return fail(SLR_ERR_INVALID_ARGUMENT, "row_order entry out of range");
+        ptr[j] = crow[r];
+        end[j] = crow[r + 1];
       }
-      ++n;
+      while (true) {
+        int64_t c = INT64_MAX;
+        for (int j = 0; j < cnt; ++j)
+          if (ptr[j] < end[j]) c = std::min<int64_t>(c, col[ptr[j]]);
+        if (c == INT64_MAX) break;
+        if (c < 0 || c > 0xffff) return fail(SLR_ERR_UNSUPPORTED, "column index outside [0, 65535]");
+        uint32_t mask = 0;
+        const int64_t first = bk;
+        for (int j = 0; j < cnt; ++j)
+          if (ptr[j] < end[j] && col[ptr[j]] == c) {
+            mask |= 1u << j;
+            if (pass == 1) plan[bk] = uint32_t(ptr[j]);
+            ++bk;
+            ++ptr[j];
+          }
+        if (pass == 1) {
+          plan[2 * st] = uint32_t(c) | (mask << 16);
+          plan[2 * st + 1] = uint32_t(first);
+        }
+        ++st;
+      }
+    }
+    if (pass == 0) {
+      n_st = st;
+      n_blk = bk;
+    } else {
+      stage_start[groups] = int32_t(st);
     }
   }
-  if (stages) stage_start[groups] = int32_t(n);
-  *n_stages = n;
+  if (2 * n_st + n_blk > INT32_MAX) return fail(SLR_ERR_UNSUPPORTED, "plan larger than 2^31 words");
+  *n_words = 2 * n_st + n_blk;
   return SLR_OK;
 }
 

@@ -362,9 +362,9 @@ def plan_row_order(crow) -> np.ndarray:
 
 
 def plan_stages(crow, col, block_p: int, row_order=None) -> tuple[np.ndarray, np.ndarray] | None:
-    """Column schedule of the tensor-core path (``slr_plan_stages``): stage
-    records and per-group starts, or None when the layer has no such path
-    (block_p not 16/32/64, or a column index above 65535)."""
+    """Column schedule of the tensor-core path (``slr_plan_stages``): the plan
+    words and the per-group stage starts, or None when the layer has no such
+    path (block_p not 16/32/64, or a column index above 65535)."""
     host = lambda t: np.ascontiguousarray(np.asarray(t.cpu() if hasattr(t, "cpu") else t), dtype=np.int32)  # noqa: E731
     c, k = host(crow), host(col)
     o = None if row_order is None else host(row_order)
@@ -377,11 +377,11 @@ def plan_stages(crow, col, block_p: int, row_order=None) -> tuple[np.ndarray, np
     if lib.slr_plan_stages(*args, None, None, 0, ctypes.byref(n)) != _lib.SLR_OK:
         return None
     G = 256 // block_p
-    stages = np.empty(max(n.value, 1), dtype=np.uint32)
+    words = np.empty(max(n.value, 1), dtype=np.uint32)
     starts = np.empty((NB + G - 1) // G + 1, dtype=np.int32)
-    _lib.check(lib.slr_plan_stages(*args, stages.ctypes.data, starts.ctypes.data, stages.shape[0], ctypes.byref(n)),
+    _lib.check(lib.slr_plan_stages(*args, words.ctypes.data, starts.ctypes.data, words.shape[0], ctypes.byref(n)),
                "plan_stages")
-    return stages[:n.value], starts
+    return words[:n.value], starts
 
 
 def plan_shards(crow, block_p: int, block_q: int, rank: int, world: int) -> np.ndarray:

@@ -97,30 +97,35 @@ def test_layer_descriptor_validation_needs_no_gpu():
 
 
 def test_stage_schedule_matches_a_python_merge():
-    from s_salaad_b200 import ops, workloads
-
     for bp, bq, dens, seed in [(32, 32, 0.3, 1), (16, 16, 0.05, 2), (64, 64, 0.5, 3)]:
         crow, col = workloads.bernoulli_structure(1024 // bp, 2048 // bq, dens, seed)
         crow, col = crow.astype(np.int32), col.astype(np.int32)
         order = ops.plan_row_order(crow)
-        stages, starts = ops.plan_stages(crow, col, bp, order)
+        words, starts = ops.plan_stages(crow, col, bp, order)
         G = 256 // bp
         NB = crow.shape[0] - 1
-        recs = []
+        recs, blks = [], []
         for gi in range((NB + G - 1) // G):
             assert starts[gi] == len(recs)
             rows = [int(order[r]) for r in range(gi * G, min(NB, gi * G + G))]
-            heads = [list(col[crow[r]:crow[r + 1]]) for r in rows]
-            while any(heads):
-                c = min(h[0] for h in heads if h)
-                mask = 0
-                for j, h in enumerate(heads):
-                    if h and h[0] == c:
+            ptr = [int(crow[r]) for r in rows]
+            end = [int(crow[r + 1]) for r in rows]
+            while any(p < e for p, e in zip(ptr, end)):
+                c = min(int(col[p]) for p, e in zip(ptr, end) if p < e)
+                mask, first = 0, len(blks)
+                for j in range(len(rows)):
+                    if ptr[j] < end[j] and int(col[ptr[j]]) == c:
                         mask |= 1 << j
-                        h.pop(0)
-                recs.append(int(c) | (mask << 16))
-        assert starts[-1] == len(recs)
-        assert stages.tolist() == recs
+                        blks.append(ptr[j])
+                        ptr[j] += 1
+                recs.append((c | (mask << 16), first))
+        n = len(recs)
+        assert starts[-1] == n
+        got = words.tolist()
+        assert got[2 * n:] == blks
+        assert [(got[2 * i], got[2 * i + 1] - 2 * n) for i in range(n)] == recs
+        # every block appears exactly once
+        assert sorted(blks) == list(range(int(crow[-1])))
     # no tensor-core schedule for other block heights
     assert ops.plan_stages(np.array([0, 1], np.int32), np.array([0], np.int32), 8) is None
 
