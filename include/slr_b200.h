@@ -56,8 +56,9 @@ typedef enum slr_status {
 } slr_status;
 
 /* slr_layer.flags: run the combine phase of large batches (M >= 256, block_p
- * 32 or 64) on SM pairs with 2-SM MMAs (M = 256).  Faster only when most
- * column runs of a row group are long (dense-ish row groups); off by default. */
+ * 32 or 64) on SM pairs with 2-SM MMAs (M = 256 per MMA) even when the layer
+ * has no column schedule.  With a schedule (slr_layer.stage_plan) the pair
+ * kernel is the default for those shapes. */
 #define SLR_FLAG_PAIR_MMA 1
 /* slr_layer.flags: launch every kernel of a call only after all earlier work
  * on the stream has finished.  Without it, the small-batch kernels (M < 128)

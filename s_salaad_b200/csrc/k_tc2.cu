@@ -3,9 +3,11 @@
 //
 // Same work decomposition as tc_rowblock_kernel (k_tc.cu): one work item =
 // a token tile x a group of G = 256/bp consecutive block-rows of the row
-// list, the producer merges the group's column lists, each distinct column
-// is one stage, each run of consecutive present rows one MMA, then the
-// low-rank chunks as N = 256 MMAs, all into one fp32 TMEM accumulator.
+// list, each distinct column of the group is one stage (taken from the
+// layer's column schedule by three producer warps that each own two ring
+// slots, or merged from col[] by one thread without a schedule), each run of
+// consecutive present rows one MMA, then the low-rank chunks as N = 256
+// MMAs, all into one fp32 TMEM accumulator.
 // What changes on a pair of SMs:
 //   * the token tile is 256: each CTA loads the x (and H) rows of its own 128
 //     tokens and keeps those 128 accumulator rows in its own TMEM;
@@ -33,7 +35,9 @@ using namespace tc;
 
 __device__ unsigned g_status_tc2 = 0;
 
-constexpr int kThreads = 192;
+constexpr int kThreads = 256;   // warps 0, 6, 7 load operands, 1 issues MMAs, 2-5 epilogue
+constexpr int kProducers = 3;   // TMA warps working from a column schedule
+constexpr int kStages = 6;      // ring slots (a multiple of kProducers)
 constexpr uint32_t kMetaLR = 1u << 30;
 constexpr uint32_t kMetaLast = 1u << 31;
 
@@ -43,6 +47,8 @@ struct Tc2Args {
   const int32_t* crow;
   const int32_t* col;
   const int32_t* rows;
+  const uint32_t* plan;   // column schedule (slr_plan_stages) or null
+  const int32_t* plan_start;
   int64_t M, ldy;
   int nrows, n_groups, n_mtiles, n_lr;
 };
@@ -69,7 +75,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr uint32_t A_SLOT = 16384;
   constexpr uint32_t B_SLOT = (G * POS > (G / 2) * AR_ROW) ? G * POS : (G / 2) * AR_ROW;
   constexpr uint32_t STAGE = A_SLOT + B_SLOT;
-  constexpr int STAGES = (196 * 1024) / STAGE > 8 ? 8 : (196 * 1024) / STAGE;
+  constexpr int STAGES = kStages;
+  static_assert(STAGES * STAGE <= 200 * 1024 && STAGES % kProducers == 0, "ring size");
   constexpr uint32_t ACC = 256;
   constexpr uint32_t IDESC_SP = idesc_f16<TI>(256, 0, true);  // N set per run
   constexpr uint32_t IDESC_LR = idesc_f16<TI>(256, 256, false);
@@ -109,7 +116,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   cluster_sync();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  if (warp >= 2) {
+  if (warp >= 2 && warp < 6) {
     const uint32_t lane_base = uint32_t(32 * (warp & 3)) << 16;
     for (uint32_t c = 0; c < 2 * ACC; c += 16) tmem_st16_zero(tmem + lane_base + c);
     tmem_st_wait();
@@ -121,8 +128,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
   const int n_items = a.n_groups * a.n_mtiles;
 
-  if (warp == 0) {
-    // ------------------------------------------------------- TMA producer
+  if (warp == 0 || warp >= 6) {
+    // ------------------------------------------------------- TMA producers
     if (lane == 0) {
       tma_prefetch_desc(&tm_x);
       if (a.crow) tma_prefetch_desc(&tm_v);
@@ -130,6 +137,90 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_prefetch_desc(&tm_h);
         tma_prefetch_desc(&tm_a);
       }
+    }
+    if (a.plan) {
+      // With the column schedule producer warp p (0, 6, 7 -> 0, 1, 2) fills
+      // the stages g with g % 3 == p: always the same two ring slots, so its
+      // waits on them stay in phase order.  Each CTA loads its own 128 token
+      // rows and its half of the B operand; loads complete on the leader's
+      // barrier.
+      const int pw = warp == 0 ? 0 : warp - 5;
+      uint32_t g = 0;
+      bool waited = false, abort_now = false;
+      for (int item = pair; item < n_items && !abort_now; item += npairs) {
+        const int gi = item / a.n_mtiles, mt = item - gi * a.n_mtiles;
+        const int r0 = gi * G;
+        const int gcount = min(G, a.nrows - r0);
+        const int m0 = mt * 256 + int(rank) * 128;  // this CTA's tokens
+        const int p0 = __ldg(a.plan_start + gi), p1 = __ldg(a.plan_start + gi + 1);
+        const int n_sp = (p1 - p0) * SUB;
+        const int n_st = max(n_sp + a.n_lr, 1);
+        const int rw = lane < gcount ? (a.rows ? a.rows[r0 + lane] : r0 + lane) : 0;
+        for (int s = (pw - int(g % kProducers) + kProducers) % kProducers; s < n_st; s += kProducers) {
+          const uint32_t gg = g + uint32_t(s);
+          const uint32_t slot = gg % STAGES, ph = (gg / STAGES) & 1;
+          int ok = lane == 0 ? int(mbar_wait(&empty[slot], ph ^ 1)) : 1;
+          ok = __shfl_sync(0xffffffffu, ok, 0);
+          if (!ok) {
+            if (lane == 0) timeout2(&s_abort);
+            abort_now = true;
+            break;
+          }
+          const uint32_t fb = mapa(smem_u32(&full[slot]), 0);
+          uint8_t* adst = smem + slot * STAGE;
+          const bool last = s == n_st - 1;
+          if (s < n_sp) {
+            const int k = p0 + s / SUB, sub = s % SUB;
+            const uint32_t rec = __ldg(a.plan + 2 * k), first = __ldg(a.plan + 2 * k + 1);
+            const uint32_t c = rec & 0xffffu, mask = rec >> 16;
+            if (lane == 0) {
+              if (leader) {
+                meta[slot] = mask | (last ? kMetaLast : 0u);
+                mbar_arrive_expect_tx(&full[slot], 2 * (X_BYTES + __popc(mask) * POS));
+              }
+              tma2_load_2d(adst, &tm_x, int(c) * BQ + sub * KS, m0, fb);
+            }
+            if ((mask >> lane) & 1u) {
+              // this row's run of consecutive present rows [j0, end): its 2*len
+              // half-block atoms, the first len on the leader, the rest on the peer
+              const uint32_t below = (1u << lane) - 1u, zeros = ~mask & below;
+              const int j0 = zeros ? 32 - __clz(zeros) : 0;
+              const int end = lane + __ffs(~(mask >> lane)) - 1;
+              const int len = end - j0;
+              const int p_run = __popc(mask & ((1u << j0) - 1u));
+              const int blk = int(__ldg(a.plan + first + __popc(mask & below)));
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                const int at = 2 * (lane - j0) + h;
+                if (at / len == int(rank))
+                  tma2_load_2d(adst + A_SLOT + (p_run + at - int(rank) * len) * POS, &tm_v, h * (BP / 2),
+                               blk * BQ + sub * KS, fb);
+              }
+            }
+          } else if (s < n_sp + a.n_lr) {
+            const int l = s - n_sp;
+            if (!waited) {
+              pdl_wait_primary();  // H comes from the preceding kernel
+              waited = true;
+            }
+            if (lane == 0) {
+              if (leader) {
+                meta[slot] = kMetaLR | (last ? kMetaLast : 0u);
+                mbar_arrive_expect_tx(&full[slot], 2 * H_BYTES + gcount * AR_ROW);
+              }
+              tma2_load_2d(adst, &tm_h, l * 64, m0, fb);
+            }
+            const int jl = lane - int(rank) * (G / 2);
+            if (jl >= 0 && jl < G / 2 && lane < gcount)
+              tma2_load_2d(adst + A_SLOT + jl * AR_ROW, &tm_a, l * 64, rw * BP, fb);
+          } else if (lane == 0 && leader) {
+            meta[slot] = kMetaLast;  // no block and no rank: the item still completes
+            mbar_arrive(&full[slot]);
+          }
+        }
+        g += uint32_t(n_st);
+      }
+    } else if (warp == 0 && lane == 0) {
       bool waited = false;
       uint32_t g = 0;
       for (int item = pair; item < n_items && !s_abort; item += npairs) {
@@ -384,7 +475,7 @@ int launch_inst(const CUtensorMap& tx, const CUtensorMap& tv, const CUtensorMap&
   constexpr uint32_t POS = KS * BP, AR_ROW = BP * 128;
   constexpr uint32_t B_SLOT = (G * POS > (G / 2) * AR_ROW) ? G * POS : (G / 2) * AR_ROW;
   constexpr uint32_t STAGE = 16384 + B_SLOT;
-  constexpr int STAGES = (196 * 1024) / STAGE > 8 ? 8 : (196 * 1024) / STAGE;
+  constexpr int STAGES = kStages;
   const size_t smem = 1024 + size_t(STAGES) * STAGE + (2 * STAGES + 4) * 8 + STAGES * 4 + 16;
   auto kern = tc2_rowblock_kernel<BP, BQ, TI, MODE>;
   SLR_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
@@ -429,9 +520,11 @@ int dispatch_bp(int bp, int bq, const CUtensorMap& tx, const CUtensorMap& tv, co
 
 }  // namespace
 
-// Measured on B200: the pair kernel beats the 1-SM kernel only when most MMAs
-// are wide (N = 256); with the short row runs of typical block-sparse layers it
-// is slower, so the dispatcher does not select it by default.
+// Measured on B200 (LLaMA-7B-shaped layers, 64x64 blocks, 4096 tokens): with
+// the column schedule the pair kernel takes 7-14% less time than the 1-SM
+// kernel (half the B operand bytes per SM, half the MMA instructions per
+// MAC); with the single-thread merge it was slower, so the dispatcher picks
+// it only when a schedule is present (or SLR_FLAG_PAIR_MMA asks for it).
 bool tc2_rowblock_supported(const RowblockArgs& a) {
   return (a.bp == 32 || a.bp == 64) && a.M >= 256 && tc_rowblock_supported(a);
 }
@@ -450,7 +543,8 @@ int launch_tc2_rowblock(const RowblockArgs& a, bool pdl, cudaStream_t s) {
     if (rc) return rc;
   }
   const int G = 256 / a.bp;
-  Tc2Args k{a.y, a.mode == MODE_FUSED ? a.bias : nullptr, sparse ? a.crow : nullptr, a.col, a.rows, a.M, a.ldy,
+  Tc2Args k{a.y, a.mode == MODE_FUSED ? a.bias : nullptr, sparse ? a.crow : nullptr, a.col, a.rows,
+            sparse ? a.stage_plan : nullptr, sparse ? a.stage_start : nullptr, a.M, a.ldy,
             int(a.nrows), int(ceil_div(a.nrows, G)), int(ceil_div(a.M, 256)), 0};
   if (a.mode == MODE_FUSED && a.r > 0) {
     k.n_lr = int(ceil_div(a.r, 64));

@@ -327,9 +327,16 @@ int prepare_forward(const slr_layer* layer, const void* x, int64_t ldx, void* y,
 // True when the combine phase runs on the small-batch kernel (mma_rowblock).
 // That kernel and h_small read x and H only after griddepcontrol.wait, so
 // both may be launched as programmatic dependents of the preceding kernel.
+// The 2-SM pair kernel runs the combine phase when the layer carries a column
+// schedule (it then beats the 1-SM kernel on B200) or when the caller asks
+// for it; it needs block_p 32 or 64 and M >= 256.
+bool use_pair(const slr_layer& L, const FwdCall& c) {
+  return c.p.path == 1 && ((L.flags & kFlagPairMma) || c.a.stage_plan != nullptr) && tc2_rowblock_supported(c.a);
+}
+
 bool small_batch_path(const slr_layer& L, const FwdCall& c) {
   if (c.p.path != 1) return false;
-  if ((L.flags & kFlagPairMma) && tc2_rowblock_supported(c.a)) return false;
+  if (use_pair(L, c)) return false;
   if (c.a.M >= kTcMinTokens && tc_rowblock_supported(c.a)) return false;
   return true;
 }
@@ -353,8 +360,7 @@ int run_lowrank(const slr_layer& L, const FwdCall& c, cudaStream_t s) {
 // before it by this library (it reads H only after griddepcontrol.wait).
 int run_combine(const slr_layer& L, const FwdCall& c, bool pdl, cudaStream_t s) {
   if (c.a.M == 0) return SLR_OK;
-  if (c.p.path == 1 && (L.flags & kFlagPairMma) && tc2_rowblock_supported(c.a))
-    return launch_tc2_rowblock(c.a, pdl && L.rank > 0 && early_start(L), s);
+  if (use_pair(L, c)) return launch_tc2_rowblock(c.a, pdl && L.rank > 0 && early_start(L), s);
   if (c.p.path == 1 && c.a.M >= kTcMinTokens && tc_rowblock_supported(c.a))
     return launch_tc_rowblock(c.a, pdl && L.rank > 0 && early_start(L), s);
   if (c.p.path == 1) return launch_mma_rowblock(c.a, early_start(L), s);
@@ -481,8 +487,7 @@ int prepare_group(const slr_layer* layers, int n, const void* x, int64_t ldx, vo
   bool grouped = n > 1 && M >= kTcMinTokens;
   for (int i = 0; grouped && i < n; ++i) {
     const slr_layer& L = layers[i];
-    grouped = gc.c[i].p.path == 1 && (L.flags & kFlagPairMma) == 0 &&
-              tc_dense_supported(x, gc.c[i].a.ldx, L.B, L.in_features, L.rank, L.dtype);
+    grouped = gc.c[i].p.path == 1 && tc_dense_supported(x, gc.c[i].a.ldx, L.B, L.in_features, L.rank, L.dtype);
     if (grouped) {
       RowblockArgs a = gc.c[i].a;
       a.H = gc.ws + size_t(gc.g.col[i]) * dtype_size(L.dtype);
