@@ -348,9 +348,10 @@ def main() -> None:
 
     K = args.steps
     mk = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
-    # Decode-sized steps are a few microseconds of GPU work: replay them from a
-    # CUDA graph so host launch overhead is not timed (one GPU, T < 128).
-    use_graph = world == 1 and T < 128
+    # One GPU: the step is captured once and replayed from a CUDA graph, so
+    # host launch overhead (ctypes + tensor-map encoding, ~15 us per call) is
+    # not timed.  With NCCL in the step (N > 1) it runs eagerly.
+    use_graph = world == 1
     graph = None
     if use_graph:
         side = torch.cuda.Stream(dev)
@@ -383,7 +384,15 @@ def main() -> None:
     step_ms = [a.elapsed_time(b) for a, b in step_ev]
     total_ms = sum(step_ms)
     has_local = [world == 1 or layers[i].desc is not None for i in range(len(specs))]
-    if graph is None:
+    if graph is not None and T >= 128:
+        # Per-kernel durations for the roofline: the same steps once more,
+        # eagerly, with events between the x*B^T and combine launches (these
+        # kernels are long enough that the host stays ahead of the GPU).
+        for k in range(K):
+            flush.zero_()
+            step(kern_ev[k])
+        torch.cuda.synchronize()
+    if graph is None or T >= 128:
         h_ms = [sum(kern_ev[k][i][0].elapsed_time(kern_ev[k][i][1]) for k in range(K)) if has_local[i] else 0.0
                 for i in range(len(specs))]
         c_ms = [sum(kern_ev[k][i][1].elapsed_time(kern_ev[k][i][2]) for k in range(K)) if has_local[i] else 0.0
@@ -416,7 +425,7 @@ def main() -> None:
         low_flops += 2 * T * s.rank * s.in_features
     tensor_bound = T >= 128
     comb_s = sum(c_ms) / 1e3
-    if graph is not None:
+    if graph is not None and not tensor_bound:
         # whole layer set per graph replay: both kernels of every projection
         op_bytes = sum(s.weight_bytes(esize) + esize * T * (s.in_features + s.out_features) for s in specs)
         achieved = op_bytes * K / (total_ms / 1e3) / 1e9
@@ -437,6 +446,8 @@ def main() -> None:
     tfile = REPO / "profiles" / "traffic.json"
     if tfile.is_file():
         traffic = json.loads(tfile.read_text()).get(args.workload)
+    if tensor_bound:
+        roof["step_tflops"] = (comb_flops + low_flops) * K / (total_ms / 1e3) / 1e12
     roof.update({"achieved": achieved, "peak": peak, "peak_source": pk_src,
                  "frac": achieved / peak, "traffic": traffic,
                  "launch_ms_mean": sum(c_ms) / (K * len(specs)),

@@ -57,6 +57,7 @@ int launch_mma_rowblock(const RowblockArgs& a, bool pdl, cudaStream_t s);
 
 // ---- tcgen05 / TMEM kernels (16-bit dtypes): large token batches.
 constexpr int64_t kTcMinTokens = 128;  // below this the mma.sync path is used
+constexpr int64_t kTileTokens = 128;   // token rows per tensor-core work item
 bool tc_rowblock_supported(const RowblockArgs& a);
 int launch_tc_rowblock(const RowblockArgs& a, bool pdl, cudaStream_t s);
 bool tc2_rowblock_supported(const RowblockArgs& a);  // 2-SM pairs, M >= 256, bp 32/64

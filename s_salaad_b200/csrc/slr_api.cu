@@ -128,6 +128,16 @@ FwdPlan plan_forward(const slr_layer& L, int64_t M, const void* x) {
   return p;
 }
 
+// The tensor-core kernels take one 128-token tile x 256 features per SM at a
+// time; with fewer than 16 such items (few tokens and few output features,
+// e.g. 128 tokens of a 2048-wide projection) the small-batch kernel, which
+// spreads 16 features x 64 tokens per CTA over all SMs, is faster.
+bool tc_worthwhile(const RowblockArgs& a) {
+  if (a.M < kTcMinTokens || a.bp <= 0) return false;
+  const int64_t G = a.bp <= 256 ? 256 / a.bp : 1;
+  return ceil_div(a.nrows, G) * ceil_div(a.M, kTileTokens) >= 16;
+}
+
 int check_layer(const slr_layer* L) {
   if (!L) return fail(SLR_ERR_INVALID_ARGUMENT, "layer is NULL");
   if (!valid_dtype(L->dtype))
@@ -224,7 +234,7 @@ int slr_bsr_addmm_inplace(void* out, const void* x, int64_t M, int64_t K, const 
   a.dtype = dtype;
   a.mode = MODE_ADDMM;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (dtype != SLR_F32 && nnz > 0 && M >= kTcMinTokens && tc_rowblock_supported(a))
+  if (dtype != SLR_F32 && nnz > 0 && tc_worthwhile(a) && tc_rowblock_supported(a))
     return launch_tc_rowblock(a, false, s);
   if (dtype != SLR_F32 && nnz > 0 && mma_rowblock_supported(a.bp, a.bq, K, 0) && aligned16(values) &&
       aligned16(x) && aligned16(out))
@@ -331,13 +341,14 @@ int prepare_forward(const slr_layer* layer, const void* x, int64_t ldx, void* y,
 // schedule (it then beats the 1-SM kernel on B200) or when the caller asks
 // for it; it needs block_p 32 or 64 and M >= 256.
 bool use_pair(const slr_layer& L, const FwdCall& c) {
-  return c.p.path == 1 && ((L.flags & kFlagPairMma) || c.a.stage_plan != nullptr) && tc2_rowblock_supported(c.a);
+  return c.p.path == 1 && tc_worthwhile(c.a) && ((L.flags & kFlagPairMma) || c.a.stage_plan != nullptr) &&
+         tc2_rowblock_supported(c.a);
 }
 
 bool small_batch_path(const slr_layer& L, const FwdCall& c) {
   if (c.p.path != 1) return false;
   if (use_pair(L, c)) return false;
-  if (c.a.M >= kTcMinTokens && tc_rowblock_supported(c.a)) return false;
+  if (tc_worthwhile(c.a) && tc_rowblock_supported(c.a)) return false;
   return true;
 }
 
@@ -345,7 +356,7 @@ bool early_start(const slr_layer& L) { return (L.flags & kFlagStrict) == 0; }
 
 int run_lowrank(const slr_layer& L, const FwdCall& c, cudaStream_t s) {
   if (L.rank == 0 || c.a.M == 0) return SLR_OK;
-  if (c.p.path == 1 && c.a.M >= kTcMinTokens &&
+  if (c.p.path == 1 && !small_batch_path(L, c) &&
       tc_dense_supported(c.a.x, c.a.ldx, L.B, L.in_features, L.rank, L.dtype))
     return launch_tc_dense(c.a.x, c.a.ldx, L.B, c.ws, c.a.M, L.in_features, L.rank, c.p.ldh, L.dtype, s);
   if (c.p.path == 1)
@@ -361,7 +372,7 @@ int run_lowrank(const slr_layer& L, const FwdCall& c, cudaStream_t s) {
 int run_combine(const slr_layer& L, const FwdCall& c, bool pdl, cudaStream_t s) {
   if (c.a.M == 0) return SLR_OK;
   if (use_pair(L, c)) return launch_tc2_rowblock(c.a, pdl && L.rank > 0 && early_start(L), s);
-  if (c.p.path == 1 && c.a.M >= kTcMinTokens && tc_rowblock_supported(c.a))
+  if (c.p.path == 1 && tc_worthwhile(c.a) && tc_rowblock_supported(c.a))
     return launch_tc_rowblock(c.a, pdl && L.rank > 0 && early_start(L), s);
   if (c.p.path == 1) return launch_mma_rowblock(c.a, early_start(L), s);
   return launch_simt_rowblock(c.a, L.dtype == SLR_F32, s);
@@ -497,7 +508,7 @@ int prepare_group(const slr_layer* layers, int n, const void* x, int64_t ldx, vo
       // the small-batch kernel, which reads the grouped H all the same.
       a.y = gc.ws;
       a.ldy = L.out_features;
-      grouped = tc_rowblock_supported(a);
+      grouped = tc_worthwhile(a) && tc_rowblock_supported(a);
     }
   }
   gc.grouped = grouped;

@@ -275,7 +275,7 @@ def test_stage_schedule_equals_runtime_merge(cuda, shape):
     spec = random_layer(n, k, bp, bq, r, dens, seed=n + k)
     d = desc_for(spec.tensors("cpu", torch.bfloat16), spec, cuda, torch.bfloat16)
     assert d.struct.stage_plan
-    x = workloads.tokens(300, k, seed=9, dtype=torch.bfloat16).to(cuda)
+    x = workloads.tokens(2300, k, seed=9, dtype=torch.bfloat16).to(cuda)
     y_plan = d.forward(x)
     d.struct.stage_plan = None
     d.struct.stage_start = None
@@ -350,7 +350,7 @@ GROUPS = {
 
 
 @pytest.mark.parametrize("group", list(GROUPS))
-@pytest.mark.parametrize("T", [1, 64, 128, 300, 1000])
+@pytest.mark.parametrize("T", [1, 64, 128, 300, 2304])
 def test_group_forward_equals_per_layer(cuda, group, T):
     specs = [random_layer(n, k, bp, bq, r, dens, seed=17 * n + r + i) for i, (n, k, bp, bq, r, dens)
              in enumerate(GROUPS[group])]
@@ -515,7 +515,9 @@ TC_SHAPES = [
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("shape", TC_SHAPES, ids=lambda s: "x".join(map(str, s)))
-@pytest.mark.parametrize("T", [128, 129, 384, 1000])
+# 128 and 384 tokens of these narrow layers take the small-batch kernel (under
+# 16 tensor-core work items); 2049 and 2304 take the tensor-core kernels.
+@pytest.mark.parametrize("T", [128, 384, 2049, 2304])
 def test_tc_fused_matches_oracle(cuda, oracle, dtype, shape, T):
     n, k, bp, bq, r, dens, bias = shape
     spec = random_layer(n, k, bp, bq, r, dens, seed=n + k + r + T, bias=bias)
@@ -526,7 +528,7 @@ def test_tc_fused_matches_oracle(cuda, oracle, dtype, shape, T):
     assert_16bit_close(y, ref)
 
 
-@pytest.mark.parametrize("T", [128, 700])
+@pytest.mark.parametrize("T", [128, 2100])
 def test_tc_low_rank_only(cuda, oracle, T):
     spec = random_layer(256, 192, 16, 16, 64, 0.0, seed=11)
     t = spec.tensors("cpu", torch.bfloat16)
@@ -540,18 +542,19 @@ def test_tc_strided_input_and_output(cuda, oracle):
     """x and y as column slices of wider buffers (row strides != K, N)."""
     spec = random_layer(256, 256, 32, 32, 64, 0.3, seed=12)
     t = spec.tensors("cpu", torch.bfloat16)
-    x = workloads.tokens(300, 256, seed=1, dtype=torch.bfloat16)
+    T = 2100  # enough 128-token tiles for the tensor-core kernels
+    x = workloads.tokens(T, 256, seed=1, dtype=torch.bfloat16)
     ref = oracle_layer(oracle, t, x)
-    xw = torch.zeros(300, 320, dtype=torch.bfloat16, device=cuda)
+    xw = torch.zeros(T, 320, dtype=torch.bfloat16, device=cuda)
     xw[:, 32:288] = x.to(cuda)
-    yw = torch.full((300, 400), 5.0, dtype=torch.bfloat16, device=cuda)
+    yw = torch.full((T, 400), 5.0, dtype=torch.bfloat16, device=cuda)
     d = desc_for(t, spec, cuda, torch.bfloat16)
     d.forward(xw[:, 32:288], out=yw[:, 64:320])
     assert_16bit_close(yw[:, 64:320], ref)
     assert torch.all(yw[:, :64] == 5.0) and torch.all(yw[:, 320:] == 5.0)
 
 
-@pytest.mark.parametrize("M", [128, 300])
+@pytest.mark.parametrize("M", [128, 1100])
 def test_tc_addmm_leaves_empty_rows_untouched(cuda, oracle, M):
     spec = random_layer(512, 256, 64, 64, 8, 0.25, seed=M)
     assert (np.diff(spec.crow) == 0).any()
@@ -593,7 +596,7 @@ def test_device_status_is_clean(cuda):
 
 @pytest.mark.parametrize("shape", [(512, 512, 64, 64, 512, 0.2, True), (384, 512, 32, 32, 256, 0.3, False),
                                    (256, 512, 64, 128, 64, 0.5, True)], ids=lambda s: "x".join(map(str, s)))
-@pytest.mark.parametrize("T", [256, 700])
+@pytest.mark.parametrize("T", [2048, 2200])
 def test_pair_mma_kernel_matches_oracle(cuda, oracle, shape, T):
     """The opt-in 2-SM combine kernel (slr_layer.flags = SLR_FLAG_PAIR_MMA)."""
     n, k, bp, bq, r, dens, bias = shape
