@@ -356,7 +356,11 @@ bool early_start(const slr_layer& L) { return (L.flags & kFlagStrict) == 0; }
 
 int run_lowrank(const slr_layer& L, const FwdCall& c, cudaStream_t s) {
   if (L.rank == 0 || c.a.M == 0) return SLR_OK;
-  if (c.p.path == 1 && !small_batch_path(L, c) &&
+  // x*B^T on the tensor cores from 128 tokens on, whatever kernel the combine
+  // phase takes: the choice depends only on M, so a token slice (>= 128
+  // tokens) or a block-row shard of the layer computes H bit for bit as the
+  // whole layer does (the small-batch kernel splits K by M).
+  if (c.p.path == 1 && c.a.M >= kTcMinTokens &&
       tc_dense_supported(c.a.x, c.a.ldx, L.B, L.in_features, L.rank, L.dtype))
     return launch_tc_dense(c.a.x, c.a.ldx, L.B, c.ws, c.a.M, L.in_features, L.rank, c.p.ldh, L.dtype, s);
   if (c.p.path == 1)
