@@ -48,6 +48,13 @@ def emit(line: dict) -> None:
 
 
 METRIC = "S+LR linear tokens/s + %HBM/TC roofline at 1/2/4/8 B200 vs AVX2 CPU & cuBLAS"
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch of the
+# kernel the roofline covers, from one ncu capture of
+# `bench.py --ncu --workload <w> --steps 1 --warmup 3` on a B200 with
+# `--metrics dram__bytes_read.sum,dram__bytes_write.sum,gpu__time_duration.sum`:
+# cfg4 = mean over the 7 combine launches of one step; cfg3-T1 = the whole
+# layer set of one step (its roofline covers the graph-replayed layer set).
+NCU_TRAFFIC = {"cfg4": 101094327.0, "cfg3-T1": 51059200.0}
 L2_FLUSH_BYTES = 256 << 20  # > 126 MB L2
 
 
@@ -442,10 +449,7 @@ def main() -> None:
         peak = P["hbm_gbs"]
         roof = {"bound": "hbm", "unit": "GB/s", "algorithmic_per_step": comb_bytes,
                 "kernel": "combine (sparse + H*A^T + bias; one launch per projection)"}
-    traffic = None
-    tfile = REPO / "profiles" / "traffic.json"
-    if tfile.is_file():
-        traffic = json.loads(tfile.read_text()).get(args.workload)
+    traffic = NCU_TRAFFIC.get(args.workload)
     if tensor_bound:
         roof["step_tflops"] = (comb_flops + low_flops) * K / (total_ms / 1e3) / 1e12
     roof.update({"achieved": achieved, "peak": peak, "peak_source": pk_src,
