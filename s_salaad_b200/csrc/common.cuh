@@ -80,6 +80,12 @@ __device__ __forceinline__ void pdl_wait_primary() {
   asm volatile("griddepcontrol.wait;" ::: "memory");
 }
 
+// The k-th work item of worker p of P when the items, listed heaviest first,
+// are dealt in snake order (0..P-1, then P-1..0, ...): every round hands each
+// worker one item, and the worker that got the heaviest item of a round gets
+// the lightest of the next, which evens out the persistent schedule's tail.
+__device__ __forceinline__ int snake_item(int k, int p, int P) { return k * P + ((k & 1) ? P - 1 - p : p); }
+
 // --------------------------------------------------------- PTX: mbarrier ----
 
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {

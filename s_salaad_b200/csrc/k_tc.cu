@@ -182,7 +182,7 @@ __global__ void __launch_bounds__(kRowThreads, 1)
       const uint32_t* blk_idx = a.plan;  // records' second words index into the plan
       uint32_t g = 0;
       bool waited = false, abort_now = false;
-      for (int item = blockIdx.x; item < n_items && !abort_now; item += gridDim.x) {
+      for (int kr = 0, item = snake_item(0, blockIdx.x, gridDim.x); item < n_items && !abort_now; ++kr, item = snake_item(kr, blockIdx.x, gridDim.x)) {
         const int gi = item / a.n_mtiles, mt = item - gi * a.n_mtiles;
         const int r0 = gi * G;
         const int gcount = min(G, a.nrows - r0);
@@ -249,7 +249,7 @@ __global__ void __launch_bounds__(kRowThreads, 1)
     uint32_t g = 0;
     // warp-uniform view of the abort flag (the loops below use warp collectives)
     auto stop = [&]() { return __any_sync(0xffffffffu, s_abort != 0); };
-    for (int item = blockIdx.x; item < n_items && !stop(); item += gridDim.x) {
+    for (int kr = 0, item = snake_item(0, blockIdx.x, gridDim.x); item < n_items && !stop(); ++kr, item = snake_item(kr, blockIdx.x, gridDim.x)) {
       const int gi = item / a.n_mtiles, mt = item - gi * a.n_mtiles;
       const int r0 = gi * G;
       const int gcount = min(G, a.nrows - r0);
@@ -352,7 +352,7 @@ __global__ void __launch_bounds__(kRowThreads, 1)
     // ------------------------------------------------------- MMA issuer
     if (lane == 0) {
       uint32_t g = 0, it = 0;
-      for (int item = blockIdx.x; item < n_items && !s_abort; item += gridDim.x, ++it) {
+      for (int kr = 0, item = snake_item(0, blockIdx.x, gridDim.x); item < n_items && !s_abort; ++kr, item = snake_item(kr, blockIdx.x, gridDim.x), ++it) {
         const uint32_t buf = it & 1, tph = (it >> 1) & 1;
         if (!mbar_wait(&tempty[buf], tph ^ 1)) {
           tc_timeout(&s_abort);
@@ -408,7 +408,7 @@ __global__ void __launch_bounds__(kRowThreads, 1)
     TI* __restrict__ y = static_cast<TI*>(a.y);
     const TI* __restrict__ bias = static_cast<const TI*>(a.bias);
     uint32_t it = 0;
-    for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++it) {
+    for (int kr = 0, item = snake_item(0, blockIdx.x, gridDim.x); item < n_items; ++kr, item = snake_item(kr, blockIdx.x, gridDim.x), ++it) {
       const int gi = item / a.n_mtiles, mt = item - gi * a.n_mtiles;
       const int r0 = gi * G;
       const int gcount = min(G, a.nrows - r0);

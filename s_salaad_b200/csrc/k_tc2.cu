@@ -147,7 +147,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int pw = warp == 0 ? 0 : warp - 5;
       uint32_t g = 0;
       bool waited = false, abort_now = false;
-      for (int item = pair; item < n_items && !abort_now; item += npairs) {
+      for (int kr = 0, item = snake_item(0, pair, npairs); item < n_items && !abort_now; ++kr, item = snake_item(kr, pair, npairs)) {
         const int gi = item / a.n_mtiles, mt = item - gi * a.n_mtiles;
         const int r0 = gi * G;
         const int gcount = min(G, a.nrows - r0);
@@ -223,7 +223,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (warp == 0 && lane == 0) {
       bool waited = false;
       uint32_t g = 0;
-      for (int item = pair; item < n_items && !s_abort; item += npairs) {
+      for (int kr = 0, item = snake_item(0, pair, npairs); item < n_items && !s_abort; ++kr, item = snake_item(kr, pair, npairs)) {
         const int gi = item / a.n_mtiles, mt = item - gi * a.n_mtiles;
         const int r0 = gi * G;
         const int gcount = min(G, a.nrows - r0);
@@ -327,7 +327,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------ MMA issuer (leader)
     if (lane == 0 && leader) {
       uint32_t g = 0, it = 0;
-      for (int item = pair; item < n_items && !s_abort; item += npairs, ++it) {
+      for (int kr = 0, item = snake_item(0, pair, npairs); item < n_items && !s_abort; ++kr, item = snake_item(kr, pair, npairs), ++it) {
         const uint32_t buf = it & 1, tph = (it >> 1) & 1;
         if (!mbar_wait(&tempty[buf], tph ^ 1)) {
           timeout2(&s_abort);
@@ -381,7 +381,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const TI* __restrict__ bias = static_cast<const TI*>(a.bias);
     const uint32_t te0 = mapa(smem_u32(&tempty[0]), 0);
     uint32_t it = 0;
-    for (int item = pair; item < n_items; item += npairs, ++it) {
+    for (int kr = 0, item = snake_item(0, pair, npairs); item < n_items; ++kr, item = snake_item(kr, pair, npairs), ++it) {
       const int gi = item / a.n_mtiles, mt = item - gi * a.n_mtiles;
       const int r0 = gi * G;
       const int gcount = min(G, a.nrows - r0);
