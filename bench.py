@@ -55,6 +55,9 @@ METRIC = "S+LR linear tokens/s + %HBM/TC roofline at 1/2/4/8 B200 vs AVX2 CPU & 
 # cfg4 = mean over the 7 combine launches of one step; cfg3-T1 = the whole
 # layer set of one step (its roofline covers the graph-replayed layer set).
 NCU_TRAFFIC = {"cfg4": 101094327.0, "cfg3-T1": 51059200.0}
+# SMs kept free of the persistent kernels at N > 1 (for the overlapping NCCL
+# all-gathers); SLR_BENCH_NCCL_SMS overrides it.
+SMS_FOR_NCCL = int(os.environ.get("SLR_BENCH_NCCL_SMS", "16"))
 L2_FLUSH_BYTES = 256 << 20  # > 126 MB L2
 
 
@@ -294,6 +297,14 @@ def main() -> None:
     groups = {}
     if world == 1:
         groups = {r: ops.LayerGroup([layers[i] for i in idx]) for r, idx in members.items() if len(idx) > 1}
+    else:
+        # each rank's shards of q/k/v (gate/up) read the whole x and keep all of B: one grouped x*B^T,
+        # computed for this rank's 1/world of the tokens and all-gathered (a few MB)
+        groups = {r: ops.LayerGroup([layers[i].desc for i in idx]) for r, idx in members.items()
+                  if all(layers[i].desc is not None for i in idx)}
+        # leave SMs to the NCCL all-gathers that overlap the next projections' kernels
+        from s_salaad_b200 import _lib
+        _lib.load().slr_set_sm_limit(_lib.load_sm_count() - SMS_FOR_NCCL)
     ys = [torch.empty(T, s.out_features, dtype=dtype, device=dev) for s in specs]
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
@@ -301,23 +312,40 @@ def main() -> None:
     def step(ev=None):
         """One forward of the layer set; ev = per-projection event triples."""
         if world > 1:
-            handles = []
-            for i, L in enumerate(layers):
-                if L.desc is not None:
+            handles = {}
+            tp = T // world
+            for r, idx in members.items():
+                grp = groups.get(r)
+                if grp is not None:
                     if ev is not None:
+                        ev[idx[0]][0].record(stream)
+                    if world >= 4 and T % world == 0 and tp >= 128:
+                        h = grp.lowrank_rows(xs[idx[0]], rank * tp, tp)
+                        rb = tp * grp.h_row_bytes()
+                        dist.all_gather_into_tensor(h, h[rank * rb:(rank + 1) * rb])
+                    else:
+                        grp.lowrank(xs[idx[0]])
+                for j, i in enumerate(idx):
+                    L = layers[i]
+                    if L.desc is None:
+                        handles[i] = L.start(xs[i])
+                        continue
+                    if ev is not None and (grp is None or j):
                         ev[i][0].record(stream)
-                    L._lowrank(xs[i])
+                    if grp is None:
+                        L._lowrank(xs[i])
                     if ev is not None:
                         ev[i][1].record(stream)
                     buf = L.local_buffer(T)
-                    L.desc.combine(xs[i], buf[rank][:, :L.width])
+                    if grp is None:
+                        L.desc.combine(xs[i], buf[rank][:, :L.width])
+                    else:
+                        grp.combine(j, xs[i], buf[rank][:, :L.width])
                     if ev is not None:
                         ev[i][2].record(stream)
                     work = dist.all_gather_into_tensor(buf.view(-1), buf[rank].view(-1), group=L.group,
                                                        async_op=True)
-                    handles.append((work, buf))
-                else:
-                    handles.append(L.start(xs[i]))
+                    handles[i] = (work, buf)
             for i, L in enumerate(layers):
                 L.finish(handles[i], ys[i])
             return
@@ -355,10 +383,10 @@ def main() -> None:
 
     K = args.steps
     mk = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
-    # One GPU: the step is captured once and replayed from a CUDA graph, so
-    # host launch overhead (ctypes + tensor-map encoding, ~15 us per call) is
-    # not timed.  With NCCL in the step (N > 1) it runs eagerly.
-    use_graph = world == 1
+    # The step is captured once and replayed from a CUDA graph (NCCL
+    # collectives included at N > 1), so host launch overhead (ctypes +
+    # tensor-map encoding, ~15 us per call; ~30 us per NCCL call) is not timed.
+    use_graph = True
     graph = None
     if use_graph:
         side = torch.cuda.Stream(dev)
@@ -370,6 +398,8 @@ def main() -> None:
                 step()
         stream.wait_stream(side)
         torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
     step_ev = [(mk(), mk()) for _ in range(K)]
     kern_ev = [[(mk(), mk(), mk()) for _ in specs] for _ in range(K)]
     with ClockSampler(local) as clocks:
@@ -463,6 +493,8 @@ def main() -> None:
         if rank == 0:
             emit({"ncu_mode": True, "ms_per_step": total_ms / K, "roofline": roof})
         if world > 1:
+            del graph  # a graph holding NCCL calls must go before the process group
+            torch.cuda.synchronize()
             dist.destroy_process_group()
         return
     launches_per_step = sum((1 if s.rank > 0 else 0) + 1 for i, s in enumerate(specs) if has_local[i])
@@ -554,7 +586,10 @@ def main() -> None:
                 "scaling": "strong", "vs_baseline": None, "dtype": "bf16" if dtype == torch.bfloat16 else "f32",
                 "data": "synthetic (seeded generators; random-init weights; no dataset)",
                 "config": {**config, "l2": "flushed (256 MB write) between timed steps",
-                           "parallelism": f"block-row shards x{world} + NCCL all-gather" if world > 1 else "1 GPU",
+                           "parallelism": (f"block-row shards x{world}, x*B^T "
+                                           + ("split by tokens + NCCL all-gather of H" if world >= 4 else "on every rank")
+                                           + ", NCCL all-gather of y, step replayed from a CUDA graph")
+                           if world > 1 else "1 GPU, step replayed from a CUDA graph",
                            "algorithmic_tflop_per_step": all_flops / 1e12},
                 "roofline": roof, "e2e": {"value": e2e_val, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                                           "d2h_bytes_per_step": d2h},
@@ -562,6 +597,8 @@ def main() -> None:
                 "cpu_baseline": cpu, "cublas_dense": cublas}
         emit(line)
     if world > 1:
+        del graph  # a graph holding NCCL calls must go before the process group
+        torch.cuda.synchronize()
         dist.barrier()
         dist.destroy_process_group()
 

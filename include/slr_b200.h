@@ -83,6 +83,10 @@ SLR_API int slr_abi_version(void);
 SLR_API const char* slr_status_string(int status);
 /* Message of the last failing call on this thread ("" if none). */
 SLR_API const char* slr_last_error(void);
+/* Caps the SMs that the persistent tensor-core kernels fill (n <= 0: all),
+ * process-wide, e.g. to leave SMs to NCCL kernels that run alongside in a
+ * multi-GPU step.  No reference counterpart. */
+SLR_API int slr_set_sm_limit(int n);
 /* Reads and clears the device-side status word that bounded waits set when
  * they time out (SLR_OK or SLR_ERR_TIMEOUT).  Synchronises the device. */
 SLR_API int slr_device_status(int* status_out);
@@ -231,7 +235,11 @@ SLR_API int slr_lrs_linear_forward_noalloc(const slr_layer* layer, const void* x
  * called on one input by the reference: y[i] = x · S_iᵀ + (x · B_iᵀ) · A_iᵀ
  * + bias_i, the results of slr_lrs_linear_forward on each layer, bit for
  * bit.  With M >= 128 on the tensor-core path the x · B_iᵀ products are one
- * GEMM over the stacked B_i (x is read once, the GEMM has n times the tiles).
+ * GEMM over the stacked B_i (x is read once, the GEMM has n times the tiles)
+ * into H [M, sum of round_up(r_i, 64)] at the start of the workspace; that
+ * layout depends on M only, so _group_lowrank on tokens [t0, t0 + m) with the
+ * workspace advanced by t0 H rows fills exactly those rows of the H of all M
+ * tokens (a multi-GPU caller can split the tokens and all-gather H).
  * Layers must share in_features and dtype; ldy may be NULL (packed rows).
  * The workspace rules are those of slr_lrs_linear_forward.
  */

@@ -30,6 +30,7 @@ SLR_F32, SLR_F16, SLR_BF16 = 0, 1, 2
 # Every function the header declares, for the symbol test.
 EXPORTED = (
     "slr_abi_version",
+    "slr_set_sm_limit",
     "slr_status_string",
     "slr_last_error",
     "slr_device_status",
@@ -80,6 +81,7 @@ class SlrLayer(ctypes.Structure):
 
 _SIGS = {
     "slr_abi_version": ([], i32),
+    "slr_set_sm_limit": ([i32], i32),
     "slr_status_string": ([i32], ctypes.c_char_p),
     "slr_last_error": ([], ctypes.c_char_p),
     "slr_device_status": ([ctypes.POINTER(ctypes.c_int)], i32),
@@ -104,6 +106,13 @@ _SIGS = {
 
 _lock = threading.Lock()
 _lib: ctypes.CDLL | None = None
+
+
+def load_sm_count() -> int:
+    """Streaming multiprocessors of the current CUDA device."""
+    import torch
+
+    return torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
 
 
 def load(path: Path | str | None = None) -> ctypes.CDLL:

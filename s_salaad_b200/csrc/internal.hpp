@@ -56,6 +56,10 @@ bool mma_rowblock_supported(int bp, int bq, int64_t K, int64_t r);
 int launch_mma_rowblock(const RowblockArgs& a, bool pdl, cudaStream_t s);
 
 // ---- tcgen05 / TMEM kernels (16-bit dtypes): large token batches.
+// SMs the persistent kernels may fill: the device's count, or fewer after
+// slr_set_sm_limit (to leave SMs to collectives running alongside).
+int sm_budget();
+
 constexpr int64_t kTcMinTokens = 128;  // below this the mma.sync path is used
 constexpr int64_t kTileTokens = 128;   // token rows per tensor-core work item
 bool tc_rowblock_supported(const RowblockArgs& a);

@@ -456,16 +456,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-int num_sms() {
-  static int n = 0;
-  if (n == 0) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    if (n <= 0) n = 148;
-  }
-  return n;
-}
+int num_sms() { return sm_budget(); }
 
 template <int BP, int BQ, typename TI, int MODE>
 int launch_inst(const CUtensorMap& tx, const CUtensorMap& tv, const CUtensorMap& th, const CUtensorMap& ta,

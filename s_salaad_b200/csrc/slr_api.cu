@@ -4,6 +4,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstring>
 #include <mutex>
 #include <numeric>
@@ -65,6 +66,22 @@ int make_tmap_2d(CUtensorMap* map, const void* base, int dtype, uint64_t inner, 
     return fail(SLR_ERR_INVALID_ARGUMENT, "cuTensorMapEncodeTiled failed (code " + std::to_string(int(r)) +
                                               "): base/stride must be 16-byte aligned");
   return SLR_OK;
+}
+
+namespace {
+std::atomic<int> g_sm_limit{0};
+}  // namespace
+
+int sm_budget() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0, v = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    n = v > 0 ? v : 148;
+  }
+  const int lim = g_sm_limit.load(std::memory_order_relaxed);
+  return (lim > 0 && lim < n) ? std::max(lim, 2) : n;
 }
 
 }  // namespace slr
@@ -166,6 +183,11 @@ int check_layer(const slr_layer* L) {
 extern "C" {
 
 int slr_abi_version(void) { return SLR_ABI_VERSION; }
+
+int slr_set_sm_limit(int n) {
+  g_sm_limit.store(n > 0 ? n : 0, std::memory_order_relaxed);
+  return SLR_OK;
+}
 
 const char* slr_status_string(int status) {
   switch (status) {
@@ -286,7 +308,7 @@ struct FwdCall {
 };
 
 int prepare_forward(const slr_layer* layer, const void* x, int64_t ldx, void* y, int64_t ldy, int64_t M,
-                    void* workspace, size_t workspace_bytes, bool need_y, FwdCall& c) {
+                    void* workspace, size_t workspace_bytes, bool need_y, FwdCall& c, bool check_ws = true) {
   int rc = check_layer(layer);
   if (rc) return rc;
   const slr_layer& L = *layer;
@@ -299,7 +321,7 @@ int prepare_forward(const slr_layer* layer, const void* x, int64_t ldx, void* y,
   // Every 16-bit path keeps H as [M, ldh] in the I/O dtype, so the two phases
   // may pick different kernels; the path only depends on x, never on y.
   c.p = plan_forward(L, M, (ldx % 8 == 0) ? x : reinterpret_cast<const void*>(uintptr_t(1)));
-  if (c.p.total > 0 && M > 0) {
+  if (check_ws && c.p.total > 0 && M > 0) {
     if (!workspace) return fail(SLR_ERR_WORKSPACE, "workspace is NULL");
     if (workspace_bytes < c.p.total)
       return fail(SLR_ERR_WORKSPACE, "workspace too small: need " + std::to_string(c.p.total) + " bytes");
@@ -419,13 +441,14 @@ namespace {
 
 constexpr int kMaxGroup = 4;  // layers per grouped call (weight segments of one x*B^T GEMM)
 
-// Workspace of slr_lrs_linear_forward_group: the group's H [M, ldh_all]
-// (layer i owns columns [col[i], col[i] + round_up(r_i, 64))), then each
-// layer's own workspace, used when the call falls back to one forward per
-// layer.
+// Workspace of slr_lrs_linear_forward_group: either the group's H
+// [M, ldh_all] (layer i owns columns [col[i], col[i] + round_up(r_i, 64)))
+// when the call is grouped, or each layer's own workspace one after another
+// when it falls back to one forward per layer; the size covers both.
 struct GroupPlan {
   int64_t ldh_all = 0;
   int64_t col[kMaxGroup] = {};
+  size_t h_bytes = 0;
   size_t off[kMaxGroup] = {}, bytes[kMaxGroup] = {};
   size_t total = 0;
 };
@@ -439,20 +462,20 @@ int plan_group(const slr_layer* layers, int n, int64_t M, GroupPlan& g) {
     if (layers[i].in_features != layers[0].in_features || layers[i].dtype != layers[0].dtype)
       return fail(SLR_ERR_INVALID_ARGUMENT, "grouped layers must share in_features and dtype (they read one x)");
   }
-  size_t off = 0;
   if (M > 0) {
     for (int i = 0; i < n; ++i) {
       g.col[i] = g.ldh_all;
       g.ldh_all += round_up(layers[i].rank, 64);
     }
-    off = align256(size_t(M) * size_t(g.ldh_all) * dtype_size(layers[0].dtype));
+    g.h_bytes = align256(size_t(M) * size_t(g.ldh_all) * dtype_size(layers[0].dtype));
   }
+  size_t off = 0;
   for (int i = 0; i < n; ++i) {
     g.off[i] = off;
     g.bytes[i] = M > 0 ? plan_forward(layers[i], M, nullptr).total : 0;
     off += align256(g.bytes[i]);
   }
-  g.total = off;
+  g.total = std::max(g.h_bytes, off);
   return SLR_OK;
 }
 
@@ -485,35 +508,31 @@ int prepare_group(const slr_layer* layers, int n, const void* x, int64_t ldx, vo
   if (rc) return rc;
   if (M < 0) return fail(SLR_ERR_INVALID_ARGUMENT, "M must be >= 0");
   if (M == 0) return SLR_OK;
-  if (gc.g.total > 0) {
+  // One x*B^T GEMM for the whole group (a single layer included) whenever
+  // every layer's x*B^T runs on the tensor cores; otherwise the layers run one
+  // after another.  The layout depends on M only, so a call on a slice of the
+  // tokens writes its rows of the same H as a call on all of them, and every
+  // combine kernel reads H through a pointer and row stride.
+  bool grouped = M >= kTcMinTokens;
+  for (int i = 0; grouped && i < n; ++i) {
+    const slr_layer& L = layers[i];
+    const int64_t lx = ldx ? ldx : L.in_features;
+    grouped = plan_forward(L, M, (lx % 8 == 0) ? x : reinterpret_cast<const void*>(uintptr_t(1))).path == 1 &&
+              L.rank > 0 && tc_dense_supported(x, lx, L.B, L.in_features, L.rank, L.dtype);
+  }
+  const size_t need = grouped ? gc.g.h_bytes : gc.g.total;
+  if (need > 0) {
     if (!workspace) return fail(SLR_ERR_WORKSPACE, "workspace is NULL");
-    if (workspace_bytes < gc.g.total)
-      return fail(SLR_ERR_WORKSPACE, "workspace too small: need " + std::to_string(gc.g.total) + " bytes");
+    if (workspace_bytes < need)
+      return fail(SLR_ERR_WORKSPACE, "workspace too small: need " + std::to_string(need) + " bytes");
     if (reinterpret_cast<uintptr_t>(workspace) & 255u) return fail(SLR_ERR_WORKSPACE, "workspace must be 256-byte aligned");
   }
   gc.ws = static_cast<uint8_t*>(workspace);
   for (int i = 0; i < n; ++i) {
+    // grouped: the layers' own workspaces are not used (the combine reads the group H)
     rc = prepare_forward(&layers[i], x, ldx, y ? y[i] : nullptr, ldy ? ldy[i] : 0, M, gc.ws + gc.g.off[i],
-                         gc.g.bytes[i], y != nullptr, gc.c[i]);
+                         gc.g.bytes[i], y != nullptr, gc.c[i], !grouped);
     if (rc) return rc;
-  }
-  // One x*B^T GEMM for the whole group when every layer takes the
-  // tensor-core path; otherwise the layers run one after another.
-  bool grouped = n > 1 && M >= kTcMinTokens;
-  for (int i = 0; grouped && i < n; ++i) {
-    const slr_layer& L = layers[i];
-    grouped = gc.c[i].p.path == 1 && tc_dense_supported(x, gc.c[i].a.ldx, L.B, L.in_features, L.rank, L.dtype);
-    if (grouped) {
-      RowblockArgs a = gc.c[i].a;
-      a.H = gc.ws + size_t(gc.g.col[i]) * dtype_size(L.dtype);
-      a.ldh = gc.g.ldh_all;
-      // The layout may not depend on y (the x*B^T phase runs without it): check
-      // with an aligned stand-in; a combine whose real y is unaligned takes
-      // the small-batch kernel, which reads the grouped H all the same.
-      a.y = gc.ws;
-      a.ldy = L.out_features;
-      grouped = tc_worthwhile(a) && tc_rowblock_supported(a);
-    }
   }
   gc.grouped = grouped;
   if (grouped)

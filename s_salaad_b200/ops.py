@@ -283,6 +283,35 @@ class LayerGroup:
                 None if ws is None else ws.data_ptr(), 0 if ws is None else ws.numel(), _stream(self.device))
         _lib.check(rc, "lrs_linear_group_lowrank")
 
+    def h_row_bytes(self) -> int:
+        """Bytes of one token's row of the group's H (x2 @ [B_0; ...].T)."""
+        esize = torch.finfo(self.dtype).bits // 8
+        return sum((d.struct.rank + 63) // 64 * 64 for d in self.descs) * esize
+
+    def lowrank_rows(self, x2: torch.Tensor, row0: int, rows: int) -> torch.Tensor:
+        """Phase 1 for tokens [row0, row0 + rows) of x2 only, written into their
+        rows of the group H of all x2.shape[0] tokens (that layout depends on
+        the token count alone); returns the whole H region of the workspace as
+        bytes, e.g. for an all-gather of the other ranks' rows."""
+        M = x2.shape[0]
+        if row0 < 0 or rows <= 0 or row0 + rows > M:
+            raise ValueError("token rows out of range")
+        # the shared-H layout needs the tensor-core x*B^T for every layer and both token counts
+        if rows < 128 or self.dtype == torch.float32 or any(
+                d.struct.rank < 64 or d.in_features < 64 or d.in_features % 8 for d in self.descs):
+            raise ValueError("lowrank_rows needs >= 128 rows, 16-bit layers with rank >= 64 and K % 8 == 0")
+        ws = self.workspace(M)
+        off = row0 * self.h_row_bytes()
+        if off % 256:
+            raise ValueError("row0 * H row bytes must be a multiple of 256 (workspace alignment)")
+        xs = x2[row0:row0 + rows]
+        with _DeviceGuard(self.device):
+            rc = _lib.load().slr_lrs_linear_group_lowrank(
+                self._structs(), len(self.descs), xs.data_ptr(), LayerDesc._ld(x2), rows,
+                ws.data_ptr() + off, ws.numel() - off, _stream(self.device))
+        _lib.check(rc, "lrs_linear_group_lowrank")
+        return ws[:M * self.h_row_bytes()]
+
     def combine(self, i: int, x2: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
         """Phase 2 of layer i (after lowrank() on the same x2)."""
         M = x2.shape[0]

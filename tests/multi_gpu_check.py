@@ -48,6 +48,35 @@ def main() -> int:
         bad += 0 if ok else 1
         print(f"rank {rank}/{world} {cfg}[{idx}] T={T} bounds={sh.bounds.tolist()} max|diff|={err:.3e} "
               f"{'ok' if ok else 'MISMATCH'}", flush=True)
+    # q/k/v shards of cfg4 as one group per rank, x*B^T split by tokens + all-gather of H
+    T = 1024
+    specs = workloads.layer_set("cfg4")[:3]
+    x = workloads.tokens(T, specs[0].in_features, seed=5, device=dev, dtype=torch.bfloat16)
+    shards, refs = [], []
+    for s in specs:
+        t = s.tensors(dev, torch.bfloat16)
+        order = torch.from_numpy(ops.plan_row_order(s.crow.astype(np.int32))).to(dev)
+        full = ops.LayerDesc(A=t["A"], B=t["B"], bias=t["bias"], crow=t["S_crow"], col=t["S_col"],
+                             values=t["S_values"], row_order=order, in_features=s.in_features,
+                             out_features=s.out_features, block_p=s.block_p, block_q=s.block_q)
+        refs.append(full.forward(x))
+        shards.append(ShardedLayer(t, s.crow, in_features=s.in_features, out_features=s.out_features,
+                                   block_p=s.block_p, block_q=s.block_q, rank=rank, world=world))
+    grp = ops.LayerGroup([sh.desc for sh in shards])
+    tp = T // world
+    h = grp.lowrank_rows(x, rank * tp, tp)
+    rb = tp * grp.h_row_bytes()
+    dist.all_gather_into_tensor(h, h[rank * rb:(rank + 1) * rb])
+    for j, (sh, ref) in enumerate(zip(shards, refs)):
+        buf = sh.local_buffer(T)
+        grp.combine(j, x, buf[rank][:, :sh.width])
+        dist.all_gather_into_tensor(buf.view(-1), buf[rank].view(-1))
+        y = sh.finish((None, buf))
+        err = float((y.float() - ref.float()).abs().max())
+        ok = err == 0.0
+        bad += 0 if ok else 1
+        print(f"rank {rank}/{world} grouped split-H cfg4[{j}] T={T} max|diff|={err:.3e} "
+              f"{'ok' if ok else 'MISMATCH'}", flush=True)
     flag = torch.tensor([bad], device=dev)
     dist.all_reduce(flag)
     dist.barrier()

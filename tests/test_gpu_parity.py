@@ -363,6 +363,14 @@ def test_group_forward_equals_per_layer(cuda, group, T):
         ref = d.forward(x)
         assert torch.equal(y, ref)
         assert torch.equal(grp.combine(i, x, torch.empty_like(ref)), ref)
+    if T >= 256 and group != "mixed":
+        # H filled in two token slices (as two ranks would) gives the same outputs
+        half = T // 2
+        grp.workspace(T).zero_()
+        grp.lowrank_rows(x, 0, half)
+        grp.lowrank_rows(x, half, T - half)
+        for i, y in enumerate(ys):
+            assert torch.equal(grp.combine(i, x, torch.empty_like(y)), y)
 
 
 # -------------------------------------------------- full-size properties --

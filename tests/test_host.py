@@ -138,10 +138,12 @@ def test_group_call_validation_needs_no_gpu():
                                A=0x1000, B=0x2000, dtype=_lib.SLR_BF16)
     ys = (ctypes.c_void_p * 5)(*([0x3000] * 5))
     grp = lambda n, M=4: lib.slr_lrs_linear_forward_group(arr, n, 0x100, 0, ys, None, M, None, 0, None)  # noqa: E731
-    # size: H [M, 64 + 64] plus one workspace per layer, all 256-aligned
+    # size: the larger of H [M, 64 + 64] (grouped call) and one workspace per layer (fallback)
     one = lib.slr_lrs_linear_workspace_size(ctypes.byref(arr[0]), 4)
     two = lib.slr_lrs_linear_group_workspace_size(arr, 2, 4)
-    assert two >= 2 * one + 4 * 128 * 2 and two % 256 == 0
+    assert two == max(2 * one, 256) and two % 256 == 0
+    big = lib.slr_lrs_linear_group_workspace_size(arr, 2, 4096)
+    assert big >= 4096 * 128 * 2
     assert grp(2) == _lib.SLR_ERR_WORKSPACE
     assert grp(0) == _lib.SLR_ERR_INVALID_ARGUMENT
     assert grp(5) == _lib.SLR_ERR_INVALID_ARGUMENT
