@@ -42,6 +42,13 @@ sys.path.insert(0, str(REPO))
 _RESULT_FD = 1
 
 
+def small_kernel_shape(s) -> tuple[int, int]:
+    """Kernel instance of a layer's small-batch combine (x sub-tile width, rank
+    chunk): layers of a group that agree run as one launch below 128 tokens."""
+    bq = s.block_q if s.nnz > 0 else 16
+    return min(bq, 64), (64 if s.rank >= 64 else 32 if s.rank >= 32 else 16)
+
+
 def emit(line: dict) -> None:
     """Write the one JSON result line to the original stdout."""
     os.write(_RESULT_FD, (json.dumps(line) + "\n").encode())
@@ -498,9 +505,10 @@ def main() -> None:
             dist.destroy_process_group()
         return
     launches_per_step = sum((1 if s.rank > 0 else 0) + 1 for i, s in enumerate(specs) if has_local[i])
-    for r, grp in groups.items():  # one x*B^T launch per group (tensor-core path)
-        if T >= 128:
-            launches_per_step -= len(members[r]) - 1
+    for r, grp in groups.items():  # one x*B^T launch per group
+        launches_per_step -= len(members[r]) - 1
+        if T < 128 and world == 1 and len({small_kernel_shape(specs[i]) for i in members[r]}) == 1:
+            launches_per_step -= len(members[r]) - 1  # and one combine launch
 
     # ------------------------------------------------------------- e2e
     x_host = {r: xin[r].cpu().pin_memory() for r in xin}

@@ -234,12 +234,16 @@ SLR_API int slr_lrs_linear_forward_noalloc(const slr_layer* layer, const void* x
  * a decoder layer, each an _LRSLinearLRBlockCUDA (ls_linear.py:124-137)
  * called on one input by the reference: y[i] = x · S_iᵀ + (x · B_iᵀ) · A_iᵀ
  * + bias_i, the results of slr_lrs_linear_forward on each layer, bit for
- * bit.  With M >= 128 on the tensor-core path the x · B_iᵀ products are one
- * GEMM over the stacked B_i (x is read once, the GEMM has n times the tiles)
- * into H [M, sum of round_up(r_i, 64)] at the start of the workspace; that
- * layout depends on M only, so _group_lowrank on tokens [t0, t0 + m) with the
- * workspace advanced by t0 H rows fills exactly those rows of the H of all M
- * tokens (a multi-GPU caller can split the tokens and all-gather H).
+ * bit.  When every layer has a rank and takes a 16-bit path, the x · B_iᵀ
+ * products are one launch over the stacked B_i into H [M, sum of
+ * round_up(r_i, 64)] at the start of the workspace: a tensor-core GEMM from
+ * M >= 128 on (x is read once, the GEMM has n times the tiles), the
+ * small-batch kernel below (each B_i keeps its own K split, so H is the same
+ * bit for bit), where the combine of all layers is one launch too when their
+ * block and rank chunk shapes agree.  The M >= 128 layout depends on M only,
+ * so _group_lowrank on tokens [t0, t0 + m) (m >= 128) with the workspace
+ * advanced by t0 H rows fills exactly those rows of the H of all M tokens (a
+ * multi-GPU caller can split the tokens and all-gather H).
  * Layers must share in_features and dtype; ldy may be NULL (packed rows).
  * The workspace rules are those of slr_lrs_linear_forward.
  */

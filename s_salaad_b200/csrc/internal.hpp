@@ -39,21 +39,37 @@ int launch_simt_h(const void* x, int64_t ldx, const void* B, void* H, int64_t M,
 int launch_simt_rowblock(const RowblockArgs& a, bool h_f32, cudaStream_t s);
 
 // ---- mma.sync + TMA kernels (16-bit dtypes): small token batches.
+// Layers sharing one x that a grouped call runs as one launch.
+constexpr int kMaxGroupLayers = 4;
+
+// x·Bᵀ for 1..kMaxGroupLayers weight segments (one layer each) into one H
+// [M, ldh]: segment s owns the 16-row tiles [seg_rt[s], seg_rt[s + 1]) of H's
+// columns and splits K as it would alone.
 struct HSmallPlan {
   int tt = 8;        // tokens per CTA (8 * NT)
-  int rt = 0;        // 16-row tiles of r covering ldh
-  int ks = 1;        // K splits
-  int64_t kchunk = 0;
   int tc = 0;        // token chunks
+  int nseg = 0;
+  int rt = 0;        // 16-column tiles of H over all segments (ldh / 16)
+  int ks_max = 1;    // largest K split of a segment
+  int seg_rt[kMaxGroupLayers + 1] = {};
+  int ks[kMaxGroupLayers] = {};
+  int64_t kchunk[kMaxGroupLayers] = {};
   size_t part_floats = 0;
   size_t counters = 0;
 };
-HSmallPlan plan_h_small(int64_t M, int64_t K, int64_t ldh);
-int launch_h_small(const void* x, int64_t ldx, const void* B, void* H, float* part, unsigned* counters,
-                   int64_t M, int64_t K, int64_t r, int64_t ldh, const HSmallPlan& plan,
-                   int dtype, bool pdl, cudaStream_t s);
+// ldh[s]: columns of H owned by segment s (a multiple of 16, >= r_s).
+HSmallPlan plan_h_small(int64_t M, int64_t K, const int64_t* ldh, int nseg);
+int launch_h_small(const void* x, int64_t ldx, const void* const* B, const int64_t* r, void* H, float* part,
+                   unsigned* counters, int64_t M, int64_t K, int64_t ldh, const HSmallPlan& plan, int dtype,
+                   bool pdl, cudaStream_t s);
 bool mma_rowblock_supported(int bp, int bq, int64_t K, int64_t r);
 int launch_mma_rowblock(const RowblockArgs& a, bool pdl, cudaStream_t s);
+// Layers that read one x and one H [M, ldh] (layer i's columns from h_col[i])
+// in one launch; false from mma_group_compatible when their shapes need
+// different kernel instances.
+bool mma_group_compatible(const RowblockArgs* a, int n);
+int launch_mma_rowblock_group(const RowblockArgs* a, const int64_t* h_col, int n, const void* H, int64_t ldh,
+                              bool pdl, cudaStream_t s);
 
 // ---- tcgen05 / TMEM kernels (16-bit dtypes): large token batches.
 // SMs the persistent kernels may fill: the device's count, or fewer after

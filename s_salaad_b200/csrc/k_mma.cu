@@ -35,17 +35,33 @@ constexpr int kFT = 16;  // output features per CTA (one m16 tile)
 // (1024-aligned for its swizzle).
 constexpr uint32_t kHOff = 2048;
 
-struct MmaArgs {
+constexpr int kMaxLayers = kMaxGroupLayers;  // layers (sharing x) per launch
+
+// One layer of a launch; its CTAs are [cta0, cta0 + nrows * ft_per_row).
+struct MmaLayer {
   void* y;
   const void* bias;
   const int32_t* crow;
   const int32_t* col;
   const int32_t* rows;
-  int64_t M, N, ldy;
+  int64_t N, ldy;
   int bp, bq, r, kc;   // kc: rank chunk per low-rank stage
   int sb;              // value blocks per sparse stage
   int ft_per_row;      // bp / 16
   int nrows;
+  int cta0;
+  int h_col0;          // first column of this layer's H in the shared H
+};
+struct MmaArgs {
+  int64_t M;
+  int n;
+  MmaLayer L[kMaxLayers];
+};
+// Tensor maps: x and H are shared by the layers of a launch (H column
+// offsets per layer), values and A are per layer.
+struct MmaMaps {
+  CUtensorMap x, h;
+  CUtensorMap v[kMaxLayers], a[kMaxLayers];
 };
 
 __device__ __forceinline__ uint32_t ld_u32(const void* p) {
@@ -70,11 +86,20 @@ __device__ __forceinline__ void ldsm_x2(uint32_t addr, uint32_t& r0, uint32_t& r
 // stages go to shared memory, those of later stages to L2, bias to shared
 // memory -- so a decode step streams its weights while the previous kernel
 // finishes.  x, H and y are read or written only after the wait.
+//
+// Several layers that read the same x (q/k/v, gate/up) run in one launch:
+// the grid is the concatenation of their CTA ranges.
 template <int NT, int KX, typename TI, int MODE>
 __global__ void __launch_bounds__(kThreads)
-    mma_rowblock_kernel(const __grid_constant__ CUtensorMap tm_vals, const __grid_constant__ CUtensorMap tm_x,
-                        const __grid_constant__ CUtensorMap tm_A, const __grid_constant__ CUtensorMap tm_h,
-                        const MmaArgs a) {
+    mma_rowblock_kernel(const __grid_constant__ MmaMaps maps, const __grid_constant__ MmaArgs ga) {
+  int li = 0;
+  while (li + 1 < ga.n && int(blockIdx.x) >= ga.L[li + 1].cta0) ++li;
+  const MmaLayer& a = ga.L[li];
+  const CUtensorMap& tm_vals = maps.v[li];
+  const CUtensorMap& tm_A = maps.a[li];
+  const CUtensorMap& tm_x = maps.x;
+  const CUtensorMap& tm_h = maps.h;
+  const int cta = int(blockIdx.x) - a.cta0;
   constexpr int TT = 8 * NT;                 // tokens per CTA
   constexpr int XB = TT * KX * 2;            // one x sub-tile (tokens x KX columns)
   constexpr int RWX = KX * 2;                // x tile row bytes (its TMA swizzle width)
@@ -96,8 +121,8 @@ __global__ void __launch_bounds__(kThreads)
 
   pdl_launch_dependents();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int ri = blockIdx.x / a.ft_per_row;
-  const int f0 = (blockIdx.x - ri * a.ft_per_row) * kFT;  // feature offset inside the block
+  const int ri = cta / a.ft_per_row;
+  const int f0 = (cta - ri * a.ft_per_row) * kFT;  // feature offset inside the block
   const int br = a.rows ? a.rows[ri] : ri;
   const int64_t t0 = int64_t(blockIdx.y) * TT;
   const int jb0 = a.crow ? a.crow[br] : 0;
@@ -176,7 +201,7 @@ __global__ void __launch_bounds__(kThreads)
               tma_load_2d(dst + v_slot + (lane * nsub + h) * XB, &tm_x, colr[s] * a.bq + h * KX, int(t0),
                           &full[s]);
         } else if (lane == 0) {
-          tma_load_2d(dst + kHOff, &tm_h, (s - n_sp) * a.kc, int(t0), &full[s]);
+          tma_load_2d(dst + kHOff, &tm_h, a.h_col0 + (s - n_sp) * a.kc, int(t0), &full[s]);
         }
       }
     }
@@ -210,7 +235,7 @@ __global__ void __launch_bounds__(kThreads)
         const int l = s - n_sp;
         mbar_arrive_expect_tx(&full[slot], lr_bytes);
         tma_load_2d(dst, &tm_A, l * a.kc, br * a.bp + f0, &full[slot]);
-        tma_load_2d(dst + kHOff, &tm_h, l * a.kc, int(t0), &full[slot]);
+        tma_load_2d(dst + kHOff, &tm_h, a.h_col0 + l * a.kc, int(t0), &full[slot]);
       }
     }
   } else {
@@ -286,7 +311,7 @@ __global__ void __launch_bounds__(kThreads)
   for (int idx = threadIdx.x; idx < kFT * TT; idx += kThreads) {
     const int n = idx % kFT, t = idx / kFT;
     const int64_t tok = t0 + t;
-    if (tok >= a.M) continue;
+    if (tok >= ga.M) continue;
     float v = 0.f;
 #pragma unroll
     for (int w = 0; w < kConsumerWarps; ++w) v += red[(w * kFT + n) * TT + t];
@@ -302,14 +327,22 @@ __global__ void __launch_bounds__(kThreads)
 
 // ------------------------------------------------------------ h_small --
 
+// H[M, ldh] = x · [B_0; ...]ᵀ: row tiles [seg_rt[s], seg_rt[s+1]) of H come
+// from the r_s rows of B_s (segments of one x, e.g. q/k/v).  Each segment
+// keeps the K split (ks[s] chunks of kchunk[s]) it would get alone, so a
+// grouped call computes every layer's H bit for bit as a call on that layer.
 struct HArgs {
   const void* x;
-  const void* B;
+  const void* B[kMaxLayers];
   void* H;
-  float* part;
-  unsigned* counters;
-  int64_t M, K, ldx, kchunk;
-  int r, ldh, ks, rt;
+  float* part;        // [rt * tc][ks_max][16][TT] split-K partials
+  unsigned* counters; // [rt * tc]
+  int64_t M, K, ldx;
+  int64_t kchunk[kMaxLayers];
+  int r[kMaxLayers];
+  int ks[kMaxLayers];
+  int seg_rt[kMaxLayers + 1];
+  int nseg, ldh, ks_max, rt;
 };
 
 __device__ __forceinline__ uint4 ldg_u128(const void* p) {
@@ -321,7 +354,7 @@ __device__ __forceinline__ uint4 ldg_u128(const void* p) {
 // and feeds them to two m16n8k16 MMAs; both operands use the same k order
 // inside the slice, which leaves the dot product unchanged.
 template <int NT, typename TI>
-__global__ void __launch_bounds__(128) h_small_kernel(const HArgs a) {
+__global__ void __launch_bounds__(128) h_small_kernel(const __grid_constant__ HArgs a) {
   pdl_launch_dependents();
   constexpr int TT = 8 * NT;
   __shared__ float red[4][16][TT];
@@ -329,15 +362,20 @@ __global__ void __launch_bounds__(128) h_small_kernel(const HArgs a) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, tig = lane & 3;
   const int rt = blockIdx.x, ks = blockIdx.y, tc = blockIdx.z;
+  int sg = 0;
+  while (sg + 1 < a.nseg && rt >= a.seg_rt[sg + 1]) ++sg;
+  const int nks = a.ks[sg];
+  if (ks >= nks) return;  // this segment splits K into fewer chunks
   const int rho0 = 16 * rt;
   const int64_t t0 = int64_t(tc) * TT;
-  const int64_t kb = int64_t(ks) * a.kchunk;
-  const int64_t ke = min(a.K, kb + a.kchunk);
+  const int64_t kb = int64_t(ks) * a.kchunk[sg];
+  const int64_t ke = min(a.K, kb + a.kchunk[sg]);
   const TI* __restrict__ x = static_cast<const TI*>(a.x);
-  const TI* __restrict__ B = static_cast<const TI*>(a.B);
-  const bool v0 = rho0 + g < a.r, v1 = rho0 + g + 8 < a.r;
-  const TI* B0 = B + int64_t(rho0 + g) * a.K;
-  const TI* B1 = B + int64_t(rho0 + g + 8) * a.K;
+  const TI* __restrict__ B = static_cast<const TI*>(a.B[sg]);
+  const int lrow = 16 * (rt - a.seg_rt[sg]);  // first row of this tile within B_sg
+  const bool v0 = lrow + g < a.r[sg], v1 = lrow + g + 8 < a.r[sg];
+  const TI* B0 = B + int64_t(lrow + g) * a.K;
+  const TI* B1 = B + int64_t(lrow + g + 8) * a.K;
 
   float acc[NT][4];
 #pragma unroll
@@ -388,7 +426,7 @@ __global__ void __launch_bounds__(128) h_small_kernel(const HArgs a) {
   __syncthreads();
 
   TI* __restrict__ H = static_cast<TI*>(a.H);
-  if (a.ks == 1) {
+  if (nks == 1) {
     for (int idx = threadIdx.x; idx < 16 * TT; idx += 128) {
       const int m = idx % 16, t = idx / 16;
       const float v = ((red[0][m][t] + red[1][m][t]) + red[2][m][t]) + red[3][m][t];
@@ -398,7 +436,7 @@ __global__ void __launch_bounds__(128) h_small_kernel(const HArgs a) {
   }
   // Split-K: publish this CTA's partial, the last CTA of the tile reduces.
   const int tile = tc * a.rt + rt;
-  float* part = a.part + size_t(tile) * a.ks * 16 * TT;
+  float* part = a.part + size_t(tile) * a.ks_max * 16 * TT;
   for (int idx = threadIdx.x; idx < 16 * TT; idx += 128) {
     const int m = idx % 16, t = idx / 16;
     part[size_t(ks) * 16 * TT + idx] = ((red[0][m][t] + red[1][m][t]) + red[2][m][t]) + red[3][m][t];
@@ -407,7 +445,7 @@ __global__ void __launch_bounds__(128) h_small_kernel(const HArgs a) {
   __syncthreads();
   if (threadIdx.x == 0) {
     const unsigned prev = atomicAdd(&a.counters[tile], 1u);
-    s_last = prev == unsigned(a.ks - 1);
+    s_last = prev == unsigned(nks - 1);
   }
   __syncthreads();
   if (!s_last) return;
@@ -415,7 +453,7 @@ __global__ void __launch_bounds__(128) h_small_kernel(const HArgs a) {
   for (int idx = threadIdx.x; idx < 16 * TT; idx += 128) {
     const int m = idx % 16, t = idx / 16;
     float v = 0.f;
-    for (int k = 0; k < a.ks; ++k) v += __ldcg(part + size_t(k) * 16 * TT + idx);
+    for (int k = 0; k < nks; ++k) v += __ldcg(part + size_t(k) * 16 * TT + idx);
     if (t0 + t < a.M) H[(t0 + t) * a.ldh + rho0 + m] = from_f<TI>(v);
   }
   if (threadIdx.x == 0) a.counters[tile] = 0u;  // ready for the next call
@@ -476,8 +514,7 @@ MmaShape mma_shape(int bq, int r, int tt) {
 }
 
 template <int NT, int KX, typename TI, int MODE>
-int launch_inst(const CUtensorMap& tv, const CUtensorMap& tx, const CUtensorMap& ta, const CUtensorMap& th,
-                const MmaArgs& k, size_t smem, dim3 grid, bool pdl, cudaStream_t s) {
+int launch_inst(const MmaMaps& maps, const MmaArgs& k, size_t smem, dim3 grid, bool pdl, cudaStream_t s) {
   auto kern = mma_rowblock_kernel<NT, KX, TI, MODE>;
   SLR_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
   cudaLaunchConfig_t cfg = {};
@@ -490,56 +527,144 @@ int launch_inst(const CUtensorMap& tv, const CUtensorMap& tx, const CUtensorMap&
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  SLR_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kern, tv, tx, ta, th, k));
+  SLR_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kern, maps, k));
   return SLR_OK;
 }
 
 template <int KX, typename TI, int MODE>
-int launch_nt(int tt, const CUtensorMap& tv, const CUtensorMap& tx, const CUtensorMap& ta,
-              const CUtensorMap& th, const MmaArgs& k, size_t smem, dim3 grid, bool pdl, cudaStream_t s) {
+int launch_nt(int tt, const MmaMaps& maps, const MmaArgs& k, size_t smem, dim3 grid, bool pdl, cudaStream_t s) {
   switch (tt) {
-    case 8: return launch_inst<1, KX, TI, MODE>(tv, tx, ta, th, k, smem, grid, pdl, s);
-    case 16: return launch_inst<2, KX, TI, MODE>(tv, tx, ta, th, k, smem, grid, pdl, s);
-    case 32: return launch_inst<4, KX, TI, MODE>(tv, tx, ta, th, k, smem, grid, pdl, s);
-    default: return launch_inst<8, KX, TI, MODE>(tv, tx, ta, th, k, smem, grid, pdl, s);
+    case 8: return launch_inst<1, KX, TI, MODE>(maps, k, smem, grid, pdl, s);
+    case 16: return launch_inst<2, KX, TI, MODE>(maps, k, smem, grid, pdl, s);
+    case 32: return launch_inst<4, KX, TI, MODE>(maps, k, smem, grid, pdl, s);
+    default: return launch_inst<8, KX, TI, MODE>(maps, k, smem, grid, pdl, s);
   }
 }
 
 template <typename TI, int MODE>
-int launch_kx(int kx, int tt, const CUtensorMap& tv, const CUtensorMap& tx, const CUtensorMap& ta,
-              const CUtensorMap& th, const MmaArgs& k, size_t smem, dim3 grid, bool pdl, cudaStream_t s) {
+int launch_kx(int kx, int tt, const MmaMaps& maps, const MmaArgs& k, size_t smem, dim3 grid, bool pdl,
+              cudaStream_t s) {
   switch (kx) {
-    case 16: return launch_nt<16, TI, MODE>(tt, tv, tx, ta, th, k, smem, grid, pdl, s);
-    case 32: return launch_nt<32, TI, MODE>(tt, tv, tx, ta, th, k, smem, grid, pdl, s);
-    default: return launch_nt<64, TI, MODE>(tt, tv, tx, ta, th, k, smem, grid, pdl, s);
+    case 16: return launch_nt<16, TI, MODE>(tt, maps, k, smem, grid, pdl, s);
+    case 32: return launch_nt<32, TI, MODE>(tt, maps, k, smem, grid, pdl, s);
+    default: return launch_nt<64, TI, MODE>(tt, maps, k, smem, grid, pdl, s);
   }
+}
+
+bool is_sparse(const RowblockArgs& a) { return a.crow != nullptr && a.nnz > 0; }
+int eff_bq(const RowblockArgs& a) { return is_sparse(a) ? a.bq : 16; }
+
+// Layer `a` as entry li of a launch: its MmaLayer (CTAs from cta0) and its
+// value / A tensor maps.  Returns the layer's dynamic shared memory in *smem.
+int fill_layer(const RowblockArgs& a, int tt, int cta0, int64_t h_col, MmaMaps& maps, MmaArgs& k, int li,
+               size_t* smem) {
+  const bool sparse = is_sparse(a);
+  const int bq = eff_bq(a);
+  const int r = a.mode == MODE_FUSED ? int(a.r) : 0;
+  const MmaShape sh = mma_shape(bq, r, tt);
+  MmaLayer& L = k.L[li];
+  L = MmaLayer{a.y, a.bias, sparse ? a.crow : nullptr, a.col, a.rows, a.N, a.ldy,
+               a.bp, bq, r, sh.kc, sh.sb, a.bp / kFT, int(a.nrows), cta0, int(h_col)};
+  *smem = sh.smem;
+  int rc;
+  if (sparse) {
+    rc = make_tmap_2d(&maps.v[li], a.values, a.dtype, uint64_t(a.bp), uint64_t(a.nnz) * a.bq,
+                      uint64_t(a.bp) * 2, uint32_t(kFT), uint32_t(sh.sb * a.bq));
+    if (rc) return rc;
+  }
+  if (r > 0) {
+    rc = make_tmap_2d(&maps.a[li], a.A, a.dtype, uint64_t(a.r), uint64_t(a.N), uint64_t(a.r) * 2,
+                      uint32_t(sh.kc), uint32_t(kFT));
+    if (rc) return rc;
+  }
+  return SLR_OK;
+}
+
+// x map (box: tt tokens x kx columns) and H map (box: tt x kc; kc is 16, 32
+// or 64 and the same box serves every layer of a launch only when their kc
+// agree, which mma_group_compatible checks).
+int fill_shared_maps(const RowblockArgs& a0, int tt, int kx, int kc, bool any_sparse, const void* H, int64_t ldh,
+                     MmaMaps& maps) {
+  int rc;
+  if (any_sparse) {
+    rc = make_tmap_2d(&maps.x, a0.x, a0.dtype, uint64_t(a0.K), uint64_t(a0.M), uint64_t(a0.ldx) * 2,
+                      uint32_t(kx), uint32_t(tt));
+    if (rc) return rc;
+  }
+  if (kc > 0) {
+    rc = make_tmap_2d(&maps.h, H, a0.dtype, uint64_t(ldh), uint64_t(a0.M), uint64_t(ldh) * 2, uint32_t(kc),
+                      uint32_t(tt));
+    if (rc) return rc;
+  }
+  return SLR_OK;
+}
+
+int launch_maps(const RowblockArgs& a0, int kx, int tt, const MmaMaps& maps, const MmaArgs& k, size_t smem,
+                int ctas, bool pdl, cudaStream_t s) {
+  const dim3 grid(unsigned(ctas), unsigned(ceil_div(a0.M, tt)));
+  if (a0.dtype == SLR_BF16)
+    return a0.mode == MODE_ADDMM ? launch_kx<__nv_bfloat16, MODE_ADDMM>(kx, tt, maps, k, smem, grid, pdl, s)
+                                 : launch_kx<__nv_bfloat16, MODE_FUSED>(kx, tt, maps, k, smem, grid, pdl, s);
+  if (a0.dtype == SLR_F16)
+    return a0.mode == MODE_ADDMM ? launch_kx<__half, MODE_ADDMM>(kx, tt, maps, k, smem, grid, pdl, s)
+                                 : launch_kx<__half, MODE_FUSED>(kx, tt, maps, k, smem, grid, pdl, s);
+  return fail(SLR_ERR_UNSUPPORTED_DTYPE, "mma path: 16-bit dtypes only");
 }
 
 }  // namespace
 
-HSmallPlan plan_h_small(int64_t M, int64_t K, int64_t ldh) {
+HSmallPlan plan_h_small(int64_t M, int64_t K, const int64_t* ldh, int nseg) {
   HSmallPlan p;
   p.tt = pick_tt(M);
-  p.rt = int(ldh / 16);
   p.tc = int(ceil_div(std::max<int64_t>(M, 1), p.tt));
-  const int64_t base = int64_t(p.rt) * p.tc;
-  const int64_t want = std::max<int64_t>(1, ceil_div(2 * 148, std::max<int64_t>(base, 1)));
+  p.nseg = nseg;
   const int64_t max_split = std::max<int64_t>(1, ceil_div(K, 128));
-  const int64_t ks = std::min(want, max_split);
-  p.kchunk = round_up(ceil_div(K, ks), 128);
-  p.ks = int(ceil_div(K, p.kchunk));
-  if (p.ks < 1) p.ks = 1;
-  p.part_floats = p.ks > 1 ? size_t(base) * p.ks * 16 * p.tt : 0;
-  p.counters = p.ks > 1 ? size_t(base) : 0;
+  for (int sg = 0; sg < nseg; ++sg) {
+    const int rt = int(ldh[sg] / 16);
+    p.seg_rt[sg] = p.rt;
+    p.rt += rt;
+    // about two CTAs per SM for this segment alone
+    const int64_t base = int64_t(rt) * p.tc;
+    const int64_t want = std::max<int64_t>(1, ceil_div(2 * 148, std::max<int64_t>(base, 1)));
+    const int64_t ks = std::min(want, max_split);
+    p.kchunk[sg] = round_up(ceil_div(K, ks), 128);
+    p.ks[sg] = std::max(1, int(ceil_div(K, p.kchunk[sg])));
+    p.ks_max = std::max(p.ks_max, p.ks[sg]);
+  }
+  p.seg_rt[nseg] = p.rt;
+  const size_t tiles = size_t(p.rt) * p.tc;
+  p.part_floats = p.ks_max > 1 ? tiles * p.ks_max * 16 * p.tt : 0;
+  p.counters = p.ks_max > 1 ? tiles : 0;
   return p;
 }
 
-int launch_h_small(const void* x, int64_t ldx, const void* B, void* H, float* part, unsigned* counters,
-                   int64_t M, int64_t K, int64_t r, int64_t ldh, const HSmallPlan& plan,
-                   int dtype, bool pdl, cudaStream_t s) {
-  if (M <= 0 || ldh <= 0) return SLR_OK;
-  HArgs a{x, B, H, part, counters, M, K, ldx, plan.kchunk, int(r), int(ldh), plan.ks, plan.rt};
-  const dim3 grid(unsigned(plan.rt), unsigned(plan.ks), unsigned(plan.tc));
+int launch_h_small(const void* x, int64_t ldx, const void* const* B, const int64_t* r, void* H, float* part,
+                   unsigned* counters, int64_t M, int64_t K, int64_t ldh, const HSmallPlan& plan, int dtype,
+                   bool pdl, cudaStream_t s) {
+  if (M <= 0 || plan.rt <= 0) return SLR_OK;
+  if (plan.nseg < 1 || plan.nseg > kMaxLayers || int64_t(plan.rt) * 16 > ldh)
+    return fail(SLR_ERR_INVALID_ARGUMENT, "h_small: bad segment plan");
+  HArgs a{};
+  a.x = x;
+  a.H = H;
+  a.part = part;
+  a.counters = counters;
+  a.M = M;
+  a.K = K;
+  a.ldx = ldx;
+  a.nseg = plan.nseg;
+  a.ldh = int(ldh);
+  a.ks_max = plan.ks_max;
+  a.rt = plan.rt;
+  for (int sg = 0; sg < plan.nseg; ++sg) {
+    a.B[sg] = B[sg];
+    a.r[sg] = int(r[sg]);
+    a.ks[sg] = plan.ks[sg];
+    a.kchunk[sg] = plan.kchunk[sg];
+    a.seg_rt[sg] = plan.seg_rt[sg];
+  }
+  a.seg_rt[plan.nseg] = plan.seg_rt[plan.nseg];
+  const dim3 grid(unsigned(plan.rt), unsigned(plan.ks_max), unsigned(plan.tc));
   if (dtype == SLR_BF16) return launch_h_small_t<__nv_bfloat16>(a, plan.tt, grid, pdl, s);
   if (dtype == SLR_F16) return launch_h_small_t<__half>(a, plan.tt, grid, pdl, s);
   return fail(SLR_ERR_UNSUPPORTED_DTYPE, "h_small: 16-bit dtypes only");
@@ -557,39 +682,60 @@ int launch_mma_rowblock(const RowblockArgs& a, bool pdl, cudaStream_t s) {
   if (a.nrows <= 0 || a.M <= 0) return SLR_OK;
   if (a.ldx % 8 != 0 || !aligned16(a.x)) return fail(SLR_ERR_UNSUPPORTED, "mma path: x must be 16-byte aligned");
   const int tt = pick_tt(a.M);
-  const bool sparse = a.crow != nullptr && a.nnz > 0;
-  const int bq = sparse ? a.bq : 16;
   const int r = a.mode == MODE_FUSED ? int(a.r) : 0;
-  const MmaShape sh = mma_shape(bq, r, tt);
-  MmaArgs k{a.y, a.bias, sparse ? a.crow : nullptr, a.col, a.rows, a.M, a.N, a.ldy,
-            a.bp, bq, r, sh.kc, sh.sb, a.bp / kFT, int(a.nrows)};
-  CUtensorMap tv{}, tx{}, ta{}, th{};
-  int rc;
-  if (sparse) {
-    rc = make_tmap_2d(&tv, a.values, a.dtype, uint64_t(a.bp), uint64_t(a.nnz) * a.bq, uint64_t(a.bp) * 2,
-                      uint32_t(kFT), uint32_t(sh.sb * a.bq));
-    if (rc) return rc;
-    rc = make_tmap_2d(&tx, a.x, a.dtype, uint64_t(a.K), uint64_t(a.M), uint64_t(a.ldx) * 2, uint32_t(sh.kx),
-                      uint32_t(tt));
-    if (rc) return rc;
+  const MmaShape sh = mma_shape(eff_bq(a), r, tt);
+  MmaMaps maps{};
+  MmaArgs k{};
+  k.M = a.M;
+  k.n = 1;
+  size_t smem = 0;
+  int rc = fill_layer(a, tt, 0, 0, maps, k, 0, &smem);
+  if (rc) return rc;
+  rc = fill_shared_maps(a, tt, sh.kx, r > 0 ? sh.kc : 0, is_sparse(a), a.H, a.ldh, maps);
+  if (rc) return rc;
+  return launch_maps(a, sh.kx, tt, maps, k, smem, int(a.nrows * (a.bp / kFT)), pdl, s);
+}
+
+bool mma_group_compatible(const RowblockArgs* a, int n) {
+  if (n < 1 || n > kMaxLayers) return false;
+  const int tt = pick_tt(a[0].M);
+  const MmaShape s0 = mma_shape(eff_bq(a[0]), a[0].mode == MODE_FUSED ? int(a[0].r) : 0, tt);
+  for (int i = 0; i < n; ++i) {
+    if (a[i].M != a[0].M || a[i].x != a[0].x || a[i].ldx != a[0].ldx || a[i].K != a[0].K ||
+        a[i].dtype != a[0].dtype || a[i].mode != MODE_FUSED || a[i].r <= 0)
+      return false;
+    const MmaShape si = mma_shape(eff_bq(a[i]), int(a[i].r), tt);
+    if (si.kx != s0.kx || si.kc != s0.kc) return false;
   }
-  if (r > 0) {
-    rc = make_tmap_2d(&ta, a.A, a.dtype, uint64_t(a.r), uint64_t(a.N), uint64_t(a.r) * 2, uint32_t(sh.kc),
-                      uint32_t(kFT));
+  return true;
+}
+
+int launch_mma_rowblock_group(const RowblockArgs* a, const int64_t* h_col, int n, const void* H, int64_t ldh,
+                              bool pdl, cudaStream_t s) {
+  if (!mma_group_compatible(a, n)) return fail(SLR_ERR_INVALID_ARGUMENT, "mma group: layers need one kernel shape");
+  if (a[0].M <= 0) return SLR_OK;
+  if (a[0].ldx % 8 != 0 || !aligned16(a[0].x)) return fail(SLR_ERR_UNSUPPORTED, "mma path: x must be 16-byte aligned");
+  const int tt = pick_tt(a[0].M);
+  const MmaShape sh = mma_shape(eff_bq(a[0]), int(a[0].r), tt);
+  MmaMaps maps{};
+  MmaArgs k{};
+  k.M = a[0].M;
+  k.n = n;
+  size_t smem = 0;
+  int ctas = 0;
+  bool any_sparse = false;
+  for (int i = 0; i < n; ++i) {
+    size_t si = 0;
+    int rc = fill_layer(a[i], tt, ctas, h_col[i], maps, k, i, &si);
     if (rc) return rc;
-    rc = make_tmap_2d(&th, a.H, a.dtype, uint64_t(a.ldh), uint64_t(a.M), uint64_t(a.ldh) * 2, uint32_t(sh.kc),
-                      uint32_t(tt));
-    if (rc) return rc;
+    smem = std::max(smem, si);
+    ctas += int(a[i].nrows * (a[i].bp / kFT));
+    any_sparse = any_sparse || is_sparse(a[i]);
   }
-  const dim3 grid(unsigned(a.nrows * (a.bp / kFT)), unsigned(ceil_div(a.M, tt)));
-  if (a.dtype == SLR_BF16)
-    return a.mode == MODE_ADDMM
-               ? launch_kx<__nv_bfloat16, MODE_ADDMM>(sh.kx, tt, tv, tx, ta, th, k, sh.smem, grid, pdl, s)
-               : launch_kx<__nv_bfloat16, MODE_FUSED>(sh.kx, tt, tv, tx, ta, th, k, sh.smem, grid, pdl, s);
-  if (a.dtype == SLR_F16)
-    return a.mode == MODE_ADDMM ? launch_kx<__half, MODE_ADDMM>(sh.kx, tt, tv, tx, ta, th, k, sh.smem, grid, pdl, s)
-                                : launch_kx<__half, MODE_FUSED>(sh.kx, tt, tv, tx, ta, th, k, sh.smem, grid, pdl, s);
-  return fail(SLR_ERR_UNSUPPORTED_DTYPE, "mma path: 16-bit dtypes only");
+  int rc = fill_shared_maps(a[0], tt, sh.kx, sh.kc, any_sparse, H, ldh, maps);
+  if (rc) return rc;
+  if (ctas == 0) return SLR_OK;
+  return launch_maps(a[0], sh.kx, tt, maps, k, smem, ctas, pdl, s);
 }
 
 int read_and_clear_status_mma(unsigned* out) {

@@ -40,7 +40,7 @@ using namespace tc;
 __device__ unsigned g_status_tc = 0;
 
 constexpr int kThreads = 192;        // tc_dense_kernel
-constexpr int kMaxSeg = 4;           // weight matrices per grouped x*B^T
+constexpr int kMaxSeg = kMaxGroupLayers;  // weight matrices per grouped x*B^T
 constexpr int kRowThreads = 288;     // tc_rowblock_kernel: warps 0, 6, 7, 8 load operands
 constexpr int kProd2 = 6;            // first of the extra TMA warps
 constexpr int kProducers = 4;        // TMA warps working from a column schedule

@@ -136,7 +136,7 @@ FwdPlan plan_forward(const slr_layer& L, int64_t M, const void* x) {
   p.h_bytes = align256(size_t(std::max<int64_t>(M, 0)) * p.ldh * hes);
   p.part_off = p.h_bytes;
   if (p.path == 1 && L.rank > 0) {
-    p.hs = plan_h_small(M, L.in_features, p.ldh);
+    p.hs = plan_h_small(M, L.in_features, &p.ldh, 1);
     p.part_bytes = align256(p.hs.part_floats * sizeof(float));
     p.cnt_bytes = align256(p.hs.counters * sizeof(unsigned));
   }
@@ -305,6 +305,8 @@ struct FwdCall {
   FwdPlan p;
   RowblockArgs a;
   uint8_t* ws = nullptr;
+  float* part = nullptr;        // h_small split-K partials
+  unsigned* counters = nullptr; // h_small tile counters (zero between calls)
 };
 
 int prepare_forward(const slr_layer* layer, const void* x, int64_t ldx, void* y, int64_t ldy, int64_t M,
@@ -328,6 +330,8 @@ int prepare_forward(const slr_layer* layer, const void* x, int64_t ldx, void* y,
     if (reinterpret_cast<uintptr_t>(workspace) & 255u) return fail(SLR_ERR_WORKSPACE, "workspace must be 256-byte aligned");
   }
   c.ws = static_cast<uint8_t*>(workspace);
+  c.part = reinterpret_cast<float*>(c.ws + c.p.part_off);
+  c.counters = reinterpret_cast<unsigned*>(c.ws + c.p.cnt_off);
   RowblockArgs& a = c.a;
   a.x = x;
   a.y = y;
@@ -385,10 +389,12 @@ int run_lowrank(const slr_layer& L, const FwdCall& c, cudaStream_t s) {
   if (c.p.path == 1 && c.a.M >= kTcMinTokens &&
       tc_dense_supported(c.a.x, c.a.ldx, L.B, L.in_features, L.rank, L.dtype))
     return launch_tc_dense(c.a.x, c.a.ldx, L.B, c.ws, c.a.M, L.in_features, L.rank, c.p.ldh, L.dtype, s);
-  if (c.p.path == 1)
-    return launch_h_small(c.a.x, c.a.ldx, L.B, c.ws, reinterpret_cast<float*>(c.ws + c.p.part_off),
-                          reinterpret_cast<unsigned*>(c.ws + c.p.cnt_off), c.a.M, L.in_features, L.rank, c.p.ldh,
-                          c.p.hs, L.dtype, early_start(L) && small_batch_path(L, c), s);
+  if (c.p.path == 1) {
+    const void* B = L.B;
+    const int64_t r = L.rank;
+    return launch_h_small(c.a.x, c.a.ldx, &B, &r, c.ws, c.part, c.counters, c.a.M, L.in_features, c.p.ldh, c.p.hs,
+                          L.dtype, early_start(L) && small_batch_path(L, c), s);
+  }
   return launch_simt_h(c.a.x, c.a.ldx, L.B, c.ws, c.a.M, L.in_features, L.rank, c.p.ldh, L.dtype,
                        L.dtype == SLR_F32, s);
 }
@@ -439,17 +445,27 @@ int slr_lrs_linear_combine(const slr_layer* layer, const void* x, int64_t ldx, v
 
 namespace {
 
-constexpr int kMaxGroup = 4;  // layers per grouped call (weight segments of one x*B^T GEMM)
+constexpr int kMaxGroup = kMaxGroupLayers;  // layers per grouped call
 
-// Workspace of slr_lrs_linear_forward_group: either the group's H
-// [M, ldh_all] (layer i owns columns [col[i], col[i] + round_up(r_i, 64)))
-// when the call is grouped, or each layer's own workspace one after another
-// when it falls back to one forward per layer; the size covers both.
+// Workspace of slr_lrs_linear_forward_group, in one of three layouts chosen
+// by M (and the layers' paths):
+//   TC    (M >= 128): the group's H [M, ldh_all] (layer i owns columns
+//         [col[i], col[i] + round_up(r_i, 64))), written by one tensor-core GEMM;
+//   SMALL (M < 128): the same H, then the split-K partials of one grouped
+//         small-batch x*B^T;
+//   EACH: each layer's own workspace one after another (one forward per layer).
+// The h_small tile counters of SMALL and EACH live in a region after all of
+// them that no layout writes otherwise: they must stay zero between calls, and
+// a call in one layout must not clobber the counters of another.
 struct GroupPlan {
   int64_t ldh_all = 0;
   int64_t col[kMaxGroup] = {};
   size_t h_bytes = 0;
+  HSmallPlan hs;                  // SMALL: all layers as segments of one x*B^T
+  size_t small_part_bytes = 0;    // at h_bytes
   size_t off[kMaxGroup] = {}, bytes[kMaxGroup] = {};
+  size_t cnt_base = 0;
+  size_t cnt_each[kMaxGroup] = {};  // EACH: layer i's counters at cnt_base + cnt_each[i]
   size_t total = 0;
 };
 
@@ -462,20 +478,31 @@ int plan_group(const slr_layer* layers, int n, int64_t M, GroupPlan& g) {
     if (layers[i].in_features != layers[0].in_features || layers[i].dtype != layers[0].dtype)
       return fail(SLR_ERR_INVALID_ARGUMENT, "grouped layers must share in_features and dtype (they read one x)");
   }
-  if (M > 0) {
-    for (int i = 0; i < n; ++i) {
-      g.col[i] = g.ldh_all;
-      g.ldh_all += round_up(layers[i].rank, 64);
-    }
-    g.h_bytes = align256(size_t(M) * size_t(g.ldh_all) * dtype_size(layers[0].dtype));
-  }
-  size_t off = 0;
+  if (M <= 0) return SLR_OK;
+  int64_t ldh[kMaxGroup];
   for (int i = 0; i < n; ++i) {
-    g.off[i] = off;
-    g.bytes[i] = M > 0 ? plan_forward(layers[i], M, nullptr).total : 0;
-    off += align256(g.bytes[i]);
+    ldh[i] = round_up(layers[i].rank, 64);
+    g.col[i] = g.ldh_all;
+    g.ldh_all += ldh[i];
   }
-  g.total = std::max(g.h_bytes, off);
+  g.h_bytes = align256(size_t(M) * size_t(g.ldh_all) * dtype_size(layers[0].dtype));
+  size_t cnt_small = 0;
+  if (M < kTcMinTokens && layers[0].dtype != SLR_F32) {
+    g.hs = plan_h_small(M, layers[0].in_features, ldh, n);
+    g.small_part_bytes = align256(g.hs.part_floats * sizeof(float));
+    cnt_small = align256(g.hs.counters * sizeof(unsigned));
+  }
+  size_t off = 0, cnt = 0;
+  for (int i = 0; i < n; ++i) {
+    const FwdPlan p = plan_forward(layers[i], M, nullptr);
+    g.off[i] = off;
+    g.bytes[i] = p.total;
+    off += align256(p.total);
+    g.cnt_each[i] = cnt;
+    cnt += p.cnt_bytes;
+  }
+  g.cnt_base = std::max(g.h_bytes + g.small_part_bytes, off);
+  g.total = g.cnt_base + std::max(cnt, cnt_small);
   return SLR_OK;
 }
 
@@ -493,12 +520,14 @@ size_t slr_lrs_linear_group_workspace_size(const slr_layer* layers, int n, int64
 
 namespace {
 
-// Argument checks, per-layer packing and the grouped/per-layer decision of
-// the group entry points.  y may be NULL (x*B^T phase only).
+// Argument checks, per-layer packing and the layout decision of the group
+// entry points.  y may be NULL (x*B^T phase only).
+enum GroupMode { GROUP_EACH = 0, GROUP_TC = 1, GROUP_SMALL = 2 };
+
 struct GroupCall {
   GroupPlan g;
   FwdCall c[kMaxGroup];
-  bool grouped = false;
+  int mode = GROUP_EACH;
   uint8_t* ws = nullptr;
 };
 
@@ -508,19 +537,22 @@ int prepare_group(const slr_layer* layers, int n, const void* x, int64_t ldx, vo
   if (rc) return rc;
   if (M < 0) return fail(SLR_ERR_INVALID_ARGUMENT, "M must be >= 0");
   if (M == 0) return SLR_OK;
-  // One x*B^T GEMM for the whole group (a single layer included) whenever
-  // every layer's x*B^T runs on the tensor cores; otherwise the layers run one
-  // after another.  The layout depends on M only, so a call on a slice of the
-  // tokens writes its rows of the same H as a call on all of them, and every
-  // combine kernel reads H through a pointer and row stride.
-  bool grouped = M >= kTcMinTokens;
-  for (int i = 0; grouped && i < n; ++i) {
+  // One x*B^T launch for the whole group (a single layer included) whenever
+  // every layer has a rank and takes the 16-bit path: the tensor-core GEMM
+  // from 128 tokens on, the small-batch kernel below.  The layout depends on
+  // M only, so a call on a slice of the tokens writes its rows of the same H
+  // as a call on all of them, and every combine kernel reads H through a
+  // pointer and row stride.
+  int mode = M >= kTcMinTokens ? GROUP_TC : GROUP_SMALL;
+  for (int i = 0; mode != GROUP_EACH && i < n; ++i) {
     const slr_layer& L = layers[i];
     const int64_t lx = ldx ? ldx : L.in_features;
-    grouped = plan_forward(L, M, (lx % 8 == 0) ? x : reinterpret_cast<const void*>(uintptr_t(1))).path == 1 &&
-              L.rank > 0 && tc_dense_supported(x, lx, L.B, L.in_features, L.rank, L.dtype);
+    const bool p16 = plan_forward(L, M, (lx % 8 == 0) ? x : reinterpret_cast<const void*>(uintptr_t(1))).path == 1;
+    if (!p16 || L.rank <= 0 ||
+        (mode == GROUP_TC && !tc_dense_supported(x, lx, L.B, L.in_features, L.rank, L.dtype)))
+      mode = GROUP_EACH;
   }
-  const size_t need = grouped ? gc.g.h_bytes : gc.g.total;
+  const size_t need = mode == GROUP_TC ? gc.g.h_bytes : gc.g.total;
   if (need > 0) {
     if (!workspace) return fail(SLR_ERR_WORKSPACE, "workspace is NULL");
     if (workspace_bytes < need)
@@ -529,13 +561,14 @@ int prepare_group(const slr_layer* layers, int n, const void* x, int64_t ldx, vo
   }
   gc.ws = static_cast<uint8_t*>(workspace);
   for (int i = 0; i < n; ++i) {
-    // grouped: the layers' own workspaces are not used (the combine reads the group H)
+    // shared-H layouts: the layers' own workspaces are not used (the combine reads the group H)
     rc = prepare_forward(&layers[i], x, ldx, y ? y[i] : nullptr, ldy ? ldy[i] : 0, M, gc.ws + gc.g.off[i],
-                         gc.g.bytes[i], y != nullptr, gc.c[i], !grouped);
+                         gc.g.bytes[i], y != nullptr, gc.c[i], mode == GROUP_EACH);
     if (rc) return rc;
+    gc.c[i].counters = reinterpret_cast<unsigned*>(gc.ws + gc.g.cnt_base + gc.g.cnt_each[i]);
   }
-  gc.grouped = grouped;
-  if (grouped)
+  gc.mode = mode;
+  if (mode != GROUP_EACH)
     for (int i = 0; i < n; ++i) {
       gc.c[i].a.H = gc.ws + size_t(gc.g.col[i]) * dtype_size(layers[i].dtype);
       gc.c[i].a.ldh = gc.g.ldh_all;
@@ -543,8 +576,14 @@ int prepare_group(const slr_layer* layers, int n, const void* x, int64_t ldx, vo
   return SLR_OK;
 }
 
+bool group_early_start(const slr_layer* layers, int n) {
+  for (int i = 0; i < n; ++i)
+    if (!early_start(layers[i])) return false;
+  return true;
+}
+
 int group_lowrank(const slr_layer* layers, int n, const GroupCall& gc, cudaStream_t s) {
-  if (!gc.grouped) {
+  if (gc.mode == GROUP_EACH) {
     for (int i = 0; i < n; ++i) {
       int rc = run_lowrank(layers[i], gc.c[i], s);
       if (rc) return rc;
@@ -557,8 +596,29 @@ int group_lowrank(const slr_layer* layers, int n, const GroupCall& gc, cudaStrea
     Bs[i] = layers[i].B;
     rs[i] = layers[i].rank;
   }
-  return launch_tc_dense_group(gc.c[0].a.x, gc.c[0].a.ldx, Bs, rs, n, gc.ws, gc.c[0].a.M, layers[0].in_features,
-                               gc.g.ldh_all, layers[0].dtype, s);
+  const RowblockArgs& a0 = gc.c[0].a;
+  if (gc.mode == GROUP_TC)
+    return launch_tc_dense_group(a0.x, a0.ldx, Bs, rs, n, gc.ws, a0.M, layers[0].in_features, gc.g.ldh_all,
+                                 layers[0].dtype, s);
+  return launch_h_small(a0.x, a0.ldx, Bs, rs, gc.ws, reinterpret_cast<float*>(gc.ws + gc.g.h_bytes),
+                        reinterpret_cast<unsigned*>(gc.ws + gc.g.cnt_base), a0.M, layers[0].in_features,
+                        gc.g.ldh_all, gc.g.hs, layers[0].dtype, group_early_start(layers, n), s);
+}
+
+// Combine phase of every layer: one small-batch launch over all of them when
+// their kernel shapes agree, else one launch per layer.
+int group_combine_all(const slr_layer* layers, int n, const GroupCall& gc, cudaStream_t s) {
+  if (gc.mode == GROUP_SMALL) {
+    RowblockArgs as[kMaxGroup];
+    for (int i = 0; i < n; ++i) as[i] = gc.c[i].a;
+    if (mma_group_compatible(as, n))
+      return launch_mma_rowblock_group(as, gc.g.col, n, gc.ws, gc.g.ldh_all, group_early_start(layers, n), s);
+  }
+  for (int i = 0; i < n; ++i) {
+    int rc = run_combine(layers[i], gc.c[i], true, s);
+    if (rc) return rc;
+  }
+  return SLR_OK;
 }
 
 }  // namespace
@@ -573,7 +633,7 @@ int slr_lrs_linear_forward_group(const slr_layer* layers, int n, const void* x, 
   int rc = prepare_group(layers, n, x, ldx, y, ldy, M, workspace, workspace_bytes, gc);
   if (rc || M == 0) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (!gc.grouped) {
+  if (gc.mode == GROUP_EACH) {
     for (int i = 0; i < n; ++i) {
       rc = run_lowrank(layers[i], gc.c[i], s);
       if (rc) return rc;
@@ -583,8 +643,8 @@ int slr_lrs_linear_forward_group(const slr_layer* layers, int n, const void* x, 
     return SLR_OK;
   }
   rc = group_lowrank(layers, n, gc, s);
-  for (int i = 0; rc == SLR_OK && i < n; ++i) rc = run_combine(layers[i], gc.c[i], true, s);
-  return rc;
+  if (rc) return rc;
+  return group_combine_all(layers, n, gc, s);
 }
 
 int slr_lrs_linear_group_lowrank(const slr_layer* layers, int n, const void* x, int64_t ldx, int64_t M,
@@ -603,10 +663,12 @@ int slr_lrs_linear_group_combine(const slr_layer* layers, int n, int i, const vo
   int rc = prepare_group(layers, n, x, ldx, nullptr, nullptr, M, workspace, workspace_bytes, gc);
   if (rc || M == 0) return rc;
   FwdCall c = gc.c[i];
-  rc = prepare_forward(&layers[i], x, ldx, y, ldy, M, gc.ws + gc.g.off[i], gc.g.bytes[i], true, c);
+  rc = prepare_forward(&layers[i], x, ldx, y, ldy, M, gc.ws + gc.g.off[i], gc.g.bytes[i], true, c,
+                       gc.mode == GROUP_EACH);
   if (rc) return rc;
   c.a.H = gc.c[i].a.H;
   c.a.ldh = gc.c[i].a.ldh;
+  c.counters = gc.c[i].counters;
   return run_combine(layers[i], c, false, static_cast<cudaStream_t>(stream));
 }
 

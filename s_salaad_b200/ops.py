@@ -230,8 +230,10 @@ class LayerGroup:
     """Layers that read the same input (q/k/v, gate/up): one grouped call.
 
     ``forward(x)`` returns each layer's ``y`` exactly as
-    :meth:`LayerDesc.forward` would; for 128 or more tokens the ``x · Bᵀ``
-    products run as one GEMM over the stacked ``B`` matrices.
+    :meth:`LayerDesc.forward` would; the ``x · Bᵀ`` products run as one
+    launch over the stacked ``B`` matrices (a tensor-core GEMM from 128 tokens
+    on) and, below 128 tokens, the combine phases of all layers as one launch
+    when their block shapes allow.
     """
 
     def __init__(self, descs: list[LayerDesc]):

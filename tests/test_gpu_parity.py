@@ -344,7 +344,8 @@ GROUPS = {
     "qkv": [(512, 512, 32, 32, 64, 0.3), (256, 512, 32, 32, 64, 0.3), (256, 512, 32, 32, 128, 0.25)],
     # gate/up-like with 64x64 blocks
     "gateup": [(1024, 512, 64, 64, 128, 0.2), (1024, 512, 64, 64, 128, 0.2)],
-    # a low-rank-only layer and a layer without bias or rank >= 64: falls back per layer
+    # a low-rank-only layer and a layer without bias or rank >= 64: per layer
+    # from 128 tokens on; below, one x*B^T launch and one combine per layer
     "mixed": [(512, 512, 16, 16, 64, 0.0), (256, 512, 16, 16, 32, 0.1)],
 }
 
@@ -363,6 +364,16 @@ def test_group_forward_equals_per_layer(cuda, group, T):
         ref = d.forward(x)
         assert torch.equal(y, ref)
         assert torch.equal(grp.combine(i, x, torch.empty_like(ref)), ref)
+    if T < 128:
+        # a call in the per-layer layout (x rows not 16-byte aligned: SIMT
+        # path) leaves the split-K counters of the grouped layout intact
+        wide = torch.zeros(T, specs[0].in_features + 1, dtype=x.dtype, device=cuda)
+        wide[:, :-1] = x
+        xo = wide[:, :-1]
+        for d, y in zip(descs, grp.forward(xo)):
+            assert torch.equal(y, d.forward(xo))
+        for y, z in zip(ys, grp.forward(x)):
+            assert torch.equal(y, z)
     if T >= 256 and group != "mixed":
         # H filled in two token slices (as two ranks would) gives the same outputs
         half = T // 2
