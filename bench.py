@@ -65,6 +65,9 @@ NCU_TRAFFIC = {"cfg4": 101094327.0, "cfg3-T1": 51059200.0}
 # SMs kept free of the persistent kernels at N > 1 (for the overlapping NCCL
 # all-gathers); SLR_BENCH_NCCL_SMS overrides it.
 SMS_FOR_NCCL = int(os.environ.get("SLR_BENCH_NCCL_SMS", "16"))
+# N > 1: combine epilogues store y straight into every rank's y (peer memory)
+# when every rank's kernels support it; 0 = NCCL all-gather of y instead
+USE_PEERS = os.environ.get("SLR_BENCH_PEERS", "1") != "0"
 L2_FLUSH_BYTES = 256 << 20  # > 126 MB L2
 
 
@@ -264,7 +267,7 @@ def main() -> None:
     import torch.distributed as dist
 
     from s_salaad_b200 import ops
-    from s_salaad_b200.shard import ShardedLayer
+    from s_salaad_b200.shard import PeerOutputs, ShardedLayer, all_ranks
 
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
@@ -309,10 +312,15 @@ def main() -> None:
         # computed for this rank's 1/world of the tokens and all-gathered (a few MB)
         groups = {r: ops.LayerGroup([layers[i].desc for i in idx]) for r, idx in members.items()
                   if all(layers[i].desc is not None for i in idx)}
+    pos = None
+    if world > 1 and USE_PEERS and all_ranks(all(L.peers_supported(xs[i]) for i, L in enumerate(layers)), dev):
+        pos = [PeerOutputs(L, T, dtype, dev) for L in layers]
+    elif world > 1:
         # leave SMs to the NCCL all-gathers that overlap the next projections' kernels
         from s_salaad_b200 import _lib
         _lib.load().slr_set_sm_limit(_lib.load_sm_count() - SMS_FOR_NCCL)
-    ys = [torch.empty(T, s.out_features, dtype=dtype, device=dev) for s in specs]
+    ys = ([po.y for po in pos] if pos is not None else
+          [torch.empty(T, s.out_features, dtype=dtype, device=dev) for s in specs])
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
 
@@ -334,6 +342,23 @@ def main() -> None:
                         grp.lowrank(xs[idx[0]])
                 for j, i in enumerate(idx):
                     L = layers[i]
+                    if pos is not None:
+                        # y tiles go straight into every rank's y; the waits end the step
+                        if L.desc is None:
+                            continue
+                        if ev is not None and (grp is None or j):
+                            ev[i][0].record(stream)
+                        if grp is None:
+                            L._lowrank(xs[i])
+                        if ev is not None:
+                            ev[i][1].record(stream)
+                        if grp is None:
+                            L.start_peers_combine(xs[i], pos[i])
+                        else:
+                            grp.combine_peers(j, xs[i], pos[i])
+                        if ev is not None:
+                            ev[i][2].record(stream)
+                        continue
                     if L.desc is None:
                         handles[i] = L.start(xs[i])
                         continue
@@ -354,7 +379,10 @@ def main() -> None:
                                                        async_op=True)
                     handles[i] = (work, buf)
             for i, L in enumerate(layers):
-                L.finish(handles[i], ys[i])
+                if pos is not None:
+                    L.finish_peers(pos[i])
+                else:
+                    L.finish(handles[i], ys[i])
             return
         for r, idx in members.items():
             grp = groups.get(r)
@@ -502,11 +530,16 @@ def main() -> None:
         if world > 1:
             del graph  # a graph holding NCCL calls must go before the process group
             torch.cuda.synchronize()
+            dist.barrier()
+            for po in pos or []:
+                po.close()
             dist.destroy_process_group()
         return
     launches_per_step = sum((1 if s.rank > 0 else 0) + 1 for i, s in enumerate(specs) if has_local[i])
     for r, grp in groups.items():  # one x*B^T launch per group
         launches_per_step -= len(members[r]) - 1
+    if pos is not None:
+        launches_per_step += len(specs)  # the wait that ends each projection's call
         if T < 128 and world == 1 and len({small_kernel_shape(specs[i]) for i in members[r]}) == 1:
             launches_per_step -= len(members[r]) - 1  # and one combine launch
 
@@ -518,6 +551,15 @@ def main() -> None:
     d2h = sum(v.numel() * v.element_size() for v in y_host) if rank == 0 else 0
 
     def e2e_step():
+        if world > 1:
+            # the timed step itself (shards, H exchange, y assembly), fed from host memory
+            for r in xin:
+                xin[r].copy_(x_host[r], non_blocking=True)
+            step()
+            if rank == 0:
+                for i in range(len(specs)):
+                    y_host[i].copy_(ys[i], non_blocking=True)
+            return
         for r in xin:
             xin_dev[r].copy_(x_host[r], non_blocking=True)
         for r, idx in members.items():
@@ -596,7 +638,9 @@ def main() -> None:
                 "config": {**config, "l2": "flushed (256 MB write) between timed steps",
                            "parallelism": (f"block-row shards x{world}, x*B^T "
                                            + ("split by tokens + NCCL all-gather of H" if world >= 4 else "on every rank")
-                                           + ", NCCL all-gather of y, step replayed from a CUDA graph")
+                                           + (", combine epilogues store y into every rank's y over NVLink (CUDA IPC)"
+                                              if pos is not None else ", NCCL all-gather of y")
+                                           + ", step replayed from a CUDA graph")
                            if world > 1 else "1 GPU, step replayed from a CUDA graph",
                            "algorithmic_tflop_per_step": all_flops / 1e12},
                 "roofline": roof, "e2e": {"value": e2e_val, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
@@ -608,6 +652,8 @@ def main() -> None:
         del graph  # a graph holding NCCL calls must go before the process group
         torch.cuda.synchronize()
         dist.barrier()
+        for po in pos or []:
+            po.close()
         dist.destroy_process_group()
 
 

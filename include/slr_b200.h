@@ -36,7 +36,7 @@
 extern "C" {
 #endif
 
-#define SLR_ABI_VERSION 2
+#define SLR_ABI_VERSION 3
 
 #if defined(__GNUC__)
 #define SLR_API __attribute__((visibility("default")))
@@ -329,6 +329,62 @@ SLR_API int slr_plan_row_order(const int32_t* crow_host, int64_t NB, int32_t* or
  */
 SLR_API int slr_plan_shards(const int32_t* crow_host, int64_t NB, int64_t block_p,
                     int64_t block_q, int64_t rank, int world, int64_t* bounds);
+
+/* ------------------------------- multi-GPU: y assembled in peer memory -- */
+
+/*
+ * A block-row-sharded layer on `world` GPUs (one process each) whose combine
+ * kernel stores every output tile into its own y AND into the y of every
+ * other rank over NVLink (CUDA IPC mappings), instead of a local slot plus an
+ * NCCL all-gather and a column reassembly.  No reference counterpart: the
+ * reference runs on one device.
+ *
+ * Each rank owns a full y [M, N] (same ldy on every rank) and, per layer, a
+ * 4-word uint64 signal slot that is zero before the first call.  y[p] is
+ * rank p's y advanced to THIS rank's first output column; signal[p] is rank
+ * p's slot of the layer.  A call is slr_lrs_linear_combine_peers (or the
+ * group form; ranks without rows of the layer call slr_peers_wait with
+ * empty_shard = 1 instead) followed by slr_peers_wait on the same stream;
+ * after the wait, y on this rank holds every rank's columns.  Every rank
+ * must make the calls of a layer in the same order.  Waits are bounded (2 s)
+ * and report SLR_ERR_TIMEOUT through slr_device_status.
+ */
+#define SLR_MAX_RANKS 8
+#define SLR_IPC_HANDLE_BYTES 64
+
+typedef struct slr_peers {
+  int32_t world;                    /* ranks, 2..SLR_MAX_RANKS */
+  int32_t rank;                     /* this rank */
+  void* y[SLR_MAX_RANKS];           /* rank p's y at this rank's first column */
+  uint64_t* signal[SLR_MAX_RANKS];  /* rank p's signal slot of this layer */
+} slr_peers;
+
+/* The IPC handle (SLR_IPC_HANDLE_BYTES) of the device allocation holding
+ * dev_ptr and dev_ptr's offset in it; slr_ipc_import on another process maps
+ * it (once per handle and process; counted) and returns the same address
+ * there; slr_ipc_release drops one import. */
+SLR_API int slr_ipc_export(const void* dev_ptr, void* handle, int64_t* offset);
+SLR_API int slr_ipc_import(const void* handle, int64_t offset, void** dev_ptr);
+SLR_API int slr_ipc_release(const void* handle);
+
+/* 1 when the combine of `layer` on M tokens (x row stride ldx) runs on the
+ * kernel that stores into peers (the 2-SM tensor-core kernel), else 0. */
+SLR_API int slr_lrs_linear_peers_supported(const slr_layer* layer, const void* x, int64_t ldx,
+                                           int64_t M);
+/* slr_lrs_linear_combine (after _lowrank on the same workspace) with the
+ * output written to peers->y[p] for every rank p. */
+SLR_API int slr_lrs_linear_combine_peers(const slr_layer* layer, const void* x, int64_t ldx,
+                                         int64_t ldy, int64_t M, void* workspace,
+                                         size_t workspace_bytes, const slr_peers* peers,
+                                         void* stream);
+/* slr_lrs_linear_group_combine (after _group_lowrank) into peers->y[p]. */
+SLR_API int slr_lrs_linear_group_combine_peers(const slr_layer* layers, int n, int i,
+                                               const void* x, int64_t ldx, int64_t ldy, int64_t M,
+                                               void* workspace, size_t workspace_bytes,
+                                               const slr_peers* peers, void* stream);
+/* Ends a call: returns (on the stream) once every rank's stores into this
+ * rank's y are visible. */
+SLR_API int slr_peers_wait(const slr_peers* peers, int empty_shard, void* stream);
 
 #ifdef __cplusplus
 }

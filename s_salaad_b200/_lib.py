@@ -50,7 +50,17 @@ EXPORTED = (
     "slr_plan_stages",
     "slr_plan_row_order",
     "slr_plan_shards",
+    "slr_ipc_export",
+    "slr_ipc_import",
+    "slr_ipc_release",
+    "slr_lrs_linear_peers_supported",
+    "slr_lrs_linear_combine_peers",
+    "slr_lrs_linear_group_combine_peers",
+    "slr_peers_wait",
 )
+
+SLR_MAX_RANKS = 8
+SLR_IPC_HANDLE_BYTES = 64
 
 i64, i32, vp, sz = ctypes.c_int64, ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t
 
@@ -79,6 +89,17 @@ class SlrLayer(ctypes.Structure):
     ]
 
 
+class SlrPeers(ctypes.Structure):
+    """Mirror of ``struct slr_peers``."""
+
+    _fields_ = [
+        ("world", ctypes.c_int32),
+        ("rank", ctypes.c_int32),
+        ("y", ctypes.c_void_p * SLR_MAX_RANKS),
+        ("signal", ctypes.c_void_p * SLR_MAX_RANKS),
+    ]
+
+
 _SIGS = {
     "slr_abi_version": ([], i32),
     "slr_set_sm_limit": ([i32], i32),
@@ -102,6 +123,15 @@ _SIGS = {
     "slr_plan_stages": ([vp, vp, i64, vp, i64, vp, vp, i64, ctypes.POINTER(i64)], i32),
     "slr_plan_row_order": ([vp, i64, vp], i32),
     "slr_plan_shards": ([vp, i64, i64, i64, i64, i32, vp], i32),
+    "slr_ipc_export": ([vp, vp, ctypes.POINTER(i64)], i32),
+    "slr_ipc_import": ([vp, i64, ctypes.POINTER(vp)], i32),
+    "slr_ipc_release": ([vp], i32),
+    "slr_lrs_linear_peers_supported": ([ctypes.POINTER(SlrLayer), vp, i64, i64], i32),
+    "slr_lrs_linear_combine_peers": ([ctypes.POINTER(SlrLayer), vp, i64, i64, i64, vp, sz,
+                                      ctypes.POINTER(SlrPeers), vp], i32),
+    "slr_lrs_linear_group_combine_peers": ([ctypes.POINTER(SlrLayer), i32, i32, vp, i64, i64, i64, vp, sz,
+                                            ctypes.POINTER(SlrPeers), vp], i32),
+    "slr_peers_wait": ([ctypes.POINTER(SlrPeers), i32, vp], i32),
 }
 
 _lock = threading.Lock()
@@ -138,7 +168,7 @@ def load(path: Path | str | None = None) -> ctypes.CDLL:
             fn = getattr(lib, name)
             fn.argtypes = args
             fn.restype = res
-        if lib.slr_abi_version() != 2:
+        if lib.slr_abi_version() != 3:
             raise RuntimeError("s_salaad_b200: libslr_b200.so ABI version mismatch")
         if path is None:
             _lib = lib

@@ -80,6 +80,36 @@ __device__ __forceinline__ void pdl_wait_primary() {
   asm volatile("griddepcontrol.wait;" ::: "memory");
 }
 
+// ------------------------------------------------- PTX: cross-GPU signals ----
+// Counters that other GPUs add to through CUDA IPC mappings over NVLink: the
+// writer release-adds at system scope, the owner acquire-loads.
+
+__device__ __forceinline__ void red_add_release_sys(unsigned long long* p, unsigned long long v) {
+  asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void fence_sc_sys() { asm volatile("fence.sc.sys;" ::: "memory"); }
+
+// Barrier among `threads` threads (whole warps) of the CTA on hardware barrier `id` (1..15).
+__device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// Spin until *p >= target, at most SLR_WAIT_LIMIT_NS; false on timeout.
+__device__ __forceinline__ bool wait_counter_geq(const unsigned long long* p, unsigned long long target) {
+  if (ld_acquire_sys(p) >= target) return true;
+  const unsigned long long t0 = globaltimer_ns();
+  while (true) {
+    __nanosleep(100);
+    if (ld_acquire_sys(p) >= target) return true;
+    if (globaltimer_ns() - t0 > SLR_WAIT_LIMIT_NS) return false;
+  }
+}
+
 // The k-th work item of worker p of P when the items, listed heaviest first,
 // are dealt in snake order (0..P-1, then P-1..0, ...): every round hands each
 // worker one item, and the worker that got the heaviest item of a round gets

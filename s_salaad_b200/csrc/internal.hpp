@@ -71,6 +71,29 @@ bool mma_group_compatible(const RowblockArgs* a, int n);
 int launch_mma_rowblock_group(const RowblockArgs* a, const int64_t* h_col, int n, const void* H, int64_t ldh,
                               bool pdl, cudaStream_t s);
 
+// ---- peer memory: a rank's output tiles stored straight into every rank's y.
+// Signal slot of one layer on each rank (4 x u64, zero at start):
+//   [0] arrivals: every rank adds 1 when its call for the layer starts;
+//   [1] completions: every rank adds kDonePerRank per call (its CTAs add 1
+//       each, CTA 0 adds kDonePerRank - gridDim.x on top) once its stores are
+//       visible;
+//   [2] calls of the layer completed on this rank (written by its own wait).
+// Call c (0-based) of a rank may store into peers only after [0] >= world *
+// (c + 1), so a peer's y is no longer read by the caller's previous work;
+// y is complete on rank p when its [1] >= world * kDonePerRank * (c + 1).
+constexpr int kMaxRanks = SLR_MAX_RANKS;
+constexpr unsigned long long kDonePerRank = 1ull << 32;
+struct PeerArgs {
+  void* y[kMaxRanks];                   // rank p's y at this rank's columns (y[me] = local)
+  unsigned long long* sig[kMaxRanks];   // rank p's signal slot of this layer
+  unsigned long long* my_sig;           // sig[me]
+  int world = 0, me = 0;
+};
+// The wait that ends a call (and, for a rank with no rows of the layer, its
+// arrival and completion signals).
+int launch_peer_wait(const PeerArgs& p, bool empty_shard, cudaStream_t s);
+int read_and_clear_status_peer(unsigned* out);
+
 // ---- tcgen05 / TMEM kernels (16-bit dtypes): large token batches.
 // SMs the persistent kernels may fill: the device's count, or fewer after
 // slr_set_sm_limit (to leave SMs to collectives running alongside).
@@ -81,7 +104,8 @@ constexpr int64_t kTileTokens = 128;   // token rows per tensor-core work item
 bool tc_rowblock_supported(const RowblockArgs& a);
 int launch_tc_rowblock(const RowblockArgs& a, bool pdl, cudaStream_t s);
 bool tc2_rowblock_supported(const RowblockArgs& a);  // 2-SM pairs, M >= 256, bp 32/64
-int launch_tc2_rowblock(const RowblockArgs& a, bool pdl, cudaStream_t s);
+// peers: also store every output tile into the other ranks' y (null = local only).
+int launch_tc2_rowblock(const RowblockArgs& a, bool pdl, cudaStream_t s, const PeerArgs* peers = nullptr);
 bool tc_dense_supported(const void* x, int64_t ldx, const void* B, int64_t K, int64_t r, int dtype);
 int launch_tc_dense(const void* x, int64_t ldx, const void* B, void* H, int64_t M, int64_t K, int64_t r,
                     int64_t ldh, int dtype, cudaStream_t s);

@@ -40,6 +40,10 @@ constexpr int kProducers = 3;   // TMA warps working from a column schedule
 constexpr int kStages = 6;      // ring slots (a multiple of kProducers)
 constexpr uint32_t kMetaLR = 1u << 30;
 constexpr uint32_t kMetaLast = 1u << 31;
+// After the ring: barriers and metadata, then (multi-GPU) the epilogue
+// staging rows of the 4 epilogue warps, 32 rows x block_p outputs each.
+constexpr uint32_t kEpiOff = 256;
+constexpr uint32_t epi_stage_bytes(int bp) { return 4u * 32u * uint32_t(bp) * 2u; }
 
 struct Tc2Args {
   void* y;
@@ -51,6 +55,7 @@ struct Tc2Args {
   const int32_t* plan_start;
   int64_t M, ldy;
   int nrows, n_groups, n_mtiles, n_lr;
+  PeerArgs peer;          // world > 1: tiles also go to the other ranks' y
 };
 
 __device__ __forceinline__ void timeout2(volatile int* abort_flag) {
@@ -380,6 +385,31 @@ __global__ void __launch_bounds__(kThreads, 1)
     TI* __restrict__ y = static_cast<TI*>(a.y);
     const TI* __restrict__ bias = static_cast<const TI*>(a.bias);
     const uint32_t te0 = mapa(smem_u32(&tempty[0]), 0);
+    constexpr int kCpr = BP / 8;  // 16-byte chunks of a row's BP outputs
+    uint4* stage_w = reinterpret_cast<uint4*>(smem + STAGES * STAGE + kEpiOff) + (warp - 2) * 32 * kCpr;
+    // Multi-GPU: this call's arrival at every rank, then (before the first
+    // store into a peer) the wait for every rank's arrival.
+    const int world = a.peer.world;
+    unsigned long long arrive_target = 0;
+    bool peer_live = world > 1, arrived = false;
+    if (world > 1) {
+      pdl_wait_primary();  // the preceding wait of this rank has counted its calls
+      arrive_target = (*reinterpret_cast<volatile unsigned long long*>(a.peer.my_sig + 2) + 1) * world;
+      if (blockIdx.x == 0 && warp == 2 && lane == 0) {
+#pragma unroll
+        for (int p = 0; p < kMaxRanks; ++p)
+          if (p < world) red_add_release_sys(a.peer.sig[p] + 0, 1ull);
+      }
+    }
+    auto wait_arrivals = [&]() {
+      int ok = lane == 0 ? int(wait_counter_geq(a.peer.my_sig + 0, arrive_target)) : 1;
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) {
+        if (lane == 0) atomicOr(&g_status_tc2, SLR_TIMEOUT_BIT);
+        peer_live = false;  // keep the local result, leave the peers alone
+      }
+      arrived = true;
+    };
     uint32_t it = 0;
     for (int kr = 0, item = snake_item(0, pair, npairs); item < n_items; ++kr, item = snake_item(kr, pair, npairs), ++it) {
       const int gi = item / a.n_mtiles, mt = item - gi * a.n_mtiles;
@@ -391,6 +421,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
+      if (peer_live && !arrived) wait_arrivals();
       const int64_t tok = int64_t(mt) * 256 + int64_t(rank) * 128 + row;
       const uint32_t acc = tmem + lane_base + buf * ACC;
       for (int j = 0; j < G; ++j) {
@@ -402,6 +433,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int br = a.rows ? a.rows[r0 + j] : r0 + j;
         TI* yr = y + tok * a.ldy + int64_t(br) * BP;
         const TI* bb = bias ? bias + int64_t(br) * BP : nullptr;
+        // Multi-GPU: the warp's 32 rows x BP features go through shared
+        // memory so that each store instruction writes whole row segments
+        // (BP * 2 bytes) -- NVLink moves short scattered writes poorly.
+        const bool staged = world > 1;
 #pragma unroll
         for (int c0 = 0; c0 < BP; c0 += 16) {
           uint32_t r[16];
@@ -436,15 +471,54 @@ __global__ void __launch_bounds__(kThreads, 1)
             o1.y = pack2(v[10], v[11], (TI*)nullptr);
             o1.z = pack2(v[12], v[13], (TI*)nullptr);
             o1.w = pack2(v[14], v[15], (TI*)nullptr);
-            reinterpret_cast<uint4*>(yr + c0)[0] = o0;
-            reinterpret_cast<uint4*>(yr + c0)[1] = o1;
+            if (staged) {
+              const int c = c0 / 8;
+              stage_w[lane * kCpr + ((c + 0) ^ (lane & (kCpr - 1)))] = o0;
+              stage_w[lane * kCpr + ((c + 1) ^ (lane & (kCpr - 1)))] = o1;
+            } else {
+              reinterpret_cast<uint4*>(yr + c0)[0] = o0;
+              reinterpret_cast<uint4*>(yr + c0)[1] = o1;
+            }
           }
+        }
+        if (staged) {
+          __syncwarp();
+          const int64_t tok0 = tok - lane;  // the warp's first row
+#pragma unroll
+          for (int i = 0; i < kCpr; ++i) {
+            const int qd = i * 32 + lane, rr = qd / kCpr, cc = qd % kCpr;
+            const uint4 v = stage_w[rr * kCpr + (cc ^ (rr & (kCpr - 1)))];
+            if (tok0 + rr < a.M) {
+              const int64_t off = (tok0 + rr) * a.ldy + int64_t(br) * BP + cc * 8;
+              *reinterpret_cast<uint4*>(y + off) = v;
+              if (peer_live) {
+#pragma unroll
+                for (int p = 0; p < kMaxRanks; ++p)
+                  if (p < world && p != a.peer.me)
+                    *reinterpret_cast<uint4*>(static_cast<TI*>(a.peer.y[p]) + off) = v;
+              }
+            }
+          }
+          __syncwarp();  // the stage is rewritten by the next block-row
         }
       }
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(te0 + buf * 8);
+    }
+    if (world > 1) {
+      // Completion: after every rank arrived (so the count belongs to this
+      // call) and this CTA's stores are visible system-wide.
+      if (peer_live && !arrived) wait_arrivals();
+      fence_sc_sys();
+      named_bar_sync(1, 128);
+      if (warp == 2 && lane == 0) {
+        const unsigned long long add = 1ull + (blockIdx.x == 0 ? kDonePerRank - gridDim.x : 0ull);
+#pragma unroll
+        for (int p = 0; p < kMaxRanks; ++p)
+          if (p < world) red_add_release_sys(a.peer.sig[p] + 1, add);
+      }
     }
   }
 
@@ -467,7 +541,8 @@ int launch_inst(const CUtensorMap& tx, const CUtensorMap& tv, const CUtensorMap&
   constexpr uint32_t B_SLOT = (G * POS > (G / 2) * AR_ROW) ? G * POS : (G / 2) * AR_ROW;
   constexpr uint32_t STAGE = 16384 + B_SLOT;
   constexpr int STAGES = kStages;
-  const size_t smem = 1024 + size_t(STAGES) * STAGE + (2 * STAGES + 4) * 8 + STAGES * 4 + 16;
+  static_assert((2 * STAGES + 4) * 8 + STAGES * 4 + 16 <= kEpiOff, "barrier area");
+  const size_t smem = 1024 + size_t(STAGES) * STAGE + kEpiOff + (k.peer.world > 1 ? epi_stage_bytes(BP) : 0);
   auto kern = tc2_rowblock_kernel<BP, BQ, TI, MODE>;
   SLR_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
   const int items = k.n_groups * k.n_mtiles;
@@ -520,7 +595,7 @@ bool tc2_rowblock_supported(const RowblockArgs& a) {
   return (a.bp == 32 || a.bp == 64) && a.M >= 256 && tc_rowblock_supported(a);
 }
 
-int launch_tc2_rowblock(const RowblockArgs& a, bool pdl, cudaStream_t s) {
+int launch_tc2_rowblock(const RowblockArgs& a, bool pdl, cudaStream_t s, const PeerArgs* peers) {
   if (a.nrows <= 0 || a.M <= 0) return SLR_OK;
   const bool sparse = a.crow != nullptr && a.nnz > 0;
   const int bq = sparse ? a.bq : 64;
@@ -537,6 +612,7 @@ int launch_tc2_rowblock(const RowblockArgs& a, bool pdl, cudaStream_t s) {
   Tc2Args k{a.y, a.mode == MODE_FUSED ? a.bias : nullptr, sparse ? a.crow : nullptr, a.col, a.rows,
             sparse ? a.stage_plan : nullptr, sparse ? a.stage_start : nullptr, a.M, a.ldy,
             int(a.nrows), int(ceil_div(a.nrows, G)), int(ceil_div(a.M, 256)), 0};
+  if (peers) k.peer = *peers;
   if (a.mode == MODE_FUSED && a.r > 0) {
     k.n_lr = int(ceil_div(a.r, 64));
     rc = make_tmap_2d(&th, a.H, a.dtype, uint64_t(a.ldh), uint64_t(a.M), uint64_t(a.ldh) * 2, 64u, 128u);

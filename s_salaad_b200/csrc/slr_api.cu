@@ -217,6 +217,9 @@ int slr_device_status(int* status_out) {
   rc = read_and_clear_status_tc2(&w);
   if (rc) return rc;
   v |= w;
+  rc = read_and_clear_status_peer(&w);
+  if (rc) return rc;
+  v |= w;
   *status_out = (v & SLR_TIMEOUT_BIT) ? SLR_ERR_TIMEOUT : SLR_OK;
   return SLR_OK;
 }
@@ -670,6 +673,89 @@ int slr_lrs_linear_group_combine(const slr_layer* layers, int n, int i, const vo
   c.a.ldh = gc.c[i].a.ldh;
   c.counters = gc.c[i].counters;
   return run_combine(layers[i], c, false, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"
+
+namespace {
+
+int to_peer_args(const slr_peers* P, PeerArgs& pa) {
+  if (!P) return fail(SLR_ERR_INVALID_ARGUMENT, "peers is NULL");
+  if (P->world < 2 || P->world > kMaxRanks || P->rank < 0 || P->rank >= P->world)
+    return fail(SLR_ERR_INVALID_ARGUMENT, "peers: world must be 2.." + std::to_string(kMaxRanks) +
+                                              " and rank in [0, world)");
+  pa = PeerArgs{};
+  pa.world = P->world;
+  pa.me = P->rank;
+  for (int p = 0; p < P->world; ++p) {
+    if (!P->y[p] || !P->signal[p]) return fail(SLR_ERR_INVALID_ARGUMENT, "peers: NULL y or signal");
+    if (!aligned16(P->y[p]) || (reinterpret_cast<uintptr_t>(P->signal[p]) & 7u))
+      return fail(SLR_ERR_INVALID_ARGUMENT, "peers: y must be 16-byte and signal 8-byte aligned");
+    pa.y[p] = P->y[p];
+    pa.sig[p] = reinterpret_cast<unsigned long long*>(P->signal[p]);
+  }
+  pa.my_sig = pa.sig[pa.me];
+  return SLR_OK;
+}
+
+int check_peer_call(const slr_layer& L, const FwdCall& c, int64_t ldy, int64_t M) {
+  if (M <= 0) return fail(SLR_ERR_INVALID_ARGUMENT, "peers: M must be > 0");
+  if ((ldy * int64_t(dtype_size(L.dtype))) % 16)
+    return fail(SLR_ERR_INVALID_ARGUMENT, "peers: y rows must be 16-byte multiples");
+  if (!use_pair(L, c))
+    return fail(SLR_ERR_UNSUPPORTED, "peers: this layer's combine does not run on the 2-SM tensor-core kernel");
+  return SLR_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int slr_lrs_linear_peers_supported(const slr_layer* layer, const void* x, int64_t ldx, int64_t M) {
+  FwdCall c;
+  if (M <= 0 || prepare_forward(layer, x, ldx, nullptr, 0, M, nullptr, 0, false, c, false) != SLR_OK) return 0;
+  return use_pair(*layer, c) ? 1 : 0;
+}
+
+int slr_lrs_linear_combine_peers(const slr_layer* layer, const void* x, int64_t ldx, int64_t ldy, int64_t M,
+                                 void* workspace, size_t workspace_bytes, const slr_peers* peers, void* stream) {
+  PeerArgs pa;
+  int rc = to_peer_args(peers, pa);
+  if (rc) return rc;
+  FwdCall c;
+  rc = prepare_forward(layer, x, ldx, pa.y[pa.me], ldy, M, workspace, workspace_bytes, true, c);
+  if (rc) return rc;
+  rc = check_peer_call(*layer, c, c.a.ldy, M);
+  if (rc) return rc;
+  return launch_tc2_rowblock(c.a, false, static_cast<cudaStream_t>(stream), &pa);
+}
+
+int slr_lrs_linear_group_combine_peers(const slr_layer* layers, int n, int i, const void* x, int64_t ldx,
+                                       int64_t ldy, int64_t M, void* workspace, size_t workspace_bytes,
+                                       const slr_peers* peers, void* stream) {
+  if (i < 0 || i >= n) return fail(SLR_ERR_INVALID_ARGUMENT, "layer index out of range");
+  PeerArgs pa;
+  int rc = to_peer_args(peers, pa);
+  if (rc) return rc;
+  GroupCall gc;
+  rc = prepare_group(layers, n, x, ldx, nullptr, nullptr, M, workspace, workspace_bytes, gc);
+  if (rc) return rc;
+  FwdCall c = gc.c[i];
+  rc = prepare_forward(&layers[i], x, ldx, pa.y[pa.me], ldy, M, gc.ws + gc.g.off[i], gc.g.bytes[i], true, c,
+                       gc.mode == GROUP_EACH);
+  if (rc) return rc;
+  c.a.H = gc.c[i].a.H;
+  c.a.ldh = gc.c[i].a.ldh;
+  rc = check_peer_call(layers[i], c, c.a.ldy, M);
+  if (rc) return rc;
+  return launch_tc2_rowblock(c.a, false, static_cast<cudaStream_t>(stream), &pa);
+}
+
+int slr_peers_wait(const slr_peers* peers, int empty_shard, void* stream) {
+  PeerArgs pa;
+  int rc = to_peer_args(peers, pa);
+  if (rc) return rc;
+  return launch_peer_wait(pa, empty_shard != 0, static_cast<cudaStream_t>(stream));
 }
 
 int slr_dense_to_bsr_mask(const void* S, int64_t n, int64_t m, int64_t block_p, int64_t block_q,

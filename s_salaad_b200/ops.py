@@ -314,6 +314,18 @@ class LayerGroup:
         _lib.check(rc, "lrs_linear_group_lowrank")
         return ws[:M * self.h_row_bytes()]
 
+    def combine_peers(self, i: int, x2: torch.Tensor, po) -> None:
+        """Phase 2 of layer i with its output stored into every rank's y
+        (``po``: a :class:`s_salaad_b200.shard.PeerOutputs` of that layer)."""
+        M = x2.shape[0]
+        ws = self.workspace(M)
+        with _DeviceGuard(self.device):
+            rc = _lib.load().slr_lrs_linear_group_combine_peers(
+                self._structs(), len(self.descs), i, x2.data_ptr(), LayerDesc._ld(x2), po.ldy, M,
+                None if ws is None else ws.data_ptr(), 0 if ws is None else ws.numel(), ctypes.byref(po.struct),
+                _stream(self.device))
+        _lib.check(rc, "lrs_linear_group_combine_peers")
+
     def combine(self, i: int, x2: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
         """Phase 2 of layer i (after lowrank() on the same x2)."""
         M = x2.shape[0]

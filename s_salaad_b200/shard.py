@@ -10,6 +10,12 @@ fused forward into its slot of a ``[P, T, Nmax]`` buffer, one all-gather
 (NCCL on GPUs) gives every rank all slots and the columns are assembled
 into y.
 
+With :class:`PeerOutputs` the all-gather disappears: every rank owns a full
+y, the other ranks' y are mapped into its address space (CUDA IPC), and the
+combine kernel's epilogue stores each output tile into all of them over
+NVLink while it computes; a wait kernel ends the call once every rank's
+tiles have landed.
+
 The reference runs on one device only; this module has no reference
 counterpart and keeps the single-device arithmetic exactly (each output
 element is computed by exactly one rank with the single-GPU kernels).
@@ -19,11 +25,13 @@ element is computed by exactly one rank with the single-GPU kernels).
 """
 from __future__ import annotations
 
+import ctypes
+
 import numpy as np
 import torch
 import torch.distributed as dist
 
-from . import ops
+from . import _lib, ops
 
 
 def shard_bounds(crow: np.ndarray, block_p: int, block_q: int, rank_r: int, world: int) -> np.ndarray:
@@ -131,10 +139,6 @@ class ShardedLayer(ShardPlan):
             if off % 256 == 0:
                 # room for the slice call's own layout (H rows, then its scratch) at the offset
                 ws = d.workspace(T, at_least=off + d.workspace_bytes(tp))
-                import ctypes
-
-                from . import _lib
-
                 xs = x2[self.rank * tp:(self.rank + 1) * tp]
                 rc = _lib.load().slr_lrs_linear_lowrank(
                     ctypes.byref(d.struct), xs.data_ptr(), xs.stride(0), tp, ws.data_ptr() + off, ws.numel() - off,
@@ -171,3 +175,113 @@ class ShardedLayer(ShardPlan):
 
     def forward(self, x2: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
         return self.finish(self.start(x2), out)
+
+    # ---------------------------------------------- y written into peer memory
+    def peers_supported(self, x2: torch.Tensor) -> bool:
+        """Whether this rank's combine can store into peers (a rank without
+        rows only takes part in the signals).  All ranks must agree before
+        :meth:`start_peers` is used: see :func:`all_ranks`."""
+        if self.desc is None:
+            return True
+        return bool(_lib.load().slr_lrs_linear_peers_supported(
+            ctypes.byref(self.desc.struct), x2.data_ptr(), ops.LayerDesc._ld(x2), x2.shape[0]))
+
+    def start_peers(self, x2: torch.Tensor, po: "PeerOutputs") -> None:
+        """x·Bᵀ, then the combine with every output tile stored into all ranks' y."""
+        if self.desc is None:
+            return
+        self._lowrank(x2)
+        self.start_peers_combine(x2, po)
+
+    def start_peers_combine(self, x2: torch.Tensor, po: "PeerOutputs") -> None:
+        """The combine alone (after the x·Bᵀ phase) into all ranks' y."""
+        if self.desc is None:
+            return
+        d = self.desc
+        ws = d.workspace(x2.shape[0])
+        with ops._DeviceGuard(self.device):
+            rc = _lib.load().slr_lrs_linear_combine_peers(
+                ctypes.byref(d.struct), x2.data_ptr(), ops.LayerDesc._ld(x2), po.ldy, x2.shape[0],
+                None if ws is None else ws.data_ptr(), 0 if ws is None else ws.numel(), ctypes.byref(po.struct),
+                torch.cuda.current_stream(self.device).cuda_stream)
+        _lib.check(rc, "lrs_linear_combine_peers")
+
+    def finish_peers(self, po: "PeerOutputs") -> torch.Tensor:
+        """Wait (on the stream) until every rank's columns are in po.y."""
+        po.wait(empty_shard=self.desc is None)
+        return po.y
+
+
+def all_ranks(flag: bool, device, group=None) -> bool:
+    """True when `flag` holds on every rank of the group."""
+    t = torch.tensor([1 if flag else 0], dtype=torch.int32, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MIN, group=group)
+    return bool(t.item())
+
+
+class PeerOutputs:
+    """The full y [T, N] of one sharded layer on this rank, with the y and
+    signal slot of every other rank mapped in (collective: every rank of the
+    group constructs it for the same layer, in the same order).
+
+    ``struct`` is the ``slr_peers`` argument of the combine: y of rank p
+    advanced to this rank's first column ``n0``.
+    """
+
+    def __init__(self, plan: ShardPlan, T: int, dtype, device, group=None):
+        self.world, self.rank = plan.world, plan.rank
+        if not 2 <= self.world <= _lib.SLR_MAX_RANKS:
+            raise ValueError(f"peer outputs need 2..{_lib.SLR_MAX_RANKS} ranks")
+        self.device = device
+        self.y = torch.empty(T, plan.out_features, dtype=dtype, device=device)
+        self.ldy = plan.out_features
+        self.signal = torch.zeros(4, dtype=torch.int64, device=device)
+        lib = _lib.load()
+        hb = _lib.SLR_IPC_HANDLE_BYTES
+        mine = np.zeros(2 * (hb + 8), dtype=np.uint8)
+        with ops._DeviceGuard(device):
+            for k, t in enumerate((self.y, self.signal)):
+                h = (ctypes.c_uint8 * hb)()
+                off = ctypes.c_int64()
+                _lib.check(lib.slr_ipc_export(t.data_ptr(), h, ctypes.byref(off)), "ipc_export")
+                base = k * (hb + 8)
+                mine[base:base + hb] = np.frombuffer(bytes(h), dtype=np.uint8)
+                mine[base + hb:base + hb + 8] = np.frombuffer(np.int64(off.value).tobytes(), dtype=np.uint8)
+        local = torch.from_numpy(mine).to(device)
+        every = torch.empty(self.world * mine.size, dtype=torch.uint8, device=device)
+        dist.all_gather_into_tensor(every, local, group=group)
+        every = every.cpu().numpy().reshape(self.world, -1)
+        self._imported: list[bytes] = []
+        st = _lib.SlrPeers()
+        st.world, st.rank = self.world, self.rank
+        col_bytes = plan.n0 * self.y.element_size()
+        with ops._DeviceGuard(device):
+            for p in range(self.world):
+                ptrs = []
+                for k, t in enumerate((self.y, self.signal)):
+                    if p == self.rank:
+                        ptrs.append(t.data_ptr())
+                        continue
+                    base = k * (hb + 8)
+                    h = bytes(every[p, base:base + hb])
+                    off = int(np.frombuffer(every[p, base + hb:base + hb + 8].tobytes(), dtype=np.int64)[0])
+                    out = ctypes.c_void_p()
+                    _lib.check(lib.slr_ipc_import(h, off, ctypes.byref(out)), "ipc_import")
+                    self._imported.append(h)
+                    ptrs.append(out.value)
+                st.y[p] = ptrs[0] + col_bytes
+                st.signal[p] = ptrs[1]
+        self.struct = st
+
+    def wait(self, empty_shard: bool = False) -> None:
+        with ops._DeviceGuard(self.device):
+            rc = _lib.load().slr_peers_wait(ctypes.byref(self.struct), 1 if empty_shard else 0,
+                                            torch.cuda.current_stream(self.device).cuda_stream)
+        _lib.check(rc, "peers_wait")
+
+    def close(self) -> None:
+        """Drop the mappings of the other ranks' buffers (after all use)."""
+        lib = _lib.load()
+        for h in self._imported:
+            lib.slr_ipc_release(h)
+        self._imported = []

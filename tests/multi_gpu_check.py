@@ -18,6 +18,58 @@ from s_salaad_b200 import ops, workloads  # noqa: E402
 from s_salaad_b200.shard import ShardedLayer  # noqa: E402
 
 
+def check_peer_outputs(rank: int, world: int, dev) -> int:
+    """Outputs stored straight into every rank's y (peer memory) equal the
+    all-gather path bit for bit, call after call, eagerly and from a CUDA graph."""
+    import ctypes
+
+    from s_salaad_b200 import _lib
+    from s_salaad_b200.shard import PeerOutputs, all_ranks
+
+    bad = 0
+    for cfg, idx, T in [("cfg4", 0, 1024), ("cfg4", 6, 300)]:
+        s = workloads.layer_set(cfg)[idx]
+        t = s.tensors(dev, torch.bfloat16)
+        x = workloads.tokens(T, s.in_features, seed=7, device=dev, dtype=torch.bfloat16)
+        sh = ShardedLayer(t, s.crow, in_features=s.in_features, out_features=s.out_features,
+                          block_p=s.block_p, block_q=s.block_q, rank=rank, world=world)
+        if not all_ranks(sh.peers_supported(x), dev):
+            print(f"rank {rank}/{world} peers {cfg}[{idx}] T={T} not supported on every rank", flush=True)
+            bad += 1
+            continue
+        ref = sh.forward(x)
+        po = PeerOutputs(sh, T, torch.bfloat16, dev)
+        errs = []
+        for _ in range(3):
+            po.y.zero_()
+            sh.start_peers(x, po)
+            y = sh.finish_peers(po)
+            errs.append(not torch.equal(y, ref))
+        stream = torch.cuda.Stream(dev)
+        stream.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(stream):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                sh.start_peers(x, po)
+                sh.finish_peers(po)
+        torch.cuda.current_stream(dev).wait_stream(stream)
+        for _ in range(3):
+            po.y.zero_()
+            g.replay()
+            errs.append(not torch.equal(po.y, ref))
+        torch.cuda.synchronize()
+        st = ctypes.c_int(-1)
+        _lib.check(_lib.load().slr_device_status(ctypes.byref(st)), "device_status")
+        ok = not any(errs) and st.value == 0
+        bad += 0 if ok else 1
+        print(f"rank {rank}/{world} peers {cfg}[{idx}] T={T} mismatching calls={sum(errs)} "
+              f"status={st.value} {'ok' if ok else 'MISMATCH'}", flush=True)
+        del g
+        dist.barrier()
+        po.close()
+    return bad
+
+
 def main() -> int:
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     local = int(os.environ.get("LOCAL_RANK", rank))
@@ -77,6 +129,28 @@ def main() -> int:
         bad += 0 if ok else 1
         print(f"rank {rank}/{world} grouped split-H cfg4[{j}] T={T} max|diff|={err:.3e} "
               f"{'ok' if ok else 'MISMATCH'}", flush=True)
+    # the same group with every combine storing into all ranks' y (peer memory)
+    from s_salaad_b200.shard import PeerOutputs, all_ranks
+    if all_ranks(all(sh.peers_supported(x) for sh in shards), dev):
+        pos = [PeerOutputs(sh, T, torch.bfloat16, dev) for sh in shards]
+        grp.lowrank(x)
+        for j, po in enumerate(pos):
+            grp.combine_peers(j, x, po)
+        for j, (sh, po, ref) in enumerate(zip(shards, pos, refs)):
+            y = sh.finish_peers(po)
+            err = float((y.float() - ref.float()).abs().max())
+            ok = err == 0.0
+            bad += 0 if ok else 1
+            print(f"rank {rank}/{world} grouped peers cfg4[{j}] T={T} max|diff|={err:.3e} "
+                  f"{'ok' if ok else 'MISMATCH'}", flush=True)
+        torch.cuda.synchronize()
+        dist.barrier()
+        for po in pos:
+            po.close()
+    else:
+        print(f"rank {rank}/{world} grouped peers: not supported on every rank", flush=True)
+        bad += 1
+    bad += check_peer_outputs(rank, world, dev)
     flag = torch.tensor([bad], device=dev)
     dist.all_reduce(flag)
     dist.barrier()
