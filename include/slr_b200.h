@@ -36,7 +36,7 @@
 extern "C" {
 #endif
 
-#define SLR_ABI_VERSION 3
+#define SLR_ABI_VERSION 4
 
 #if defined(__GNUC__)
 #define SLR_API __attribute__((visibility("default")))
@@ -164,6 +164,11 @@ typedef struct slr_layer {
                                   row_order and block_p; NULL = computed on
                                   the fly by the kernel (same result) */
   const int32_t* stage_start;  /* device int32 [groups + 1] from slr_plan_stages */
+  int64_t route_out_features;  /* 0, or (for a block-row shard of a wider layer)
+                                  the whole layer's out_features: kernels are
+                                  then chosen as for the whole layer, so the
+                                  shard's outputs equal the whole layer's bit
+                                  for bit */
 } slr_layer;
 
 /*

@@ -86,6 +86,7 @@ class SlrLayer(ctypes.Structure):
         ("flags", ctypes.c_int32),
         ("stage_plan", ctypes.c_void_p),
         ("stage_start", ctypes.c_void_p),
+        ("route_out_features", ctypes.c_int64),
     ]
 
 
@@ -168,7 +169,7 @@ def load(path: Path | str | None = None) -> ctypes.CDLL:
             fn = getattr(lib, name)
             fn.argtypes = args
             fn.restype = res
-        if lib.slr_abi_version() != 3:
+        if lib.slr_abi_version() != 4:
             raise RuntimeError("s_salaad_b200: libslr_b200.so ABI version mismatch")
         if path is None:
             _lib = lib

@@ -25,6 +25,7 @@ struct RowblockArgs {
   const uint32_t* stage_plan = nullptr;  // column schedule of each 256-feature row group
   const int32_t* stage_start = nullptr;  // (from slr_plan_stages), or null
   int64_t nrows = 0;
+  int64_t route_nrows = 0;  // block-rows of the whole layer for kernel choice (0 = nrows)
   int64_t M = 0, K = 0, N = 0, r = 0, nnz = 0;
   int64_t ldx = 0, ldy = 0;  // row strides of x and y (elements)
   int bp = 0, bq = 0;

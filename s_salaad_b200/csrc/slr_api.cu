@@ -149,10 +149,12 @@ FwdPlan plan_forward(const slr_layer& L, int64_t M, const void* x) {
 // time; with fewer than 16 such items (few tokens and few output features,
 // e.g. 128 tokens of a 2048-wide projection) the small-batch kernel, which
 // spreads 16 features x 64 tokens per CTA over all SMs, is faster.
+// A block-row shard decides as its whole layer would (route_nrows).
 bool tc_worthwhile(const RowblockArgs& a) {
   if (a.M < kTcMinTokens || a.bp <= 0) return false;
   const int64_t G = a.bp <= 256 ? 256 / a.bp : 1;
-  return ceil_div(a.nrows, G) * ceil_div(a.M, kTileTokens) >= 16;
+  const int64_t rows = a.route_nrows > 0 ? a.route_nrows : a.nrows;
+  return ceil_div(rows, G) * ceil_div(a.M, kTileTokens) >= 16;
 }
 
 int check_layer(const slr_layer* L) {
@@ -164,6 +166,8 @@ int check_layer(const slr_layer* L) {
     return fail(SLR_ERR_INVALID_ARGUMENT, "in_features/out_features must be > 0 and rank >= 0");
   if (L->rank > 0 && (!L->A || !L->B)) return fail(SLR_ERR_INVALID_ARGUMENT, "A and B are required when rank > 0");
   if (L->nnz < 0) return fail(SLR_ERR_INVALID_ARGUMENT, "nnz must be >= 0");
+  if (L->route_out_features != 0 && L->route_out_features < L->out_features)
+    return fail(SLR_ERR_INVALID_ARGUMENT, "route_out_features must be 0 or >= out_features");
   if (L->nnz > 0) {
     if (!L->crow || !L->col || !L->values) return fail(SLR_ERR_INVALID_ARGUMENT, "crow/col/values are required when nnz > 0");
     if (L->block_p <= 0 || L->block_q <= 0) return fail(SLR_ERR_INVALID_ARGUMENT, "block_p/block_q must be > 0");
@@ -349,6 +353,7 @@ int prepare_forward(const slr_layer* layer, const void* x, int64_t ldx, void* y,
   a.stage_plan = (L.nnz > 0 && L.stage_start) ? L.stage_plan : nullptr;
   a.stage_start = a.stage_plan ? L.stage_start : nullptr;
   a.nrows = L.out_features / c.p.row_bp;
+  a.route_nrows = L.route_out_features > 0 ? ceil_div(L.route_out_features, c.p.row_bp) : 0;
   a.M = M;
   a.K = L.in_features;
   a.N = L.out_features;

@@ -121,9 +121,12 @@ class LayerDesc:
     """
 
     def __init__(self, *, A, B, bias=None, crow=None, col=None, values=None, row_order=None,
-                 in_features: int, out_features: int, block_p: int = 0, block_q: int = 0, flags: int = 0):
+                 in_features: int, out_features: int, block_p: int = 0, block_q: int = 0, flags: int = 0,
+                 route_out_features: int = 0):
         self.tensors = dict(A=A, B=B, bias=bias, crow=crow, col=col, values=values, row_order=row_order)
         self.flags = int(flags)  # slr_layer.flags: SLR_FLAG_PAIR_MMA | SLR_FLAG_STRICT_ORDER
+        # a block-row shard: kernels chosen as for the whole layer of this width
+        self.route_out_features = int(route_out_features)
         self.in_features = int(in_features)
         self.out_features = int(out_features)
         self.block_p = int(block_p)
@@ -155,6 +158,7 @@ class LayerDesc:
         s.bias = _ptr(t["bias"])
         s.dtype = slr_dtype(A.dtype)
         s.flags = self.flags
+        s.route_out_features = self.route_out_features
         self.device = A.device
         self.dtype = A.dtype
         self.key = tuple(_ptr(v) for v in t.values())

@@ -114,7 +114,7 @@ class ShardedLayer(ShardPlan):
                                       crow=p["S_crow"] if nnz else None, col=p["S_col"] if nnz else None,
                                       values=p["S_values"] if nnz else None, row_order=order if nnz else None,
                                       in_features=in_features, out_features=self.width, block_p=block_p,
-                                      block_q=block_q)
+                                      block_q=block_q, route_out_features=out_features)
         self._buf: torch.Tensor | None = None
 
     def local_buffer(self, T: int) -> torch.Tensor:

@@ -416,6 +416,26 @@ def test_full_size_configs_match_torch_fp32(cuda, cfg, T):
         assert_16bit_close(y, torch_ref(t, spec, x))
 
 
+@pytest.mark.parametrize("cfg,idx,T,world", [("cfg4", 6, 300, 8), ("cfg4", 0, 128, 8), ("cfg3", 4, 16, 4)])
+def test_block_row_shards_equal_whole_layer(cuda, cfg, idx, T, world):
+    """Each rank's shard (built on one GPU here) reproduces its columns of the
+    whole layer bit for bit: kernels are chosen for the whole layer's width,
+    even where the shard alone would take the small-batch kernel."""
+    from s_salaad_b200.shard import ShardedLayer
+
+    spec = workloads.layer_set(cfg)[idx]
+    t = spec.tensors(cuda, torch.bfloat16)
+    x = workloads.tokens(T, spec.in_features, seed=3, device=cuda, dtype=torch.bfloat16)
+    ref = desc_for(t, spec, cuda, torch.bfloat16).forward(x)
+    for rank in range(world):
+        sh = ShardedLayer(t, spec.crow, in_features=spec.in_features, out_features=spec.out_features,
+                          block_p=spec.block_p, block_q=spec.block_q, rank=rank, world=world)
+        if sh.desc is None:
+            continue
+        y = sh.desc.forward(x)
+        assert torch.equal(y, ref[:, sh.n0:sh.n0 + sh.width]), (rank, sh.bounds)
+
+
 # ------------------------------------------------------------ conversion --
 
 def test_dense_to_bsr_gpu_is_bit_exact_with_reference(cuda):
