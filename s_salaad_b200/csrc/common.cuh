@@ -210,6 +210,23 @@ __device__ __forceinline__ void tma_prefetch_l2_2d(const void* tmap, int32_t c0,
 }
 // 2-D tiled load of one box into shared memory; completes `bytes` on `bar`.
 // c0 is the innermost (contiguous) coordinate in elements.
+// Tiled TMA store shared -> global (this GPU's memory or a peer's through a
+// CUDA IPC mapping), tracked in the issuing thread's bulk groups.
+__device__ __forceinline__ void tma_store_2d(const void* tmap, const void* smem_src, int32_t c0, int32_t c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(tmap)),
+               "r"(smem_u32(smem_src)), "r"(c0), "r"(c1)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// The thread's bulk stores have read their shared-memory source.
+__device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// The thread's bulk stores are complete.
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const void* tmap, int32_t c0,
                                             int32_t c1, uint64_t* bar) {
   asm volatile(

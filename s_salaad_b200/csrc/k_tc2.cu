@@ -41,8 +41,9 @@ constexpr int kStages = 6;      // ring slots (a multiple of kProducers)
 constexpr uint32_t kMetaLR = 1u << 30;
 constexpr uint32_t kMetaLast = 1u << 31;
 // After the ring: barriers and metadata, then (multi-GPU) the epilogue
-// staging rows of the 4 epilogue warps, 32 rows x block_p outputs each.
-constexpr uint32_t kEpiOff = 256;
+// staging tiles of the 4 epilogue warps, 32 rows x block_p outputs each,
+// laid out as the TMA store's swizzle (128B for block_p 64, 64B for 32).
+constexpr uint32_t kEpiOff = 1024;
 constexpr uint32_t epi_stage_bytes(int bp) { return 4u * 32u * uint32_t(bp) * 2u; }
 
 struct Tc2Args {
@@ -58,6 +59,12 @@ struct Tc2Args {
   PeerArgs peer;          // world > 1: tiles also go to the other ranks' y
 };
 
+// world > 1: TMA store maps of every rank's y at this rank's columns
+// ([M, N] of this layer, box block_p x 32 rows); m[me] is the local y.
+struct YMaps {
+  CUtensorMap m[kMaxRanks];
+};
+
 __device__ __forceinline__ void timeout2(volatile int* abort_flag) {
   atomicOr(&g_status_tc2, SLR_TIMEOUT_BIT);
   *abort_flag = 1;
@@ -67,7 +74,7 @@ template <int BP, int BQ, typename TI, int MODE>
 __global__ void __launch_bounds__(kThreads, 1)
     tc2_rowblock_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_v,
                         const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ CUtensorMap tm_a,
-                        const Tc2Args a) {
+                        const Tc2Args a, const __grid_constant__ YMaps ym) {
   constexpr int G = 256 / BP;            // block-rows per item
   constexpr int KS = BQ < 64 ? BQ : 64;  // k per sparse stage
   constexpr int SUB = BQ / KS;
@@ -386,6 +393,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const TI* __restrict__ bias = static_cast<const TI*>(a.bias);
     const uint32_t te0 = mapa(smem_u32(&tempty[0]), 0);
     constexpr int kCpr = BP / 8;  // 16-byte chunks of a row's BP outputs
+    // 16-byte chunk c of staging row r, as TMA's 128B (BP 64) / 64B (BP 32) swizzle places it
+    auto epi_swz = [](int r, int c) { return BP == 64 ? (c ^ (r & 7)) : (c ^ ((r >> 1) & 3)); };
     uint4* stage_w = reinterpret_cast<uint4*>(smem + STAGES * STAGE + kEpiOff) + (warp - 2) * 32 * kCpr;
     // Multi-GPU: this call's arrival at every rank, then (before the first
     // store into a peer) the wait for every rank's arrival.
@@ -433,10 +442,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int br = a.rows ? a.rows[r0 + j] : r0 + j;
         TI* yr = y + tok * a.ldy + int64_t(br) * BP;
         const TI* bb = bias ? bias + int64_t(br) * BP : nullptr;
-        // Multi-GPU: the warp's 32 rows x BP features go through shared
-        // memory so that each store instruction writes whole row segments
-        // (BP * 2 bytes) -- NVLink moves short scattered writes poorly.
+        // Multi-GPU: the warp's 32 rows x BP features go to shared memory and
+        // leave as one TMA store per destination (its own y and every peer's
+        // y over NVLink); the TMA engine keeps the remote writes in flight
+        // while the warps move on.
         const bool staged = world > 1;
+        if (staged) {
+          if (lane == 0) bulk_wait_read_all();  // the previous tile has left the stage
+          __syncwarp();
+        }
 #pragma unroll
         for (int c0 = 0; c0 < BP; c0 += 16) {
           uint32_t r[16];
@@ -473,8 +487,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             o1.w = pack2(v[14], v[15], (TI*)nullptr);
             if (staged) {
               const int c = c0 / 8;
-              stage_w[lane * kCpr + ((c + 0) ^ (lane & (kCpr - 1)))] = o0;
-              stage_w[lane * kCpr + ((c + 1) ^ (lane & (kCpr - 1)))] = o1;
+              stage_w[lane * kCpr + epi_swz(lane, c + 0)] = o0;
+              stage_w[lane * kCpr + epi_swz(lane, c + 1)] = o1;
             } else {
               reinterpret_cast<uint4*>(yr + c0)[0] = o0;
               reinterpret_cast<uint4*>(yr + c0)[1] = o1;
@@ -482,24 +496,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         if (staged) {
+          fence_proxy_async_smem();  // the stage's generic writes, before the TMA reads them
           __syncwarp();
-          const int64_t tok0 = tok - lane;  // the warp's first row
+          const int64_t tok0 = tok - lane;  // the warp's first row (rows >= M are clipped)
+          if (lane == 0 && tok0 < a.M) {
 #pragma unroll
-          for (int i = 0; i < kCpr; ++i) {
-            const int qd = i * 32 + lane, rr = qd / kCpr, cc = qd % kCpr;
-            const uint4 v = stage_w[rr * kCpr + (cc ^ (rr & (kCpr - 1)))];
-            if (tok0 + rr < a.M) {
-              const int64_t off = (tok0 + rr) * a.ldy + int64_t(br) * BP + cc * 8;
-              *reinterpret_cast<uint4*>(y + off) = v;
-              if (peer_live) {
-#pragma unroll
-                for (int p = 0; p < kMaxRanks; ++p)
-                  if (p < world && p != a.peer.me)
-                    *reinterpret_cast<uint4*>(static_cast<TI*>(a.peer.y[p]) + off) = v;
-              }
-            }
+            for (int p = 0; p < kMaxRanks; ++p)
+              if (p < world && (p == a.peer.me || peer_live))
+                tma_store_2d(&ym.m[p], stage_w, br * BP, int(tok0));
+            bulk_commit();
           }
-          __syncwarp();  // the stage is rewritten by the next block-row
         }
       }
       tmem_st_wait();
@@ -511,6 +517,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Completion: after every rank arrived (so the count belongs to this
       // call) and this CTA's stores are visible system-wide.
       if (peer_live && !arrived) wait_arrivals();
+      if (lane == 0) bulk_wait_all();
+      __syncwarp();
+      fence_proxy_async_global();
       fence_sc_sys();
       named_bar_sync(1, 128);
       if (warp == 2 && lane == 0) {
@@ -534,7 +543,7 @@ int num_sms() { return sm_budget(); }
 
 template <int BP, int BQ, typename TI, int MODE>
 int launch_inst(const CUtensorMap& tx, const CUtensorMap& tv, const CUtensorMap& th, const CUtensorMap& ta,
-                const Tc2Args& k, bool pdl, cudaStream_t s) {
+                const Tc2Args& k, const YMaps& ym, bool pdl, cudaStream_t s) {
   constexpr int G = 256 / BP;
   constexpr int KS = BQ < 64 ? BQ : 64;
   constexpr uint32_t POS = KS * BP, AR_ROW = BP * 128;
@@ -560,27 +569,27 @@ int launch_inst(const CUtensorMap& tx, const CUtensorMap& tv, const CUtensorMap&
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 2 : 1;
-  SLR_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kern, tx, tv, th, ta, k));
+  SLR_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kern, tx, tv, th, ta, k, ym));
   return SLR_OK;
 }
 
 template <int BP, typename TI, int MODE>
 int dispatch_bq(int bq, const CUtensorMap& tx, const CUtensorMap& tv, const CUtensorMap& th,
-                const CUtensorMap& ta, const Tc2Args& k, bool pdl, cudaStream_t s) {
+                const CUtensorMap& ta, const Tc2Args& k, const YMaps& ym, bool pdl, cudaStream_t s) {
   switch (bq) {
-    case 16: return launch_inst<BP, 16, TI, MODE>(tx, tv, th, ta, k, pdl, s);
-    case 32: return launch_inst<BP, 32, TI, MODE>(tx, tv, th, ta, k, pdl, s);
-    case 64: return launch_inst<BP, 64, TI, MODE>(tx, tv, th, ta, k, pdl, s);
-    case 128: return launch_inst<BP, 128, TI, MODE>(tx, tv, th, ta, k, pdl, s);
+    case 16: return launch_inst<BP, 16, TI, MODE>(tx, tv, th, ta, k, ym, pdl, s);
+    case 32: return launch_inst<BP, 32, TI, MODE>(tx, tv, th, ta, k, ym, pdl, s);
+    case 64: return launch_inst<BP, 64, TI, MODE>(tx, tv, th, ta, k, ym, pdl, s);
+    case 128: return launch_inst<BP, 128, TI, MODE>(tx, tv, th, ta, k, ym, pdl, s);
     default: return fail(SLR_ERR_UNSUPPORTED, "2-SM path: block_q must be 16, 32, 64 or 128");
   }
 }
 
 template <typename TI, int MODE>
 int dispatch_bp(int bp, int bq, const CUtensorMap& tx, const CUtensorMap& tv, const CUtensorMap& th,
-                const CUtensorMap& ta, const Tc2Args& k, bool pdl, cudaStream_t s) {
-  if (bp == 32) return dispatch_bq<32, TI, MODE>(bq, tx, tv, th, ta, k, pdl, s);
-  if (bp == 64) return dispatch_bq<64, TI, MODE>(bq, tx, tv, th, ta, k, pdl, s);
+                const CUtensorMap& ta, const Tc2Args& k, const YMaps& ym, bool pdl, cudaStream_t s) {
+  if (bp == 32) return dispatch_bq<32, TI, MODE>(bq, tx, tv, th, ta, k, ym, pdl, s);
+  if (bp == 64) return dispatch_bq<64, TI, MODE>(bq, tx, tv, th, ta, k, ym, pdl, s);
   return fail(SLR_ERR_UNSUPPORTED, "2-SM path: block_p must be 32 or 64");
 }
 
@@ -612,7 +621,16 @@ int launch_tc2_rowblock(const RowblockArgs& a, bool pdl, cudaStream_t s, const P
   Tc2Args k{a.y, a.mode == MODE_FUSED ? a.bias : nullptr, sparse ? a.crow : nullptr, a.col, a.rows,
             sparse ? a.stage_plan : nullptr, sparse ? a.stage_start : nullptr, a.M, a.ldy,
             int(a.nrows), int(ceil_div(a.nrows, G)), int(ceil_div(a.M, 256)), 0};
-  if (peers) k.peer = *peers;
+  YMaps ym{};
+  if (peers && peers->world > 1) {
+    k.peer = *peers;
+    // TMA store maps of every rank's y at this rank's columns: [M, N], box bp x 32 rows
+    for (int p = 0; p < peers->world; ++p) {
+      rc = make_tmap_2d(&ym.m[p], peers->y[p], a.dtype, uint64_t(a.N), uint64_t(a.M), uint64_t(a.ldy) * 2,
+                        uint32_t(a.bp), 32u);
+      if (rc) return rc;
+    }
+  }
   if (a.mode == MODE_FUSED && a.r > 0) {
     k.n_lr = int(ceil_div(a.r, 64));
     rc = make_tmap_2d(&th, a.H, a.dtype, uint64_t(a.ldh), uint64_t(a.M), uint64_t(a.ldh) * 2, 64u, 128u);
@@ -621,10 +639,10 @@ int launch_tc2_rowblock(const RowblockArgs& a, bool pdl, cudaStream_t s, const P
     if (rc) return rc;
   }
   if (a.dtype == SLR_BF16)
-    return a.mode == MODE_ADDMM ? dispatch_bp<__nv_bfloat16, MODE_ADDMM>(a.bp, bq, tx, tv, th, ta, k, pdl, s)
-                                : dispatch_bp<__nv_bfloat16, MODE_FUSED>(a.bp, bq, tx, tv, th, ta, k, pdl, s);
-  return a.mode == MODE_ADDMM ? dispatch_bp<__half, MODE_ADDMM>(a.bp, bq, tx, tv, th, ta, k, pdl, s)
-                              : dispatch_bp<__half, MODE_FUSED>(a.bp, bq, tx, tv, th, ta, k, pdl, s);
+    return a.mode == MODE_ADDMM ? dispatch_bp<__nv_bfloat16, MODE_ADDMM>(a.bp, bq, tx, tv, th, ta, k, ym, pdl, s)
+                                : dispatch_bp<__nv_bfloat16, MODE_FUSED>(a.bp, bq, tx, tv, th, ta, k, ym, pdl, s);
+  return a.mode == MODE_ADDMM ? dispatch_bp<__half, MODE_ADDMM>(a.bp, bq, tx, tv, th, ta, k, ym, pdl, s)
+                              : dispatch_bp<__half, MODE_FUSED>(a.bp, bq, tx, tv, th, ta, k, ym, pdl, s);
 }
 
 int read_and_clear_status_tc2(unsigned* out) {
