@@ -64,10 +64,6 @@ struct MmaMaps {
   CUtensorMap v[kMaxLayers], a[kMaxLayers];
 };
 
-__device__ __forceinline__ uint32_t ld_u32(const void* p) {
-  return *static_cast<const uint32_t*>(p);
-}
-
 __device__ __forceinline__ void ldsm_x2(uint32_t addr, uint32_t& r0, uint32_t& r1) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(addr));
 }
