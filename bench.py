@@ -61,7 +61,7 @@ METRIC = "S+LR linear tokens/s + %HBM/TC roofline at 1/2/4/8 B200 vs AVX2 CPU & 
 # `--metrics dram__bytes_read.sum,dram__bytes_write.sum,gpu__time_duration.sum`:
 # cfg4 = mean over the 7 combine launches of one step; cfg3-T1 = the whole
 # layer set of one step (its roofline covers the graph-replayed layer set).
-NCU_TRAFFIC = {"cfg4": 101094327.0, "cfg3-T1": 51059200.0}
+NCU_TRAFFIC = {"cfg4": 101094327.0, "cfg3-T1": 50881280.0}
 # SMs kept free of the persistent kernels at N > 1 (for the overlapping NCCL
 # all-gathers); SLR_BENCH_NCCL_SMS overrides it.
 SMS_FOR_NCCL = int(os.environ.get("SLR_BENCH_NCCL_SMS", "16"))
