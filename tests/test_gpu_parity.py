@@ -416,6 +416,28 @@ def test_full_size_configs_match_torch_fp32(cuda, cfg, T):
         assert_16bit_close(y, torch_ref(t, spec, x))
 
 
+@pytest.mark.parametrize("cfg,members,T", [("cfg4", (0, 1, 2), 1024), ("cfg4", (4, 5), 512), ("cfg4", (3,), 768),
+                                            ("cfg3", (4, 5), 384)])
+def test_group_h_is_identical_for_any_token_slicing(cuda, cfg, members, T):
+    """x*B^T computed on 128-token slices (1-SM tensor-core kernel) equals the
+    whole batch's (2-SM pair kernel, other tile widths) bit for bit."""
+    specs = [workloads.layer_set(cfg)[i] for i in members]
+    descs = [desc_for(s.tensors(cuda, torch.bfloat16), s, cuda, torch.bfloat16) for s in specs]
+    x = workloads.tokens(T, specs[0].in_features, seed=9, device=cuda, dtype=torch.bfloat16)
+    grp = ops.LayerGroup(descs)
+    nb = T * grp.h_row_bytes()
+    grp.lowrank(x)
+    whole = grp.workspace(T)[:nb].clone()
+    grp.workspace(T).zero_()
+    for r0 in range(0, T, 128):
+        grp.lowrank_rows(x, r0, 128)
+    assert torch.equal(grp.workspace(T)[:nb], whole)
+    # and the combine on that H equals the per-layer forward
+    for i, d in enumerate(descs):
+        assert torch.equal(grp.combine(i, x, torch.empty(T, d.out_features, dtype=torch.bfloat16, device=cuda)),
+                           d.forward(x))
+
+
 @pytest.mark.parametrize("cfg,idx,T,world", [("cfg4", 6, 300, 8), ("cfg4", 0, 128, 8), ("cfg3", 4, 16, 4)])
 def test_block_row_shards_equal_whole_layer(cuda, cfg, idx, T, world):
     """Each rank's shard (built on one GPU here) reproduces its columns of the
