@@ -573,17 +573,71 @@ def main() -> None:
                 for i in idx:
                     y_host[i].copy_(ys[i], non_blocking=True)
 
-    for _ in range(2):
-        e2e_step()
-    torch.cuda.synchronize()
-    e2e_ev = [(mk(), mk()) for _ in range(K)]
-    for k in range(K):
-        flush.zero_()
-        e2e_ev[k][0].record(stream)
-        e2e_step()
-        e2e_ev[k][1].record(stream)
-    torch.cuda.synchronize()
-    e2e_ms = torch.tensor([sum(a.elapsed_time(b) for a, b in e2e_ev)], device=dev, dtype=torch.float64)
+    if world == 1 and T >= 128:
+        # Two steps in flight, as a server would run them: step k+1's inputs
+        # cross PCIe on one copy stream while step k computes, and each
+        # projection's y leaves on a second copy stream as soon as it is
+        # written (H2D and D2H use separate copy engines).  Every step still
+        # moves all of its inputs in and all of its outputs out; x and y are
+        # larger than L2, so no flush is needed between steps.  (Decode-sized
+        # steps are bound by host launch overhead, which the extra streams and
+        # events would only add to: they run one after another below.)
+        s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+        xb = [{r: torch.empty_like(xin[r]) for r in xin} for _ in range(2)]
+        yb = [[torch.empty_like(ys[i]) for i in range(len(specs))] for _ in range(2)]
+        ev_in = [torch.cuda.Event() for _ in range(2)]    # inputs of buffer b landed
+        ev_read = [torch.cuda.Event() for _ in range(2)]  # step on buffer b no longer reads x
+        ev_out = [torch.cuda.Event() for _ in range(2)]   # outputs of buffer b copied out
+        ev_y = [[torch.cuda.Event() for _ in specs] for _ in range(2)]
+
+        def e2e_pipelined(k: int) -> None:
+            b = k & 1
+            if k >= 2:
+                s_in.wait_event(ev_read[b])
+            with torch.cuda.stream(s_in):
+                for r in xin:
+                    xb[b][r].copy_(x_host[r], non_blocking=True)
+            ev_in[b].record(s_in)
+            stream.wait_event(ev_in[b])
+            if k >= 2:
+                stream.wait_event(ev_out[b])
+            for r, idx in members.items():
+                if r in groups:
+                    groups[r].forward(xb[b][r], [yb[b][i] for i in idx])
+                else:
+                    for i in idx:
+                        layers[i].forward(xb[b][r], yb[b][i])
+                for i in idx:
+                    ev_y[b][i].record(stream)
+            ev_read[b].record(stream)
+            for i in range(len(specs)):
+                s_out.wait_event(ev_y[b][i])
+                with torch.cuda.stream(s_out):
+                    y_host[i].copy_(yb[b][i], non_blocking=True)
+            ev_out[b].record(s_out)
+
+        for k in range(2):
+            e2e_pipelined(k)
+        torch.cuda.synchronize()
+        t0, t1 = mk(), mk()
+        t0.record(s_in)
+        for k in range(K):
+            e2e_pipelined(k)
+        t1.record(s_out)
+        torch.cuda.synchronize()
+        e2e_ms = torch.tensor([t0.elapsed_time(t1)], device=dev, dtype=torch.float64)
+    else:
+        for _ in range(2):
+            e2e_step()
+        torch.cuda.synchronize()
+        e2e_ev = [(mk(), mk()) for _ in range(K)]
+        for k in range(K):
+            flush.zero_()
+            e2e_ev[k][0].record(stream)
+            e2e_step()
+            e2e_ev[k][1].record(stream)
+        torch.cuda.synchronize()
+        e2e_ms = torch.tensor([sum(a.elapsed_time(b) for a, b in e2e_ev)], device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
     e2e_val = T * K / (e2e_ms.item() / 1e3)
