@@ -49,6 +49,8 @@ class _LRSLinearBase(nn.Module):
         else:
             self.bias = None
         self._desc: ops.LayerDesc | None = None
+        self._group = None  # set by efficient.model.group_projections
+        self._group_index = 0
 
     # ------------------------------------------------------------ kernels --
     def _check_device(self) -> None:
@@ -71,6 +73,8 @@ class _LRSLinearBase(nn.Module):
         return d
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if self._group is not None and x.is_cuda and x.dtype == self.A.dtype:
+            return self._group.output(self._group_index, x)
         return ops.lrs_linear_forward(self._layer_desc(), x)
 
 

@@ -245,3 +245,28 @@ LLAMA_60M = {
     "max_position_embeddings": 1024, "rms_norm_eps": 1e-6, "hidden_act": "silu",
     "tie_word_embeddings": False, "bos_token_id": 0, "eos_token_id": 1, "pad_token_id": None,
 }
+
+
+def compressed_bundle(path, *, n_layers: int = 8, seed: int = 0):
+    """Write a synthetic cfg2 bundle: a randomly initialised LLaMA-60M-shaped
+    model whose 7 × n_layers projections are S+LR (16×16 blocks, 50 % block
+    density, rank 64, N(0, 0.02) weights as ``layer_set("cfg2")``), in the
+    bundle format of ``save_artifact``.  Returns the dense weights
+    ``{name: A·B + S}`` (fp32, CPU) for a reference model."""
+    from .efficient.artifact import save_artifact
+    from .efficient.model import build_model_from_config
+
+    config = dict(LLAMA_60M, num_hidden_layers=n_layers)
+    torch.manual_seed(seed)
+    model = build_model_from_config(config, attn_implementation="sdpa")
+    layers, dense = {}, {}
+    for spec in layer_set("cfg2", seed=seed):
+        if int(spec.name.split(".")[2]) >= n_layers:
+            continue
+        t = spec.tensors("cpu", torch.float32)
+        S = torch.sparse_bsr_tensor(t["crow"], t["col"], t["values_pq"],
+                                    size=(spec.out_features, spec.in_features))
+        layers[spec.name] = {"A": t["A"], "B": t["B"], "S": S, "block_p": spec.block_p, "block_q": spec.block_q}
+        dense[spec.name] = t["A"] @ t["B"] + S.to_dense()
+    save_artifact(path, layers, {"mode": "synthetic"}, model=model, model_config=config)
+    return dense

@@ -223,3 +223,37 @@ def test_layer_api_rejects_cpu_tensors():
     with pytest.raises(ValueError, match="CUDA"):
         LRSLinear(A, B, S.to_sparse_bsr(blocksize=(16, 16)), in_features=96, out_features=64, block_p=16,
                   block_q=16)
+
+
+def test_bundle_round_trip_and_errors(tmp_path):
+    """save_artifact / load_artifact keep the reference's bundle format
+    (ssalaad/efficient/artifact.py:78-118) and its error messages."""
+    from s_salaad_b200.efficient import export_model_config, load_artifact, save_artifact
+
+    model = torch.nn.Sequential(torch.nn.Linear(32, 16), torch.nn.Linear(16, 8))
+    S = torch.zeros(16, 32)
+    S[:16, 16:32] = 0.5
+    layers = {"0": {"A": torch.randn(16, 4), "B": torch.randn(4, 32), "S": S.to_sparse_bsr(blocksize=(16, 16)),
+                    "block_p": 16, "block_q": 16}}
+    config = {"model_type": "llama", "hidden_size": 32, "run_name": "dropped", "tokenizer_id": str(tmp_path)}
+    path = tmp_path / "sub" / "bundle.pt"
+    save_artifact(path, layers, {"mode": "x", "step": 3}, model=model, model_config=config)
+    p = load_artifact(path)
+    assert p["format_version"] == 1 and p["meta"] == {"mode": "x"}
+    assert p["model_config"] == {"model_type": "llama", "hidden_size": 32}
+    assert set(p["base_state_dict"]) == {"0.bias", "1.weight", "1.bias"}
+    assert torch.equal(p["layers"]["0"]["S"].to_dense(), S)
+    assert export_model_config({"tokenizer_id": "org/name", "foo": 1}) == {"tokenizer_id": "org/name"}
+    torch.save({"format_version": 1}, tmp_path / "partial.pt")
+    with pytest.raises(ValueError, match="complete model bundle"):
+        load_artifact(tmp_path / "partial.pt")
+    torch.save({**p, "format_version": 2}, tmp_path / "v2.pt")
+    with pytest.raises(ValueError, match="Unsupported model bundle version"):
+        load_artifact(tmp_path / "v2.pt")
+
+
+def test_efficient_model_requires_cuda(tmp_path):
+    from s_salaad_b200.efficient import build_efficient_model
+
+    with pytest.raises(ValueError, match="CUDA"):
+        build_efficient_model(tmp_path / "missing.pt", device="cpu")
