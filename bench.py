@@ -2,7 +2,7 @@
 """S+LR linear forward benchmark (B200).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload cfg4|cfg3-T<T>|cfg5-T<T>|cfg1|cfg2]
+                    [--workload cfg4|cfg3-T<T>|cfg5-T<T>|cfg1|cfg2|cfg2-model]
 
 Prints ONE JSON line (rank 0).  A step is one forward of the workload's
 layer set over one batch of T synthetic tokens:
@@ -206,6 +206,75 @@ def cpu_reference_run(specs, T_sample: int, steps: int, warmup: int, budget_s: f
 
 # ---------------------------------------------------------------- main --
 
+def model_bench(args) -> None:
+    """cfg2 as a whole model: the 8-layer LLaMA-60M-shaped model of a
+    synthetic bundle, loaded by build_efficient_model (every projection an
+    S+LR layer, q/k/v and gate/up grouped), forward on batch 8 x 256 tokens
+    replayed from a CUDA graph; the same model with dense bf16 weights
+    (cuBLAS) beside it.  One GPU, no reference arm (the reference's CPU model
+    forward is not a kernel comparison)."""
+    import tempfile
+
+    from s_salaad_b200 import workloads
+    from s_salaad_b200.efficient import build_efficient_model, build_model_from_config, load_artifact
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    batch, seq = 8, 256
+    with tempfile.TemporaryDirectory() as d:
+        path = Path(d) / "cfg2.pt"
+        dense = workloads.compressed_bundle(path, n_layers=8)
+        model, config, _ = build_efficient_model(path, device=dev)
+        payload = load_artifact(path)
+        ref = build_model_from_config(payload["model_config"], attn_implementation="sdpa")
+        ref.load_state_dict(payload["base_state_dict"], strict=False)
+        with torch.no_grad():
+            for name, W in dense.items():
+                ref.get_submodule(name).weight.copy_(W)
+        ref = ref.to(device=dev, dtype=torch.bfloat16).eval()
+    g = torch.Generator(device="cpu").manual_seed(0)
+    ids = torch.randint(0, config["vocab_size"], (batch, seq), generator=g).to(dev)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    mk = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
+
+    def timed(m) -> float:
+        with torch.no_grad():
+            side = torch.cuda.Stream(dev)
+            side.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(side):
+                for _ in range(args.warmup):
+                    m(ids)
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph, stream=side):
+                    m(ids)
+            torch.cuda.current_stream(dev).wait_stream(side)
+            for _ in range(3):
+                graph.replay()
+            torch.cuda.synchronize()
+            ev = [(mk(), mk()) for _ in range(args.steps)]
+            for a, b in ev:
+                flush.zero_()
+                a.record()
+                graph.replay()
+                b.record()
+            torch.cuda.synchronize()
+        return sum(a.elapsed_time(b) for a, b in ev) / args.steps
+
+    with ClockSampler(0) as clocks:
+        ms = timed(model)
+    ms_dense = timed(ref)
+    emit({"metric": "compressed LLaMA-60M-shaped model forward tokens/s (cfg2, whole model)",
+          "value": batch * seq / (ms / 1e3), "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
+          "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+          "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded bundle; random ids)",
+          "config": {"workload": "cfg2-model: 8 decoder layers, 56 S+LR projections (16x16 blocks, 50 %, r 64), "
+                                 "batch 8 x seq 256, forward replayed from a CUDA graph",
+                     "l2": "flushed (256 MB write) between timed steps"},
+          "dense_bf16": {"ms_per_step": ms_dense, "value": batch * seq / (ms_dense / 1e3),
+                         "what": "the same model with dense W = A*B + S (torch/cuBLAS), same graph replay"},
+          "clocks": clocks.summary()})
+
+
 def main() -> None:
     # Only the result line goes to stdout: libraries (NCCL, torch) may print
     # there, so fd 1 points at stderr for the run and the line is written to
@@ -235,6 +304,8 @@ def main() -> None:
 
     from s_salaad_b200 import workloads
 
+    if args.workload == "cfg2-model":
+        return model_bench(args)
     cfg, T = parse_workload(args.workload)
     specs = workloads.layer_set(cfg)
     world = int(os.environ.get("WORLD_SIZE", "1"))
