@@ -29,7 +29,7 @@ __device__ unsigned g_status_mma = 0;
 
 constexpr int kConsumerWarps = 8;
 constexpr int kThreads = (kConsumerWarps + 1) * 32;
-constexpr int kStages = 6;
+constexpr int kStages = 6;  // ring slots at most (a launch uses 4..kStages)
 constexpr int kFT = 16;  // output features per CTA (one m16 tile)
 // Low-rank stage layout: A rows (16 x kc, at most 2 KB) at 0, H tile at 2 KB
 // (1024-aligned for its swizzle).
@@ -55,6 +55,7 @@ struct MmaLayer {
 struct MmaArgs {
   int64_t M;
   int n;
+  int stages;  // ring slots of this launch (fewer slots -> more CTAs per SM)
   MmaLayer L[kMaxLayers];
 };
 // Tensor maps: x and H are shared by the layers of a launch (H column
@@ -78,7 +79,7 @@ __device__ __forceinline__ void ldsm_x2(uint32_t addr, uint32_t& r0, uint32_t& r
 // on M, tokens on N); partial sums are reduced across warps in a fixed order.
 //
 // Launched as a programmatic dependent (PDL): before griddepcontrol.wait the
-// CTA touches weights only -- the value and A boxes of the first kStages
+// CTA touches weights only -- the value and A boxes of the first ring-full of
 // stages go to shared memory, those of later stages to L2, bias to shared
 // memory -- so a decode step streams its weights while the previous kernel
 // finishes.  x, H and y are read or written only after the wait.
@@ -109,9 +110,10 @@ __global__ void __launch_bounds__(kThreads)
   uint32_t stage_bytes = v_slot + x_region;
   if (stage_bytes < kHOff + TT * a.kc * 2) stage_bytes = kHOff + TT * a.kc * 2;
   stage_bytes = (stage_bytes + 1023) & ~1023u;
-  float* red = reinterpret_cast<float*>(smem + kStages * stage_bytes);  // [8][16][TT]
+  const int S = ga.stages;
+  float* red = reinterpret_cast<float*>(smem + S * stage_bytes);  // [8][16][TT]
   uint64_t* full = reinterpret_cast<uint64_t*>(red + kConsumerWarps * kFT * TT);
-  uint64_t* empty = full + kStages;
+  uint64_t* empty = full + S;
   __shared__ int s_abort;
   __shared__ float s_bias[kFT];
 
@@ -129,7 +131,7 @@ __global__ void __launch_bounds__(kThreads)
   const int64_t n0 = int64_t(br) * a.bp + f0;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], kConsumerWarps);
     }
@@ -154,7 +156,7 @@ __global__ void __launch_bounds__(kThreads)
         tma_prefetch_desc(&tm_h);
       }
     }
-    const int npre = min(n_total, kStages);
+    const int npre = min(n_total, S);
     // Weights of the first npre stages (fresh slots: no empty-barrier wait).
     int colr[kStages];
 #pragma unroll
@@ -203,9 +205,9 @@ __global__ void __launch_bounds__(kThreads)
     }
     // Remaining stages through the ring.
     for (int s = npre; s < n_total; ++s) {
-      const int slot = s % kStages;
+      const int slot = s % S;
       int ok = 1;
-      if (lane == 0) ok = mbar_wait(&empty[slot], ((s / kStages) & 1) ^ 1) ? 1 : 0;
+      if (lane == 0) ok = mbar_wait(&empty[slot], ((s / S) & 1) ^ 1) ? 1 : 0;
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) {
         if (lane == 0) {
@@ -244,8 +246,8 @@ __global__ void __launch_bounds__(kThreads)
       for (int e = 0; e < 4; ++e) acc[nt][e] = 0.f;
 
     for (int s = 0; s < n_total; ++s) {
-      const int slot = s % kStages;
-      if (!mbar_wait(&full[slot], (s / kStages) & 1)) {
+      const int slot = s % S;
+      if (!mbar_wait(&full[slot], (s / S) & 1)) {
         atomicOr(&g_status_mma, SLR_TIMEOUT_BIT);
         s_abort = 1;
         break;
@@ -489,8 +491,24 @@ int pick_tt(int64_t M) {
 
 struct MmaShape {
   int sb, kc, kx;
-  size_t smem;
+  uint32_t stage;  // bytes of one ring slot
 };
+
+// Dynamic shared memory of a launch with `stages` ring slots of `stage` bytes.
+size_t mma_smem(uint32_t stage, int stages, int tt) {
+  return 1024 + size_t(stages) * stage + sizeof(float) * kConsumerWarps * kFT * tt + 2 * size_t(stages) * 8;
+}
+
+int device_sms() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 1;
+  }
+  return n;
+}
 
 MmaShape mma_shape(int bq, int r, int tt) {
   MmaShape m;
@@ -504,15 +522,33 @@ MmaShape mma_shape(int bq, int r, int tt) {
   const uint32_t x_region = uint32_t(m.sb * (bq / m.kx) * tt * m.kx * 2);
   uint32_t stage = v_slot + x_region;
   if (stage < kHOff + uint32_t(tt * m.kc * 2)) stage = kHOff + uint32_t(tt * m.kc * 2);
-  stage = (stage + 1023) & ~1023u;
-  m.smem = 1024 + size_t(kStages) * stage + sizeof(float) * kConsumerWarps * kFT * tt + 2 * kStages * 8;
+  m.stage = (stage + 1023) & ~1023u;
   return m;
 }
 
+// Ring depth: the full kStages slots unless 4 slots fit enough more CTAs per
+// SM to need fewer waves of the grid (decode grids of several hundred CTAs
+// then run in one wave; a CTA needs a few stages only at small token counts).
 template <int NT, int KX, typename TI, int MODE>
-int launch_inst(const MmaMaps& maps, const MmaArgs& k, size_t smem, dim3 grid, bool pdl, cudaStream_t s) {
+int launch_inst(const MmaMaps& maps, MmaArgs k, uint32_t stage, dim3 grid, bool pdl, cudaStream_t s) {
   auto kern = mma_rowblock_kernel<NT, KX, TI, MODE>;
-  SLR_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+  constexpr int TT = 8 * NT;
+  const size_t smem_full = mma_smem(stage, kStages, TT), smem_low = mma_smem(stage, 4, TT);
+  SLR_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem_full)));
+  // CTAs per SM of this kernel instance at both depths (cached per slot size)
+  thread_local uint32_t c_stage = 0;
+  thread_local int occ_full = 0, occ_low = 0;
+  if (c_stage != stage) {
+    SLR_CHECK_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ_full, kern, kThreads, smem_full));
+    SLR_CHECK_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ_low, kern, kThreads, smem_low));
+    c_stage = stage;
+  }
+  const int64_t ctas = int64_t(grid.x) * grid.y;
+  const int64_t sms = device_sms();
+  const int64_t waves_full = ceil_div(ctas, sms * std::max(occ_full, 1));
+  const int64_t waves_low = ceil_div(ctas, sms * std::max(occ_low, 1));
+  k.stages = waves_low < waves_full ? 4 : kStages;
+  const size_t smem = k.stages == kStages ? smem_full : smem_low;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = dim3(kThreads);
@@ -528,22 +564,22 @@ int launch_inst(const MmaMaps& maps, const MmaArgs& k, size_t smem, dim3 grid, b
 }
 
 template <int KX, typename TI, int MODE>
-int launch_nt(int tt, const MmaMaps& maps, const MmaArgs& k, size_t smem, dim3 grid, bool pdl, cudaStream_t s) {
+int launch_nt(int tt, const MmaMaps& maps, const MmaArgs& k, uint32_t stage, dim3 grid, bool pdl, cudaStream_t s) {
   switch (tt) {
-    case 8: return launch_inst<1, KX, TI, MODE>(maps, k, smem, grid, pdl, s);
-    case 16: return launch_inst<2, KX, TI, MODE>(maps, k, smem, grid, pdl, s);
-    case 32: return launch_inst<4, KX, TI, MODE>(maps, k, smem, grid, pdl, s);
-    default: return launch_inst<8, KX, TI, MODE>(maps, k, smem, grid, pdl, s);
+    case 8: return launch_inst<1, KX, TI, MODE>(maps, k, stage, grid, pdl, s);
+    case 16: return launch_inst<2, KX, TI, MODE>(maps, k, stage, grid, pdl, s);
+    case 32: return launch_inst<4, KX, TI, MODE>(maps, k, stage, grid, pdl, s);
+    default: return launch_inst<8, KX, TI, MODE>(maps, k, stage, grid, pdl, s);
   }
 }
 
 template <typename TI, int MODE>
-int launch_kx(int kx, int tt, const MmaMaps& maps, const MmaArgs& k, size_t smem, dim3 grid, bool pdl,
+int launch_kx(int kx, int tt, const MmaMaps& maps, const MmaArgs& k, uint32_t stage, dim3 grid, bool pdl,
               cudaStream_t s) {
   switch (kx) {
-    case 16: return launch_nt<16, TI, MODE>(tt, maps, k, smem, grid, pdl, s);
-    case 32: return launch_nt<32, TI, MODE>(tt, maps, k, smem, grid, pdl, s);
-    default: return launch_nt<64, TI, MODE>(tt, maps, k, smem, grid, pdl, s);
+    case 16: return launch_nt<16, TI, MODE>(tt, maps, k, stage, grid, pdl, s);
+    case 32: return launch_nt<32, TI, MODE>(tt, maps, k, stage, grid, pdl, s);
+    default: return launch_nt<64, TI, MODE>(tt, maps, k, stage, grid, pdl, s);
   }
 }
 
@@ -551,9 +587,9 @@ bool is_sparse(const RowblockArgs& a) { return a.crow != nullptr && a.nnz > 0; }
 int eff_bq(const RowblockArgs& a) { return is_sparse(a) ? a.bq : 16; }
 
 // Layer `a` as entry li of a launch: its MmaLayer (CTAs from cta0) and its
-// value / A tensor maps.  Returns the layer's dynamic shared memory in *smem.
+// value / A tensor maps.  Returns the layer's ring slot bytes in *stage.
 int fill_layer(const RowblockArgs& a, int tt, int cta0, int64_t h_col, MmaMaps& maps, MmaArgs& k, int li,
-               size_t* smem) {
+               uint32_t* stage) {
   const bool sparse = is_sparse(a);
   const int bq = eff_bq(a);
   const int r = a.mode == MODE_FUSED ? int(a.r) : 0;
@@ -561,7 +597,7 @@ int fill_layer(const RowblockArgs& a, int tt, int cta0, int64_t h_col, MmaMaps& 
   MmaLayer& L = k.L[li];
   L = MmaLayer{a.y, a.bias, sparse ? a.crow : nullptr, a.col, a.rows, a.N, a.ldy,
                a.bp, bq, r, sh.kc, sh.sb, a.bp / kFT, int(a.nrows), cta0, int(h_col)};
-  *smem = sh.smem;
+  *stage = sh.stage;
   int rc;
   if (sparse) {
     rc = make_tmap_2d(&maps.v[li], a.values, a.dtype, uint64_t(a.bp), uint64_t(a.nnz) * a.bq,
@@ -595,15 +631,15 @@ int fill_shared_maps(const RowblockArgs& a0, int tt, int kx, int kc, bool any_sp
   return SLR_OK;
 }
 
-int launch_maps(const RowblockArgs& a0, int kx, int tt, const MmaMaps& maps, const MmaArgs& k, size_t smem,
+int launch_maps(const RowblockArgs& a0, int kx, int tt, const MmaMaps& maps, const MmaArgs& k, uint32_t stage,
                 int ctas, bool pdl, cudaStream_t s) {
   const dim3 grid(unsigned(ctas), unsigned(ceil_div(a0.M, tt)));
   if (a0.dtype == SLR_BF16)
-    return a0.mode == MODE_ADDMM ? launch_kx<__nv_bfloat16, MODE_ADDMM>(kx, tt, maps, k, smem, grid, pdl, s)
-                                 : launch_kx<__nv_bfloat16, MODE_FUSED>(kx, tt, maps, k, smem, grid, pdl, s);
+    return a0.mode == MODE_ADDMM ? launch_kx<__nv_bfloat16, MODE_ADDMM>(kx, tt, maps, k, stage, grid, pdl, s)
+                                 : launch_kx<__nv_bfloat16, MODE_FUSED>(kx, tt, maps, k, stage, grid, pdl, s);
   if (a0.dtype == SLR_F16)
-    return a0.mode == MODE_ADDMM ? launch_kx<__half, MODE_ADDMM>(kx, tt, maps, k, smem, grid, pdl, s)
-                                 : launch_kx<__half, MODE_FUSED>(kx, tt, maps, k, smem, grid, pdl, s);
+    return a0.mode == MODE_ADDMM ? launch_kx<__half, MODE_ADDMM>(kx, tt, maps, k, stage, grid, pdl, s)
+                                 : launch_kx<__half, MODE_FUSED>(kx, tt, maps, k, stage, grid, pdl, s);
   return fail(SLR_ERR_UNSUPPORTED_DTYPE, "mma path: 16-bit dtypes only");
 }
 
@@ -684,12 +720,12 @@ int launch_mma_rowblock(const RowblockArgs& a, bool pdl, cudaStream_t s) {
   MmaArgs k{};
   k.M = a.M;
   k.n = 1;
-  size_t smem = 0;
-  int rc = fill_layer(a, tt, 0, 0, maps, k, 0, &smem);
+  uint32_t stage = 0;
+  int rc = fill_layer(a, tt, 0, 0, maps, k, 0, &stage);
   if (rc) return rc;
   rc = fill_shared_maps(a, tt, sh.kx, r > 0 ? sh.kc : 0, is_sparse(a), a.H, a.ldh, maps);
   if (rc) return rc;
-  return launch_maps(a, sh.kx, tt, maps, k, smem, int(a.nrows * (a.bp / kFT)), pdl, s);
+  return launch_maps(a, sh.kx, tt, maps, k, stage, int(a.nrows * (a.bp / kFT)), pdl, s);
 }
 
 bool mma_group_compatible(const RowblockArgs* a, int n) {
@@ -717,21 +753,21 @@ int launch_mma_rowblock_group(const RowblockArgs* a, const int64_t* h_col, int n
   MmaArgs k{};
   k.M = a[0].M;
   k.n = n;
-  size_t smem = 0;
+  uint32_t stage = 0;
   int ctas = 0;
   bool any_sparse = false;
   for (int i = 0; i < n; ++i) {
-    size_t si = 0;
+    uint32_t si = 0;
     int rc = fill_layer(a[i], tt, ctas, h_col[i], maps, k, i, &si);
     if (rc) return rc;
-    smem = std::max(smem, si);
+    stage = std::max(stage, si);
     ctas += int(a[i].nrows * (a[i].bp / kFT));
     any_sparse = any_sparse || is_sparse(a[i]);
   }
   int rc = fill_shared_maps(a[0], tt, sh.kx, sh.kc, any_sparse, H, ldh, maps);
   if (rc) return rc;
   if (ctas == 0) return SLR_OK;
-  return launch_maps(a[0], sh.kx, tt, maps, k, smem, ctas, pdl, s);
+  return launch_maps(a[0], sh.kx, tt, maps, k, stage, ctas, pdl, s);
 }
 
 int read_and_clear_status_mma(unsigned* out) {
