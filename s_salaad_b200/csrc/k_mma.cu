@@ -9,7 +9,7 @@
 //                       tokens): a producer warp streams the 16-column slice of
 //                       the row's BSR values, the x tiles at those blocks'
 //                       columns, and (fused layer) the row's A rows and H tiles
-//                       through a 6-stage TMA/mbarrier ring; eight consumer
+//                       through a 4- or 6-slot TMA/mbarrier ring; eight consumer
 //                       warps run m16n8k16 MMAs from shared memory only; the
 //                       epilogue adds bias (fused) or the previous `out`
 //                       (in-place operator) and stores once.
