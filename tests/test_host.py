@@ -257,3 +257,27 @@ def test_efficient_model_requires_cuda(tmp_path):
 
     with pytest.raises(ValueError, match="CUDA"):
         build_efficient_model(tmp_path / "missing.pt", device="cpu")
+
+
+def test_peer_call_validation_needs_no_gpu():
+    """slr_peers arguments are checked before anything touches a GPU."""
+    lib = _lib.load()
+    L = _lib.SlrLayer(in_features=256, out_features=256, rank=64, block_p=64, block_q=64, nnz=0,
+                      A=0x1000, B=0x2000, dtype=_lib.SLR_BF16)
+    P = _lib.SlrPeers()
+    call = lambda: lib.slr_lrs_linear_combine_peers(ctypes.byref(L), 0x100, 0, 256, 512, None, 0,  # noqa: E731
+                                                    ctypes.byref(P), None)
+    P.world, P.rank = 1, 0
+    assert call() == _lib.SLR_ERR_INVALID_ARGUMENT and "world" in _lib.last_error()
+    P.world, P.rank = 2, 2
+    assert call() == _lib.SLR_ERR_INVALID_ARGUMENT
+    P.rank = 0
+    assert call() == _lib.SLR_ERR_INVALID_ARGUMENT and "NULL" in _lib.last_error()
+    P.y[0], P.y[1], P.signal[0], P.signal[1] = 0x10000, 0x20008, 0x30000, 0x40000
+    assert call() == _lib.SLR_ERR_INVALID_ARGUMENT and "aligned" in _lib.last_error()
+    assert lib.slr_peers_wait(None, 0, None) == _lib.SLR_ERR_INVALID_ARGUMENT
+    assert lib.slr_lrs_linear_peers_supported(ctypes.byref(L), 0x100, 0, 0) == 0
+    h = (ctypes.c_uint8 * _lib.SLR_IPC_HANDLE_BYTES)()
+    off = ctypes.c_int64()
+    assert lib.slr_ipc_export(None, h, ctypes.byref(off)) == _lib.SLR_ERR_INVALID_ARGUMENT
+    assert lib.slr_ipc_release(bytes(_lib.SLR_IPC_HANDLE_BYTES)) == _lib.SLR_ERR_INVALID_ARGUMENT
