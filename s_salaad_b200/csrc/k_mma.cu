@@ -45,7 +45,8 @@ struct MmaLayer {
   const int32_t* col;
   const int32_t* rows;
   int64_t N, ldy;
-  int bp, bq, r, kc;   // kc: rank chunk per low-rank stage
+  int bp, bq, r, kc;   // kc: rank columns per chunk (one A box + one H box)
+  int lrc;             // chunks per low-rank stage
   int sb;              // value blocks per sparse stage
   int ft_per_row;      // bp / 16
   int nrows;
@@ -106,7 +107,8 @@ __global__ void __launch_bounds__(kThreads)
   const uint32_t v_bytes = uint32_t(a.sb * a.bq * kFT * 2);   // values box of a stage
   const uint32_t v_slot = (v_bytes + 1023) & ~1023u;
   const uint32_t x_region = uint32_t(a.sb * nsub * XB);
-  const uint32_t lr_bytes = uint32_t(kFT * a.kc * 2 + TT * a.kc * 2);
+  const uint32_t chunk_bytes = uint32_t(kFT * a.kc * 2 + TT * a.kc * 2);  // A + H of one chunk
+  const uint32_t cs = (kHOff + TT * a.kc * 2 + 1023) & ~1023u;            // chunk stride in a slot
   uint32_t stage_bytes = v_slot + x_region;
   if (stage_bytes < kHOff + TT * a.kc * 2) stage_bytes = kHOff + TT * a.kc * 2;
   stage_bytes = (stage_bytes + 1023) & ~1023u;
@@ -126,7 +128,10 @@ __global__ void __launch_bounds__(kThreads)
   const int jb0 = a.crow ? a.crow[br] : 0;
   const int nblk = a.crow ? a.crow[br + 1] - jb0 : 0;
   const int n_sp = (nblk + a.sb - 1) / a.sb;
-  const int n_lr = MODE == MODE_FUSED ? (a.r + a.kc - 1) / a.kc : 0;
+  // low-rank stages: lrc chunks of kc rank columns each (chunk c of the
+  // stage at offset c * cs: A rows [16 x kc], then the H tile at kHOff)
+  const int n_chunks = MODE == MODE_FUSED ? (a.r + a.kc - 1) / a.kc : 0;
+  const int n_lr = (n_chunks + a.lrc - 1) / a.lrc;
   const int n_total = n_sp + n_lr;
   const int64_t n0 = int64_t(br) * a.bp + f0;
 
@@ -173,8 +178,10 @@ __global__ void __launch_bounds__(kThreads)
             tma_load_2d(dst, &tm_vals, f0, (jb0 + j0) * a.bq, &full[s]);
           }
         } else if (lane == 0) {
-          mbar_arrive_expect_tx(&full[s], lr_bytes);
-          tma_load_2d(dst, &tm_A, (s - n_sp) * a.kc, br * a.bp + f0, &full[s]);
+          const int c0 = (s - n_sp) * a.lrc, nch = min(a.lrc, n_chunks - c0);
+          mbar_arrive_expect_tx(&full[s], uint32_t(nch) * chunk_bytes);
+          for (int c = 0; c < nch; ++c)
+            tma_load_2d(dst + c * cs, &tm_A, (c0 + c) * a.kc, br * a.bp + f0, &full[s]);
         }
       }
     }
@@ -183,7 +190,8 @@ __global__ void __launch_bounds__(kThreads)
       if (s < n_sp)
         tma_prefetch_l2_2d(&tm_vals, f0, (jb0 + s * a.sb) * a.bq);
       else
-        tma_prefetch_l2_2d(&tm_A, (s - n_sp) * a.kc, br * a.bp + f0);
+        for (int c = (s - n_sp) * a.lrc; c < min(n_chunks, (s - n_sp + 1) * a.lrc); ++c)
+          tma_prefetch_l2_2d(&tm_A, c * a.kc, br * a.bp + f0);
     }
     pdl_wait_primary();  // x and H come from preceding kernels
     __syncwarp();
@@ -199,7 +207,9 @@ __global__ void __launch_bounds__(kThreads)
               tma_load_2d(dst + v_slot + (lane * nsub + h) * XB, &tm_x, colr[s] * a.bq + h * KX, int(t0),
                           &full[s]);
         } else if (lane == 0) {
-          tma_load_2d(dst + kHOff, &tm_h, a.h_col0 + (s - n_sp) * a.kc, int(t0), &full[s]);
+          const int c0 = (s - n_sp) * a.lrc, nch = min(a.lrc, n_chunks - c0);
+          for (int c = 0; c < nch; ++c)
+            tma_load_2d(dst + c * cs + kHOff, &tm_h, a.h_col0 + (c0 + c) * a.kc, int(t0), &full[s]);
         }
       }
     }
@@ -230,10 +240,12 @@ __global__ void __launch_bounds__(kThreads)
           for (int h = 0; h < nsub; ++h)
             tma_load_2d(dst + v_slot + (lane * nsub + h) * XB, &tm_x, c * a.bq + h * KX, int(t0), &full[slot]);
       } else if (lane == 0) {
-        const int l = s - n_sp;
-        mbar_arrive_expect_tx(&full[slot], lr_bytes);
-        tma_load_2d(dst, &tm_A, l * a.kc, br * a.bp + f0, &full[slot]);
-        tma_load_2d(dst + kHOff, &tm_h, a.h_col0 + l * a.kc, int(t0), &full[slot]);
+        const int c0 = (s - n_sp) * a.lrc, nch = min(a.lrc, n_chunks - c0);
+        mbar_arrive_expect_tx(&full[slot], uint32_t(nch) * chunk_bytes);
+        for (int c = 0; c < nch; ++c) {
+          tma_load_2d(dst + c * cs, &tm_A, (c0 + c) * a.kc, br * a.bp + f0, &full[slot]);
+          tma_load_2d(dst + c * cs + kHOff, &tm_h, a.h_col0 + (c0 + c) * a.kc, int(t0), &full[slot]);
+        }
       }
     }
   } else {
@@ -272,17 +284,20 @@ __global__ void __launch_bounds__(kThreads)
           }
         }
       } else {
-        const int steps = a.kc >> 4;
-        const int l = s - n_sp;
+        const int per = a.kc >> 4;              // k16 steps of a chunk
+        const int c0 = (s - n_sp) * a.lrc;
+        const int steps = min(a.lrc, n_chunks - c0) * per;
         const int kcb = a.kc * 2;               // A / H tile row bytes
         for (int kk = warp; kk < steps; kk += kConsumerWarps) {
-          if (l * a.kc + 16 * kk >= a.r) break;
+          const int c = kk / per, k16 = kk - c * per;
+          if ((c0 + c) * a.kc + 16 * k16 >= a.r) break;
+          const uint32_t cb = base + uint32_t(c) * cs;
           uint32_t af[4];
-          ldsm_x4(base + swz_offset((lj & 1) * 8 + li, 2 * kk + (lj >> 1), kcb), af[0], af[1], af[2], af[3]);
+          ldsm_x4(cb + swz_offset((lj & 1) * 8 + li, 2 * k16 + (lj >> 1), kcb), af[0], af[1], af[2], af[3]);
 #pragma unroll
           for (int nt = 0; nt < NT; ++nt) {
             uint32_t b0, b1;
-            ldsm_x2(base + kHOff + swz_offset(8 * nt + li, 2 * kk + (lj & 1), kcb), b0, b1);
+            ldsm_x2(cb + kHOff + swz_offset(8 * nt + li, 2 * k16 + (lj & 1), kcb), b0, b1);
             mma16816<TI>::run(acc[nt], af, b0, b1);
           }
         }
@@ -491,6 +506,7 @@ int pick_tt(int64_t M) {
 
 struct MmaShape {
   int sb, kc, kx;
+  int lrc;         // rank chunks per low-rank stage
   uint32_t stage;  // bytes of one ring slot
 };
 
@@ -523,6 +539,12 @@ MmaShape mma_shape(int bq, int r, int tt) {
   uint32_t stage = v_slot + x_region;
   if (stage < kHOff + uint32_t(tt * m.kc * 2)) stage = kHOff + uint32_t(tt * m.kc * 2);
   m.stage = (stage + 1023) & ~1023u;
+  // As many rank chunks per low-rank stage as the slot holds (fewer ring
+  // rounds per CTA at small token counts, where the slot is sized by the
+  // sparse stages and one chunk fills a quarter of it).
+  const uint32_t cs = (kHOff + uint32_t(tt * m.kc * 2) + 1023) & ~1023u;
+  const int chunks = r > 0 ? (r + m.kc - 1) / m.kc : 1;
+  m.lrc = std::max(1, std::min(chunks, int(m.stage / cs)));
   return m;
 }
 
@@ -596,7 +618,7 @@ int fill_layer(const RowblockArgs& a, int tt, int cta0, int64_t h_col, MmaMaps& 
   const MmaShape sh = mma_shape(bq, r, tt);
   MmaLayer& L = k.L[li];
   L = MmaLayer{a.y, a.bias, sparse ? a.crow : nullptr, a.col, a.rows, a.N, a.ldy,
-               a.bp, bq, r, sh.kc, sh.sb, a.bp / kFT, int(a.nrows), cta0, int(h_col)};
+               a.bp, bq, r, sh.kc, sh.lrc, sh.sb, a.bp / kFT, int(a.nrows), cta0, int(h_col)};
   *stage = sh.stage;
   int rc;
   if (sparse) {
