@@ -172,10 +172,10 @@ typedef struct slr_layer {
 } slr_layer;
 
 /*
- * Workspace bytes that slr_lrs_linear_forward needs for M tokens.  The
- * workspace must be 256-byte aligned, zero-filled before its FIRST use (the
- * library leaves its counters at zero after every call), and not shared by
- * calls that may overlap on the GPU.
+ * Workspace bytes that slr_lrs_linear_forward needs for M tokens (it holds
+ * H = x·Bᵀ between the two phases).  The workspace must be 256-byte aligned
+ * and not shared by calls that may overlap on the GPU; it needs no
+ * initialisation.
  */
 SLR_API size_t slr_lrs_linear_workspace_size(const slr_layer* layer, int64_t M);
 

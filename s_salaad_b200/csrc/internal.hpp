@@ -55,14 +55,11 @@ struct HSmallPlan {
   int seg_rt[kMaxGroupLayers + 1] = {};
   int ks[kMaxGroupLayers] = {};
   int64_t kchunk[kMaxGroupLayers] = {};
-  size_t part_floats = 0;
-  size_t counters = 0;
 };
 // ldh[s]: columns of H owned by segment s (a multiple of 16, >= r_s).
 HSmallPlan plan_h_small(int64_t M, int64_t K, const int64_t* ldh, int nseg);
-int launch_h_small(const void* x, int64_t ldx, const void* const* B, const int64_t* r, void* H, float* part,
-                   unsigned* counters, int64_t M, int64_t K, int64_t ldh, const HSmallPlan& plan, int dtype,
-                   bool pdl, cudaStream_t s);
+int launch_h_small(const void* x, int64_t ldx, const void* const* B, const int64_t* r, void* H, int64_t M,
+                   int64_t K, int64_t ldh, const HSmallPlan& plan, int dtype, bool pdl, cudaStream_t s);
 bool mma_rowblock_supported(int bp, int bq, int64_t K, int64_t r);
 int launch_mma_rowblock(const RowblockArgs& a, bool pdl, cudaStream_t s);
 // Layers that read one x and one H [M, ldh] (layer i's columns from h_col[i])

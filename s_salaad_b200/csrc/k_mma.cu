@@ -3,8 +3,8 @@
 // n8 tile and the weights stream from HBM exactly once.
 //
 //   h_small_kernel      H[M, ldh] = x · Bᵀ (rounded to the I/O dtype): split-K
-//                       over the CTAs, partial sums reduced deterministically
-//                       by the last CTA of each 16-row tile (fixed order).
+//                       over the CTAs of a cluster, partial sums reduced
+//                       through distributed shared memory in a fixed order.
 //   mma_rowblock_kernel one CTA per (16 output features of a block-row, <=64
 //                       tokens): a producer warp streams the 16-column slice of
 //                       the row's BSR values, the x tiles at those blocks'
@@ -21,6 +21,7 @@
 #include <algorithm>
 
 #include "internal.hpp"
+#include "tcgen05.cuh"
 
 namespace slr {
 namespace {
@@ -36,6 +37,7 @@ constexpr int kFT = 16;  // output features per CTA (one m16 tile)
 constexpr uint32_t kHOff = 2048;
 
 constexpr int kMaxLayers = kMaxGroupLayers;  // layers (sharing x) per launch
+constexpr int kMaxKSplit = 8;                 // h_small K-chunks per tile (one cluster)
 
 // One layer of a launch; its CTAs are [cta0, cta0 + nrows * ft_per_row).
 struct MmaLayer {
@@ -348,8 +350,6 @@ struct HArgs {
   const void* x;
   const void* B[kMaxLayers];
   void* H;
-  float* part;        // [rt * tc][ks_max][16][TT] split-K partials
-  unsigned* counters; // [rt * tc]
   int64_t M, K, ldx;
   int64_t kchunk[kMaxLayers];
   int r[kMaxLayers];
@@ -362,114 +362,108 @@ __device__ __forceinline__ uint4 ldg_u128(const void* p) {
   return __ldg(static_cast<const uint4*>(p));
 }
 
+// A float in another CTA's shared memory (shared::cluster address from mapa).
+__device__ __forceinline__ float ld_shared_cluster_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+
 // One CTA (4 warps) = 16 rows of B x one K-chunk x 8*NT tokens.  Each lane
 // loads 16 contiguous bytes of a B row and of an x row per 32-wide k slice
 // and feeds them to two m16n8k16 MMAs; both operands use the same k order
-// inside the slice, which leaves the dot product unchanged.
+// inside the slice, which leaves the dot product unchanged.  The K-chunks of
+// a tile are the CTAs of one cluster (gridDim.y = ks_max): each leaves its
+// partial sum in shared memory and CTA 0 of the cluster adds them in chunk
+// order through distributed shared memory and writes H.
 template <int NT, typename TI>
 __global__ void __launch_bounds__(128) h_small_kernel(const __grid_constant__ HArgs a) {
   pdl_launch_dependents();
   constexpr int TT = 8 * NT;
   __shared__ float red[4][16][TT];
-  __shared__ int s_last;
+  __shared__ float part[16 * TT];  // this CTA's partial sum, [t][m]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, tig = lane & 3;
-  const int rt = blockIdx.x, ks = blockIdx.y, tc = blockIdx.z;
+  const int rt = blockIdx.x, ks = blockIdx.y, tc = blockIdx.z;  // ks = rank in the cluster
   int sg = 0;
   while (sg + 1 < a.nseg && rt >= a.seg_rt[sg + 1]) ++sg;
   const int nks = a.ks[sg];
-  if (ks >= nks) return;  // this segment splits K into fewer chunks
-  const int rho0 = 16 * rt;
-  const int64_t t0 = int64_t(tc) * TT;
-  const int64_t kb = int64_t(ks) * a.kchunk[sg];
-  const int64_t ke = min(a.K, kb + a.kchunk[sg]);
-  const TI* __restrict__ x = static_cast<const TI*>(a.x);
-  const TI* __restrict__ B = static_cast<const TI*>(a.B[sg]);
-  const int lrow = 16 * (rt - a.seg_rt[sg]);  // first row of this tile within B_sg
-  const bool v0 = lrow + g < a.r[sg], v1 = lrow + g + 8 < a.r[sg];
-  const TI* B0 = B + int64_t(lrow + g) * a.K;
-  const TI* B1 = B + int64_t(lrow + g + 8) * a.K;
+  if (ks < nks) {  // CTAs past the segment's K split only take part in the cluster barriers
+    const int64_t t0 = int64_t(tc) * TT;
+    const int64_t kb = int64_t(ks) * a.kchunk[sg];
+    const int64_t ke = min(a.K, kb + a.kchunk[sg]);
+    const TI* __restrict__ x = static_cast<const TI*>(a.x);
+    const TI* __restrict__ B = static_cast<const TI*>(a.B[sg]);
+    const int lrow = 16 * (rt - a.seg_rt[sg]);  // first row of this tile within B_sg
+    const bool v0 = lrow + g < a.r[sg], v1 = lrow + g + 8 < a.r[sg];
+    const TI* B0 = B + int64_t(lrow + g) * a.K;
+    const TI* B1 = B + int64_t(lrow + g + 8) * a.K;
 
-  float acc[NT][4];
-#pragma unroll
-  for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-    for (int e = 0; e < 4; ++e) acc[nt][e] = 0.f;
+    float acc[NT][4];
+  #pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+  #pragma unroll
+      for (int e = 0; e < 4; ++e) acc[nt][e] = 0.f;
 
-  const uint4 z = make_uint4(0, 0, 0, 0);
-  auto step = [&](int64_t kk, bool kin, const uint4& A0, const uint4& A1) {
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-      const int64_t t = t0 + 8 * nt + g;
-      const uint4 X = (t < a.M && kin) ? ldg_u128(x + t * a.ldx + kk) : z;
-      const uint32_t s0[4] = {A0.x, A1.x, A0.y, A1.y};
-      const uint32_t s1[4] = {A0.z, A1.z, A0.w, A1.w};
-      mma16816<TI>::run(acc[nt], s0, X.x, X.y);
-      mma16816<TI>::run(acc[nt], s1, X.z, X.w);
+    const uint4 z = make_uint4(0, 0, 0, 0);
+    auto step = [&](int64_t kk, bool kin, const uint4& A0, const uint4& A1) {
+  #pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        const int64_t t = t0 + 8 * nt + g;
+        const uint4 X = (t < a.M && kin) ? ldg_u128(x + t * a.ldx + kk) : z;
+        const uint32_t s0[4] = {A0.x, A1.x, A0.y, A1.y};
+        const uint32_t s1[4] = {A0.z, A1.z, A0.w, A1.w};
+        mma16816<TI>::run(acc[nt], s0, X.x, X.y);
+        mma16816<TI>::run(acc[nt], s1, X.z, X.w);
+      }
+    };
+    // B (a weight) for the first kPre slices is loaded before griddepcontrol.wait,
+    // overlapping the preceding kernel; x only after it.
+    constexpr int kPre = 4;
+    uint4 pa0[kPre], pa1[kPre];
+  #pragma unroll
+    for (int i = 0; i < kPre; ++i) {
+      const int64_t k = kb + 32 * warp + 128 * i;
+      const int64_t kk = k + 8 * tig;
+      const bool kin = k < ke && kk < ke;
+      pa0[i] = (v0 && kin) ? ldg_u128(B0 + kk) : z;
+      pa1[i] = (v1 && kin) ? ldg_u128(B1 + kk) : z;
     }
-  };
-  // B (a weight) for the first kPre slices is loaded before griddepcontrol.wait,
-  // overlapping the preceding kernel; x only after it.
-  constexpr int kPre = 4;
-  uint4 pa0[kPre], pa1[kPre];
-#pragma unroll
-  for (int i = 0; i < kPre; ++i) {
-    const int64_t k = kb + 32 * warp + 128 * i;
-    const int64_t kk = k + 8 * tig;
-    const bool kin = k < ke && kk < ke;
-    pa0[i] = (v0 && kin) ? ldg_u128(B0 + kk) : z;
-    pa1[i] = (v1 && kin) ? ldg_u128(B1 + kk) : z;
-  }
-  pdl_wait_primary();
-#pragma unroll
-  for (int i = 0; i < kPre; ++i) {
-    const int64_t k = kb + 32 * warp + 128 * i;
-    if (k < ke) step(k + 8 * tig, k + 8 * tig < ke, pa0[i], pa1[i]);
-  }
-  for (int64_t k = kb + 32 * warp + 128 * kPre; k < ke; k += 128) {
-    const int64_t kk = k + 8 * tig;
-    const bool kin = kk < ke;
-    step(kk, kin, (v0 && kin) ? ldg_u128(B0 + kk) : z, (v1 && kin) ? ldg_u128(B1 + kk) : z);
-  }
-#pragma unroll
-  for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-    for (int e = 0; e < 4; ++e)
-      red[warp][g + ((e & 2) ? 8 : 0)][8 * nt + 2 * tig + (e & 1)] = acc[nt][e];
-  __syncthreads();
-
-  TI* __restrict__ H = static_cast<TI*>(a.H);
-  if (nks == 1) {
+    pdl_wait_primary();
+  #pragma unroll
+    for (int i = 0; i < kPre; ++i) {
+      const int64_t k = kb + 32 * warp + 128 * i;
+      if (k < ke) step(k + 8 * tig, k + 8 * tig < ke, pa0[i], pa1[i]);
+    }
+    for (int64_t k = kb + 32 * warp + 128 * kPre; k < ke; k += 128) {
+      const int64_t kk = k + 8 * tig;
+      const bool kin = kk < ke;
+      step(kk, kin, (v0 && kin) ? ldg_u128(B0 + kk) : z, (v1 && kin) ? ldg_u128(B1 + kk) : z);
+    }
+  #pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+  #pragma unroll
+      for (int e = 0; e < 4; ++e)
+        red[warp][g + ((e & 2) ? 8 : 0)][8 * nt + 2 * tig + (e & 1)] = acc[nt][e];
+    __syncthreads();
     for (int idx = threadIdx.x; idx < 16 * TT; idx += 128) {
       const int m = idx % 16, t = idx / 16;
-      const float v = ((red[0][m][t] + red[1][m][t]) + red[2][m][t]) + red[3][m][t];
+      part[idx] = ((red[0][m][t] + red[1][m][t]) + red[2][m][t]) + red[3][m][t];
+    }
+  }  // ks < nks
+  tc::cluster_sync();  // every partial is in its CTA's shared memory
+  if (ks == 0) {
+    TI* __restrict__ H = static_cast<TI*>(a.H);
+    const int64_t t0 = int64_t(tc) * TT;
+    const int rho0 = 16 * rt;
+    for (int idx = threadIdx.x; idx < 16 * TT; idx += 128) {
+      const int m = idx % 16, t = idx / 16;
+      float v = part[idx];
+      for (int k = 1; k < nks; ++k) v += ld_shared_cluster_f32(tc::mapa(smem_u32(&part[idx]), uint32_t(k)));
       if (t0 + t < a.M) H[(t0 + t) * a.ldh + rho0 + m] = from_f<TI>(v);
     }
-    return;
   }
-  // Split-K: publish this CTA's partial, the last CTA of the tile reduces.
-  const int tile = tc * a.rt + rt;
-  float* part = a.part + size_t(tile) * a.ks_max * 16 * TT;
-  for (int idx = threadIdx.x; idx < 16 * TT; idx += 128) {
-    const int m = idx % 16, t = idx / 16;
-    part[size_t(ks) * 16 * TT + idx] = ((red[0][m][t] + red[1][m][t]) + red[2][m][t]) + red[3][m][t];
-  }
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    const unsigned prev = atomicAdd(&a.counters[tile], 1u);
-    s_last = prev == unsigned(nks - 1);
-  }
-  __syncthreads();
-  if (!s_last) return;
-  __threadfence();
-  for (int idx = threadIdx.x; idx < 16 * TT; idx += 128) {
-    const int m = idx % 16, t = idx / 16;
-    float v = 0.f;
-    for (int k = 0; k < nks; ++k) v += __ldcg(part + size_t(k) * 16 * TT + idx);
-    if (t0 + t < a.M) H[(t0 + t) * a.ldh + rho0 + m] = from_f<TI>(v);
-  }
-  if (threadIdx.x == 0) a.counters[tile] = 0u;  // ready for the next call
+  tc::cluster_sync();  // no CTA leaves while CTA 0 may still read its partial
 }
 
 template <int NT, typename TI>
@@ -478,11 +472,15 @@ int launch_h_small_inst(const HArgs& a, dim3 grid, bool pdl, cudaStream_t s) {
   cfg.gridDim = grid;
   cfg.blockDim = dim3(128);
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;  // the K-chunks of a tile
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = grid.y;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = pdl ? 1 : 0;
+  cfg.numAttrs = pdl ? 2 : 1;
   SLR_CHECK_CUDA(cudaLaunchKernelEx(&cfg, h_small_kernel<NT, TI>, a));
   return SLR_OK;
 }
@@ -672,7 +670,8 @@ HSmallPlan plan_h_small(int64_t M, int64_t K, const int64_t* ldh, int nseg) {
   p.tt = pick_tt(M);
   p.tc = int(ceil_div(std::max<int64_t>(M, 1), p.tt));
   p.nseg = nseg;
-  const int64_t max_split = std::max<int64_t>(1, ceil_div(K, 128));
+  // at most 8 K-chunks: they reduce within one (portable-size) cluster
+  const int64_t max_split = std::min<int64_t>(kMaxKSplit, std::max<int64_t>(1, ceil_div(K, 128)));
   for (int sg = 0; sg < nseg; ++sg) {
     const int rt = int(ldh[sg] / 16);
     p.seg_rt[sg] = p.rt;
@@ -686,23 +685,17 @@ HSmallPlan plan_h_small(int64_t M, int64_t K, const int64_t* ldh, int nseg) {
     p.ks_max = std::max(p.ks_max, p.ks[sg]);
   }
   p.seg_rt[nseg] = p.rt;
-  const size_t tiles = size_t(p.rt) * p.tc;
-  p.part_floats = p.ks_max > 1 ? tiles * p.ks_max * 16 * p.tt : 0;
-  p.counters = p.ks_max > 1 ? tiles : 0;
   return p;
 }
 
-int launch_h_small(const void* x, int64_t ldx, const void* const* B, const int64_t* r, void* H, float* part,
-                   unsigned* counters, int64_t M, int64_t K, int64_t ldh, const HSmallPlan& plan, int dtype,
-                   bool pdl, cudaStream_t s) {
+int launch_h_small(const void* x, int64_t ldx, const void* const* B, const int64_t* r, void* H, int64_t M,
+                   int64_t K, int64_t ldh, const HSmallPlan& plan, int dtype, bool pdl, cudaStream_t s) {
   if (M <= 0 || plan.rt <= 0) return SLR_OK;
   if (plan.nseg < 1 || plan.nseg > kMaxLayers || int64_t(plan.rt) * 16 > ldh)
     return fail(SLR_ERR_INVALID_ARGUMENT, "h_small: bad segment plan");
   HArgs a{};
   a.x = x;
   a.H = H;
-  a.part = part;
-  a.counters = counters;
   a.M = M;
   a.K = K;
   a.ldx = ldx;

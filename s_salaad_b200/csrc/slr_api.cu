@@ -102,8 +102,6 @@ struct FwdPlan {
   int path = 0;          // 0 = simt, 1 = mma (small M)
   int64_t ldh = 0;       // row stride of H
   size_t h_bytes = 0;
-  size_t part_off = 0, part_bytes = 0;
-  size_t cnt_off = 0, cnt_bytes = 0;
   size_t total = 0;
   int row_bp = 0;        // block-row height used by the kernels
   HSmallPlan hs;
@@ -134,14 +132,8 @@ FwdPlan plan_forward(const slr_layer& L, int64_t M, const void* x) {
   p.ldh = L.rank > 0 ? round_up(L.rank, 64) : 0;
   const size_t hes = (p.path == 0 && !is16) ? 4 : dtype_size(L.dtype);
   p.h_bytes = align256(size_t(std::max<int64_t>(M, 0)) * p.ldh * hes);
-  p.part_off = p.h_bytes;
-  if (p.path == 1 && L.rank > 0) {
-    p.hs = plan_h_small(M, L.in_features, &p.ldh, 1);
-    p.part_bytes = align256(p.hs.part_floats * sizeof(float));
-    p.cnt_bytes = align256(p.hs.counters * sizeof(unsigned));
-  }
-  p.cnt_off = p.part_off + p.part_bytes;
-  p.total = p.cnt_off + p.cnt_bytes;
+  if (p.path == 1 && L.rank > 0) p.hs = plan_h_small(M, L.in_features, &p.ldh, 1);
+  p.total = p.h_bytes;
   return p;
 }
 
@@ -312,8 +304,6 @@ struct FwdCall {
   FwdPlan p;
   RowblockArgs a;
   uint8_t* ws = nullptr;
-  float* part = nullptr;        // h_small split-K partials
-  unsigned* counters = nullptr; // h_small tile counters (zero between calls)
 };
 
 int prepare_forward(const slr_layer* layer, const void* x, int64_t ldx, void* y, int64_t ldy, int64_t M,
@@ -337,8 +327,6 @@ int prepare_forward(const slr_layer* layer, const void* x, int64_t ldx, void* y,
     if (reinterpret_cast<uintptr_t>(workspace) & 255u) return fail(SLR_ERR_WORKSPACE, "workspace must be 256-byte aligned");
   }
   c.ws = static_cast<uint8_t*>(workspace);
-  c.part = reinterpret_cast<float*>(c.ws + c.p.part_off);
-  c.counters = reinterpret_cast<unsigned*>(c.ws + c.p.cnt_off);
   RowblockArgs& a = c.a;
   a.x = x;
   a.y = y;
@@ -400,7 +388,7 @@ int run_lowrank(const slr_layer& L, const FwdCall& c, cudaStream_t s) {
   if (c.p.path == 1) {
     const void* B = L.B;
     const int64_t r = L.rank;
-    return launch_h_small(c.a.x, c.a.ldx, &B, &r, c.ws, c.part, c.counters, c.a.M, L.in_features, c.p.ldh, c.p.hs,
+    return launch_h_small(c.a.x, c.a.ldx, &B, &r, c.ws, c.a.M, L.in_features, c.p.ldh, c.p.hs,
                           L.dtype, early_start(L) && small_batch_path(L, c), s);
   }
   return launch_simt_h(c.a.x, c.a.ldx, L.B, c.ws, c.a.M, L.in_features, L.rank, c.p.ldh, L.dtype,
@@ -459,21 +447,14 @@ constexpr int kMaxGroup = kMaxGroupLayers;  // layers per grouped call
 // by M (and the layers' paths):
 //   TC    (M >= 128): the group's H [M, ldh_all] (layer i owns columns
 //         [col[i], col[i] + round_up(r_i, 64))), written by one tensor-core GEMM;
-//   SMALL (M < 128): the same H, then the split-K partials of one grouped
-//         small-batch x*B^T;
+//   SMALL (M < 128): the same H, written by one grouped small-batch x*B^T;
 //   EACH: each layer's own workspace one after another (one forward per layer).
-// The h_small tile counters of SMALL and EACH live in a region after all of
-// them that no layout writes otherwise: they must stay zero between calls, and
-// a call in one layout must not clobber the counters of another.
 struct GroupPlan {
   int64_t ldh_all = 0;
   int64_t col[kMaxGroup] = {};
   size_t h_bytes = 0;
   HSmallPlan hs;                  // SMALL: all layers as segments of one x*B^T
-  size_t small_part_bytes = 0;    // at h_bytes
   size_t off[kMaxGroup] = {}, bytes[kMaxGroup] = {};
-  size_t cnt_base = 0;
-  size_t cnt_each[kMaxGroup] = {};  // EACH: layer i's counters at cnt_base + cnt_each[i]
   size_t total = 0;
 };
 
@@ -494,23 +475,14 @@ int plan_group(const slr_layer* layers, int n, int64_t M, GroupPlan& g) {
     g.ldh_all += ldh[i];
   }
   g.h_bytes = align256(size_t(M) * size_t(g.ldh_all) * dtype_size(layers[0].dtype));
-  size_t cnt_small = 0;
-  if (M < kTcMinTokens && layers[0].dtype != SLR_F32) {
-    g.hs = plan_h_small(M, layers[0].in_features, ldh, n);
-    g.small_part_bytes = align256(g.hs.part_floats * sizeof(float));
-    cnt_small = align256(g.hs.counters * sizeof(unsigned));
-  }
-  size_t off = 0, cnt = 0;
+  if (M < kTcMinTokens && layers[0].dtype != SLR_F32) g.hs = plan_h_small(M, layers[0].in_features, ldh, n);
+  size_t off = 0;
   for (int i = 0; i < n; ++i) {
-    const FwdPlan p = plan_forward(layers[i], M, nullptr);
     g.off[i] = off;
-    g.bytes[i] = p.total;
-    off += align256(p.total);
-    g.cnt_each[i] = cnt;
-    cnt += p.cnt_bytes;
+    g.bytes[i] = plan_forward(layers[i], M, nullptr).total;
+    off += align256(g.bytes[i]);
   }
-  g.cnt_base = std::max(g.h_bytes + g.small_part_bytes, off);
-  g.total = g.cnt_base + std::max(cnt, cnt_small);
+  g.total = std::max(g.h_bytes, off);
   return SLR_OK;
 }
 
@@ -573,7 +545,6 @@ int prepare_group(const slr_layer* layers, int n, const void* x, int64_t ldx, vo
     rc = prepare_forward(&layers[i], x, ldx, y ? y[i] : nullptr, ldy ? ldy[i] : 0, M, gc.ws + gc.g.off[i],
                          gc.g.bytes[i], y != nullptr, gc.c[i], mode == GROUP_EACH);
     if (rc) return rc;
-    gc.c[i].counters = reinterpret_cast<unsigned*>(gc.ws + gc.g.cnt_base + gc.g.cnt_each[i]);
   }
   gc.mode = mode;
   if (mode != GROUP_EACH)
@@ -608,9 +579,8 @@ int group_lowrank(const slr_layer* layers, int n, const GroupCall& gc, cudaStrea
   if (gc.mode == GROUP_TC)
     return launch_tc_dense_group(a0.x, a0.ldx, Bs, rs, n, gc.ws, a0.M, layers[0].in_features, gc.g.ldh_all,
                                  layers[0].dtype, s);
-  return launch_h_small(a0.x, a0.ldx, Bs, rs, gc.ws, reinterpret_cast<float*>(gc.ws + gc.g.h_bytes),
-                        reinterpret_cast<unsigned*>(gc.ws + gc.g.cnt_base), a0.M, layers[0].in_features,
-                        gc.g.ldh_all, gc.g.hs, layers[0].dtype, group_early_start(layers, n), s);
+  return launch_h_small(a0.x, a0.ldx, Bs, rs, gc.ws, a0.M, layers[0].in_features, gc.g.ldh_all, gc.g.hs,
+                        layers[0].dtype, group_early_start(layers, n), s);
 }
 
 // Combine phase of every layer: one small-batch launch over all of them when
@@ -676,7 +646,6 @@ int slr_lrs_linear_group_combine(const slr_layer* layers, int n, int i, const vo
   if (rc) return rc;
   c.a.H = gc.c[i].a.H;
   c.a.ldh = gc.c[i].a.ldh;
-  c.counters = gc.c[i].counters;
   return run_combine(layers[i], c, false, static_cast<cudaStream_t>(stream));
 }
 

@@ -6,8 +6,7 @@
 // stream capture is active (an allocation there would break the capture), or
 // a latency-critical serving loop that must never enter the driver's
 // allocator.  This entry point takes no workspace.  Its scratch — the
-// low-rank intermediate H = x·Bᵀ plus, for small token counts, the split-K
-// partial sums and their counters — lives in one fixed array inside this
+// low-rank intermediate H = x·Bᵀ — lives in one fixed array inside this
 // library's device image, kScratchBytes per device.
 //
 // Behaviour a caller must know:
@@ -16,10 +15,9 @@
 //  * The first call on a device looks up the array's device address for that
 //    device (cudaGetSymbolAddress, with the device current); make that first
 //    call before any stream capture.
-//  * All calls share the one array and it keeps the previous call's contents.
-//    Each call clears the part it needs (a memset on the caller's stream);
-//    calls that may run at the same time on the GPU (different streams, or
-//    several devices' work aliased by the caller) race on it.
+//  * All calls share the one array; calls that may run at the same time on
+//    the GPU (different streams, or several devices' work aliased by the
+//    caller) race on it.
 //  * A call whose token count needs more scratch than the array holds is
 //    rejected with SLR_ERR_WORKSPACE before anything is launched.
 #include <mutex>
@@ -69,8 +67,6 @@ extern "C" int slr_lrs_linear_forward_noalloc(const slr_layer* layer, const void
   if (need > 0) {
     int rc = scratch_address(&ws);
     if (rc) return rc;
-    // The previous call's contents are still there: restart the counters (and H) at zero.
-    SLR_CHECK_CUDA(cudaMemsetAsync(ws, 0, need, static_cast<cudaStream_t>(stream)));
   }
   return slr_lrs_linear_forward(layer, x, ldx, y, ldy, M, ws, need > 0 ? kScratchBytes : 0, stream);
 }

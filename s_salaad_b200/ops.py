@@ -183,8 +183,7 @@ class LayerDesc:
         if need == 0:
             return None
         if self._ws is None or self._ws.numel() < need or self._ws.device != self.device:
-            # zero-filled once: the library keeps its split-K counters at zero
-            self._ws = torch.zeros(need, dtype=torch.uint8, device=self.device)
+            self._ws = torch.empty(need, dtype=torch.uint8, device=self.device)
         return self._ws
 
     @staticmethod
