@@ -130,8 +130,9 @@ class ShardedLayer(ShardPlan):
         if self.rank_r == 0 or ws is None:
             return
         tp = T // self.world
-        # token split only on the tensor-core path (>= 128 rows per rank): the small-M
-        # path keeps split-K counters after its H rows, which the H all-gather would overwrite
+        # token split only on the tensor-core path (>= 128 rows per rank): there the H
+        # of a token slice equals those rows of the whole H bit for bit (the small-M
+        # kernel splits K by the token count)
         if self.split_lowrank and self.world > 1 and T % self.world == 0 and tp >= 128 and x2.stride(1) == 1:
             ldh = (self.rank_r + 63) // 64 * 64
             hbytes = T * ldh * x2.element_size()

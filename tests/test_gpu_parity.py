@@ -365,8 +365,8 @@ def test_group_forward_equals_per_layer(cuda, group, T):
         assert torch.equal(y, ref)
         assert torch.equal(grp.combine(i, x, torch.empty_like(ref)), ref)
     if T < 128:
-        # a call in the per-layer layout (x rows not 16-byte aligned: SIMT
-        # path) leaves the split-K counters of the grouped layout intact
+        # calls alternating between the per-layer layout (x rows not 16-byte
+        # aligned: SIMT path) and the grouped one on one workspace
         wide = torch.zeros(T, specs[0].in_features + 1, dtype=x.dtype, device=cuda)
         wide[:, :-1] = x
         xo = wide[:, :-1]
