@@ -559,6 +559,15 @@ def test_reference_operator_name(cuda, oracle):
                                                         t["S_values"].to(cuda), t["S_active_rows"].to(cuda))
     assert_16bit_close(y, torch.from_numpy(ref))
     assert get_tuned_config(32, 32)["BM"] == 1
+    # the fused layer as one operator equals the layer descriptor's forward
+    d = desc_for(t, spec, cuda, torch.bfloat16)
+    dt = d.tensors
+    xs = x.to(cuda)
+    yo = torch.ops.ssalaad.slr_linear(xs, dt["A"], dt["B"], dt["bias"], dt["crow"], dt["col"], dt["values"], 32, 32)
+    assert torch.equal(yo, d.forward(xs))
+    lr = ops.LayerDesc(A=dt["A"], B=dt["B"], in_features=128, out_features=128)
+    yl = torch.ops.ssalaad.slr_linear(xs, dt["A"], dt["B"], None, None, None, None, 0, 0)
+    assert torch.equal(yl, lr.forward(xs))
 
 
 # ------------------------------------------------- tcgen05 (M >= 128) path --

@@ -281,3 +281,16 @@ def test_peer_call_validation_needs_no_gpu():
     off = ctypes.c_int64()
     assert lib.slr_ipc_export(None, h, ctypes.byref(off)) == _lib.SLR_ERR_INVALID_ARGUMENT
     assert lib.slr_ipc_release(bytes(_lib.SLR_IPC_HANDLE_BYTES)) == _lib.SLR_ERR_INVALID_ARGUMENT
+
+
+def test_operators_register_with_shapes_on_meta_tensors():
+    """ssalaad::tilelang_bsr_addmm_inplace_dense_ and ssalaad::slr_linear are
+    defined with fake (meta) implementations, so tracing needs no GPU."""
+    from s_salaad_b200.cuda_sparse import register_reference_op
+
+    register_reference_op()
+    x = torch.empty(3, 5, 64, device="meta", dtype=torch.bfloat16)
+    A = torch.empty(32, 8, device="meta", dtype=torch.bfloat16)
+    B = torch.empty(8, 64, device="meta", dtype=torch.bfloat16)
+    y = torch.ops.ssalaad.slr_linear(x, A, B, None, None, None, None, 0, 0)
+    assert y.shape == (3, 5, 32) and y.dtype == torch.bfloat16
