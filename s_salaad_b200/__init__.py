@@ -4,7 +4,9 @@
 hand-written CUDA kernels of ``libslr_b200.so`` (C ABI: include/slr_b200.h).
 The package mirrors the reference's module and operator API
 (``efficient.LRSLinear``, ``efficient.dense_to_bsr``,
-``cuda_sparse.register_reference_op``).  CUDA only; no CPU fallback.
+``efficient.build_efficient_model``, ``cuda_sparse.register_reference_op``);
+``ops.LayerGroup`` runs layers that read one input together and ``shard``
+splits a layer by block-rows over several GPUs.  CUDA only; no CPU fallback.
 """
 from . import ops
 from ._lib import LIB_PATH, load
