@@ -1,8 +1,9 @@
 """Generate the golden vectors in tests/golden/ by running the S-SALAAD
 reference itself (CPU parts) on seeded inputs.
 
-Run in a container that has the reference sources (read-only) at
-``--ref`` (default /root/reference):
+Run in a container that has the reference sources (read-only); ``--ref``
+gives their root directory (the default is where this build's container
+mounts them):
 
     python tests/golden/make_golden.py
 
