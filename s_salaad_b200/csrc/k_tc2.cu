@@ -94,6 +94,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr uint32_t IDESC_LR = idesc_f16<TI>(256, 256, false);
   static_assert(BP == 32 || BP == 64, "2-SM path: block_p 32 or 64");
   static_assert(STAGE % 1024 == 0 && POS % 256 == 0, "stage alignment");
+  // Schedule columns per sparse stage: a 32-deep column fills half a stage,
+  // so two of them share one (same MMAs in the same order, half the per-stage
+  // barrier, TMA and issue overhead).
+  constexpr int CPS = BQ == 32 ? 2 : 1;
+  static_assert(CPS * X_BYTES <= A_SLOT && CPS * G * POS <= B_SLOT && G <= 8, "stage holds CPS columns");
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -165,7 +170,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int gcount = min(G, a.nrows - r0);
         const int m0 = mt * 256 + int(rank) * 128;  // this CTA's tokens
         const int p0 = __ldg(a.plan_start + gi), p1 = __ldg(a.plan_start + gi + 1);
-        const int n_sp = (p1 - p0) * SUB;
+        const int n_sp = ((p1 - p0 + CPS - 1) / CPS) * SUB;
         const int n_st = max(n_sp + a.n_lr, 1);
         const int rw = lane < gcount ? (a.rows ? a.rows[r0 + lane] : r0 + lane) : 0;
         for (int s = (pw - int(g % kProducers) + kProducers) % kProducers; s < n_st; s += kProducers) {
@@ -182,32 +187,55 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* adst = smem + slot * STAGE;
           const bool last = s == n_st - 1;
           if (s < n_sp) {
-            const int k = p0 + s / SUB, sub = s % SUB;
-            const uint32_t rec = __ldg(a.plan + 2 * k), first = __ldg(a.plan + 2 * k + 1);
-            const uint32_t c = rec & 0xffffu, mask = rec >> 16;
+            const int kb = p0 + (s / SUB) * CPS, sub = s % SUB;
+            const int nc = min(CPS, p1 - kb);  // schedule columns in this stage
+            uint32_t cols[CPS], masks[CPS], firsts[CPS];
+#pragma unroll
+            for (int c = 0; c < CPS; ++c) {
+              cols[c] = masks[c] = firsts[c] = 0u;
+              if (c < nc) {
+                const uint32_t rec = __ldg(a.plan + 2 * (kb + c));
+                cols[c] = rec & 0xffffu;
+                masks[c] = rec >> 16;
+                firsts[c] = __ldg(a.plan + 2 * (kb + c) + 1);
+              }
+            }
+            uint32_t atoms = 0;
+#pragma unroll
+            for (int c = 0; c < CPS; ++c) atoms += uint32_t(__popc(masks[c]));
             if (lane == 0) {
               if (leader) {
-                meta[slot] = mask | (last ? kMetaLast : 0u);
-                mbar_arrive_expect_tx(&full[slot], 2 * (X_BYTES + __popc(mask) * POS));
+                uint32_t mm = masks[0];
+                if (CPS == 2) mm |= masks[CPS - 1] << 8;
+                meta[slot] = mm | (last ? kMetaLast : 0u);
+                mbar_arrive_expect_tx(&full[slot], 2 * (uint32_t(nc) * X_BYTES + atoms * POS));
               }
-              tma2_load_2d(adst, &tm_x, int(c) * BQ + sub * KS, m0, fb);
-            }
-            if ((mask >> lane) & 1u) {
-              // this row's run of consecutive present rows [j0, end): its 2*len
-              // half-block atoms, the first len on the leader, the rest on the peer
-              const uint32_t below = (1u << lane) - 1u, zeros = ~mask & below;
-              const int j0 = zeros ? 32 - __clz(zeros) : 0;
-              const int end = lane + __ffs(~(mask >> lane)) - 1;
-              const int len = end - j0;
-              const int p_run = __popc(mask & ((1u << j0) - 1u));
-              const int blk = int(__ldg(a.plan + first + __popc(mask & below)));
 #pragma unroll
-              for (int h = 0; h < 2; ++h) {
-                const int at = 2 * (lane - j0) + h;
-                if (at / len == int(rank))
-                  tma2_load_2d(adst + A_SLOT + (p_run + at - int(rank) * len) * POS, &tm_v, h * (BP / 2),
-                               blk * BQ + sub * KS, fb);
+              for (int c = 0; c < CPS; ++c)
+                if (c < nc) tma2_load_2d(adst + c * X_BYTES, &tm_x, int(cols[c]) * BQ + sub * KS, m0, fb);
+            }
+            uint32_t off = 0;  // this column's first atom in the stage's B slot
+#pragma unroll
+            for (int c = 0; c < CPS; ++c) {
+              const uint32_t mask = masks[c];
+              if ((mask >> lane) & 1u) {
+                // this row's run of consecutive present rows [j0, end): its 2*len
+                // half-block atoms, the first len on the leader, the rest on the peer
+                const uint32_t below = (1u << lane) - 1u, zeros = ~mask & below;
+                const int j0 = zeros ? 32 - __clz(zeros) : 0;
+                const int end = lane + __ffs(~(mask >> lane)) - 1;
+                const int len = end - j0;
+                const int p_run = int(off) + __popc(mask & ((1u << j0) - 1u));
+                const int blk = int(__ldg(a.plan + firsts[c] + __popc(mask & below)));
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                  const int at = 2 * (lane - j0) + h;
+                  if (at / len == int(rank))
+                    tma2_load_2d(adst + A_SLOT + (p_run + at - int(rank) * len) * POS, &tm_v, h * (BP / 2),
+                                 blk * BQ + sub * KS, fb);
+                }
               }
+              off += uint32_t(__popc(mask));
             }
           } else if (s < n_sp + a.n_lr) {
             const int l = s - n_sp;
@@ -362,19 +390,26 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int kk = 0; kk < 4; ++kk)
               umma2_f16(d, sdesc(abase + kk * 32, 16, 1024, 2), sdesc(bbase + kk * 32, 16, 1024, 2), IDESC_LR, 1u);
           } else {
-            uint32_t mask = m & 0xffffu, p = 0;
-            while (mask) {
-              const int j = __ffs(mask) - 1;
-              const int len = __ffs(~(mask >> j)) - 1;
-              mask &= ~(((1u << len) - 1u) << j);
-              const uint32_t idesc = IDESC_SP | (uint32_t(len * BP) >> 3) << 17;
+            // up to CPS schedule columns: row masks in bits [0, 8) and [8, 16),
+            // x tiles one after another in the A slot, atoms packed in the B slot
+            uint32_t p = 0;
 #pragma unroll
-              for (int kk = 0; kk < KS / 16; ++kk) {
-                const uint64_t ad = sdesc(abase + kk * 32, 16, 8 * XW, layout_for(XW));
-                const uint64_t bd = sdesc(bbase + p * POS + kk * 16 * HW, POS, 8 * HW, layout_for(HW));
-                umma2_f16(d + j * BP, ad, bd, idesc, 1u);
+            for (int c = 0; c < CPS; ++c) {
+              uint32_t mask = (m >> (8 * c)) & 0xffu;
+              const uint32_t xa = abase + uint32_t(c) * X_BYTES;
+              while (mask) {
+                const int j = __ffs(mask) - 1;
+                const int len = __ffs(~(mask >> j)) - 1;
+                mask &= ~(((1u << len) - 1u) << j);
+                const uint32_t idesc = IDESC_SP | (uint32_t(len * BP) >> 3) << 17;
+#pragma unroll
+                for (int kk = 0; kk < KS / 16; ++kk) {
+                  const uint64_t ad = sdesc(xa + kk * 32, 16, 8 * XW, layout_for(XW));
+                  const uint64_t bd = sdesc(bbase + p * POS + kk * 16 * HW, POS, 8 * HW, layout_for(HW));
+                  umma2_f16(d + j * BP, ad, bd, idesc, 1u);
+                }
+                p += len;
               }
-              p += len;
             }
           }
           umma2_commit_both(&empty[slot]);
