@@ -294,3 +294,21 @@ def test_operators_register_with_shapes_on_meta_tensors():
     B = torch.empty(8, 64, device="meta", dtype=torch.bfloat16)
     y = torch.ops.ssalaad.slr_linear(x, A, B, None, None, None, None, 0, 0)
     assert y.shape == (3, 5, 32) and y.dtype == torch.bfloat16
+
+
+def test_synthetic_bundle_is_a_loadable_cfg2_model(tmp_path):
+    """The cfg2 bundle writer produces a reference-format bundle whose layers
+    rebuild the dense weights A·B + S it returns (CPU only; one layer)."""
+    from s_salaad_b200 import workloads
+    from s_salaad_b200.efficient import load_artifact
+
+    path = tmp_path / "cfg2.pt"
+    dense = workloads.compressed_bundle(path, n_layers=1)
+    p = load_artifact(path)
+    assert set(p["layers"]) == set(dense) and len(dense) == 7
+    assert p["model_config"]["num_hidden_layers"] == 1 and p["model_config"]["hidden_size"] == 512
+    for name, data in p["layers"].items():
+        W = data["A"] @ data["B"] + data["S"].to_dense()
+        assert torch.equal(W, dense[name])
+        assert (data["block_p"], data["block_q"]) == (16, 16)
+    assert not any(k.endswith("q_proj.weight") for k in p["base_state_dict"])
