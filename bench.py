@@ -585,7 +585,8 @@ def main() -> None:
         peak = P["hbm_gbs"]
         roof = {"bound": "hbm", "unit": "GB/s", "algorithmic_per_step": comb_bytes,
                 "kernel": "combine (sparse + H*A^T + bias; one launch per projection)"}
-    traffic = NCU_TRAFFIC.get(args.workload)
+    # captured on one GPU (full layers); a shard's launches move other byte counts
+    traffic = NCU_TRAFFIC.get(args.workload) if world == 1 else None
     if tensor_bound:
         roof["step_tflops"] = (comb_flops + low_flops) * K / (total_ms / 1e3) / 1e12
     roof.update({"achieved": achieved, "peak": peak, "peak_source": pk_src,
