@@ -20,7 +20,7 @@ block-row sharded over the ranks and y is all-gathered (NCCL), so the total
 work is fixed (strong scaling).  `--impl reference` times the reference's
 CPU implementation of the path (its AVX2 BSR kernel, compiled from the
 reference sources into oracle/_ref, plus the low-rank F.linear calls and the
-bias, in fp32) on this host's cores over a bounded token sample.
+bias, in fp32) on this host's cores over the same token batch.
 """
 from __future__ import annotations
 
@@ -162,11 +162,12 @@ class ClockSampler:
 def cpu_reference_run(specs, T_sample: int, steps: int, warmup: int, budget_s: float | None):
     """Time the reference CPU path (AVX2 kernel from oracle/_ref + MKL
     F.linear + bias, fp32) on T_sample tokens through the layer set.
-    Returns (seconds per sample, kind, cores, reps)."""
+    Returns (seconds per sample, kind, cores, CPU model name)."""
     sys.path.insert(0, str(REPO / "oracle"))
     import slr_oracle  # noqa: E402  (CPU baseline leg)
 
     cores = slr_oracle.max_threads()
+    cpu_model = cpu_model_name()
     torch.set_num_threads(cores)
     mod = slr_oracle.ref_avx2_module()
     kind = "reference" if mod is not None else "port"
@@ -201,7 +202,18 @@ def cpu_reference_run(specs, T_sample: int, steps: int, warmup: int, budget_s: f
             break
     if kind == "port":
         cores = 1
-    return times, kind, cores
+    return times, kind, cores, cpu_model
+
+
+def cpu_model_name() -> str:
+    """The host CPU's model name (what lscpu reports), from /proc/cpuinfo."""
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
 
 
 # ---------------------------------------------------------------- main --
@@ -311,7 +323,8 @@ def main() -> None:
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
-    T_sample = args.cpu_sample_tokens or min(T, 256)
+    # the CPU legs run the workload's full token batch unless a sample is asked for
+    T_sample = args.cpu_sample_tokens or T
     config = {"workload": f"{cfg}: {len(specs)} S+LR projections, T={T}",
               "tokens_per_step": T, "projections": [[s.name, s.out_features, s.in_features] for s in specs],
               "block": [specs[0].block_p, specs[0].block_q], "rank": specs[0].rank,
@@ -321,14 +334,14 @@ def main() -> None:
     if args.impl == "reference":
         if rank != 0:
             return
-        times, kind, cores = cpu_reference_run(specs, T_sample, args.steps, args.warmup, None)
+        times, kind, cores, model = cpu_reference_run(specs, T_sample, args.steps, args.warmup, None)
         tok_s = T_sample * len(times) / sum(times)
         line = {"metric": METRIC, "impl": "reference", "value": tok_s, "unit": "tokens/s", "n_gpus": world,
                 "steps": len(times), "warmup": args.warmup, "ms_per_step": 1e3 * statistics.mean(times),
                 "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
                 "data": "synthetic (seeded; no dataset)",
-                "config": {**config, "cpu_sample_tokens": T_sample, "parallelism": "host threads"},
-                "cpu_baseline": {"value": tok_s, "unit": "tokens/s", "cores": cores, "kind": kind,
+                "config": {**config, "parallelism": "host threads (CPU)"},
+                "cpu_baseline": {"value": tok_s, "unit": "tokens/s", "cores": cores, "kind": kind, "cpu_model": model,
                                  "sample": f"{T_sample} of {T} tokens per step through all {len(specs)} projections"},
                 "e2e": {"value": tok_s, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
         emit(line)
@@ -750,8 +763,9 @@ def main() -> None:
     # ------------------------------------------------------- CPU baseline
     cpu = None
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
-        times, kind, cores = cpu_reference_run(specs, T_sample, 0, 1, args.cpu_budget_s)
+        times, kind, cores, model = cpu_reference_run(specs, T_sample, 0, 1, args.cpu_budget_s)
         cpu = {"value": T_sample * len(times) / sum(times), "unit": "tokens/s", "cores": cores, "kind": kind,
+               "cpu_model": model,
                "sample": f"{T_sample} of {T} tokens x {len(times)} reps through all {len(specs)} projections, "
                          f"fp32 (reference AVX2 BSR kernel + MKL low-rank + bias)"}
 

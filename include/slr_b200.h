@@ -36,7 +36,7 @@
 extern "C" {
 #endif
 
-#define SLR_ABI_VERSION 4
+#define SLR_ABI_VERSION 5
 
 #if defined(__GNUC__)
 #define SLR_API __attribute__((visibility("default")))
@@ -227,8 +227,10 @@ SLR_API int slr_lrs_linear_combine(const slr_layer* layer, const void* x, int64_
  * (held by every GPU that loads the library until exit); a token count that
  * needs more is rejected with SLR_ERR_WORKSPACE before any launch.  The first
  * call on a device looks up the array's address for that device: make it
- * before any stream capture.  All calls share the array (each clears what it
- * uses on `stream`); calls that overlap on the GPU race on it.
+ * before any stream capture.  The address is kept for the life of the
+ * process, so a cudaDeviceReset after the first call is not supported.  The
+ * scratch needs no initialisation: each call overwrites what it reads.  All
+ * calls share the array; calls that overlap on the GPU race on it.
  */
 SLR_API int slr_lrs_linear_forward_noalloc(const slr_layer* layer, const void* x,
                            int64_t ldx, void* y, int64_t ldy, int64_t M,
@@ -345,17 +347,35 @@ SLR_API int slr_plan_shards(const int32_t* crow_host, int64_t NB, int64_t block_
  * reference runs on one device.
  *
  * Each rank owns a full y [M, N] (same ldy on every rank) and, per layer, a
- * 4-word uint64 signal slot that is zero before the first call.  y[p] is
- * rank p's y advanced to THIS rank's first output column; signal[p] is rank
- * p's slot of the layer.  A call is slr_lrs_linear_combine_peers (or the
- * group form; ranks without rows of the layer call slr_peers_wait with
- * empty_shard = 1 instead) followed by slr_peers_wait on the same stream;
- * after the wait, y on this rank holds every rank's columns.  Every rank
- * must make the calls of a layer in the same order.  Waits are bounded (2 s)
- * and report SLR_ERR_TIMEOUT through slr_device_status.
+ * signal slot of SLR_SIGNAL_WORDS uint64 words that is zero before the first
+ * call.  y[p] is rank p's y advanced to THIS rank's first output column;
+ * signal[p] is rank p's slot of the layer.  A call is
+ * slr_lrs_linear_combine_peers (or the group form; ranks without rows of the
+ * layer call slr_peers_wait with empty_shard = 1 instead) followed by
+ * slr_peers_wait on the same stream; after the wait, y on this rank holds
+ * every rank's columns.  Every rank must make the calls of a layer in the
+ * same order.  Each rank numbers the calls by its own count and writes its
+ * number into one word per rank of every slot, so words left by an older
+ * call never satisfy a newer call's wait.
+ *
+ * Waits on other ranks are bounded (slr_set_wait_limit_ns, 2 s by default)
+ * and report SLR_ERR_TIMEOUT through slr_device_status.  A rank that gives up
+ * a wait marks the call as failed in every rank's slot, so every rank's wait
+ * for that call reports the timeout and the y of that call must not be used.
+ * If every rank still makes every call, the next calls are synchronised again
+ * by their numbers.  A rank that skips (or repeats) a call makes every later
+ * wait of the layer time out on all ranks, until all ranks meet on the host
+ * and zero their slots.
  */
 #define SLR_MAX_RANKS 8
 #define SLR_IPC_HANDLE_BYTES 64
+#define SLR_SIGNAL_WORDS 32
+
+/* Limit, in ns, of every later wait on other ranks (the peer epilogue and
+ * slr_peers_wait), process-wide; 0 restores the default of 2 s.  Waits inside
+ * one kernel (its own pipeline) keep their fixed 2 s limit.  No reference
+ * counterpart. */
+SLR_API int slr_set_wait_limit_ns(uint64_t ns);
 
 typedef struct slr_peers {
   int32_t world;                    /* ranks, 2..SLR_MAX_RANKS */

@@ -13,7 +13,12 @@ a second pin for the C oracle.  It is built here, where the reference sources
 exist, and travels to the GPU box as a prebuilt ``.so``; it is listed in
 .gitignore so it never enters the history.
 
-Usage:  python oracle/build_ref.py [--src PATH] [--force]
+The reference project's root directory comes from the caller: the ``root``
+argument of :func:`build`, the ``--ref-root`` option, or the environment
+variable ``SLR_REFERENCE_ROOT``.  Without any of them nothing is built and a
+prebuilt module, if present, is used as is.
+
+Usage:  python oracle/build_ref.py --ref-root DIR [--force]
 """
 from __future__ import annotations
 
@@ -28,7 +33,7 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 OUT_DIR = HERE / "_ref"
 MODULE = "slr_ref_avx2"
-DEFAULT_SRC = Path("/root/reference/ssalaad/cpu_sparse/bsr_addmm_avx2.cpp")
+SRC_IN_PROJECT = Path("ssalaad/cpu_sparse/bsr_addmm_avx2.cpp")  # path within the reference project
 
 
 def output_path() -> Path:
@@ -36,12 +41,16 @@ def output_path() -> Path:
     return OUT_DIR / f"{MODULE}{suffix}"
 
 
-def build(src: Path = DEFAULT_SRC, force: bool = False, quiet: bool = False) -> Path | None:
-    """Compile the reference kernel; returns the module path, or None when the
-    reference sources are absent (as on the GPU box, which uses the prebuilt file)."""
+def build(root: Path | str | None = None, force: bool = False, quiet: bool = False) -> Path | None:
+    """Compile the reference kernel of the reference project at `root`
+    (default: $SLR_REFERENCE_ROOT); returns the module path, or None when the
+    reference sources are absent (as on the GPU box, which uses the prebuilt
+    file)."""
     out = output_path()
     stamp = OUT_DIR / "source.sha1"
-    if not src.is_file():
+    root = root if root is not None else os.environ.get("SLR_REFERENCE_ROOT")
+    src = Path(root) / SRC_IN_PROJECT if root else None
+    if src is None or not src.is_file():
         return out if out.is_file() else None
     digest = hashlib.sha1(src.read_bytes()).hexdigest()
     if out.is_file() and stamp.is_file() and stamp.read_text().strip() == digest and not force:
@@ -84,9 +93,10 @@ def load():
 
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
-    ap.add_argument("--src", type=Path, default=DEFAULT_SRC)
+    ap.add_argument("--ref-root", type=Path, default=None,
+                    help="root of the S-SALAAD reference project (default: $SLR_REFERENCE_ROOT)")
     ap.add_argument("--force", action="store_true")
     a = ap.parse_args()
-    p = build(a.src, a.force)
+    p = build(a.ref_root, a.force)
     print(p if p else "reference sources absent; nothing built")
     sys.exit(0 if p else 1)

@@ -13,6 +13,7 @@ from pathlib import Path
 LIB_PATH = Path(__file__).resolve().parent / "libslr_b200.so"
 
 # slr_status codes (include/slr_b200.h)
+ABI_VERSION = 5  # SLR_ABI_VERSION of include/slr_b200.h
 SLR_OK = 0
 # slr_layer.flags bits (include/slr_b200.h)
 SLR_FLAG_PAIR_MMA = 1
@@ -57,10 +58,12 @@ EXPORTED = (
     "slr_lrs_linear_combine_peers",
     "slr_lrs_linear_group_combine_peers",
     "slr_peers_wait",
+    "slr_set_wait_limit_ns",
 )
 
 SLR_MAX_RANKS = 8
 SLR_IPC_HANDLE_BYTES = 64
+SLR_SIGNAL_WORDS = 32
 
 i64, i32, vp, sz = ctypes.c_int64, ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t
 
@@ -133,6 +136,7 @@ _SIGS = {
     "slr_lrs_linear_group_combine_peers": ([ctypes.POINTER(SlrLayer), i32, i32, vp, i64, i64, i64, vp, sz,
                                             ctypes.POINTER(SlrPeers), vp], i32),
     "slr_peers_wait": ([ctypes.POINTER(SlrPeers), i32, vp], i32),
+    "slr_set_wait_limit_ns": ([ctypes.c_uint64], i32),
 }
 
 _lock = threading.Lock()
@@ -169,7 +173,7 @@ def load(path: Path | str | None = None) -> ctypes.CDLL:
             fn = getattr(lib, name)
             fn.argtypes = args
             fn.restype = res
-        if lib.slr_abi_version() != 4:
+        if lib.slr_abi_version() != ABI_VERSION:
             raise RuntimeError("s_salaad_b200: libslr_b200.so ABI version mismatch")
         if path is None:
             _lib = lib

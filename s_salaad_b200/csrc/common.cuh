@@ -87,6 +87,9 @@ __device__ __forceinline__ void pdl_wait_primary() {
 __device__ __forceinline__ void red_add_release_sys(unsigned long long* p, unsigned long long v) {
   asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
+__device__ __forceinline__ void st_release_sys(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
 __device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p) {
   unsigned long long v;
   asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
@@ -99,15 +102,20 @@ __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
-// Spin until *p >= target, at most SLR_WAIT_LIMIT_NS; false on timeout.
-__device__ __forceinline__ bool wait_counter_geq(const unsigned long long* p, unsigned long long target) {
-  if (ld_acquire_sys(p) >= target) return true;
+// Spin until p[q] >= target (eq: == target) for every q < n (words of other
+// ranks), at most limit_ns in all; false on timeout.
+__device__ __forceinline__ bool wait_words(const unsigned long long* p, int n, unsigned long long target,
+                                           unsigned long long limit_ns, bool eq) {
   const unsigned long long t0 = globaltimer_ns();
-  while (true) {
-    __nanosleep(100);
-    if (ld_acquire_sys(p) >= target) return true;
-    if (globaltimer_ns() - t0 > SLR_WAIT_LIMIT_NS) return false;
+  for (int q = 0; q < n; ++q) {
+    while (true) {
+      const unsigned long long v = ld_acquire_sys(p + q);
+      if (eq ? v == target : v >= target) break;
+      if (globaltimer_ns() - t0 > limit_ns) return false;
+      __nanosleep(100);
+    }
   }
+  return true;
 }
 
 // The k-th work item of worker p of P when the items, listed heaviest first,

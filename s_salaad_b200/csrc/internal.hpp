@@ -70,23 +70,40 @@ int launch_mma_rowblock_group(const RowblockArgs* a, const int64_t* h_col, int n
                               bool pdl, cudaStream_t s);
 
 // ---- peer memory: a rank's output tiles stored straight into every rank's y.
-// Signal slot of one layer on each rank (4 x u64, zero at start):
-//   [0] arrivals: every rank adds 1 when its call for the layer starts;
-//   [1] completions: every rank adds kDonePerRank per call (its CTAs add 1
-//       each, CTA 0 adds kDonePerRank - gridDim.x on top) once its stores are
-//       visible;
-//   [2] calls of the layer completed on this rank (written by its own wait).
-// Call c (0-based) of a rank may store into peers only after [0] >= world *
-// (c + 1), so a peer's y is no longer read by the caller's previous work;
-// y is complete on rank p when its [1] >= world * kDonePerRank * (c + 1).
+// Signal slot of one layer on each rank (SLR_SIGNAL_WORDS x u64, zero at start).
+// Every rank numbers the calls of a layer by its own count (1, 2, ...), so
+// words written for one call never satisfy the wait of another:
+//   [kSigArrive + p] rank p stores its call number (release) when the call
+//                    starts;
+//   [kSigDone + p]   rank p adds kDonePerRank per call once its stores are
+//                    visible (its CTAs add 1 each, CTA 0 adds
+//                    kDonePerRank - gridDim.x on top);
+//   [kSigFail + p]   rank p stores the number of a call in which one of its
+//                    CTAs gave up a wait (its tiles for that call may be
+//                    missing), before adding its completion;
+//   [kSigCalls]      calls of the layer completed on this rank (written by its
+//                    own wait).
+// Call c of a rank may store into peers only once every [kSigArrive + q] ==
+// c (so a peer's y is no longer read by that rank's previous call; a rank
+// that skipped a call, or is a call ahead, never matches and the wait times
+// out); y is complete on rank p after call c when every [kSigDone + q] >=
+// kDonePerRank * c and no [kSigFail + q] == c.
 constexpr int kMaxRanks = SLR_MAX_RANKS;
+constexpr int kSigArrive = 0;
+constexpr int kSigDone = kMaxRanks;
+constexpr int kSigFail = 2 * kMaxRanks;
+constexpr int kSigCalls = 3 * kMaxRanks;
+static_assert(kSigCalls < SLR_SIGNAL_WORDS, "signal slot layout");
 constexpr unsigned long long kDonePerRank = 1ull << 32;
 struct PeerArgs {
   void* y[kMaxRanks];                   // rank p's y at this rank's columns (y[me] = local)
   unsigned long long* sig[kMaxRanks];   // rank p's signal slot of this layer
   unsigned long long* my_sig;           // sig[me]
+  unsigned long long wait_ns = 0;       // limit of each wait on other ranks
   int world = 0, me = 0;
 };
+// Limit of the waits on other ranks (slr_set_wait_limit_ns), in ns.
+unsigned long long peer_wait_limit_ns();
 // The wait that ends a call (and, for a rank with no rows of the layer, its
 // arrival and completion signals).
 int launch_peer_wait(const PeerArgs& p, bool empty_shard, cudaStream_t s);

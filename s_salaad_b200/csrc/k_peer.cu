@@ -6,6 +6,7 @@
 // It replaces the NCCL all-gather of y (plus the column reassembly) that a
 // block-row-sharded layer otherwise needs: each rank's tiles reach the peers
 // while the kernel is still computing, and nothing is copied afterwards.
+#include <atomic>
 #include <cstring>
 #include <map>
 #include <mutex>
@@ -19,27 +20,38 @@ namespace {
 __device__ unsigned g_status_peer = 0;
 
 // One thread: for a rank without rows of the layer, take part in the call
-// (arrive, wait for the others, count an empty completion); then wait until
-// every rank's stores into this rank's y are visible and count the call.
+// (announce it, wait for the others, count an empty completion); then wait
+// until every rank's stores into this rank's y are visible, check that no
+// rank gave up during the call, and count the call.  Calls are numbered by
+// this rank's own count (slot word kSigCalls).
 __global__ void peer_wait_kernel(const PeerArgs p, int empty_shard) {
   if (threadIdx.x != 0) return;
   unsigned long long* me = p.my_sig;
-  const unsigned long long calls = *reinterpret_cast<volatile unsigned long long*>(me + 2);
-  const unsigned long long w = unsigned(p.world);
+  const unsigned long long call = *reinterpret_cast<volatile unsigned long long*>(me + kSigCalls) + 1;
   if (empty_shard) {
 #pragma unroll
     for (int r = 0; r < kMaxRanks; ++r)
-      if (r < p.world) red_add_release_sys(p.sig[r] + 0, 1ull);
-    if (!wait_counter_geq(me + 0, (calls + 1) * w)) atomicOr(&g_status_peer, SLR_TIMEOUT_BIT);
+      if (r < p.world) st_release_sys(p.sig[r] + kSigArrive + p.me, call);
+    if (!wait_words(me + kSigArrive, p.world, call, p.wait_ns, true)) {
+      atomicOr(&g_status_peer, SLR_TIMEOUT_BIT);
+#pragma unroll
+      for (int r = 0; r < kMaxRanks; ++r)
+        if (r < p.world) st_release_sys(p.sig[r] + kSigFail + p.me, call);
+    }
     fence_sc_sys();
 #pragma unroll
     for (int r = 0; r < kMaxRanks; ++r)
-      if (r < p.world) red_add_release_sys(p.sig[r] + 1, kDonePerRank);
+      if (r < p.world) red_add_release_sys(p.sig[r] + kSigDone + p.me, kDonePerRank);
   }
-  if (!wait_counter_geq(me + 1, (calls + 1) * w * kDonePerRank)) atomicOr(&g_status_peer, SLR_TIMEOUT_BIT);
-  *reinterpret_cast<volatile unsigned long long*>(me + 2) = calls + 1;
+  bool ok = wait_words(me + kSigDone, p.world, call * kDonePerRank, p.wait_ns, false);
+  for (int q = 0; ok && q < p.world; ++q)
+    if (ld_acquire_sys(me + kSigFail + q) == call) ok = false;
+  if (!ok) atomicOr(&g_status_peer, SLR_TIMEOUT_BIT);
+  *reinterpret_cast<volatile unsigned long long*>(me + kSigCalls) = call;
   __threadfence();
 }
+
+std::atomic<unsigned long long> g_wait_limit_ns{SLR_WAIT_LIMIT_NS};
 
 using GetAddressRangeFn = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
 
@@ -66,6 +78,8 @@ std::map<std::string, Mapping> g_ipc;
 
 }  // namespace
 
+unsigned long long peer_wait_limit_ns() { return g_wait_limit_ns.load(std::memory_order_relaxed); }
+
 int launch_peer_wait(const PeerArgs& p, bool empty_shard, cudaStream_t s) {
   peer_wait_kernel<<<1, 32, 0, s>>>(p, empty_shard ? 1 : 0);
   SLR_CHECK_LAUNCH("peer_wait_kernel");
@@ -85,6 +99,11 @@ int read_and_clear_status_peer(unsigned* out) {
 using namespace slr;
 
 extern "C" {
+
+int slr_set_wait_limit_ns(uint64_t ns) {
+  g_wait_limit_ns.store(ns > 0 ? ns : SLR_WAIT_LIMIT_NS, std::memory_order_relaxed);
+  return SLR_OK;
+}
 
 int slr_ipc_export(const void* dev_ptr, void* handle, int64_t* offset) {
   if (!dev_ptr || !handle || !offset) return fail(SLR_ERR_INVALID_ARGUMENT, "slr_ipc_export: NULL argument");

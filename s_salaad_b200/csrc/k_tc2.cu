@@ -109,6 +109,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* meta = reinterpret_cast<uint32_t*>(tempty + 2);
   uint32_t* tmem_slot = meta + STAGES;
   __shared__ volatile int s_abort;
+  __shared__ volatile int s_peer_fail;  // an epilogue warp gave up waiting for the other ranks
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_rank();
@@ -124,6 +125,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     fence_mbar_init();
     s_abort = 0;
+    s_peer_fail = 0;
   }
   if (warp == 1) {
     tmem_alloc2(tmem_slot, 2 * ACC);
@@ -434,22 +436,25 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Multi-GPU: this call's arrival at every rank, then (before the first
     // store into a peer) the wait for every rank's arrival.
     const int world = a.peer.world;
-    unsigned long long arrive_target = 0;
+    unsigned long long call_no = 0;  // this rank's call of the layer, 1-based
     bool peer_live = world > 1, arrived = false;
     if (world > 1) {
       pdl_wait_primary();  // the preceding wait of this rank has counted its calls
-      arrive_target = (*reinterpret_cast<volatile unsigned long long*>(a.peer.my_sig + 2) + 1) * world;
+      call_no = *reinterpret_cast<volatile unsigned long long*>(a.peer.my_sig + kSigCalls) + 1;
       if (blockIdx.x == 0 && warp == 2 && lane == 0) {
 #pragma unroll
         for (int p = 0; p < kMaxRanks; ++p)
-          if (p < world) red_add_release_sys(a.peer.sig[p] + 0, 1ull);
+          if (p < world) st_release_sys(a.peer.sig[p] + kSigArrive + a.peer.me, call_no);
       }
     }
     auto wait_arrivals = [&]() {
-      int ok = lane == 0 ? int(wait_counter_geq(a.peer.my_sig + 0, arrive_target)) : 1;
+      int ok = lane == 0 ? int(wait_words(a.peer.my_sig + kSigArrive, world, call_no, a.peer.wait_ns, true)) : 1;
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) {
-        if (lane == 0) atomicOr(&g_status_tc2, SLR_TIMEOUT_BIT);
+        if (lane == 0) {
+          atomicOr(&g_status_tc2, SLR_TIMEOUT_BIT);
+          s_peer_fail = 1;
+        }
         peer_live = false;  // keep the local result, leave the peers alone
       }
       arrived = true;
@@ -550,7 +555,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (world > 1) {
       // Completion: after every rank arrived (so the count belongs to this
-      // call) and this CTA's stores are visible system-wide.
+      // call) and this CTA's stores are visible system-wide.  A CTA that gave
+      // up on a wait first marks the call as failed at every rank, so their
+      // waits report a timeout instead of passing on an incomplete y; it
+      // still counts its completion, which keeps the counts in step.
       if (peer_live && !arrived) wait_arrivals();
       if (lane == 0) bulk_wait_all();
       __syncwarp();
@@ -558,10 +566,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       fence_sc_sys();
       named_bar_sync(1, 128);
       if (warp == 2 && lane == 0) {
+        if (s_abort || s_peer_fail) {
+#pragma unroll
+          for (int p = 0; p < kMaxRanks; ++p)
+            if (p < world) st_release_sys(a.peer.sig[p] + kSigFail + a.peer.me, call_no);
+        }
         const unsigned long long add = 1ull + (blockIdx.x == 0 ? kDonePerRank - gridDim.x : 0ull);
 #pragma unroll
         for (int p = 0; p < kMaxRanks; ++p)
-          if (p < world) red_add_release_sys(a.peer.sig[p] + 1, add);
+          if (p < world) red_add_release_sys(a.peer.sig[p] + kSigDone + a.peer.me, add);
       }
     }
   }

@@ -669,6 +669,7 @@ int to_peer_args(const slr_peers* P, PeerArgs& pa) {
     pa.sig[p] = reinterpret_cast<unsigned long long*>(P->signal[p]);
   }
   pa.my_sig = pa.sig[pa.me];
+  pa.wait_ns = peer_wait_limit_ns();
   return SLR_OK;
 }
 

@@ -236,7 +236,7 @@ class PeerOutputs:
         self.device = device
         self.y = torch.empty(T, plan.out_features, dtype=dtype, device=device)
         self.ldy = plan.out_features
-        self.signal = torch.zeros(4, dtype=torch.int64, device=device)
+        self.signal = torch.zeros(_lib.SLR_SIGNAL_WORDS, dtype=torch.int64, device=device)
         lib = _lib.load()
         hb = _lib.SLR_IPC_HANDLE_BYTES
         mine = np.zeros(2 * (hb + 8), dtype=np.uint8)

@@ -1,11 +1,10 @@
 """Generate the golden vectors in tests/golden/ by running the S-SALAAD
 reference itself (CPU parts) on seeded inputs.
 
-Run in a container that has the reference sources (read-only); ``--ref``
-gives their root directory (the default is where this build's container
-mounts them):
+Run where the reference sources exist (read-only); ``--ref`` gives the root
+directory of the reference project:
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py --ref DIR
 
 What is run, all from the reference, unmodified:
   * ``ssalaad.cpu_sparse.bsr_addmm_avx2_`` (its AVX2 kernel, built by the
@@ -74,7 +73,7 @@ def t2n(t):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", required=True, help="root directory of the S-SALAAD reference project")
     args = ap.parse_args()
     sys.path.insert(0, args.ref)
     from ssalaad.cpu_sparse import SUPPORTED_BLOCK_SIZES, bsr_addmm_avx2_

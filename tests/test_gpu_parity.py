@@ -13,11 +13,13 @@ All calls go through the C ABI (ctypes) of libslr_b200.so.
 """
 from __future__ import annotations
 
+import os
+
 import numpy as np
 import pytest
 import torch
 
-from conftest import load_golden
+from conftest import load_golden, record_parity
 from s_salaad_b200 import _lib, ops, workloads
 from s_salaad_b200.efficient import LRSLinear, _LRSLinearLR, _LRSLinearLRBlockCUDA, dense_to_bsr
 
@@ -41,6 +43,9 @@ def assert_16bit_close(y: torch.Tensor, ref: torch.Tensor, tol: float = BF16_TOL
     dtype = y.dtype
     y = y.float().cpu()
     ref = ref.float().cpu()
+    case = os.environ.get("PYTEST_CURRENT_TEST", "?").split(" ")[0].split("::")[-1]
+    if not case.startswith("test_full_size"):  # those log themselves, projection by projection
+        record_parity(case, y, ref)
     assert torch.isfinite(y).all()
     err = (y - ref).abs()
     bound = tol * rms(ref) + half_ulp(ref, dtype) + 1e-6
@@ -403,17 +408,27 @@ def torch_ref(t: dict, spec, x: torch.Tensor) -> torch.Tensor:
     return y
 
 
-@pytest.mark.parametrize("cfg,T", [("cfg3", 1), ("cfg3", 16), ("cfg3", 128), ("cfg3", 2048), ("cfg5", 1),
-                                   ("cfg5", 32), ("cfg4", 4096)])
-def test_full_size_configs_match_torch_fp32(cuda, cfg, T):
-    specs = workloads.layer_set(cfg)
-    if cfg == "cfg4":
-        specs = [specs[0], specs[6]]  # one 4096x4096 and the 4096x11008 down projection
-    for i, spec in enumerate(specs):
-        t = spec.tensors(cuda, torch.bfloat16)
-        x = workloads.tokens(T, spec.in_features, seed=i, device=cuda, dtype=torch.bfloat16)
-        y = ops.lrs_linear_forward(desc_for(t, spec, cuda, torch.bfloat16), x)
-        assert_16bit_close(y, torch_ref(t, spec, x))
+@pytest.mark.parametrize("cfg,T", [("cfg3", 1), ("cfg3", 16), ("cfg3", 128), ("cfg3", 2048), ("cfg3", 8192),
+                                   ("cfg5", 1), ("cfg5", 32), ("cfg4", 4096), ("cfg2", 2048)])
+def test_full_size_configs_match_torch_fp32(cuda, cfg, T, parity_log):
+    """Every projection of the layer set at its full size and token count
+    against a plain PyTorch fp32 reference on the GPU (TF32 off); the achieved
+    max|err| / RMS(y_ref) of each projection is recorded (north_star's
+    criterion is max|err| <= 2e-2 * RMS; the asserted bound adds half an ulp
+    of the bf16 output, see the module docstring)."""
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        for i, spec in enumerate(workloads.layer_set(cfg)):
+            t = spec.tensors(cuda, torch.bfloat16)
+            x = workloads.tokens(T, spec.in_features, seed=i, device=cuda, dtype=torch.bfloat16)
+            y = ops.lrs_linear_forward(desc_for(t, spec, cuda, torch.bfloat16), x)
+            ref = torch_ref(t, spec, x)
+            parity_log(f"{cfg} T={T} {spec.name} {spec.out_features}x{spec.in_features}", y, ref)
+            assert_16bit_close(y, ref)
+            del t, x, y, ref
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
 
 
 @pytest.mark.parametrize("cfg,members,T", [("cfg4", (0, 1, 2), 1024), ("cfg4", (4, 5), 512), ("cfg4", (3,), 768),

@@ -65,3 +65,24 @@ def test_noalloc_refuses_requests_beyond_its_array(cuda):
     rc = lib.slr_lrs_linear_forward_noalloc(ctypes.byref(desc.struct), 16, 512, 16, 384, M, None)
     assert rc == _lib.SLR_ERR_WORKSPACE
     assert "bytes of scratch" in _lib.last_error()
+
+
+def test_noalloc_size_limit_is_exact(cuda):
+    """The largest token count whose scratch fits the 16 MiB array runs and
+    matches the workspace forward; one token more is refused."""
+    lib = _lib.load()
+    spec, desc = _layer(cuda, 0)
+    limit = 16 << 20
+    M = limit // (64 * 2)  # H = x * B^T: 64 rank columns of 2 bytes per token
+    assert desc.workspace_bytes(M) <= limit < desc.workspace_bytes(M + 1)
+    x = workloads.tokens(M, 512, seed=11, device=cuda, dtype=torch.bfloat16)
+    ref = desc.forward(x)
+    y = torch.full_like(ref, float("nan"))
+    stream = torch.cuda.current_stream(cuda).cuda_stream
+    _lib.check(lib.slr_lrs_linear_forward_noalloc(ctypes.byref(desc.struct), x.data_ptr(), 512, y.data_ptr(), 384,
+                                                  M, stream), "slr_lrs_linear_forward_noalloc")
+    torch.cuda.synchronize()
+    _close(y, ref)
+    rc = lib.slr_lrs_linear_forward_noalloc(ctypes.byref(desc.struct), x.data_ptr(), 512, y.data_ptr(), 384,
+                                            M + 1, stream)
+    assert rc == _lib.SLR_ERR_WORKSPACE
