@@ -54,46 +54,83 @@ def encode_s_for_artifact(S: torch.Tensor, *, block_p: int | None = None, block_
     return S.to_sparse_csr()
 
 
+def _local_tokenizer(name: str) -> bool:
+    """A tokenizer given as a file-system path (not portable with a bundle)."""
+    path = Path(name)
+    return path.is_absolute() or path.exists()
+
+
 def export_model_config(config: dict) -> dict:
     """The architecture and tokenizer fields of a model configuration; a
-    tokenizer given as a local path is dropped (reference ssalaad/train/model.py:63-69)."""
-    result = {key: value for key, value in config.items() if key in MODEL_FIELDS}
-    tokenizer = result.get("tokenizer_id", "")
-    if tokenizer and (Path(tokenizer).is_absolute() or Path(tokenizer).exists()):
-        result.pop("tokenizer_id")
-    return result
+    tokenizer given as a local path is dropped (reference
+    ssalaad/train/model.py:63-69)."""
+    exported = {}
+    for key, value in config.items():
+        if key not in MODEL_FIELDS:
+            continue
+        if key == "tokenizer_id" and value and _local_tokenizer(str(value)):
+            continue
+        exported[key] = value
+    return exported
+
+
+FORMAT_VERSION = 1
+# Keys of a bundle (format version 1; the reference's save/load_artifact,
+# ssalaad/efficient/artifact.py:78-118) and the meta entries it keeps.
+_BUNDLE_KEYS = ("format_version", "layers", "base_state_dict", "model_config", "meta")
+_META_KEYS = frozenset({"mode", "param_count", "p_tgt_million"})
+_ERR_INCOMPLETE = "Expected a complete model bundle produced by the compression entry point."
+_ERR_VERSION = "Unsupported model bundle version."
+
+
+class _Bundle:
+    """One compressed model on disk: the compressed layers (name -> factors
+    and S), every other tensor of the model, its configuration and a few
+    meta entries."""
+
+    def __init__(self, layers: dict, base_state: dict, model_config: dict, meta: dict):
+        self.layers = layers
+        self.base_state = base_state
+        self.model_config = model_config
+        self.meta = meta
+
+    @classmethod
+    def from_model(cls, model: torch.nn.Module, layers: dict, meta: dict, model_config: dict) -> "_Bundle":
+        # the weights of the compressed modules live in `layers`, not in the base state
+        replaced = {f"{name}.weight" for name in layers}
+        base = {}
+        for key, tensor in model.state_dict().items():
+            if key not in replaced:
+                base[key] = tensor.detach().to("cpu", copy=True)
+        kept_meta = {k: v for k, v in meta.items() if k in _META_KEYS}
+        return cls(layers, base, export_model_config(model_config), kept_meta)
+
+    def to_payload(self) -> dict:
+        return dict(zip(_BUNDLE_KEYS, (FORMAT_VERSION, self.layers, self.base_state, self.model_config,
+                                       self.meta)))
+
+    @staticmethod
+    def check_payload(payload: Any) -> dict:
+        if not isinstance(payload, dict) or any(k not in payload for k in _BUNDLE_KEYS):
+            raise ValueError(_ERR_INCOMPLETE)
+        if payload["format_version"] != FORMAT_VERSION:
+            raise ValueError(_ERR_VERSION)
+        return payload
 
 
 def save_artifact(path: str | Path, layers: dict[str, dict[str, Any]], meta: dict[str, Any], *,
                   model: torch.nn.Module, model_config: dict) -> None:
     """Write compressed layers and every remaining model tensor as one bundle
-    (reference artifact.py:78-105)."""
-    allowed_meta = {"mode", "param_count", "p_tgt_million"}
-    compressed_keys = {name + ".weight" for name in layers}
-    base_state = {key: tensor.detach().cpu().clone() for key, tensor in model.state_dict().items()
-                  if key not in compressed_keys}
-    payload = {
-        "format_version": 1,
-        "layers": layers,
-        "base_state_dict": base_state,
-        "model_config": export_model_config(model_config),
-        "meta": {key: value for key, value in meta.items() if key in allowed_meta},
-    }
-    destination = Path(path)
-    destination.parent.mkdir(parents=True, exist_ok=True)
-    torch.save(payload, destination)
+    in the reference's format (ssalaad/efficient/artifact.py:78-105)."""
+    target = Path(path)
+    target.parent.mkdir(parents=True, exist_ok=True)
+    torch.save(_Bundle.from_model(model, layers, meta, model_config).to_payload(), target)
 
 
 def load_artifact(path: str | Path) -> dict[str, Any]:
     """Read a bundle; anything but a complete version-1 bundle raises
-    ValueError with the reference's messages (reference artifact.py:108-118)."""
-    payload = torch.load(path, map_location="cpu", weights_only=True)
-    required = {"format_version", "layers", "base_state_dict", "model_config", "meta"}
-    if not isinstance(payload, dict) or not required.issubset(payload):
-        raise ValueError("Expected a complete model bundle produced by the compression entry point.")
-    if payload["format_version"] != 1:
-        raise ValueError("Unsupported model bundle version.")
-    return payload
+    ValueError with the reference's messages (ssalaad/efficient/artifact.py:108-118)."""
+    return _Bundle.check_payload(torch.load(path, map_location="cpu", weights_only=True))
 
 
 def module_buffers(S: torch.Tensor, block_p: int, block_q: int):

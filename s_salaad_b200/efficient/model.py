@@ -1,7 +1,7 @@
 """A compressed model with the B200 layers swapped in.
 
-Mirrors ``build_efficient_model`` (``ssalaad/efficient/model.py:11-63``) and
-the model factory it uses (``ssalaad/train/model.py:14-17, 78-94``): the
+The counterpart of ``build_efficient_model`` (``ssalaad/efficient/model.py:11-63``)
+and of the model factory it uses (``ssalaad/train/model.py:14-17, 78-94``): the
 bundle's base weights are loaded into a Hugging Face model built from its
 configuration, and every compressed projection becomes an
 :func:`~s_salaad_b200.efficient.LRSLinear`.  Same arguments, return value
@@ -23,30 +23,43 @@ from .artifact import load_artifact
 from .ls_linear import LRSLinear, _LRSLinearBase
 
 
-def _model_classes() -> dict:
-    from transformers import LlamaConfig, LlamaForCausalLM, Qwen3Config, Qwen3ForCausalLM
+# Architectures a bundle may name (reference ssalaad/train/model.py:14-17).
+_ARCHITECTURES = {"llama": "LlamaForCausalLM", "qwen3": "Qwen3ForCausalLM"}
 
-    return {"llama": (LlamaConfig, LlamaForCausalLM), "qwen3": (Qwen3Config, Qwen3ForCausalLM)}
+
+def _config_kwargs(config: dict, attn_implementation: str | None, overrides: dict) -> dict:
+    """Keyword arguments of the Hugging Face configuration class for a
+    bundle's model configuration: the recipe name max_sequence_length stands
+    for max_position_embeddings (unless that is given too), a pad id of -1
+    means none, the model is built without a KV cache, and non-None
+    overrides win."""
+    has_positions = "max_position_embeddings" in config
+    kwargs = {}
+    for key, value in config.items():
+        if key == "max_sequence_length" and not has_positions:
+            key = "max_position_embeddings"
+        if key == "pad_token_id" and value == -1:
+            value = None
+        kwargs[key] = value
+    kwargs["use_cache"] = False
+    if attn_implementation is not None:
+        kwargs["attn_implementation"] = attn_implementation
+    kwargs.update((k, v) for k, v in overrides.items() if v is not None)
+    return kwargs
 
 
 def build_model_from_config(config: dict, *, attn_implementation: str | None = None, **overrides) -> nn.Module:
-    """A randomly initialised model of the configured architecture
-    (reference ssalaad/train/model.py:78-94)."""
-    config = dict(config)
-    if "max_sequence_length" in config and "max_position_embeddings" not in config:
-        config["max_position_embeddings"] = config.pop("max_sequence_length")
-    if config.get("pad_token_id") == -1:
-        config["pad_token_id"] = None
-    config["use_cache"] = False
-    if attn_implementation is not None:
-        config["attn_implementation"] = attn_implementation
-    config.update({key: value for key, value in overrides.items() if value is not None})
-    classes = _model_classes()
-    model_type = config.get("model_type", "llama")
-    if model_type not in classes:
+    """A randomly initialised model of the configured architecture (the
+    reference's factory, ssalaad/train/model.py:78-94: same arguments and
+    ValueError for an unknown model type)."""
+    import transformers
+
+    kwargs = _config_kwargs(config, attn_implementation, overrides)
+    model_type = kwargs.pop("model_type", "llama")
+    if model_type not in _ARCHITECTURES:
         raise ValueError(f"Unsupported model type: {model_type}")
-    config_cls, model_cls = classes[model_type]
-    return model_cls(config_cls(**config))
+    hf_config = transformers.AutoConfig.for_model(model_type, **kwargs)
+    return getattr(transformers, _ARCHITECTURES[model_type])(hf_config)
 
 
 class _ProjectionGroup:
@@ -114,51 +127,76 @@ def group_projections(model: nn.Module) -> int:
     return count
 
 
+# Error texts of the reference loader (ssalaad/efficient/model.py:11-63), kept
+# because callers match on them.
+_ERR_WEIGHTS = "The bundle does not contain exactly the required model weights."
+
+
+def _check_weight_coverage(model: nn.Module, base_state: dict, layers: dict) -> None:
+    """The bundle's base tensors plus the compressed layers' weights must be
+    exactly the model's state, each tensor from one place."""
+    compressed = {f"{name}.weight" for name in layers}
+    base = set(base_state)
+    if set(model.state_dict()) != base | compressed or base & compressed:
+        raise ValueError(_ERR_WEIGHTS)
+
+
+def _dense_weight(module: nn.Module, data: dict) -> torch.Tensor | None:
+    """The dense weight a compressed entry stands for when it is not served
+    by an S+LR layer: an explicit W, or A·B + S materialised for an
+    embedding; None for a linear layer (it becomes an LRSLinear)."""
+    if "W" in data:
+        return data["W"]
+    if isinstance(module, nn.Embedding):
+        return data["A"].float() @ data["B"].float() + data["S"].to_dense().float()
+    return None
+
+
+def _slr_layer(module: nn.Linear, data: dict, device, dtype) -> nn.Module:
+    """The B200 S+LR layer replacing a compressed nn.Linear."""
+    on = dict(device=device, dtype=dtype)
+    bias = None if module.bias is None else module.bias.detach().to(**on)
+    shape = {k: data.get(k) for k in ("block_p", "block_q", "nm_n", "nm_m")}
+    return LRSLinear(data["A"].to(**on), data["B"].to(**on), data["S"].to(**on), in_features=module.in_features,
+                     out_features=module.out_features, bias=bias, **shape)
+
+
 def build_efficient_model(path, *, device="cuda", dtype=None, group: bool = True):
-    """Load a complete compressed model (reference efficient/model.py:11-63)
-    onto a CUDA device with the B200 kernels; returns (model, model_config, meta)."""
+    """Load a complete compressed model (the reference's
+    ssalaad/efficient/model.py:11-63: same bundle, return value
+    (model, model_config, meta) and errors) onto a CUDA device with the B200
+    kernels.  The loader first checks that the bundle covers the model
+    exactly and that every compressed entry is a linear or embedding module,
+    then loads the base tensors and installs each entry: an S+LR layer for a
+    linear module, a dense weight for an explicit W or an embedding."""
     device = torch.device(device)
     if device.type != "cuda":
         raise ValueError("s_salaad_b200 runs compressed models on CUDA devices only.")
     dtype = dtype or torch.bfloat16
-    payload = load_artifact(path)
-    model = build_model_from_config(payload["model_config"], attn_implementation="sdpa")
-    layers = payload["layers"]
-    missing, unexpected = model.load_state_dict(payload["base_state_dict"], strict=False)
-    expected = {name + ".weight" for name in layers}
-    if set(missing) != expected or unexpected:
-        raise ValueError("The bundle does not contain exactly the required model weights.")
-    model.to(dtype=dtype)
-    for name, data in layers.items():
-        old = model.get_submodule(name)
-        if not isinstance(old, (nn.Linear, nn.Embedding)):
+    bundle = load_artifact(path)
+    model = build_model_from_config(bundle["model_config"], attn_implementation="sdpa")
+    compressed = bundle["layers"]
+    _check_weight_coverage(model, bundle["base_state_dict"], compressed)
+    targets = {}
+    for name in compressed:
+        module = model.get_submodule(name)
+        if not isinstance(module, (nn.Linear, nn.Embedding)):
             raise TypeError(f"Unsupported compressed module: {name}")
-        if "W" in data:
-            weight = data["W"]
-        elif isinstance(old, nn.Embedding):
-            weight = data["A"].float() @ data["B"].float() + data["S"].to_dense().float()
-        else:
-            new = LRSLinear(
-                data["A"].to(device=device, dtype=dtype),
-                data["B"].to(device=device, dtype=dtype),
-                data["S"].to(device=device, dtype=dtype),
-                in_features=old.in_features,
-                out_features=old.out_features,
-                bias=old.bias.detach().to(device=device, dtype=dtype) if old.bias is not None else None,
-                block_p=data.get("block_p"),
-                block_q=data.get("block_q"),
-                nm_n=data.get("nm_n"),
-                nm_m=data.get("nm_m"),
-            )
-            parent_name, _, attr = name.rpartition(".")
-            parent = model.get_submodule(parent_name) if parent_name else model
-            setattr(parent, attr, new)
-            continue
-        if weight.shape != old.weight.shape:
+        targets[name] = module
+    model.load_state_dict(bundle["base_state_dict"], strict=False)
+    model.to(dtype=dtype)
+    for name, module in targets.items():
+        data = compressed[name]
+        weight = _dense_weight(module, data)
+        if weight is None:
+            owner, _, attr = name.rpartition(".")
+            setattr(model.get_submodule(owner) if owner else model, attr, _slr_layer(module, data, device, dtype))
+        elif tuple(weight.shape) != tuple(module.weight.shape):
             raise ValueError(f"Weight shape mismatch: {name}")
-        with torch.no_grad():
-            old.weight.copy_(weight.to(dtype=dtype))
+        else:
+            with torch.no_grad():
+                module.weight.copy_(weight.to(dtype=dtype))
     model = model.to(device=device).eval()
     if group:
         group_projections(model)
-    return model, payload["model_config"], payload["meta"]
+    return model, bundle["model_config"], bundle["meta"]
