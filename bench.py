@@ -49,6 +49,16 @@ def small_kernel_shape(s) -> tuple[int, int]:
     return min(bq, 64), (64 if s.rank >= 64 else 32 if s.rank >= 32 else 16)
 
 
+def multi_launches(specs) -> int:
+    """Launches of one multi-input call over `specs` below 128 tokens: one
+    x*B^T launch, then one combine launch when every layer has a rank and the
+    same small-batch kernel shape, else one per layer (a layer without rank
+    sends every layer through its own forward)."""
+    if any(s.rank <= 0 for s in specs):
+        return sum(2 if s.rank > 0 else 1 for s in specs)
+    return 1 + (1 if len({small_kernel_shape(s) for s in specs}) == 1 else len(specs))
+
+
 def emit(line: dict) -> None:
     """Write the one JSON result line to the original stdout."""
     os.write(_RESULT_FD, (json.dumps(line) + "\n").encode())
@@ -218,6 +228,90 @@ def cpu_model_name() -> str:
 
 # ---------------------------------------------------------------- main --
 
+DECODE_POINTS = ("cfg3-T1", "cfg3-T16", "cfg5-T1", "cfg5-T32")
+
+
+def graph_ms(fn, dev, steps: int, warmup: int, flush: torch.Tensor) -> float:
+    """Mean device time of `fn` replayed from a CUDA graph, L2 flushed
+    between replays (outside the events)."""
+    side = torch.cuda.Stream(dev)
+    cur = torch.cuda.current_stream(dev)
+    side.wait_stream(cur)
+    with torch.cuda.stream(side):
+        for _ in range(max(warmup, 1)):
+            fn()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=side):
+            fn()
+    cur.wait_stream(side)
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize(dev)
+    mk = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
+    ev = [(mk(), mk()) for _ in range(steps)]
+    for a, b in ev:
+        flush.zero_()
+        a.record(cur)
+        graph.replay()
+        b.record(cur)
+    torch.cuda.synchronize(dev)
+    return sum(a.elapsed_time(b) for a, b in ev) / steps
+
+
+def decode_points(dev, steps: int, warmup: int, flush: torch.Tensor, hbm_gbs: float) -> dict:
+    """The decode-sized workloads (HBM-bound) on one GPU, each as
+    * `multi`: the whole projection set as one multi-input call (the inputs are
+      independent in the layer set: 2 launches);
+    * `model_order`: per input group, in decoder order (q/k/v grouped, o,
+      gate/up grouped, down), as a model that chains them would call them.
+    Algorithmic bytes: weights and indices of every projection plus x and y
+    (2 bytes per element); frac = achieved / measured HBM peak."""
+    from s_salaad_b200 import ops, workloads
+
+    out = {}
+    for name in DECODE_POINTS:
+        cfg, T = parse_workload(name)
+        specs = workloads.layer_set(cfg)
+        roles = input_roles(specs)
+        layers = []
+        for s in specs:
+            t = s.tensors(dev, torch.bfloat16)
+            order = torch.from_numpy(ops.plan_row_order(s.crow.astype(np.int32))).to(dev)
+            layers.append(ops.LayerDesc(A=t["A"], B=t["B"], bias=t["bias"], crow=t["S_crow"], col=t["S_col"],
+                                        values=t["S_values"], row_order=order, in_features=s.in_features,
+                                        out_features=s.out_features, block_p=s.block_p, block_q=s.block_q))
+        xin = {}
+        for i, s in enumerate(specs):
+            xin.setdefault(roles[i], workloads.tokens(T, s.in_features, seed=100 + roles[i], device=dev,
+                                                      dtype=torch.bfloat16))
+        xs = [xin[roles[i]] for i in range(len(specs))]
+        ys = [torch.empty(T, s.out_features, dtype=torch.bfloat16, device=dev) for s in specs]
+        lset = ops.LayerSet(layers)
+        members: dict[int, list[int]] = {}
+        for i, r in enumerate(roles):
+            members.setdefault(r, []).append(i)
+        groups = {r: ops.LayerGroup([layers[i] for i in idx]) for r, idx in members.items() if len(idx) > 1}
+
+        def chained():
+            for r, idx in members.items():
+                if r in groups:
+                    groups[r].forward(xs[idx[0]], [ys[i] for i in idx])
+                else:
+                    for i in idx:
+                        layers[i].forward(xs[i], ys[i])
+
+        nbytes = sum(s.weight_bytes(2) + 2 * T * (s.in_features + s.out_features) for s in specs)
+        ms = graph_ms(lambda: lset.forward(xs, ys), dev, steps, warmup, flush)
+        ms_chain = graph_ms(chained, dev, steps, warmup, flush)
+        gbs, gbs_chain = nbytes / (ms / 1e3) / 1e9, nbytes / (ms_chain / 1e3) / 1e9
+        out[name] = {"ms_per_step": ms, "tokens_per_s": T / (ms / 1e3), "algorithmic_bytes": nbytes,
+                     "achieved_gbs": gbs, "frac": gbs / hbm_gbs, "launches": multi_launches(specs),
+                     "model_order": {"ms_per_step": ms_chain, "achieved_gbs": gbs_chain, "frac": gbs_chain / hbm_gbs}}
+        del layers, lset, groups, xs, ys, xin
+        torch.cuda.empty_cache()
+    return out
+
+
 def model_bench(args) -> None:
     """cfg2 as a whole model: the 8-layer LLaMA-60M-shaped model of a
     synthetic bundle, loaded by build_efficient_model (every projection an
@@ -306,11 +400,12 @@ def main() -> None:
     ap.add_argument("--cpu-budget-s", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-cublas", action="store_true")
+    ap.add_argument("--no-decode", action="store_true", help="skip the decode points of the headline run")
     ap.add_argument("--ncu", action="store_true",
                     help="profiling mode: warm-up + timed steps only (no e2e, cuBLAS or CPU legs)")
     args = ap.parse_args()
     if args.ncu:
-        args.no_cublas = args.no_cpu_baseline = True
+        args.no_cublas = args.no_cpu_baseline = args.no_decode = True
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
 
@@ -405,6 +500,9 @@ def main() -> None:
         _lib.load().slr_set_sm_limit(_lib.load_sm_count() - SMS_FOR_NCCL)
     ys = ([po.y for po in pos] if pos is not None else
           [torch.empty(T, s.out_features, dtype=dtype, device=dev) for s in specs])
+    # one GPU, decode-sized batch: the projections (independent inputs) run as
+    # one slr_lrs_linear_forward_multi call
+    lset = ops.LayerSet(layers) if (world == 1 and T < 128 and dtype != torch.float32) else None
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
 
@@ -467,6 +565,10 @@ def main() -> None:
                     L.finish_peers(pos[i])
                 else:
                     L.finish(handles[i], ys[i])
+            return
+        if lset is not None and ev is None:
+            # decode-sized batch: every projection in one multi-input call (2 launches)
+            lset.forward(xs, ys)
             return
         for r, idx in members.items():
             grp = groups.get(r)
@@ -586,7 +688,8 @@ def main() -> None:
         op_bytes = sum(s.weight_bytes(esize) + esize * T * (s.in_features + s.out_features) for s in specs)
         achieved = op_bytes * K / (total_ms / 1e3) / 1e9
         roof = {"bound": "hbm", "unit": "GB/s", "algorithmic_per_step": op_bytes,
-                "kernel": "layer set from a CUDA graph: x*B^T + combine kernels of all projections"}
+                "kernel": "layer set from a CUDA graph: one multi-input call (x*B^T launch + combine launch) "
+                          "over all projections"}
         peak = P["hbm_gbs"]
     elif tensor_bound:
         achieved = comb_flops * K / comb_s / 1e12
@@ -623,10 +726,10 @@ def main() -> None:
     launches_per_step = sum((1 if s.rank > 0 else 0) + 1 for i, s in enumerate(specs) if has_local[i])
     for r, grp in groups.items():  # one x*B^T launch per group
         launches_per_step -= len(members[r]) - 1
+    if lset is not None:
+        launches_per_step = multi_launches(specs)
     if pos is not None:
         launches_per_step += len(specs)  # the wait that ends each projection's call
-        if T < 128 and world == 1 and len({small_kernel_shape(specs[i]) for i in members[r]}) == 1:
-            launches_per_step -= len(members[r]) - 1  # and one combine launch
 
     # ------------------------------------------------------------- e2e
     x_host = {r: xin[r].cpu().pin_memory() for r in xin}
@@ -647,6 +750,12 @@ def main() -> None:
             return
         for r in xin:
             xin_dev[r].copy_(x_host[r], non_blocking=True)
+        if lset is not None:
+            lset.forward([xin_dev[roles[i]] for i in range(len(specs))], ys)
+            if rank == 0:
+                for i in range(len(specs)):
+                    y_host[i].copy_(ys[i], non_blocking=True)
+            return
         for r, idx in members.items():
             x_r = xin_dev[r]
             if r in groups:
@@ -760,6 +869,11 @@ def main() -> None:
                   "W = A*B + S in bf16, same shapes and inputs"}
         del Ws
 
+    # ------------------------------------------- decode points (N=1 headline)
+    decode = None
+    if world == 1 and args.workload == "cfg4" and not args.no_decode:
+        decode = decode_points(dev, max(K, 20), args.warmup, flush, P["hbm_gbs"])
+
     # ------------------------------------------------------- CPU baseline
     cpu = None
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
@@ -787,6 +901,11 @@ def main() -> None:
                                           "d2h_bytes_per_step": d2h},
                 "gpu_launches": launches_per_step * K, "clocks": clocks.summary(),
                 "cpu_baseline": cpu, "cublas_dense": cublas}
+        if decode is not None:
+            line["decode"] = {"what": "decode-sized layer sets on 1 GPU, each step replayed from a CUDA graph with L2 "
+                                      "flushed between steps; roofline = algorithmic bytes (weights, indices, x, y) "
+                                      "per step / time, against the measured HBM peak",
+                              "peak_gbs": P["hbm_gbs"], "points": decode}
         emit(line)
     if world > 1:
         del graph  # a graph holding NCCL calls must go before the process group

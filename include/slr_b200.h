@@ -268,6 +268,27 @@ SLR_API int slr_lrs_linear_group_combine(const slr_layer* layers, int n, int i,
                            const void* x, int64_t ldx, void* y, int64_t ldy, int64_t M,
                            void* workspace, size_t workspace_bytes, void* stream);
 
+/*
+ * n (1..8) layers, each with its own input: y[i] = x[i] · S_iᵀ +
+ * (x[i] · B_iᵀ) · A_iᵀ + bias_i for i < n, the result of
+ * slr_lrs_linear_forward on each layer bit for bit.  It serves a step that
+ * runs independent projections side by side (a layer set whose inputs are
+ * all ready, or the same projection of several models); layers may also
+ * share an input (pass the same pointer).  Below 128 tokens, when every layer
+ * takes the 16-bit small-batch path and has a rank, all x[i] · B_iᵀ products
+ * are one launch and the combine phases of all layers one more launch (when
+ * their block and rank-chunk shapes agree; else one per layer), instead of
+ * two launches per layer.  From 128 tokens on the layers run one forward
+ * each.  Layers share the dtype; ldx / ldy may be NULL (packed rows).  The
+ * workspace rules are those of slr_lrs_linear_forward.  No reference
+ * counterpart (the reference calls its layers one by one,
+ * ssalaad/efficient/ls_linear.py:124-137).
+ */
+SLR_API size_t slr_lrs_linear_multi_workspace_size(const slr_layer* layers, int n, int64_t M);
+SLR_API int slr_lrs_linear_forward_multi(const slr_layer* layers, int n, const void* const* x,
+                           const int64_t* ldx, void* const* y, const int64_t* ldy, int64_t M,
+                           void* workspace, size_t workspace_bytes, void* stream);
+
 /* --------------------------------------------------- dense -> BSR -- */
 
 /*

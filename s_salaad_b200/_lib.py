@@ -59,6 +59,8 @@ EXPORTED = (
     "slr_lrs_linear_group_combine_peers",
     "slr_peers_wait",
     "slr_set_wait_limit_ns",
+    "slr_lrs_linear_multi_workspace_size",
+    "slr_lrs_linear_forward_multi",
 )
 
 SLR_MAX_RANKS = 8
@@ -137,6 +139,9 @@ _SIGS = {
                                             ctypes.POINTER(SlrPeers), vp], i32),
     "slr_peers_wait": ([ctypes.POINTER(SlrPeers), i32, vp], i32),
     "slr_set_wait_limit_ns": ([ctypes.c_uint64], i32),
+    "slr_lrs_linear_multi_workspace_size": ([ctypes.POINTER(SlrLayer), i32, i64], sz),
+    "slr_lrs_linear_forward_multi": ([ctypes.POINTER(SlrLayer), i32, ctypes.POINTER(vp), ctypes.POINTER(i64),
+                                      ctypes.POINTER(vp), ctypes.POINTER(i64), i64, vp, sz, vp], i32),
 }
 
 _lock = threading.Lock()

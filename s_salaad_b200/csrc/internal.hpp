@@ -42,32 +42,43 @@ int launch_simt_rowblock(const RowblockArgs& a, bool h_f32, cudaStream_t s);
 // ---- mma.sync + TMA kernels (16-bit dtypes): small token batches.
 // Layers sharing one x that a grouped call runs as one launch.
 constexpr int kMaxGroupLayers = 4;
+// Layers (each with its own x, or groups sharing one) in one small-batch launch.
+constexpr int kMaxLaunchLayers = 8;
 
-// x·Bᵀ for 1..kMaxGroupLayers weight segments (one layer each) into one H
-// [M, ldh]: segment s owns the 16-row tiles [seg_rt[s], seg_rt[s + 1]) of H's
-// columns and splits K as it would alone.
+// x·Bᵀ for 1..kMaxLaunchLayers weight segments (one layer each) into one H
+// [M, ldh]: segment s reads its own x (segments of a group share one), owns
+// the 16-row tiles [seg_rt[s], seg_rt[s + 1]) of H's columns and splits K as
+// it would alone.
 struct HSmallPlan {
   int tt = 8;        // tokens per CTA (8 * NT)
   int tc = 0;        // token chunks
   int nseg = 0;
   int rt = 0;        // 16-column tiles of H over all segments (ldh / 16)
   int ks_max = 1;    // largest K split of a segment
-  int seg_rt[kMaxGroupLayers + 1] = {};
-  int ks[kMaxGroupLayers] = {};
-  int64_t kchunk[kMaxGroupLayers] = {};
+  int seg_rt[kMaxLaunchLayers + 1] = {};
+  int ks[kMaxLaunchLayers] = {};
+  int64_t kchunk[kMaxLaunchLayers] = {};
 };
-// ldh[s]: columns of H owned by segment s (a multiple of 16, >= r_s).
-HSmallPlan plan_h_small(int64_t M, int64_t K, const int64_t* ldh, int nseg);
-int launch_h_small(const void* x, int64_t ldx, const void* const* B, const int64_t* r, void* H, int64_t M,
-                   int64_t K, int64_t ldh, const HSmallPlan& plan, int dtype, bool pdl, cudaStream_t s);
+// K[s]: input width of segment s; ldh[s]: columns of H owned by segment s (a
+// multiple of 16, >= r_s).
+HSmallPlan plan_h_small(int64_t M, const int64_t* K, const int64_t* ldh, int nseg);
+// pdl: may start while the preceding kernel runs (B loads only before the
+// wait).  Either way the next kernel can start only after this one's wait,
+// so it may read anything the kernels before this one wrote (x_early below).
+int launch_h_small(const void* const* x, const int64_t* ldx, const void* const* B, const int64_t* r, void* H,
+                   int64_t M, const int64_t* K, int64_t ldh, const HSmallPlan& plan, int dtype, bool pdl,
+                   cudaStream_t s);
 bool mma_rowblock_supported(int bp, int bq, int64_t K, int64_t r);
-int launch_mma_rowblock(const RowblockArgs& a, bool pdl, cudaStream_t s);
-// Layers that read one x and one H [M, ldh] (layer i's columns from h_col[i])
-// in one launch; false from mma_group_compatible when their shapes need
-// different kernel instances.
-bool mma_group_compatible(const RowblockArgs* a, int n);
+// x_early: the kernel issued just before is this call's h_small, so x is
+// complete at launch and the combine reads it before griddepcontrol.wait.
+int launch_mma_rowblock(const RowblockArgs& a, bool pdl, cudaStream_t s, bool x_early = false);
+// Layers that read one H [M, ldh] (layer i's columns from h_col[i]), each its
+// own x (or one shared x), in one launch; false from mma_group_compatible
+// when their shapes need different kernel instances (or, with shared_x, when
+// they do not read one x).
+bool mma_group_compatible(const RowblockArgs* a, int n, bool shared_x);
 int launch_mma_rowblock_group(const RowblockArgs* a, const int64_t* h_col, int n, const void* H, int64_t ldh,
-                              bool pdl, cudaStream_t s);
+                              bool pdl, cudaStream_t s, bool x_early = false);
 
 // ---- peer memory: a rank's output tiles stored straight into every rank's y.
 // Signal slot of one layer on each rank (SLR_SIGNAL_WORDS x u64, zero at start).

@@ -36,7 +36,7 @@ constexpr int kFT = 16;  // output features per CTA (one m16 tile)
 // (1024-aligned for its swizzle).
 constexpr uint32_t kHOff = 2048;
 
-constexpr int kMaxLayers = kMaxGroupLayers;  // layers (sharing x) per launch
+constexpr int kMaxLayers = kMaxLaunchLayers;  // layers per launch
 constexpr int kMaxKSplit = 8;                 // h_small K-chunks per tile (one cluster)
 
 // One layer of a launch; its CTAs are [cta0, cta0 + nrows * ft_per_row).
@@ -58,14 +58,15 @@ struct MmaLayer {
 struct MmaArgs {
   int64_t M;
   int n;
-  int stages;  // ring slots of this launch (fewer slots -> more CTAs per SM)
+  int stages;   // ring slots of this launch (fewer slots -> more CTAs per SM)
+  int x_early;  // x is complete at launch: read it before griddepcontrol.wait
   MmaLayer L[kMaxLayers];
 };
-// Tensor maps: x and H are shared by the layers of a launch (H column
-// offsets per layer), values and A are per layer.
+// Tensor maps: H is shared by the layers of a launch (H column offsets per
+// layer); x, values and A are per layer (layers of a group share one x).
 struct MmaMaps {
-  CUtensorMap x, h;
-  CUtensorMap v[kMaxLayers], a[kMaxLayers];
+  CUtensorMap h;
+  CUtensorMap x[kMaxLayers], v[kMaxLayers], a[kMaxLayers];
 };
 
 __device__ __forceinline__ void ldsm_x2(uint32_t addr, uint32_t& r0, uint32_t& r1) {
@@ -85,10 +86,15 @@ __device__ __forceinline__ void ldsm_x2(uint32_t addr, uint32_t& r0, uint32_t& r
 // CTA touches weights only -- the value and A boxes of the first ring-full of
 // stages go to shared memory, those of later stages to L2, bias to shared
 // memory -- so a decode step streams its weights while the previous kernel
-// finishes.  x, H and y are read or written only after the wait.
+// finishes.  H and y are read or written only after the wait; x too, unless
+// x_early says that x was complete when the kernel was launched (the
+// preceding kernel is this call's h_small, which lets dependents start only
+// after its own wait on the kernel before it): the sparse stages then run
+// while h_small computes H, and the wait comes before the first H load.
 //
-// Several layers that read the same x (q/k/v, gate/up) run in one launch:
-// the grid is the concatenation of their CTA ranges.
+// Several layers run in one launch (q/k/v or gate/up sharing one x, or
+// independent projections each with its own x): the grid is the
+// concatenation of their CTA ranges.
 template <int NT, int KX, typename TI, int MODE>
 __global__ void __launch_bounds__(kThreads)
     mma_rowblock_kernel(const __grid_constant__ MmaMaps maps, const __grid_constant__ MmaArgs ga) {
@@ -97,7 +103,7 @@ __global__ void __launch_bounds__(kThreads)
   const MmaLayer& a = ga.L[li];
   const CUtensorMap& tm_vals = maps.v[li];
   const CUtensorMap& tm_A = maps.a[li];
-  const CUtensorMap& tm_x = maps.x;
+  const CUtensorMap& tm_x = maps.x[li];
   const CUtensorMap& tm_h = maps.h;
   const int cta = int(blockIdx.x) - a.cta0;
   constexpr int TT = 8 * NT;                 // tokens per CTA
@@ -195,7 +201,9 @@ __global__ void __launch_bounds__(kThreads)
         for (int c = (s - n_sp) * a.lrc; c < min(n_chunks, (s - n_sp + 1) * a.lrc); ++c)
           tma_prefetch_l2_2d(&tm_A, c * a.kc, br * a.bp + f0);
     }
-    pdl_wait_primary();  // x and H come from preceding kernels
+    // x and H come from preceding kernels (x may already be complete, see x_early)
+    bool waited = !ga.x_early;
+    if (waited) pdl_wait_primary();
     __syncwarp();
     // Activations of the pre-filled stages.
 #pragma unroll
@@ -208,10 +216,16 @@ __global__ void __launch_bounds__(kThreads)
             for (int h = 0; h < nsub; ++h)
               tma_load_2d(dst + v_slot + (lane * nsub + h) * XB, &tm_x, colr[s] * a.bq + h * KX, int(t0),
                           &full[s]);
-        } else if (lane == 0) {
-          const int c0 = (s - n_sp) * a.lrc, nch = min(a.lrc, n_chunks - c0);
-          for (int c = 0; c < nch; ++c)
-            tma_load_2d(dst + c * cs + kHOff, &tm_h, a.h_col0 + (c0 + c) * a.kc, int(t0), &full[s]);
+        } else {
+          if (!waited) {
+            pdl_wait_primary();  // H is written by the preceding kernel
+            waited = true;
+          }
+          if (lane == 0) {
+            const int c0 = (s - n_sp) * a.lrc, nch = min(a.lrc, n_chunks - c0);
+            for (int c = 0; c < nch; ++c)
+              tma_load_2d(dst + c * cs + kHOff, &tm_h, a.h_col0 + (c0 + c) * a.kc, int(t0), &full[s]);
+          }
         }
       }
     }
@@ -241,12 +255,18 @@ __global__ void __launch_bounds__(kThreads)
         if (lane < nb)
           for (int h = 0; h < nsub; ++h)
             tma_load_2d(dst + v_slot + (lane * nsub + h) * XB, &tm_x, c * a.bq + h * KX, int(t0), &full[slot]);
-      } else if (lane == 0) {
-        const int c0 = (s - n_sp) * a.lrc, nch = min(a.lrc, n_chunks - c0);
-        mbar_arrive_expect_tx(&full[slot], uint32_t(nch) * chunk_bytes);
-        for (int c = 0; c < nch; ++c) {
-          tma_load_2d(dst + c * cs, &tm_A, (c0 + c) * a.kc, br * a.bp + f0, &full[slot]);
-          tma_load_2d(dst + c * cs + kHOff, &tm_h, a.h_col0 + (c0 + c) * a.kc, int(t0), &full[slot]);
+      } else {
+        if (!waited) {
+          pdl_wait_primary();  // H is written by the preceding kernel
+          waited = true;
+        }
+        if (lane == 0) {
+          const int c0 = (s - n_sp) * a.lrc, nch = min(a.lrc, n_chunks - c0);
+          mbar_arrive_expect_tx(&full[slot], uint32_t(nch) * chunk_bytes);
+          for (int c = 0; c < nch; ++c) {
+            tma_load_2d(dst + c * cs, &tm_A, (c0 + c) * a.kc, br * a.bp + f0, &full[slot]);
+            tma_load_2d(dst + c * cs + kHOff, &tm_h, a.h_col0 + (c0 + c) * a.kc, int(t0), &full[slot]);
+          }
         }
       }
     }
@@ -347,10 +367,11 @@ __global__ void __launch_bounds__(kThreads)
 // keeps the K split (ks[s] chunks of kchunk[s]) it would get alone, so a
 // grouped call computes every layer's H bit for bit as a call on that layer.
 struct HArgs {
-  const void* x;
+  const void* x[kMaxLayers];  // segment s reads x[s] [M, K[s]] (row stride ldx[s])
   const void* B[kMaxLayers];
   void* H;
-  int64_t M, K, ldx;
+  int64_t M;
+  int64_t K[kMaxLayers], ldx[kMaxLayers];
   int64_t kchunk[kMaxLayers];
   int r[kMaxLayers];
   int ks[kMaxLayers];
@@ -376,9 +397,14 @@ __device__ __forceinline__ float ld_shared_cluster_f32(uint32_t addr) {
 // a tile are the CTAs of one cluster (gridDim.y = ks_max): each leaves its
 // partial sum in shared memory and CTA 0 of the cluster adds them in chunk
 // order through distributed shared memory and writes H.
+//
+// Launch order: a CTA loads its first B slices, waits for the preceding
+// kernel (griddepcontrol.wait), and only then lets the next kernel start
+// (griddepcontrol.launch_dependents).  So when the next kernel starts, every
+// kernel before this one has completed: this call's combine may read x at
+// once and need wait only for H.
 template <int NT, typename TI>
 __global__ void __launch_bounds__(128) h_small_kernel(const __grid_constant__ HArgs a) {
-  pdl_launch_dependents();
   constexpr int TT = 8 * NT;
   __shared__ float red[4][16][TT];
   __shared__ float part[16 * TT];  // this CTA's partial sum, [t][m]
@@ -388,16 +414,21 @@ __global__ void __launch_bounds__(128) h_small_kernel(const __grid_constant__ HA
   int sg = 0;
   while (sg + 1 < a.nseg && rt >= a.seg_rt[sg + 1]) ++sg;
   const int nks = a.ks[sg];
-  if (ks < nks) {  // CTAs past the segment's K split only take part in the cluster barriers
+  if (ks >= nks) {
+    // past the segment's K split: only the launch order and the cluster barriers
+    pdl_wait_primary();
+    pdl_launch_dependents();
+  } else {
     const int64_t t0 = int64_t(tc) * TT;
+    const int64_t K = a.K[sg], ldx = a.ldx[sg];
     const int64_t kb = int64_t(ks) * a.kchunk[sg];
-    const int64_t ke = min(a.K, kb + a.kchunk[sg]);
-    const TI* __restrict__ x = static_cast<const TI*>(a.x);
+    const int64_t ke = min(K, kb + a.kchunk[sg]);
+    const TI* __restrict__ x = static_cast<const TI*>(a.x[sg]);
     const TI* __restrict__ B = static_cast<const TI*>(a.B[sg]);
     const int lrow = 16 * (rt - a.seg_rt[sg]);  // first row of this tile within B_sg
     const bool v0 = lrow + g < a.r[sg], v1 = lrow + g + 8 < a.r[sg];
-    const TI* B0 = B + int64_t(lrow + g) * a.K;
-    const TI* B1 = B + int64_t(lrow + g + 8) * a.K;
+    const TI* B0 = B + int64_t(lrow + g) * K;
+    const TI* B1 = B + int64_t(lrow + g + 8) * K;
 
     float acc[NT][4];
   #pragma unroll
@@ -410,7 +441,7 @@ __global__ void __launch_bounds__(128) h_small_kernel(const __grid_constant__ HA
   #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
         const int64_t t = t0 + 8 * nt + g;
-        const uint4 X = (t < a.M && kin) ? ldg_u128(x + t * a.ldx + kk) : z;
+        const uint4 X = (t < a.M && kin) ? ldg_u128(x + t * ldx + kk) : z;
         const uint32_t s0[4] = {A0.x, A1.x, A0.y, A1.y};
         const uint32_t s1[4] = {A0.z, A1.z, A0.w, A1.w};
         mma16816<TI>::run(acc[nt], s0, X.x, X.y);
@@ -430,6 +461,7 @@ __global__ void __launch_bounds__(128) h_small_kernel(const __grid_constant__ HA
       pa1[i] = (v1 && kin) ? ldg_u128(B1 + kk) : z;
     }
     pdl_wait_primary();
+    pdl_launch_dependents();
   #pragma unroll
     for (int i = 0; i < kPre; ++i) {
       const int64_t k = kb + 32 * warp + 128 * i;
@@ -607,7 +639,7 @@ bool is_sparse(const RowblockArgs& a) { return a.crow != nullptr && a.nnz > 0; }
 int eff_bq(const RowblockArgs& a) { return is_sparse(a) ? a.bq : 16; }
 
 // Layer `a` as entry li of a launch: its MmaLayer (CTAs from cta0) and its
-// value / A tensor maps.  Returns the layer's ring slot bytes in *stage.
+// x / value / A tensor maps.  Returns the layer's ring slot bytes in *stage.
 int fill_layer(const RowblockArgs& a, int tt, int cta0, int64_t h_col, MmaMaps& maps, MmaArgs& k, int li,
                uint32_t* stage) {
   const bool sparse = is_sparse(a);
@@ -623,6 +655,10 @@ int fill_layer(const RowblockArgs& a, int tt, int cta0, int64_t h_col, MmaMaps& 
     rc = make_tmap_2d(&maps.v[li], a.values, a.dtype, uint64_t(a.bp), uint64_t(a.nnz) * a.bq,
                       uint64_t(a.bp) * 2, uint32_t(kFT), uint32_t(sh.sb * a.bq));
     if (rc) return rc;
+    // x box: tt tokens x kx columns
+    rc = make_tmap_2d(&maps.x[li], a.x, a.dtype, uint64_t(a.K), uint64_t(a.M), uint64_t(a.ldx) * 2,
+                      uint32_t(sh.kx), uint32_t(tt));
+    if (rc) return rc;
   }
   if (r > 0) {
     rc = make_tmap_2d(&maps.a[li], a.A, a.dtype, uint64_t(a.r), uint64_t(a.N), uint64_t(a.r) * 2,
@@ -632,23 +668,13 @@ int fill_layer(const RowblockArgs& a, int tt, int cta0, int64_t h_col, MmaMaps& 
   return SLR_OK;
 }
 
-// x map (box: tt tokens x kx columns) and H map (box: tt x kc; kc is 16, 32
-// or 64 and the same box serves every layer of a launch only when their kc
-// agree, which mma_group_compatible checks).
-int fill_shared_maps(const RowblockArgs& a0, int tt, int kx, int kc, bool any_sparse, const void* H, int64_t ldh,
-                     MmaMaps& maps) {
-  int rc;
-  if (any_sparse) {
-    rc = make_tmap_2d(&maps.x, a0.x, a0.dtype, uint64_t(a0.K), uint64_t(a0.M), uint64_t(a0.ldx) * 2,
-                      uint32_t(kx), uint32_t(tt));
-    if (rc) return rc;
-  }
-  if (kc > 0) {
-    rc = make_tmap_2d(&maps.h, H, a0.dtype, uint64_t(ldh), uint64_t(a0.M), uint64_t(ldh) * 2, uint32_t(kc),
+// H map (box: tt x kc; kc is 16, 32 or 64 and the same box serves every
+// layer of a launch only when their kc agree, which mma_group_compatible
+// checks).
+int fill_h_map(const RowblockArgs& a0, int tt, int kc, const void* H, int64_t ldh, MmaMaps& maps) {
+  if (kc <= 0) return SLR_OK;
+  return make_tmap_2d(&maps.h, H, a0.dtype, uint64_t(ldh), uint64_t(a0.M), uint64_t(ldh) * 2, uint32_t(kc),
                       uint32_t(tt));
-    if (rc) return rc;
-  }
-  return SLR_OK;
 }
 
 int launch_maps(const RowblockArgs& a0, int kx, int tt, const MmaMaps& maps, const MmaArgs& k, uint32_t stage,
@@ -665,14 +691,15 @@ int launch_maps(const RowblockArgs& a0, int kx, int tt, const MmaMaps& maps, con
 
 }  // namespace
 
-HSmallPlan plan_h_small(int64_t M, int64_t K, const int64_t* ldh, int nseg) {
+HSmallPlan plan_h_small(int64_t M, const int64_t* Ks, const int64_t* ldh, int nseg) {
   HSmallPlan p;
   p.tt = pick_tt(M);
   p.tc = int(ceil_div(std::max<int64_t>(M, 1), p.tt));
   p.nseg = nseg;
-  // at most 8 K-chunks: they reduce within one (portable-size) cluster
-  const int64_t max_split = std::min<int64_t>(kMaxKSplit, std::max<int64_t>(1, ceil_div(K, 128)));
   for (int sg = 0; sg < nseg; ++sg) {
+    const int64_t K = Ks[sg];
+    // at most 8 K-chunks: they reduce within one (portable-size) cluster
+    const int64_t max_split = std::min<int64_t>(kMaxKSplit, std::max<int64_t>(1, ceil_div(K, 128)));
     const int rt = int(ldh[sg] / 16);
     p.seg_rt[sg] = p.rt;
     p.rt += rt;
@@ -688,22 +715,23 @@ HSmallPlan plan_h_small(int64_t M, int64_t K, const int64_t* ldh, int nseg) {
   return p;
 }
 
-int launch_h_small(const void* x, int64_t ldx, const void* const* B, const int64_t* r, void* H, int64_t M,
-                   int64_t K, int64_t ldh, const HSmallPlan& plan, int dtype, bool pdl, cudaStream_t s) {
+int launch_h_small(const void* const* x, const int64_t* ldx, const void* const* B, const int64_t* r, void* H,
+                   int64_t M, const int64_t* K, int64_t ldh, const HSmallPlan& plan, int dtype, bool pdl,
+                   cudaStream_t s) {
   if (M <= 0 || plan.rt <= 0) return SLR_OK;
   if (plan.nseg < 1 || plan.nseg > kMaxLayers || int64_t(plan.rt) * 16 > ldh)
     return fail(SLR_ERR_INVALID_ARGUMENT, "h_small: bad segment plan");
   HArgs a{};
-  a.x = x;
   a.H = H;
   a.M = M;
-  a.K = K;
-  a.ldx = ldx;
   a.nseg = plan.nseg;
   a.ldh = int(ldh);
   a.ks_max = plan.ks_max;
   a.rt = plan.rt;
   for (int sg = 0; sg < plan.nseg; ++sg) {
+    a.x[sg] = x[sg];
+    a.ldx[sg] = ldx[sg];
+    a.K[sg] = K[sg];
     a.B[sg] = B[sg];
     a.r[sg] = int(r[sg]);
     a.ks[sg] = plan.ks[sg];
@@ -725,7 +753,7 @@ bool mma_rowblock_supported(int bp, int bq, int64_t K, int64_t r) {
   return true;
 }
 
-int launch_mma_rowblock(const RowblockArgs& a, bool pdl, cudaStream_t s) {
+int launch_mma_rowblock(const RowblockArgs& a, bool pdl, cudaStream_t s, bool x_early) {
   if (a.nrows <= 0 || a.M <= 0) return SLR_OK;
   if (a.ldx % 8 != 0 || !aligned16(a.x)) return fail(SLR_ERR_UNSUPPORTED, "mma path: x must be 16-byte aligned");
   const int tt = pick_tt(a.M);
@@ -735,22 +763,24 @@ int launch_mma_rowblock(const RowblockArgs& a, bool pdl, cudaStream_t s) {
   MmaArgs k{};
   k.M = a.M;
   k.n = 1;
+  k.x_early = x_early ? 1 : 0;
   uint32_t stage = 0;
   int rc = fill_layer(a, tt, 0, 0, maps, k, 0, &stage);
   if (rc) return rc;
-  rc = fill_shared_maps(a, tt, sh.kx, r > 0 ? sh.kc : 0, is_sparse(a), a.H, a.ldh, maps);
+  rc = fill_h_map(a, tt, r > 0 ? sh.kc : 0, a.H, a.ldh, maps);
   if (rc) return rc;
   return launch_maps(a, sh.kx, tt, maps, k, stage, int(a.nrows * (a.bp / kFT)), pdl, s);
 }
 
-bool mma_group_compatible(const RowblockArgs* a, int n) {
+bool mma_group_compatible(const RowblockArgs* a, int n, bool shared_x) {
   if (n < 1 || n > kMaxLayers) return false;
   const int tt = pick_tt(a[0].M);
   const MmaShape s0 = mma_shape(eff_bq(a[0]), a[0].mode == MODE_FUSED ? int(a[0].r) : 0, tt);
   for (int i = 0; i < n; ++i) {
-    if (a[i].M != a[0].M || a[i].x != a[0].x || a[i].ldx != a[0].ldx || a[i].K != a[0].K ||
-        a[i].dtype != a[0].dtype || a[i].mode != MODE_FUSED || a[i].r <= 0)
+    if (a[i].M != a[0].M || a[i].dtype != a[0].dtype || a[i].mode != MODE_FUSED || a[i].r <= 0)
       return false;
+    if (shared_x && (a[i].x != a[0].x || a[i].ldx != a[0].ldx || a[i].K != a[0].K)) return false;
+    if (a[i].ldx % 8 != 0 || !aligned16(a[i].x)) return false;
     const MmaShape si = mma_shape(eff_bq(a[i]), int(a[i].r), tt);
     if (si.kx != s0.kx || si.kc != s0.kc) return false;
   }
@@ -758,28 +788,26 @@ bool mma_group_compatible(const RowblockArgs* a, int n) {
 }
 
 int launch_mma_rowblock_group(const RowblockArgs* a, const int64_t* h_col, int n, const void* H, int64_t ldh,
-                              bool pdl, cudaStream_t s) {
-  if (!mma_group_compatible(a, n)) return fail(SLR_ERR_INVALID_ARGUMENT, "mma group: layers need one kernel shape");
+                              bool pdl, cudaStream_t s, bool x_early) {
+  if (!mma_group_compatible(a, n, false)) return fail(SLR_ERR_INVALID_ARGUMENT, "mma group: layers need one kernel shape");
   if (a[0].M <= 0) return SLR_OK;
-  if (a[0].ldx % 8 != 0 || !aligned16(a[0].x)) return fail(SLR_ERR_UNSUPPORTED, "mma path: x must be 16-byte aligned");
   const int tt = pick_tt(a[0].M);
   const MmaShape sh = mma_shape(eff_bq(a[0]), int(a[0].r), tt);
   MmaMaps maps{};
   MmaArgs k{};
   k.M = a[0].M;
   k.n = n;
+  k.x_early = x_early ? 1 : 0;
   uint32_t stage = 0;
   int ctas = 0;
-  bool any_sparse = false;
   for (int i = 0; i < n; ++i) {
     uint32_t si = 0;
     int rc = fill_layer(a[i], tt, ctas, h_col[i], maps, k, i, &si);
     if (rc) return rc;
     stage = std::max(stage, si);
     ctas += int(a[i].nrows * (a[i].bp / kFT));
-    any_sparse = any_sparse || is_sparse(a[i]);
   }
-  int rc = fill_shared_maps(a[0], tt, sh.kx, sh.kc, any_sparse, H, ldh, maps);
+  int rc = fill_h_map(a[0], tt, sh.kc, H, ldh, maps);
   if (rc) return rc;
   if (ctas == 0) return SLR_OK;
   return launch_maps(a[0], sh.kx, tt, maps, k, stage, ctas, pdl, s);

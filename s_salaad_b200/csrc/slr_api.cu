@@ -132,7 +132,7 @@ FwdPlan plan_forward(const slr_layer& L, int64_t M, const void* x) {
   p.ldh = L.rank > 0 ? round_up(L.rank, 64) : 0;
   const size_t hes = (p.path == 0 && !is16) ? 4 : dtype_size(L.dtype);
   p.h_bytes = align256(size_t(std::max<int64_t>(M, 0)) * p.ldh * hes);
-  if (p.path == 1 && L.rank > 0) p.hs = plan_h_small(M, L.in_features, &p.ldh, 1);
+  if (p.path == 1 && L.rank > 0) p.hs = plan_h_small(M, &L.in_features, &p.ldh, 1);
   p.total = p.h_bytes;
   return p;
 }
@@ -387,22 +387,32 @@ int run_lowrank(const slr_layer& L, const FwdCall& c, cudaStream_t s) {
     return launch_tc_dense(c.a.x, c.a.ldx, L.B, c.ws, c.a.M, L.in_features, L.rank, c.p.ldh, L.dtype, s);
   if (c.p.path == 1) {
     const void* B = L.B;
-    const int64_t r = L.rank;
-    return launch_h_small(c.a.x, c.a.ldx, &B, &r, c.ws, c.a.M, L.in_features, c.p.ldh, c.p.hs,
-                          L.dtype, early_start(L) && small_batch_path(L, c), s);
+    const void* x = c.a.x;
+    const int64_t r = L.rank, ldx = c.a.ldx, K = L.in_features;
+    return launch_h_small(&x, &ldx, &B, &r, c.ws, c.a.M, &K, c.p.ldh, c.p.hs, L.dtype,
+                          early_start(L) && small_batch_path(L, c), s);
   }
   return launch_simt_h(c.a.x, c.a.ldx, L.B, c.ws, c.a.M, L.in_features, L.rank, c.p.ldh, L.dtype,
                        L.dtype == SLR_F32, s);
 }
 
+// True when run_lowrank launches h_small for this call: every kernel after it
+// in the call then starts with x complete (h_small lets dependents start only
+// after its own wait on the kernel before it).
+bool lowrank_is_h_small(const slr_layer& L, const FwdCall& c) {
+  return L.rank > 0 && c.a.M > 0 && c.p.path == 1 &&
+         !(c.a.M >= kTcMinTokens && tc_dense_supported(c.a.x, c.a.ldx, L.B, L.in_features, L.rank, L.dtype));
+}
+
 // pdl: the tensor-core combine may overlap the x*B^T kernel issued just
 // before it by this library (it reads H only after griddepcontrol.wait).
-int run_combine(const slr_layer& L, const FwdCall& c, bool pdl, cudaStream_t s) {
+// x_early: an h_small of this call precedes the combine (lowrank_is_h_small).
+int run_combine(const slr_layer& L, const FwdCall& c, bool pdl, cudaStream_t s, bool x_early = false) {
   if (c.a.M == 0) return SLR_OK;
   if (use_pair(L, c)) return launch_tc2_rowblock(c.a, pdl && L.rank > 0 && early_start(L), s);
   if (c.p.path == 1 && tc_worthwhile(c.a) && tc_rowblock_supported(c.a))
     return launch_tc_rowblock(c.a, pdl && L.rank > 0 && early_start(L), s);
-  if (c.p.path == 1) return launch_mma_rowblock(c.a, early_start(L), s);
+  if (c.p.path == 1) return launch_mma_rowblock(c.a, early_start(L), s, x_early);
   return launch_simt_rowblock(c.a, L.dtype == SLR_F32, s);
 }
 
@@ -418,7 +428,7 @@ int slr_lrs_linear_forward(const slr_layer* layer, const void* x, int64_t ldx, v
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   rc = run_lowrank(*layer, c, s);
   if (rc) return rc;
-  return run_combine(*layer, c, true, s);
+  return run_combine(*layer, c, true, s, lowrank_is_h_small(*layer, c));
 }
 
 int slr_lrs_linear_lowrank(const slr_layer* layer, const void* x, int64_t ldx, int64_t M, void* workspace,
@@ -475,7 +485,11 @@ int plan_group(const slr_layer* layers, int n, int64_t M, GroupPlan& g) {
     g.ldh_all += ldh[i];
   }
   g.h_bytes = align256(size_t(M) * size_t(g.ldh_all) * dtype_size(layers[0].dtype));
-  if (M < kTcMinTokens && layers[0].dtype != SLR_F32) g.hs = plan_h_small(M, layers[0].in_features, ldh, n);
+  if (M < kTcMinTokens && layers[0].dtype != SLR_F32) {
+    int64_t Ks[kMaxGroup];
+    for (int i = 0; i < n; ++i) Ks[i] = layers[i].in_features;
+    g.hs = plan_h_small(M, Ks, ldh, n);
+  }
   size_t off = 0;
   for (int i = 0; i < n; ++i) {
     g.off[i] = off;
@@ -579,21 +593,30 @@ int group_lowrank(const slr_layer* layers, int n, const GroupCall& gc, cudaStrea
   if (gc.mode == GROUP_TC)
     return launch_tc_dense_group(a0.x, a0.ldx, Bs, rs, n, gc.ws, a0.M, layers[0].in_features, gc.g.ldh_all,
                                  layers[0].dtype, s);
-  return launch_h_small(a0.x, a0.ldx, Bs, rs, gc.ws, a0.M, layers[0].in_features, gc.g.ldh_all, gc.g.hs,
-                        layers[0].dtype, group_early_start(layers, n), s);
+  const void* xs[kMaxGroup];
+  int64_t ldxs[kMaxGroup], Ks[kMaxGroup];
+  for (int i = 0; i < n; ++i) {
+    xs[i] = a0.x;
+    ldxs[i] = a0.ldx;
+    Ks[i] = layers[0].in_features;
+  }
+  return launch_h_small(xs, ldxs, Bs, rs, gc.ws, a0.M, Ks, gc.g.ldh_all, gc.g.hs, layers[0].dtype,
+                        group_early_start(layers, n), s);
 }
 
 // Combine phase of every layer: one small-batch launch over all of them when
-// their kernel shapes agree, else one launch per layer.
-int group_combine_all(const slr_layer* layers, int n, const GroupCall& gc, cudaStream_t s) {
+// their kernel shapes agree, else one launch per layer.  x_early: this call's
+// h_small was launched just before (GROUP_SMALL after group_lowrank).
+int group_combine_all(const slr_layer* layers, int n, const GroupCall& gc, cudaStream_t s, bool x_early) {
   if (gc.mode == GROUP_SMALL) {
     RowblockArgs as[kMaxGroup];
     for (int i = 0; i < n; ++i) as[i] = gc.c[i].a;
-    if (mma_group_compatible(as, n))
-      return launch_mma_rowblock_group(as, gc.g.col, n, gc.ws, gc.g.ldh_all, group_early_start(layers, n), s);
+    if (mma_group_compatible(as, n, true))
+      return launch_mma_rowblock_group(as, gc.g.col, n, gc.ws, gc.g.ldh_all, group_early_start(layers, n), s,
+                                       x_early);
   }
   for (int i = 0; i < n; ++i) {
-    int rc = run_combine(layers[i], gc.c[i], true, s);
+    int rc = run_combine(layers[i], gc.c[i], true, s, x_early);
     if (rc) return rc;
   }
   return SLR_OK;
@@ -615,14 +638,14 @@ int slr_lrs_linear_forward_group(const slr_layer* layers, int n, const void* x, 
     for (int i = 0; i < n; ++i) {
       rc = run_lowrank(layers[i], gc.c[i], s);
       if (rc) return rc;
-      rc = run_combine(layers[i], gc.c[i], true, s);
+      rc = run_combine(layers[i], gc.c[i], true, s, lowrank_is_h_small(layers[i], gc.c[i]));
       if (rc) return rc;
     }
     return SLR_OK;
   }
   rc = group_lowrank(layers, n, gc, s);
   if (rc) return rc;
-  return group_combine_all(layers, n, gc, s);
+  return group_combine_all(layers, n, gc, s, gc.mode == GROUP_SMALL);
 }
 
 int slr_lrs_linear_group_lowrank(const slr_layer* layers, int n, const void* x, int64_t ldx, int64_t M,
@@ -647,6 +670,132 @@ int slr_lrs_linear_group_combine(const slr_layer* layers, int n, int i, const vo
   c.a.H = gc.c[i].a.H;
   c.a.ldh = gc.c[i].a.ldh;
   return run_combine(layers[i], c, false, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"
+
+namespace {
+
+constexpr int kMaxMulti = kMaxLaunchLayers;  // layers per multi-input call
+
+// Workspace of slr_lrs_linear_forward_multi: below 128 tokens with every
+// layer on the 16-bit small-batch path with a rank, one H [M, sum of
+// round_up(r_i, 64)] (layer i's columns from col[i]) filled by one h_small
+// launch; otherwise each layer's own forward workspace, one after another.
+struct MultiPlan {
+  bool small = false;
+  int64_t ldh_all = 0;
+  int64_t col[kMaxMulti] = {};
+  size_t h_bytes = 0;
+  HSmallPlan hs;
+  size_t off[kMaxMulti] = {}, bytes[kMaxMulti] = {};
+  size_t total = 0;
+};
+
+int plan_multi(const slr_layer* layers, int n, const void* const* x, const int64_t* ldx, int64_t M,
+               MultiPlan& m) {
+  if (!layers || n <= 0 || n > kMaxMulti)
+    return fail(SLR_ERR_INVALID_ARGUMENT, "a multi-input call holds 1 to " + std::to_string(kMaxMulti) + " layers");
+  for (int i = 0; i < n; ++i) {
+    int rc = check_layer(&layers[i]);
+    if (rc) return rc;
+    if (layers[i].dtype != layers[0].dtype)
+      return fail(SLR_ERR_INVALID_ARGUMENT, "the layers of a multi-input call must share one dtype");
+  }
+  if (M < 0) return fail(SLR_ERR_INVALID_ARGUMENT, "M must be >= 0");
+  size_t off = 0;
+  m.small = M > 0 && M < kTcMinTokens && layers[0].dtype != SLR_F32;
+  int64_t ldh[kMaxMulti], Ks[kMaxMulti];
+  for (int i = 0; i < n; ++i) {
+    const slr_layer& L = layers[i];
+    const void* xi = x ? x[i] : nullptr;
+    const int64_t lx = (ldx && ldx[i]) ? ldx[i] : L.in_features;
+    m.off[i] = off;
+    m.bytes[i] = plan_forward(L, M, nullptr).total;
+    off += align256(m.bytes[i]);
+    if (x && plan_forward(L, M, (lx % 8 == 0) ? xi : reinterpret_cast<const void*>(uintptr_t(1))).path != 1)
+      m.small = false;
+    if (L.rank <= 0) m.small = false;
+    ldh[i] = round_up(std::max<int64_t>(L.rank, 0), 64);
+    Ks[i] = L.in_features;
+    m.col[i] = m.ldh_all;
+    m.ldh_all += ldh[i];
+  }
+  m.h_bytes = align256(size_t(std::max<int64_t>(M, 0)) * size_t(m.ldh_all) * dtype_size(layers[0].dtype));
+  if (m.small) m.hs = plan_h_small(M, Ks, ldh, n);
+  // sized for either layout, so the size query needs no inputs
+  m.total = std::max(m.h_bytes, off);
+  return SLR_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t slr_lrs_linear_multi_workspace_size(const slr_layer* layers, int n, int64_t M) {
+  MultiPlan m;
+  if (plan_multi(layers, n, nullptr, nullptr, M, m) != SLR_OK) return 0;
+  return m.total;
+}
+
+int slr_lrs_linear_forward_multi(const slr_layer* layers, int n, const void* const* x, const int64_t* ldx,
+                                 void* const* y, const int64_t* ldy, int64_t M, void* workspace,
+                                 size_t workspace_bytes, void* stream) {
+  if (!x || !y) return fail(SLR_ERR_INVALID_ARGUMENT, "x/y is NULL");
+  MultiPlan m;
+  int rc = plan_multi(layers, n, x, ldx, M, m);
+  if (rc || M == 0) return rc;
+  if (m.total > 0) {
+    if (!workspace) return fail(SLR_ERR_WORKSPACE, "workspace is NULL");
+    if (workspace_bytes < m.total)
+      return fail(SLR_ERR_WORKSPACE, "workspace too small: need " + std::to_string(m.total) + " bytes");
+    if (reinterpret_cast<uintptr_t>(workspace) & 255u) return fail(SLR_ERR_WORKSPACE, "workspace must be 256-byte aligned");
+  }
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  FwdCall c[kMaxMulti];
+  for (int i = 0; i < n; ++i) {
+    rc = prepare_forward(&layers[i], x[i], ldx ? ldx[i] : 0, y[i], ldy ? ldy[i] : 0, M, ws + m.off[i], m.bytes[i],
+                         true, c[i], !m.small);
+    if (rc) return rc;
+  }
+  if (!m.small) {
+    for (int i = 0; i < n; ++i) {
+      rc = run_lowrank(layers[i], c[i], s);
+      if (rc) return rc;
+      rc = run_combine(layers[i], c[i], true, s, lowrank_is_h_small(layers[i], c[i]));
+      if (rc) return rc;
+    }
+    return SLR_OK;
+  }
+  // One h_small launch for every layer's x*B^T (each layer keeps the K split it
+  // would get alone, so H is the one of slr_lrs_linear_forward bit for bit),
+  // then the combines: one launch when the kernel shapes agree.
+  const void* xs[kMaxMulti];
+  const void* Bs[kMaxMulti];
+  int64_t ldxs[kMaxMulti], rs[kMaxMulti], Ks[kMaxMulti];
+  bool pdl = true;
+  for (int i = 0; i < n; ++i) {
+    xs[i] = c[i].a.x;
+    ldxs[i] = c[i].a.ldx;
+    Bs[i] = layers[i].B;
+    rs[i] = layers[i].rank;
+    Ks[i] = layers[i].in_features;
+    c[i].a.H = ws + size_t(m.col[i]) * dtype_size(layers[i].dtype);
+    c[i].a.ldh = m.ldh_all;
+    pdl = pdl && early_start(layers[i]);
+  }
+  rc = launch_h_small(xs, ldxs, Bs, rs, ws, M, Ks, m.ldh_all, m.hs, layers[0].dtype, pdl, s);
+  if (rc) return rc;
+  RowblockArgs as[kMaxMulti];
+  for (int i = 0; i < n; ++i) as[i] = c[i].a;
+  if (mma_group_compatible(as, n, false))
+    return launch_mma_rowblock_group(as, m.col, n, ws, m.ldh_all, pdl, s, true);
+  for (int i = 0; i < n; ++i) {
+    rc = run_combine(layers[i], c[i], true, s, true);
+    if (rc) return rc;
+  }
+  return SLR_OK;
 }
 
 }  // extern "C"

@@ -5,7 +5,8 @@
   operator (reference: ssalaad/tilelang_sparse/addmm_inplace.py:88-141).
 * :class:`LayerDesc` / :func:`lrs_linear_forward` — the fused S+LR forward
   ``y = x @ S.T + (x @ B.T) @ A.T + bias`` (reference:
-  ssalaad/efficient/ls_linear.py:124-137).
+  ssalaad/efficient/ls_linear.py:124-137); :class:`LayerGroup` for layers
+  that read one input, :class:`LayerSet` for independent layers side by side.
 * :func:`dense_to_bsr_cuda` — bit-exact GPU ``dense_to_bsr``
   (reference: ssalaad/efficient/artifact.py:20-37).
 * :func:`plan_row_order`, :func:`plan_shards` — host planning helpers.
@@ -340,6 +341,59 @@ class LayerGroup:
                 _stream(self.device))
         _lib.check(rc, "lrs_linear_group_combine")
         return out
+
+
+class LayerSet:
+    """Independent layers run side by side, each on its own input (one
+    ``slr_lrs_linear_forward_multi`` call): ``forward(xs)`` returns what
+    :meth:`LayerDesc.forward` gives for each layer, bit for bit.  Below 128
+    tokens every layer's ``x · Bᵀ`` is one launch and the combine phases one
+    more (two launches for the whole set instead of two per layer)."""
+
+    def __init__(self, descs: list[LayerDesc]):
+        if not 1 <= len(descs) <= 8:
+            raise ValueError("a layer set holds 1 to 8 layers")
+        if len({d.dtype for d in descs}) != 1:
+            raise ValueError("the layers of a set must share one dtype")
+        self.descs = list(descs)
+        self.device = descs[0].device
+        self.dtype = descs[0].dtype
+        self._ws: torch.Tensor | None = None
+
+    def _structs(self):
+        arr = (_lib.SlrLayer * len(self.descs))()
+        for i, d in enumerate(self.descs):
+            ctypes.memmove(ctypes.byref(arr[i]), ctypes.byref(d.struct), ctypes.sizeof(_lib.SlrLayer))
+        return arr
+
+    def workspace(self, M: int) -> torch.Tensor | None:
+        need = int(_lib.load().slr_lrs_linear_multi_workspace_size(self._structs(), len(self.descs), M))
+        if need == 0:
+            return None
+        if self._ws is None or self._ws.numel() < need:
+            self._ws = torch.empty(need, dtype=torch.uint8, device=self.device)
+        return self._ws
+
+    def forward(self, xs: list[torch.Tensor], outs: list[torch.Tensor] | None = None) -> list[torch.Tensor]:
+        n = len(self.descs)
+        if len(xs) != n:
+            raise ValueError(f"{n} layers need {n} inputs")
+        M = xs[0].shape[0]
+        if any(x.shape[0] != M for x in xs):
+            raise ValueError("every input of a layer set has the same number of rows")
+        if outs is None:
+            outs = [torch.empty(M, d.out_features, dtype=self.dtype, device=self.device) for d in self.descs]
+        ws = self.workspace(M)
+        xp = (ctypes.c_void_p * n)(*[x.data_ptr() for x in xs])
+        lx = (ctypes.c_int64 * n)(*[LayerDesc._ld(x) for x in xs])
+        yp = (ctypes.c_void_p * n)(*[o.data_ptr() for o in outs])
+        ly = (ctypes.c_int64 * n)(*[LayerDesc._ld(o) for o in outs])
+        with _DeviceGuard(self.device):
+            rc = _lib.load().slr_lrs_linear_forward_multi(
+                self._structs(), n, xp, lx, yp, ly, M, None if ws is None else ws.data_ptr(),
+                0 if ws is None else ws.numel(), _stream(self.device))
+        _lib.check(rc, "lrs_linear_forward_multi")
+        return outs
 
 
 def lrs_linear_forward(desc: LayerDesc, x: torch.Tensor) -> torch.Tensor:

@@ -693,3 +693,86 @@ def test_pair_mma_kernel_matches_oracle(cuda, oracle, shape, T):
     d.struct.flags = 1
     y = ops.lrs_linear_forward(d, x.to(cuda))
     assert_16bit_close(y, ref)
+
+
+# --------------------------------------------- independent layers (multi) --
+
+MULTI = {
+    # one kernel shape (32-wide blocks, rank chunk 64): one x*B^T and one combine launch below 128 tokens;
+    # inputs 0 and 1 read one x, the others their own (different widths)
+    "one_shape": [(512, 512, 32, 32, 64, 0.3, 0), (256, 512, 32, 32, 128, 0.3, 0), (384, 768, 32, 32, 64, 0.25, 1),
+                  (768, 384, 32, 32, 256, 0.3, 2), (512, 1536, 32, 32, 64, 0.2, 3)],
+    # different x sub-tile widths and a low-rank-only layer: one x*B^T launch, a combine per layer
+    "mixed": [(512, 512, 16, 16, 64, 0.3, 0), (256, 768, 32, 32, 64, 0.3, 1), (512, 512, 16, 16, 64, 0.0, 2)],
+    # a layer without rank: every layer runs its own forward
+    "no_rank": [(512, 512, 32, 32, 64, 0.3, 0), (256, 512, 32, 32, 0, 0.3, 1)],
+}
+
+
+def _multi_layers(cuda, name, seed0=400):
+    specs, descs = [], []
+    for i, (n, k, bp, bq, r, dens, _) in enumerate(MULTI[name]):
+        spec = random_layer(n, k, bp, bq, r, dens, seed=seed0 + 13 * i)
+        specs.append(spec)
+        descs.append(desc_for(spec.tensors("cpu", torch.bfloat16), spec, cuda, torch.bfloat16))
+    return specs, descs
+
+
+@pytest.mark.parametrize("name", list(MULTI))
+@pytest.mark.parametrize("T", [1, 8, 16, 33, 64, 127, 128, 300])
+def test_multi_forward_equals_per_layer(cuda, oracle, name, T):
+    specs, descs = _multi_layers(cuda, name)
+    inputs = {}
+    xs = []
+    for (n, k, *_rest, inp), spec in zip(MULTI[name], specs):
+        if inp not in inputs:
+            inputs[inp] = workloads.tokens(T, k, seed=T + 31 * inp, dtype=torch.bfloat16).to(cuda)
+        xs.append(inputs[inp])
+    ys = ops.LayerSet(descs).forward(xs)
+    for d, x, y in zip(descs, xs, ys):
+        assert torch.equal(y, d.forward(x))
+    if T in (1, 33):  # and the oracle, once per regime
+        for spec, d, x, y in zip(specs, descs, xs, ys):
+            t = spec.tensors("cpu", torch.bfloat16)
+            assert_16bit_close(y, oracle_layer(oracle, t, x.cpu()))
+
+
+@pytest.mark.parametrize("T", [1, 16, 64])
+def test_multi_chained_early_start_equals_strict_order(cuda, T):
+    """Back-to-back multi calls whose inputs are the previous call's outputs:
+    the combine reads x before its wait on h_small (x is complete by then);
+    results equal fully serialised launches bit for bit, eagerly and from a
+    CUDA graph."""
+    def build(flags):
+        specs = [random_layer(512, 512, 32, 32, 64, 0.3, seed=700 + i, value_std=0.05) for i in range(4)]
+        ds = [desc_for(s.tensors("cpu", torch.bfloat16), s, cuda, torch.bfloat16) for s in specs]
+        for d in ds:
+            d.flags = flags
+            d.refresh()
+        lset = ops.LayerSet(ds)
+
+        def run(xs):
+            for _ in range(4):
+                ys = lset.forward(xs)
+                xs = [ys[(i + 1) % len(ys)] for i in range(len(ys))]
+            return xs
+        return run
+
+    xs = [workloads.tokens(T, 512, seed=T + i, dtype=torch.bfloat16).to(cuda) for i in range(4)]
+    early = build(0)
+    ref = build(_lib.SLR_FLAG_STRICT_ORDER)(xs)
+    out = early(xs)
+    for a, b in zip(out, ref):
+        assert torch.equal(a, b)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        early(xs)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            gout = early(xs)
+    torch.cuda.current_stream().wait_stream(s)
+    g.replay()
+    torch.cuda.synchronize()
+    for a, b in zip(gout, ref):
+        assert torch.equal(a, b)
