@@ -58,10 +58,8 @@ struct MmaLayer {
 struct MmaArgs {
   int64_t M;
   int n;
-  int n_items;           // work items of all layers (16-feature row slices)
-  int stages;            // ring slots of this launch
-  uint32_t stage_bytes;  // bytes of one ring slot (the largest any layer needs)
-  int x_early;           // x is complete at launch: read it before griddepcontrol.wait
+  int stages;   // ring slots of this launch (fewer slots -> more CTAs per SM)
+  int x_early;  // x is complete at launch: read it before griddepcontrol.wait
   MmaLayer L[kMaxLayers];
 };
 // Tensor maps: H is shared by the layers of a launch (H column offsets per
@@ -75,83 +73,75 @@ __device__ __forceinline__ void ldsm_x2(uint32_t addr, uint32_t& r0, uint32_t& r
   asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(addr));
 }
 
-// Work item = 16 output features (a column slice of one block-row of one
-// layer) x 8*NT tokens (token tile blockIdx.y).  The kernel is persistent: CTA
-// b takes items b, b + gridDim.x, ... (numbered layer by layer, each layer's
-// rows in its row order, heaviest first) and one ring of stages runs through
-// all of them, so the next item's weights stream in while the current one
-// finishes and no CTA is launched per item.  Warp 8 is the producer: per
-// sparse stage it TMA-loads the 16-column slice of `sb` consecutive value
-// blocks of the row (one box) and, for each of those blocks, the x tile
-// [tokens x bq] at that block's column (lane j reads col[] of block j and
-// issues its x tiles); per low-rank stage the 16 rows of A and the H tile
-// [tokens x kc] of up to `lrc` rank chunks.  Warps 0-7 split each stage's k16
-// steps, take ldmatrix fragments from shared memory only, and run m16n8k16
-// MMAs (features on M, tokens on N); at the end of an item their partial sums
-// are reduced in a fixed order and y is written once.
+// One CTA = 16 output features (a column slice of one block-row) x 8*NT
+// tokens.  Warp 8 is the producer: per sparse stage it TMA-loads the 16-column
+// slice of `sb` consecutive value blocks of the row (one box) and, for each of
+// those blocks, the x tile [tokens x bq] at that block's column (lane j reads
+// col[] of block j and issues its x tiles); per low-rank stage the 16 rows of
+// A and the H tile [tokens x kc].  Warps 0-7 split each stage's k16 steps, take
+// ldmatrix fragments from shared memory only, and run m16n8k16 MMAs (features
+// on M, tokens on N); partial sums are reduced across warps in a fixed order.
 //
 // Launched as a programmatic dependent (PDL): before griddepcontrol.wait the
 // CTA touches weights only -- the value and A boxes of the first ring-full of
-// stages go to shared memory, those of every later stage of its items to L2 --
-// so a decode step streams its weights while the previous kernel finishes.  H
-// and y are read or written only after the wait; x too, unless x_early says
-// that x was complete when the kernel was launched (the preceding kernel is
-// this call's h_small, which lets dependents start only after its own wait on
-// the kernel before it): the sparse stages then run while h_small computes H,
-// and the wait comes before the first H load.
+// stages go to shared memory, those of later stages to L2, bias to shared
+// memory -- so a decode step streams its weights while the previous kernel
+// finishes.  H and y are read or written only after the wait; x too, unless
+// x_early says that x was complete when the kernel was launched (the
+// preceding kernel is this call's h_small, which lets dependents start only
+// after its own wait on the kernel before it): the sparse stages then run
+// while h_small computes H, and the wait comes before the first H load.
 //
-// A wait that times out sets the device status and s_abort; from then on no
-// warp waits or stores, every warp still takes the same barriers, and the
-// producer waits (bounded) for its copies in flight before the CTA exits.
+// Several layers run in one launch (q/k/v or gate/up sharing one x, or
+// independent projections each with its own x): the grid is the
+// concatenation of their CTA ranges.
 template <int NT, int KX, typename TI, int MODE>
-__global__ void __launch_bounds__(kThreads, NT <= 2 ? 4 : 2)
+__global__ void __launch_bounds__(kThreads)
     mma_rowblock_kernel(const __grid_constant__ MmaMaps maps, const __grid_constant__ MmaArgs ga) {
-  constexpr int TT = 8 * NT;                 // tokens per item
+  int li = 0;
+  while (li + 1 < ga.n && int(blockIdx.x) >= ga.L[li + 1].cta0) ++li;
+  const MmaLayer& a = ga.L[li];
+  const CUtensorMap& tm_vals = maps.v[li];
+  const CUtensorMap& tm_A = maps.a[li];
+  const CUtensorMap& tm_x = maps.x[li];
+  const CUtensorMap& tm_h = maps.h;
+  const int cta = int(blockIdx.x) - a.cta0;
+  constexpr int TT = 8 * NT;                 // tokens per CTA
   constexpr int XB = TT * KX * 2;            // one x sub-tile (tokens x KX columns)
   constexpr int RWX = KX * 2;                // x tile row bytes (its TMA swizzle width)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int nsub = a.bq / KX;                            // x sub-tiles per block
+  const uint32_t v_bytes = uint32_t(a.sb * a.bq * kFT * 2);   // values box of a stage
+  const uint32_t v_slot = (v_bytes + 1023) & ~1023u;
+  const uint32_t x_region = uint32_t(a.sb * nsub * XB);
+  const uint32_t chunk_bytes = uint32_t(kFT * a.kc * 2 + TT * a.kc * 2);  // A + H of one chunk
+  const uint32_t cs = (kHOff + TT * a.kc * 2 + 1023) & ~1023u;            // chunk stride in a slot
+  uint32_t stage_bytes = v_slot + x_region;
+  if (stage_bytes < kHOff + TT * a.kc * 2) stage_bytes = kHOff + TT * a.kc * 2;
+  stage_bytes = (stage_bytes + 1023) & ~1023u;
   const int S = ga.stages;
-  const uint32_t stage_bytes = ga.stage_bytes;
   float* red = reinterpret_cast<float*>(smem + S * stage_bytes);  // [8][16][TT]
   uint64_t* full = reinterpret_cast<uint64_t*>(red + kConsumerWarps * kFT * TT);
   uint64_t* empty = full + S;
-  __shared__ volatile int s_abort;
-  __shared__ int s_issued;  // stages the producer issued
+  __shared__ int s_abort;
+  __shared__ float s_bias[kFT];
 
   pdl_launch_dependents();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ri = cta / a.ft_per_row;
+  const int f0 = (cta - ri * a.ft_per_row) * kFT;  // feature offset inside the block
+  const int br = a.rows ? a.rows[ri] : ri;
   const int64_t t0 = int64_t(blockIdx.y) * TT;
-
-  // Everything an item needs, from its number.
-  struct Item {
-    int li, f0, br, jb0, nblk, n_sp, n_chunks, n_lr, n_total;
-    int64_t n0;
-  };
-  auto item_at = [&](int q) {
-    Item it;
-    int li = 0;
-    while (li + 1 < ga.n && q >= ga.L[li + 1].cta0) ++li;
-    const MmaLayer& a = ga.L[li];
-    const int cta = q - a.cta0;
-    const int ri = cta / a.ft_per_row;
-    it.li = li;
-    it.f0 = (cta - ri * a.ft_per_row) * kFT;
-    it.br = a.rows ? __ldg(a.rows + ri) : ri;
-    it.jb0 = a.crow ? __ldg(a.crow + it.br) : 0;
-    it.nblk = a.crow ? __ldg(a.crow + it.br + 1) - it.jb0 : 0;
-    it.n_sp = (it.nblk + a.sb - 1) / a.sb;
-    it.n_chunks = MODE == MODE_FUSED ? (a.r + a.kc - 1) / a.kc : 0;
-    it.n_lr = (it.n_chunks + a.lrc - 1) / a.lrc;
-    it.n_total = it.n_sp + it.n_lr;
-    it.n0 = int64_t(it.br) * a.bp + it.f0;
-    return it;
-  };
-  // Byte layout of a stage of layer a: values box, then the x sub-tiles of its
-  // blocks; a low-rank stage holds chunks of (A rows, H tile) cs bytes apart.
-  auto v_bytes_of = [](const MmaLayer& a) { return uint32_t(a.sb * a.bq * kFT * 2); };
-  auto v_slot_of = [](const MmaLayer& a) { return (uint32_t(a.sb * a.bq * kFT * 2) + 1023) & ~1023u; };
-  auto cs_of = [](const MmaLayer& a) { return (kHOff + uint32_t(TT * a.kc * 2) + 1023) & ~1023u; };
+  const int jb0 = a.crow ? a.crow[br] : 0;
+  const int nblk = a.crow ? a.crow[br + 1] - jb0 : 0;
+  const int n_sp = (nblk + a.sb - 1) / a.sb;
+  // low-rank stages: lrc chunks of kc rank columns each (chunk c of the
+  // stage at offset c * cs: A rows [16 x kc], then the H tile at kHOff)
+  const int n_chunks = MODE == MODE_FUSED ? (a.r + a.kc - 1) / a.kc : 0;
+  const int n_lr = (n_chunks + a.lrc - 1) / a.lrc;
+  const int n_total = n_sp + n_lr;
+  const int64_t n0 = int64_t(br) * a.bp + f0;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -160,130 +150,90 @@ __global__ void __launch_bounds__(kThreads, NT <= 2 ? 4 : 2)
     }
     fence_mbar_init();
     s_abort = 0;
-    s_issued = 0;
+  }
+  if (threadIdx.x < kFT) {
+    const TI* bias = static_cast<const TI*>(a.bias);
+    s_bias[threadIdx.x] = (MODE == MODE_FUSED && bias != nullptr) ? to_f(bias[n0 + threadIdx.x]) : 0.f;
   }
   __syncthreads();
 
   if (warp == kConsumerWarps) {
     // ------------------------------------------------------------ producer
-    if (lane == 0) {  // the descriptors a layer has (x and values if sparse, A and H if it has a rank)
-      for (int li = 0; li < ga.n; ++li) {
-        if (ga.L[li].crow) {
-          tma_prefetch_desc(&maps.x[li]);
-          tma_prefetch_desc(&maps.v[li]);
-        }
-        if (MODE == MODE_FUSED && ga.L[li].r > 0) {
-          tma_prefetch_desc(&maps.a[li]);
-          if (li == 0) tma_prefetch_desc(&maps.h);
-        }
+    if (lane == 0) {
+      if (n_sp) {
+        tma_prefetch_desc(&tm_vals);
+        tma_prefetch_desc(&tm_x);
+      }
+      if (n_lr) {
+        tma_prefetch_desc(&tm_A);
+        tma_prefetch_desc(&tm_h);
       }
     }
-    // Phase A, before griddepcontrol.wait: weights only.  The first ring-full
-    // of stages (possibly spanning items) gets its weight boxes in shared
-    // memory, its expect_tx covering the activations that follow after the
-    // wait; per slot the producer keeps what phase B needs.
-    // per slot: layer | low-rank flag << 4 | first chunk << 5 | chunks << 17 | blocks << 24
-    uint32_t sl[kStages];
+    const int npre = min(n_total, S);
+    // Weights of the first npre stages (fresh slots: no empty-barrier wait).
     int colr[kStages];
-    int g = 0;  // stages issued
-    int q = int(blockIdx.x);
-    Item it = q < ga.n_items ? item_at(q) : Item{};
-    int s_in = 0;  // next stage of `it`
 #pragma unroll
-    for (int slot = 0; slot < kStages; ++slot) {
-      sl[slot] = 0;
-      colr[slot] = 0;
-      if (slot >= S) continue;
-      while (q < ga.n_items && s_in >= it.n_total) {
-        q += gridDim.x;
-        if (q < ga.n_items) it = item_at(q);
-        s_in = 0;
-      }
-      if (q >= ga.n_items) continue;
-      const MmaLayer& a = ga.L[it.li];
-      uint8_t* dst = smem + slot * stage_bytes;
-      if (s_in < it.n_sp) {
-        const int j0 = s_in * a.sb, nb = min(a.sb, it.nblk - j0);
-        sl[slot] = uint32_t(it.li) | uint32_t(nb) << 24;
-        if (lane < nb) colr[slot] = __ldg(a.col + it.jb0 + j0 + lane);
-        if (lane == 0) {
-          mbar_arrive_expect_tx(&full[slot], v_bytes_of(a) + uint32_t(nb * (a.bq / KX) * XB));
-          tma_load_2d(dst, &maps.v[it.li], it.f0, (it.jb0 + j0) * a.bq, &full[slot]);
-        }
-      } else {
-        const int c0 = (s_in - it.n_sp) * a.lrc, nch = min(a.lrc, it.n_chunks - c0);
-        sl[slot] = uint32_t(it.li) | 16u | uint32_t(c0) << 5 | uint32_t(nch) << 17;
-        if (lane == 0) {
-          mbar_arrive_expect_tx(&full[slot], uint32_t(nch) * uint32_t(kFT * a.kc * 2 + TT * a.kc * 2));
+    for (int s = 0; s < kStages; ++s) {
+      colr[s] = 0;
+      if (s < npre) {
+        uint8_t* dst = smem + s * stage_bytes;
+        if (s < n_sp) {
+          const int j0 = s * a.sb;
+          const int nb = min(a.sb, nblk - j0);
+          if (lane < nb) colr[s] = __ldg(a.col + jb0 + j0 + lane);
+          if (lane == 0) {
+            mbar_arrive_expect_tx(&full[s], v_bytes + uint32_t(nb * nsub * XB));
+            tma_load_2d(dst, &tm_vals, f0, (jb0 + j0) * a.bq, &full[s]);
+          }
+        } else if (lane == 0) {
+          const int c0 = (s - n_sp) * a.lrc, nch = min(a.lrc, n_chunks - c0);
+          mbar_arrive_expect_tx(&full[s], uint32_t(nch) * chunk_bytes);
           for (int c = 0; c < nch; ++c)
-            tma_load_2d(dst + c * cs_of(a), &maps.a[it.li], (c0 + c) * a.kc, it.br * a.bp + it.f0, &full[slot]);
+            tma_load_2d(dst + c * cs, &tm_A, (c0 + c) * a.kc, br * a.bp + f0, &full[s]);
         }
       }
-      ++s_in;
-      ++g;
     }
-    // Weights of every later stage of this CTA's items into L2.
-    {
-      int q2 = q, s2 = s_in, k = 0;
-      Item i2 = it;
-      while (q2 < ga.n_items) {
-        if (s2 >= i2.n_total) {
-          q2 += gridDim.x;
-          if (q2 < ga.n_items) i2 = item_at(q2);
-          s2 = 0;
-          continue;
-        }
-        if ((k++ & 31) == lane) {
-          const MmaLayer& a = ga.L[i2.li];
-          if (s2 < i2.n_sp) {
-            tma_prefetch_l2_2d(&maps.v[i2.li], i2.f0, (i2.jb0 + s2 * a.sb) * a.bq);
-          } else {
-            const int c0 = (s2 - i2.n_sp) * a.lrc;
-            for (int c = c0; c < min(i2.n_chunks, c0 + a.lrc); ++c)
-              tma_prefetch_l2_2d(&maps.a[i2.li], c * a.kc, i2.br * a.bp + i2.f0);
+    // Weights of the later stages into L2.
+    for (int s = npre + lane; s < n_total; s += 32) {
+      if (s < n_sp)
+        tma_prefetch_l2_2d(&tm_vals, f0, (jb0 + s * a.sb) * a.bq);
+      else
+        for (int c = (s - n_sp) * a.lrc; c < min(n_chunks, (s - n_sp + 1) * a.lrc); ++c)
+          tma_prefetch_l2_2d(&tm_A, c * a.kc, br * a.bp + f0);
+    }
+    // x and H come from preceding kernels (x may already be complete, see x_early)
+    bool waited = !ga.x_early;
+    if (waited) pdl_wait_primary();
+    __syncwarp();
+    // Activations of the pre-filled stages.
+#pragma unroll
+    for (int s = 0; s < kStages; ++s) {
+      if (s < npre) {
+        uint8_t* dst = smem + s * stage_bytes;
+        if (s < n_sp) {
+          const int nb = min(a.sb, nblk - s * a.sb);
+          if (lane < nb)
+            for (int h = 0; h < nsub; ++h)
+              tma_load_2d(dst + v_slot + (lane * nsub + h) * XB, &tm_x, colr[s] * a.bq + h * KX, int(t0),
+                          &full[s]);
+        } else {
+          if (!waited) {
+            pdl_wait_primary();  // H is written by the preceding kernel
+            waited = true;
+          }
+          if (lane == 0) {
+            const int c0 = (s - n_sp) * a.lrc, nch = min(a.lrc, n_chunks - c0);
+            for (int c = 0; c < nch; ++c)
+              tma_load_2d(dst + c * cs + kHOff, &tm_h, a.h_col0 + (c0 + c) * a.kc, int(t0), &full[s]);
           }
         }
-        ++s2;
       }
     }
-    // Phase B: the activations of the pre-filled stages.
-    bool waited = !ga.x_early;
-    if (waited) pdl_wait_primary();  // x comes from the preceding kernels
-    __syncwarp();
-#pragma unroll
-    for (int slot = 0; slot < kStages; ++slot) {
-      if (slot >= g) continue;
-      const int li = int(sl[slot] & 15u);
-      const MmaLayer& a = ga.L[li];
-      uint8_t* dst = smem + slot * stage_bytes;
-      if (!(sl[slot] & 16u)) {
-        if (lane < int(sl[slot] >> 24))
-          for (int h = 0; h < a.bq / KX; ++h)
-            tma_load_2d(dst + v_slot_of(a) + (lane * (a.bq / KX) + h) * XB, &maps.x[li], colr[slot] * a.bq + h * KX,
-                        int(t0), &full[slot]);
-      } else {
-        if (!waited) {
-          pdl_wait_primary();  // H is written by the preceding kernel
-          waited = true;
-        }
-        if (lane == 0) {
-          const int c0 = int((sl[slot] >> 5) & 0xfffu), nch = int((sl[slot] >> 17) & 0x7fu);
-          for (int c = 0; c < nch; ++c)
-            tma_load_2d(dst + c * cs_of(a) + kHOff, &maps.h, a.h_col0 + (c0 + c) * a.kc, int(t0), &full[slot]);
-        }
-      }
-    }
-    // Phase C: every remaining stage through the ring.
-    while (true) {
-      while (q < ga.n_items && s_in >= it.n_total) {
-        q += gridDim.x;
-        if (q < ga.n_items) it = item_at(q);
-        s_in = 0;
-      }
-      if (q >= ga.n_items || s_abort) break;
-      const int slot = g % S;
+    // Remaining stages through the ring.
+    for (int s = npre; s < n_total; ++s) {
+      const int slot = s % S;
       int ok = 1;
-      if (lane == 0) ok = mbar_wait(&empty[slot], ((g / S) & 1) ^ 1) ? 1 : 0;
+      if (lane == 0) ok = mbar_wait(&empty[slot], ((s / S) & 1) ^ 1) ? 1 : 0;
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) {
         if (lane == 0) {
@@ -292,144 +242,121 @@ __global__ void __launch_bounds__(kThreads, NT <= 2 ? 4 : 2)
         }
         break;
       }
-      const MmaLayer& a = ga.L[it.li];
       uint8_t* dst = smem + slot * stage_bytes;
-      if (s_in < it.n_sp) {
-        const int j0 = s_in * a.sb, nb = min(a.sb, it.nblk - j0);
-        const int c = lane < nb ? __ldg(a.col + it.jb0 + j0 + lane) : 0;
+      if (s < n_sp) {
+        const int j0 = s * a.sb;
+        const int nb = min(a.sb, nblk - j0);
+        const int c = lane < nb ? __ldg(a.col + jb0 + j0 + lane) : 0;
         if (lane == 0) {
-          mbar_arrive_expect_tx(&full[slot], v_bytes_of(a) + uint32_t(nb * (a.bq / KX) * XB));
-          tma_load_2d(dst, &maps.v[it.li], it.f0, (it.jb0 + j0) * a.bq, &full[slot]);
+          mbar_arrive_expect_tx(&full[slot], v_bytes + uint32_t(nb * nsub * XB));
+          tma_load_2d(dst, &tm_vals, f0, (jb0 + j0) * a.bq, &full[slot]);
         }
         __syncwarp();
         if (lane < nb)
-          for (int h = 0; h < a.bq / KX; ++h)
-            tma_load_2d(dst + v_slot_of(a) + (lane * (a.bq / KX) + h) * XB, &maps.x[it.li], c * a.bq + h * KX,
-                        int(t0), &full[slot]);
+          for (int h = 0; h < nsub; ++h)
+            tma_load_2d(dst + v_slot + (lane * nsub + h) * XB, &tm_x, c * a.bq + h * KX, int(t0), &full[slot]);
       } else {
         if (!waited) {
           pdl_wait_primary();  // H is written by the preceding kernel
           waited = true;
         }
         if (lane == 0) {
-          const int c0 = (s_in - it.n_sp) * a.lrc, nch = min(a.lrc, it.n_chunks - c0);
-          mbar_arrive_expect_tx(&full[slot], uint32_t(nch) * uint32_t(kFT * a.kc * 2 + TT * a.kc * 2));
+          const int c0 = (s - n_sp) * a.lrc, nch = min(a.lrc, n_chunks - c0);
+          mbar_arrive_expect_tx(&full[slot], uint32_t(nch) * chunk_bytes);
           for (int c = 0; c < nch; ++c) {
-            tma_load_2d(dst + c * cs_of(a), &maps.a[it.li], (c0 + c) * a.kc, it.br * a.bp + it.f0, &full[slot]);
-            tma_load_2d(dst + c * cs_of(a) + kHOff, &maps.h, a.h_col0 + (c0 + c) * a.kc, int(t0), &full[slot]);
+            tma_load_2d(dst + c * cs, &tm_A, (c0 + c) * a.kc, br * a.bp + f0, &full[slot]);
+            tma_load_2d(dst + c * cs + kHOff, &tm_h, a.h_col0 + (c0 + c) * a.kc, int(t0), &full[slot]);
           }
         }
       }
-      ++s_in;
-      ++g;
     }
-    if (lane == 0) s_issued = g;
   } else {
-  // ------------------------------------------------------------- consumers
-  const int lj = lane >> 3, lk = lane & 7;
-  const int g8 = lane >> 2, tig = lane & 3;
-  bool waited_y = false;
-  int gs = 0;  // stages consumed
-  for (int q = int(blockIdx.x); q < ga.n_items; q += gridDim.x) {
-    const Item it = item_at(q);
-    const MmaLayer& a = ga.L[it.li];
-    const int nsub = a.bq / KX;
-    const uint32_t v_slot = v_slot_of(a), cs = cs_of(a);
+    // ----------------------------------------------------------- consumers
+    const int lj = lane >> 3, li = lane & 7;
     float acc[NT][4];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
       for (int e = 0; e < 4; ++e) acc[nt][e] = 0.f;
-    for (int s = 0; s < it.n_total; ++s, ++gs) {
-      const int slot = gs % S;
-      if (!s_abort && !mbar_wait(&full[slot], (gs / S) & 1)) {
+
+    for (int s = 0; s < n_total; ++s) {
+      const int slot = s % S;
+      if (!mbar_wait(&full[slot], (s / S) & 1)) {
         atomicOr(&g_status_mma, SLR_TIMEOUT_BIT);
         s_abort = 1;
+        break;
       }
-      if (!s_abort) {
-        const uint32_t base = smem_u32(smem + slot * stage_bytes);
-        if (s < it.n_sp) {
-          const int nb = min(a.sb, it.nblk - s * a.sb);
-          const int steps = nb * (a.bq >> 4);
-          for (int kk = warp; kk < steps; kk += kConsumerWarps) {
-            const int row = 16 * kk;              // k row inside the stage's value rows
-            const int j = row / a.bq, kin = row - j * a.bq;
-            uint32_t af[4];
-            // values slice [k rows x 16 features], 32-byte rows (SWIZZLE_32B)
-            ldsm_x4_trans(base + swz_offset(row + (lj >> 1) * 8 + lk, lj & 1, 32), af[0], af[1], af[2], af[3]);
-            const uint32_t xt = base + v_slot + uint32_t((j * nsub + kin / KX) * XB);
-            const int kc16 = (kin % KX) >> 3;     // 16-byte chunk of the k16 step in the x row
+      const uint32_t base = smem_u32(smem + slot * stage_bytes);
+      if (s < n_sp) {
+        const int nb = min(a.sb, nblk - s * a.sb);
+        const int steps = nb * (a.bq >> 4);
+        for (int kk = warp; kk < steps; kk += kConsumerWarps) {
+          const int row = 16 * kk;              // k row inside the stage's value rows
+          const int j = row / a.bq, kin = row - j * a.bq;
+          uint32_t af[4];
+          // values slice [k rows x 16 features], 32-byte rows (SWIZZLE_32B)
+          ldsm_x4_trans(base + swz_offset(row + (lj >> 1) * 8 + li, lj & 1, 32), af[0], af[1], af[2], af[3]);
+          const uint32_t xt = base + v_slot + uint32_t((j * nsub + kin / KX) * XB);
+          const int kc16 = (kin % KX) >> 3;     // 16-byte chunk of the k16 step in the x row
 #pragma unroll
-            for (int nt = 0; nt < NT; ++nt) {
-              uint32_t b0, b1;
-              ldsm_x2(xt + swz_offset(8 * nt + lk, kc16 + (lj & 1), RWX), b0, b1);
-              mma16816<TI>::run(acc[nt], af, b0, b1);
-            }
+          for (int nt = 0; nt < NT; ++nt) {
+            uint32_t b0, b1;
+            ldsm_x2(xt + swz_offset(8 * nt + li, kc16 + (lj & 1), RWX), b0, b1);
+            mma16816<TI>::run(acc[nt], af, b0, b1);
           }
-        } else {
-          const int per = a.kc >> 4;              // k16 steps of a chunk
-          const int c0 = (s - it.n_sp) * a.lrc;
-          const int steps = min(a.lrc, it.n_chunks - c0) * per;
-          const int kcb = a.kc * 2;               // A / H tile row bytes
-          for (int kk = warp; kk < steps; kk += kConsumerWarps) {
-            const int c = kk / per, k16 = kk - c * per;
-            if ((c0 + c) * a.kc + 16 * k16 >= a.r) break;
-            const uint32_t cb = base + uint32_t(c) * cs;
-            uint32_t af[4];
-            ldsm_x4(cb + swz_offset((lj & 1) * 8 + lk, 2 * k16 + (lj >> 1), kcb), af[0], af[1], af[2], af[3]);
+        }
+      } else {
+        const int per = a.kc >> 4;              // k16 steps of a chunk
+        const int c0 = (s - n_sp) * a.lrc;
+        const int steps = min(a.lrc, n_chunks - c0) * per;
+        const int kcb = a.kc * 2;               // A / H tile row bytes
+        for (int kk = warp; kk < steps; kk += kConsumerWarps) {
+          const int c = kk / per, k16 = kk - c * per;
+          if ((c0 + c) * a.kc + 16 * k16 >= a.r) break;
+          const uint32_t cb = base + uint32_t(c) * cs;
+          uint32_t af[4];
+          ldsm_x4(cb + swz_offset((lj & 1) * 8 + li, 2 * k16 + (lj >> 1), kcb), af[0], af[1], af[2], af[3]);
 #pragma unroll
-            for (int nt = 0; nt < NT; ++nt) {
-              uint32_t b0, b1;
-              ldsm_x2(cb + kHOff + swz_offset(8 * nt + lk, 2 * k16 + (lj & 1), kcb), b0, b1);
-              mma16816<TI>::run(acc[nt], af, b0, b1);
-            }
+          for (int nt = 0; nt < NT; ++nt) {
+            uint32_t b0, b1;
+            ldsm_x2(cb + kHOff + swz_offset(8 * nt + li, 2 * k16 + (lj & 1), kcb), b0, b1);
+            mma16816<TI>::run(acc[nt], af, b0, b1);
           }
         }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[slot]);
     }
-    // ----------------------------------------------------------- epilogue
+    const int g = lane >> 2, tig = lane & 3;
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const int m = g8 + ((e & 2) ? 8 : 0);
+        const int m = g + ((e & 2) ? 8 : 0);
         const int t = 8 * nt + 2 * tig + (e & 1);
         red[(warp * kFT + m) * TT + t] = acc[nt][e];
       }
-    named_bar_sync(1, kConsumerWarps * 32);
-    if (!s_abort) {
-      if (!waited_y) {
-        pdl_wait_primary();  // y may be read (in-place operator) or written by preceding kernels
-        waited_y = true;
-      }
-      TI* __restrict__ y = static_cast<TI*>(a.y);
-      const TI* __restrict__ bias = static_cast<const TI*>(a.bias);
-      for (int idx = threadIdx.x; idx < kFT * TT; idx += kConsumerWarps * 32) {
-        const int n = idx % kFT, t = idx / kFT;
-        const int64_t tok = t0 + t;
-        if (tok >= ga.M) continue;
-        float v = 0.f;
-#pragma unroll
-        for (int w = 0; w < kConsumerWarps; ++w) v += red[(w * kFT + n) * TT + t];
-        const int64_t gi = tok * a.ldy + it.n0 + n;
-        if (MODE == MODE_ADDMM) {
-          v = to_f(y[gi]) + v;
-        } else if (bias != nullptr) {
-          v = v + to_f(__ldg(bias + it.n0 + n));
-        }
-        y[gi] = from_f<TI>(v);
-      }
-    }
-    named_bar_sync(1, kConsumerWarps * 32);  // red is free for the next item
   }
-  }  // consumers
   __syncthreads();
-  if (warp == kConsumerWarps && lane == 0 && s_abort) {
-    // wait (bounded) for the copies still in flight before the CTA exits
-    const int g = s_issued;
-    for (int k = max(0, g - S); k < g; ++k) (void)mbar_wait(&full[k % S], (k / S) & 1);
+  if (s_abort) return;
+
+  // ------------------------------------------------------------- epilogue
+  pdl_wait_primary();  // y may be read (in-place operator) or written by preceding kernels
+  TI* __restrict__ y = static_cast<TI*>(a.y);
+  for (int idx = threadIdx.x; idx < kFT * TT; idx += kThreads) {
+    const int n = idx % kFT, t = idx / kFT;
+    const int64_t tok = t0 + t;
+    if (tok >= ga.M) continue;
+    float v = 0.f;
+#pragma unroll
+    for (int w = 0; w < kConsumerWarps; ++w) v += red[(w * kFT + n) * TT + t];
+    const int64_t gi = tok * a.ldy + n0 + n;
+    if (MODE == MODE_ADDMM) {
+      v = to_f(y[gi]) + v;
+    } else if (a.bias != nullptr) {
+      v = v + s_bias[n];
+    }
+    y[gi] = from_f<TI>(v);
   }
 }
 
@@ -668,10 +595,9 @@ MmaShape mma_shape(int bq, int r, int tt) {
   return m;
 }
 
-// Ring depth and grid of the persistent kernel: the depth (kStages or 4
-// slots) that keeps more slots in flight per SM (CTAs per SM x slots; on a tie
-// the shallower ring, i.e. more CTAs), and as many CTAs as fit the SMs at once
-// (at most one per item).
+// Ring depth: the full kStages slots unless 4 slots fit enough more CTAs per
+// SM to need fewer waves of the grid (decode grids of several hundred CTAs
+// then run in one wave; a CTA needs a few stages only at small token counts).
 template <int NT, int KX, typename TI, int MODE>
 int launch_inst(const MmaMaps& maps, MmaArgs k, uint32_t stage, dim3 grid, bool pdl, cudaStream_t s) {
   auto kern = mma_rowblock_kernel<NT, KX, TI, MODE>;
@@ -686,15 +612,12 @@ int launch_inst(const MmaMaps& maps, MmaArgs k, uint32_t stage, dim3 grid, bool 
     SLR_CHECK_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ_low, kern, kThreads, smem_low));
     c_stage = stage;
   }
-  if (occ_full < 1 && occ_low < 1) return fail(SLR_ERR_UNSUPPORTED, "mma path: ring does not fit in shared memory");
-  const bool low = occ_low * 4 >= occ_full * kStages;
-  k.stages = low ? 4 : kStages;
-  k.stage_bytes = stage;
-  k.n_items = int(grid.x);
-  const int occ = low ? occ_low : occ_full;
-  const size_t smem = low ? smem_low : smem_full;
-  const int64_t fit = int64_t(device_sms()) * std::max(occ, 1);
-  grid.x = unsigned(std::min<int64_t>(grid.x, std::max<int64_t>(1, fit / std::max<int64_t>(grid.y, 1))));
+  const int64_t ctas = int64_t(grid.x) * grid.y;
+  const int64_t sms = device_sms();
+  const int64_t waves_full = ceil_div(ctas, sms * std::max(occ_full, 1));
+  const int64_t waves_low = ceil_div(ctas, sms * std::max(occ_low, 1));
+  k.stages = waves_low < waves_full ? 4 : kStages;
+  const size_t smem = k.stages == kStages ? smem_full : smem_low;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = dim3(kThreads);
