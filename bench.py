@@ -312,6 +312,34 @@ def decode_points(dev, steps: int, warmup: int, flush: torch.Tensor, hbm_gbs: fl
     return out
 
 
+def generation_bench(model, dense, vocab: int, dev, batch: int = 8, prompt: int = 128, new: int = 64) -> dict:
+    """Greedy generation tokens/s (new tokens per second over the batch),
+    eager (the KV cache grows each step), timed with CUDA events around the
+    whole call: the KV-cached loop on the S+LR model (decode kernels), the
+    same loop on the dense bf16 model, and the reference's loop (the whole
+    prefix recomputed each step) on the S+LR model over fewer tokens."""
+    from s_salaad_b200.inference import generate, generate_no_cache
+
+    g = torch.Generator(device="cpu").manual_seed(11)
+    ids = torch.randint(0, vocab, (batch, prompt), generator=g).to(dev)
+
+    def rate(fn, m, n) -> float:
+        fn(m, ids, 2)  # warm-up
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        a.record()
+        fn(m, ids, n)
+        b.record()
+        torch.cuda.synchronize()
+        return batch * n / (a.elapsed_time(b) / 1e3)
+
+    return {"unit": "new tokens/s", "batch": batch, "prompt": prompt, "new_tokens": new,
+            "kv_cache_slr": rate(generate, model, new), "kv_cache_dense_bf16": rate(generate, dense, new),
+            "no_cache_slr_reference_loop": rate(generate_no_cache, model, 16),
+            "what": "greedy decoding, eager steps; the reference loop recomputes the prefix each step "
+                    "(measured over 16 new tokens)"}
+
+
 def model_bench(args) -> None:
     """cfg2 as a whole model: the 8-layer LLaMA-60M-shaped model of a
     synthetic bundle, loaded by build_efficient_model (every projection an
@@ -369,6 +397,7 @@ def model_bench(args) -> None:
     with ClockSampler(0) as clocks:
         ms = timed(model)
     ms_dense = timed(ref)
+    gen = generation_bench(model, ref, config["vocab_size"], dev)
     emit({"metric": "compressed LLaMA-60M-shaped model forward tokens/s (cfg2, whole model)",
           "value": batch * seq / (ms / 1e3), "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
           "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
@@ -378,6 +407,7 @@ def model_bench(args) -> None:
                      "l2": "flushed (256 MB write) between timed steps"},
           "dense_bf16": {"ms_per_step": ms_dense, "value": batch * seq / (ms_dense / 1e3),
                          "what": "the same model with dense W = A*B + S (torch/cuBLAS), same graph replay"},
+          "generate": gen,
           "clocks": clocks.summary()})
 
 
