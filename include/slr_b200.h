@@ -289,6 +289,56 @@ SLR_API int slr_lrs_linear_forward_multi(const slr_layer* layers, int n, const v
                            const int64_t* ldx, void* const* y, const int64_t* ldy, int64_t M,
                            void* workspace, size_t workspace_bytes, void* stream);
 
+/* ------------------------------------------- N:M 2:4 + low-rank layer -- */
+
+/*
+ * The other compressed-layer kind of the reference: y = x · Sᵀ + (x · Bᵀ) ·
+ * Aᵀ + bias with S 2:4 sparse along K (at most 2 nonzeros in every aligned
+ * group of 4 input features of a row), _LRSLinearLRNM (ssalaad/efficient/
+ * ls_linear.py:167-224), whose forward (:210-221) runs S on torch's
+ * semi-structured (cuSPARSELt) tensor.  Here S is kept as
+ *   values [N, K/2]  (dtype) the two kept entries of every group of 4, in
+ *                    K order (zeros at the lowest unused positions of a group
+ *                    with fewer nonzeros);
+ *   meta   [N, K/32] uint32: word w of row n covers K [32w, 32w + 32), bits
+ *                    [4i, 4i + 4) group i: low 2 bits the position of the
+ *                    first kept entry, high 2 bits the second (first < second).
+ * 16-bit dtypes; N % 16 == 0, K % 32 == 0, rank % 8 == 0 (rank >= 16).
+ */
+typedef struct slr_nm_layer {
+  int64_t in_features;    /* K */
+  int64_t out_features;   /* N */
+  int64_t rank;           /* r */
+  const void* values;     /* device [N, K/2] */
+  const uint32_t* meta;   /* device [N, K/32] */
+  const void* A;          /* device [N, r] */
+  const void* B;          /* device [r, K] */
+  const void* bias;       /* device [N] or NULL */
+  int32_t dtype;          /* SLR_F16 or SLR_BF16 */
+  int32_t flags;          /* 0 or SLR_FLAG_STRICT_ORDER */
+} slr_nm_layer;
+
+/*
+ * Dense S [N, K] (row-major, dtype) -> values and meta above.  Entries that
+ * are nonzero (or NaN) are kept; SLR_ERR_BAD_INDEX if a group of 4 holds more
+ * than two of them (S is not 2:4 sparse).  Synchronises `stream`.  No
+ * reference counterpart: the reference packs with
+ * torch.sparse.to_sparse_semi_structured (ssalaad/efficient/artifact.py:44-61).
+ */
+SLR_API int slr_nm_compress(const void* S, int64_t N, int64_t K, int dtype, void* values, uint32_t* meta,
+                            void* stream);
+/* Workspace bytes of slr_nm_linear_forward for M tokens (holds H = x · Bᵀ). */
+SLR_API size_t slr_nm_linear_workspace_size(const slr_nm_layer* layer, int64_t M);
+/*
+ * y[M, N] = x[M, K] · Sᵀ + (x · Bᵀ) · Aᵀ + bias: x · Bᵀ rounded to the dtype
+ * (the reference's latent), then the 2:4 sparse product on the sparse tensor
+ * cores, H · Aᵀ and the bias accumulated in fp32 and rounded once (the
+ * reference rounds the sparse product, the addmm and the bias add each).
+ * ldx / ldy: row strides in elements (0 = K / N).
+ */
+SLR_API int slr_nm_linear_forward(const slr_nm_layer* layer, const void* x, int64_t ldx, void* y, int64_t ldy,
+                                  int64_t M, void* workspace, size_t workspace_bytes, void* stream);
+
 /* --------------------------------------------------- dense -> BSR -- */
 
 /*

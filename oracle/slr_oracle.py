@@ -204,6 +204,38 @@ def lr_forward_f32(x, A, B, bias=None):
     return lrs_forward_f32(x, A, B, None, None, None, None, bias)
 
 
+def nm_project_2_4(R):
+    """Keep the 2 largest-magnitude entries of every aligned group of 4 along
+    the last axis (the reference's projection onto the 2:4 set,
+    ssalaad/inference/egar.py:285-291); returns a torch tensor like R."""
+    import torch
+
+    R = torch.as_tensor(_np(R))
+    n, k = R.shape
+    g = R.reshape(n, k // 4, 4)
+    keep = torch.zeros_like(g, dtype=torch.bool)
+    keep.scatter_(-1, g.abs().topk(2, dim=-1).indices, True)
+    return (g * keep).reshape(n, k)
+
+
+def nm_forward_f32(x, A, B, S, bias=None):
+    """Restates ``_LRSLinearLRNM.forward`` (ls_linear.py:210-221) in float32
+    on the CPU: ``latent = F.linear(x, B)``; ``y = F.linear(x, S)`` with S the
+    dense 2:4 matrix; ``y += latent @ A.T``; then the bias (:41-44)."""
+    import torch
+    import torch.nn.functional as F
+
+    x = torch.as_tensor(_np(x)).float()
+    shape = x.shape
+    x2 = x.reshape(-1, shape[-1])
+    latent = F.linear(x2, torch.as_tensor(_np(B)).float())
+    y = F.linear(x2, torch.as_tensor(_np(S)).float())
+    y.addmm_(latent, torch.as_tensor(_np(A)).float().t())
+    if bias is not None:
+        y.add_(torch.as_tensor(_np(bias)).float())
+    return y.reshape(*shape[:-1], y.shape[-1])
+
+
 def ref_avx2_module():
     """The reference's own AVX2 kernel compiled by oracle/build_ref.py, or None."""
     try:

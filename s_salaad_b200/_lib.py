@@ -61,6 +61,9 @@ EXPORTED = (
     "slr_set_wait_limit_ns",
     "slr_lrs_linear_multi_workspace_size",
     "slr_lrs_linear_forward_multi",
+    "slr_nm_compress",
+    "slr_nm_linear_workspace_size",
+    "slr_nm_linear_forward",
 )
 
 SLR_MAX_RANKS = 8
@@ -92,6 +95,23 @@ class SlrLayer(ctypes.Structure):
         ("stage_plan", ctypes.c_void_p),
         ("stage_start", ctypes.c_void_p),
         ("route_out_features", ctypes.c_int64),
+    ]
+
+
+class SlrNmLayer(ctypes.Structure):
+    """Mirror of ``struct slr_nm_layer``."""
+
+    _fields_ = [
+        ("in_features", ctypes.c_int64),
+        ("out_features", ctypes.c_int64),
+        ("rank", ctypes.c_int64),
+        ("values", ctypes.c_void_p),
+        ("meta", ctypes.c_void_p),
+        ("A", ctypes.c_void_p),
+        ("B", ctypes.c_void_p),
+        ("bias", ctypes.c_void_p),
+        ("dtype", ctypes.c_int32),
+        ("flags", ctypes.c_int32),
     ]
 
 
@@ -142,6 +162,9 @@ _SIGS = {
     "slr_lrs_linear_multi_workspace_size": ([ctypes.POINTER(SlrLayer), i32, i64], sz),
     "slr_lrs_linear_forward_multi": ([ctypes.POINTER(SlrLayer), i32, ctypes.POINTER(vp), ctypes.POINTER(i64),
                                       ctypes.POINTER(vp), ctypes.POINTER(i64), i64, vp, sz, vp], i32),
+    "slr_nm_compress": ([vp, i64, i64, i32, vp, vp, vp], i32),
+    "slr_nm_linear_workspace_size": ([ctypes.POINTER(SlrNmLayer), i64], sz),
+    "slr_nm_linear_forward": ([ctypes.POINTER(SlrNmLayer), vp, i64, vp, i64, i64, vp, sz, vp], i32),
 }
 
 _lock = threading.Lock()

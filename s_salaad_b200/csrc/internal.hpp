@@ -140,6 +140,13 @@ int launch_tc_dense(const void* x, int64_t ldx, const void* B, void* H, int64_t 
 int launch_tc_dense_group(const void* x, int64_t ldx, const void* const* Bs, const int64_t* rs, int n,
                           void* H, int64_t M, int64_t K, int64_t ldh, int dtype, cudaStream_t s);
 
+// ---- N:M 2:4 + low-rank layer (16-bit): packer and fused combine (mma.sp).
+int launch_nm_pack(const void* S, int64_t N, int64_t K, int dtype, void* values, uint32_t* meta, int* bad,
+                   cudaStream_t s);
+int launch_nm_combine(const void* x, int64_t ldx, void* y, int64_t ldy, const void* values, const uint32_t* meta,
+                      const void* A, const void* H, int64_t ldh, const void* bias, int64_t M, int64_t N, int64_t K,
+                      int64_t r, int dtype, cudaStream_t s);
+
 // ---- dense -> BSR conversion.
 int launch_bsr_mask(const void* S, int64_t n, int64_t m, int64_t bp, int64_t bq, int dtype,
                     uint8_t* mask, int64_t* crow, cudaStream_t s);

@@ -676,6 +676,96 @@ int slr_lrs_linear_group_combine(const slr_layer* layers, int n, int i, const vo
 
 namespace {
 
+// The low-rank half of an N:M layer as an S+LR layer without S: its x·Bᵀ
+// runs on the same kernels (h_small / tc_dense) into the same H layout.
+slr_layer nm_lowrank_layer(const slr_nm_layer& L) {
+  slr_layer lr{};
+  lr.in_features = L.in_features;
+  lr.out_features = L.out_features;
+  lr.rank = L.rank;
+  lr.A = L.A;
+  lr.B = L.B;
+  lr.bias = L.bias;
+  lr.dtype = L.dtype;
+  lr.flags = L.flags & kFlagStrict;
+  return lr;
+}
+
+int check_nm_layer(const slr_nm_layer* L) {
+  if (!L) return fail(SLR_ERR_INVALID_ARGUMENT, "layer is NULL");
+  if (L->dtype != SLR_F16 && L->dtype != SLR_BF16)
+    return fail(SLR_ERR_UNSUPPORTED_DTYPE, "N:M layer: dtype must be SLR_F16 or SLR_BF16");
+  if (L->in_features <= 0 || L->out_features <= 0 || L->in_features % 32 || L->out_features % 16)
+    return fail(SLR_ERR_INVALID_ARGUMENT, "N:M layer: in_features % 32 == 0 and out_features % 16 == 0 required");
+  if (L->rank < 16 || L->rank % 8) return fail(SLR_ERR_UNSUPPORTED, "N:M layer: rank must be a multiple of 8, >= 16");
+  if (!L->values || !L->meta || !L->A || !L->B) return fail(SLR_ERR_INVALID_ARGUMENT, "N:M layer: NULL tensor");
+  if ((L->flags & ~kFlagStrict) != 0) return fail(SLR_ERR_INVALID_ARGUMENT, "unknown flags");
+  if (!aligned16(L->values) || !aligned16(L->A) || !aligned16(L->B))
+    return fail(SLR_ERR_UNSUPPORTED, "N:M layer: values, A and B must be 16-byte aligned");
+  return SLR_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int slr_nm_compress(const void* S, int64_t N, int64_t K, int dtype, void* values, uint32_t* meta, void* stream) {
+  if (dtype != SLR_F16 && dtype != SLR_BF16) return fail(SLR_ERR_UNSUPPORTED_DTYPE, "N:M: 16-bit dtypes only");
+  if (N <= 0 || K <= 0 || K % 32) return fail(SLR_ERR_INVALID_ARGUMENT, "N:M: K must be a positive multiple of 32");
+  if (!S || !values || !meta) return fail(SLR_ERR_INVALID_ARGUMENT, "null pointer");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int* flag = nullptr;
+  SLR_CHECK_CUDA(cudaHostAlloc(&flag, sizeof(int), cudaHostAllocMapped));
+  *flag = 0;
+  int* dflag = nullptr;
+  cudaError_t e = cudaHostGetDevicePointer(&dflag, flag, 0);
+  int rc = e == cudaSuccess ? SLR_OK : cuda_fail(e, "cudaHostGetDevicePointer");
+  if (!rc) rc = launch_nm_pack(S, N, K, dtype, values, meta, dflag, s);
+  if (!rc) {
+    e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) rc = cuda_fail(e, "nm_compress sync");
+  }
+  const int bad = *flag;
+  cudaFreeHost(flag);
+  if (rc) return rc;
+  if (bad) return fail(SLR_ERR_BAD_INDEX, "S is not 2:4 sparse: a group of 4 input features holds more than 2 entries");
+  return SLR_OK;
+}
+
+size_t slr_nm_linear_workspace_size(const slr_nm_layer* layer, int64_t M) {
+  if (check_nm_layer(layer) != SLR_OK || M < 0) return 0;
+  const slr_layer lr = nm_lowrank_layer(*layer);
+  return slr_lrs_linear_workspace_size(&lr, M);
+}
+
+int slr_nm_linear_forward(const slr_nm_layer* layer, const void* x, int64_t ldx, void* y, int64_t ldy, int64_t M,
+                          void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_nm_layer(layer);
+  if (rc) return rc;
+  const slr_nm_layer& L = *layer;
+  if (ldx == 0) ldx = L.in_features;
+  if (ldy == 0) ldy = L.out_features;
+  if (M < 0 || ldx < L.in_features || ldy < L.out_features)
+    return fail(SLR_ERR_INVALID_ARGUMENT, "bad M or row strides");
+  if (M == 0) return SLR_OK;
+  if (!x || !y) return fail(SLR_ERR_INVALID_ARGUMENT, "x/y is NULL");
+  if (ldx % 8 || !aligned16(x)) return fail(SLR_ERR_UNSUPPORTED, "N:M layer: x rows must be 16-byte aligned");
+  const slr_layer lr = nm_lowrank_layer(L);
+  FwdCall c;
+  rc = prepare_forward(&lr, x, ldx, y, ldy, M, workspace, workspace_bytes, true, c);
+  if (rc) return rc;
+  if (c.p.path != 1) return fail(SLR_ERR_UNSUPPORTED, "N:M layer: shapes outside the 16-bit kernels");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  rc = run_lowrank(lr, c, s);
+  if (rc) return rc;
+  return launch_nm_combine(x, ldx, y, ldy, L.values, L.meta, L.A, c.ws, c.p.ldh, L.bias, M, L.out_features,
+                           L.in_features, L.rank, L.dtype, s);
+}
+
+}  // extern "C"
+
+namespace {
+
 constexpr int kMaxMulti = kMaxLaunchLayers;  // layers per multi-input call
 
 // Workspace of slr_lrs_linear_forward_multi: below 128 tokens with every

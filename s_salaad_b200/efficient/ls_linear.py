@@ -14,9 +14,12 @@ kernels of libslr_b200 instead of F.linear + TileLang:
   calls, the in-place TileLang kernel and a bias pass.
 * :func:`LRSLinear` (reference :227-285) — the factory.
 
+* :class:`_LRSLinearLRNM` (reference :167-224) — S 2:4 sparse along K: the
+  sparse product on the sparse tensor cores (mma.sp) fused with the
+  up-projection and the bias, instead of cuSPARSELt plus addmm and a bias pass.
+
 There is no CPU path: CPU tensors are rejected with ValueError (the
-reference's CPU kernel stays the oracle).  The N:M kind (reference :167-224)
-is not provided.
+reference's CPU kernel stays the oracle).
 """
 from __future__ import annotations
 
@@ -139,13 +142,62 @@ class _LRSLinearLRBlockCUDA(_LRSLinearLRBlockBase):
                     values=self.S_values, row_order=self._row_order)
 
 
+class _LRSLinearLRNM(_LRSLinearBase):
+    """S with at most 2 nonzeros in every aligned group of 4 input features.
+
+    Same constructor arguments, persistent buffers (``A``, ``B``, ``bias``)
+    and ``S_nnz`` (kept entries, K/2 per row) as the reference class
+    (ls_linear.py:167-190); S may be given dense or as a torch sparse tensor
+    (the reference takes torch's semi-structured packing of it).  S is kept in
+    the library's compressed layout (``_nm_values`` [N, K/2] and ``_nm_meta``
+    [N, K/32], non-persistent like the reference's packed buffers)."""
+
+    kind = "nm"
+
+    def __init__(self, A: torch.Tensor, B: torch.Tensor, S: torch.Tensor, *, in_features: int, out_features: int,
+                 bias: torch.Tensor | None = None) -> None:
+        super().__init__(A, B, in_features=in_features, out_features=out_features, bias=bias)
+        self._check_device()
+        if A.dtype not in (torch.float16, torch.bfloat16):
+            raise ValueError("The B200 N:M kernel requires fp16 or bf16.")
+        dense = S.to_dense() if S.layout != torch.strided else S
+        if tuple(dense.shape) != (out_features, in_features):
+            raise ValueError(f"S shape {tuple(dense.shape)} must equal "
+                             f"(out_features, in_features)=({out_features},{in_features})")
+        values, meta = ops.nm_compress(dense.to(device=A.device, dtype=A.dtype))
+        self.S_nnz = int(values.numel())
+        self.register_buffer("_nm_values", values, persistent=False)
+        self.register_buffer("_nm_meta", meta, persistent=False)
+        self._nm_desc: ops.NmLayerDesc | None = None
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        t = (self._nm_values, self._nm_meta, self.A, self.B, self.bias)
+        key = tuple(None if v is None else v.data_ptr() for v in t)
+        d = self._nm_desc
+        if d is None or getattr(d, "key", None) != key:
+            d = ops.NmLayerDesc(values=self._nm_values, meta=self._nm_meta, A=self.A, B=self.B, bias=self.bias,
+                                in_features=self.in_features, out_features=self.out_features)
+            d.key = key
+            self._nm_desc = d
+        shape = x.shape
+        x2 = x.reshape(-1, shape[-1])
+        if not x2.is_contiguous():
+            x2 = x2.contiguous()
+        return d.forward(x2).reshape(*shape[:-1], self.out_features)
+
+    def extra_repr(self) -> str:
+        return (f"in_features={self.in_features}, out_features={self.out_features}, rank={self.r}, "
+                f"S_nnz={self.S_nnz}, N:M 2:4 (sparse tensor cores), bias={self.bias is not None}")
+
+
 def LRSLinear(A, B, S_sparse, *, in_features, out_features, bias=None, block_p=None, block_q=None,
               nm_n=None, nm_m=None):
     """Compute ``x @ (A @ B + S).T + bias`` with the B200 kernels.
 
     Same dispatch as the reference factory (ls_linear.py:227-285): LR-only
-    when S has no stored entry, the block kernel for BSR S.  N:M S and CPU
-    tensors are rejected (ValueError) — this package is the CUDA path only.
+    when S has no stored entry, the N:M 2:4 kernel when ``nm_n``/``nm_m`` are
+    given, the block kernel for BSR S.  CPU tensors are rejected (ValueError)
+    — this package is the CUDA path only.
     """
     if S_sparse.layout == torch.strided:
         nnz = int(torch.count_nonzero(S_sparse))
@@ -157,7 +209,9 @@ def LRSLinear(A, B, S_sparse, *, in_features, out_features, bias=None, block_p=N
     if nnz == 0:
         return _LRSLinearLR(A, B, **kwargs)
     if nm_n is not None:
-        raise ValueError("N:M inference is not provided by s_salaad_b200.")
+        if (nm_n, nm_m) != (2, 4):
+            raise ValueError("N:M inference requires CUDA and a 2:4 mask.")
+        return _LRSLinearLRNM(A, B, S_sparse, **kwargs)
     if block_p is None or block_q is None:
         raise ValueError("Sparse S needs a recorded block shape to pick a kernel.")
     if S_sparse.layout == torch.strided:

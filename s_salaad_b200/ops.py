@@ -396,6 +396,76 @@ class LayerSet:
         return outs
 
 
+# ------------------------------------------------ N:M 2:4 + low-rank --
+
+def nm_compress(S: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Dense 2:4-sparse S [N, K] (CUDA, fp16/bf16) -> (values [N, K/2],
+    meta [N, K/32] int32 view of the uint32 words), the layout of
+    ``slr_nm_compress``.  ValueError if S is not 2:4 sparse."""
+    _require_cuda("S", S)
+    if S.dim() != 2:
+        raise ValueError("S must be 2-D")
+    N, K = S.shape
+    if K % 32:
+        raise ValueError(f"N:M layer: in_features {K} must be a multiple of 32")
+    S = S.contiguous()
+    values = torch.empty(N, K // 2, dtype=S.dtype, device=S.device)
+    meta = torch.empty(N, K // 32, dtype=torch.int32, device=S.device)
+    with _DeviceGuard(S.device):
+        rc = _lib.load().slr_nm_compress(S.data_ptr(), N, K, slr_dtype(S.dtype), values.data_ptr(),
+                                         meta.data_ptr(), _stream(S.device))
+    _lib.check(rc, "nm_compress")
+    return values, meta
+
+
+def nm_expand(values: torch.Tensor, meta: torch.Tensor) -> torch.Tensor:
+    """Inverse of :func:`nm_compress` (host-side torch ops): the dense S."""
+    N, half = values.shape
+    K = 2 * half
+    words = meta.to(torch.int64) & 0xFFFFFFFF                        # [N, K/32]
+    shifts = torch.arange(8, device=meta.device) * 4
+    nib = (words.unsqueeze(-1) >> shifts) & 0xF                       # [N, K/32, 8]
+    first, second = nib & 3, nib >> 2
+    base = (torch.arange(K // 4, device=meta.device) * 4).view(K // 32, 8)
+    pos = torch.stack((first + base, second + base), dim=-1).reshape(N, K // 2)
+    S = torch.zeros(N, K, dtype=values.dtype, device=values.device)
+    S.scatter_(1, pos, values)
+    return S
+
+
+class NmLayerDesc:
+    """Owns an ``slr_nm_layer`` descriptor plus its workspace (the N:M 2:4 +
+    low-rank layer: values/meta from :func:`nm_compress`, A [N, r], B [r, K])."""
+
+    def __init__(self, *, values, meta, A, B, bias=None, in_features: int, out_features: int, flags: int = 0):
+        self.tensors = dict(values=values, meta=meta, A=A, B=B, bias=bias)
+        self.in_features, self.out_features = int(in_features), int(out_features)
+        s = self.struct = _lib.SlrNmLayer()
+        s.in_features, s.out_features, s.rank = self.in_features, self.out_features, int(A.shape[1])
+        s.values, s.meta = values.data_ptr(), meta.data_ptr()
+        s.A, s.B, s.bias = A.data_ptr(), B.data_ptr(), _ptr(bias)
+        s.dtype, s.flags = slr_dtype(A.dtype), int(flags)
+        self.device, self.dtype = A.device, A.dtype
+        self._ws: torch.Tensor | None = None
+
+    def forward(self, x2: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        lib = _lib.load()
+        M = x2.shape[0]
+        if out is None:
+            out = torch.empty(M, self.out_features, dtype=self.dtype, device=self.device)
+        need = int(lib.slr_nm_linear_workspace_size(ctypes.byref(self.struct), M))
+        if need and (self._ws is None or self._ws.numel() < need):
+            self._ws = torch.empty(need, dtype=torch.uint8, device=self.device)
+        ws = self._ws if need else None
+        with _DeviceGuard(self.device):
+            rc = lib.slr_nm_linear_forward(ctypes.byref(self.struct), x2.data_ptr(), LayerDesc._ld(x2),
+                                           out.data_ptr(), LayerDesc._ld(out), M,
+                                           None if ws is None else ws.data_ptr(), 0 if ws is None else ws.numel(),
+                                           _stream(self.device))
+        _lib.check(rc, "nm_linear_forward")
+        return out
+
+
 def lrs_linear_forward(desc: LayerDesc, x: torch.Tensor) -> torch.Tensor:
     """``y = x @ S.T + (x @ B.T) @ A.T + bias`` for x of shape ``[..., in]``."""
     _require_cuda("x", x)
