@@ -215,7 +215,7 @@ def nm_project_2_4(R):
     g = R.reshape(n, k // 4, 4)
     keep = torch.zeros_like(g, dtype=torch.bool)
     keep.scatter_(-1, g.abs().topk(2, dim=-1).indices, True)
-    return (g * keep).reshape(n, k)
+    return torch.where(keep, g, torch.zeros_like(g)).reshape(n, k)
 
 
 def nm_forward_f32(x, A, B, S, bias=None):

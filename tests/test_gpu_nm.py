@@ -38,6 +38,7 @@ def sparse_2_4(n, k, seed, std=0.02, dtype=torch.bfloat16, partial=True):
         first = groups[one].clone()
         keep = first.abs().argmax(-1, keepdim=True)
         groups[one] = torch.zeros_like(first).scatter_(-1, keep, first.gather(-1, keep))
+    assert not bool((S == 0).logical_and(S.signbit()).any())  # every dropped entry is +0
     return S.to(dtype)
 
 
