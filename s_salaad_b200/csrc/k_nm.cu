@@ -18,8 +18,11 @@
 //                     [4i, 4i + 4) describe group i (K 32w + 4i .. + 3): low
 //                     2 bits the position of the first kept entry, high 2
 //                     bits the second (first < second).
-// That word is what mma.sp takes as the metadata of one row of a 16 x 32 A
-// tile, so the kernel hands it over unchanged.
+// mma.sp (m16n8k32, 16-bit, sparsity selector 0) takes the metadata of a 16 x
+// 32 A tile from lanes 4g and 4g + 1 of each quad g: lane 4g holds groups 0-3
+// of rows g (bits 0-15) and g + 8 (bits 16-31), lane 4g + 1 groups 4-7 of the
+// same rows (checked on a B200 with an exact small-integer product); the
+// kernel builds those registers from the two rows' words.
 #include <algorithm>
 
 #include "internal.hpp"
@@ -177,9 +180,13 @@ __global__ void __launch_bounds__(kNmWarps * 32) nm_combine_kernel(const NmArgs 
         const TI* src = x + (tok < a.M ? tok : 0) * a.ldx + int64_t(s) * 32 + c * 8;
         cp_async16(slot + A_TILE + xr * 64 + ((c ^ ((xr >> 1) & 3)) << 4), src, tok < a.M ? 16u : 0u);
       }
-      // metadata: lane 4g holds row g's word, lane 4g + 1 row g + 8's
+      // metadata: lane 4g takes groups 0-3 of rows g and g + 8, lane 4g + 1 groups 4-7
       uint32_t m = 0;
-      if (tq < 2) m = __ldg(a.meta + (f0 + g + 8 * tq) * (a.K / 32) + s);
+      if (tq < 2) {
+        const uint32_t w0 = __ldg(a.meta + (f0 + g) * (a.K / 32) + s);
+        const uint32_t w1 = __ldg(a.meta + (f0 + g + 8) * (a.K / 32) + s);
+        m = tq == 0 ? ((w0 & 0xffffu) | (w1 << 16)) : ((w0 >> 16) | (w1 & 0xffff0000u));
+      }
       metas[i % kNmDepth] = m;
     } else {
       const int l = warp + kNmWarps * (i - my_sp);  // rank chunk of 16
