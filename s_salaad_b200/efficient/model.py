@@ -88,7 +88,10 @@ class _ProjectionGroup:
         return self._group
 
     def output(self, i: int, x: torch.Tensor) -> torch.Tensor:
-        key = (x.data_ptr(), x._version, tuple(x.shape), x.dtype, x.device)
+        # inference tensors keep no version counter; there the storage, shape
+        # and the pending outputs being taken in member order identify the call
+        version = -1 if x.is_inference() else x._version
+        key = (x.data_ptr(), version, tuple(x.shape), x.dtype, x.device)
         if self._input_key == key and self._pending[i] is not None:
             y, self._pending[i] = self._pending[i], None
             return y
