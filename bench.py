@@ -340,6 +340,50 @@ def generation_bench(model, dense, vocab: int, dev, batch: int = 8, prompt: int 
                     "(measured over 16 new tokens)"}
 
 
+def nm_points(dev, steps: int, warmup: int, flush: torch.Tensor, peaks_: dict) -> dict:
+    """The N:M 2:4 + low-rank layer (the reference's other compressed-layer
+    kind) on a LLaMA-7B-shaped MLP projection: 11008 x 4096, S 2:4 (the 2
+    largest of N(0, 0.02) in every group of 4), rank 512, bf16, at a decode
+    and a prefill token count; each beside dense cuBLAS on W = A*B + S, both
+    replayed from a CUDA graph with L2 flushed between replays.  Decode: HBM
+    roofline on the algorithmic bytes (S values + metadata, A, B, bias, x, y).
+    Prefill: FLOP rate on 2*T*(N*K/2 + r*(N+K)) against the measured dense
+    bf16 peak."""
+    from s_salaad_b200 import workloads
+    from s_salaad_b200.efficient import LRSLinear
+
+    n, k, r = 11008, 4096, 512
+    g = torch.Generator(device="cpu").manual_seed(24)
+    R = torch.randn(n, k, generator=g) * 0.02
+    grp = R.view(n, k // 4, 4)
+    keep = torch.zeros_like(grp, dtype=torch.bool).scatter_(-1, grp.abs().topk(2, dim=-1).indices, True)
+    S = torch.where(keep, grp, torch.zeros_like(grp)).view(n, k).to(dev, torch.bfloat16)
+    A = (torch.randn(n, r, generator=g) * (0.02 / 8)).to(dev, torch.bfloat16)
+    B = (torch.randn(r, k, generator=g) * (0.02 / 8)).to(dev, torch.bfloat16)
+    bias = (torch.randn(n, generator=g) * 0.01).to(dev, torch.bfloat16)
+    layer = LRSLinear(A, B, S, in_features=k, out_features=n, bias=bias, nm_n=2, nm_m=4)
+    W = (A.float() @ B.float() + S.float()).to(torch.bfloat16)
+    out = {}
+    for T in (1, 4096):
+        x = workloads.tokens(T, k, seed=T, device=dev, dtype=torch.bfloat16)
+        y = torch.empty(T, n, device=dev, dtype=torch.bfloat16)
+        ms = graph_ms(lambda: layer(x), dev, steps, warmup, flush)
+        ms_dense = graph_ms(lambda: torch.addmm(bias, x, W.t(), out=y), dev, steps, warmup, flush)
+        point = {"ms": ms, "tokens_per_s": T / (ms / 1e3), "cublas_dense_ms": ms_dense}
+        if T <= 16:
+            nbytes = 2 * n * (k // 2) + 4 * n * (k // 32) + 2 * r * (n + k) + 2 * n + 2 * T * (k + n)
+            point.update({"algorithmic_bytes": nbytes, "achieved_gbs": nbytes / (ms / 1e3) / 1e9,
+                          "frac": nbytes / (ms / 1e3) / 1e9 / peaks_["hbm_gbs"], "bound": "hbm"})
+        else:
+            fl = 2 * T * (n * k // 2 + r * (n + k))
+            point.update({"algorithmic_flops": fl, "achieved_tflops": fl / (ms / 1e3) / 1e12,
+                          "frac": fl / (ms / 1e3) / 1e12 / peaks_["bf16_tflops"], "bound": "tensor (dense peak)"})
+        out[f"T{T}"] = point
+        del x, y
+    return {"shape": [n, k], "rank": r, "sparsity": "2:4 along K", "kernel": "mma.sp (m16n8k32) + mma.sync, one "
+            "fused launch after x*B^T", "points": out}
+
+
 def model_bench(args) -> None:
     """cfg2 as a whole model: the 8-layer LLaMA-60M-shaped model of a
     synthetic bundle, loaded by build_efficient_model (every projection an
@@ -901,8 +945,10 @@ def main() -> None:
 
     # ------------------------------------------- decode points (N=1 headline)
     decode = None
+    nm24 = None
     if world == 1 and args.workload == "cfg4" and not args.no_decode:
         decode = decode_points(dev, max(K, 20), args.warmup, flush, P["hbm_gbs"])
+        nm24 = nm_points(dev, max(K, 20), args.warmup, flush, P)
 
     # ------------------------------------------------------- CPU baseline
     cpu = None
@@ -931,6 +977,8 @@ def main() -> None:
                                           "d2h_bytes_per_step": d2h},
                 "gpu_launches": launches_per_step * K, "clocks": clocks.summary(),
                 "cpu_baseline": cpu, "cublas_dense": cublas}
+        if nm24 is not None:
+            line["nm24"] = nm24
         if decode is not None:
             line["decode"] = {"what": "decode-sized layer sets on 1 GPU, each step replayed from a CUDA graph with L2 "
                                       "flushed between steps; roofline = algorithmic bytes (weights, indices, x, y) "
