@@ -324,7 +324,7 @@ def generation_bench(model, dense, vocab: int, dev, batch: int = 8, prompt: int 
     ids = torch.randint(0, vocab, (batch, prompt), generator=g).to(dev)
 
     def rate(fn, m, n) -> float:
-        fn(m, ids, 2)  # warm-up
+        fn(m, ids, n)  # warm-up over the same lengths (attention set-up per KV length is paid here)
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         torch.cuda.synchronize()
         a.record()

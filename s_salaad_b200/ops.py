@@ -30,7 +30,14 @@ def slr_dtype(dtype: torch.dtype) -> int:
         raise TypeError(f"s_salaad_b200 supports float32/float16/bfloat16, got {dtype}") from None
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def _stream(device: torch.device) -> int:
+    """The current CUDA stream of `device` as a raw handle (the cheap path
+    when torch provides it: this runs once per library call)."""
+    if _raw_stream is not None:
+        return _raw_stream(device.index if device.index is not None else torch.cuda.current_device())
     return torch.cuda.current_stream(device).cuda_stream
 
 
@@ -134,6 +141,7 @@ class LayerDesc:
         self.block_q = int(block_q)
         self.struct = _lib.SlrLayer()
         self._ws: torch.Tensor | None = None
+        self._ws_sizes: dict = {}
         self._plan_key = None
         self._plan = None
         self.refresh()
@@ -177,7 +185,14 @@ class LayerDesc:
         s.stage_start = self._plan[1].data_ptr() if self._plan is not None else None
 
     def workspace_bytes(self, M: int) -> int:
-        return int(_lib.load().slr_lrs_linear_workspace_size(ctypes.byref(self.struct), M))
+        key = (bytes(self.struct), M)  # the size depends on the descriptor and M only
+        need = self._ws_sizes.get(key)
+        if need is None:
+            need = int(_lib.load().slr_lrs_linear_workspace_size(ctypes.byref(self.struct), M))
+            if len(self._ws_sizes) > 64:
+                self._ws_sizes.clear()
+            self._ws_sizes[key] = need
+        return need
 
     def workspace(self, M: int, at_least: int = 0) -> torch.Tensor | None:
         need = max(self.workspace_bytes(M), at_least)
@@ -251,13 +266,19 @@ class LayerGroup:
         self._ws: torch.Tensor | None = None
 
     def _structs(self):
-        arr = (_lib.SlrLayer * len(self.descs))()
-        for i, d in enumerate(self.descs):
-            ctypes.memmove(ctypes.byref(arr[i]), ctypes.byref(d.struct), ctypes.sizeof(_lib.SlrLayer))
-        return arr
+        """The members' descriptors as one C array (rebuilt when one changes)."""
+        blob = b"".join(bytes(d.struct) for d in self.descs)
+        if blob != getattr(self, "_blob", None):
+            arr = (_lib.SlrLayer * len(self.descs))()
+            ctypes.memmove(arr, blob, len(blob))
+            self._arr, self._blob, self._ws_sizes = arr, blob, {}
+        return self._arr
 
     def workspace(self, M: int) -> torch.Tensor | None:
-        need = int(_lib.load().slr_lrs_linear_group_workspace_size(self._structs(), len(self.descs), M))
+        arr = self._structs()
+        need = self._ws_sizes.get(M)
+        if need is None:
+            need = self._ws_sizes[M] = int(_lib.load().slr_lrs_linear_group_workspace_size(arr, len(self.descs), M))
         if need == 0:
             return None
         if self._ws is None or self._ws.numel() < need:
@@ -361,13 +382,19 @@ class LayerSet:
         self._ws: torch.Tensor | None = None
 
     def _structs(self):
-        arr = (_lib.SlrLayer * len(self.descs))()
-        for i, d in enumerate(self.descs):
-            ctypes.memmove(ctypes.byref(arr[i]), ctypes.byref(d.struct), ctypes.sizeof(_lib.SlrLayer))
-        return arr
+        """The members' descriptors as one C array (rebuilt when one changes)."""
+        blob = b"".join(bytes(d.struct) for d in self.descs)
+        if blob != getattr(self, "_blob", None):
+            arr = (_lib.SlrLayer * len(self.descs))()
+            ctypes.memmove(arr, blob, len(blob))
+            self._arr, self._blob, self._ws_sizes = arr, blob, {}
+        return self._arr
 
     def workspace(self, M: int) -> torch.Tensor | None:
-        need = int(_lib.load().slr_lrs_linear_multi_workspace_size(self._structs(), len(self.descs), M))
+        arr = self._structs()
+        need = self._ws_sizes.get(M)
+        if need is None:
+            need = self._ws_sizes[M] = int(_lib.load().slr_lrs_linear_multi_workspace_size(arr, len(self.descs), M))
         if need == 0:
             return None
         if self._ws is None or self._ws.numel() < need:

@@ -391,8 +391,10 @@ def test_group_forward_equals_per_layer(cuda, group, T):
 
 # -------------------------------------------------- full-size properties --
 
-def torch_ref(t: dict, spec, x: torch.Tensor) -> torch.Tensor:
-    """Plain PyTorch fp32 reference of the same op (on the GPU, full size)."""
+def torch_ref(t: dict, spec, x: torch.Tensor, round_h: bool = False) -> torch.Tensor:
+    """Plain PyTorch fp32 reference of the same op (on the GPU, full size).
+    round_h: x·Bᵀ rounded to the input dtype first, as the reference's CUDA
+    layer's first F.linear returns it (ls_linear.py:131)."""
     S = torch.zeros(spec.out_features, spec.in_features, device=x.device)
     vals = t["values_pq"].to(x.device).float()
     rows = torch.from_numpy(np.repeat(np.arange(spec.nb), np.diff(spec.crow))).to(x.device)
@@ -402,7 +404,10 @@ def torch_ref(t: dict, spec, x: torch.Tensor) -> torch.Tensor:
     Sb[rows, cols] = vals
     S = Sb.permute(0, 2, 1, 3).reshape(spec.out_features, spec.in_features)
     xf = x.float()
-    y = xf @ S.T + (xf @ t["B"].to(x.device).float().T) @ t["A"].to(x.device).float().T
+    h = xf @ t["B"].to(x.device).float().T
+    if round_h:
+        h = h.to(x.dtype).float()
+    y = xf @ S.T + h @ t["A"].to(x.device).float().T
     if t["bias"] is not None:
         y = y + t["bias"].to(x.device).float()
     return y
@@ -425,6 +430,8 @@ def test_full_size_configs_match_torch_fp32(cuda, cfg, T, parity_log):
             y = ops.lrs_linear_forward(desc_for(t, spec, cuda, torch.bfloat16), x)
             ref = torch_ref(t, spec, x)
             parity_log(f"{cfg} T={T} {spec.name} {spec.out_features}x{spec.in_features}", y, ref)
+            # the same against the reference's arithmetic up to x·Bᵀ (rounded like its latent)
+            parity_log(f"{cfg} T={T} {spec.name} vs H rounded", y, torch_ref(t, spec, x, round_h=True))
             assert_16bit_close(y, ref)
             del t, x, y, ref
     finally:
