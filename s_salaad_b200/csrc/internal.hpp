@@ -133,12 +133,14 @@ bool tc2_rowblock_supported(const RowblockArgs& a);  // 2-SM pairs, M >= 256, bp
 // peers: also store every output tile into the other ranks' y (null = local only).
 int launch_tc2_rowblock(const RowblockArgs& a, bool pdl, cudaStream_t s, const PeerArgs* peers = nullptr);
 bool tc_dense_supported(const void* x, int64_t ldx, const void* B, int64_t K, int64_t r, int dtype);
+// pdl: may start while the preceding kernel runs (it waits for that kernel
+// before its first load).
 int launch_tc_dense(const void* x, int64_t ldx, const void* B, void* H, int64_t M, int64_t K, int64_t r,
-                    int64_t ldh, int dtype, cudaStream_t s);
+                    int64_t ldh, int dtype, cudaStream_t s, bool pdl = false);
 // x · [B_0; ...; B_{n-1}]ᵀ (n <= 4, same K) into H [M, ldh]: segment i takes
 // columns [sum_{j<i} round_up(r_j, 64), + round_up(r_i, 64)).
 int launch_tc_dense_group(const void* x, int64_t ldx, const void* const* Bs, const int64_t* rs, int n,
-                          void* H, int64_t M, int64_t K, int64_t ldh, int dtype, cudaStream_t s);
+                          void* H, int64_t M, int64_t K, int64_t ldh, int dtype, cudaStream_t s, bool pdl = false);
 
 // ---- N:M 2:4 + low-rank layer (16-bit): packer and fused combine (mma.sp).
 int launch_nm_pack(const void* S, int64_t N, int64_t K, int dtype, void* values, uint32_t* meta, int* bad,

@@ -518,7 +518,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
   __shared__ volatile int s_abort;
 
-  pdl_launch_dependents();  // the combine kernel may start its sparse part
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -541,11 +540,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const int n_items = a.n_mtiles * a.n_ntiles;
+  // Launched as a programmatic dependent, this kernel waits here for the kernel
+  // before it (x may be its output) and only then lets the next one start
+  // (the combine, which reads x before its own wait and H after it).  So a
+  // chain combine -> x*B^T -> combine never reads an unfinished x.
+  pdl_wait_primary();
+  pdl_launch_dependents();
 
   if (warp == 0) {
     if (lane == 0) {
       tma_prefetch_desc(&tm_x);
       for (int sg = 0; sg < a.n_seg; ++sg) tma_prefetch_desc(&maps.b[sg]);
+
       uint32_t g = 0;
       for (int item = blockIdx.x; item < n_items && !s_abort; item += gridDim.x) {
         const int mt = item % a.n_mtiles, nt = item / a.n_mtiles;
@@ -739,7 +745,7 @@ bool tc_dense_supported(const void* x, int64_t ldx, const void* B, int64_t K, in
 }
 
 int launch_tc_dense_group(const void* x, int64_t ldx, const void* const* Bs, const int64_t* rs, int n,
-                          void* H, int64_t M, int64_t K, int64_t ldh, int dtype, cudaStream_t s) {
+                          void* H, int64_t M, int64_t K, int64_t ldh, int dtype, cudaStream_t s, bool pdl) {
   if (M <= 0 || n <= 0) return SLR_OK;
   if (n > kMaxSeg) return fail(SLR_ERR_UNSUPPORTED, "tc_dense: too many weight matrices in one group");
   CUtensorMap tx{};
@@ -773,8 +779,17 @@ int launch_tc_dense_group(const void* x, int64_t ldx, const void* const* Bs, con
     const int stages = std::min(8, int((196 * 1024) / stage));
     const size_t smem = 1024 + size_t(stages) * stage + (2 * stages + 4) * 8 + 16;
     SLR_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
-    kern<<<unsigned(std::min(items, num_sms())), kThreads, smem, s>>>(tx, maps, k);
-    SLR_CHECK_LAUNCH("tc_dense_kernel");
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(unsigned(std::min(items, num_sms())));
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    SLR_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kern, tx, maps, k));
     return SLR_OK;
   };
   if (dtype == SLR_BF16) {
@@ -788,9 +803,9 @@ int launch_tc_dense_group(const void* x, int64_t ldx, const void* const* Bs, con
 }
 
 int launch_tc_dense(const void* x, int64_t ldx, const void* B, void* H, int64_t M, int64_t K, int64_t r,
-                    int64_t ldh, int dtype, cudaStream_t s) {
+                    int64_t ldh, int dtype, cudaStream_t s, bool pdl) {
   if (M <= 0 || r <= 0) return SLR_OK;
-  return launch_tc_dense_group(x, ldx, &B, &r, 1, H, M, K, ldh, dtype, s);
+  return launch_tc_dense_group(x, ldx, &B, &r, 1, H, M, K, ldh, dtype, s, pdl);
 }
 
 int read_and_clear_status_tc(unsigned* out) {

@@ -135,6 +135,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   cluster_sync();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // The next kernel of the stream (the next projection's combine or x*B^T,
+  // launched as a programmatic dependent) may take SMs as this persistent
+  // grid's CTAs leave; it reads what this grid writes only after its own
+  // griddepcontrol.wait.
+  pdl_launch_dependents();
   if (warp >= 2 && warp < 6) {
     const uint32_t lane_base = uint32_t(32 * (warp & 3)) << 16;
     for (uint32_t c = 0; c < 2 * ACC; c += 16) tmem_st16_zero(tmem + lane_base + c);

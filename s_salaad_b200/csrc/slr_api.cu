@@ -384,7 +384,8 @@ int run_lowrank(const slr_layer& L, const FwdCall& c, cudaStream_t s) {
   // whole layer does (the small-batch kernel splits K by M).
   if (c.p.path == 1 && c.a.M >= kTcMinTokens &&
       tc_dense_supported(c.a.x, c.a.ldx, L.B, L.in_features, L.rank, L.dtype))
-    return launch_tc_dense(c.a.x, c.a.ldx, L.B, c.ws, c.a.M, L.in_features, L.rank, c.p.ldh, L.dtype, s);
+    return launch_tc_dense(c.a.x, c.a.ldx, L.B, c.ws, c.a.M, L.in_features, L.rank, c.p.ldh, L.dtype, s,
+                           early_start(L));
   if (c.p.path == 1) {
     const void* B = L.B;
     const void* x = c.a.x;
@@ -592,7 +593,7 @@ int group_lowrank(const slr_layer* layers, int n, const GroupCall& gc, cudaStrea
   const RowblockArgs& a0 = gc.c[0].a;
   if (gc.mode == GROUP_TC)
     return launch_tc_dense_group(a0.x, a0.ldx, Bs, rs, n, gc.ws, a0.M, layers[0].in_features, gc.g.ldh_all,
-                                 layers[0].dtype, s);
+                                 layers[0].dtype, s, group_early_start(layers, n));
   const void* xs[kMaxGroup];
   int64_t ldxs[kMaxGroup], Ks[kMaxGroup];
   for (int i = 0; i < n; ++i) {

@@ -309,12 +309,14 @@ def _chain(cuda, T, flags, between=None, shared_ws=True):
     return run
 
 
-@pytest.mark.parametrize("T", [1, 16, 64])
+@pytest.mark.parametrize("T", [1, 16, 64, 600])
 @pytest.mark.parametrize("variant", ["shared_ws", "own_ws", "torch_op_between"])
 def test_chained_layers_early_start_equals_strict_order(cuda, T, variant):
-    """Back-to-back small-batch calls overlap through programmatic dependent
-    launch (weights loaded before griddepcontrol.wait); the results must be
-    bit-identical to fully serialised launches (SLR_FLAG_STRICT_ORDER)."""
+    """Back-to-back calls overlap through programmatic dependent launch
+    (small batches: weights loaded before griddepcontrol.wait; 600 tokens: the
+    tensor-core combine -> x*B^T -> combine chain, each layer's x the previous
+    layer's y); the results must be bit-identical to fully serialised
+    launches (SLR_FLAG_STRICT_ORDER)."""
     between = (lambda h: h * 0.5) if variant == "torch_op_between" else None
     x = workloads.tokens(T, 1024, seed=T, dtype=torch.bfloat16).to(cuda)
     y_early = _chain(cuda, T, 0, between, variant != "own_ws")(x)
