@@ -260,10 +260,12 @@ def graph_ms(fn, dev, steps: int, warmup: int, flush: torch.Tensor) -> float:
 
 def decode_points(dev, steps: int, warmup: int, flush: torch.Tensor, hbm_gbs: float) -> dict:
     """The decode-sized workloads (HBM-bound) on one GPU, each as
-    * `multi`: the whole projection set as one multi-input call (the inputs are
-      independent in the layer set: 2 launches);
+    * the whole projection set as one call (the inputs are independent in the
+      layer set): one launch of the single-launch decode kernel;
     * `model_order`: per input group, in decoder order (q/k/v grouped, o,
-      gate/up grouped, down), as a model that chains them would call them.
+      gate/up grouped, down), as a model that chains them would call them
+      (one launch per group);
+    * `two_launch_path`: the set as one call on the x·Bᵀ + combine kernels.
     Algorithmic bytes: weights and indices of every projection plus x and y
     (2 bytes per element); frac = achieved / measured HBM peak."""
     from s_salaad_b200 import ops, workloads
@@ -301,12 +303,19 @@ def decode_points(dev, steps: int, warmup: int, flush: torch.Tensor, hbm_gbs: fl
                         layers[i].forward(xs[i], ys[i])
 
         nbytes = sum(s.weight_bytes(2) + 2 * T * (s.in_features + s.out_features) for s in specs)
+        single = ops.decode_supported(layers, xs)
         ms = graph_ms(lambda: lset.forward(xs, ys), dev, steps, warmup, flush)
         ms_chain = graph_ms(chained, dev, steps, warmup, flush)
+        with ops.single_launch_decode(False):
+            ms_two = graph_ms(lambda: lset.forward(xs, ys), dev, steps, warmup, flush)
         gbs, gbs_chain = nbytes / (ms / 1e3) / 1e9, nbytes / (ms_chain / 1e3) / 1e9
         out[name] = {"ms_per_step": ms, "tokens_per_s": T / (ms / 1e3), "algorithmic_bytes": nbytes,
-                     "achieved_gbs": gbs, "frac": gbs / hbm_gbs, "launches": multi_launches(specs),
-                     "model_order": {"ms_per_step": ms_chain, "achieved_gbs": gbs_chain, "frac": gbs_chain / hbm_gbs}}
+                     "achieved_gbs": gbs, "frac": gbs / hbm_gbs,
+                     "launches": 1 if single else multi_launches(specs),
+                     "model_order": {"ms_per_step": ms_chain, "achieved_gbs": gbs_chain, "frac": gbs_chain / hbm_gbs,
+                                     "launches": len(members) if single else None},
+                     "two_launch_path": {"ms_per_step": ms_two, "frac": nbytes / (ms_two / 1e3) / 1e9 / hbm_gbs,
+                                         "launches": multi_launches(specs)}}
         del layers, lset, groups, xs, ys, xin
         torch.cuda.empty_cache()
     return out
@@ -801,7 +810,8 @@ def main() -> None:
     for r, grp in groups.items():  # one x*B^T launch per group
         launches_per_step -= len(members[r]) - 1
     if lset is not None:
-        launches_per_step = multi_launches(specs)
+        xs_set = [xin[roles[i]] for i in range(len(specs))]
+        launches_per_step = 1 if ops.decode_supported(layers, xs_set) else multi_launches(specs)
     if pos is not None:
         launches_per_step += len(specs)  # the wait that ends each projection's call
 

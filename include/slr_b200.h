@@ -36,7 +36,7 @@
 extern "C" {
 #endif
 
-#define SLR_ABI_VERSION 5
+#define SLR_ABI_VERSION 6
 
 #if defined(__GNUC__)
 #define SLR_API __attribute__((visibility("default")))
@@ -289,6 +289,45 @@ SLR_API int slr_lrs_linear_forward_multi(const slr_layer* layers, int n, const v
                            const int64_t* ldx, void* const* y, const int64_t* ldy, int64_t M,
                            void* workspace, size_t workspace_bytes, void* stream);
 
+/* --------------------------------------------- single-launch decode -- */
+
+/* Bytes of the control block of slr_lrs_linear_decode. */
+#define SLR_DECODE_CTRL_BYTES 4096
+/* Largest token count of slr_lrs_linear_decode. */
+#define SLR_DECODE_MAX_TOKENS 32
+
+/*
+ * n (1..8) layers, each with its own input (or a shared one), and 1 ..
+ * SLR_DECODE_MAX_TOKENS tokens in ONE kernel launch: x[i] · B_iᵀ and the
+ * combine phase of every layer run in one persistent kernel (the combine of a
+ * layer waits inside the kernel until that layer's H is written), so a decode
+ * step pays one kernel boundary.  y[i] = x[i] · S_iᵀ + (x[i] · B_iᵀ) · A_iᵀ +
+ * bias_i, x · Bᵀ rounded to the dtype and the rest accumulated in fp32 and
+ * rounded once, as in slr_lrs_linear_forward.  The arithmetic of a layer
+ * depends on its own shape only: the result is the same bit for bit whatever
+ * the other layers of the call and whatever M <= SLR_DECODE_MAX_TOKENS for the
+ * same token rows (it is not bit-identical to the two-launch path of
+ * slr_lrs_linear_forward, which splits K differently).
+ *
+ * Handled (slr_lrs_linear_decode_supported): 16-bit dtypes, one dtype for all
+ * layers; rank a multiple of 16 up to 512; in_features and ldx multiples of
+ * 8; block_p and block_q 16, 32 or 64; x, A, B and values 16-byte aligned.
+ * ctrl: SLR_DECODE_CTRL_BYTES of device memory, 16-byte aligned, all zero
+ * before the first call that uses it; every call leaves it zero again (also
+ * a call that reports SLR_ERR_TIMEOUT).  Calls that may run at the same time
+ * on the GPU need separate control blocks.  The workspace (size from
+ * slr_lrs_linear_decode_workspace_size) needs no initialisation.  ldx / ldy
+ * may be NULL (packed rows).  No reference counterpart (the reference runs
+ * two F.linear calls, the sparse operator and the bias add per layer,
+ * ssalaad/efficient/ls_linear.py:124-137).
+ */
+SLR_API int slr_lrs_linear_decode_supported(const slr_layer* layers, int n, const void* const* x,
+                           const int64_t* ldx, int64_t M);
+SLR_API size_t slr_lrs_linear_decode_workspace_size(const slr_layer* layers, int n, int64_t M);
+SLR_API int slr_lrs_linear_decode(const slr_layer* layers, int n, const void* const* x,
+                           const int64_t* ldx, void* const* y, const int64_t* ldy, int64_t M,
+                           void* workspace, size_t workspace_bytes, void* ctrl, void* stream);
+
 /* ------------------------------------------- N:M 2:4 + low-rank layer -- */
 
 /*
@@ -443,9 +482,10 @@ SLR_API int slr_plan_shards(const int32_t* crow_host, int64_t NB, int64_t block_
 #define SLR_SIGNAL_WORDS 32
 
 /* Limit, in ns, of every later wait on other ranks (the peer epilogue and
- * slr_peers_wait), process-wide; 0 restores the default of 2 s.  Waits inside
- * one kernel (its own pipeline) keep their fixed 2 s limit.  No reference
- * counterpart. */
+ * slr_peers_wait) and of the decode kernel's wait for H written by its other
+ * CTAs (there at most 1 s), process-wide; 0 restores the default of 2 s.
+ * Waits inside one CTA (its own pipeline) keep their fixed 2 s limit.  No
+ * reference counterpart. */
 SLR_API int slr_set_wait_limit_ns(uint64_t ns);
 
 typedef struct slr_peers {

@@ -13,7 +13,7 @@ from pathlib import Path
 LIB_PATH = Path(__file__).resolve().parent / "libslr_b200.so"
 
 # slr_status codes (include/slr_b200.h)
-ABI_VERSION = 5  # SLR_ABI_VERSION of include/slr_b200.h
+ABI_VERSION = 6  # SLR_ABI_VERSION of include/slr_b200.h
 SLR_OK = 0
 # slr_layer.flags bits (include/slr_b200.h)
 SLR_FLAG_PAIR_MMA = 1
@@ -61,6 +61,9 @@ EXPORTED = (
     "slr_set_wait_limit_ns",
     "slr_lrs_linear_multi_workspace_size",
     "slr_lrs_linear_forward_multi",
+    "slr_lrs_linear_decode_supported",
+    "slr_lrs_linear_decode_workspace_size",
+    "slr_lrs_linear_decode",
     "slr_nm_compress",
     "slr_nm_linear_workspace_size",
     "slr_nm_linear_forward",
@@ -69,6 +72,8 @@ EXPORTED = (
 SLR_MAX_RANKS = 8
 SLR_IPC_HANDLE_BYTES = 64
 SLR_SIGNAL_WORDS = 32
+SLR_DECODE_CTRL_BYTES = 4096
+SLR_DECODE_MAX_TOKENS = 32
 
 i64, i32, vp, sz = ctypes.c_int64, ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t
 
@@ -162,6 +167,11 @@ _SIGS = {
     "slr_lrs_linear_multi_workspace_size": ([ctypes.POINTER(SlrLayer), i32, i64], sz),
     "slr_lrs_linear_forward_multi": ([ctypes.POINTER(SlrLayer), i32, ctypes.POINTER(vp), ctypes.POINTER(i64),
                                       ctypes.POINTER(vp), ctypes.POINTER(i64), i64, vp, sz, vp], i32),
+    "slr_lrs_linear_decode_supported": ([ctypes.POINTER(SlrLayer), i32, ctypes.POINTER(vp), ctypes.POINTER(i64),
+                                         i64], i32),
+    "slr_lrs_linear_decode_workspace_size": ([ctypes.POINTER(SlrLayer), i32, i64], sz),
+    "slr_lrs_linear_decode": ([ctypes.POINTER(SlrLayer), i32, ctypes.POINTER(vp), ctypes.POINTER(i64),
+                               ctypes.POINTER(vp), ctypes.POINTER(i64), i64, vp, sz, vp, vp], i32),
     "slr_nm_compress": ([vp, i64, i64, i32, vp, vp, vp], i32),
     "slr_nm_linear_workspace_size": ([ctypes.POINTER(SlrNmLayer), i64], sz),
     "slr_nm_linear_forward": ([ctypes.POINTER(SlrNmLayer), vp, i64, vp, i64, i64, vp, sz, vp], i32),

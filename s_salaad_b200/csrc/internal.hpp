@@ -17,6 +17,7 @@ struct RowblockArgs {
   const void* H = nullptr;      // [M, ldh] low-rank intermediate x·Bᵀ (FUSED)
   int64_t ldh = 0;
   const void* A = nullptr;      // [N, r]
+  const void* B = nullptr;      // [r, K] (read by the single-launch decode kernel)
   const void* bias = nullptr;   // [N] or null
   const int32_t* crow = nullptr;  // [NB+1] or null (no sparse term)
   const int32_t* col = nullptr;
@@ -79,6 +80,15 @@ int launch_mma_rowblock(const RowblockArgs& a, bool pdl, cudaStream_t s, bool x_
 bool mma_group_compatible(const RowblockArgs* a, int n, bool shared_x);
 int launch_mma_rowblock_group(const RowblockArgs* a, const int64_t* h_col, int n, const void* H, int64_t ldh,
                               bool pdl, cudaStream_t s, bool x_early = false);
+
+// ---- single-launch decode: x·Bᵀ and the combine of up to kMaxLaunchLayers
+// layers (16-bit, 1..SLR_DECODE_MAX_TOKENS tokens, MODE_FUSED) in one
+// persistent kernel; ctrl is the caller's zeroed control block.
+bool decode_supported(const RowblockArgs* layers, int n, int64_t M);
+size_t decode_workspace_size(const RowblockArgs* layers, int n, int64_t M);
+int launch_decode(const RowblockArgs* layers, int n, int64_t M, void* workspace, size_t workspace_bytes,
+                  unsigned* ctrl, bool pdl, cudaStream_t s);
+int read_and_clear_status_dec(unsigned* out);
 
 // ---- peer memory: a rank's output tiles stored straight into every rank's y.
 // Signal slot of one layer on each rank (SLR_SIGNAL_WORDS x u64, zero at start).

@@ -216,6 +216,9 @@ int slr_device_status(int* status_out) {
   rc = read_and_clear_status_peer(&w);
   if (rc) return rc;
   v |= w;
+  rc = read_and_clear_status_dec(&w);
+  if (rc) return rc;
+  v |= w;
   *status_out = (v & SLR_TIMEOUT_BIT) ? SLR_ERR_TIMEOUT : SLR_OK;
   return SLR_OK;
 }
@@ -333,6 +336,7 @@ int prepare_forward(const slr_layer* layer, const void* x, int64_t ldx, void* y,
   a.H = L.rank > 0 ? c.ws : nullptr;
   a.ldh = c.p.ldh;
   a.A = L.A;
+  a.B = L.B;
   a.bias = L.bias;
   a.crow = L.nnz > 0 ? L.crow : nullptr;
   a.col = L.col;
@@ -1092,6 +1096,67 @@ int slr_plan_shards(const int32_t* crow_host, int64_t NB, int64_t block_p, int64
   }
   bounds[world] = NB;
   return SLR_OK;
+}
+
+}  // extern "C"
+
+namespace {
+
+// Checks and argument packing of the single-launch decode call (inputs
+// optional for the size and support queries).
+int prepare_decode(const slr_layer* layers, int n, const void* const* x, const int64_t* ldx, void* const* y,
+                   const int64_t* ldy, int64_t M, RowblockArgs* as) {
+  if (!layers || n <= 0 || n > kMaxLaunchLayers)
+    return fail(SLR_ERR_INVALID_ARGUMENT, "a decode call holds 1 to " + std::to_string(kMaxLaunchLayers) + " layers");
+  if (M < 0) return fail(SLR_ERR_INVALID_ARGUMENT, "M must be >= 0");
+  for (int i = 0; i < n; ++i) {
+    if (layers[i].dtype != layers[0].dtype)
+      return fail(SLR_ERR_INVALID_ARGUMENT, "the layers of a decode call must share one dtype");
+    FwdCall c;
+    const void* xi = x ? x[i] : nullptr;
+    void* yi = y ? y[i] : nullptr;
+    int rc = prepare_forward(&layers[i], xi, ldx ? ldx[i] : 0, yi, ldy ? ldy[i] : 0, x ? M : 0, nullptr, 0, y != nullptr,
+                             c, false);
+    if (rc) return rc;
+    as[i] = c.a;
+    as[i].M = M;
+  }
+  return SLR_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int slr_lrs_linear_decode_supported(const slr_layer* layers, int n, const void* const* x, const int64_t* ldx,
+                                    int64_t M) {
+  RowblockArgs as[kMaxLaunchLayers];
+  if (prepare_decode(layers, n, x, ldx, nullptr, nullptr, M, as) != SLR_OK) return 0;
+  return decode_supported(as, n, M) ? 1 : 0;
+}
+
+size_t slr_lrs_linear_decode_workspace_size(const slr_layer* layers, int n, int64_t M) {
+  RowblockArgs as[kMaxLaunchLayers];
+  if (prepare_decode(layers, n, nullptr, nullptr, nullptr, nullptr, M, as) != SLR_OK) return 0;
+  return decode_workspace_size(as, n, M);
+}
+
+int slr_lrs_linear_decode(const slr_layer* layers, int n, const void* const* x, const int64_t* ldx, void* const* y,
+                          const int64_t* ldy, int64_t M, void* workspace, size_t workspace_bytes, void* ctrl,
+                          void* stream) {
+  if (!x || !y) return fail(SLR_ERR_INVALID_ARGUMENT, "x/y is NULL");
+  RowblockArgs as[kMaxLaunchLayers];
+  int rc = prepare_decode(layers, n, x, ldx, y, ldy, M, as);
+  if (rc || M == 0) return rc;
+  if (!decode_supported(as, n, M))
+    return fail(SLR_ERR_UNSUPPORTED, "decode: layer set outside the single-launch path "
+                                     "(16-bit, rank % 16 == 0 and <= 512, blocks 16/32/64, M <= 32, aligned inputs)");
+  if (workspace && (reinterpret_cast<uintptr_t>(workspace) & 255u))
+    return fail(SLR_ERR_WORKSPACE, "workspace must be 256-byte aligned");
+  bool pdl = true;
+  for (int i = 0; i < n; ++i) pdl = pdl && early_start(layers[i]);
+  return launch_decode(as, n, M, workspace, workspace_bytes, static_cast<unsigned*>(ctrl), pdl,
+                       static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

@@ -7,12 +7,15 @@
   ``y = x @ S.T + (x @ B.T) @ A.T + bias`` (reference:
   ssalaad/efficient/ls_linear.py:124-137); :class:`LayerGroup` for layers
   that read one input, :class:`LayerSet` for independent layers side by side.
+  From 1 to 32 tokens all three run the single-launch decode kernel
+  (``slr_lrs_linear_decode``); :func:`single_launch_decode` switches it off.
 * :func:`dense_to_bsr_cuda` — bit-exact GPU ``dense_to_bsr``
   (reference: ssalaad/efficient/artifact.py:20-37).
 * :func:`plan_row_order`, :func:`plan_shards` — host planning helpers.
 """
 from __future__ import annotations
 
+import contextlib
 import ctypes
 
 import numpy as np
@@ -121,6 +124,81 @@ def validate_bsr(crow, col, nbk: int, active_rows) -> None:
 
 # ------------------------------------------------------------ S+LR layer --
 
+# ------------------------------------------------------- decode path --
+
+_single_launch = True
+
+
+@contextlib.contextmanager
+def single_launch_decode(enabled: bool):
+    """Within the block, calls of 1..32 tokens take (enabled) or skip the
+    single-launch decode kernel; skipped, they run x·Bᵀ and the combine as two
+    launches (``slr_lrs_linear_forward`` and its group / multi forms)."""
+    global _single_launch
+    prev, _single_launch = _single_launch, bool(enabled)
+    try:
+        yield
+    finally:
+        _single_launch = prev
+
+
+def decode_supported(descs: list["LayerDesc"], xs: list[torch.Tensor]) -> bool:
+    """Whether these layers on these inputs (1..32 rows) run on the
+    single-launch decode kernel."""
+    n = len(descs)
+    arr = (_lib.SlrLayer * n)(*[d.struct for d in descs])
+    xp = (ctypes.c_void_p * n)(*[x.data_ptr() for x in xs])
+    lx = (ctypes.c_int64 * n)(*[LayerDesc._ld(x) for x in xs])
+    return _single_launch and bool(_lib.load().slr_lrs_linear_decode_supported(arr, n, xp, lx, xs[0].shape[0]))
+
+
+class _DecodeState:
+    """Control block (zeroed once; each call leaves it zero) and workspace of
+    ``slr_lrs_linear_decode`` for one owner of descriptors.  An owner's calls
+    must not run on two streams at once (they share the control block)."""
+
+    __slots__ = ("ctrl", "ws", "ok", "sizes")
+
+    def __init__(self):
+        self.ctrl: torch.Tensor | None = None
+        self.ws: torch.Tensor | None = None
+        self.ok: dict = {}
+        self.sizes: dict = {}
+
+    def run(self, arr, blob: bytes, n: int, xs: list[torch.Tensor], ys: list[torch.Tensor], M: int,
+            device: torch.device) -> bool:
+        """Runs the call on the decode kernel if it qualifies; False if not."""
+        if not _single_launch or not 1 <= M <= _lib.SLR_DECODE_MAX_TOKENS:
+            return False
+        lib = _lib.load()
+        xp = (ctypes.c_void_p * n)(*[x.data_ptr() for x in xs])
+        lx = (ctypes.c_int64 * n)(*[LayerDesc._ld(x) for x in xs])
+        key = (blob, M, tuple(x.data_ptr() % 16 for x in xs), tuple(lx))
+        ok = self.ok.get(key)
+        if ok is None:
+            if len(self.ok) > 256:
+                self.ok.clear()
+            ok = self.ok[key] = bool(lib.slr_lrs_linear_decode_supported(arr, n, xp, lx, M))
+        if not ok:
+            return False
+        need = self.sizes.get((blob, M))
+        if need is None:
+            if len(self.sizes) > 256:
+                self.sizes.clear()
+            need = self.sizes[(blob, M)] = int(lib.slr_lrs_linear_decode_workspace_size(arr, n, M))
+        if self.ctrl is None or self.ctrl.device != device:
+            self.ctrl = torch.zeros(_lib.SLR_DECODE_CTRL_BYTES // 4, dtype=torch.int32, device=device)
+        if need and (self.ws is None or self.ws.numel() < need or self.ws.device != device):
+            self.ws = torch.empty(need, dtype=torch.uint8, device=device)
+        yp = (ctypes.c_void_p * n)(*[y.data_ptr() for y in ys])
+        ly = (ctypes.c_int64 * n)(*[LayerDesc._ld(y) for y in ys])
+        with _DeviceGuard(device):
+            rc = lib.slr_lrs_linear_decode(arr, n, xp, lx, yp, ly, M, None if not need else self.ws.data_ptr(),
+                                           need, self.ctrl.data_ptr(), _stream(device))
+        _lib.check(rc, "lrs_linear_decode")
+        return True
+
+
 class LayerDesc:
     """Owns an ``slr_layer`` descriptor plus the layer's workspace.
 
@@ -144,6 +222,7 @@ class LayerDesc:
         self._ws_sizes: dict = {}
         self._plan_key = None
         self._plan = None
+        self._decode = _DecodeState()
         self.refresh()
 
     def refresh(self, **tensors) -> None:
@@ -214,6 +293,8 @@ class LayerDesc:
         M = x2.shape[0]
         if out is None:
             out = torch.empty(M, self.out_features, dtype=self.dtype, device=self.device)
+        if self._decode.run(ctypes.byref(self.struct), bytes(self.struct), 1, [x2], [out], M, self.device):
+            return out
         ws = self.workspace(M)
         with _DeviceGuard(self.device):
             rc = lib.slr_lrs_linear_forward(
@@ -264,6 +345,7 @@ class LayerGroup:
         self.device = descs[0].device
         self.dtype = descs[0].dtype
         self._ws: torch.Tensor | None = None
+        self._decode = _DecodeState()
 
     def _structs(self):
         """The members' descriptors as one C array (rebuilt when one changes)."""
@@ -290,6 +372,9 @@ class LayerGroup:
         n = len(self.descs)
         if outs is None:
             outs = [torch.empty(M, d.out_features, dtype=self.dtype, device=self.device) for d in self.descs]
+        arr = self._structs()
+        if self._decode.run(arr, self._blob, n, [x2] * n, outs, M, self.device):
+            return outs
         ws = self.workspace(M)
         ys = (ctypes.c_void_p * n)(*[o.data_ptr() for o in outs])
         lds = (ctypes.c_int64 * n)(*[LayerDesc._ld(o) for o in outs])
@@ -367,7 +452,8 @@ class LayerGroup:
 class LayerSet:
     """Independent layers run side by side, each on its own input (one
     ``slr_lrs_linear_forward_multi`` call): ``forward(xs)`` returns what
-    :meth:`LayerDesc.forward` gives for each layer, bit for bit.  Below 128
+    :meth:`LayerDesc.forward` gives for each layer, bit for bit.  From 1 to
+    32 tokens the whole set is one launch of the decode kernel; up to 127
     tokens every layer's ``x · Bᵀ`` is one launch and the combine phases one
     more (two launches for the whole set instead of two per layer)."""
 
@@ -380,6 +466,7 @@ class LayerSet:
         self.device = descs[0].device
         self.dtype = descs[0].dtype
         self._ws: torch.Tensor | None = None
+        self._decode = _DecodeState()
 
     def _structs(self):
         """The members' descriptors as one C array (rebuilt when one changes)."""
@@ -410,6 +497,9 @@ class LayerSet:
             raise ValueError("every input of a layer set has the same number of rows")
         if outs is None:
             outs = [torch.empty(M, d.out_features, dtype=self.dtype, device=self.device) for d in self.descs]
+        arr = self._structs()
+        if self._decode.run(arr, self._blob, n, xs, outs, M, self.device):
+            return outs
         ws = self.workspace(M)
         xp = (ctypes.c_void_p * n)(*[x.data_ptr() for x in xs])
         lx = (ctypes.c_int64 * n)(*[LayerDesc._ld(x) for x in xs])

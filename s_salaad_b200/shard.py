@@ -155,8 +155,12 @@ class ShardedLayer(ShardPlan):
         T = x2.shape[0]
         buf = self.local_buffer(T)
         if self.desc is not None:
-            self._lowrank(x2)
-            self.desc.combine(x2, buf[self.rank][:, :self.width])
+            if T <= _lib.SLR_DECODE_MAX_TOKENS:
+                # decode sizes: the single-launch kernel when it applies (as the whole layer's forward)
+                self.desc.forward(x2, buf[self.rank][:, :self.width])
+            else:
+                self._lowrank(x2)
+                self.desc.combine(x2, buf[self.rank][:, :self.width])
         work = None
         if self.world > 1:
             work = dist.all_gather_into_tensor(buf.view(-1), buf[self.rank].view(-1), group=self.group,
