@@ -81,6 +81,15 @@ USE_PEERS = os.environ.get("SLR_BENCH_PEERS", "1") != "0"
 L2_FLUSH_BYTES = 256 << 20  # > 126 MB L2
 
 
+def flush_l2(buf: torch.Tensor) -> None:
+    """Evict L2 between timed steps: write a buffer twice the L2 size, then
+    read it back, so every line the write left dirty is written back before
+    the next step (a write alone leaves ~126 MB of dirty lines whose
+    write-back would compete with the step's reads)."""
+    buf.zero_()
+    buf.sum(dtype=torch.int32)
+
+
 # ------------------------------------------------------------ workloads --
 
 def parse_workload(name: str) -> tuple[str, int]:
@@ -250,7 +259,7 @@ def graph_ms(fn, dev, steps: int, warmup: int, flush: torch.Tensor) -> float:
     mk = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
     ev = [(mk(), mk()) for _ in range(steps)]
     for a, b in ev:
-        flush.zero_()
+        flush_l2(flush)
         a.record(cur)
         graph.replay()
         b.record(cur)
@@ -261,11 +270,11 @@ def graph_ms(fn, dev, steps: int, warmup: int, flush: torch.Tensor) -> float:
 def decode_points(dev, steps: int, warmup: int, flush: torch.Tensor, hbm_gbs: float) -> dict:
     """The decode-sized workloads (HBM-bound) on one GPU, each as
     * the whole projection set as one call (the inputs are independent in the
-      layer set): one launch of the single-launch decode kernel;
+      layer set): x·Bᵀ of every layer in one launch, the combines in another;
     * `model_order`: per input group, in decoder order (q/k/v grouped, o,
-      gate/up grouped, down), as a model that chains them would call them
-      (one launch per group);
-    * `two_launch_path`: the set as one call on the x·Bᵀ + combine kernels.
+      gate/up grouped, down), as a model that chains them would call them;
+    * `single_launch_kernel`: both again on the opt-in single-launch decode
+      kernel (x·Bᵀ and the combine of a call in one launch).
     Algorithmic bytes: weights and indices of every projection plus x and y
     (2 bytes per element); frac = achieved / measured HBM peak."""
     from s_salaad_b200 import ops, workloads
@@ -303,19 +312,22 @@ def decode_points(dev, steps: int, warmup: int, flush: torch.Tensor, hbm_gbs: fl
                         layers[i].forward(xs[i], ys[i])
 
         nbytes = sum(s.weight_bytes(2) + 2 * T * (s.in_features + s.out_features) for s in specs)
-        single = ops.decode_supported(layers, xs)
         ms = graph_ms(lambda: lset.forward(xs, ys), dev, steps, warmup, flush)
         ms_chain = graph_ms(chained, dev, steps, warmup, flush)
-        with ops.single_launch_decode(False):
-            ms_two = graph_ms(lambda: lset.forward(xs, ys), dev, steps, warmup, flush)
+        single = None
+        if ops.decode_supported(layers, xs):
+            with ops.single_launch_decode(True):
+                ms_one = graph_ms(lambda: lset.forward(xs, ys), dev, steps, warmup, flush)
+                ms_one_chain = graph_ms(chained, dev, steps, warmup, flush)
+            single = {"ms_per_step": ms_one, "frac": nbytes / (ms_one / 1e3) / 1e9 / hbm_gbs, "launches": 1,
+                      "model_order": {"ms_per_step": ms_one_chain,
+                                      "frac": nbytes / (ms_one_chain / 1e3) / 1e9 / hbm_gbs,
+                                      "launches": len(members)}}
         gbs, gbs_chain = nbytes / (ms / 1e3) / 1e9, nbytes / (ms_chain / 1e3) / 1e9
         out[name] = {"ms_per_step": ms, "tokens_per_s": T / (ms / 1e3), "algorithmic_bytes": nbytes,
-                     "achieved_gbs": gbs, "frac": gbs / hbm_gbs,
-                     "launches": 1 if single else multi_launches(specs),
-                     "model_order": {"ms_per_step": ms_chain, "achieved_gbs": gbs_chain, "frac": gbs_chain / hbm_gbs,
-                                     "launches": len(members) if single else None},
-                     "two_launch_path": {"ms_per_step": ms_two, "frac": nbytes / (ms_two / 1e3) / 1e9 / hbm_gbs,
-                                         "launches": multi_launches(specs)}}
+                     "achieved_gbs": gbs, "frac": gbs / hbm_gbs, "launches": multi_launches(specs),
+                     "model_order": {"ms_per_step": ms_chain, "achieved_gbs": gbs_chain, "frac": gbs_chain / hbm_gbs},
+                     "single_launch_kernel": single}
         del layers, lset, groups, xs, ys, xin
         torch.cuda.empty_cache()
     return out
@@ -440,7 +452,7 @@ def model_bench(args) -> None:
             torch.cuda.synchronize()
             ev = [(mk(), mk()) for _ in range(args.steps)]
             for a, b in ev:
-                flush.zero_()
+                flush_l2(flush)
                 a.record()
                 graph.replay()
                 b.record()
@@ -457,7 +469,7 @@ def model_bench(args) -> None:
           "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded bundle; random ids)",
           "config": {"workload": "cfg2-model: 8 decoder layers, 56 S+LR projections (16x16 blocks, 50 %, r 64), "
                                  "batch 8 x seq 256, forward replayed from a CUDA graph",
-                     "l2": "flushed (256 MB write) between timed steps"},
+                     "l2": "flushed between timed steps (256 MB written, then read back)"},
           "dense_bf16": {"ms_per_step": ms_dense, "value": batch * seq / (ms_dense / 1e3),
                          "what": "the same model with dense W = A*B + S (torch/cuBLAS), same graph replay"},
           "generate": gen,
@@ -712,7 +724,7 @@ def main() -> None:
             dist.barrier()
         torch.cuda.synchronize()
         for k in range(K):
-            flush.zero_()  # evict L2 between timed steps (outside the events)
+            flush_l2(flush)  # evict L2 between timed steps (outside the events)
             step_ev[k][0].record(stream)
             if graph is not None:
                 graph.replay()
@@ -730,7 +742,7 @@ def main() -> None:
         # eagerly, with events between the x*B^T and combine launches (these
         # kernels are long enough that the host stays ahead of the GPU).
         for k in range(K):
-            flush.zero_()
+            flush_l2(flush)
             step(kern_ev[k])
         torch.cuda.synchronize()
     if graph is None or T >= 128:
@@ -810,8 +822,7 @@ def main() -> None:
     for r, grp in groups.items():  # one x*B^T launch per group
         launches_per_step -= len(members[r]) - 1
     if lset is not None:
-        xs_set = [xin[roles[i]] for i in range(len(specs))]
-        launches_per_step = 1 if ops.decode_supported(layers, xs_set) else multi_launches(specs)
+        launches_per_step = multi_launches(specs)
     if pos is not None:
         launches_per_step += len(specs)  # the wait that ends each projection's call
 
@@ -910,7 +921,7 @@ def main() -> None:
         torch.cuda.synchronize()
         e2e_ev = [(mk(), mk()) for _ in range(K)]
         for k in range(K):
-            flush.zero_()
+            flush_l2(flush)
             e2e_ev[k][0].record(stream)
             e2e_step()
             e2e_ev[k][1].record(stream)
@@ -940,7 +951,7 @@ def main() -> None:
         torch.cuda.synchronize()
         dev_ev = [(mk(), mk()) for _ in range(K)]
         for k in range(K):
-            flush.zero_()
+            flush_l2(flush)
             dev_ev[k][0].record(stream)
             for i in range(len(specs)):
                 torch.matmul(xs[i], Ws[i].T, out=ys[i]) if biases[i] is None else fl(xs[i], Ws[i], biases[i])
@@ -975,7 +986,7 @@ def main() -> None:
                 "warmup": args.warmup, "ms_per_step": total_ms / K, "higher_is_better": True,
                 "scaling": "strong", "vs_baseline": None, "dtype": "bf16" if dtype == torch.bfloat16 else "f32",
                 "data": "synthetic (seeded generators; random-init weights; no dataset)",
-                "config": {**config, "l2": "flushed (256 MB write) between timed steps",
+                "config": {**config, "l2": "flushed between timed steps (256 MB written, then read back)",
                            "parallelism": (f"block-row shards x{world}, x*B^T "
                                            + ("split by tokens + NCCL all-gather of H" if world >= 4 else "on every rank")
                                            + (", combine epilogues store y into every rank's y over NVLink (CUDA IPC)"

@@ -299,9 +299,14 @@ SLR_API int slr_lrs_linear_forward_multi(const slr_layer* layers, int n, const v
 /*
  * n (1..8) layers, each with its own input (or a shared one), and 1 ..
  * SLR_DECODE_MAX_TOKENS tokens in ONE kernel launch: x[i] · B_iᵀ and the
- * combine phase of every layer run in one persistent kernel (the combine of a
- * layer waits inside the kernel until that layer's H is written), so a decode
- * step pays one kernel boundary.  y[i] = x[i] · S_iᵀ + (x[i] · B_iᵀ) · A_iᵀ +
+ * combine phase of every layer run in one kernel (each CTA computes a tile
+ * of some layer's H and one block-row of some layer's y; a block-row waits
+ * inside the kernel until its layer's H is written), so a decode step pays
+ * one kernel boundary.  An alternative to the two-launch small-batch path
+ * of slr_lrs_linear_forward / _forward_multi, not a replacement: measured on
+ * B200 it is faster only for large layer sets (seven LLaMA-1B-shaped
+ * projections at one token: 36 µs against 38 µs) and slower for single
+ * layers and small layer sets.  y[i] = x[i] · S_iᵀ + (x[i] · B_iᵀ) · A_iᵀ +
  * bias_i, x · Bᵀ rounded to the dtype and the rest accumulated in fp32 and
  * rounded once, as in slr_lrs_linear_forward.  The arithmetic of a layer
  * depends on its own shape only: the result is the same bit for bit whatever

@@ -7,11 +7,8 @@
   ``y = x @ S.T + (x @ B.T) @ A.T + bias`` (reference:
   ssalaad/efficient/ls_linear.py:124-137); :class:`LayerGroup` for layers
   that read one input, :class:`LayerSet` for independent layers side by side.
-  From 1 to 32 tokens all three run the single-launch decode kernel
-  (``slr_lrs_linear_decode``); :func:`single_launch_decode` switches it off.
-* :func:`dense_to_bsr_cuda` — bit-exact GPU ``dense_to_bsr``
-  (reference: ssalaad/efficient/artifact.py:20-37).
-* :func:`plan_row_order`, :func:`plan_shards` — host planning helpers.
+  Within :func:`single_launch_decode` (off by default), calls of 1 to 32
+  tokens run the single-launch decode kernel (``slr_lrs_linear_decode``).
 """
 from __future__ import annotations
 
@@ -126,14 +123,17 @@ def validate_bsr(crow, col, nbk: int, active_rows) -> None:
 
 # ------------------------------------------------------- decode path --
 
-_single_launch = True
+# Off by default: on B200 the two-launch path (x·Bᵀ, then the combine as a
+# programmatic dependent) is as fast or faster except for large layer sets.
+_single_launch = False
 
 
 @contextlib.contextmanager
 def single_launch_decode(enabled: bool):
     """Within the block, calls of 1..32 tokens take (enabled) or skip the
-    single-launch decode kernel; skipped, they run x·Bᵀ and the combine as two
-    launches (``slr_lrs_linear_forward`` and its group / multi forms)."""
+    single-launch decode kernel; skipped (the default), they run x·Bᵀ and the
+    combine as two launches (``slr_lrs_linear_forward`` and its group / multi
+    forms)."""
     global _single_launch
     prev, _single_launch = _single_launch, bool(enabled)
     try:
@@ -143,13 +143,13 @@ def single_launch_decode(enabled: bool):
 
 
 def decode_supported(descs: list["LayerDesc"], xs: list[torch.Tensor]) -> bool:
-    """Whether these layers on these inputs (1..32 rows) run on the
-    single-launch decode kernel."""
+    """Whether these layers on these inputs (1..32 rows) can run on the
+    single-launch decode kernel (it does so within single_launch_decode(True))."""
     n = len(descs)
     arr = (_lib.SlrLayer * n)(*[d.struct for d in descs])
     xp = (ctypes.c_void_p * n)(*[x.data_ptr() for x in xs])
     lx = (ctypes.c_int64 * n)(*[LayerDesc._ld(x) for x in xs])
-    return _single_launch and bool(_lib.load().slr_lrs_linear_decode_supported(arr, n, xp, lx, xs[0].shape[0]))
+    return bool(_lib.load().slr_lrs_linear_decode_supported(arr, n, xp, lx, xs[0].shape[0]))
 
 
 class _DecodeState:
@@ -452,8 +452,7 @@ class LayerGroup:
 class LayerSet:
     """Independent layers run side by side, each on its own input (one
     ``slr_lrs_linear_forward_multi`` call): ``forward(xs)`` returns what
-    :meth:`LayerDesc.forward` gives for each layer, bit for bit.  From 1 to
-    32 tokens the whole set is one launch of the decode kernel; up to 127
+    :meth:`LayerDesc.forward` gives for each layer, bit for bit.  Up to 127
     tokens every layer's ``x · Bᵀ`` is one launch and the combine phases one
     more (two launches for the whole set instead of two per layer)."""
 

@@ -21,6 +21,14 @@ from test_gpu_parity import assert_16bit_close, desc_for, oracle_layer, random_l
 
 pytestmark = pytest.mark.gpu
 
+
+@pytest.fixture(autouse=True)
+def _single_launch():
+    """The library's calls of 1..32 tokens take the single-launch kernel
+    (opt-in; the two-launch path is the default)."""
+    with ops.single_launch_decode(True):
+        yield
+
 SHAPES = [
     # n, k, bp, bq, r, density: K below and above one 1024-wide H chunk, every block size
     (256, 512, 16, 16, 32, 0.3),

@@ -366,11 +366,16 @@ def test_group_forward_equals_per_layer(cuda, group, T):
     x = workloads.tokens(T, specs[0].in_features, seed=T + 5, dtype=torch.bfloat16).to(cuda)
     grp = ops.LayerGroup(descs)
     ys = grp.forward(x)
-    grp.lowrank(x)
-    for i, (d, y) in enumerate(zip(descs, ys)):
-        ref = d.forward(x)
-        assert torch.equal(y, ref)
-        assert torch.equal(grp.combine(i, x, torch.empty_like(ref)), ref)
+    for d, y in zip(descs, ys):
+        assert torch.equal(y, d.forward(x))
+    # the two phases against the forward that runs them as two launches
+    with ops.single_launch_decode(False):
+        ys2 = grp.forward(x)
+        grp.lowrank(x)
+        for i, (d, y) in enumerate(zip(descs, ys2)):
+            ref = d.forward(x)
+            assert torch.equal(y, ref)
+            assert torch.equal(grp.combine(i, x, torch.empty_like(ref)), ref)
     if T < 128:
         # calls alternating between the per-layer layout (x rows not 16-byte
         # aligned: SIMT path) and the grouped one on one workspace
