@@ -71,7 +71,7 @@ METRIC = "S+LR linear tokens/s + %HBM/TC roofline at 1/2/4/8 B200 vs AVX2 CPU & 
 # `--metrics dram__bytes_read.sum,dram__bytes_write.sum,gpu__time_duration.sum`:
 # cfg4 = mean over the 7 combine launches of one step; cfg3-T1 = the whole
 # layer set of one step (its roofline covers the graph-replayed layer set).
-NCU_TRAFFIC = {"cfg4": 101094327.0, "cfg3-T1": 50881280.0}
+NCU_TRAFFIC = {"cfg3-T1": 50881280.0}
 # SMs kept free of the persistent kernels at N > 1 (for the overlapping NCCL
 # all-gathers); SLR_BENCH_NCCL_SMS overrides it.
 SMS_FOR_NCCL = int(os.environ.get("SLR_BENCH_NCCL_SMS", "16"))
@@ -595,9 +595,11 @@ def main() -> None:
         _lib.load().slr_set_sm_limit(_lib.load_sm_count() - SMS_FOR_NCCL)
     ys = ([po.y for po in pos] if pos is not None else
           [torch.empty(T, s.out_features, dtype=dtype, device=dev) for s in specs])
-    # one GPU, decode-sized batch: the projections (independent inputs) run as
-    # one slr_lrs_linear_forward_multi call
-    lset = ops.LayerSet(layers) if (world == 1 and T < 128 and dtype != torch.float32) else None
+    # one GPU: the projections (independent inputs) run as one layer-set call
+    # (slr_lrs_linear_forward_multi): below 128 tokens x*B^T of all of them in
+    # one launch and the combines in another; from 128 tokens x*B^T per
+    # projection and, on the pair kernel, the combines of all in one launch
+    lset = ops.LayerSet(layers) if (world == 1 and dtype != torch.float32) else None
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
 
@@ -661,10 +663,22 @@ def main() -> None:
                 else:
                     L.finish(handles[i], ys[i])
             return
-        if lset is not None and ev is None:
-            # decode-sized batch: every projection in one multi-input call (2 launches)
-            lset.forward(xs, ys)
+        if lset is not None:
+            if ev is None:
+                lset.forward(xs, ys)
+            else:
+                # the set's two phases, charged to its first projection
+                ev[0][0].record(stream)
+                lset.lowrank(xs)
+                ev[0][1].record(stream)
+                lset.combine(xs, ys)
+                ev[0][2].record(stream)
             return
+        step_roles(ev)
+
+    def step_roles(ev=None):
+        """One GPU: the projections per input, in a decoder's order (q/k/v
+        grouped, o, gate/up grouped, down), as a model issues them."""
         for r, idx in members.items():
             grp = groups.get(r)
             if grp is None:
@@ -745,7 +759,10 @@ def main() -> None:
             flush_l2(flush)
             step(kern_ev[k])
         torch.cuda.synchronize()
-    if graph is None or T >= 128:
+    if lset is not None and T >= 128:
+        h_ms = [sum(kern_ev[k][0][0].elapsed_time(kern_ev[k][0][1]) for k in range(K))] + [0.0] * (len(specs) - 1)
+        c_ms = [sum(kern_ev[k][0][1].elapsed_time(kern_ev[k][0][2]) for k in range(K))] + [0.0] * (len(specs) - 1)
+    elif graph is None or T >= 128:
         h_ms = [sum(kern_ev[k][i][0].elapsed_time(kern_ev[k][i][1]) for k in range(K)) if has_local[i] else 0.0
                 for i in range(len(specs))]
         c_ms = [sum(kern_ev[k][i][1].elapsed_time(kern_ev[k][i][2]) for k in range(K)) if has_local[i] else 0.0
@@ -757,6 +774,13 @@ def main() -> None:
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     total_ms, comb_ms_max, low_ms_max = t.tolist()
+
+    # combine launches of the layer-set call: one when every projection takes the
+    # pair kernel (2-SM, block_p 32/64, 256+ tokens, column schedule, enough items)
+    pair_set = lset is not None and T >= 256 and all(
+        s.nnz > 0 and s.block_p in (32, 64)
+        and -(-s.out_features // s.block_p // (256 // s.block_p)) * -(-T // 128) >= 16 for s in specs)
+    comb_launches = 1 if pair_set else len(specs)
 
     # ------------------------------------------------- roofline (combine)
     P, pk_src = peaks()
@@ -790,7 +814,9 @@ def main() -> None:
         achieved = comb_flops * K / comb_s / 1e12
         peak = P["bf16_tflops"]
         roof = {"bound": "tensor", "unit": "TFLOP/s", "algorithmic_per_step": comb_flops,
-                "kernel": "combine (sparse + H*A^T + bias; one launch per projection)"}
+                "kernel": ("combine (sparse + H*A^T + bias) of all projections of the set"
+                           + (" in one launch of the 2-SM pair kernel" if pair_set else ", one launch each")
+                           if lset is not None else "combine (sparse + H*A^T + bias; one launch per projection)")}
     else:
         achieved = comb_bytes * K / comb_s / 1e9
         peak = P["hbm_gbs"]
@@ -802,8 +828,8 @@ def main() -> None:
         roof["step_tflops"] = (comb_flops + low_flops) * K / (total_ms / 1e3) / 1e12
     roof.update({"achieved": achieved, "peak": peak, "peak_source": pk_src,
                  "frac": achieved / peak, "traffic": traffic,
-                 "launch_ms_mean": sum(c_ms) / (K * len(specs)),
-                 "lowrank_kernel_ms_mean": sum(h_ms) / (K * len(specs)),
+                 "combine_ms_per_step": sum(c_ms) / K, "combine_launches_per_step": comb_launches,
+                 "lowrank_ms_per_step": sum(h_ms) / K,
                  "lowrank_tflops": low_flops * K / (sum(h_ms) / 1e3) / 1e12 if sum(h_ms) else None})
 
     value = T * K / (total_ms / 1e3)
@@ -822,7 +848,7 @@ def main() -> None:
     for r, grp in groups.items():  # one x*B^T launch per group
         launches_per_step -= len(members[r]) - 1
     if lset is not None:
-        launches_per_step = multi_launches(specs)
+        launches_per_step = multi_launches(specs) if T < 128 else len(members) + comb_launches
     if pos is not None:
         launches_per_step += len(specs)  # the wait that ends each projection's call
 
@@ -964,6 +990,14 @@ def main() -> None:
                   "W = A*B + S in bf16, same shapes and inputs"}
         del Ws
 
+    # ------------------------------------- the same step in model order (N=1)
+    model_order = None
+    if world == 1 and lset is not None and T >= 128:
+        mo_ms = graph_ms(step_roles, dev, K, args.warmup, flush)
+        model_order = {"ms_per_step": mo_ms, "tokens_per_s": T / (mo_ms / 1e3),
+                       "what": "the projections per input in a decoder's order (q/k/v grouped, o, gate/up grouped, "
+                               "down), graph-replayed, L2 flushed between steps"}
+
     # ------------------------------------------- decode points (N=1 headline)
     decode = None
     nm24 = None
@@ -992,12 +1026,15 @@ def main() -> None:
                                            + (", combine epilogues store y into every rank's y over NVLink (CUDA IPC)"
                                               if pos is not None else ", NCCL all-gather of y")
                                            + ", step replayed from a CUDA graph")
-                           if world > 1 else "1 GPU, step replayed from a CUDA graph",
+                           if world > 1 else ("1 GPU, the projections (independent inputs) as one layer-set call, "
+                                              "step replayed from a CUDA graph"),
                            "algorithmic_tflop_per_step": all_flops / 1e12},
                 "roofline": roof, "e2e": {"value": e2e_val, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                                           "d2h_bytes_per_step": d2h},
                 "gpu_launches": launches_per_step * K, "clocks": clocks.summary(),
                 "cpu_baseline": cpu, "cublas_dense": cublas}
+        if model_order is not None:
+            line["model_order"] = model_order
         if nm24 is not None:
             line["nm24"] = nm24
         if decode is not None:

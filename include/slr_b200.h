@@ -36,7 +36,7 @@
 extern "C" {
 #endif
 
-#define SLR_ABI_VERSION 6
+#define SLR_ABI_VERSION 7
 
 #if defined(__GNUC__)
 #define SLR_API __attribute__((visibility("default")))
@@ -260,7 +260,9 @@ SLR_API int slr_lrs_linear_forward_group(const slr_layer* layers, int n, const v
                            void* workspace, size_t workspace_bytes, void* stream);
 /* The two phases of slr_lrs_linear_forward_group, like _lowrank / _combine
  * for one layer: the group's x · B_iᵀ, then layer i's combine (any order of
- * i, same x, M and workspace). */
+ * i, same x, M and workspace).  Within slr_lrs_linear_forward_group, from
+ * 128 tokens on, the combines of layers that all take the 2-SM pair kernel
+ * with one block shape are one launch. */
 SLR_API int slr_lrs_linear_group_lowrank(const slr_layer* layers, int n, const void* x,
                            int64_t ldx, int64_t M, void* workspace,
                            size_t workspace_bytes, void* stream);
@@ -286,6 +288,18 @@ SLR_API int slr_lrs_linear_group_combine(const slr_layer* layers, int n, int i,
  */
 SLR_API size_t slr_lrs_linear_multi_workspace_size(const slr_layer* layers, int n, int64_t M);
 SLR_API int slr_lrs_linear_forward_multi(const slr_layer* layers, int n, const void* const* x,
+                           const int64_t* ldx, void* const* y, const int64_t* ldy, int64_t M,
+                           void* workspace, size_t workspace_bytes, void* stream);
+/* The two phases of slr_lrs_linear_forward_multi (same layers, inputs, M and
+ * workspace in both calls): every layer's x[i] · B_iᵀ, then the combines.
+ * From 128 tokens on, when every layer takes the 2-SM pair kernel with one
+ * block shape (layers with a column schedule), the combines of all layers
+ * are ONE launch whose work items are dealt as one list, so the set pays
+ * one persistent-schedule tail; results equal per-layer calls bit for bit. */
+SLR_API int slr_lrs_linear_multi_lowrank(const slr_layer* layers, int n, const void* const* x,
+                           const int64_t* ldx, int64_t M, void* workspace, size_t workspace_bytes,
+                           void* stream);
+SLR_API int slr_lrs_linear_multi_combine(const slr_layer* layers, int n, const void* const* x,
                            const int64_t* ldx, void* const* y, const int64_t* ldy, int64_t M,
                            void* workspace, size_t workspace_bytes, void* stream);
 

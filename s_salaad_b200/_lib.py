@@ -13,7 +13,7 @@ from pathlib import Path
 LIB_PATH = Path(__file__).resolve().parent / "libslr_b200.so"
 
 # slr_status codes (include/slr_b200.h)
-ABI_VERSION = 6  # SLR_ABI_VERSION of include/slr_b200.h
+ABI_VERSION = 7  # SLR_ABI_VERSION of include/slr_b200.h
 SLR_OK = 0
 # slr_layer.flags bits (include/slr_b200.h)
 SLR_FLAG_PAIR_MMA = 1
@@ -61,6 +61,8 @@ EXPORTED = (
     "slr_set_wait_limit_ns",
     "slr_lrs_linear_multi_workspace_size",
     "slr_lrs_linear_forward_multi",
+    "slr_lrs_linear_multi_lowrank",
+    "slr_lrs_linear_multi_combine",
     "slr_lrs_linear_decode_supported",
     "slr_lrs_linear_decode_workspace_size",
     "slr_lrs_linear_decode",
@@ -166,6 +168,10 @@ _SIGS = {
     "slr_set_wait_limit_ns": ([ctypes.c_uint64], i32),
     "slr_lrs_linear_multi_workspace_size": ([ctypes.POINTER(SlrLayer), i32, i64], sz),
     "slr_lrs_linear_forward_multi": ([ctypes.POINTER(SlrLayer), i32, ctypes.POINTER(vp), ctypes.POINTER(i64),
+                                      ctypes.POINTER(vp), ctypes.POINTER(i64), i64, vp, sz, vp], i32),
+    "slr_lrs_linear_multi_lowrank": ([ctypes.POINTER(SlrLayer), i32, ctypes.POINTER(vp), ctypes.POINTER(i64), i64,
+                                      vp, sz, vp], i32),
+    "slr_lrs_linear_multi_combine": ([ctypes.POINTER(SlrLayer), i32, ctypes.POINTER(vp), ctypes.POINTER(i64),
                                       ctypes.POINTER(vp), ctypes.POINTER(i64), i64, vp, sz, vp], i32),
     "slr_lrs_linear_decode_supported": ([ctypes.POINTER(SlrLayer), i32, ctypes.POINTER(vp), ctypes.POINTER(i64),
                                          i64], i32),

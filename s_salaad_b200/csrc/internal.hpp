@@ -142,6 +142,11 @@ int launch_tc_rowblock(const RowblockArgs& a, bool pdl, cudaStream_t s);
 bool tc2_rowblock_supported(const RowblockArgs& a);  // 2-SM pairs, M >= 256, bp 32/64
 // peers: also store every output tile into the other ranks' y (null = local only).
 int launch_tc2_rowblock(const RowblockArgs& a, bool pdl, cudaStream_t s, const PeerArgs* peers = nullptr);
+// Up to kMaxLaunchLayers layers in one launch of the pair kernel (one
+// persistent schedule, one tail): every layer sparse with a column schedule,
+// one block shape, token count, dtype and mode; local y only.
+bool tc2_group_compatible(const RowblockArgs* a, int n);
+int launch_tc2_rowblock_group(const RowblockArgs* a, int n, bool pdl, cudaStream_t s);
 bool tc_dense_supported(const void* x, int64_t ldx, const void* B, int64_t K, int64_t r, int dtype);
 // pdl: may start while the preceding kernel runs (it waits for that kernel
 // before its first load).

@@ -65,6 +65,28 @@ struct YMaps {
   CUtensorMap m[kMaxRanks];
 };
 
+// Several layers in one launch (same block shape, token count and mode):
+// their work items are numbered one layer after the other, item0[l] being
+// layer l's first, and dealt to the pairs as one list, so the launch has one
+// persistent-schedule tail instead of one per layer.
+constexpr int kTc2Layers = kMaxLaunchLayers;
+struct Tc2Set {
+  Tc2Args L[kTc2Layers];
+  int n;
+  int item0[kTc2Layers + 1];
+};
+// x tiles, value atoms, H tiles and A rows of each layer.
+struct Tc2Maps {
+  CUtensorMap x[kTc2Layers], v[kTc2Layers], h[kTc2Layers], a[kTc2Layers];
+};
+
+// Layer of work item `item` and the item's index within that layer.
+__device__ __forceinline__ int tc2_layer_of(const Tc2Set& set, int item) {
+  int l = 0;
+  while (l + 1 < set.n && item >= set.item0[l + 1]) ++l;
+  return l;
+}
+
 __device__ __forceinline__ void timeout2(volatile int* abort_flag) {
   atomicOr(&g_status_tc2, SLR_TIMEOUT_BIT);
   *abort_flag = 1;
@@ -72,9 +94,8 @@ __device__ __forceinline__ void timeout2(volatile int* abort_flag) {
 
 template <int BP, int BQ, typename TI, int MODE>
 __global__ void __launch_bounds__(kThreads, 1)
-    tc2_rowblock_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_v,
-                        const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ CUtensorMap tm_a,
-                        const Tc2Args a, const __grid_constant__ YMaps ym) {
+    tc2_rowblock_kernel(const __grid_constant__ Tc2Maps maps, const __grid_constant__ Tc2Set set,
+                        const __grid_constant__ YMaps ym) {
   constexpr int G = 256 / BP;            // block-rows per item
   constexpr int KS = BQ < 64 ? BQ : 64;  // k per sparse stage
   constexpr int SUB = BQ / KS;
@@ -150,19 +171,20 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
 
   const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
-  const int n_items = a.n_groups * a.n_mtiles;
+  const int n_items = set.item0[set.n];
 
   if (warp == 0 || warp >= 6) {
     // ------------------------------------------------------- TMA producers
-    if (lane == 0) {
-      tma_prefetch_desc(&tm_x);
-      if (a.crow) tma_prefetch_desc(&tm_v);
-      if (a.n_lr) {
-        tma_prefetch_desc(&tm_h);
-        tma_prefetch_desc(&tm_a);
+    if (lane == 0)
+      for (int l = 0; l < set.n; ++l) {
+        tma_prefetch_desc(&maps.x[l]);
+        if (set.L[l].crow) tma_prefetch_desc(&maps.v[l]);
+        if (set.L[l].n_lr) {
+          tma_prefetch_desc(&maps.h[l]);
+          tma_prefetch_desc(&maps.a[l]);
+        }
       }
-    }
-    if (a.plan) {
+    if (set.L[0].plan) {
       // With the column schedule producer warp p (0, 6, 7 -> 0, 1, 2) fills
       // the stages g with g % 3 == p: always the same two ring slots, so its
       // waits on them stay in phase order.  Each CTA loads its own 128 token
@@ -172,7 +194,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t g = 0;
       bool waited = false, abort_now = false;
       for (int kr = 0, item = snake_item(0, pair, npairs); item < n_items && !abort_now; ++kr, item = snake_item(kr, pair, npairs)) {
-        const int gi = item / a.n_mtiles, mt = item - gi * a.n_mtiles;
+        const int li = tc2_layer_of(set, item);
+        const Tc2Args& a = set.L[li];
+        const CUtensorMap* tm_x = &maps.x[li];
+        const CUtensorMap* tm_v = &maps.v[li];
+        const CUtensorMap* tm_h = &maps.h[li];
+        const CUtensorMap* tm_a = &maps.a[li];
+        const int litem = item - set.item0[li];
+        const int gi = litem / a.n_mtiles, mt = litem - gi * a.n_mtiles;
         const int r0 = gi * G;
         const int gcount = min(G, a.nrows - r0);
         const int m0 = mt * 256 + int(rank) * 128;  // this CTA's tokens
@@ -219,7 +248,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               }
 #pragma unroll
               for (int c = 0; c < CPS; ++c)
-                if (c < nc) tma2_load_2d(adst + c * X_BYTES, &tm_x, int(cols[c]) * BQ + sub * KS, m0, fb);
+                if (c < nc) tma2_load_2d(adst + c * X_BYTES, tm_x, int(cols[c]) * BQ + sub * KS, m0, fb);
             }
             uint32_t off = 0;  // this column's first atom in the stage's B slot
 #pragma unroll
@@ -238,7 +267,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int h = 0; h < 2; ++h) {
                   const int at = 2 * (lane - j0) + h;
                   if (at / len == int(rank))
-                    tma2_load_2d(adst + A_SLOT + (p_run + at - int(rank) * len) * POS, &tm_v, h * (BP / 2),
+                    tma2_load_2d(adst + A_SLOT + (p_run + at - int(rank) * len) * POS, tm_v, h * (BP / 2),
                                  blk * BQ + sub * KS, fb);
                 }
               }
@@ -255,11 +284,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 meta[slot] = kMetaLR | (last ? kMetaLast : 0u);
                 mbar_arrive_expect_tx(&full[slot], 2 * H_BYTES + gcount * AR_ROW);
               }
-              tma2_load_2d(adst, &tm_h, l * 64, m0, fb);
+              tma2_load_2d(adst, tm_h, l * 64, m0, fb);
             }
             const int jl = lane - int(rank) * (G / 2);
             if (jl >= 0 && jl < G / 2 && lane < gcount)
-              tma2_load_2d(adst + A_SLOT + jl * AR_ROW, &tm_a, l * 64, rw * BP, fb);
+              tma2_load_2d(adst + A_SLOT + jl * AR_ROW, tm_a, l * 64, rw * BP, fb);
           } else if (lane == 0 && leader) {
             meta[slot] = kMetaLast;  // no block and no rank: the item still completes
             mbar_arrive(&full[slot]);
@@ -268,6 +297,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         g += uint32_t(n_st);
       }
     } else if (warp == 0 && lane == 0) {
+      // (a launch without a schedule holds one layer)
+      const Tc2Args& a = set.L[0];
+      const CUtensorMap* tm_x = &maps.x[0];
+      const CUtensorMap* tm_v = &maps.v[0];
+      const CUtensorMap* tm_h = &maps.h[0];
+      const CUtensorMap* tm_a = &maps.a[0];
       bool waited = false;
       uint32_t g = 0;
       for (int kr = 0, item = snake_item(0, pair, npairs); item < n_items && !s_abort; ++kr, item = snake_item(kr, pair, npairs)) {
@@ -316,7 +351,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               mbar_arrive_expect_tx(&full[slot], 2 * (X_BYTES + pc * POS));
             }
             uint8_t* adst = smem + slot * STAGE;
-            tma2_load_2d(adst, &tm_x, c * BQ + sub * KS, m0, fb);
+            tma2_load_2d(adst, tm_x, c * BQ + sub * KS, m0, fb);
             // runs of consecutive rows: this CTA's len atoms of each run, packed
             uint32_t m = mask, p = 0;
             while (m) {
@@ -326,7 +361,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               for (int i = 0; i < len; ++i) {
                 const int at = int(rank) * len + i;  // atom index within the run
                 const int row = j + (at >> 1), half = at & 1;
-                tma2_load_2d(adst + A_SLOT + (p + i) * POS, &tm_v, half * (BP / 2), blk[row] * BQ + sub * KS, fb);
+                tma2_load_2d(adst + A_SLOT + (p + i) * POS, tm_v, half * (BP / 2), blk[row] * BQ + sub * KS, fb);
               }
               p += len;
             }
@@ -350,9 +385,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_arrive_expect_tx(&full[slot], 2 * H_BYTES + gcount * AR_ROW);
           }
           uint8_t* adst = smem + slot * STAGE;
-          tma2_load_2d(adst, &tm_h, l * 64, m0, fb);
+          tma2_load_2d(adst, tm_h, l * 64, m0, fb);
           for (int j = int(rank) * (G / 2); j < (int(rank) + 1) * (G / 2) && j < gcount; ++j)
-            tma2_load_2d(adst + A_SLOT + (j - int(rank) * (G / 2)) * AR_ROW, &tm_a, l * 64, rw[j] * BP, fb);
+            tma2_load_2d(adst + A_SLOT + (j - int(rank) * (G / 2)) * AR_ROW, tm_a, l * 64, rw[j] * BP, fb);
           published = true;
         }
         if (!published && !s_abort) {
@@ -431,8 +466,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q = warp & 3;
     const uint32_t lane_base = uint32_t(32 * q) << 16;
     const int row = 32 * q + lane;
-    TI* __restrict__ y = static_cast<TI*>(a.y);
-    const TI* __restrict__ bias = static_cast<const TI*>(a.bias);
+    const Tc2Args& a0 = set.L[0];  // the peer epilogue runs in one-layer launches only
     const uint32_t te0 = mapa(smem_u32(&tempty[0]), 0);
     constexpr int kCpr = BP / 8;  // 16-byte chunks of a row's BP outputs
     // 16-byte chunk c of staging row r, as TMA's 128B (BP 64) / 64B (BP 32) swizzle places it
@@ -440,20 +474,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint4* stage_w = reinterpret_cast<uint4*>(smem + STAGES * STAGE + kEpiOff) + (warp - 2) * 32 * kCpr;
     // Multi-GPU: this call's arrival at every rank, then (before the first
     // store into a peer) the wait for every rank's arrival.
-    const int world = a.peer.world;
+    const int world = a0.peer.world;
     unsigned long long call_no = 0;  // this rank's call of the layer, 1-based
     bool peer_live = world > 1, arrived = false;
     if (world > 1) {
       pdl_wait_primary();  // the preceding wait of this rank has counted its calls
-      call_no = *reinterpret_cast<volatile unsigned long long*>(a.peer.my_sig + kSigCalls) + 1;
+      call_no = *reinterpret_cast<volatile unsigned long long*>(a0.peer.my_sig + kSigCalls) + 1;
       if (blockIdx.x == 0 && warp == 2 && lane == 0) {
 #pragma unroll
         for (int p = 0; p < kMaxRanks; ++p)
-          if (p < world) st_release_sys(a.peer.sig[p] + kSigArrive + a.peer.me, call_no);
+          if (p < world) st_release_sys(a0.peer.sig[p] + kSigArrive + a0.peer.me, call_no);
       }
     }
     auto wait_arrivals = [&]() {
-      int ok = lane == 0 ? int(wait_words(a.peer.my_sig + kSigArrive, world, call_no, a.peer.wait_ns, true)) : 1;
+      int ok = lane == 0 ? int(wait_words(a0.peer.my_sig + kSigArrive, world, call_no, a0.peer.wait_ns, true)) : 1;
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) {
         if (lane == 0) {
@@ -466,7 +500,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
     uint32_t it = 0;
     for (int kr = 0, item = snake_item(0, pair, npairs); item < n_items; ++kr, item = snake_item(kr, pair, npairs), ++it) {
-      const int gi = item / a.n_mtiles, mt = item - gi * a.n_mtiles;
+      const int li = tc2_layer_of(set, item);
+      const Tc2Args& a = set.L[li];
+      TI* __restrict__ y = static_cast<TI*>(a.y);
+      const TI* __restrict__ bias = static_cast<const TI*>(a.bias);
+      const int litem = item - set.item0[li];
+      const int gi = litem / a.n_mtiles, mt = litem - gi * a.n_mtiles;
       const int r0 = gi * G;
       const int gcount = min(G, a.nrows - r0);
       const uint32_t buf = it & 1, tph = (it >> 1) & 1;
@@ -547,7 +586,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (lane == 0 && tok0 < a.M) {
 #pragma unroll
             for (int p = 0; p < kMaxRanks; ++p)
-              if (p < world && (p == a.peer.me || peer_live))
+              if (p < world && (p == a0.peer.me || peer_live))
                 tma_store_2d(&ym.m[p], stage_w, br * BP, int(tok0));
             bulk_commit();
           }
@@ -574,12 +613,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (s_abort || s_peer_fail) {
 #pragma unroll
           for (int p = 0; p < kMaxRanks; ++p)
-            if (p < world) st_release_sys(a.peer.sig[p] + kSigFail + a.peer.me, call_no);
+            if (p < world) st_release_sys(a0.peer.sig[p] + kSigFail + a0.peer.me, call_no);
         }
         const unsigned long long add = 1ull + (blockIdx.x == 0 ? kDonePerRank - gridDim.x : 0ull);
 #pragma unroll
         for (int p = 0; p < kMaxRanks; ++p)
-          if (p < world) red_add_release_sys(a.peer.sig[p] + kSigDone + a.peer.me, add);
+          if (p < world) red_add_release_sys(a0.peer.sig[p] + kSigDone + a0.peer.me, add);
       }
     }
   }
@@ -595,8 +634,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 int num_sms() { return sm_budget(); }
 
 template <int BP, int BQ, typename TI, int MODE>
-int launch_inst(const CUtensorMap& tx, const CUtensorMap& tv, const CUtensorMap& th, const CUtensorMap& ta,
-                const Tc2Args& k, const YMaps& ym, bool pdl, cudaStream_t s) {
+int launch_inst(const Tc2Maps& maps, const Tc2Set& set, const YMaps& ym, bool pdl, cudaStream_t s) {
   constexpr int G = 256 / BP;
   constexpr int KS = BQ < 64 ? BQ : 64;
   constexpr uint32_t POS = KS * BP, AR_ROW = BP * 128;
@@ -604,10 +642,10 @@ int launch_inst(const CUtensorMap& tx, const CUtensorMap& tv, const CUtensorMap&
   constexpr uint32_t STAGE = 16384 + B_SLOT;
   constexpr int STAGES = kStages;
   static_assert((2 * STAGES + 4) * 8 + STAGES * 4 + 16 <= kEpiOff, "barrier area");
-  const size_t smem = 1024 + size_t(STAGES) * STAGE + kEpiOff + (k.peer.world > 1 ? epi_stage_bytes(BP) : 0);
+  const size_t smem = 1024 + size_t(STAGES) * STAGE + kEpiOff + (set.L[0].peer.world > 1 ? epi_stage_bytes(BP) : 0);
   auto kern = tc2_rowblock_kernel<BP, BQ, TI, MODE>;
   SLR_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
-  const int items = k.n_groups * k.n_mtiles;
+  const int items = set.item0[set.n];
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(unsigned(2 * std::min(items, num_sms() / 2)));
   cfg.blockDim = dim3(kThreads);
@@ -622,28 +660,62 @@ int launch_inst(const CUtensorMap& tx, const CUtensorMap& tv, const CUtensorMap&
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 2 : 1;
-  SLR_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kern, tx, tv, th, ta, k, ym));
+  SLR_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kern, maps, set, ym));
   return SLR_OK;
 }
 
 template <int BP, typename TI, int MODE>
-int dispatch_bq(int bq, const CUtensorMap& tx, const CUtensorMap& tv, const CUtensorMap& th,
-                const CUtensorMap& ta, const Tc2Args& k, const YMaps& ym, bool pdl, cudaStream_t s) {
+int dispatch_bq(int bq, const Tc2Maps& maps, const Tc2Set& set, const YMaps& ym, bool pdl, cudaStream_t s) {
   switch (bq) {
-    case 16: return launch_inst<BP, 16, TI, MODE>(tx, tv, th, ta, k, ym, pdl, s);
-    case 32: return launch_inst<BP, 32, TI, MODE>(tx, tv, th, ta, k, ym, pdl, s);
-    case 64: return launch_inst<BP, 64, TI, MODE>(tx, tv, th, ta, k, ym, pdl, s);
-    case 128: return launch_inst<BP, 128, TI, MODE>(tx, tv, th, ta, k, ym, pdl, s);
+    case 16: return launch_inst<BP, 16, TI, MODE>(maps, set, ym, pdl, s);
+    case 32: return launch_inst<BP, 32, TI, MODE>(maps, set, ym, pdl, s);
+    case 64: return launch_inst<BP, 64, TI, MODE>(maps, set, ym, pdl, s);
+    case 128: return launch_inst<BP, 128, TI, MODE>(maps, set, ym, pdl, s);
     default: return fail(SLR_ERR_UNSUPPORTED, "2-SM path: block_q must be 16, 32, 64 or 128");
   }
 }
 
 template <typename TI, int MODE>
-int dispatch_bp(int bp, int bq, const CUtensorMap& tx, const CUtensorMap& tv, const CUtensorMap& th,
-                const CUtensorMap& ta, const Tc2Args& k, const YMaps& ym, bool pdl, cudaStream_t s) {
-  if (bp == 32) return dispatch_bq<32, TI, MODE>(bq, tx, tv, th, ta, k, ym, pdl, s);
-  if (bp == 64) return dispatch_bq<64, TI, MODE>(bq, tx, tv, th, ta, k, ym, pdl, s);
+int dispatch_bp(int bp, int bq, const Tc2Maps& maps, const Tc2Set& set, const YMaps& ym, bool pdl, cudaStream_t s) {
+  if (bp == 32) return dispatch_bq<32, TI, MODE>(bq, maps, set, ym, pdl, s);
+  if (bp == 64) return dispatch_bq<64, TI, MODE>(bq, maps, set, ym, pdl, s);
   return fail(SLR_ERR_UNSUPPORTED, "2-SM path: block_p must be 32 or 64");
+}
+
+// Layer `a` as entry li of a launch: its Tc2Args and tensor maps.
+int fill_tc2_layer(const RowblockArgs& a, Tc2Maps& maps, Tc2Set& set, int li) {
+  const bool sparse = a.crow != nullptr && a.nnz > 0;
+  const int bq = sparse ? a.bq : 64;
+  const int ks = bq < 64 ? bq : 64;
+  int rc = make_tmap_2d(&maps.x[li], a.x, a.dtype, uint64_t(a.K), uint64_t(a.M), uint64_t(a.ldx) * 2, uint32_t(ks),
+                        128u);
+  if (rc) return rc;
+  if (sparse) {
+    rc = make_tmap_2d(&maps.v[li], a.values, a.dtype, uint64_t(a.bp), uint64_t(a.nnz) * a.bq, uint64_t(a.bp) * 2,
+                      uint32_t(a.bp / 2), uint32_t(ks));
+    if (rc) return rc;
+  }
+  const int G = 256 / a.bp;
+  set.L[li] = Tc2Args{a.y, a.mode == MODE_FUSED ? a.bias : nullptr, sparse ? a.crow : nullptr, a.col, a.rows,
+                      sparse ? a.stage_plan : nullptr, sparse ? a.stage_start : nullptr, a.M, a.ldy,
+                      int(a.nrows), int(ceil_div(a.nrows, G)), int(ceil_div(a.M, 256)), 0};
+  if (a.mode == MODE_FUSED && a.r > 0) {
+    set.L[li].n_lr = int(ceil_div(a.r, 64));
+    rc = make_tmap_2d(&maps.h[li], a.H, a.dtype, uint64_t(a.ldh), uint64_t(a.M), uint64_t(a.ldh) * 2, 64u, 128u);
+    if (rc) return rc;
+    rc = make_tmap_2d(&maps.a[li], a.A, a.dtype, uint64_t(a.r), uint64_t(a.N), uint64_t(a.r) * 2, 64u, uint32_t(a.bp));
+    if (rc) return rc;
+  }
+  return SLR_OK;
+}
+
+int dispatch_set(const RowblockArgs& a0, int bq, const Tc2Maps& maps, const Tc2Set& set, const YMaps& ym, bool pdl,
+                 cudaStream_t s) {
+  if (a0.dtype == SLR_BF16)
+    return a0.mode == MODE_ADDMM ? dispatch_bp<__nv_bfloat16, MODE_ADDMM>(a0.bp, bq, maps, set, ym, pdl, s)
+                                 : dispatch_bp<__nv_bfloat16, MODE_FUSED>(a0.bp, bq, maps, set, ym, pdl, s);
+  return a0.mode == MODE_ADDMM ? dispatch_bp<__half, MODE_ADDMM>(a0.bp, bq, maps, set, ym, pdl, s)
+                               : dispatch_bp<__half, MODE_FUSED>(a0.bp, bq, maps, set, ym, pdl, s);
 }
 
 }  // namespace
@@ -660,23 +732,16 @@ bool tc2_rowblock_supported(const RowblockArgs& a) {
 int launch_tc2_rowblock(const RowblockArgs& a, bool pdl, cudaStream_t s, const PeerArgs* peers) {
   if (a.nrows <= 0 || a.M <= 0) return SLR_OK;
   const bool sparse = a.crow != nullptr && a.nnz > 0;
-  const int bq = sparse ? a.bq : 64;
-  const int ks = bq < 64 ? bq : 64;
-  CUtensorMap tx{}, tv{}, th{}, ta{};
-  int rc = make_tmap_2d(&tx, a.x, a.dtype, uint64_t(a.K), uint64_t(a.M), uint64_t(a.ldx) * 2, uint32_t(ks), 128u);
+  Tc2Maps maps{};
+  Tc2Set set{};
+  int rc = fill_tc2_layer(a, maps, set, 0);
   if (rc) return rc;
-  if (sparse) {
-    rc = make_tmap_2d(&tv, a.values, a.dtype, uint64_t(a.bp), uint64_t(a.nnz) * a.bq, uint64_t(a.bp) * 2,
-                      uint32_t(a.bp / 2), uint32_t(ks));
-    if (rc) return rc;
-  }
-  const int G = 256 / a.bp;
-  Tc2Args k{a.y, a.mode == MODE_FUSED ? a.bias : nullptr, sparse ? a.crow : nullptr, a.col, a.rows,
-            sparse ? a.stage_plan : nullptr, sparse ? a.stage_start : nullptr, a.M, a.ldy,
-            int(a.nrows), int(ceil_div(a.nrows, G)), int(ceil_div(a.M, 256)), 0};
+  set.n = 1;
+  set.item0[0] = 0;
+  set.item0[1] = set.L[0].n_groups * set.L[0].n_mtiles;
   YMaps ym{};
   if (peers && peers->world > 1) {
-    k.peer = *peers;
+    set.L[0].peer = *peers;
     // TMA store maps of every rank's y at this rank's columns: [M, N], box bp x 32 rows
     for (int p = 0; p < peers->world; ++p) {
       rc = make_tmap_2d(&ym.m[p], peers->y[p], a.dtype, uint64_t(a.N), uint64_t(a.M), uint64_t(a.ldy) * 2,
@@ -684,18 +749,36 @@ int launch_tc2_rowblock(const RowblockArgs& a, bool pdl, cudaStream_t s, const P
       if (rc) return rc;
     }
   }
-  if (a.mode == MODE_FUSED && a.r > 0) {
-    k.n_lr = int(ceil_div(a.r, 64));
-    rc = make_tmap_2d(&th, a.H, a.dtype, uint64_t(a.ldh), uint64_t(a.M), uint64_t(a.ldh) * 2, 64u, 128u);
-    if (rc) return rc;
-    rc = make_tmap_2d(&ta, a.A, a.dtype, uint64_t(a.r), uint64_t(a.N), uint64_t(a.r) * 2, 64u, uint32_t(a.bp));
-    if (rc) return rc;
+  return dispatch_set(a, sparse ? a.bq : 64, maps, set, ym, pdl, s);
+}
+
+bool tc2_group_compatible(const RowblockArgs* as, int n) {
+  if (n < 1 || n > kTc2Layers) return false;
+  const RowblockArgs& a0 = as[0];
+  for (int i = 0; i < n; ++i) {
+    const RowblockArgs& a = as[i];
+    const bool sparse = a.crow != nullptr && a.nnz > 0;
+    if (!sparse || !a.stage_plan || !a.stage_start || !tc2_rowblock_supported(a)) return false;
+    if (a.bp != a0.bp || a.bq != a0.bq || a.M != a0.M || a.dtype != a0.dtype || a.mode != a0.mode) return false;
   }
-  if (a.dtype == SLR_BF16)
-    return a.mode == MODE_ADDMM ? dispatch_bp<__nv_bfloat16, MODE_ADDMM>(a.bp, bq, tx, tv, th, ta, k, ym, pdl, s)
-                                : dispatch_bp<__nv_bfloat16, MODE_FUSED>(a.bp, bq, tx, tv, th, ta, k, ym, pdl, s);
-  return a.mode == MODE_ADDMM ? dispatch_bp<__half, MODE_ADDMM>(a.bp, bq, tx, tv, th, ta, k, ym, pdl, s)
-                              : dispatch_bp<__half, MODE_FUSED>(a.bp, bq, tx, tv, th, ta, k, ym, pdl, s);
+  return true;
+}
+
+int launch_tc2_rowblock_group(const RowblockArgs* as, int n, bool pdl, cudaStream_t s) {
+  if (!tc2_group_compatible(as, n)) return fail(SLR_ERR_UNSUPPORTED, "2-SM path: layers cannot share one launch");
+  if (as[0].M <= 0) return SLR_OK;
+  Tc2Maps maps{};
+  Tc2Set set{};
+  set.n = n;
+  set.item0[0] = 0;
+  for (int i = 0; i < n; ++i) {
+    int rc = fill_tc2_layer(as[i], maps, set, i);
+    if (rc) return rc;
+    set.item0[i + 1] = set.item0[i] + set.L[i].n_groups * set.L[i].n_mtiles;
+  }
+  if (set.item0[n] == 0) return SLR_OK;
+  const YMaps ym{};
+  return dispatch_set(as[0], as[0].bq, maps, set, ym, pdl, s);
 }
 
 int read_and_clear_status_tc2(unsigned* out) {

@@ -613,6 +613,17 @@ int group_lowrank(const slr_layer* layers, int n, const GroupCall& gc, cudaStrea
 // their kernel shapes agree, else one launch per layer.  x_early: this call's
 // h_small was launched just before (GROUP_SMALL after group_lowrank).
 int group_combine_all(const slr_layer* layers, int n, const GroupCall& gc, cudaStream_t s, bool x_early) {
+  if (gc.mode == GROUP_TC && n > 1) {
+    // every layer on the pair kernel: one launch for all (one schedule tail)
+    RowblockArgs as[kMaxGroup];
+    bool all_pair = true, pdl = true;
+    for (int i = 0; i < n; ++i) {
+      as[i] = gc.c[i].a;
+      all_pair = all_pair && use_pair(layers[i], gc.c[i]);
+      pdl = pdl && layers[i].rank > 0 && early_start(layers[i]);
+    }
+    if (all_pair && tc2_group_compatible(as, n)) return launch_tc2_rowblock_group(as, n, pdl, s);
+  }
   if (gc.mode == GROUP_SMALL) {
     RowblockArgs as[kMaxGroup];
     for (int i = 0; i < n; ++i) as[i] = gc.c[i].a;
@@ -823,6 +834,144 @@ int plan_multi(const slr_layer* layers, int n, const void* const* x, const int64
   return SLR_OK;
 }
 
+// One multi-input call, checked and packed once: every layer's forward
+// arguments; below 128 tokens their H share one buffer (one h_small launch),
+// from 128 tokens on each layer keeps its own (layers on one input share
+// their run's), and pair_group says whether all combines run as one launch of
+// the pair kernel.
+struct MultiCall {
+  MultiPlan m;
+  FwdCall c[kMaxMulti];
+  bool pair_group = false;
+  bool pdl = true;
+  // From 128 tokens: runs of consecutive layers that read one x (same
+  // pointer, stride and width) whose x*B^T is one grouped tensor-core GEMM
+  // into one H (the run's own workspace regions, taken together).
+  int n_runs = 0;
+  int run0[kMaxMulti + 1] = {};
+  bool grouped[kMaxMulti] = {};
+  GroupCall gc[kMaxMulti];
+};
+
+int prepare_multi(const slr_layer* layers, int n, const void* const* x, const int64_t* ldx, void* const* y,
+                  const int64_t* ldy, int64_t M, void* workspace, size_t workspace_bytes, bool need_y,
+                  MultiCall& mc) {
+  if (!x || (need_y && !y)) return fail(SLR_ERR_INVALID_ARGUMENT, "x/y is NULL");
+  int rc = plan_multi(layers, n, x, ldx, M, mc.m);
+  if (rc || M == 0) return rc;
+  const MultiPlan& m = mc.m;
+  if (m.total > 0) {
+    if (!workspace) return fail(SLR_ERR_WORKSPACE, "workspace is NULL");
+    if (workspace_bytes < m.total)
+      return fail(SLR_ERR_WORKSPACE, "workspace too small: need " + std::to_string(m.total) + " bytes");
+    if (reinterpret_cast<uintptr_t>(workspace) & 255u) return fail(SLR_ERR_WORKSPACE, "workspace must be 256-byte aligned");
+  }
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  for (int i = 0; i < n; ++i) {
+    rc = prepare_forward(&layers[i], x[i], ldx ? ldx[i] : 0, need_y ? y[i] : nullptr, ldy ? ldy[i] : 0, M,
+                         ws + m.off[i], m.bytes[i], need_y, mc.c[i], !m.small);
+    if (rc) return rc;
+  }
+  if (m.small) {
+    for (int i = 0; i < n; ++i) {
+      mc.c[i].a.H = ws + size_t(m.col[i]) * dtype_size(layers[i].dtype);
+      mc.c[i].a.ldh = m.ldh_all;
+      mc.pdl = mc.pdl && early_start(layers[i]);
+    }
+  } else {
+    // runs of layers on one input: one grouped x*B^T each
+    for (int i = 0; i < n;) {
+      const int64_t lx = (ldx && ldx[i]) ? ldx[i] : layers[i].in_features;
+      int j = i + 1;
+      while (j < n && j - i < kMaxGroup && x[j] == x[i] && layers[j].in_features == layers[i].in_features &&
+             ((ldx && ldx[j]) ? ldx[j] : layers[j].in_features) == lx)
+        ++j;
+      const int r = mc.n_runs++;
+      mc.run0[r] = i;
+      mc.run0[r + 1] = j;
+      if (j - i > 1 && M >= kTcMinTokens) {
+        size_t bytes = 0;
+        for (int k = i; k < j; ++k) bytes += align256(m.bytes[k]);
+        GroupCall& gc = mc.gc[r];
+        rc = prepare_group(&layers[i], j - i, x[i], lx, need_y ? y + i : nullptr, ldy ? ldy + i : nullptr, M,
+                           ws + m.off[i], bytes, gc);
+        if (rc) return rc;
+        if (gc.mode == GROUP_TC) {
+          mc.grouped[r] = true;
+          for (int k = i; k < j; ++k) mc.c[k] = gc.c[k - i];
+        }
+      }
+      i = j;
+    }
+    RowblockArgs as[kMaxMulti];
+    bool all_pair = M >= kTcMinTokens && n > 1;
+    for (int i = 0; i < n && all_pair; ++i) {
+      as[i] = mc.c[i].a;
+      all_pair = use_pair(layers[i], mc.c[i]);
+      mc.pdl = mc.pdl && layers[i].rank > 0 && early_start(layers[i]);
+    }
+    mc.pair_group = all_pair && tc2_group_compatible(as, n);
+  }
+  return SLR_OK;
+}
+
+// x*B^T of every layer: one h_small launch below 128 tokens (each layer keeps
+// the K split it would get alone, so H is the one of slr_lrs_linear_forward
+// bit for bit), else each layer's own.
+int multi_lowrank(const slr_layer* layers, int n, const MultiCall& mc, void* workspace, cudaStream_t s) {
+  if (!mc.m.small) {
+    for (int r = 0; r < mc.n_runs; ++r) {
+      const int i0 = mc.run0[r], i1 = mc.run0[r + 1];
+      if (mc.grouped[r]) {
+        int rc = group_lowrank(&layers[i0], i1 - i0, mc.gc[r], s);
+        if (rc) return rc;
+        continue;
+      }
+      for (int i = i0; i < i1; ++i) {
+        int rc = run_lowrank(layers[i], mc.c[i], s);
+        if (rc) return rc;
+      }
+    }
+    return SLR_OK;
+  }
+  const void* xs[kMaxMulti];
+  const void* Bs[kMaxMulti];
+  int64_t ldxs[kMaxMulti], rs[kMaxMulti], Ks[kMaxMulti];
+  for (int i = 0; i < n; ++i) {
+    xs[i] = mc.c[i].a.x;
+    ldxs[i] = mc.c[i].a.ldx;
+    Bs[i] = layers[i].B;
+    rs[i] = layers[i].rank;
+    Ks[i] = layers[i].in_features;
+  }
+  return launch_h_small(xs, ldxs, Bs, rs, workspace, mc.c[0].a.M, Ks, mc.m.ldh_all, mc.m.hs, layers[0].dtype, mc.pdl,
+                        s);
+}
+
+// The combines: one launch when the kernel shapes agree (the pair kernel from
+// 128 tokens on, the small-batch kernel below), else one per layer.  x_early:
+// this call's h_small was launched just before.
+int multi_combine(const slr_layer* layers, int n, const MultiCall& mc, void* workspace, cudaStream_t s,
+                  bool x_early) {
+  RowblockArgs as[kMaxMulti];
+  for (int i = 0; i < n; ++i) as[i] = mc.c[i].a;
+  if (!mc.m.small) {
+    if (mc.pair_group) return launch_tc2_rowblock_group(as, n, mc.pdl, s);
+    for (int i = 0; i < n; ++i) {
+      int rc = run_combine(layers[i], mc.c[i], true, s, false);
+      if (rc) return rc;
+    }
+    return SLR_OK;
+  }
+  if (mma_group_compatible(as, n, false))
+    return launch_mma_rowblock_group(as, mc.m.col, n, workspace, mc.m.ldh_all, mc.pdl, s, x_early);
+  for (int i = 0; i < n; ++i) {
+    int rc = run_combine(layers[i], mc.c[i], true, s, x_early);
+    if (rc) return rc;
+  }
+  return SLR_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -836,61 +985,42 @@ size_t slr_lrs_linear_multi_workspace_size(const slr_layer* layers, int n, int64
 int slr_lrs_linear_forward_multi(const slr_layer* layers, int n, const void* const* x, const int64_t* ldx,
                                  void* const* y, const int64_t* ldy, int64_t M, void* workspace,
                                  size_t workspace_bytes, void* stream) {
-  if (!x || !y) return fail(SLR_ERR_INVALID_ARGUMENT, "x/y is NULL");
-  MultiPlan m;
-  int rc = plan_multi(layers, n, x, ldx, M, m);
+  MultiCall mc;
+  int rc = prepare_multi(layers, n, x, ldx, y, ldy, M, workspace, workspace_bytes, true, mc);
   if (rc || M == 0) return rc;
-  if (m.total > 0) {
-    if (!workspace) return fail(SLR_ERR_WORKSPACE, "workspace is NULL");
-    if (workspace_bytes < m.total)
-      return fail(SLR_ERR_WORKSPACE, "workspace too small: need " + std::to_string(m.total) + " bytes");
-    if (reinterpret_cast<uintptr_t>(workspace) & 255u) return fail(SLR_ERR_WORKSPACE, "workspace must be 256-byte aligned");
-  }
-  uint8_t* ws = static_cast<uint8_t*>(workspace);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  FwdCall c[kMaxMulti];
-  for (int i = 0; i < n; ++i) {
-    rc = prepare_forward(&layers[i], x[i], ldx ? ldx[i] : 0, y[i], ldy ? ldy[i] : 0, M, ws + m.off[i], m.bytes[i],
-                         true, c[i], !m.small);
-    if (rc) return rc;
-  }
-  if (!m.small) {
+  bool any_grouped = false;
+  for (int r = 0; r < mc.n_runs; ++r) any_grouped = any_grouped || mc.grouped[r];
+  if (!mc.m.small && !mc.pair_group && !any_grouped) {
+    // each layer's forward in turn
     for (int i = 0; i < n; ++i) {
-      rc = run_lowrank(layers[i], c[i], s);
+      rc = run_lowrank(layers[i], mc.c[i], s);
       if (rc) return rc;
-      rc = run_combine(layers[i], c[i], true, s, lowrank_is_h_small(layers[i], c[i]));
+      rc = run_combine(layers[i], mc.c[i], true, s, lowrank_is_h_small(layers[i], mc.c[i]));
       if (rc) return rc;
     }
     return SLR_OK;
   }
-  // One h_small launch for every layer's x*B^T (each layer keeps the K split it
-  // would get alone, so H is the one of slr_lrs_linear_forward bit for bit),
-  // then the combines: one launch when the kernel shapes agree.
-  const void* xs[kMaxMulti];
-  const void* Bs[kMaxMulti];
-  int64_t ldxs[kMaxMulti], rs[kMaxMulti], Ks[kMaxMulti];
-  bool pdl = true;
-  for (int i = 0; i < n; ++i) {
-    xs[i] = c[i].a.x;
-    ldxs[i] = c[i].a.ldx;
-    Bs[i] = layers[i].B;
-    rs[i] = layers[i].rank;
-    Ks[i] = layers[i].in_features;
-    c[i].a.H = ws + size_t(m.col[i]) * dtype_size(layers[i].dtype);
-    c[i].a.ldh = m.ldh_all;
-    pdl = pdl && early_start(layers[i]);
-  }
-  rc = launch_h_small(xs, ldxs, Bs, rs, ws, M, Ks, m.ldh_all, m.hs, layers[0].dtype, pdl, s);
+  rc = multi_lowrank(layers, n, mc, workspace, s);
   if (rc) return rc;
-  RowblockArgs as[kMaxMulti];
-  for (int i = 0; i < n; ++i) as[i] = c[i].a;
-  if (mma_group_compatible(as, n, false))
-    return launch_mma_rowblock_group(as, m.col, n, ws, m.ldh_all, pdl, s, true);
-  for (int i = 0; i < n; ++i) {
-    rc = run_combine(layers[i], c[i], true, s, true);
-    if (rc) return rc;
-  }
-  return SLR_OK;
+  return multi_combine(layers, n, mc, workspace, s, mc.m.small);
+}
+
+int slr_lrs_linear_multi_lowrank(const slr_layer* layers, int n, const void* const* x, const int64_t* ldx,
+                                 int64_t M, void* workspace, size_t workspace_bytes, void* stream) {
+  MultiCall mc;
+  int rc = prepare_multi(layers, n, x, ldx, nullptr, nullptr, M, workspace, workspace_bytes, false, mc);
+  if (rc || M == 0) return rc;
+  return multi_lowrank(layers, n, mc, workspace, static_cast<cudaStream_t>(stream));
+}
+
+int slr_lrs_linear_multi_combine(const slr_layer* layers, int n, const void* const* x, const int64_t* ldx,
+                                 void* const* y, const int64_t* ldy, int64_t M, void* workspace,
+                                 size_t workspace_bytes, void* stream) {
+  MultiCall mc;
+  int rc = prepare_multi(layers, n, x, ldx, y, ldy, M, workspace, workspace_bytes, true, mc);
+  if (rc || M == 0) return rc;
+  return multi_combine(layers, n, mc, workspace, static_cast<cudaStream_t>(stream), false);
 }
 
 }  // extern "C"

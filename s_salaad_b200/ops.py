@@ -511,6 +511,39 @@ class LayerSet:
         _lib.check(rc, "lrs_linear_forward_multi")
         return outs
 
+    def _ptrs(self, xs, outs=None):
+        n = len(self.descs)
+        xp = (ctypes.c_void_p * n)(*[x.data_ptr() for x in xs])
+        lx = (ctypes.c_int64 * n)(*[LayerDesc._ld(x) for x in xs])
+        if outs is None:
+            return xp, lx, None, None
+        yp = (ctypes.c_void_p * n)(*[o.data_ptr() for o in outs])
+        ly = (ctypes.c_int64 * n)(*[LayerDesc._ld(o) for o in outs])
+        return xp, lx, yp, ly
+
+    def lowrank(self, xs: list[torch.Tensor]) -> None:
+        """Phase 1 alone: every layer's x @ B.T into the set's workspace."""
+        M = xs[0].shape[0]
+        ws = self.workspace(M)
+        xp, lx, _, _ = self._ptrs(xs)
+        with _DeviceGuard(self.device):
+            rc = _lib.load().slr_lrs_linear_multi_lowrank(
+                self._structs(), len(self.descs), xp, lx, M, None if ws is None else ws.data_ptr(),
+                0 if ws is None else ws.numel(), _stream(self.device))
+        _lib.check(rc, "lrs_linear_multi_lowrank")
+
+    def combine(self, xs: list[torch.Tensor], outs: list[torch.Tensor]) -> list[torch.Tensor]:
+        """Phase 2 alone (after lowrank() on the same inputs): every layer's y."""
+        M = xs[0].shape[0]
+        ws = self.workspace(M)
+        xp, lx, yp, ly = self._ptrs(xs, outs)
+        with _DeviceGuard(self.device):
+            rc = _lib.load().slr_lrs_linear_multi_combine(
+                self._structs(), len(self.descs), xp, lx, yp, ly, M, None if ws is None else ws.data_ptr(),
+                0 if ws is None else ws.numel(), _stream(self.device))
+        _lib.check(rc, "lrs_linear_multi_combine")
+        return outs
+
 
 # ------------------------------------------------ N:M 2:4 + low-rank --
 

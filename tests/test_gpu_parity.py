@@ -752,6 +752,46 @@ def test_multi_forward_equals_per_layer(cuda, oracle, name, T):
             assert_16bit_close(y, oracle_layer(oracle, t, x.cpu()))
 
 
+@pytest.mark.parametrize("name", list(MULTI))
+@pytest.mark.parametrize("T", [1, 64, 300])
+def test_multi_phases_equal_forward(cuda, name, T):
+    """slr_lrs_linear_multi_lowrank + _multi_combine give the forward bit for bit."""
+    specs, descs = _multi_layers(cuda, name)
+    xs = [workloads.tokens(T, n_k[1], seed=T + 3 * i, dtype=torch.bfloat16).to(cuda)
+          for i, n_k in enumerate(MULTI[name])]
+    lset = ops.LayerSet(descs)
+    ref = [y.clone() for y in lset.forward(xs)]
+    outs = [torch.full_like(y, float("nan")) for y in ref]
+    lset.lowrank(xs)
+    lset.combine(xs, outs)
+    for a, b in zip(outs, ref):
+        assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("T", [300, 1024])
+def test_pair_kernel_layer_set_in_one_launch(cuda, oracle, T):
+    """Four cfg4 projections (64x64 blocks, column schedules, Zipf rows), each
+    with its own input: their combines run as ONE launch of the 2-SM pair
+    kernel (items of all layers dealt as one list) and equal the per-layer
+    forwards bit for bit; also as a group (q/k/v on one input)."""
+    cfg = workloads.layer_set("cfg4")
+    specs = [cfg[i] for i in (0, 3, 4, 6)]
+    tens = [s.tensors(cuda, torch.bfloat16) for s in specs]
+    descs = [desc_for(t, s, cuda, torch.bfloat16) for t, s in zip(tens, specs)]
+    xs = [workloads.tokens(T, s.in_features, seed=T + i, device=cuda, dtype=torch.bfloat16)
+          for i, s in enumerate(specs)]
+    ys = ops.LayerSet(descs).forward(xs)
+    for d, x, y in zip(descs, xs, ys):
+        assert torch.equal(y, d.forward(x))
+    qkv = [desc_for(cfg[i].tensors(cuda, torch.bfloat16), cfg[i], cuda, torch.bfloat16) for i in (0, 1, 2)]
+    x = xs[0]
+    for d, y in zip(qkv, ops.LayerGroup(qkv).forward(x)):
+        assert torch.equal(y, d.forward(x))
+    # one projection against the fp32 oracle on a token slice (the oracle is slow)
+    t = {k: (v.cpu() if v is not None else None) for k, v in tens[1].items()}
+    assert_16bit_close(ys[1][:64], oracle_layer(oracle, t, xs[1][:64].cpu()))
+
+
 @pytest.mark.parametrize("T", [1, 16, 64])
 def test_multi_chained_early_start_equals_strict_order(cuda, T):
     """Back-to-back multi calls whose inputs are the previous call's outputs:
