@@ -496,6 +496,8 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-cublas", action="store_true")
     ap.add_argument("--no-decode", action="store_true", help="skip the decode points of the headline run")
+    ap.add_argument("--decode-kernel", action="store_true",
+                    help="calls of 1..32 tokens take the opt-in single-launch decode kernel")
     ap.add_argument("--ncu", action="store_true",
                     help="profiling mode: warm-up + timed steps only (no e2e, cuBLAS or CPU legs)")
     args = ap.parse_args()
@@ -504,8 +506,10 @@ def main() -> None:
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
 
-    from s_salaad_b200 import workloads
+    from s_salaad_b200 import ops, workloads
 
+    if args.decode_kernel:
+        ops._single_launch = True  # the process's calls of 1..32 tokens: ops.single_launch_decode(True)
     if args.workload == "cfg2-model":
         return model_bench(args)
     cfg, T = parse_workload(args.workload)

@@ -603,14 +603,31 @@ int launch_inst(const MmaMaps& maps, MmaArgs k, uint32_t stage, dim3 grid, bool 
   auto kern = mma_rowblock_kernel<NT, KX, TI, MODE>;
   constexpr int TT = 8 * NT;
   const size_t smem_full = mma_smem(stage, kStages, TT), smem_low = mma_smem(stage, 4, TT);
-  SLR_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem_full)));
-  // CTAs per SM of this kernel instance at both depths (cached per slot size)
-  thread_local uint32_t c_stage = 0;
-  thread_local int occ_full = 0, occ_low = 0;
-  if (c_stage != stage) {
+  // CTAs per SM of this kernel instance at both depths, per slot size (the
+  // layers of a model alternate between a few sizes; the queries and the
+  // attribute are host calls worth avoiding on every launch)
+  struct Occ {
+    uint32_t stage;
+    int full, low;
+  };
+  thread_local Occ cache[8] = {};
+  thread_local int n_cached = 0;
+  thread_local size_t max_smem_set = 0;
+  if (smem_full > max_smem_set) {
+    SLR_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem_full)));
+    max_smem_set = smem_full;
+  }
+  int occ_full = -1, occ_low = -1;
+  for (int i = 0; i < n_cached; ++i)
+    if (cache[i].stage == stage) {
+      occ_full = cache[i].full;
+      occ_low = cache[i].low;
+    }
+  if (occ_full < 0) {
     SLR_CHECK_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ_full, kern, kThreads, smem_full));
     SLR_CHECK_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ_low, kern, kThreads, smem_low));
-    c_stage = stage;
+    cache[n_cached % 8] = Occ{stage, occ_full, occ_low};
+    ++n_cached;
   }
   const int64_t ctas = int64_t(grid.x) * grid.y;
   const int64_t sms = device_sms();

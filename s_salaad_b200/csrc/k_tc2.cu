@@ -70,6 +70,9 @@ struct YMaps {
 // layer l's first, and dealt to the pairs as one list, so the launch has one
 // persistent-schedule tail instead of one per layer.
 constexpr int kTc2Layers = kMaxLaunchLayers;
+// Row groups of a launch that can be put in one heaviest-first order in
+// shared memory at the start of the kernel.
+constexpr int kOrderCap = 512;
 struct Tc2Set {
   Tc2Args L[kTc2Layers];
   int n;
@@ -173,6 +176,54 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
   const int n_items = set.item0[set.n];
 
+  // Items in one heaviest-first order over all layers of the launch: every
+  // CTA ranks the row groups by their stages (schedule columns + rank chunks;
+  // ties by layer, then group) in shared memory, and item i is token tile
+  // i % n_mtiles of the group ranked i / n_mtiles.  The ranking is the same
+  // in every CTA, and an item's arithmetic does not depend on its place.
+  __shared__ uint32_t s_order[kOrderCap], s_weight[kOrderCap];
+  int n_groups_all = 0;
+  for (int l = 0; l < set.n; ++l) n_groups_all += set.L[l].n_groups;
+  // (one layer: its row groups are already planned heaviest first)
+  const bool ordered = set.n > 1 && set.L[0].plan != nullptr && n_groups_all <= kOrderCap;
+  if (ordered) {
+    for (int gs = threadIdx.x; gs < n_groups_all; gs += blockDim.x) {
+      int l = 0, gi = gs;
+      while (gi >= set.L[l].n_groups) gi -= set.L[l++].n_groups;
+      s_weight[gs] = uint32_t(__ldg(set.L[l].plan_start + gi + 1) - __ldg(set.L[l].plan_start + gi) + set.L[l].n_lr);
+      s_order[gs] = 0u;
+    }
+    __syncthreads();
+    for (int gs = threadIdx.x; gs < n_groups_all; gs += blockDim.x) {
+      const uint32_t w = s_weight[gs];
+      int rk = 0;
+      for (int j = 0; j < n_groups_all; ++j) {
+        const uint32_t wj = s_weight[j];
+        rk += (wj > w || (wj == w && j < gs)) ? 1 : 0;
+      }
+      int l = 0, gi = gs;
+      while (gi >= set.L[l].n_groups) gi -= set.L[l++].n_groups;
+      s_order[rk] = (uint32_t(l) << 16) | uint32_t(gi);
+    }
+    __syncthreads();
+  }
+  // layer, row group and token tile of work item `item`
+  auto decode_item = [&](int item, int& li, int& gi, int& mt) {
+    if (ordered) {
+      const int nm = set.L[0].n_mtiles;
+      const int gs = item / nm;
+      mt = item - gs * nm;
+      const uint32_t e = s_order[gs];
+      li = int(e >> 16);
+      gi = int(e & 0xffffu);
+    } else {
+      li = tc2_layer_of(set, item);
+      const int litem = item - set.item0[li];
+      gi = litem / set.L[li].n_mtiles;
+      mt = litem - gi * set.L[li].n_mtiles;
+    }
+  };
+
   if (warp == 0 || warp >= 6) {
     // ------------------------------------------------------- TMA producers
     if (lane == 0)
@@ -194,14 +245,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t g = 0;
       bool waited = false, abort_now = false;
       for (int kr = 0, item = snake_item(0, pair, npairs); item < n_items && !abort_now; ++kr, item = snake_item(kr, pair, npairs)) {
-        const int li = tc2_layer_of(set, item);
+        int li, gi, mt;
+        decode_item(item, li, gi, mt);
         const Tc2Args& a = set.L[li];
         const CUtensorMap* tm_x = &maps.x[li];
         const CUtensorMap* tm_v = &maps.v[li];
         const CUtensorMap* tm_h = &maps.h[li];
         const CUtensorMap* tm_a = &maps.a[li];
-        const int litem = item - set.item0[li];
-        const int gi = litem / a.n_mtiles, mt = litem - gi * a.n_mtiles;
         const int r0 = gi * G;
         const int gcount = min(G, a.nrows - r0);
         const int m0 = mt * 256 + int(rank) * 128;  // this CTA's tokens
@@ -500,12 +550,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
     uint32_t it = 0;
     for (int kr = 0, item = snake_item(0, pair, npairs); item < n_items; ++kr, item = snake_item(kr, pair, npairs), ++it) {
-      const int li = tc2_layer_of(set, item);
+      int li, gi, mt;
+      decode_item(item, li, gi, mt);
       const Tc2Args& a = set.L[li];
       TI* __restrict__ y = static_cast<TI*>(a.y);
       const TI* __restrict__ bias = static_cast<const TI*>(a.bias);
-      const int litem = item - set.item0[li];
-      const int gi = litem / a.n_mtiles, mt = litem - gi * a.n_mtiles;
       const int r0 = gi * G;
       const int gcount = min(G, a.nrows - r0);
       const uint32_t buf = it & 1, tph = (it >> 1) & 1;
