@@ -241,110 +241,195 @@ __global__ void __launch_bounds__(kThreads, 1)
       // waits on them stay in phase order.  Each CTA loads its own 128 token
       // rows and its half of the B operand; loads complete on the leader's
       // barrier.
+      // A warp's stages pass through a three-deep software pipeline: before
+      // it waits for the slot of stage k it requests the schedule records of
+      // stage k+2 and the value-block indices of stage k+1 (which need k+1's
+      // records, requested one step earlier); an item's row-group bounds and
+      // row indices are requested one item ahead.  The latency of these
+      // dependent global loads then overlaps the slot waits instead of
+      // adding to every slot's round trip.
       const int pw = warp == 0 ? 0 : warp - 5;
-      uint32_t g = 0;
-      bool waited = false, abort_now = false;
-      for (int kr = 0, item = snake_item(0, pair, npairs); item < n_items && !abort_now; ++kr, item = snake_item(kr, pair, npairs)) {
-        int li, gi, mt;
-        decode_item(item, li, gi, mt);
-        const Tc2Args& a = set.L[li];
-        const CUtensorMap* tm_x = &maps.x[li];
-        const CUtensorMap* tm_v = &maps.v[li];
-        const CUtensorMap* tm_h = &maps.h[li];
-        const CUtensorMap* tm_a = &maps.a[li];
-        const int r0 = gi * G;
-        const int gcount = min(G, a.nrows - r0);
-        const int m0 = mt * 256 + int(rank) * 128;  // this CTA's tokens
-        const int p0 = __ldg(a.plan_start + gi), p1 = __ldg(a.plan_start + gi + 1);
-        const int n_sp = ((p1 - p0 + CPS - 1) / CPS) * SUB;
-        const int n_st = max(n_sp + a.n_lr, 1);
-        const int rw = lane < gcount ? (a.rows ? a.rows[r0 + lane] : r0 + lane) : 0;
-        for (int s = (pw - int(g % kProducers) + kProducers) % kProducers; s < n_st; s += kProducers) {
-          const uint32_t gg = g + uint32_t(s);
-          const uint32_t slot = gg % STAGES, ph = (gg / STAGES) & 1;
-          int ok = lane == 0 ? int(mbar_wait(&empty[slot], ph ^ 1)) : 1;
-          ok = __shfl_sync(0xffffffffu, ok, 0);
-          if (!ok) {
-            if (lane == 0) timeout2(&s_abort);
-            abort_now = true;
-            break;
-          }
-          const uint32_t fb = mapa(smem_u32(&full[slot]), 0);
-          uint8_t* adst = smem + slot * STAGE;
-          const bool last = s == n_st - 1;
-          if (s < n_sp) {
-            const int kb = p0 + (s / SUB) * CPS, sub = s % SUB;
-            const int nc = min(CPS, p1 - kb);  // schedule columns in this stage
-            uint32_t cols[CPS], masks[CPS], firsts[CPS];
-#pragma unroll
-            for (int c = 0; c < CPS; ++c) {
-              cols[c] = masks[c] = firsts[c] = 0u;
-              if (c < nc) {
-                const uint32_t rec = __ldg(a.plan + 2 * (kb + c));
-                cols[c] = rec & 0xffffu;
-                masks[c] = rec >> 16;
-                firsts[c] = __ldg(a.plan + 2 * (kb + c) + 1);
-              }
-            }
-            uint32_t atoms = 0;
-#pragma unroll
-            for (int c = 0; c < CPS; ++c) atoms += uint32_t(__popc(masks[c]));
-            if (lane == 0) {
-              if (leader) {
-                uint32_t mm = masks[0];
-                if (CPS == 2) mm |= masks[CPS - 1] << 8;
-                meta[slot] = mm | (last ? kMetaLast : 0u);
-                mbar_arrive_expect_tx(&full[slot], 2 * (uint32_t(nc) * X_BYTES + atoms * POS));
-              }
-#pragma unroll
-              for (int c = 0; c < CPS; ++c)
-                if (c < nc) tma2_load_2d(adst + c * X_BYTES, tm_x, int(cols[c]) * BQ + sub * KS, m0, fb);
-            }
-            uint32_t off = 0;  // this column's first atom in the stage's B slot
-#pragma unroll
-            for (int c = 0; c < CPS; ++c) {
-              const uint32_t mask = masks[c];
-              if ((mask >> lane) & 1u) {
-                // this row's run of consecutive present rows [j0, end): its 2*len
-                // half-block atoms, the first len on the leader, the rest on the peer
-                const uint32_t below = (1u << lane) - 1u, zeros = ~mask & below;
-                const int j0 = zeros ? 32 - __clz(zeros) : 0;
-                const int end = lane + __ffs(~(mask >> lane)) - 1;
-                const int len = end - j0;
-                const int p_run = int(off) + __popc(mask & ((1u << j0) - 1u));
-                const int blk = int(__ldg(a.plan + firsts[c] + __popc(mask & below)));
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                  const int at = 2 * (lane - j0) + h;
-                  if (at / len == int(rank))
-                    tma2_load_2d(adst + A_SLOT + (p_run + at - int(rank) * len) * POS, tm_v, h * (BP / 2),
-                                 blk * BQ + sub * KS, fb);
-                }
-              }
-              off += uint32_t(__popc(mask));
-            }
-          } else if (s < n_sp + a.n_lr) {
-            const int l = s - n_sp;
-            if (!waited) {
-              pdl_wait_primary();  // H comes from the preceding kernel
-              waited = true;
-            }
-            if (lane == 0) {
-              if (leader) {
-                meta[slot] = kMetaLR | (last ? kMetaLast : 0u);
-                mbar_arrive_expect_tx(&full[slot], 2 * H_BYTES + gcount * AR_ROW);
-              }
-              tma2_load_2d(adst, tm_h, l * 64, m0, fb);
-            }
-            const int jl = lane - int(rank) * (G / 2);
-            if (jl >= 0 && jl < G / 2 && lane < gcount)
-              tma2_load_2d(adst + A_SLOT + jl * AR_ROW, tm_a, l * 64, rw * BP, fb);
-          } else if (lane == 0 && leader) {
-            meta[slot] = kMetaLast;  // no block and no rank: the item still completes
-            mbar_arrive(&full[slot]);
-          }
+      struct ItemCtx {
+        int kr, li, gi, mt, p0, p1, rw;
+        uint32_t g0;  // the item's first stage in the launch's stage sequence
+        bool valid;
+      };
+      struct Stage {
+        int li, mt, gcount, rw, n_sp, n_st, s, kb, nc;
+        uint32_t gg;  // stage index in the launch's stage sequence
+        uint32_t rec[CPS], firsts[CPS];
+        int blk[CPS];
+        bool valid;
+      };
+      auto load_ctx = [&](int kr) {
+        ItemCtx c;
+        const int item = snake_item(kr, pair, npairs);
+        c.kr = kr;
+        c.valid = item < n_items;
+        c.g0 = 0;
+        c.li = c.gi = c.mt = c.p0 = c.p1 = c.rw = 0;
+        if (c.valid) {
+          decode_item(item, c.li, c.gi, c.mt);
+          const Tc2Args& a = set.L[c.li];
+          c.p0 = __ldg(a.plan_start + c.gi);
+          c.p1 = __ldg(a.plan_start + c.gi + 1);
+          const int r0 = c.gi * G;
+          c.rw = lane < min(G, a.nrows - r0) ? (a.rows ? __ldg(a.rows + r0 + lane) : r0 + lane) : 0;
         }
-        g += uint32_t(n_st);
+        return c;
+      };
+      auto n_sp_of = [&](const ItemCtx& c) { return ((c.p1 - c.p0 + CPS - 1) / CPS) * SUB; };
+      auto n_st_of = [&](const ItemCtx& c) { return max(n_sp_of(c) + set.L[c.li].n_lr, 1); };
+      // iterator over this warp's stages: stage s_it of item ci (cn: the next item)
+      ItemCtx ci = load_ctx(0), cn = load_ctx(1);
+      int s_it = pw;
+      auto settle = [&]() {
+        while (ci.valid && s_it >= n_st_of(ci)) {
+          const int n = n_st_of(ci);
+          s_it -= n;
+          const uint32_t g0 = ci.g0 + uint32_t(n);
+          ci = cn;
+          ci.g0 = g0;
+          cn = load_ctx(ci.kr + 1);
+        }
+      };
+      // the iterator's stage; requests its schedule records
+      auto make_stage = [&](Stage& st) {
+        st.valid = ci.valid;
+        st.li = ci.li;
+        st.mt = ci.mt;
+        st.rw = ci.rw;
+        st.s = s_it;
+        st.gg = ci.g0 + uint32_t(s_it);
+        st.kb = st.nc = 0;
+#pragma unroll
+        for (int c = 0; c < CPS; ++c) {
+          st.rec[c] = st.firsts[c] = 0u;
+          st.blk[c] = 0;
+        }
+        if (!st.valid) return;
+        const Tc2Args& a = set.L[ci.li];
+        st.gcount = min(G, a.nrows - ci.gi * G);
+        st.n_sp = n_sp_of(ci);
+        st.n_st = n_st_of(ci);
+        if (s_it < st.n_sp) {
+          st.kb = ci.p0 + (s_it / SUB) * CPS;
+          st.nc = min(CPS, ci.p1 - st.kb);
+#pragma unroll
+          for (int c = 0; c < CPS; ++c)
+            if (c < st.nc) {
+              st.rec[c] = __ldg(a.plan + 2 * (st.kb + c));
+              st.firsts[c] = __ldg(a.plan + 2 * (st.kb + c) + 1);
+            }
+        }
+      };
+      // requests the value-block index of this lane's row in each column
+      auto fetch_blocks = [&](Stage& st) {
+        if (!st.valid || st.s >= st.n_sp) return;
+        const uint32_t* plan = set.L[st.li].plan;
+#pragma unroll
+        for (int c = 0; c < CPS; ++c) {
+          const uint32_t mask = st.rec[c] >> 16;
+          if (c < st.nc && ((mask >> lane) & 1u))
+            st.blk[c] = int(__ldg(plan + st.firsts[c] + __popc(mask & ((1u << lane) - 1u))));
+        }
+      };
+      bool waited = false;
+      // waits for the stage's slot and issues its loads; false on a timeout
+      auto issue = [&](const Stage& st) -> bool {
+        const Tc2Args& a = set.L[st.li];
+        const CUtensorMap* tm_x = &maps.x[st.li];
+        const CUtensorMap* tm_v = &maps.v[st.li];
+        const CUtensorMap* tm_h = &maps.h[st.li];
+        const CUtensorMap* tm_a = &maps.a[st.li];
+        const int s = st.s;
+        const uint32_t slot = st.gg % STAGES, ph = (st.gg / STAGES) & 1;
+        int ok = lane == 0 ? int(mbar_wait(&empty[slot], ph ^ 1)) : 1;
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) return false;
+        const uint32_t fb = mapa(smem_u32(&full[slot]), 0);
+        uint8_t* adst = smem + slot * STAGE;
+        const bool last = s == st.n_st - 1;
+        const int m0 = st.mt * 256 + int(rank) * 128;  // this CTA's tokens
+        if (s < st.n_sp) {
+          const int sub = s % SUB;
+          uint32_t atoms = 0;
+#pragma unroll
+          for (int c = 0; c < CPS; ++c) atoms += uint32_t(__popc(st.rec[c] >> 16));
+          if (lane == 0) {
+            if (leader) {
+              uint32_t mm = st.rec[0] >> 16;
+              if (CPS == 2) mm |= (st.rec[CPS - 1] >> 16) << 8;
+              meta[slot] = mm | (last ? kMetaLast : 0u);
+              mbar_arrive_expect_tx(&full[slot], 2 * (uint32_t(st.nc) * X_BYTES + atoms * POS));
+            }
+#pragma unroll
+            for (int c = 0; c < CPS; ++c)
+              if (c < st.nc) tma2_load_2d(adst + c * X_BYTES, tm_x, int(st.rec[c] & 0xffffu) * BQ + sub * KS, m0, fb);
+          }
+          uint32_t off = 0;  // this column's first atom in the stage's B slot
+#pragma unroll
+          for (int c = 0; c < CPS; ++c) {
+            const uint32_t mask = st.rec[c] >> 16;
+            if ((mask >> lane) & 1u) {
+              // this row's run of consecutive present rows [j0, end): its 2*len
+              // half-block atoms, the first len on the leader, the rest on the peer
+              const uint32_t below = (1u << lane) - 1u, zeros = ~mask & below;
+              const int j0 = zeros ? 32 - __clz(zeros) : 0;
+              const int end = lane + __ffs(~(mask >> lane)) - 1;
+              const int len = end - j0;
+              const int p_run = int(off) + __popc(mask & ((1u << j0) - 1u));
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                const int at = 2 * (lane - j0) + h;
+                if (at / len == int(rank))
+                  tma2_load_2d(adst + A_SLOT + (p_run + at - int(rank) * len) * POS, tm_v, h * (BP / 2),
+                               st.blk[c] * BQ + sub * KS, fb);
+              }
+            }
+            off += uint32_t(__popc(mask));
+          }
+        } else if (s < st.n_sp + a.n_lr) {
+          const int l = s - st.n_sp;
+          if (!waited) {
+            pdl_wait_primary();  // H comes from the preceding kernel
+            waited = true;
+          }
+          if (lane == 0) {
+            if (leader) {
+              meta[slot] = kMetaLR | (last ? kMetaLast : 0u);
+              mbar_arrive_expect_tx(&full[slot], 2 * H_BYTES + st.gcount * AR_ROW);
+            }
+            tma2_load_2d(adst, tm_h, l * 64, m0, fb);
+          }
+          const int jl = lane - int(rank) * (G / 2);
+          if (jl >= 0 && jl < G / 2 && lane < st.gcount)
+            tma2_load_2d(adst + A_SLOT + jl * AR_ROW, tm_a, l * 64, st.rw * BP, fb);
+        } else if (lane == 0 && leader) {
+          meta[slot] = kMetaLast;  // no block and no rank: the item still completes
+          mbar_arrive(&full[slot]);
+        }
+        return true;
+      };
+      Stage d0, d1, d2;
+      settle();
+      make_stage(d0);
+      s_it += kProducers;
+      settle();
+      make_stage(d1);
+      fetch_blocks(d0);
+      while (d0.valid) {
+        s_it += kProducers;
+        settle();
+        make_stage(d2);   // records of stage k+2
+        fetch_blocks(d1);  // block indices of stage k+1
+        if (__shfl_sync(0xffffffffu, int(s_abort), 0)) break;  // another role gave up: unwind
+        if (!issue(d0)) {
+          if (lane == 0) timeout2(&s_abort);
+          break;
+        }
+        d0 = d1;
+        d1 = d2;
       }
     } else if (warp == 0 && lane == 0) {
       // (a launch without a schedule holds one layer)

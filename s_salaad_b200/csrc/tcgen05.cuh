@@ -107,7 +107,12 @@ __device__ __forceinline__ uint32_t mapa(uint32_t addr, uint32_t rank) {
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
   return r;
 }
+// Every thread of the cluster calls it.  The barrier is .aligned (all lanes of
+// a warp execute it together), so the warp first reconverges: warps whose lane
+// 0 ran a role loop alone (the MMA issuer, a TMA producer) would otherwise
+// reach it split.
 __device__ __forceinline__ void cluster_sync() {
+  __syncwarp();
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 __device__ __forceinline__ void tmem_alloc2(uint32_t* dst, uint32_t ncols) {
