@@ -69,9 +69,10 @@ METRIC = "S+LR linear tokens/s + %HBM/TC roofline at 1/2/4/8 B200 vs AVX2 CPU & 
 # kernel the roofline covers, from one ncu capture of
 # `bench.py --ncu --workload <w> --steps 1 --warmup 3` on a B200 with
 # `--metrics dram__bytes_read.sum,dram__bytes_write.sum,gpu__time_duration.sum`:
-# cfg4 = mean over the 7 combine launches of one step; cfg3-T1 = the whole
+# cfg4 and cfg3-T2048 = the one combine launch of the layer set (third launch
+# of the process, `-k regex:tc2_rowblock -s 2 -c 1`); cfg3-T1 = the whole
 # layer set of one step (its roofline covers the graph-replayed layer set).
-NCU_TRAFFIC = {"cfg3-T1": 50881280.0}
+NCU_TRAFFIC = {"cfg3-T1": 50881280.0, "cfg4": 1001.91e6, "cfg3-T2048": 144.76e6}
 # SMs kept free of the persistent kernels at N > 1 (for the overlapping NCCL
 # all-gathers); SLR_BENCH_NCCL_SMS overrides it.
 SMS_FOR_NCCL = int(os.environ.get("SLR_BENCH_NCCL_SMS", "16"))
