@@ -366,7 +366,9 @@ def nm_points(dev, steps: int, warmup: int, flush: torch.Tensor, peaks_: dict) -
     """The N:M 2:4 + low-rank layer (the reference's other compressed-layer
     kind) on a LLaMA-7B-shaped MLP projection: 11008 x 4096, S 2:4 (the 2
     largest of N(0, 0.02) in every group of 4), rank 512, bf16, at a decode
-    and a prefill token count; each beside dense cuBLAS on W = A*B + S, both
+    and a prefill token count (below 256 tokens the mma.sp kernel, from 256
+    S unpacked into dense blocks on the tensor-core combine, the unpacking
+    inside the timed call); each beside dense cuBLAS on W = A*B + S, both
     replayed from a CUDA graph with L2 flushed between replays.  Decode: HBM
     roofline on the algorithmic bytes (S values + metadata, A, B, bias, x, y).
     Prefill: FLOP rate on 2*T*(N*K/2 + r*(N+K)) against the measured dense
@@ -402,8 +404,11 @@ def nm_points(dev, steps: int, warmup: int, flush: torch.Tensor, peaks_: dict) -
                           "frac": fl / (ms / 1e3) / 1e12 / peaks_["bf16_tflops"], "bound": "tensor (dense peak)"})
         out[f"T{T}"] = point
         del x, y
-    return {"shape": [n, k], "rank": r, "sparsity": "2:4 along K", "kernel": "mma.sp (m16n8k32) + mma.sync, one "
-            "fused launch after x*B^T", "points": out}
+    return {"shape": [n, k], "rank": r, "sparsity": "2:4 along K",
+            "kernel": {"T1": "mma.sp (m16n8k32) + mma.sync, one fused launch after x*B^T",
+                       "T4096": "S unpacked per call into full-density 64x64 blocks, then x*B^T and the 2-SM "
+                                "tcgen05 combine (the block-sparse layer's kernels)"},
+            "points": out}
 
 
 def model_bench(args) -> None:

@@ -163,6 +163,13 @@ int launch_nm_pack(const void* S, int64_t N, int64_t K, int dtype, void* values,
 int launch_nm_combine(const void* x, int64_t ldx, void* y, int64_t ldy, const void* values, const uint32_t* meta,
                       const void* A, const void* H, int64_t ldh, const void* bias, int64_t M, int64_t N, int64_t K,
                       int64_t r, int dtype, cudaStream_t s);
+// Prefill form of the layer: S unpacked into all (N/64) x (K/64) blocks of 64
+// x 64 in the combine's value layout ([k][n] per block, row-major block
+// order), with the row pointers, column indices and column schedule
+// (slr_plan_stages layout, natural row order, block_p 64) of that structure.
+int64_t nm_dense_plan_words(int64_t N, int64_t K);
+int launch_nm_dense_blocks(const void* values, const uint32_t* meta, int64_t N, int64_t K, int dtype, void* blocks,
+                           uint32_t* plan, int32_t* stage_start, int32_t* crow, int32_t* col, cudaStream_t s);
 
 // ---- dense -> BSR conversion.
 int launch_bsr_mask(const void* S, int64_t n, int64_t m, int64_t bp, int64_t bq, int dtype,

@@ -280,6 +280,69 @@ __global__ void __launch_bounds__(kNmWarps * 32) nm_combine_kernel(const NmArgs 
 
 int nm_pick_tt(int64_t M) { return M <= 8 ? 8 : M <= 16 ? 16 : M <= 32 ? 32 : 64; }
 
+// ------------------------------------------------ prefill: dense 64 x 64 blocks --
+//
+// From 256 tokens the layer runs as a full-density block-sparse layer on the
+// 2-SM tensor-core combine: S is unpacked per call into every 64 x 64 block
+// in the combine's value layout, block (i, j) at index i * (K/64) + j holding
+// S[64i + n][64j + k] at [k][n], and a column schedule of the full structure
+// is written beside it.  One CTA per block: each thread expands 4 groups of 4
+// (16 K entries) of one row into a shared tile, transposed, then the tile
+// leaves as 16-byte stores.
+constexpr int kUnpackPad = 72;  // tile row (64 n + 8): 16-byte aligned, fewer bank conflicts
+
+template <typename TI>
+__global__ void __launch_bounds__(256) nm_unpack_blocks_kernel(const TI* __restrict__ values,
+                                                               const uint32_t* __restrict__ meta, int64_t K,
+                                                               int64_t KB, TI* __restrict__ blocks) {
+  __shared__ __align__(16) TI tile[64 * kUnpackPad];  // [k][n]
+  const int64_t bi = blockIdx.x / KB, bj = blockIdx.x - bi * KB;
+  const int n = threadIdx.x >> 2, q = threadIdx.x & 3;  // row n of the block, K entries [16q, 16q + 16)
+  const int64_t row = bi * 64 + n, k0 = bj * 64 + q * 16;
+  const uint4 v = *reinterpret_cast<const uint4*>(values + row * (K / 2) + k0 / 2);  // 8 kept entries
+  const uint32_t word = __ldg(meta + row * (K / 32) + k0 / 32) >> (16 * (q & 1));  // their 4 groups
+  const TI* kept = reinterpret_cast<const TI*>(&v);
+  const TI zero = from_f<TI>(0.f);
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    const uint32_t nib = (word >> (4 * g)) & 0xfu;
+    const int p0 = int(nib & 3u), p1 = int(nib >> 2);
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+      tile[(q * 16 + 4 * g + e) * kUnpackPad + n] = e == p0 ? kept[2 * g] : (e == p1 ? kept[2 * g + 1] : zero);
+  }
+  __syncthreads();
+  // the block's 64 x 64 entries, [k][n]: thread t writes k = t / 4, n = 16 (t % 4) .. + 16
+  const int k = threadIdx.x >> 2, c = (threadIdx.x & 3) * 16;
+  uint4* out = reinterpret_cast<uint4*>(blocks + blockIdx.x * int64_t(64 * 64) + k * 64 + c);
+  const uint4* src = reinterpret_cast<const uint4*>(tile + k * kUnpackPad + c);
+  out[0] = src[0];
+  out[1] = src[1];
+}
+
+// Row pointers, column indices and the column schedule (the layout
+// slr_plan_stages writes) of NB x KB present blocks, natural row order, groups
+// of G = 4 block-rows (block_p 64): group gi has one stage per column s, all
+// its rows present; the block indices follow the 2 * groups * KB records.
+__global__ void dense_plan_kernel(int64_t NB, int64_t KB, uint32_t* __restrict__ plan, int32_t* __restrict__ stage_start,
+                                  int32_t* __restrict__ crow, int32_t* __restrict__ col) {
+  constexpr int G = 4;
+  const int64_t groups = (NB + G - 1) / G, n_st = groups * KB;
+  const int64_t idx = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx < n_st) {
+    const int64_t gi = idx / KB, s = idx - gi * KB;
+    const int cnt = int(NB - gi * G < G ? NB - gi * G : G);
+    // blocks of the groups before: gi * G * KB (only the last group is short)
+    const int64_t first = 2 * n_st + gi * G * KB + s * cnt;
+    plan[2 * idx] = uint32_t(s) | (((1u << cnt) - 1u) << 16);
+    plan[2 * idx + 1] = uint32_t(first);
+    for (int j = 0; j < cnt; ++j) plan[first + j] = uint32_t((gi * G + j) * KB + s);
+  }
+  if (idx <= groups) stage_start[idx] = int32_t(idx * KB);
+  if (idx <= NB) crow[idx] = int32_t(idx * KB);
+  if (idx < NB * KB) col[idx] = int32_t(idx % KB);
+}
+
 template <int NT, typename TI>
 int launch_nm_inst(const NmArgs& a, cudaStream_t s) {
   constexpr int TT = 8 * NT;
@@ -329,6 +392,34 @@ int launch_nm_combine(const void* x, int64_t ldx, void* y, int64_t ldy, const vo
   if (dtype == SLR_BF16) return launch_nm_t<__nv_bfloat16>(a, s);
   if (dtype == SLR_F16) return launch_nm_t<__half>(a, s);
   return fail(SLR_ERR_UNSUPPORTED_DTYPE, "N:M layer: 16-bit dtypes only");
+}
+
+int64_t nm_dense_plan_words(int64_t N, int64_t K) {
+  const int64_t NB = N / 64, KB = K / 64, groups = (NB + 3) / 4;
+  return 2 * groups * KB + NB * KB;
+}
+
+int launch_nm_dense_blocks(const void* values, const uint32_t* meta, int64_t N, int64_t K, int dtype, void* blocks,
+                           uint32_t* plan, int32_t* stage_start, int32_t* crow, int32_t* col, cudaStream_t s) {
+  const int64_t NB = N / 64, KB = K / 64;
+  if (NB <= 0 || KB <= 0) return SLR_OK;
+  if (N % 64 || K % 64) return fail(SLR_ERR_UNSUPPORTED, "N:M dense blocks: N and K must be multiples of 64");
+  if (nm_dense_plan_words(N, K) > INT32_MAX) return fail(SLR_ERR_UNSUPPORTED, "N:M dense blocks: schedule too large");
+  const unsigned nblk = unsigned(NB * KB);
+  if (dtype == SLR_BF16)
+    nm_unpack_blocks_kernel<__nv_bfloat16><<<nblk, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(values), meta, K,
+                                                                 KB, static_cast<__nv_bfloat16*>(blocks));
+  else if (dtype == SLR_F16)
+    nm_unpack_blocks_kernel<__half><<<nblk, 256, 0, s>>>(static_cast<const __half*>(values), meta, K, KB,
+                                                          static_cast<__half*>(blocks));
+  else
+    return fail(SLR_ERR_UNSUPPORTED_DTYPE, "N:M layer: 16-bit dtypes only");
+  SLR_CHECK_LAUNCH("nm_unpack_blocks_kernel");
+  const int64_t groups = (NB + 3) / 4;
+  const int64_t work = std::max(std::max(NB * KB, NB + 1), std::max(groups * KB, groups + 1));
+  dense_plan_kernel<<<unsigned(ceil_div(work, 256)), 256, 0, s>>>(NB, KB, plan, stage_start, crow, col);
+  SLR_CHECK_LAUNCH("dense_plan_kernel");
+  return SLR_OK;
 }
 
 }  // namespace slr

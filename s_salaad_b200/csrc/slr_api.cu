@@ -707,6 +707,42 @@ slr_layer nm_lowrank_layer(const slr_nm_layer& L) {
   return lr;
 }
 
+// Prefill route of the N:M layer (M >= kNmDenseTokens): S unpacked per call
+// into full-density 64 x 64 blocks in the workspace and the layer run as a
+// block-sparse S+LR layer on the 2-SM tensor-core combine, whose 256-wide
+// MMAs keep the tensor cores busy where the mma.sp kernel's 16-feature tiles
+// re-read S for every 64 tokens.  Same arithmetic: x·Sᵀ, H·Aᵀ and the bias
+// accumulated in fp32, y rounded once.
+constexpr int64_t kNmDenseTokens = 256;
+
+struct NmDenseLayout {
+  size_t blocks = 0, plan = 0, start = 0, crow = 0, col = 0, total = 0;
+};
+
+bool nm_dense_route(const slr_nm_layer& L, int64_t M) {
+  return M >= kNmDenseTokens && L.out_features % 64 == 0 && L.in_features % 64 == 0 && L.rank % 64 == 0 &&
+         (L.flags & kFlagStrict) == 0;
+}
+
+// Offsets of the route's buffers after the first `base` bytes of the workspace.
+NmDenseLayout nm_dense_layout(const slr_nm_layer& L, size_t base) {
+  const int64_t NB = L.out_features / 64, KB = L.in_features / 64, groups = (NB + 3) / 4;
+  NmDenseLayout d;
+  size_t o = align256(base);
+  d.blocks = o;
+  o = align256(o + size_t(L.out_features) * size_t(L.in_features) * dtype_size(L.dtype));
+  d.plan = o;
+  o = align256(o + 4 * size_t(nm_dense_plan_words(L.out_features, L.in_features)));
+  d.start = o;
+  o = align256(o + 4 * size_t(groups + 1));
+  d.crow = o;
+  o = align256(o + 4 * size_t(NB + 1));
+  d.col = o;
+  o = align256(o + 4 * size_t(NB * KB));
+  d.total = o;
+  return d;
+}
+
 int check_nm_layer(const slr_nm_layer* L) {
   if (!L) return fail(SLR_ERR_INVALID_ARGUMENT, "layer is NULL");
   if (L->dtype != SLR_F16 && L->dtype != SLR_BF16)
@@ -751,7 +787,8 @@ int slr_nm_compress(const void* S, int64_t N, int64_t K, int dtype, void* values
 size_t slr_nm_linear_workspace_size(const slr_nm_layer* layer, int64_t M) {
   if (check_nm_layer(layer) != SLR_OK || M < 0) return 0;
   const slr_layer lr = nm_lowrank_layer(*layer);
-  return slr_lrs_linear_workspace_size(&lr, M);
+  const size_t base = slr_lrs_linear_workspace_size(&lr, M);
+  return nm_dense_route(*layer, M) ? nm_dense_layout(*layer, base).total : base;
 }
 
 int slr_nm_linear_forward(const slr_nm_layer* layer, const void* x, int64_t ldx, void* y, int64_t ldy, int64_t M,
@@ -772,6 +809,42 @@ int slr_nm_linear_forward(const slr_nm_layer* layer, const void* x, int64_t ldx,
   if (rc) return rc;
   if (c.p.path != 1) return fail(SLR_ERR_UNSUPPORTED, "N:M layer: shapes outside the 16-bit kernels");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (nm_dense_route(L, M)) {
+    const NmDenseLayout d = nm_dense_layout(L, slr_lrs_linear_workspace_size(&lr, M));
+    uint8_t* w = static_cast<uint8_t*>(workspace);
+    RowblockArgs a;
+    a.x = x;
+    a.y = y;
+    a.H = c.ws;
+    a.ldh = c.p.ldh;
+    a.A = L.A;
+    a.B = L.B;
+    a.bias = L.bias;
+    a.crow = reinterpret_cast<const int32_t*>(w + d.crow);
+    a.col = reinterpret_cast<const int32_t*>(w + d.col);
+    a.values = w + d.blocks;
+    a.stage_plan = reinterpret_cast<const uint32_t*>(w + d.plan);
+    a.stage_start = reinterpret_cast<const int32_t*>(w + d.start);
+    a.nrows = L.out_features / 64;
+    a.M = M;
+    a.K = L.in_features;
+    a.N = L.out_features;
+    a.r = L.rank;
+    a.nnz = a.nrows * (L.in_features / 64);
+    a.ldx = ldx;
+    a.ldy = ldy;
+    a.bp = a.bq = 64;
+    a.dtype = L.dtype;
+    a.mode = MODE_FUSED;
+    if (workspace_bytes >= d.total && tc2_rowblock_supported(a)) {
+      rc = launch_nm_dense_blocks(L.values, L.meta, L.out_features, L.in_features, L.dtype, w + d.blocks,
+                                  reinterpret_cast<uint32_t*>(w + d.plan), reinterpret_cast<int32_t*>(w + d.start),
+                                  reinterpret_cast<int32_t*>(w + d.crow), reinterpret_cast<int32_t*>(w + d.col), s);
+      if (!rc) rc = run_lowrank(lr, c, s);
+      if (!rc) rc = launch_tc2_rowblock(a, false, s);
+      return rc;
+    }
+  }
   rc = run_lowrank(lr, c, s);
   if (rc) return rc;
   return launch_nm_combine(x, ldx, y, ldy, L.values, L.meta, L.A, c.ws, c.p.ldh, L.bias, M, L.out_features,

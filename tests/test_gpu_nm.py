@@ -130,3 +130,37 @@ def test_nm_full_size_matches_torch_fp32(cuda, T, parity_log):
     parity_log(f"nm24 T={T} 11008x4096 r512", y, ref)
     assert_16bit_close(y, ref)
     assert rms(ref) > 0
+
+
+@pytest.mark.parametrize("T", [255, 256, 1000])
+def test_nm_prefill_route(cuda, oracle, T):
+    """From 256 tokens (out, in and rank multiples of 64) S is unpacked per
+    call into full-density 64 x 64 blocks and the layer runs on the 2-SM
+    tensor-core combine: the workspace then holds the unpacked S, and the
+    result meets the same bound against the fp32 oracle as the mma.sp kernel's
+    below 256 tokens."""
+    import ctypes
+
+    from s_salaad_b200 import _lib
+
+    n, k, r = 512, 1024, 128
+    dtype = torch.bfloat16
+    g = torch.Generator().manual_seed(T)
+    S = sparse_2_4(n, k, seed=T, dtype=dtype)
+    A = (torch.randn(n, r, generator=g) * 0.02).to(dtype)
+    B = (torch.randn(r, k, generator=g) * 0.02).to(dtype)
+    bias = (torch.randn(n, generator=g) * 0.01).to(dtype)
+    values, meta = ops.nm_compress(S.to(cuda))
+    desc = ops.NmLayerDesc(values=values, meta=meta, A=A.to(cuda), B=B.to(cuda), bias=bias.to(cuda),
+                           in_features=k, out_features=n)
+    lib = _lib.load()
+    ws = int(lib.slr_nm_linear_workspace_size(ctypes.byref(desc.struct), T))
+    ws_h = int(lib.slr_nm_linear_workspace_size(ctypes.byref(desc.struct), 255))
+    if T >= 256:
+        assert ws >= ws_h + n * k * 2  # the unpacked S
+    x = workloads.tokens(T, k, seed=T, dtype=dtype)
+    y = desc.forward(x.to(cuda))
+    ref = oracle.nm_forward_f32(x.float(), A.float(), B.float(), S.float(), bias.float())
+    assert_16bit_close(y, ref)
+    # a second call reuses the workspace (the blocks and the schedule are rewritten)
+    assert torch.equal(desc.forward(x.to(cuda)), y)
