@@ -79,6 +79,8 @@ SMS_FOR_NCCL = int(os.environ.get("SLR_BENCH_NCCL_SMS", "16"))
 # N > 1: combine epilogues store y straight into every rank's y (peer memory)
 # when every rank's kernels support it; 0 = NCCL all-gather of y instead
 USE_PEERS = os.environ.get("SLR_BENCH_PEERS", "1") != "0"
+# ... and then all projections' combines in one launch of the 2-SM kernel; 0 = one launch each
+SET_PEERS = os.environ.get("SLR_BENCH_SET_PEERS", "1") != "0"
 L2_FLUSH_BYTES = 256 << 20  # > 126 MB L2
 
 
@@ -603,6 +605,13 @@ def main() -> None:
         # leave SMs to the NCCL all-gathers that overlap the next projections' kernels
         from s_salaad_b200 import _lib
         _lib.load().slr_set_sm_limit(_lib.load_sm_count() - SMS_FOR_NCCL)
+    # N > 1 with peer outputs: the combines of all projections in one launch of
+    # the 2-SM kernel (one signal slot, one wait) when they share its shape
+    set_peers = (pos is not None and SET_PEERS and T >= 256 and len(specs) <= 8
+                 and all(s.nnz > 0 and s.block_p in (32, 64) and (s.block_p, s.block_q) ==
+                         (specs[0].block_p, specs[0].block_q) for s in specs))
+    if set_peers:
+        from s_salaad_b200.shard import finish_set_peers, start_set_peers
     ys = ([po.y for po in pos] if pos is not None else
           [torch.empty(T, s.out_features, dtype=dtype, device=dev) for s in specs])
     # one GPU: the projections (independent inputs) run as one layer-set call
@@ -617,6 +626,7 @@ def main() -> None:
         """One forward of the layer set; ev = per-projection event triples."""
         if world > 1:
             handles = {}
+            hs = [None] * len(specs)  # H of each projection (set_peers)
             tp = T // world
             for r, idx in members.items():
                 grp = groups.get(r)
@@ -629,6 +639,20 @@ def main() -> None:
                         dist.all_gather_into_tensor(h, h[rank * rb:(rank + 1) * rb])
                     else:
                         grp.lowrank(xs[idx[0]])
+                if set_peers:
+                    # x*B^T only; the combines of all projections follow as one launch
+                    for j, i in enumerate(idx):
+                        L = layers[i]
+                        if ev is not None and (grp is None or j):
+                            ev[i][0].record(stream)
+                        if grp is None and L.desc is not None:
+                            L._lowrank(xs[i])
+                        if ev is not None:
+                            ev[i][1].record(stream)
+                            ev[i][2].record(stream)
+                        if L.desc is not None:
+                            hs[i] = grp.h_of(j, T) if grp is not None else L.h_address(T)
+                    continue
                 for j, i in enumerate(idx):
                     L = layers[i]
                     if pos is not None:
@@ -667,6 +691,13 @@ def main() -> None:
                     work = dist.all_gather_into_tensor(buf.view(-1), buf[rank].view(-1), group=L.group,
                                                        async_op=True)
                     handles[i] = (work, buf)
+            if set_peers:
+                launched = start_set_peers(layers, xs, pos, hs, pos[0])
+                if ev is not None:
+                    # the set's combine, charged to the last projection (its x*B^T ended just before)
+                    ev[len(specs) - 1][2].record(stream)
+                finish_set_peers(pos[0], launched)
+                return
             for i, L in enumerate(layers):
                 if pos is not None:
                     L.finish_peers(pos[i])
@@ -790,7 +821,7 @@ def main() -> None:
     pair_set = lset is not None and T >= 256 and all(
         s.nnz > 0 and s.block_p in (32, 64)
         and -(-s.out_features // s.block_p // (256 // s.block_p)) * -(-T // 128) >= 16 for s in specs)
-    comb_launches = 1 if pair_set else len(specs)
+    comb_launches = 1 if (pair_set or set_peers) else len(specs)
 
     # ------------------------------------------------- roofline (combine)
     P, pk_src = peaks()
@@ -825,8 +856,10 @@ def main() -> None:
         peak = P["bf16_tflops"]
         roof = {"bound": "tensor", "unit": "TFLOP/s", "algorithmic_per_step": comb_flops,
                 "kernel": ("combine (sparse + H*A^T + bias) of all projections of the set"
-                           + (" in one launch of the 2-SM pair kernel" if pair_set else ", one launch each")
-                           if lset is not None else "combine (sparse + H*A^T + bias; one launch per projection)")}
+                           + (" in one launch of the 2-SM pair kernel" if (pair_set or set_peers)
+                              else ", one launch each")
+                           + (", tiles stored into every rank's y" if set_peers else ""))
+                if (lset is not None or set_peers) else "combine (sparse + H*A^T + bias; one launch per projection)"}
     else:
         achieved = comb_bytes * K / comb_s / 1e9
         peak = P["hbm_gbs"]
@@ -859,8 +892,10 @@ def main() -> None:
         launches_per_step -= len(members[r]) - 1
     if lset is not None:
         launches_per_step = multi_launches(specs) if T < 128 else len(members) + comb_launches
+    if set_peers:
+        launches_per_step += 1 - sum(1 for i in range(len(specs)) if has_local[i])  # one combine, not one each
     if pos is not None:
-        launches_per_step += len(specs)  # the wait that ends each projection's call
+        launches_per_step += 1 if set_peers else len(specs)  # the wait(s) that end the call(s)
 
     # ------------------------------------------------------------- e2e
     x_host = {r: xin[r].cpu().pin_memory() for r in xin}
@@ -1033,8 +1068,10 @@ def main() -> None:
                 "config": {**config, "l2": "flushed between timed steps (256 MB written, then read back)",
                            "parallelism": (f"block-row shards x{world}, x*B^T "
                                            + ("split by tokens + NCCL all-gather of H" if world >= 4 else "on every rank")
-                                           + (", combine epilogues store y into every rank's y over NVLink (CUDA IPC)"
-                                              if pos is not None else ", NCCL all-gather of y")
+                                           + ((", the combines of all projections in one launch whose epilogue "
+                                               "stores y into every rank's y over NVLink (CUDA IPC)") if set_peers
+                                              else ", combine epilogues store y into every rank's y over NVLink "
+                                                   "(CUDA IPC)" if pos is not None else ", NCCL all-gather of y")
                                            + ", step replayed from a CUDA graph")
                            if world > 1 else ("1 GPU, the projections (independent inputs) as one layer-set call, "
                                               "step replayed from a CUDA graph"),

@@ -36,7 +36,7 @@
 extern "C" {
 #endif
 
-#define SLR_ABI_VERSION 7
+#define SLR_ABI_VERSION 8
 
 #if defined(__GNUC__)
 #define SLR_API __attribute__((visibility("default")))
@@ -537,6 +537,22 @@ SLR_API int slr_lrs_linear_group_combine_peers(const slr_layer* layers, int n, i
                                                const void* x, int64_t ldx, int64_t ldy, int64_t M,
                                                void* workspace, size_t workspace_bytes,
                                                const slr_peers* peers, void* stream);
+/* The combines of n (<= 8) layers in ONE launch of the 2-SM kernel, every
+ * output tile stored into every rank's y: layer i's into peers[i].y[p].  H[i]
+ * is layer i's H = x·Bᵀ [M, ldh[i]] (0 = round_up(rank, 64)) from its low-rank
+ * phase, wherever the caller keeps it (a layer's or a group's workspace, rows
+ * gathered from other ranks).  The launch's arrival and completion signals
+ * use sync's signal slots (sync.y is not read); end the call with
+ * slr_peers_wait(sync, 0, stream).  A rank with no rows in any of the layers
+ * calls slr_peers_wait(sync, 1, stream) instead (SLR_ERR_INVALID_ARGUMENT
+ * here).  SLR_ERR_UNSUPPORTED when the layers cannot share one launch (each
+ * on the 2-SM kernel with a column schedule, one block shape, M and dtype).
+ * Every rank must make the calls with the same sync slot in the same order.
+ * No reference counterpart. */
+SLR_API int slr_lrs_linear_multi_combine_peers(const slr_layer* layers, int n, const void* const* x,
+                                               const int64_t* ldx, const void* const* H, const int64_t* ldh,
+                                               const int64_t* ldy, int64_t M, const slr_peers* peers,
+                                               const slr_peers* sync, void* stream);
 /* Ends a call: returns (on the stream) once every rank's stores into this
  * rank's y are visible. */
 SLR_API int slr_peers_wait(const slr_peers* peers, int empty_shard, void* stream);

@@ -13,7 +13,7 @@ from pathlib import Path
 LIB_PATH = Path(__file__).resolve().parent / "libslr_b200.so"
 
 # slr_status codes (include/slr_b200.h)
-ABI_VERSION = 7  # SLR_ABI_VERSION of include/slr_b200.h
+ABI_VERSION = 8  # SLR_ABI_VERSION of include/slr_b200.h
 SLR_OK = 0
 # slr_layer.flags bits (include/slr_b200.h)
 SLR_FLAG_PAIR_MMA = 1
@@ -57,6 +57,7 @@ EXPORTED = (
     "slr_lrs_linear_peers_supported",
     "slr_lrs_linear_combine_peers",
     "slr_lrs_linear_group_combine_peers",
+    "slr_lrs_linear_multi_combine_peers",
     "slr_peers_wait",
     "slr_set_wait_limit_ns",
     "slr_lrs_linear_multi_workspace_size",
@@ -164,6 +165,9 @@ _SIGS = {
                                       ctypes.POINTER(SlrPeers), vp], i32),
     "slr_lrs_linear_group_combine_peers": ([ctypes.POINTER(SlrLayer), i32, i32, vp, i64, i64, i64, vp, sz,
                                             ctypes.POINTER(SlrPeers), vp], i32),
+    "slr_lrs_linear_multi_combine_peers": ([ctypes.POINTER(SlrLayer), i32, ctypes.POINTER(vp), ctypes.POINTER(i64),
+                                            ctypes.POINTER(vp), ctypes.POINTER(i64), ctypes.POINTER(i64), i64,
+                                            ctypes.POINTER(SlrPeers), ctypes.POINTER(SlrPeers), vp], i32),
     "slr_peers_wait": ([ctypes.POINTER(SlrPeers), i32, vp], i32),
     "slr_set_wait_limit_ns": ([ctypes.c_uint64], i32),
     "slr_lrs_linear_multi_workspace_size": ([ctypes.POINTER(SlrLayer), i32, i64], sz),

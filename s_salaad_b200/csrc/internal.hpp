@@ -142,6 +142,11 @@ int launch_tc_rowblock(const RowblockArgs& a, bool pdl, cudaStream_t s);
 bool tc2_rowblock_supported(const RowblockArgs& a);  // 2-SM pairs, M >= 256, bp 32/64
 // peers: also store every output tile into the other ranks' y (null = local only).
 int launch_tc2_rowblock(const RowblockArgs& a, bool pdl, cudaStream_t s, const PeerArgs* peers = nullptr);
+// The combines of n layers in one launch, every output tile also stored into
+// every rank's y: layer i's into peers[i].y[p]; the launch's arrival and
+// completion signals are sync's.
+int launch_tc2_rowblock_group_peers(const RowblockArgs* as, int n, const PeerArgs* peers, const PeerArgs& sync,
+                                    cudaStream_t s);
 // Up to kMaxLaunchLayers layers in one launch of the pair kernel (one
 // persistent schedule, one tail): every layer sparse with a column schedule,
 // one block shape, token count, dtype and mode; local y only.

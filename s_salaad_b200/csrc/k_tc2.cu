@@ -60,17 +60,18 @@ struct Tc2Args {
   int xgrp;               // layers of a launch that read the same x share it
 };
 
-// world > 1: TMA store maps of every rank's y at this rank's columns
-// ([M, N] of this layer, box block_p x 32 rows); m[me] is the local y.
-struct YMaps {
-  CUtensorMap m[kMaxRanks];
-};
 
 // Several layers in one launch (same block shape, token count and mode):
 // their work items are numbered one layer after the other, item0[l] being
 // layer l's first, and dealt to the pairs as one list, so the launch has one
 // persistent-schedule tail instead of one per layer.
 constexpr int kTc2Layers = kMaxLaunchLayers;
+// world > 1: TMA store maps of every rank's y at this rank's columns, per
+// layer of the launch ([M, N] of the layer, box block_p x 32 rows); m[l][me]
+// is layer l's local y.
+struct YMaps {
+  CUtensorMap m[kTc2Layers][kMaxRanks];
+};
 // Row groups of a launch that can be put in one heaviest-first order in
 // shared memory at the start of the kernel.
 constexpr int kOrderCap = 512;
@@ -630,7 +631,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q = warp & 3;
     const uint32_t lane_base = uint32_t(32 * q) << 16;
     const int row = 32 * q + lane;
-    const Tc2Args& a0 = set.L[0];  // the peer epilogue runs in one-layer launches only
+    const Tc2Args& a0 = set.L[0];  // its peer args carry the launch's signal slots
     const uint32_t te0 = mapa(smem_u32(&tempty[0]), 0);
     constexpr int kCpr = BP / 8;  // 16-byte chunks of a row's BP outputs
     // 16-byte chunk c of staging row r, as TMA's 128B (BP 64) / 64B (BP 32) swizzle places it
@@ -750,7 +751,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int p = 0; p < kMaxRanks; ++p)
               if (p < world && (p == a0.peer.me || peer_live))
-                tma_store_2d(&ym.m[p], stage_w, br * BP, int(tok0));
+                tma_store_2d(&ym.m[li][p], stage_w, br * BP, int(tok0));
             bulk_commit();
           }
         }
@@ -907,7 +908,7 @@ int launch_tc2_rowblock(const RowblockArgs& a, bool pdl, cudaStream_t s, const P
     set.L[0].peer = *peers;
     // TMA store maps of every rank's y at this rank's columns: [M, N], box bp x 32 rows
     for (int p = 0; p < peers->world; ++p) {
-      rc = make_tmap_2d(&ym.m[p], peers->y[p], a.dtype, uint64_t(a.N), uint64_t(a.M), uint64_t(a.ldy) * 2,
+      rc = make_tmap_2d(&ym.m[0][p], peers->y[p], a.dtype, uint64_t(a.N), uint64_t(a.M), uint64_t(a.ldy) * 2,
                         uint32_t(a.bp), 32u);
       if (rc) return rc;
     }
@@ -948,6 +949,41 @@ int launch_tc2_rowblock_group(const RowblockArgs* as, int n, bool pdl, cudaStrea
   if (set.item0[n] == 0) return SLR_OK;
   const YMaps ym{};
   return dispatch_set(as[0], as[0].bq, maps, set, ym, pdl, s);
+}
+
+int launch_tc2_rowblock_group_peers(const RowblockArgs* as, int n, const PeerArgs* peers, const PeerArgs& sync,
+                                    cudaStream_t s) {
+  if (!tc2_group_compatible(as, n)) return fail(SLR_ERR_UNSUPPORTED, "2-SM path: layers cannot share one launch");
+  if (sync.world < 2) return fail(SLR_ERR_INVALID_ARGUMENT, "peers: world must be >= 2");
+  if (as[0].M <= 0) return SLR_OK;
+  Tc2Maps maps{};
+  Tc2Set set{};
+  YMaps ym{};
+  set.n = n;
+  set.item0[0] = 0;
+  for (int i = 0; i < n; ++i) {
+    int rc = fill_tc2_layer(as[i], maps, set, i);
+    if (rc) return rc;
+    set.item0[i + 1] = set.item0[i] + set.L[i].n_groups * set.L[i].n_mtiles;
+    set.L[i].xgrp = i;
+    for (int j = 0; j < i; ++j)
+      if (as[j].x == as[i].x) {
+        set.L[i].xgrp = set.L[j].xgrp;
+        break;
+      }
+    // the launch's signals are sync's; layer i's tiles go to every rank's y of layer i
+    set.L[i].peer = sync;
+    for (int p = 0; p < sync.world; ++p) {
+      set.L[i].peer.y[p] = peers[i].y[p];
+      rc = make_tmap_2d(&ym.m[i][p], peers[i].y[p], as[i].dtype, uint64_t(as[i].N), uint64_t(as[i].M),
+                        uint64_t(as[i].ldy) * 2, uint32_t(as[i].bp), 32u);
+      if (rc) return rc;
+    }
+  }
+  if (set.item0[n] == 0)
+    return fail(SLR_ERR_INVALID_ARGUMENT, "peers: no rows of these layers on this rank (end the call with the "
+                                          "empty-shard wait instead)");
+  return dispatch_set(as[0], as[0].bq, maps, set, ym, false, s);
 }
 
 int read_and_clear_status_tc2(unsigned* out) {

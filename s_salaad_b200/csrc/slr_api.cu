@@ -1173,6 +1173,41 @@ int slr_lrs_linear_group_combine_peers(const slr_layer* layers, int n, int i, co
   return launch_tc2_rowblock(c.a, false, static_cast<cudaStream_t>(stream), &pa);
 }
 
+int slr_lrs_linear_multi_combine_peers(const slr_layer* layers, int n, const void* const* x, const int64_t* ldx,
+                                       const void* const* H, const int64_t* ldh, const int64_t* ldy, int64_t M,
+                                       const slr_peers* peers, const slr_peers* sync, void* stream) {
+  if (!layers || !x || !peers || !sync || n < 1 || n > kMaxLaunchLayers)
+    return fail(SLR_ERR_INVALID_ARGUMENT, "bad arguments (1.." + std::to_string(kMaxLaunchLayers) + " layers)");
+  PeerArgs ps;
+  int rc = to_peer_args(sync, ps);
+  if (rc) return rc;
+  PeerArgs pa[kMaxLaunchLayers];
+  RowblockArgs as[kMaxLaunchLayers];
+  for (int i = 0; i < n; ++i) {
+    rc = to_peer_args(&peers[i], pa[i]);
+    if (rc) return rc;
+    if (pa[i].world != ps.world || pa[i].me != ps.me)
+      return fail(SLR_ERR_INVALID_ARGUMENT, "peers: world or rank differs between the layers and sync");
+    const int64_t lx = (ldx && ldx[i]) ? ldx[i] : layers[i].in_features;
+    const int64_t ly = (ldy && ldy[i]) ? ldy[i] : layers[i].out_features;
+    FwdCall c;
+    rc = prepare_forward(&layers[i], x[i], lx, pa[i].y[pa[i].me], ly, M, nullptr, 0, true, c, false);
+    if (rc) return rc;
+    if (layers[i].rank > 0) {
+      const int64_t lh = (ldh && ldh[i]) ? ldh[i] : round_up(layers[i].rank, 64);
+      if (!H || !H[i] || !aligned16(H[i]) || lh < layers[i].rank || lh % 8)
+        return fail(SLR_ERR_INVALID_ARGUMENT, "H of layer " + std::to_string(i) +
+                                                  ": NULL, not 16-byte aligned, or ldh < rank / not a multiple of 8");
+      c.a.H = H[i];
+      c.a.ldh = lh;
+    }
+    rc = check_peer_call(layers[i], c, c.a.ldy, M);
+    if (rc) return rc;
+    as[i] = c.a;
+  }
+  return launch_tc2_rowblock_group_peers(as, n, pa, ps, static_cast<cudaStream_t>(stream));
+}
+
 int slr_peers_wait(const slr_peers* peers, int empty_shard, void* stream) {
   PeerArgs pa;
   int rc = to_peer_args(peers, pa);

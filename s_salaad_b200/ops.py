@@ -400,6 +400,17 @@ class LayerGroup:
         esize = torch.finfo(self.dtype).bits // 8
         return sum((d.struct.rank + 63) // 64 * 64 for d in self.descs) * esize
 
+    def h_of(self, i: int, M: int) -> tuple[int, int]:
+        """(device address, row stride in elements) of layer i's H after
+        :meth:`lowrank` or :meth:`lowrank_rows` on M >= 128 tokens: its
+        columns of the group H [M, sum of round_up(rank, 64)] at the start of
+        the workspace (the layout of the tensor-core path)."""
+        if M < 128 or self.dtype == torch.float32:
+            raise ValueError("the shared-H layout is the 16-bit tensor-core path's (M >= 128)")
+        esize = torch.finfo(self.dtype).bits // 8
+        widths = [(d.struct.rank + 63) // 64 * 64 for d in self.descs]
+        return self.workspace(M).data_ptr() + sum(widths[:i]) * esize, sum(widths)
+
     def lowrank_rows(self, x2: torch.Tensor, row0: int, rows: int) -> torch.Tensor:
         """Phase 1 for tokens [row0, row0 + rows) of x2 only, written into their
         rows of the group H of all x2.shape[0] tokens (that layout depends on

@@ -211,10 +211,54 @@ class ShardedLayer(ShardPlan):
                 torch.cuda.current_stream(self.device).cuda_stream)
         _lib.check(rc, "lrs_linear_combine_peers")
 
+    def h_address(self, T: int) -> tuple[int, int] | None:
+        """(device address, row stride) of the H that :meth:`_lowrank` leaves
+        in this rank's layer workspace for T tokens; None without rows or rank."""
+        if self.desc is None or self.rank_r == 0:
+            return None
+        return self.desc.workspace(T).data_ptr(), (self.rank_r + 63) // 64 * 64
+
     def finish_peers(self, po: "PeerOutputs") -> torch.Tensor:
         """Wait (on the stream) until every rank's columns are in po.y."""
         po.wait(empty_shard=self.desc is None)
         return po.y
+
+
+def start_set_peers(layers: list[ShardedLayer], xs: list[torch.Tensor], pos: list["PeerOutputs"],
+                    hs: list[tuple[int, int] | None], sync: "PeerOutputs") -> bool:
+    """The combines of a set of sharded layers (after their x·Bᵀ phases) in
+    ONE launch of the 2-SM kernel, every output tile stored into every rank's
+    y (layer i's into ``pos[i].y``); the launch's arrival and completion
+    signals use ``sync``'s slot (``slr_lrs_linear_multi_combine_peers``).
+    ``hs[i]`` is (address, row stride) of layer i's H (:meth:`ShardedLayer.h_address`,
+    :meth:`s_salaad_b200.ops.LayerGroup.h_of`).  Returns False, launching
+    nothing, when this rank holds no rows of any of the layers.  Every rank
+    calls it with the same layers and ``sync``, in the same order, and ends the
+    call with :func:`finish_set_peers`."""
+    idx = [i for i, L in enumerate(layers) if L.desc is not None]
+    if not idx:
+        return False
+    n = len(idx)
+    T = xs[idx[0]].shape[0]
+    structs = (_lib.SlrLayer * n)(*[layers[i].desc.struct for i in idx])
+    xp = (ctypes.c_void_p * n)(*[xs[i].data_ptr() for i in idx])
+    lx = (ctypes.c_int64 * n)(*[ops.LayerDesc._ld(xs[i]) for i in idx])
+    hp = (ctypes.c_void_p * n)(*[hs[i][0] if hs[i] else None for i in idx])
+    lh = (ctypes.c_int64 * n)(*[hs[i][1] if hs[i] else 0 for i in idx])
+    ly = (ctypes.c_int64 * n)(*[pos[i].ldy for i in idx])
+    ps = (_lib.SlrPeers * n)(*[pos[i].struct for i in idx])
+    with ops._DeviceGuard(sync.device):
+        rc = _lib.load().slr_lrs_linear_multi_combine_peers(
+            structs, n, xp, lx, hp, lh, ly, T, ps, ctypes.byref(sync.struct),
+            torch.cuda.current_stream(sync.device).cuda_stream)
+    _lib.check(rc, "lrs_linear_multi_combine_peers")
+    return True
+
+
+def finish_set_peers(sync: "PeerOutputs", launched: bool) -> None:
+    """Ends a :func:`start_set_peers` call: once it returns (on the stream)
+    every rank's tiles of every layer of the set are in this rank's y."""
+    sync.wait(empty_shard=not launched)
 
 
 def all_ranks(flag: bool, device, group=None) -> bool:

@@ -70,6 +70,52 @@ def check_peer_outputs(rank: int, world: int, dev) -> int:
     return bad
 
 
+def check_set_peers(rank: int, world: int, dev, x, grp, shards, refs) -> int:
+    """q/k/v (one group, one H) and o_proj (its own input and H) of cfg4: the
+    four combines as ONE launch storing into every rank's y, signals on the
+    first layer's slot; twice, each equal to the single-GPU forward bit for bit."""
+    from s_salaad_b200.shard import PeerOutputs, ShardedLayer, all_ranks, finish_set_peers, start_set_peers
+
+    T = x.shape[0]
+    s_o = workloads.layer_set("cfg4")[3]
+    t = s_o.tensors(dev, torch.bfloat16)
+    x_o = workloads.tokens(T, s_o.in_features, seed=6, device=dev, dtype=torch.bfloat16)
+    order = torch.from_numpy(ops.plan_row_order(s_o.crow.astype(np.int32))).to(dev)
+    full = ops.LayerDesc(A=t["A"], B=t["B"], bias=t["bias"], crow=t["S_crow"], col=t["S_col"],
+                         values=t["S_values"], row_order=order, in_features=s_o.in_features,
+                         out_features=s_o.out_features, block_p=s_o.block_p, block_q=s_o.block_q)
+    ref_o = full.forward(x_o)
+    sh_o = ShardedLayer(t, s_o.crow, in_features=s_o.in_features, out_features=s_o.out_features,
+                        block_p=s_o.block_p, block_q=s_o.block_q, rank=rank, world=world)
+    layers = list(shards) + [sh_o]
+    xs = [x, x, x, x_o]
+    wants = list(refs) + [ref_o]
+    if not all_ranks(all(L.peers_supported(xi) for L, xi in zip(layers, xs)), dev):
+        print(f"rank {rank}/{world} set peers: not supported on every rank", flush=True)
+        return 1
+    pos = [PeerOutputs(L, T, torch.bfloat16, dev) for L in layers]
+    bad = 0
+    for call in range(2):
+        for po in pos:
+            po.y.fill_(float("nan"))
+        grp.lowrank(x)
+        sh_o._lowrank(x_o)
+        hs = [grp.h_of(j, T) for j in range(3)] + [sh_o.h_address(T)]
+        launched = start_set_peers(layers, xs, pos, hs, pos[0])
+        finish_set_peers(pos[0], launched)
+        for j, (po, ref) in enumerate(zip(pos, wants)):
+            err = float((po.y.float() - ref.float()).abs().nan_to_num(float("inf")).max())
+            ok = err == 0.0
+            bad += 0 if ok else 1
+            print(f"rank {rank}/{world} set peers call {call} cfg4[{j}] T={T} max|diff|={err:.3e} "
+                  f"{'ok' if ok else 'MISMATCH'}", flush=True)
+    torch.cuda.synchronize()
+    dist.barrier()
+    for po in pos:
+        po.close()
+    return bad
+
+
 def main() -> int:
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     local = int(os.environ.get("LOCAL_RANK", rank))
@@ -150,6 +196,7 @@ def main() -> int:
     else:
         print(f"rank {rank}/{world} grouped peers: not supported on every rank", flush=True)
         bad += 1
+    bad += check_set_peers(rank, world, dev, x, grp, shards, refs)
     bad += check_peer_outputs(rank, world, dev)
     flag = torch.tensor([bad], device=dev)
     dist.all_reduce(flag)

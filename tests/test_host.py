@@ -32,7 +32,7 @@ def test_library_exports_every_declared_symbol():
     for name in _declared_symbols():
         assert name in exported, name
         assert getattr(lib, name) is not None
-    assert lib.slr_abi_version() == _lib.ABI_VERSION == 7
+    assert lib.slr_abi_version() == _lib.ABI_VERSION == 8
 
 
 def test_library_is_built_for_sm100a():
