@@ -81,6 +81,10 @@ SMS_FOR_NCCL = int(os.environ.get("SLR_BENCH_NCCL_SMS", "16"))
 USE_PEERS = os.environ.get("SLR_BENCH_PEERS", "1") != "0"
 # ... and then all projections' combines in one launch of the 2-SM kernel; 0 = one launch each
 SET_PEERS = os.environ.get("SLR_BENCH_SET_PEERS", "1") != "0"
+# N >= 4: x*B^T of a group split by tokens over the ranks + NCCL all-gather of H (1); the
+# default computes it whole on every rank, which measured faster (cfg4, 4 x B200: 0.19 against
+# 0.35 ms per step: the collective's latency exceeds the GEMM time it saves)
+SPLIT_H = os.environ.get("SLR_BENCH_SPLIT_H", "0") == "1"
 L2_FLUSH_BYTES = 256 << 20  # > 126 MB L2
 
 
@@ -633,7 +637,7 @@ def main() -> None:
                 if grp is not None:
                     if ev is not None:
                         ev[idx[0]][0].record(stream)
-                    if world >= 4 and T % world == 0 and tp >= 128:
+                    if SPLIT_H and world >= 4 and T % world == 0 and tp >= 128:
                         h = grp.lowrank_rows(xs[idx[0]], rank * tp, tp)
                         rb = tp * grp.h_row_bytes()
                         dist.all_gather_into_tensor(h, h[rank * rb:(rank + 1) * rb])
@@ -1067,7 +1071,8 @@ def main() -> None:
                 "data": "synthetic (seeded generators; random-init weights; no dataset)",
                 "config": {**config, "l2": "flushed between timed steps (256 MB written, then read back)",
                            "parallelism": (f"block-row shards x{world}, x*B^T "
-                                           + ("split by tokens + NCCL all-gather of H" if world >= 4 else "on every rank")
+                                           + ("split by tokens + NCCL all-gather of H" if (SPLIT_H and world >= 4)
+                                              else "on every rank")
                                            + ((", the combines of all projections in one launch whose epilogue "
                                                "stores y into every rank's y over NVLink (CUDA IPC)") if set_peers
                                               else ", combine epilogues store y into every rank's y over NVLink "
