@@ -568,9 +568,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* adst = smem + slot * STAGE;
           mbar_arrive_expect_tx(&full[slot], STAGE);
           tma_load_2d(adst, &tm_x, s * 64, mt * kTileM, &full[slot]);
-#pragma unroll
-          for (int j = 0; j < BN / 64; ++j)
-            tma_load_2d(adst + A_BYTES + j * 8192, tm_b, s * 64, nl * BN + j * 64, &full[slot]);
+          // the whole BN x 64 tile of B as one box (one TMA issue instead of
+          // BN / 64: this thread's per-box issue cost bounds the kernel)
+          tma_load_2d(adst + A_BYTES, tm_b, s * 64, nl * BN, &full[slot]);
         }
       }
     }
@@ -761,8 +761,6 @@ int launch_tc_dense_group(const void* x, int64_t ldx, const void* const* Bs, con
     total += cols[i];
     all256 = all256 && cols[i] % 256 == 0;
     all128 = all128 && cols[i] % 128 == 0;
-    rc = make_tmap_2d(&maps.b[i], Bs[i], dtype, uint64_t(K), uint64_t(rs[i]), uint64_t(K) * 2, 64u, 64u);
-    if (rc) return rc;
   }
   if (total > ldh) return fail(SLR_ERR_WORKSPACE, "tc_dense: H row narrower than the group's columns");
   const int n_mtiles = int(ceil_div(M, kTileM));
@@ -771,6 +769,11 @@ int launch_tc_dense_group(const void* x, int64_t ldx, const void* const* Bs, con
   int bn = 64;
   if (all256 && int64_t(n_mtiles) * (total / 256) * 2 >= num_sms()) bn = 256;
   else if (all128) bn = 128;
+  // B tiles of bn rows (rank columns of H) x 64 k, one box each; rows past r_i read as zeros
+  for (int i = 0; i < n; ++i) {
+    rc = make_tmap_2d(&maps.b[i], Bs[i], dtype, uint64_t(K), uint64_t(rs[i]), uint64_t(K) * 2, 64u, uint32_t(bn));
+    if (rc) return rc;
+  }
   DenseArgs k{H, M, ldh, n_mtiles, int(total / bn), int(ceil_div(K, 64)), n, {0}};
   for (int i = 0; i < n; ++i) k.seg_nt[i + 1] = k.seg_nt[i] + int(cols[i] / bn);
   const int items = k.n_mtiles * k.n_ntiles;
