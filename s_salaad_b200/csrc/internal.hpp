@@ -157,10 +157,23 @@ bool tc_dense_supported(const void* x, int64_t ldx, const void* B, int64_t K, in
 // before its first load).
 int launch_tc_dense(const void* x, int64_t ldx, const void* B, void* H, int64_t M, int64_t K, int64_t r,
                     int64_t ldh, int dtype, cudaStream_t s, bool pdl = false);
-// x · [B_0; ...; B_{n-1}]ᵀ (n <= 4, same K) into H [M, ldh]: segment i takes
+// x · [B_0; ...; B_{n-1}]ᵀ (n <= 8, same K) into H [M, ldh]: segment i takes
 // columns [sum_{j<i} round_up(r_j, 64), + round_up(r_i, 64)).
 int launch_tc_dense_group(const void* x, int64_t ldx, const void* const* Bs, const int64_t* rs, int n,
                           void* H, int64_t M, int64_t K, int64_t ldh, int dtype, cudaStream_t s, bool pdl = false);
+// One x·Bᵀ product of a launch: H [M, ldh] (its first round_up(r, 64) columns)
+// = x [M, K] · B [r, K]ᵀ.
+struct DenseSeg {
+  const void* x;
+  int64_t ldx, K;
+  const void* B;
+  int64_t r;
+  void* H;
+  int64_t ldh;
+};
+// Up to kMaxLaunchLayers products (several inputs, each its own K and H) in
+// one launch; each H element is the one launch_tc_dense computes.
+int launch_tc_dense_multi(const DenseSeg* segs, int n, int64_t M, int dtype, cudaStream_t s, bool pdl = false);
 
 // ---- N:M 2:4 + low-rank layer (16-bit): packer and fused combine (mma.sp).
 int launch_nm_pack(const void* S, int64_t N, int64_t K, int dtype, void* values, uint32_t* meta, int* bad,

@@ -40,7 +40,7 @@ using namespace tc;
 __device__ unsigned g_status_tc = 0;
 
 constexpr int kThreads = 192;        // tc_dense_kernel
-constexpr int kMaxSeg = kMaxGroupLayers;  // weight matrices per grouped x*B^T
+constexpr int kMaxSeg = kMaxLaunchLayers;  // weight matrices per x*B^T launch
 constexpr int kRowThreads = 288;     // tc_rowblock_kernel: warps 0, 6, 7, 8 load operands
 constexpr int kProd2 = 6;            // first of the extra TMA warps
 constexpr int kProducers = 4;        // TMA warps working from a column schedule
@@ -485,24 +485,29 @@ __global__ void __launch_bounds__(kRowThreads, 1)
 
 // ---------------------------------------------------------- dense GEMM --
 
-// H[M, ldh] = x · [B_0; B_1; ...]ᵀ: up to kMaxSeg weight matrices that share
-// x (the q/k/v or gate/up projections of a decoder layer) are one GEMM; the
-// N tiles of segment s are [seg_nt[s], seg_nt[s+1]) and read B_s.
+// H_s[M, ldh_s] = x_s · B_sᵀ for up to kMaxSeg segments in one launch: the
+// weight matrices that share an x (the q/k/v or gate/up projections of a
+// decoder layer) and the layers with their own x, each segment with its own
+// K and H.  The N tiles of segment s are [seg_nt[s], seg_nt[s+1]); an H
+// element is the same dot product in the same k order whatever the launch.
 struct DenseArgs {
-  void* H;
-  int64_t M, ldh;
-  int n_mtiles, n_ntiles, n_k;
+  int64_t M;
+  int n_mtiles, n_ntiles;
   int n_seg;
   int seg_nt[kMaxSeg + 1];
+  int seg_nk[kMaxSeg];     // 64-wide k chunks
+  int seg_x[kMaxSeg];      // x map of the segment
+  void* seg_H[kMaxSeg];    // the segment's first H column
+  int64_t seg_ldh[kMaxSeg];
 };
 struct DenseMaps {
   CUtensorMap b[kMaxSeg];
+  CUtensorMap x[kMaxSeg];
 };
 
 template <int BN, typename TI>
 __global__ void __launch_bounds__(kThreads, 1)
-    tc_dense_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ DenseMaps maps,
-                    const DenseArgs a) {
+    tc_dense_kernel(const __grid_constant__ DenseMaps maps, const __grid_constant__ DenseArgs a) {
   constexpr uint32_t A_BYTES = kTileM * 128, B_BYTES = BN * 128;
   constexpr uint32_t STAGE = A_BYTES + B_BYTES;
   constexpr int STAGES = (196 * 1024) / STAGE > 8 ? 8 : (196 * 1024) / STAGE;
@@ -549,8 +554,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      tma_prefetch_desc(&tm_x);
-      for (int sg = 0; sg < a.n_seg; ++sg) tma_prefetch_desc(&maps.b[sg]);
+      for (int sg = 0; sg < a.n_seg; ++sg) {
+        tma_prefetch_desc(&maps.b[sg]);
+        tma_prefetch_desc(&maps.x[a.seg_x[sg]]);
+      }
 
       uint32_t g = 0;
       for (int item = blockIdx.x; item < n_items && !s_abort; item += gridDim.x) {
@@ -558,8 +565,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         int sg = 0;
         while (sg + 1 < a.n_seg && nt >= a.seg_nt[sg + 1]) ++sg;
         const CUtensorMap* tm_b = &maps.b[sg];
+        const CUtensorMap* tm_x = &maps.x[a.seg_x[sg]];
         const int nl = nt - a.seg_nt[sg];
-        for (int s = 0; s < a.n_k; ++s, ++g) {
+        for (int s = 0; s < a.seg_nk[sg]; ++s, ++g) {
           const uint32_t slot = g % STAGES, ph = (g / STAGES) & 1;
           if (!mbar_wait(&empty[slot], ph ^ 1)) {
             tc_timeout(&s_abort);
@@ -567,7 +575,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           uint8_t* adst = smem + slot * STAGE;
           mbar_arrive_expect_tx(&full[slot], STAGE);
-          tma_load_2d(adst, &tm_x, s * 64, mt * kTileM, &full[slot]);
+          tma_load_2d(adst, tm_x, s * 64, mt * kTileM, &full[slot]);
           // the whole BN x 64 tile of B as one box (one TMA issue instead of
           // BN / 64: this thread's per-box issue cost bounds the kernel)
           tma_load_2d(adst + A_BYTES, tm_b, s * 64, nl * BN, &full[slot]);
@@ -585,8 +593,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_after();
         const uint32_t d = tmem + buf * BN;
+        int sg = 0;
+        while (sg + 1 < a.n_seg && item / a.n_mtiles >= a.seg_nt[sg + 1]) ++sg;
         uint32_t acc = 0;
-        for (int s = 0; s < a.n_k; ++s, ++g) {
+        for (int s = 0; s < a.seg_nk[sg]; ++s, ++g) {
           const uint32_t slot = g % STAGES, ph = (g / STAGES) & 1;
           if (!mbar_wait(&full[slot], ph)) {
             tc_timeout(&s_abort);
@@ -608,10 +618,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     const int q = warp & 3;
     const int row = 32 * q + lane;
-    TI* __restrict__ H = static_cast<TI*>(a.H);
     uint32_t it = 0;
     for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++it) {
       const int mt = item % a.n_mtiles, nt = item / a.n_mtiles;
+      int sg = 0;
+      while (sg + 1 < a.n_seg && nt >= a.seg_nt[sg + 1]) ++sg;
+      TI* __restrict__ H = static_cast<TI*>(a.seg_H[sg]);
+      const int64_t ldh = a.seg_ldh[sg];
+      const int nl = nt - a.seg_nt[sg];
       const uint32_t buf = it & 1, tph = (it >> 1) & 1;
       if (!mbar_wait_warp(&tfull[buf], tph, 256)) {
         if (lane == 0) tc_timeout(&s_abort);
@@ -628,7 +642,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int j = 0; j < 8; ++j) p[j] = pack2(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]), (TI*)nullptr);
         if (tok < a.M) {
-          uint4* hr = reinterpret_cast<uint4*>(H + tok * a.ldh + int64_t(nt) * BN + c0);
+          uint4* hr = reinterpret_cast<uint4*>(H + tok * ldh + int64_t(nl) * BN + c0);
           hr[0] = make_uint4(p[0], p[1], p[2], p[3]);
           hr[1] = make_uint4(p[4], p[5], p[6], p[7]);
         }
@@ -744,38 +758,62 @@ bool tc_dense_supported(const void* x, int64_t ldx, const void* B, int64_t K, in
   return dtype != SLR_F32 && r >= 64 && K >= 64 && K % 8 == 0 && ldx % 8 == 0 && aligned16(x) && aligned16(B);
 }
 
-int launch_tc_dense_group(const void* x, int64_t ldx, const void* const* Bs, const int64_t* rs, int n,
-                          void* H, int64_t M, int64_t K, int64_t ldh, int dtype, cudaStream_t s, bool pdl) {
+int launch_tc_dense_multi(const DenseSeg* segs, int n, int64_t M, int dtype, cudaStream_t s, bool pdl) {
   if (M <= 0 || n <= 0) return SLR_OK;
-  if (n > kMaxSeg) return fail(SLR_ERR_UNSUPPORTED, "tc_dense: too many weight matrices in one group");
-  CUtensorMap tx{};
+  if (n > kMaxSeg) return fail(SLR_ERR_UNSUPPORTED, "tc_dense: too many weight matrices in one launch");
+  // segments with the longest K first (the heaviest items lead the deal); an
+  // H element does not depend on the order
+  int ord[kMaxSeg];
+  for (int i = 0; i < n; ++i) ord[i] = i;
+  std::stable_sort(ord, ord + n, [&](int a, int b) { return segs[a].K > segs[b].K; });
   DenseMaps maps{};
-  int rc = make_tmap_2d(&tx, x, dtype, uint64_t(K), uint64_t(M), uint64_t(ldx) * 2, 64u, uint32_t(kTileM));
-  if (rc) return rc;
-  // Each segment's columns [r_s rounded up to 64) of H; the tile width must divide every one.
+  DenseArgs k{};
+  k.M = M;
+  k.n_mtiles = int(ceil_div(M, kTileM));
+  k.n_seg = n;
+  // each segment's columns: r_s rounded up to 64; the tile width must divide every one
   int64_t cols[kMaxSeg];
   int64_t total = 0;
   bool all256 = true, all128 = true;
   for (int i = 0; i < n; ++i) {
-    cols[i] = round_up(rs[i], 64);
+    const DenseSeg& g = segs[ord[i]];
+    cols[i] = round_up(g.r, 64);
     total += cols[i];
     all256 = all256 && cols[i] % 256 == 0;
     all128 = all128 && cols[i] % 128 == 0;
+    if (cols[i] > g.ldh) return fail(SLR_ERR_WORKSPACE, "tc_dense: H row narrower than the layer's columns");
   }
-  if (total > ldh) return fail(SLR_ERR_WORKSPACE, "tc_dense: H row narrower than the group's columns");
-  const int n_mtiles = int(ceil_div(M, kTileM));
   // Widest tile that divides every segment and still gives the SMs work:
-  // wide tiles move fewer operand bytes per MAC (the bound of this kernel).
+  // wide tiles move fewer operand bytes per MAC.
   int bn = 64;
-  if (all256 && int64_t(n_mtiles) * (total / 256) * 2 >= num_sms()) bn = 256;
+  if (all256 && int64_t(k.n_mtiles) * (total / 256) * 2 >= num_sms()) bn = 256;
   else if (all128) bn = 128;
-  // B tiles of bn rows (rank columns of H) x 64 k, one box each; rows past r_i read as zeros
+  int nx = 0;
   for (int i = 0; i < n; ++i) {
-    rc = make_tmap_2d(&maps.b[i], Bs[i], dtype, uint64_t(K), uint64_t(rs[i]), uint64_t(K) * 2, 64u, uint32_t(bn));
+    const DenseSeg& g = segs[ord[i]];
+    // one x map per distinct x (same pointer, stride and width)
+    int xi = -1;
+    for (int j = 0; j < i && xi < 0; ++j) {
+      const DenseSeg& h = segs[ord[j]];
+      if (h.x == g.x && h.ldx == g.ldx && h.K == g.K) xi = k.seg_x[j];
+    }
+    if (xi < 0) {
+      xi = nx++;
+      int rc = make_tmap_2d(&maps.x[xi], g.x, dtype, uint64_t(g.K), uint64_t(M), uint64_t(g.ldx) * 2, 64u,
+                            uint32_t(kTileM));
+      if (rc) return rc;
+    }
+    // B tiles of bn rows (rank columns of H) x 64 k, one box each; rows past r read as zeros
+    int rc = make_tmap_2d(&maps.b[i], g.B, dtype, uint64_t(g.K), uint64_t(g.r), uint64_t(g.K) * 2, 64u,
+                          uint32_t(bn));
     if (rc) return rc;
+    k.seg_x[i] = xi;
+    k.seg_nk[i] = int(ceil_div(g.K, 64));
+    k.seg_H[i] = g.H;
+    k.seg_ldh[i] = g.ldh;
+    k.seg_nt[i + 1] = k.seg_nt[i] + int(cols[i] / bn);
   }
-  DenseArgs k{H, M, ldh, n_mtiles, int(total / bn), int(ceil_div(K, 64)), n, {0}};
-  for (int i = 0; i < n; ++i) k.seg_nt[i + 1] = k.seg_nt[i] + int(cols[i] / bn);
+  k.n_ntiles = k.seg_nt[n];
   const int items = k.n_mtiles * k.n_ntiles;
   auto launch = [&](auto kern, int BN) -> int {
     const uint32_t stage = kTileM * 128 + BN * 128;
@@ -792,7 +830,7 @@ int launch_tc_dense_group(const void* x, int64_t ldx, const void* const* Bs, con
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    SLR_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kern, tx, maps, k));
+    SLR_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kern, maps, k));
     return SLR_OK;
   };
   if (dtype == SLR_BF16) {
@@ -803,6 +841,20 @@ int launch_tc_dense_group(const void* x, int64_t ldx, const void* const* Bs, con
   if (bn == 256) return launch(tc_dense_kernel<256, __half>, 256);
   if (bn == 128) return launch(tc_dense_kernel<128, __half>, 128);
   return launch(tc_dense_kernel<64, __half>, 64);
+}
+
+int launch_tc_dense_group(const void* x, int64_t ldx, const void* const* Bs, const int64_t* rs, int n,
+                          void* H, int64_t M, int64_t K, int64_t ldh, int dtype, cudaStream_t s, bool pdl) {
+  if (M <= 0 || n <= 0) return SLR_OK;
+  if (n > kMaxSeg) return fail(SLR_ERR_UNSUPPORTED, "tc_dense: too many weight matrices in one group");
+  DenseSeg segs[kMaxSeg];
+  int64_t col = 0;
+  for (int i = 0; i < n; ++i) {
+    segs[i] = DenseSeg{x, ldx, K, Bs[i], rs[i], static_cast<uint8_t*>(H) + col * dtype_size(dtype), ldh};
+    col += round_up(rs[i], 64);
+  }
+  if (col > ldh) return fail(SLR_ERR_WORKSPACE, "tc_dense: H row narrower than the group's columns");
+  return launch_tc_dense_multi(segs, n, M, dtype, s, pdl);
 }
 
 int launch_tc_dense(const void* x, int64_t ldx, const void* B, void* H, int64_t M, int64_t K, int64_t r,

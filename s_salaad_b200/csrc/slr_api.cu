@@ -993,6 +993,34 @@ int prepare_multi(const slr_layer* layers, int n, const void* const* x, const in
 // bit for bit), else each layer's own.
 int multi_lowrank(const slr_layer* layers, int n, const MultiCall& mc, void* workspace, cudaStream_t s) {
   if (!mc.m.small) {
+    // From 128 tokens: every layer's x*B^T (one segment per layer, the
+    // grouped runs' layers into their shared H) in ONE tensor-core launch,
+    // the layers with the longest K first, when every layer takes that kernel;
+    // H is bit for bit the per-run launches'.
+    DenseSeg segs[kMaxMulti];
+    int ns = 0;
+    bool all_tc = true, pdl = true;
+    for (int r = 0; r < mc.n_runs && all_tc; ++r) {
+      const int i0 = mc.run0[r], i1 = mc.run0[r + 1];
+      for (int i = i0; i < i1 && all_tc; ++i) {
+        const slr_layer& L = layers[i];
+        const FwdCall& c = mc.c[i];
+        if (L.rank == 0 || c.a.M == 0) continue;
+        all_tc = L.dtype == layers[0].dtype;
+        if (mc.grouped[r]) {
+          const GroupCall& gc = mc.gc[r];
+          segs[ns++] = DenseSeg{c.a.x, c.a.ldx, L.in_features, L.B, L.rank,
+                                gc.ws + size_t(gc.g.col[i - i0]) * dtype_size(L.dtype), gc.g.ldh_all};
+          pdl = pdl && group_early_start(&layers[i0], i1 - i0);
+        } else {
+          all_tc = all_tc && c.p.path == 1 && c.a.M >= kTcMinTokens &&
+                   tc_dense_supported(c.a.x, c.a.ldx, L.B, L.in_features, L.rank, L.dtype);
+          segs[ns++] = DenseSeg{c.a.x, c.a.ldx, L.in_features, L.B, L.rank, c.ws, c.p.ldh};
+          pdl = pdl && early_start(L);
+        }
+      }
+    }
+    if (all_tc && ns > 1) return launch_tc_dense_multi(segs, ns, mc.c[0].a.M, layers[0].dtype, s, pdl);
     for (int r = 0; r < mc.n_runs; ++r) {
       const int i0 = mc.run0[r], i1 = mc.run0[r + 1];
       if (mc.grouped[r]) {
