@@ -616,6 +616,10 @@ def main() -> None:
                          (specs[0].block_p, specs[0].block_q) for s in specs))
     if set_peers:
         from s_salaad_b200.shard import finish_set_peers, start_set_peers
+    # ... and this rank's x*B^T of all projections in one launch (a layer set over its shards)
+    local = [i for i in range(len(specs)) if world > 1 and layers[i].desc is not None]
+    pset = (ops.LayerSet([layers[i].desc for i in local])
+            if set_peers and not SPLIT_H and 1 <= len(local) <= 8 else None)
     ys = ([po.y for po in pos] if pos is not None else
           [torch.empty(T, s.out_features, dtype=dtype, device=dev) for s in specs])
     # one GPU: the projections (independent inputs) run as one layer-set call
@@ -628,6 +632,27 @@ def main() -> None:
 
     def step(ev=None):
         """One forward of the layer set; ev = per-projection event triples."""
+        if world > 1 and pset is not None:
+            xs_l = [xs[i] for i in local]
+            if ev is not None:
+                ev[local[0]][0].record(stream)
+            pset.lowrank(xs_l)
+            if ev is not None:
+                # the set's x*B^T charged to its first projection, its combine to the same one
+                for i in range(len(specs)):
+                    if i != local[0]:
+                        ev[i][0].record(stream)
+                    ev[i][1].record(stream)
+                    if i != local[0]:
+                        ev[i][2].record(stream)
+            hs = [None] * len(specs)
+            for i, h in zip(local, pset.h_addresses(xs_l)):
+                hs[i] = h
+            launched = start_set_peers(layers, xs, pos, hs, pos[0])
+            if ev is not None:
+                ev[local[0]][2].record(stream)
+            finish_set_peers(pos[0], launched)
+            return
         if world > 1:
             handles = {}
             hs = [None] * len(specs)  # H of each projection (set_peers)
@@ -898,6 +923,8 @@ def main() -> None:
         launches_per_step = multi_launches(specs) if T < 128 else len(members) + comb_launches
     if set_peers:
         launches_per_step += 1 - sum(1 for i in range(len(specs)) if has_local[i])  # one combine, not one each
+    if pset is not None:
+        launches_per_step = 2  # one x*B^T launch and one combine launch for the set
     if pos is not None:
         launches_per_step += 1 if set_peers else len(specs)  # the wait(s) that end the call(s)
 
@@ -1072,6 +1099,7 @@ def main() -> None:
                 "config": {**config, "l2": "flushed between timed steps (256 MB written, then read back)",
                            "parallelism": (f"block-row shards x{world}, x*B^T "
                                            + ("split by tokens + NCCL all-gather of H" if (SPLIT_H and world >= 4)
+                                              else "of all projections in one launch on every rank" if pset is not None
                                               else "on every rank")
                                            + ((", the combines of all projections in one launch whose epilogue "
                                                "stores y into every rank's y over NVLink (CUDA IPC)") if set_peers

@@ -290,6 +290,14 @@ SLR_API size_t slr_lrs_linear_multi_workspace_size(const slr_layer* layers, int 
 SLR_API int slr_lrs_linear_forward_multi(const slr_layer* layers, int n, const void* const* x,
                            const int64_t* ldx, void* const* y, const int64_t* ldy, int64_t M,
                            void* workspace, size_t workspace_bytes, void* stream);
+/* Where slr_lrs_linear_multi_lowrank leaves each layer's H = x·Bᵀ for this
+ * call (same arguments): H[i] its first element, ldh[i] its row stride in
+ * elements (NULL / 0 for a layer without rank).  For callers that read H
+ * themselves, e.g. slr_lrs_linear_multi_combine_peers.  No reference
+ * counterpart. */
+SLR_API int slr_lrs_linear_multi_h(const slr_layer* layers, int n, const void* const* x,
+                                   const int64_t* ldx, int64_t M, void* workspace,
+                                   size_t workspace_bytes, void** H, int64_t* ldh);
 /* The two phases of slr_lrs_linear_forward_multi (same layers, inputs, M and
  * workspace in both calls): every layer's x[i] · B_iᵀ, then the combines.
  * From 128 tokens on, when every layer takes the 2-SM pair kernel with one

@@ -58,6 +58,7 @@ EXPORTED = (
     "slr_lrs_linear_combine_peers",
     "slr_lrs_linear_group_combine_peers",
     "slr_lrs_linear_multi_combine_peers",
+    "slr_lrs_linear_multi_h",
     "slr_peers_wait",
     "slr_set_wait_limit_ns",
     "slr_lrs_linear_multi_workspace_size",
@@ -168,6 +169,8 @@ _SIGS = {
     "slr_lrs_linear_multi_combine_peers": ([ctypes.POINTER(SlrLayer), i32, ctypes.POINTER(vp), ctypes.POINTER(i64),
                                             ctypes.POINTER(vp), ctypes.POINTER(i64), ctypes.POINTER(i64), i64,
                                             ctypes.POINTER(SlrPeers), ctypes.POINTER(SlrPeers), vp], i32),
+    "slr_lrs_linear_multi_h": ([ctypes.POINTER(SlrLayer), i32, ctypes.POINTER(vp), ctypes.POINTER(i64), i64, vp, sz,
+                                ctypes.POINTER(vp), ctypes.POINTER(i64)], i32),
     "slr_peers_wait": ([ctypes.POINTER(SlrPeers), i32, vp], i32),
     "slr_set_wait_limit_ns": ([ctypes.c_uint64], i32),
     "slr_lrs_linear_multi_workspace_size": ([ctypes.POINTER(SlrLayer), i32, i64], sz),

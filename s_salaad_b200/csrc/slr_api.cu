@@ -1115,6 +1115,19 @@ int slr_lrs_linear_multi_lowrank(const slr_layer* layers, int n, const void* con
   return multi_lowrank(layers, n, mc, workspace, static_cast<cudaStream_t>(stream));
 }
 
+int slr_lrs_linear_multi_h(const slr_layer* layers, int n, const void* const* x, const int64_t* ldx, int64_t M,
+                           void* workspace, size_t workspace_bytes, void** H, int64_t* ldh) {
+  if (!H || !ldh) return fail(SLR_ERR_INVALID_ARGUMENT, "H/ldh is NULL");
+  MultiCall mc;
+  int rc = prepare_multi(layers, n, x, ldx, nullptr, nullptr, M, workspace, workspace_bytes, false, mc);
+  if (rc) return rc;
+  for (int i = 0; i < n; ++i) {
+    H[i] = M > 0 && layers[i].rank > 0 ? const_cast<void*>(mc.c[i].a.H) : nullptr;
+    ldh[i] = M > 0 && layers[i].rank > 0 ? mc.c[i].a.ldh : 0;
+  }
+  return SLR_OK;
+}
+
 int slr_lrs_linear_multi_combine(const slr_layer* layers, int n, const void* const* x, const int64_t* ldx,
                                  void* const* y, const int64_t* ldy, int64_t M, void* workspace,
                                  size_t workspace_bytes, void* stream) {

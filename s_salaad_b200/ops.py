@@ -543,6 +543,20 @@ class LayerSet:
                 0 if ws is None else ws.numel(), _stream(self.device))
         _lib.check(rc, "lrs_linear_multi_lowrank")
 
+    def h_addresses(self, xs: list[torch.Tensor]) -> list[tuple[int, int] | None]:
+        """(device address, row stride) of each layer's H that :meth:`lowrank`
+        leaves in the set's workspace for these inputs (None without rank)."""
+        M = xs[0].shape[0]
+        ws = self.workspace(M)
+        n = len(self.descs)
+        xp, lx, _, _ = self._ptrs(xs)
+        hp = (ctypes.c_void_p * n)()
+        lh = (ctypes.c_int64 * n)()
+        rc = _lib.load().slr_lrs_linear_multi_h(self._structs(), n, xp, lx, M, None if ws is None else ws.data_ptr(),
+                                                0 if ws is None else ws.numel(), hp, lh)
+        _lib.check(rc, "lrs_linear_multi_h")
+        return [(int(hp[i]), int(lh[i])) if hp[i] else None for i in range(n)]
+
     def combine(self, xs: list[torch.Tensor], outs: list[torch.Tensor]) -> list[torch.Tensor]:
         """Phase 2 alone (after lowrank() on the same inputs): every layer's y."""
         M = xs[0].shape[0]

@@ -73,7 +73,8 @@ def check_peer_outputs(rank: int, world: int, dev) -> int:
 def check_set_peers(rank: int, world: int, dev, x, grp, shards, refs) -> int:
     """q/k/v (one group, one H) and o_proj (its own input and H) of cfg4: the
     four combines as ONE launch storing into every rank's y, signals on the
-    first layer's slot; twice, each equal to the single-GPU forward bit for bit."""
+    first layer's slot; three calls (the last with the four x*B^T products as
+    one layer-set launch), each equal to the single-GPU forward bit for bit."""
     from s_salaad_b200.shard import PeerOutputs, ShardedLayer, all_ranks, finish_set_peers, start_set_peers
 
     T = x.shape[0]
@@ -95,12 +96,17 @@ def check_set_peers(rank: int, world: int, dev, x, grp, shards, refs) -> int:
         return 1
     pos = [PeerOutputs(L, T, torch.bfloat16, dev) for L in layers]
     bad = 0
-    for call in range(2):
+    lset = ops.LayerSet([L.desc for L in layers])
+    for call in range(3):
         for po in pos:
             po.y.fill_(float("nan"))
-        grp.lowrank(x)
-        sh_o._lowrank(x_o)
-        hs = [grp.h_of(j, T) for j in range(3)] + [sh_o.h_address(T)]
+        if call < 2:
+            grp.lowrank(x)
+            sh_o._lowrank(x_o)
+            hs = [grp.h_of(j, T) for j in range(3)] + [sh_o.h_address(T)]
+        else:  # the four x*B^T products as one launch of the layer set
+            lset.lowrank(xs)
+            hs = lset.h_addresses(xs)
         launched = start_set_peers(layers, xs, pos, hs, pos[0])
         finish_set_peers(pos[0], launched)
         for j, (po, ref) in enumerate(zip(pos, wants)):
