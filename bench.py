@@ -27,7 +27,9 @@ from __future__ import annotations
 import argparse
 import json
 import os
+import shutil
 import statistics
+import subprocess
 import sys
 import threading
 import time
@@ -131,7 +133,10 @@ def peaks() -> tuple[dict, str]:
 # --------------------------------------------------------------- clocks --
 
 class ClockSampler:
-    """Polls NVML (SM clock, max clock, throttle reasons) in a thread."""
+    """Polls the SM clock, max clock and clock-event (throttle) reasons in a
+    thread while the timed region runs: through NVML, or `nvidia-smi` when
+    NVML cannot be initialised; one sample is always taken as the region
+    starts and one as it ends, so a short region still has a record."""
 
     REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
                0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown"}
@@ -139,30 +144,47 @@ class ClockSampler:
     def __init__(self, index: int):
         self.samples: list[tuple[int, int]] = []
         self.max_mhz = None
+        self.index = index
         self._stop = threading.Event()
         self._thread = None
-        try:
-            import pynvml
+        self.nv = None
+        for _ in range(2):
+            try:
+                import pynvml
 
-            pynvml.nvmlInit()
-            self.nv = pynvml
-            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
-            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
-        except Exception:  # noqa: BLE001 - clocks are best effort
-            self.nv = None
+                pynvml.nvmlInit()
+                self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+                self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+                self.nv = pynvml
+                break
+            except Exception:  # noqa: BLE001 - clocks are best effort
+                time.sleep(0.05)
+        self.smi = self.nv is None and shutil.which("nvidia-smi") is not None
+
+    def _sample(self) -> None:
+        try:
+            if self.nv is not None:
+                mhz = self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM)
+                rs = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+            elif self.smi:
+                out = subprocess.run(["nvidia-smi", "-i", str(self.index), "--format=csv,noheader,nounits",
+                                      "--query-gpu=clocks.sm,clocks.max.sm,clocks_event_reasons.active"],
+                                     capture_output=True, text=True, timeout=5).stdout.strip().split(",")
+                mhz, self.max_mhz, rs = int(out[0]), int(out[1]), int(out[2].strip(), 16)
+            else:
+                return
+            self.samples.append((mhz, rs))
+        except Exception:  # noqa: BLE001
+            pass
 
     def _run(self):
         while not self._stop.is_set():
-            try:
-                mhz = self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM)
-                rs = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
-                self.samples.append((mhz, rs))
-            except Exception:  # noqa: BLE001
-                pass
+            self._sample()
             time.sleep(0.002)
 
     def __enter__(self):
-        if self.nv is not None:
+        self._sample()
+        if self.nv is not None or self.smi:
             self._thread = threading.Thread(target=self._run, daemon=True)
             self._thread.start()
         return self
@@ -171,6 +193,7 @@ class ClockSampler:
         self._stop.set()
         if self._thread:
             self._thread.join()
+        self._sample()
 
     def summary(self) -> dict:
         if not self.samples:
