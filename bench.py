@@ -640,9 +640,9 @@ def main() -> None:
     if set_peers:
         from s_salaad_b200.shard import finish_set_peers, start_set_peers
     # ... and this rank's x*B^T of all projections in one launch (a layer set over its shards)
-    local = [i for i in range(len(specs)) if world > 1 and layers[i].desc is not None]
-    pset = (ops.LayerSet([layers[i].desc for i in local])
-            if set_peers and not SPLIT_H and 1 <= len(local) <= 8 else None)
+    mine = [i for i in range(len(specs)) if world > 1 and layers[i].desc is not None]
+    pset = (ops.LayerSet([layers[i].desc for i in mine])
+            if set_peers and not SPLIT_H and 1 <= len(mine) <= 8 else None)
     ys = ([po.y for po in pos] if pos is not None else
           [torch.empty(T, s.out_features, dtype=dtype, device=dev) for s in specs])
     # one GPU: the projections (independent inputs) run as one layer-set call
@@ -656,24 +656,24 @@ def main() -> None:
     def step(ev=None):
         """One forward of the layer set; ev = per-projection event triples."""
         if world > 1 and pset is not None:
-            xs_l = [xs[i] for i in local]
+            xs_l = [xs[i] for i in mine]
             if ev is not None:
-                ev[local[0]][0].record(stream)
+                ev[mine[0]][0].record(stream)
             pset.lowrank(xs_l)
             if ev is not None:
                 # the set's x*B^T charged to its first projection, its combine to the same one
                 for i in range(len(specs)):
-                    if i != local[0]:
+                    if i != mine[0]:
                         ev[i][0].record(stream)
                     ev[i][1].record(stream)
-                    if i != local[0]:
+                    if i != mine[0]:
                         ev[i][2].record(stream)
             hs = [None] * len(specs)
-            for i, h in zip(local, pset.h_addresses(xs_l)):
+            for i, h in zip(mine, pset.h_addresses(xs_l)):
                 hs[i] = h
             launched = start_set_peers(layers, xs, pos, hs, pos[0])
             if ev is not None:
-                ev[local[0]][2].record(stream)
+                ev[mine[0]][2].record(stream)
             finish_set_peers(pos[0], launched)
             return
         if world > 1:
