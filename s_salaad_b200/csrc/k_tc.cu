@@ -490,15 +490,26 @@ __global__ void __launch_bounds__(kRowThreads, 1)
 // decoder layer) and the layers with their own x, each segment with its own
 // K and H.  The N tiles of segment s are [seg_nt[s], seg_nt[s+1]); an H
 // element is the same dot product in the same k order whatever the launch.
+//
+// Items (one 128-token x BN tile each) weigh their segment's k chunks, so a
+// launch that mixes K = 11008 with K = 4096 segments is unbalanced under a
+// round-robin deal.  The host deals them longest first to the least loaded
+// CTA; CTA c runs deal_item[deal_off[c] .. deal_off[c+1]).  Larger launches
+// than the tables hold (deal == 0) fall back to item = c + j * gridDim.x.
+constexpr int kDealCtas = 160;
+constexpr int kDealItems = 2048;
 struct DenseArgs {
   int64_t M;
   int n_mtiles, n_ntiles;
   int n_seg;
+  int deal;
   int seg_nt[kMaxSeg + 1];
   int seg_nk[kMaxSeg];     // 64-wide k chunks
   int seg_x[kMaxSeg];      // x map of the segment
   void* seg_H[kMaxSeg];    // the segment's first H column
   int64_t seg_ldh[kMaxSeg];
+  uint16_t deal_off[kDealCtas + 1];
+  uint16_t deal_item[kDealItems];
 };
 struct DenseMaps {
   CUtensorMap b[kMaxSeg];
@@ -545,6 +556,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const int n_items = a.n_mtiles * a.n_ntiles;
+  // this CTA's items: the host's deal, or round-robin
+  const int first = a.deal ? int(a.deal_off[blockIdx.x]) : int(blockIdx.x);
+  const int n_mine = a.deal ? int(a.deal_off[blockIdx.x + 1]) - first
+                            : (n_items - int(blockIdx.x) + int(gridDim.x) - 1) / int(gridDim.x);
+  auto item_at = [&](int j) -> int {
+    return a.deal ? int(a.deal_item[first + j]) : first + j * int(gridDim.x);
+  };
   // Launched as a programmatic dependent, this kernel waits here for the kernel
   // before it (x may be its output) and only then lets the next one start
   // (the combine, which reads x before its own wait and H after it).  So a
@@ -560,7 +578,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
 
       uint32_t g = 0;
-      for (int item = blockIdx.x; item < n_items && !s_abort; item += gridDim.x) {
+      for (int j = 0; j < n_mine && !s_abort; ++j) {
+        const int item = item_at(j);
         const int mt = item % a.n_mtiles, nt = item / a.n_mtiles;
         int sg = 0;
         while (sg + 1 < a.n_seg && nt >= a.seg_nt[sg + 1]) ++sg;
@@ -585,7 +604,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       uint32_t g = 0, it = 0;
-      for (int item = blockIdx.x; item < n_items && !s_abort; item += gridDim.x, ++it) {
+      for (int j = 0; j < n_mine && !s_abort; ++j, ++it) {
+        const int item = item_at(j);
         const uint32_t buf = it & 1, tph = (it >> 1) & 1;
         if (!mbar_wait(&tempty[buf], tph ^ 1)) {
           tc_timeout(&s_abort);
@@ -619,7 +639,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q = warp & 3;
     const int row = 32 * q + lane;
     uint32_t it = 0;
-    for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++it) {
+    for (int j = 0; j < n_mine; ++j, ++it) {
+      const int item = item_at(j);
       const int mt = item % a.n_mtiles, nt = item / a.n_mtiles;
       int sg = 0;
       while (sg + 1 < a.n_seg && nt >= a.seg_nt[sg + 1]) ++sg;
@@ -758,6 +779,50 @@ bool tc_dense_supported(const void* x, int64_t ldx, const void* B, int64_t K, in
   return dtype != SLR_F32 && r >= 64 && K >= 64 && K % 8 == 0 && ldx % 8 == 0 && aligned16(x) && aligned16(B);
 }
 
+// Longest-processing-time deal of a dense launch's items to `grid` CTAs.  The
+// items of segment s are [seg_nt[s], seg_nt[s+1]) x n_mtiles, each weighing
+// w[s]; the segments come heaviest first, so walking the items in index order
+// takes them heaviest first, and each goes to the least loaded CTA (ties to the
+// lowest index: equal weights deal round-robin).  off[c] .. off[c+1] indexes
+// CTA c's items in `item`, in the order it runs them.
+static void deal_longest_first(const int* seg_nt, const int* w, int n_seg, int n_mtiles, int grid,
+                               uint16_t* off, uint16_t* item) {
+  struct Bin {
+    int64_t load;
+    int cta;
+  };
+  auto before = [](const Bin& x, const Bin& y) { return x.load < y.load || (x.load == y.load && x.cta < y.cta); };
+  Bin heap[kDealCtas];
+  for (int c = 0; c < grid; ++c) heap[c] = Bin{0, c};  // ascending: already a min-heap
+  uint8_t owner[kDealItems];
+  int cnt[kDealCtas] = {};
+  int i = 0;
+  for (int sg = 0; sg < n_seg; ++sg) {
+    const int end = seg_nt[sg + 1] * n_mtiles;
+    for (; i < end; ++i) {
+      owner[i] = uint8_t(heap[0].cta);
+      ++cnt[heap[0].cta];
+      heap[0].load += w[sg];
+      for (int p = 0;;) {
+        const int l = 2 * p + 1, r = l + 1;
+        int m = p;
+        if (l < grid && before(heap[l], heap[m])) m = l;
+        if (r < grid && before(heap[r], heap[m])) m = r;
+        if (m == p) break;
+        std::swap(heap[p], heap[m]);
+        p = m;
+      }
+    }
+  }
+  int pos[kDealCtas];
+  off[0] = 0;
+  for (int c = 0; c < grid; ++c) {
+    pos[c] = off[c];
+    off[c + 1] = uint16_t(off[c] + cnt[c]);
+  }
+  for (int j = 0; j < i; ++j) item[pos[owner[j]]++] = uint16_t(j);
+}
+
 int launch_tc_dense_multi(const DenseSeg* segs, int n, int64_t M, int dtype, cudaStream_t s, bool pdl) {
   if (M <= 0 || n <= 0) return SLR_OK;
   if (n > kMaxSeg) return fail(SLR_ERR_UNSUPPORTED, "tc_dense: too many weight matrices in one launch");
@@ -815,13 +880,22 @@ int launch_tc_dense_multi(const DenseSeg* segs, int n, int64_t M, int dtype, cud
   }
   k.n_ntiles = k.seg_nt[n];
   const int items = k.n_mtiles * k.n_ntiles;
+  const int grid = std::min(items, num_sms());
+  if (items <= kDealItems && grid <= kDealCtas) {
+    // item i belongs to segment sg(i); its weight is the segment's k chunks
+    // plus two for the tile's epilogue
+    int w[kMaxSeg];
+    for (int i = 0; i < n; ++i) w[i] = k.seg_nk[i] + 2;
+    deal_longest_first(k.seg_nt, w, n, k.n_mtiles, grid, k.deal_off, k.deal_item);
+    k.deal = 1;
+  }
   auto launch = [&](auto kern, int BN) -> int {
     const uint32_t stage = kTileM * 128 + BN * 128;
     const int stages = std::min(8, int((196 * 1024) / stage));
     const size_t smem = 1024 + size_t(stages) * stage + (2 * stages + 4) * 8 + 16;
     SLR_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(unsigned(std::min(items, num_sms())));
+    cfg.gridDim = dim3(unsigned(grid));
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
