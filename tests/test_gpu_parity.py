@@ -752,6 +752,33 @@ def test_multi_forward_equals_per_layer(cuda, oracle, name, T):
             assert_16bit_close(y, oracle_layer(oracle, t, x.cpu()))
 
 
+@pytest.mark.parametrize("name", ["one_shape", "mixed"])
+@pytest.mark.parametrize("sms", [2, 6, 37])
+def test_layer_set_on_few_ctas_equals_full_grid(cuda, name, sms):
+    """The persistent kernels capped at a few CTAs (slr_set_sm_limit): each
+    x*B^T CTA runs several items of different K, dealt longest first to the
+    least-loaded CTA, and each combine pair several row groups.  The layer
+    set's outputs equal those computed on the full grid bit for bit, so the
+    deal loses and repeats no tile."""
+    specs, descs = _multi_layers(cuda, name)
+    T = 300
+    inputs, xs = {}, []
+    for (n, k, *_rest, inp) in MULTI[name]:
+        if inp not in inputs:
+            inputs[inp] = workloads.tokens(T, k, seed=T + 31 * inp, dtype=torch.bfloat16).to(cuda)
+        xs.append(inputs[inp])
+    ref = [y.clone() for y in ops.LayerSet(descs).forward(xs)]
+    lib = _lib.load()
+    try:
+        assert lib.slr_set_sm_limit(sms) == 0
+        ys = ops.LayerSet(descs).forward(xs)
+        torch.cuda.synchronize()
+    finally:
+        lib.slr_set_sm_limit(0)
+    for a, b in zip(ys, ref):
+        assert torch.equal(a, b)
+
+
 @pytest.mark.parametrize("name", list(MULTI))
 @pytest.mark.parametrize("T", [1, 64, 300])
 def test_multi_phases_equal_forward(cuda, name, T):
@@ -768,12 +795,14 @@ def test_multi_phases_equal_forward(cuda, name, T):
         assert torch.equal(a, b)
 
 
-@pytest.mark.parametrize("T", [300, 1024])
+@pytest.mark.parametrize("T", [300, 1024, 4096])
 def test_pair_kernel_layer_set_in_one_launch(cuda, oracle, T):
     """Four cfg4 projections (64x64 blocks, column schedules, Zipf rows), each
     with its own input: their combines run as ONE launch of the 2-SM pair
     kernel (items of all layers dealt as one list) and equal the per-layer
-    forwards bit for bit; also as a group (q/k/v on one input)."""
+    forwards bit for bit; also as a group (q/k/v on one input).  At 4096
+    tokens their x*B^T launch has 256 items of K = 11008 and K = 4096 for the
+    148 CTAs, dealt longest first."""
     cfg = workloads.layer_set("cfg4")
     specs = [cfg[i] for i in (0, 3, 4, 6)]
     tens = [s.tensors(cuda, torch.bfloat16) for s in specs]
